@@ -1,0 +1,256 @@
+"""Python driver for the CPU oracle -- TEST INFRASTRUCTURE ONLY.
+
+Loads ``oracle/_build/libgs_oracle.so`` (built from ``gs_oracle.c`` by
+``oracle/Makefile``) and exposes the reference rasterizer's stages on numpy
+arrays. Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU
+baseline use this module; the product never imports it.
+
+Scalar folding follows the reference: ``lim_x``/``lim_y``, the ellipsoid
+extent and cutoff are computed in Python double and rounded to float32 where
+the kernels consume them (project.py:158-159,308; composite.py:226;
+project_bwd.py:376-377).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+import os
+import subprocess
+from dataclasses import dataclass
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIBRARY = os.path.join(HERE, "_build", "libgs_oracle.so")
+
+_f32p = np.ctypeslib.ndpointer(dtype=np.float32, flags="C_CONTIGUOUS")
+_i32p = np.ctypeslib.ndpointer(dtype=np.int32, flags="C_CONTIGUOUS")
+_i64p = np.ctypeslib.ndpointer(dtype=np.int64, flags="C_CONTIGUOUS")
+
+
+class Params(ctypes.Structure):
+    _fields_ = [
+        ("fx", ctypes.c_float), ("fy", ctypes.c_float), ("cx", ctypes.c_float),
+        ("cy", ctypes.c_float), ("width", ctypes.c_int32), ("height", ctypes.c_int32),
+        ("tile_size", ctypes.c_int32), ("gaussian_mode", ctypes.c_int32),
+        ("near_plane", ctypes.c_float), ("far_plane", ctypes.c_float),
+        ("lim_x", ctypes.c_float), ("lim_y", ctypes.c_float),
+        ("bwd_lim_x", ctypes.c_float), ("bwd_lim_y", ctypes.c_float),
+        ("extent", ctypes.c_float), ("cutoff", ctypes.c_float),
+        ("opacity_threshold", ctypes.c_float),
+    ]
+
+
+def build() -> str:
+    """Compile the oracle library if it is missing or older than its sources."""
+    sources = [os.path.join(HERE, f) for f in ("gs_oracle.c", "detmath.h", "Makefile")]
+    if not os.path.exists(LIBRARY) or os.path.getmtime(LIBRARY) < max(map(os.path.getmtime, sources)):
+        subprocess.run(["make", "-s", "-C", HERE], check=True)
+    return LIBRARY
+
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        _lib = ctypes.CDLL(build())
+        P = ctypes.POINTER(Params)
+        i64, i32 = ctypes.c_int64, ctypes.c_int32
+        _lib.gso_project.argtypes = [i64, _f32p, _f32p, _f32p, _f32p, _f32p, i32, _f32p, _f32p, P,
+                                     _f32p, _f32p, _f32p, _f32p, _i32p, _i32p]
+        _lib.gso_total.argtypes = [i64, _i32p]
+        _lib.gso_total.restype = i64
+        _lib.gso_bin.argtypes = [i64, _i32p, _f32p, _i32p, i32, i32, ctypes.c_void_p,
+                                 ctypes.c_void_p, _i32p, ctypes.c_void_p, _i64p]
+        _lib.gso_composite.argtypes = [_f32p, _f32p, _f32p, _f32p, _i32p, _i64p, P,
+                                       ctypes.c_void_p, i32, _f32p, _f32p, _i32p]
+        _lib.gso_composite_bwd.argtypes = [i64, _f32p, _f32p, _f32p, _f32p, _i32p, _i64p, i64,
+                                           _f32p, _f32p, _i32p, P, _f32p]
+        _lib.gso_project_bwd.argtypes = [i64, _f32p, _f32p, _f32p, _f32p, _f32p, i32, _f32p, _f32p,
+                                         _f32p, _f32p, _i32p, P, _f32p, _f32p, _f32p, _f32p,
+                                         _f32p]
+        _lib.gso_exp_array.argtypes = [i64, _f32p, _f32p]
+        _lib.gso_log_array.argtypes = [i64, _f32p, _f32p]
+    return _lib
+
+
+@dataclass
+class Settings:
+    fx: float
+    fy: float
+    cx: float
+    cy: float
+    width: int
+    height: int
+    tile_size: int = 16
+    opacity_threshold: float = 0.999
+    near: float = 0.2
+    far: float = 100.0
+    rendering_mode: str = "gaussian"
+    confidence: float = 0.95
+
+    @property
+    def tiles_w(self) -> int:
+        return self.width // self.tile_size
+
+    @property
+    def num_tiles(self) -> int:
+        return (self.width // self.tile_size) * (self.height // self.tile_size)
+
+    def params(self) -> Params:
+        tiles_w = self.width // self.tile_size
+        tiles_h = self.height // self.tile_size
+        ellipsoid = self.rendering_mode == "ellipsoid"
+        return Params(
+            fx=self.fx, fy=self.fy, cx=self.cx, cy=self.cy,
+            width=self.width, height=self.height, tile_size=self.tile_size,
+            gaussian_mode=0 if ellipsoid else 1,
+            near_plane=self.near, far_plane=self.far,
+            lim_x=1.3 * tiles_w * self.tile_size / (2.0 * self.fx),
+            lim_y=1.3 * tiles_h * self.tile_size / (2.0 * self.fy),
+            bwd_lim_x=1.3 * self.width / (2.0 * self.fx),
+            bwd_lim_y=1.3 * self.height / (2.0 * self.fy),
+            extent=math.sqrt(-2 * math.log1p(-self.confidence)) if ellipsoid else 3.0,
+            cutoff=-2.0 * math.log1p(-self.confidence),
+            opacity_threshold=self.opacity_threshold,
+        )
+
+
+def _c(a, dtype=np.float32):
+    return np.ascontiguousarray(a, dtype=dtype)
+
+
+def project(mean, rotation, scale, opacity, color, camera_rotation, camera_translation,
+            s: Settings) -> dict:
+    n = mean.shape[0]
+    num_sh = color.shape[1]
+    out = dict(
+        projected_mean=np.empty((n, 3), np.float32),
+        inverse_covariance=np.empty((n, 2, 2), np.float32),
+        projected_color=np.empty((n, 3), np.float32),
+        projected_opacity=np.empty((n, 1), np.float32),
+        bounds=np.empty((n, 2, 2), np.int32),
+        counts=np.empty((n,), np.int32),
+    )
+    p = s.params()
+    lib().gso_project(n, _c(mean), _c(rotation), _c(scale), _c(opacity), _c(color), num_sh,
+                      _c(camera_rotation), _c(camera_translation), ctypes.byref(p),
+                      out["projected_mean"], out["inverse_covariance"], out["projected_color"],
+                      out["projected_opacity"], out["bounds"], out["counts"])
+    return out
+
+
+def bin(bounds, depths, counts, s: Settings, with_keys: bool = False) -> dict:
+    bounds, depths, counts = _c(bounds, np.int32), _c(depths), _c(counts, np.int32)
+    n = counts.shape[0]
+    total = lib().gso_total(n, counts)
+    sorted_ids = np.empty((total,), np.int32)
+    ranges = np.empty((s.num_tiles, 2), np.int64)
+    keys = np.empty((total,), np.int64) if with_keys else None
+    ids = np.empty((total,), np.int32) if with_keys else None
+    sorted_keys = np.empty((total,), np.int64) if with_keys else None
+    ptr = lambda a: a.ctypes.data if a is not None else None  # noqa: E731
+    lib().gso_bin(n, bounds, depths, counts, s.tiles_w, s.num_tiles, ptr(keys), ptr(ids),
+                  sorted_ids, ptr(sorted_keys), ranges)
+    out = dict(gaussian_ids=sorted_ids, ranges=ranges)
+    if with_keys:
+        out.update(keys=keys, ids=ids, sorted_keys=sorted_keys)
+    return out
+
+
+def composite(projected_mean, inverse_covariance, projected_color, projected_opacity,
+              gaussian_ids, ranges, s: Settings, tiles=None) -> dict:
+    h, w = s.height, s.width
+    image = np.zeros((h, w, 3), np.float32)
+    final_t = np.ones((h, w), np.float32)
+    n_contrib = np.zeros((h, w), np.int32)
+    tiles_arr = None if tiles is None else _c(tiles, np.int32)
+    p = s.params()
+    lib().gso_composite(_c(projected_mean), _c(inverse_covariance), _c(projected_color),
+                        _c(projected_opacity), _c(gaussian_ids, np.int32), _c(ranges, np.int64),
+                        ctypes.byref(p), None if tiles_arr is None else tiles_arr.ctypes.data,
+                        0 if tiles_arr is None else len(tiles_arr), image, final_t, n_contrib)
+    return dict(image=image, final_transmittance=final_t, n_contributors=n_contrib)
+
+
+def rasterize(mean, rotation, scale, opacity, color, camera_rotation, camera_translation,
+              s: Settings) -> dict:
+    """All ten outputs of the ``gaussian_splats::rasterize`` op, plus bounds."""
+    out = project(mean, rotation, scale, opacity, color, camera_rotation, camera_translation, s)
+    out.update(bin(out["bounds"], out["projected_mean"][:, 2], out["counts"], s))
+    out.update(composite(out["projected_mean"], out["inverse_covariance"],
+                         out["projected_color"], out["projected_opacity"],
+                         out["gaussian_ids"], out["ranges"], s))
+    return out
+
+
+def composite_bwd(fwd: dict, grad_image, s: Settings) -> np.ndarray:
+    n = fwd["projected_mean"].shape[0]
+    grad = np.empty((n, 9), np.float32)
+    p = s.params()
+    lib().gso_composite_bwd(n, _c(fwd["projected_mean"]), _c(fwd["inverse_covariance"]),
+                            _c(fwd["projected_color"]), _c(fwd["projected_opacity"]),
+                            _c(fwd["gaussian_ids"], np.int32), _c(fwd["ranges"], np.int64),
+                            len(fwd["gaussian_ids"]), _c(grad_image),
+                            _c(fwd["final_transmittance"]), _c(fwd["n_contributors"], np.int32),
+                            ctypes.byref(p), grad)
+    return grad
+
+
+def project_bwd(mean, rotation, scale, opacity, color, camera_rotation, camera_translation,
+                inverse_covariance, grad_projected, counts, s: Settings) -> dict:
+    n = mean.shape[0]
+    num_sh = color.shape[1]
+    out = dict(mean=np.empty((n, 3), np.float32), rotation=np.empty((n, 4), np.float32),
+               scale=np.empty((n, 3), np.float32), opacity=np.empty((n, 1), np.float32),
+               color=np.empty((n, num_sh, 3), np.float32))
+    p = s.params()
+    lib().gso_project_bwd(n, _c(mean), _c(rotation), _c(scale), _c(opacity), _c(color), num_sh,
+                          _c(camera_rotation), _c(camera_translation), _c(inverse_covariance),
+                          _c(grad_projected), _c(counts, np.int32), ctypes.byref(p),
+                          out["mean"], out["rotation"], out["scale"], out["opacity"],
+                          out["color"])
+    return out
+
+
+def backward(inputs: dict, fwd: dict, grad_image, s: Settings) -> dict:
+    """Parameter gradients for ``grad_image`` (interface.py:176-239)."""
+    grad_projected = composite_bwd(fwd, grad_image, s)
+    grads = project_bwd(inputs["mean"], inputs["rotation"], inputs["scale"], inputs["opacity"],
+                        inputs["color"], inputs["camera_rotation"], inputs["camera_translation"],
+                        fwd["inverse_covariance"], grad_projected, fwd["counts"], s)
+    grads["grad_projected"] = grad_projected
+    return grads
+
+
+def exp(x) -> np.ndarray:
+    x = _c(x)
+    y = np.empty_like(x)
+    lib().gso_exp_array(x.size, x, y)
+    return y
+
+
+def log(x) -> np.ndarray:
+    x = _c(x)
+    y = np.empty_like(x)
+    lib().gso_log_array(x.size, x, y)
+    return y
+
+
+def load_golden(path: str) -> tuple[dict, Settings, dict]:
+    """Inputs, settings and recorded reference outputs of a golden ``.npz``."""
+    d = np.load(path)
+    inputs = {k[3:]: d[k] for k in d.files if k.startswith("in_")}
+    fx, fy, cx, cy = (float(v) for v in inputs["intrinsics"])
+    w, h = (int(v) for v in inputs["image_size"])
+    near, far = (float(v) for v in inputs["near_far"])
+    s = Settings(fx=fx, fy=fy, cx=cx, cy=cy, width=w, height=h,
+                 tile_size=int(inputs["tile_size"]),
+                 opacity_threshold=float(inputs["opacity_threshold"]), near=near, far=far,
+                 rendering_mode=str(inputs["rendering_mode"]),
+                 confidence=float(inputs["confidence"]))
+    expected = {k: d[k] for k in d.files if not k.startswith("in_")}
+    return inputs, s, expected

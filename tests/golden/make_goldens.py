@@ -1,0 +1,226 @@
+"""Generate golden vectors by running the reference's own rasterizer.
+
+The reference (VikaasVarma/gaussian-splats) is pure Python; its GPU path is six
+Triton kernels wrapped in the ``gaussian_splats::rasterize`` custom op
+(kernels/rasterize/interface.py:17-244). Triton's CPU interpreter
+(``TRITON_INTERPRET=1``) runs those same kernels without a GPU, so this script
+imports the reference from a source checkout, calls the op (forward and, where
+the case asks, autograd backward), and writes inputs, all ten op outputs and
+the parameter gradients to ``tests/golden/<case>.npz``.
+
+Run it where the reference checkout exists (it is not needed afterwards):
+
+    TRITON_INTERPRET=1 TORCHDYNAMO_DISABLE=1 PYTHONDONTWRITEBYTECODE=1 \
+        python tests/golden/make_goldens.py --reference <checkout>/src [case ...]
+
+Scenes:
+* ``fixture_*``: the reference's own test fixture (kernels/rasterize/tests/
+  common.py:19-50: seed 42, 5 % near-plane, far-plane, off-screen and large
+  Gaussians, 32x32, fx = fy = 24), with the camera turned to face +Z so the
+  Gaussians are in front of it (the stock fixture's identity camera sees none
+  of them; ``fixture_degenerate`` keeps that camera).
+* ``mini2`` / ``mini5``: configs 2 and 5 at a few thousand Gaussians and a
+  small padded image (96x60 and 64x60), L1 loss against a random target.
+* ``config1``: the full config-1 forward (16,384 Gaussians, 256x256).
+* ``intersections``: the reference's random-bounds emit/sort case
+  (kernels/rasterize/tests/test_intersections.py:8-18).
+"""
+
+from __future__ import annotations
+
+import argparse
+import os
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+HERE = Path(__file__).resolve().parent
+REPO = HERE.parent.parent
+
+OUTPUT_NAMES = (
+    "image",
+    "final_transmittance",
+    "n_contributors",
+    "projected_mean",
+    "inverse_covariance",
+    "projected_color",
+    "projected_opacity",
+    "gaussian_ids",
+    "ranges",
+    "counts",
+)
+PARAM_NAMES = ("mean", "rotation", "scale", "opacity", "color")
+
+
+def _fixture(sh_degree: int, num_points: int = 1000, face: bool = True):
+    from gaussian_splats.kernels.rasterize.tests.common import make_scene
+
+    splats, camera = make_scene(num_points, sh_degree=sh_degree)
+    if face:
+        # Half turn about +Y: camera axes (-x, y, -z), so world +Z is in front.
+        camera.rotation = torch.tensor([0.0, 0.0, 1.0, 0.0])
+    tensors = tuple(getattr(splats, n).detach().clone() for n in PARAM_NAMES)
+    fx, fy = camera.focal_length
+    cx, cy = camera.principal_point
+    w, h = camera.image_size
+    return tensors, camera.rotation_matrix, camera.translation.clone(), (fx, fy, cx, cy, w, h)
+
+
+def _from_scene(scene):
+    camera = scene.cameras[0]
+    fx, fy = camera.focal_length
+    cx, cy = camera.principal_point
+    w, h = camera.image_size
+    return (
+        scene.tensors(),
+        camera.rotation_matrix,
+        camera.translation.clone(),
+        (fx, fy, cx, cy, w, h),
+    )
+
+
+def build_case(name: str) -> dict:
+    sys.path.insert(0, str(REPO))
+    from gaussian_splats_b200 import scenes
+
+    settings = dict(tile_size=8, opacity_threshold=0.999, near=0.1, far=100.0,
+                    rendering_mode="gaussian", confidence=0.95)
+    crop = None
+    target = None
+    loss = "square_mean"
+    backward = True
+    if name == "fixture_sh1_t8":
+        tensors, cam_r, cam_t, intr = _fixture(1)
+    elif name == "fixture_sh0_t8":
+        tensors, cam_r, cam_t, intr = _fixture(0)
+        backward = False
+    elif name == "fixture_sh4_t8":
+        tensors, cam_r, cam_t, intr = _fixture(4)
+        backward = False
+    elif name == "fixture_sh2_t8":
+        tensors, cam_r, cam_t, intr = _fixture(2)
+    elif name == "fixture_sh3_t16":
+        tensors, cam_r, cam_t, intr = _fixture(3)
+        settings["tile_size"] = 16
+    elif name == "fixture_sh1_t4":
+        tensors, cam_r, cam_t, intr = _fixture(1)
+        settings["tile_size"] = 4
+    elif name == "fixture_ellipsoid":
+        tensors, cam_r, cam_t, intr = _fixture(1)
+        settings["rendering_mode"] = "ellipsoid"
+        backward = False
+    elif name == "fixture_degenerate":
+        tensors, cam_r, cam_t, intr = _fixture(1, face=False)
+        backward = False
+    elif name == "mini2":
+        scene = scenes.config2(num_points=3000, width=96, height=60, log_scale=(-3.5, 0.7))
+        tensors, cam_r, cam_t, intr = _from_scene(scene)
+        settings.update(tile_size=16, near=0.2)
+        crop, target, loss = scene.crop, scene.targets[0], "l1"
+    elif name == "mini5":
+        scene = scenes.config5(num_points=1500, width=64, height=60)
+        tensors, cam_r, cam_t, intr = _from_scene(scene)
+        settings.update(tile_size=16, near=0.2)
+        crop, target, loss = scene.crop, scene.targets[0], "l1"
+    elif name == "config1":
+        scene = scenes.config1()
+        tensors, cam_r, cam_t, intr = _from_scene(scene)
+        settings.update(tile_size=16, near=scene.settings.near)
+        backward = False
+    else:
+        raise KeyError(name)
+    return dict(tensors=tensors, cam_r=cam_r, cam_t=cam_t, intr=intr, settings=settings,
+                crop=crop, target=target, loss=loss, backward=backward)
+
+
+def run_case(name: str) -> dict:
+    import gaussian_splats.kernels.rasterize.interface  # noqa: F401  registers the op
+
+    case = build_case(name)
+    tensors = [t.clone().requires_grad_(case["backward"]) for t in case["tensors"]]
+    fx, fy, cx, cy, w, h = case["intr"]
+    s = case["settings"]
+    args = (*tensors, case["cam_r"], case["cam_t"], float(fx), float(fy), float(cx), float(cy),
+            int(w), int(h), s["tile_size"], s["opacity_threshold"], s["near"], s["far"],
+            s["rendering_mode"], s["confidence"])
+    out = torch.ops.gaussian_splats.rasterize(*args)
+    record = {}
+    for i, t in enumerate(case["tensors"]):
+        record["in_" + PARAM_NAMES[i]] = t.numpy()
+    record["in_camera_rotation"] = case["cam_r"].numpy()
+    record["in_camera_translation"] = case["cam_t"].numpy()
+    record["in_intrinsics"] = np.array([fx, fy, cx, cy], dtype=np.float64)
+    record["in_image_size"] = np.array([w, h], dtype=np.int64)
+    record["in_tile_size"] = np.array(s["tile_size"])
+    record["in_opacity_threshold"] = np.array(s["opacity_threshold"])
+    record["in_near_far"] = np.array([s["near"], s["far"]])
+    record["in_rendering_mode"] = np.array(s["rendering_mode"])
+    record["in_confidence"] = np.array(s["confidence"])
+    for n, t in zip(OUTPUT_NAMES, out):
+        record["out_" + n] = t.detach().numpy()
+    if case["backward"]:
+        image = out[0]
+        if case["loss"] == "l1":
+            cw, ch = case["crop"]
+            loss = (image[:ch, :cw] - case["target"]).abs().mean()
+            record["in_target"] = case["target"].numpy()
+            record["in_crop"] = np.array(case["crop"])
+        else:
+            loss = image.square().mean()
+        grad_image = torch.autograd.grad(loss, image, retain_graph=True)[0]
+        grads = torch.autograd.grad(image, tensors, grad_image)
+        record["in_grad_image"] = grad_image.numpy()
+        for n, g in zip(PARAM_NAMES, grads):
+            record["grad_" + n] = g.numpy()
+    return record
+
+
+def run_intersections() -> dict:
+    """The reference's random-bounds case, through its Triton emit + torch sort."""
+    from gaussian_splats.kernels.rasterize.intersections import (
+        emit_intersections,
+        sort_intersections,
+    )
+
+    tiles_w = tiles_h = 8
+    with torch.random.fork_rng():
+        torch.manual_seed(42)
+        corners = torch.randint(0, tiles_w + 1, (256, 2, 2))
+        depths = torch.rand(256) * 10.0 + 0.1
+    bounds = torch.stack((corners.amin(dim=-1), corners.amax(dim=-1)), dim=-1).to(torch.int32)
+    counts = (bounds[:, :, 1] - bounds[:, :, 0]).prod(dim=-1).to(torch.int32)
+    keys, ids = emit_intersections(bounds, depths, counts, tiles_w)
+    sorted_ids, ranges = sort_intersections(keys, ids, tiles_w * tiles_h)
+    return dict(
+        in_bounds=bounds.numpy(), in_depths=depths.numpy(), in_counts=counts.numpy(),
+        in_tiles=np.array([tiles_w, tiles_h]), out_keys=keys.numpy(), out_ids=ids.numpy(),
+        out_sorted_ids=sorted_ids.numpy(), out_ranges=ranges.numpy(),
+    )
+
+
+CASES = ("intersections", "fixture_degenerate", "fixture_sh1_t8", "fixture_sh0_t8",
+         "fixture_sh4_t8", "fixture_sh2_t8", "fixture_ellipsoid", "fixture_sh1_t4",
+         "fixture_sh3_t16", "mini5", "mini2", "config1")
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser()
+    parser.add_argument("--reference", required=True, help="path to the reference's src/")
+    parser.add_argument("cases", nargs="*", default=list(CASES))
+    args = parser.parse_args()
+    if os.environ.get("TRITON_INTERPRET") != "1":
+        raise SystemExit("set TRITON_INTERPRET=1 (the Triton kernels run on the CPU interpreter)")
+    sys.path.insert(0, args.reference)
+    torch.set_num_threads(os.cpu_count() or 1)
+    for name in args.cases:
+        t0 = time.time()
+        record = run_intersections() if name == "intersections" else run_case(name)
+        np.savez_compressed(HERE / f"{name}.npz", **record)
+        print(f"{name}: {time.time() - t0:.1f}s", flush=True)
+
+
+if __name__ == "__main__":
+    main()
