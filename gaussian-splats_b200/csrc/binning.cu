@@ -1,0 +1,584 @@
+// Tile binning: which Gaussians touch which tile, in front-to-back order.
+//
+// The reference emits one int64 key (tile << 32 | depth bits) per
+// (Gaussian, tile) pair in Gaussian order and sorts all of them
+// (intersections.py:10-88): a 64-bit radix sort over every intersection.
+// The same order -- by tile, then depth bits, then Gaussian index -- comes
+// out of two much cheaper stable sorts:
+//   1. sort only the Gaussians with count > 0 by their 32-bit depth bits
+//      (stable, so equal depths keep index order);
+//   2. emit every Gaussian's tiles in that depth order (tile id = key,
+//      Gaussian = value) and stably sort by tile id, which needs only
+//      ceil(log2(num_tiles)) bits (13 for 1080p at 16x16: two 8-bit passes).
+// Within a tile the emission order is the depth order, and the stable tile
+// sort keeps it.
+//
+// Both sorts are LSD radix sorts with 8-bit digits, one kernel per pass in
+// the "onesweep" style: each CTA ranks a 4096-key tile in shared memory
+// (warp-level match_any ranking, which is stable), publishes its per-digit
+// counts, computes its global offsets by decoupled look-back over the
+// preceding CTAs, and writes the keys out digit-grouped and coalesced. CTAs
+// take their tile index from an atomic counter, so a CTA only ever waits on
+// CTAs that already started. Every spin is bounded; on expiry the CTA records
+// an error word and proceeds, so a fault costs a wrong result and an error
+// code, never a hung GPU.
+#include "common.cuh"
+
+namespace gs {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kItems = 16;
+constexpr int kTile = kThreads * kItems;  // 4096 keys per CTA
+constexpr int kRadix = 256;
+constexpr uint32_t kFlagAggregate = 1u << 30;
+constexpr uint32_t kFlagPrefix = 2u << 30;
+constexpr uint32_t kValueMask = (1u << 30) - 1;
+constexpr uint64_t kScanFlagAggregate = 1ull << 62;
+constexpr uint64_t kScanFlagPrefix = 2ull << 62;
+constexpr uint64_t kScanValueMask = (1ull << 62) - 1;
+constexpr int kSpinLimit = 1 << 22;  // with 64 ns backoff: ~0.3 s before giving up
+
+// Error word bits (BinHeader::error).
+constexpr uint32_t kErrLookbackTimeout = 1u;
+
+__device__ __forceinline__ uint32_t ld_volatile(const uint32_t* p) {
+  return *reinterpret_cast<const volatile uint32_t*>(p);
+}
+__device__ __forceinline__ uint64_t ld_volatile(const uint64_t* p) {
+  return *reinterpret_cast<const volatile uint64_t*>(p);
+}
+__device__ __forceinline__ void st_volatile(uint32_t* p, uint32_t v) {
+  *reinterpret_cast<volatile uint32_t*>(p) = v;
+}
+__device__ __forceinline__ void st_volatile(uint64_t* p, uint64_t v) {
+  *reinterpret_cast<volatile uint64_t*>(p) = v;
+}
+
+__device__ __forceinline__ unsigned lanemask_lt() {
+  unsigned m;
+  asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
+  return m;
+}
+
+// Inputs of a sort pass. `valid(i)` filters elements (only the depth sort's
+// first pass drops Gaussians with count 0); `key`/`value` read element i.
+struct DepthSource {  // key = depth bits of projected_mean[i, 2], value = i
+  const float* projected_mean;
+  const int32_t* counts;
+  __device__ __forceinline__ bool valid(int64_t i) const { return __ldg(counts + i) > 0; }
+  __device__ __forceinline__ uint32_t key(int64_t i) const {
+    return __float_as_uint(__ldg(projected_mean + 3 * i + 2));
+  }
+  __device__ __forceinline__ uint32_t value(int64_t i) const { return static_cast<uint32_t>(i); }
+};
+
+struct ArraySource {
+  const uint32_t* keys;
+  const uint32_t* values;
+  __device__ __forceinline__ bool valid(int64_t) const { return true; }
+  __device__ __forceinline__ uint32_t key(int64_t i) const { return keys[i]; }
+  __device__ __forceinline__ uint32_t value(int64_t i) const { return values[i]; }
+};
+
+// Element count of a pass: a host value, or a device word written earlier on
+// the stream (the number of visible Gaussians).
+struct Count {
+  int64_t host;
+  const uint32_t* device;
+  __device__ __forceinline__ int64_t get() const { return device ? *device : host; }
+};
+
+// Per-digit histograms of every pass at once (the global digit offsets each
+// pass needs), plus the number of valid elements.
+template <class Source>
+__global__ void __launch_bounds__(kThreads) upsweep_kernel(Source src, int64_t n, int num_passes,
+                                                          int shift0, uint32_t* __restrict__ hist,
+                                                          uint32_t* __restrict__ valid_total) {
+  __shared__ uint32_t s_hist[4][kRadix];
+  for (int i = threadIdx.x; i < 4 * kRadix; i += kThreads) (&s_hist[0][0])[i] = 0;
+  __syncthreads();
+  uint32_t valid_here = 0;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * kThreads) {
+    if (!src.valid(i)) continue;
+    ++valid_here;
+    const uint32_t key = src.key(i);
+    for (int p = 0; p < num_passes; ++p) atomicAdd(&s_hist[p][(key >> (shift0 + 8 * p)) & 0xFF], 1u);
+  }
+  if (valid_total) {
+    for (int o = 16; o > 0; o >>= 1) valid_here += __shfl_xor_sync(0xffffffffu, valid_here, o);
+    if ((threadIdx.x & 31) == 0 && valid_here) atomicAdd(valid_total, valid_here);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < num_passes * kRadix; i += kThreads) {
+    const uint32_t c = (&s_hist[0][0])[i];
+    if (c) atomicAdd(hist + i, c);
+  }
+}
+
+// Block-wide exclusive scan of one value per thread (kThreads values).
+__device__ __forceinline__ uint32_t block_exclusive_scan(uint32_t v, uint32_t* s_tmp,
+                                                         uint32_t* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint32_t x = v;
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) s_tmp[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    uint32_t w = lane < kWarps ? s_tmp[lane] : 0;
+    for (int o = 1; o < kWarps; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    if (lane < kWarps) s_tmp[lane] = w;  // inclusive warp totals
+  }
+  __syncthreads();
+  const uint32_t warp_prefix = warp ? s_tmp[warp - 1] : 0;
+  if (total) *total = s_tmp[kWarps - 1];
+  __syncthreads();
+  return warp_prefix + x - v;
+}
+
+// One stable LSD pass over 8 bits at `shift`.
+template <class Source>
+__global__ void __launch_bounds__(kThreads) sort_pass_kernel(
+    Source src, Count count, int shift, const uint32_t* __restrict__ pass_hist,
+    uint32_t* __restrict__ status, uint32_t* __restrict__ tile_counter,
+    uint32_t* __restrict__ keys_out, uint32_t* __restrict__ values_out,
+    uint32_t* __restrict__ error) {
+  __shared__ uint32_t s_warp_hist[kWarps][kRadix];
+  __shared__ uint32_t s_local_start[kRadix];
+  __shared__ uint32_t s_global_base[kRadix];
+  __shared__ uint32_t s_keys[kTile];
+  __shared__ uint32_t s_values[kTile];
+  __shared__ uint32_t s_tmp[kWarps];
+  __shared__ uint32_t s_block, s_total;
+
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) s_block = atomicAdd(tile_counter, 1u);
+  for (int i = threadIdx.x; i < kWarps * kRadix; i += kThreads) (&s_warp_hist[0][0])[i] = 0;
+  __syncthreads();
+  const uint32_t block = s_block;
+  const int64_t n = count.get();
+  const int64_t tile_start = static_cast<int64_t>(block) * kTile;
+  if (tile_start >= n) return;  // uniform: every later tile is empty too
+
+  // Rank: warp w owns keys [w*512, w*512+512) of the tile, 32 per step in
+  // order, so (step, lane) order is input order and ranks are stable.
+  uint32_t keys[kItems], values[kItems], ranks[kItems];
+  int digits[kItems];
+  const unsigned lt = lanemask_lt();
+#pragma unroll
+  for (int j = 0; j < kItems; ++j) {
+    const int64_t idx = tile_start + warp * (kItems * 32) + j * 32 + lane;
+    const bool ok = idx < n && src.valid(idx);
+    keys[j] = ok ? src.key(idx) : 0u;
+    values[j] = ok ? src.value(idx) : 0u;
+    digits[j] = ok ? static_cast<int>((keys[j] >> shift) & 0xFF) : kRadix;
+  }
+#pragma unroll
+  for (int j = 0; j < kItems; ++j) {
+    const int d = digits[j];
+    const unsigned peers = __match_any_sync(0xffffffffu, d);
+    const int leader = __ffs(peers) - 1;
+    uint32_t base = 0;
+    if (lane == leader && d < kRadix) {
+      base = s_warp_hist[warp][d];
+      s_warp_hist[warp][d] = base + __popc(peers);
+    }
+    base = __shfl_sync(0xffffffffu, base, leader);
+    ranks[j] = base + __popc(peers & lt);
+    __syncwarp();
+  }
+  __syncthreads();
+
+  // Per digit (thread d): warp offsets, block count, local start, global base.
+  const int d = threadIdx.x;
+  uint32_t block_count = 0;
+#pragma unroll
+  for (int w = 0; w < kWarps; ++w) {
+    const uint32_t c = s_warp_hist[w][d];
+    s_warp_hist[w][d] = block_count;
+    block_count += c;
+  }
+  uint32_t* my_status = status + static_cast<int64_t>(block) * kRadix + d;
+  st_volatile(my_status, (block == 0 ? kFlagPrefix : kFlagAggregate) | block_count);
+  uint32_t exclusive = 0;
+  if (block > 0) {
+    int64_t b = static_cast<int64_t>(block) - 1;
+    while (b >= 0) {
+      const uint32_t* s = status + b * kRadix + d;
+      uint32_t word = ld_volatile(s);
+      int spins = 0;
+      while ((word >> 30) == 0) {
+        if (++spins > kSpinLimit) {
+          atomicOr(error, kErrLookbackTimeout);
+          break;
+        }
+        if (spins > 64) __nanosleep(64);
+        word = ld_volatile(s);
+      }
+      exclusive += word & kValueMask;
+      if ((word >> 30) != 1) break;  // inclusive prefix found (or timed out)
+      --b;
+    }
+    st_volatile(my_status, kFlagPrefix | (exclusive + block_count));
+  }
+  // Global exclusive offset of digit d across the whole pass.
+  const uint32_t digit_start = block_exclusive_scan(pass_hist[d], s_tmp, nullptr);
+  s_global_base[d] = digit_start + exclusive;
+  s_local_start[d] = block_exclusive_scan(block_count, s_tmp, &s_total);
+  __syncthreads();
+
+  // Reorder the tile in shared memory by digit, then write runs coalesced.
+#pragma unroll
+  for (int j = 0; j < kItems; ++j) {
+    const int dj = digits[j];
+    if (dj < kRadix) {
+      const uint32_t pos = s_local_start[dj] + s_warp_hist[warp][dj] + ranks[j];
+      s_keys[pos] = keys[j];
+      s_values[pos] = values[j];
+    }
+  }
+  __syncthreads();
+  const uint32_t total = s_total;
+  for (uint32_t k = threadIdx.x; k < total; k += kThreads) {
+    const uint32_t key = s_keys[k];
+    const int dk = (key >> shift) & 0xFF;
+    const uint32_t out = s_global_base[dk] + (k - s_local_start[dk]);
+    if (keys_out) keys_out[out] = key;
+    values_out[out] = s_values[k];
+  }
+}
+
+// Exclusive prefix sum of counts[ids[j]] for j < V (decoupled look-back).
+// The last CTA writes the grand total.
+__global__ void __launch_bounds__(kThreads) count_scan_kernel(
+    const uint32_t* __restrict__ ids, const uint32_t* __restrict__ num_valid,
+    const int32_t* __restrict__ counts, uint64_t* __restrict__ status,
+    uint32_t* __restrict__ tile_counter, uint32_t* __restrict__ offsets,
+    int64_t* __restrict__ total_out, uint32_t* __restrict__ error) {
+  __shared__ uint32_t s_tmp[kWarps];
+  __shared__ uint32_t s_block;
+  __shared__ uint64_t s_exclusive;
+  if (threadIdx.x == 0) s_block = atomicAdd(tile_counter, 1u);
+  __syncthreads();
+  const uint32_t block = s_block;
+  const int64_t n = *num_valid;
+  const int64_t tile_start = static_cast<int64_t>(block) * kTile;
+  if (tile_start >= n) {
+    if (block == 0 && threadIdx.x == 0) *total_out = 0;
+    return;
+  }
+  // Thread t owns kItems consecutive elements.
+  uint32_t c[kItems];
+  uint32_t local = 0;
+  const int64_t base = tile_start + static_cast<int64_t>(threadIdx.x) * kItems;
+#pragma unroll
+  for (int j = 0; j < kItems; ++j) {
+    const int64_t idx = base + j;
+    c[j] = idx < n ? static_cast<uint32_t>(__ldg(counts + ids[idx])) : 0u;
+    local += c[j];
+  }
+  uint32_t block_total;
+  const uint32_t thread_prefix = block_exclusive_scan(local, s_tmp, &block_total);
+  if (threadIdx.x == 0) {
+    uint64_t* my_status = status + block;
+    st_volatile(my_status, (block == 0 ? kScanFlagPrefix : kScanFlagAggregate) | block_total);
+    uint64_t exclusive = 0;
+    if (block > 0) {
+      int64_t b = static_cast<int64_t>(block) - 1;
+      while (b >= 0) {
+        uint64_t word = ld_volatile(status + b);
+        int spins = 0;
+        while ((word >> 62) == 0) {
+          if (++spins > kSpinLimit) {
+            atomicOr(error, kErrLookbackTimeout);
+            break;
+          }
+          if (spins > 64) __nanosleep(64);
+          word = ld_volatile(status + b);
+        }
+        exclusive += word & kScanValueMask;
+        if ((word >> 62) != 1) break;
+        --b;
+      }
+      st_volatile(my_status, kScanFlagPrefix | (exclusive + block_total));
+    }
+    s_exclusive = exclusive;
+    if (tile_start + kTile >= n) *total_out = static_cast<int64_t>(exclusive + block_total);
+  }
+  __syncthreads();
+  // Offsets are stored as 32 bits; totals of 2^30 and more are rejected on
+  // the host before anything reads them.
+  uint32_t run = static_cast<uint32_t>(s_exclusive) + thread_prefix;
+#pragma unroll
+  for (int j = 0; j < kItems; ++j) {
+    const int64_t idx = base + j;
+    if (idx < n) offsets[idx] = run;
+    run += c[j];
+  }
+}
+
+// Writes every (tile, Gaussian) pair of the depth-ordered Gaussians. A warp
+// handles 32 consecutive Gaussians, whose outputs form one contiguous range;
+// lanes stride over that range (each output finds its Gaussian by binary
+// search over the warp's prefix sums), so writes are coalesced and a Gaussian
+// covering many tiles is spread across the warp.
+__global__ void __launch_bounds__(kThreads) emit_kernel(
+    const uint32_t* __restrict__ sorted_ids, const uint32_t* __restrict__ num_valid,
+    const uint32_t* __restrict__ offsets, const int32_t* __restrict__ counts,
+    const int4* __restrict__ bounds, int tiles_w, uint32_t* __restrict__ tile_keys,
+    uint32_t* __restrict__ values) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp_first = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) - lane;
+  const int64_t n = *num_valid;
+  if (warp_first >= n) return;  // uniform per warp
+  const int64_t j = warp_first + lane;
+  const bool ok = j < n;
+  const uint32_t g = ok ? sorted_ids[j] : 0u;
+  const int4 b = ok ? __ldg(bounds + g) : make_int4(0, 1, 0, 0);
+  const uint32_t cnt = ok ? static_cast<uint32_t>(__ldg(counts + g)) : 0u;
+  uint32_t incl = cnt;
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  const uint32_t excl = incl - cnt;
+  const uint32_t total = __shfl_sync(0xffffffffu, incl, 31);
+  const uint32_t out0 = __shfl_sync(0xffffffffu, ok ? offsets[j] : 0u, 0);
+  const int width = b.y - b.x;
+  for (uint32_t r = 0; r < total; r += 32) {
+    const uint32_t o = r + lane;
+    // Largest source lane s with excl[s] <= o (lanes with cnt 0 share excl
+    // with the next lane; taking the largest lands on one with cnt > 0).
+    int s = 0;
+#pragma unroll
+    for (int step = 16; step > 0; step >>= 1) {
+      const uint32_t e = __shfl_sync(0xffffffffu, excl, s + step);
+      if (e <= o) s += step;
+    }
+    const uint32_t src_excl = __shfl_sync(0xffffffffu, excl, s);
+    const uint32_t src_g = __shfl_sync(0xffffffffu, g, s);
+    const int src_xmin = __shfl_sync(0xffffffffu, b.x, s);
+    const int src_ymin = __shfl_sync(0xffffffffu, b.z, s);
+    const int src_width = __shfl_sync(0xffffffffu, width, s);
+    if (o < total) {
+      const int local = static_cast<int>(o - src_excl);
+      const int tile = (src_ymin + local / src_width) * tiles_w + src_xmin + local % src_width;
+      tile_keys[out0 + o] = static_cast<uint32_t>(tile);
+      values[out0 + o] = src_g;
+    }
+  }
+}
+
+// ranges[t] = [lower_bound(t), lower_bound(t + 1)) over the sorted tile keys.
+__global__ void ranges_kernel(const uint32_t* __restrict__ sorted_keys, int64_t total,
+                              int64_t num_tiles, int64_t* __restrict__ ranges) {
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (t >= num_tiles) return;
+  auto lower_bound = [&](uint64_t value) {
+    int64_t lo = 0, hi = total;
+    while (lo < hi) {
+      const int64_t mid = (lo + hi) >> 1;
+      if (sorted_keys[mid] < value) lo = mid + 1; else hi = mid;
+    }
+    return lo;
+  };
+  ranges[2 * t] = lower_bound(static_cast<uint64_t>(t));
+  ranges[2 * t + 1] = lower_bound(static_cast<uint64_t>(t) + 1);
+}
+
+// ---------------------------------------------------------------- workspaces
+
+constexpr uint64_t kAlign = 256;
+inline uint64_t align_up(uint64_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
+
+// Counters and flags that must start at zero (zeroed with the status words).
+struct BinHeader {
+  uint32_t hist[4][kRadix];
+  uint32_t num_valid;
+  uint32_t pass_counters[4];
+  uint32_t scan_counter;
+  uint32_t error;
+  uint32_t pad_;
+  int64_t total;
+};
+
+struct CountLayout {
+  uint64_t header, depth_status, scan_status, zero_bytes;
+  uint64_t keys_a, keys_b, ids_a, ids_b, offsets, bytes;
+  explicit CountLayout(int64_t n) {
+    const uint64_t blocks = (n + kTile - 1) / kTile;
+    uint64_t at = 0;
+    header = at; at = align_up(at + sizeof(BinHeader));
+    depth_status = at; at = align_up(at + blocks * kRadix * 4 * 4);
+    scan_status = at; at = align_up(at + blocks * 8);
+    zero_bytes = at;
+    keys_a = at; at = align_up(at + 4 * static_cast<uint64_t>(n));
+    keys_b = at; at = align_up(at + 4 * static_cast<uint64_t>(n));
+    ids_a = at; at = align_up(at + 4 * static_cast<uint64_t>(n));
+    ids_b = at; at = align_up(at + 4 * static_cast<uint64_t>(n));
+    offsets = at; at = align_up(at + 4 * static_cast<uint64_t>(n));
+    bytes = at;
+  }
+};
+
+inline int tile_bits(int64_t num_tiles) {
+  int bits = 0;
+  while ((int64_t{1} << bits) < num_tiles) ++bits;
+  return bits;
+}
+
+struct SortLayout {
+  uint64_t header, status, zero_bytes, keys_a, keys_b, values_a, values_b, bytes;
+  int passes;
+  SortLayout(int64_t total, int64_t num_tiles) {
+    passes = (tile_bits(num_tiles) + 7) / 8;
+    const uint64_t blocks = (total + kTile - 1) / kTile;
+    uint64_t at = 0;
+    header = at; at = align_up(at + sizeof(BinHeader));
+    status = at; at = align_up(at + blocks * kRadix * 4 * (passes ? passes : 1));
+    zero_bytes = at;
+    keys_a = at; at = align_up(at + 4 * static_cast<uint64_t>(total));
+    keys_b = at; at = align_up(at + 4 * static_cast<uint64_t>(total));
+    values_a = at; at = align_up(at + 4 * static_cast<uint64_t>(total));
+    values_b = at; at = align_up(at + 4 * static_cast<uint64_t>(total));
+    bytes = at;
+  }
+};
+
+template <class T>
+T* at(void* base, uint64_t offset) {
+  return reinterpret_cast<T*>(static_cast<char*>(base) + offset);
+}
+template <class T>
+const T* at(const void* base, uint64_t offset) {
+  return reinterpret_cast<const T*>(static_cast<const char*>(base) + offset);
+}
+
+inline unsigned upsweep_blocks(int64_t n) {
+  const int64_t want = (n + kThreads * 8 - 1) / (kThreads * 8);
+  return static_cast<unsigned>(want < 4 * kSmCount ? (want > 0 ? want : 1) : 4 * kSmCount);
+}
+
+}  // namespace
+
+uint64_t bin_count_workspace_size(int64_t n) { return CountLayout(n).bytes; }
+uint64_t bin_sort_workspace_size(int64_t total, int64_t num_tiles) {
+  return SortLayout(total, num_tiles).bytes;
+}
+
+// Where the depth-sorted Gaussian ids end up after the 4 passes.
+static uint64_t sorted_ids_offset(const CountLayout& L) { return L.ids_a; }
+
+int32_t launch_bin_count(int64_t n, const float* projected_mean, const int32_t* counts,
+                         void* workspace, int64_t* total_host, uint32_t* error_host,
+                         cudaStream_t stream) {
+  const CountLayout L(n);
+  BinHeader* h = at<BinHeader>(workspace, L.header);
+  GS_CUDA_TRY(cudaMemsetAsync(workspace, 0, L.zero_bytes, stream));
+  if (n > 0) {
+    const int64_t blocks = (n + kTile - 1) / kTile;
+    upsweep_kernel<<<upsweep_blocks(n), kThreads, 0, stream>>>(
+        DepthSource{projected_mean, counts}, n, 4, 0, &h->hist[0][0], &h->num_valid);
+    GS_TRY(check_launch());
+    uint32_t* depth_status = at<uint32_t>(workspace, L.depth_status);
+    uint32_t* kA = at<uint32_t>(workspace, L.keys_a);
+    uint32_t* kB = at<uint32_t>(workspace, L.keys_b);
+    uint32_t* vA = at<uint32_t>(workspace, L.ids_a);
+    uint32_t* vB = at<uint32_t>(workspace, L.ids_b);
+    // Pass 0 filters and reads the projection outputs directly; passes 1-3
+    // ping-pong A -> B -> A so the ids finish in ids_a.
+    sort_pass_kernel<<<blocks, kThreads, 0, stream>>>(
+        DepthSource{projected_mean, counts}, Count{n, nullptr}, 0, &h->hist[0][0], depth_status,
+        &h->pass_counters[0], kB, vB, &h->error);
+    GS_TRY(check_launch());
+    uint32_t* ins_k[3] = {kB, kA, kB};
+    uint32_t* ins_v[3] = {vB, vA, vB};
+    uint32_t* outs_k[3] = {kA, kB, nullptr};
+    uint32_t* outs_v[3] = {vA, vB, vA};
+    for (int p = 1; p < 4; ++p) {
+      sort_pass_kernel<<<blocks, kThreads, 0, stream>>>(
+          ArraySource{ins_k[p - 1], ins_v[p - 1]}, Count{0, &h->num_valid}, 8 * p,
+          &h->hist[p][0], depth_status + static_cast<int64_t>(p) * blocks * kRadix,
+          &h->pass_counters[p], outs_k[p - 1], outs_v[p - 1], &h->error);
+      GS_TRY(check_launch());
+    }
+    count_scan_kernel<<<blocks, kThreads, 0, stream>>>(
+        at<uint32_t>(workspace, sorted_ids_offset(L)), &h->num_valid, counts,
+        at<uint64_t>(workspace, L.scan_status), &h->scan_counter,
+        at<uint32_t>(workspace, L.offsets), &h->total, &h->error);
+    GS_TRY(check_launch());
+  }
+  int64_t result[2];
+  GS_CUDA_TRY(cudaMemcpyAsync(result, &h->total, sizeof(int64_t), cudaMemcpyDeviceToHost, stream));
+  GS_CUDA_TRY(cudaMemcpyAsync(error_host, &h->error, sizeof(uint32_t), cudaMemcpyDeviceToHost,
+                              stream));
+  GS_CUDA_TRY(cudaStreamSynchronize(stream));
+  *total_host = result[0];
+  return GS_OK;
+}
+
+int32_t launch_bin_sort(int64_t n, int64_t total, const int32_t* bounds, const int32_t* counts,
+                        const gs_params& p, const void* count_workspace, void* sort_workspace,
+                        int32_t* gaussian_ids, int64_t* ranges, cudaStream_t stream) {
+  const CountLayout C(n);
+  const int64_t tiles_w = p.width / p.tile_size;
+  const int64_t num_tiles = tiles_w * (p.height / p.tile_size);
+  const SortLayout L(total, num_tiles);
+  const BinHeader* ch = at<BinHeader>(count_workspace, C.header);
+  BinHeader* h = at<BinHeader>(sort_workspace, L.header);
+  GS_CUDA_TRY(cudaMemsetAsync(sort_workspace, 0, L.zero_bytes, stream));
+  uint32_t* kA = at<uint32_t>(sort_workspace, L.keys_a);
+  uint32_t* kB = at<uint32_t>(sort_workspace, L.keys_b);
+  uint32_t* vA = at<uint32_t>(sort_workspace, L.values_a);
+  uint32_t* vB = at<uint32_t>(sort_workspace, L.values_b);
+  uint32_t* out_ids = reinterpret_cast<uint32_t*>(gaussian_ids);
+  const uint32_t* sorted_keys = kA;
+  if (total > 0) {
+    const int passes = L.passes;
+    emit_kernel<<<ceil_div(n, kThreads), kThreads, 0, stream>>>(
+        at<uint32_t>(count_workspace, sorted_ids_offset(C)), &ch->num_valid,
+        at<uint32_t>(count_workspace, C.offsets), counts, reinterpret_cast<const int4*>(bounds),
+        static_cast<int>(tiles_w), kA, passes == 0 ? out_ids : vA);
+    GS_TRY(check_launch());
+    if (passes > 0) {
+      upsweep_kernel<<<upsweep_blocks(total), kThreads, 0, stream>>>(
+          ArraySource{kA, vA}, total, passes, 0, &h->hist[0][0], nullptr);
+      GS_TRY(check_launch());
+      const int64_t blocks = (total + kTile - 1) / kTile;
+      uint32_t* src_k = kA;
+      uint32_t* src_v = vA;
+      for (int pass = 0; pass < passes; ++pass) {
+        uint32_t* dst_k = (pass % 2 == 0) ? kB : kA;
+        uint32_t* dst_v = (pass == passes - 1) ? out_ids : ((pass % 2 == 0) ? vB : vA);
+        sort_pass_kernel<<<blocks, kThreads, 0, stream>>>(
+            ArraySource{src_k, src_v}, Count{total, nullptr}, 8 * pass, &h->hist[pass][0],
+            at<uint32_t>(sort_workspace, L.status) + static_cast<int64_t>(pass) * blocks * kRadix,
+            &h->pass_counters[pass], dst_k, dst_v, &h->error);
+        GS_TRY(check_launch());
+        src_k = dst_k;
+        src_v = dst_v;
+      }
+      sorted_keys = src_k;
+    }
+  }
+  if (num_tiles > 0) {
+    ranges_kernel<<<ceil_div(num_tiles, 256), 256, 0, stream>>>(sorted_keys, total, num_tiles,
+                                                               ranges);
+    GS_TRY(check_launch());
+  }
+  return GS_OK;
+}
+
+// Error word of the last binning on this workspace pair (sync-free read is
+// the caller's job; 0 = no look-back ever timed out).
+uint64_t bin_error_word_offset() { return offsetof(BinHeader, error); }
+
+}  // namespace gs

@@ -1,0 +1,202 @@
+// extern "C" entry points declared in include/gs_b200.h: argument checks,
+// then the stage launchers.
+#include <cstdint>
+#include <cstdio>
+
+#include "common.cuh"
+
+namespace gs {
+
+int32_t launch_project_fwd(int64_t, int32_t, const float*, const float*, const float*,
+                           const float*, const float*, const float*, const float*,
+                           const gs_params&, float*, float*, float*, float*, int32_t*, int32_t*,
+                           cudaStream_t);
+int32_t launch_project_bwd(int64_t, int32_t, const float*, const float*, const float*,
+                           const float*, const float*, const float*, const float*, const float*,
+                           const float*, const int32_t*, const gs_params&, float*, float*, float*,
+                           float*, float*, cudaStream_t);
+int32_t launch_det_math(int, int64_t, const float*, float*, cudaStream_t);
+uint64_t bin_count_workspace_size(int64_t);
+uint64_t bin_sort_workspace_size(int64_t, int64_t);
+uint64_t bin_error_word_offset();
+int32_t launch_bin_count(int64_t, const float*, const int32_t*, void*, int64_t*, uint32_t*,
+                         cudaStream_t);
+int32_t launch_bin_sort(int64_t, int64_t, const int32_t*, const int32_t*, const gs_params&,
+                        const void*, void*, int32_t*, int64_t*, cudaStream_t);
+int32_t launch_composite_fwd(const float*, const float*, const float*, const float*,
+                             const int32_t*, const int64_t*, const gs_params&, float*, float*,
+                             int32_t*, cudaStream_t);
+int32_t launch_composite_bwd(int64_t, const float*, const float*, const float*, const float*,
+                             const int32_t*, const int64_t*, const float*, const float*,
+                             const int32_t*, const gs_params&, float*, cudaStream_t);
+
+namespace {
+thread_local int32_t g_last_cuda_error = 0;
+
+bool aligned(const void* ptr, uintptr_t bytes) {
+  return (reinterpret_cast<uintptr_t>(ptr) % bytes) == 0;
+}
+
+bool valid_sh(int32_t num_sh) {
+  return num_sh == 1 || num_sh == 4 || num_sh == 9 || num_sh == 16 || num_sh == 25;
+}
+
+int32_t check_params(const gs_params* p) {
+  if (!p) return GS_ERR_INVALID_ARGUMENT;
+  const int ts = p->tile_size;
+  if (ts != 4 && ts != 8 && ts != 16 && ts != 32) return GS_ERR_INVALID_ARGUMENT;
+  if (p->width < 0 || p->height < 0 || p->width % ts || p->height % ts)
+    return GS_ERR_INVALID_ARGUMENT;
+  return GS_OK;
+}
+
+// Gaussian index and intersection offsets are 32-bit in the binning kernels.
+constexpr int64_t kMaxGaussians = int64_t{1} << 30;
+constexpr int64_t kMaxIntersections = int64_t{1} << 30;
+}  // namespace
+
+void set_cuda_error(cudaError_t err) { g_last_cuda_error = static_cast<int32_t>(err); }
+
+}  // namespace gs
+
+using gs::as_cuda;
+
+extern "C" {
+
+int32_t gs_version(void) { return 100; }
+
+int32_t gs_last_cuda_error(void) { return gs::g_last_cuda_error; }
+
+int32_t gs_project_fwd(int64_t n, int32_t num_sh, const float* mean, const float* rotation,
+                       const float* scale, const float* opacity, const float* color,
+                       const float* camera_rotation, const float* camera_translation,
+                       const gs_params* params, float* projected_mean, float* inverse_covariance,
+                       float* projected_color, float* projected_opacity, int32_t* bounds,
+                       int32_t* counts, gs_stream_t stream) {
+  GS_TRY(gs::check_params(params));
+  if (n < 0 || n >= gs::kMaxGaussians) return GS_ERR_INVALID_ARGUMENT;
+  if (!gs::valid_sh(num_sh)) return num_sh > 25 ? GS_ERR_UNSUPPORTED : GS_ERR_INVALID_ARGUMENT;
+  if (!gs::aligned(rotation, 16) || !gs::aligned(inverse_covariance, 16) ||
+      !gs::aligned(bounds, 16) || ((num_sh == 4 || num_sh == 16) && !gs::aligned(color, 16)))
+    return GS_ERR_MISALIGNED;
+  return gs::launch_project_fwd(n, num_sh, mean, rotation, scale, opacity, color, camera_rotation,
+                                camera_translation, *params, projected_mean, inverse_covariance,
+                                projected_color, projected_opacity, bounds, counts,
+                                as_cuda(stream));
+}
+
+uint64_t gs_bin_count_workspace_size(int64_t n) {
+  return gs::bin_count_workspace_size(n < 0 ? 0 : n);
+}
+
+uint64_t gs_bin_sort_workspace_size(int64_t total, int64_t num_tiles) {
+  return gs::bin_sort_workspace_size(total < 0 ? 0 : total, num_tiles < 0 ? 0 : num_tiles);
+}
+
+int32_t gs_bin_count(int64_t n, const float* projected_mean, const int32_t* counts,
+                     void* workspace, uint64_t workspace_bytes, int64_t* total_host,
+                     gs_stream_t stream) {
+  if (n < 0 || n >= gs::kMaxGaussians || !total_host) return GS_ERR_INVALID_ARGUMENT;
+  if (workspace_bytes < gs::bin_count_workspace_size(n)) return GS_ERR_INVALID_ARGUMENT;
+  if (!gs::aligned(workspace, 256)) return GS_ERR_MISALIGNED;
+  uint32_t error = 0;
+  GS_TRY(gs::launch_bin_count(n, projected_mean, counts, workspace, total_host, &error,
+                              as_cuda(stream)));
+  if (error) return GS_ERR_TIMEOUT;
+  if (*total_host >= gs::kMaxIntersections) return GS_ERR_CAPACITY;
+  return GS_OK;
+}
+
+int32_t gs_bin_sort(int64_t n, int64_t total, const int32_t* bounds, const int32_t* counts,
+                    const gs_params* params, const void* count_workspace,
+                    uint64_t count_workspace_bytes, void* sort_workspace,
+                    uint64_t sort_workspace_bytes, int32_t* gaussian_ids, int64_t* ranges,
+                    gs_stream_t stream) {
+  GS_TRY(gs::check_params(params));
+  if (n < 0 || n >= gs::kMaxGaussians || total < 0) return GS_ERR_INVALID_ARGUMENT;
+  if (total >= gs::kMaxIntersections) return GS_ERR_CAPACITY;
+  const int64_t num_tiles = static_cast<int64_t>(params->width / params->tile_size) *
+                            (params->height / params->tile_size);
+  if (count_workspace_bytes < gs::bin_count_workspace_size(n) ||
+      sort_workspace_bytes < gs::bin_sort_workspace_size(total, num_tiles))
+    return GS_ERR_INVALID_ARGUMENT;
+  if (!gs::aligned(count_workspace, 256) || !gs::aligned(sort_workspace, 256) ||
+      !gs::aligned(bounds, 16))
+    return GS_ERR_MISALIGNED;
+  return gs::launch_bin_sort(n, total, bounds, counts, *params, count_workspace, sort_workspace,
+                             gaussian_ids, ranges, as_cuda(stream));
+}
+
+int32_t gs_bin_check(const void* count_workspace, const void* sort_workspace,
+                     gs_stream_t stream) {
+  uint32_t words[2] = {0, 0};
+  const uint64_t off = gs::bin_error_word_offset();
+  if (count_workspace)
+    GS_CUDA_TRY(cudaMemcpyAsync(&words[0], static_cast<const char*>(count_workspace) + off, 4,
+                                cudaMemcpyDeviceToHost, as_cuda(stream)));
+  if (sort_workspace)
+    GS_CUDA_TRY(cudaMemcpyAsync(&words[1], static_cast<const char*>(sort_workspace) + off, 4,
+                                cudaMemcpyDeviceToHost, as_cuda(stream)));
+  GS_CUDA_TRY(cudaStreamSynchronize(as_cuda(stream)));
+  return (words[0] | words[1]) ? GS_ERR_TIMEOUT : GS_OK;
+}
+
+int32_t gs_composite_fwd(const float* projected_mean, const float* inverse_covariance,
+                         const float* projected_color, const float* projected_opacity,
+                         const int32_t* gaussian_ids, const int64_t* ranges,
+                         const gs_params* params, float* image, float* final_transmittance,
+                         int32_t* n_contributors, gs_stream_t stream) {
+  GS_TRY(gs::check_params(params));
+  if (!gs::aligned(inverse_covariance, 16)) return GS_ERR_MISALIGNED;
+  return gs::launch_composite_fwd(projected_mean, inverse_covariance, projected_color,
+                                  projected_opacity, gaussian_ids, ranges, *params, image,
+                                  final_transmittance, n_contributors, as_cuda(stream));
+}
+
+int32_t gs_composite_bwd(int64_t n, const float* projected_mean, const float* inverse_covariance,
+                         const float* projected_color, const float* projected_opacity,
+                         const int32_t* gaussian_ids, const int64_t* ranges,
+                         const float* grad_image, const float* final_transmittance,
+                         const int32_t* n_contributors, const gs_params* params,
+                         float* grad_projected, gs_stream_t stream) {
+  GS_TRY(gs::check_params(params));
+  if (n < 0) return GS_ERR_INVALID_ARGUMENT;
+  if (!params->gaussian_mode) return GS_ERR_UNSUPPORTED;  // interface.py:184-186
+  if (!gs::aligned(inverse_covariance, 16)) return GS_ERR_MISALIGNED;
+  return gs::launch_composite_bwd(n, projected_mean, inverse_covariance, projected_color,
+                                  projected_opacity, gaussian_ids, ranges, grad_image,
+                                  final_transmittance, n_contributors, *params, grad_projected,
+                                  as_cuda(stream));
+}
+
+int32_t gs_project_bwd(int64_t n, int32_t num_sh, const float* mean, const float* rotation,
+                       const float* scale, const float* opacity, const float* color,
+                       const float* camera_rotation, const float* camera_translation,
+                       const float* inverse_covariance, const float* grad_projected,
+                       const int32_t* counts, const gs_params* params, float* grad_mean,
+                       float* grad_rotation, float* grad_scale, float* grad_opacity,
+                       float* grad_color, gs_stream_t stream) {
+  GS_TRY(gs::check_params(params));
+  if (n < 0 || n >= gs::kMaxGaussians) return GS_ERR_INVALID_ARGUMENT;
+  if (!gs::valid_sh(num_sh)) return num_sh > 25 ? GS_ERR_UNSUPPORTED : GS_ERR_INVALID_ARGUMENT;
+  if (!gs::aligned(rotation, 16) || !gs::aligned(inverse_covariance, 16) ||
+      !gs::aligned(grad_rotation, 16) ||
+      ((num_sh == 4 || num_sh == 16) && !gs::aligned(color, 16)))
+    return GS_ERR_MISALIGNED;
+  return gs::launch_project_bwd(n, num_sh, mean, rotation, scale, opacity, color,
+                                camera_rotation, camera_translation, inverse_covariance,
+                                grad_projected, counts, *params, grad_mean, grad_rotation,
+                                grad_scale, grad_opacity, grad_color, as_cuda(stream));
+}
+
+int32_t gs_det_exp(int64_t n, const float* x, float* y, gs_stream_t stream) {
+  if (n < 0) return GS_ERR_INVALID_ARGUMENT;
+  return gs::launch_det_math(0, n, x, y, as_cuda(stream));
+}
+
+int32_t gs_det_log(int64_t n, const float* x, float* y, gs_stream_t stream) {
+  if (n < 0) return GS_ERR_INVALID_ARGUMENT;
+  return gs::launch_det_math(1, n, x, y, as_cuda(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,63 @@
+// Shared definitions for the rasterizer kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "../../include/gs_b200.h"
+#include "detmath.cuh"
+
+namespace gs {
+
+constexpr float kAlphaMin = 1.0f / 255.0f;  // composite.py:170, composite_bwd.py:121
+constexpr float kAlphaMax = 0.99f;           // composite.py:169
+constexpr int kSmCount = 148;                // B200: 2 dies x 74 SMs
+
+// Records the last CUDA error for gs_last_cuda_error(); defined in capi.cu.
+void set_cuda_error(cudaError_t err);
+
+inline int32_t check_launch() {
+  cudaError_t err = cudaGetLastError();
+  if (err != cudaSuccess) {
+    set_cuda_error(err);
+    return GS_ERR_CUDA;
+  }
+  return GS_OK;
+}
+
+#define GS_CUDA_TRY(expr)                    \
+  do {                                       \
+    cudaError_t gs_err_ = (expr);            \
+    if (gs_err_ != cudaSuccess) {            \
+      ::gs::set_cuda_error(gs_err_);         \
+      return GS_ERR_CUDA;                    \
+    }                                        \
+  } while (0)
+
+#define GS_TRY(expr)                         \
+  do {                                       \
+    int32_t gs_status_ = (expr);             \
+    if (gs_status_ != GS_OK) return gs_status_; \
+  } while (0)
+
+inline cudaStream_t as_cuda(gs_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
+
+inline unsigned ceil_div(int64_t a, int64_t b) { return static_cast<unsigned>((a + b - 1) / b); }
+
+// Pair evaluation shared by the forward and backward compositors:
+// d^2 = xx dx^2 + 2 xy dx dy + yy dy^2 with integer pixel coordinates
+// (composite.py:159-161), evaluated as fmaf(xx*dx, dx, fmaf((2xy)*dx, dy, (yy*dy)*dy)).
+__device__ __forceinline__ float pair_d2(float dx, float dy, float xx, float xy2, float yy) {
+  return fmaf(xx * dx, dx, fmaf(xy2 * dx, dy, (yy * dy) * dy));
+}
+
+// d^2 above which alpha = min(o e^{-d^2/2}, 0.99) is certainly below 1/255
+// (given det_exp's < 1 ulp error): 2 log(255 o) plus a 1e-3 margin that
+// dwarfs the rounding of this bound. Pairs beyond it leave T and C unchanged,
+// so skipping them is exact. Ellipsoid mode uses its own cutoff directly.
+__device__ __forceinline__ float skip_cutoff(float opacity, const gs_params& p) {
+  return p.gaussian_mode ? fmaf(2.0f, det_log(opacity * 255.0f), 1e-3f) : p.cutoff;
+}
+
+}  // namespace gs

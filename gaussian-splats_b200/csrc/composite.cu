@@ -1,0 +1,302 @@
+// Per-tile alpha compositing, forward and backward.
+//
+// One CTA per tile, one thread per pixel (TS x TS threads). The tile's list
+// of Gaussians -- ids[start:end), front to back -- is staged into shared
+// memory in batches of TS*TS entries (one entry per thread: a gather of the
+// projected mean, conic, opacity and colour), and every pixel then walks the
+// batch from shared memory. The work is FP32 arithmetic per (pixel, Gaussian)
+// pair; nothing here is a dense contraction, so tensor cores have no role.
+//
+// Forward (composite.py:25-107). Per pair:
+//   d2 = fmaf(xx dx, dx, fmaf(2xy dx, dy, (yy dy) dy)),  p = exp(-d2/2),
+//   alpha = min(o p, 0.99), alpha < 1/255 -> 0, C += T alpha c, T *= 1 - alpha
+// while the pixel is active ((1 - T) < threshold). Pairs with
+// d2 > skip_cutoff(o) have alpha = 0 and change nothing, so they are skipped
+// before the exp. A pixel's contributor count is the number of list entries
+// it saw while active, i.e. (index of the entry that ended it) + 1, or the
+// list length if it never ended; the tile stops once every pixel has ended
+// (composite.py:187-188).
+//
+// Backward (composite_bwd.py:47-277). Walks the list back to front from
+// start + max(n_contributors); a running suffix per pixel (transmittance
+// product and composited colour of the entries behind) replaces the
+// reference's chunked associative scan; T at an entry is recovered as
+// final_T / max(suffix_T (1 - alpha), 1e-4) and the termination test is
+// re-evaluated on it, as the reference does. Each warp sums its 32 pixels'
+// 9-vector per entry with shuffles (skipped when no lane contributes) and
+// adds it to grad_projected[g] with one atomic per component.
+#include "common.cuh"
+
+namespace gs {
+namespace {
+
+template <int TS>
+struct TileShape {
+  static constexpr int kPixels = TS * TS;
+  static constexpr int kBatch = kPixels < 256 ? kPixels : 256;  // list entries staged at once
+  static constexpr int kWarpLanes = kPixels < 32 ? kPixels : 32;
+  static constexpr unsigned kWarpMask = kPixels < 32 ? ((1u << kPixels) - 1u) : 0xffffffffu;
+};
+
+// Gathers entry k of the sorted list into the shared-memory batch slot.
+struct Staged {
+  float4 a;  // mean_x, mean_y, conic_xx, 2 conic_xy
+  float4 b;  // conic_yy, opacity, skip cutoff, conic_xy
+  float4 c;  // r, g, b, gaussian id (bits)
+};
+
+__device__ __forceinline__ Staged stage_entry(int32_t g, const float* __restrict__ projected_mean,
+                                              const float* __restrict__ inverse_covariance,
+                                              const float* __restrict__ projected_color,
+                                              const float* __restrict__ projected_opacity,
+                                              const gs_params& p) {
+  const float mx = __ldg(projected_mean + 3 * static_cast<int64_t>(g));
+  const float my = __ldg(projected_mean + 3 * static_cast<int64_t>(g) + 1);
+  const float4 conic = __ldg(reinterpret_cast<const float4*>(inverse_covariance) + g);
+  const float o = __ldg(projected_opacity + g);
+  const float r = __ldg(projected_color + 3 * static_cast<int64_t>(g));
+  const float gg = __ldg(projected_color + 3 * static_cast<int64_t>(g) + 1);
+  const float b = __ldg(projected_color + 3 * static_cast<int64_t>(g) + 2);
+  Staged s;
+  s.a = make_float4(mx, my, conic.x, 2.0f * conic.y);
+  s.b = make_float4(conic.w, o, skip_cutoff(o, p), conic.y);
+  s.c = make_float4(r, gg, b, __int_as_float(g));
+  return s;
+}
+
+template <int TS>
+__global__ void __launch_bounds__(TS * TS) composite_fwd_kernel(
+    const float* __restrict__ projected_mean, const float* __restrict__ inverse_covariance,
+    const float* __restrict__ projected_color, const float* __restrict__ projected_opacity,
+    const int32_t* __restrict__ gaussian_ids, const int64_t* __restrict__ ranges,
+    const gs_params p, float* __restrict__ image, float* __restrict__ final_transmittance,
+    int32_t* __restrict__ n_contributors) {
+  constexpr int NB = TileShape<TS>::kBatch;
+  __shared__ float4 s_a[NB];
+  __shared__ float4 s_b[NB];
+  __shared__ float4 s_c[NB];
+  const int tile = blockIdx.x;
+  const int tiles_w = p.width / TS;
+  const int tid = threadIdx.x;
+  const int px = (tile % tiles_w) * TS + tid % TS;
+  const int py = (tile / tiles_w) * TS + tid / TS;
+  const float fpx = static_cast<float>(px), fpy = static_cast<float>(py);
+  const int64_t start = ranges[2 * tile], end = ranges[2 * tile + 1];
+  const float threshold = p.opacity_threshold;
+  const bool gaussian = p.gaussian_mode != 0;
+
+  float T = 1.0f, cr = 0.0f, cg = 0.0f, cb = 0.0f;
+  bool done = !((1.0f - T) < threshold);
+  int64_t contrib = 0;
+  for (int64_t batch = start; batch < end; batch += NB) {
+    const int64_t k = batch + tid;
+    if (tid < NB && k < end) {
+      const Staged s = stage_entry(__ldg(gaussian_ids + k), projected_mean, inverse_covariance,
+                                   projected_color, projected_opacity, p);
+      s_a[tid] = s.a;
+      s_b[tid] = s.b;
+      s_c[tid] = s.c;
+    }
+    __syncthreads();
+    if (!done) {
+      const int count = static_cast<int>(end - batch < NB ? end - batch : NB);
+      for (int j = 0; j < count; ++j) {
+        const float4 a = s_a[j];
+        const float4 b = s_b[j];
+        const float dx = fpx - a.x, dy = fpy - a.y;
+        const float d2 = pair_d2(dx, dy, a.z, a.w, b.x);
+        if (!(d2 <= b.z)) continue;
+        float alpha;
+        if (gaussian) {
+          const float prob = d2 >= 0.0f ? det_exp_nonpositive(-0.5f * d2) : det_exp(-0.5f * d2);
+          alpha = fminf(b.y * prob, kAlphaMax);
+        } else {
+          alpha = fminf(b.y, kAlphaMax);
+        }
+        if (!(alpha >= kAlphaMin)) continue;
+        const float4 c = s_c[j];
+        const float weight = T * alpha;
+        cr = fmaf(weight, c.x, cr);
+        cg = fmaf(weight, c.y, cg);
+        cb = fmaf(weight, c.z, cb);
+        T = T * (1.0f - alpha);
+        if (!((1.0f - T) < threshold)) {
+          done = true;
+          contrib = batch + j + 1 - start;
+          break;
+        }
+      }
+    }
+    if (__syncthreads_count(!done) == 0) break;
+  }
+  if (!done) contrib = end - start;
+  const int64_t pix = static_cast<int64_t>(py) * p.width + px;
+  image[3 * pix] = cr;
+  image[3 * pix + 1] = cg;
+  image[3 * pix + 2] = cb;
+  final_transmittance[pix] = T;
+  n_contributors[pix] = static_cast<int32_t>(contrib);
+}
+
+template <int TS>
+__global__ void __launch_bounds__(TS * TS) composite_bwd_kernel(
+    const float* __restrict__ projected_mean, const float* __restrict__ inverse_covariance,
+    const float* __restrict__ projected_color, const float* __restrict__ projected_opacity,
+    const int32_t* __restrict__ gaussian_ids, const int64_t* __restrict__ ranges,
+    const float* __restrict__ grad_image, const float* __restrict__ final_transmittance,
+    const int32_t* __restrict__ n_contributors, const gs_params p,
+    float* __restrict__ grad_projected) {
+  using Shape = TileShape<TS>;
+  constexpr int NB = Shape::kBatch;
+  constexpr unsigned kMask = Shape::kWarpMask;
+  __shared__ float4 s_a[NB];
+  __shared__ float4 s_b[NB];
+  __shared__ float4 s_c[NB];
+  __shared__ int s_max_contrib;
+  const int tile = blockIdx.x;
+  const int tiles_w = p.width / TS;
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int px = (tile % tiles_w) * TS + tid % TS;
+  const int py = (tile / tiles_w) * TS + tid / TS;
+  const float fpx = static_cast<float>(px), fpy = static_cast<float>(py);
+  const int64_t pix = static_cast<int64_t>(py) * p.width + px;
+  const float threshold = p.opacity_threshold;
+  const float gr = __ldg(grad_image + 3 * pix), gg = __ldg(grad_image + 3 * pix + 1),
+              gb = __ldg(grad_image + 3 * pix + 2);
+  const float t_final = __ldg(final_transmittance + pix);
+  const int contrib = __ldg(n_contributors + pix);
+  if (tid == 0) s_max_contrib = 0;
+  __syncthreads();
+  const int warp_max = __reduce_max_sync(kMask, contrib);
+  if (lane == 0) atomicMax(&s_max_contrib, warp_max);
+  __syncthreads();
+  const int64_t start = ranges[2 * tile];
+  int64_t end = ranges[2 * tile + 1];
+  if (end > start + s_max_contrib) end = start + s_max_contrib;  // composite_bwd.py:81-83
+
+  float st = 1.0f, sr = 0.0f, sg = 0.0f, sb = 0.0f;  // suffix behind the current entry
+  for (int64_t batch_end = end; batch_end > start; batch_end -= NB) {
+    const int64_t batch_start = batch_end - NB > start ? batch_end - NB : start;
+    const int64_t k = batch_start + tid;
+    if (tid < NB && k < batch_end) {
+      const Staged s = stage_entry(__ldg(gaussian_ids + k), projected_mean, inverse_covariance,
+                                   projected_color, projected_opacity, p);
+      s_a[tid] = s.a;
+      s_b[tid] = s.b;
+      s_c[tid] = s.c;
+    }
+    __syncthreads();
+    for (int j = static_cast<int>(batch_end - batch_start) - 1; j >= 0; --j) {
+      const int64_t position = batch_start + j - start;
+      float v[9];
+#pragma unroll
+      for (int q = 0; q < 9; ++q) v[q] = 0.0f;
+      bool active = false;
+      if (position < contrib) {
+        const float4 a = s_a[j];
+        const float4 b = s_b[j];
+        const float dx = fpx - a.x, dy = fpy - a.y;
+        const float xx = a.z, xy = b.w, yy = b.x, o = b.y;
+        const float d2 = pair_d2(dx, dy, xx, a.w, yy);
+        if (d2 <= b.z) {
+          const float prob = d2 >= 0.0f ? det_exp_nonpositive(-0.5f * d2) : det_exp(-0.5f * d2);
+          const float alpha_raw = o * prob;
+          const float alpha = fminf(alpha_raw, kAlphaMax);
+          if (alpha >= kAlphaMin) {
+            active = true;
+            const float4 c = s_c[j];
+            const float denominator = fmaxf(st * (1.0f - alpha), 1e-4f);
+            const float forward = t_final / denominator;
+            const bool still = (1.0f - forward) < threshold;
+            float weight_grad = gr * (c.x - sr);
+            weight_grad += gg * (c.y - sg);
+            weight_grad += gb * (c.z - sb);
+            float grad_alpha = still ? forward * weight_grad : 0.0f;
+            grad_alpha = alpha_raw < kAlphaMax ? grad_alpha : 0.0f;
+            const float probability_grad = grad_alpha * o;
+            const float grad_color = forward * alpha;
+            const float grad_distance = -0.5f * prob * probability_grad;
+            v[0] = -2.0f * grad_distance * (xx * dx + xy * dy);
+            v[1] = -2.0f * grad_distance * (xy * dx + yy * dy);
+            v[2] = grad_distance * dx * dx;
+            v[3] = grad_distance * dx * dy;
+            v[4] = grad_distance * dy * dy;
+            v[5] = grad_color * gr;
+            v[6] = grad_color * gg;
+            v[7] = grad_color * gb;
+            v[8] = grad_alpha * prob;
+            const float local_t = 1.0f - alpha;
+            sr = fmaf(local_t, sr, alpha * c.x);
+            sg = fmaf(local_t, sg, alpha * c.y);
+            sb = fmaf(local_t, sb, alpha * c.z);
+            st = st * local_t;
+          }
+        }
+      }
+      if (__any_sync(kMask, active)) {
+#pragma unroll
+        for (int q = 0; q < 9; ++q) {
+#pragma unroll
+          for (int o = Shape::kWarpLanes / 2; o > 0; o >>= 1) v[q] += __shfl_xor_sync(kMask, v[q], o);
+        }
+        if (lane == 0) {
+          const int g = __float_as_int(s_c[j].w);
+          float* dst = grad_projected + 9 * static_cast<int64_t>(g);
+#pragma unroll
+          for (int q = 0; q < 9; ++q) atomicAdd(dst + q, v[q]);
+        }
+      }
+    }
+    __syncthreads();
+  }
+}
+
+}  // namespace
+
+#define GS_TILE_DISPATCH(ts, LAUNCH)      \
+  switch (ts) {                            \
+    case 4: LAUNCH(4); break;              \
+    case 8: LAUNCH(8); break;              \
+    case 16: LAUNCH(16); break;            \
+    case 32: LAUNCH(32); break;            \
+    default: return GS_ERR_INVALID_ARGUMENT; \
+  }
+
+int32_t launch_composite_fwd(const float* projected_mean, const float* inverse_covariance,
+                             const float* projected_color, const float* projected_opacity,
+                             const int32_t* gaussian_ids, const int64_t* ranges,
+                             const gs_params& p, float* image, float* final_transmittance,
+                             int32_t* n_contributors, cudaStream_t stream) {
+  const int64_t num_tiles =
+      static_cast<int64_t>(p.width / p.tile_size) * (p.height / p.tile_size);
+  if (num_tiles == 0) return GS_OK;
+#define GS_LAUNCH(TS)                                                                          \
+  composite_fwd_kernel<TS><<<static_cast<unsigned>(num_tiles), TS * TS, 0, stream>>>(         \
+      projected_mean, inverse_covariance, projected_color, projected_opacity, gaussian_ids,    \
+      ranges, p, image, final_transmittance, n_contributors)
+  GS_TILE_DISPATCH(p.tile_size, GS_LAUNCH)
+#undef GS_LAUNCH
+  return check_launch();
+}
+
+int32_t launch_composite_bwd(int64_t n, const float* projected_mean,
+                             const float* inverse_covariance, const float* projected_color,
+                             const float* projected_opacity, const int32_t* gaussian_ids,
+                             const int64_t* ranges, const float* grad_image,
+                             const float* final_transmittance, const int32_t* n_contributors,
+                             const gs_params& p, float* grad_projected, cudaStream_t stream) {
+  GS_CUDA_TRY(cudaMemsetAsync(grad_projected, 0, sizeof(float) * 9 * n, stream));
+  const int64_t num_tiles =
+      static_cast<int64_t>(p.width / p.tile_size) * (p.height / p.tile_size);
+  if (num_tiles == 0 || n == 0) return GS_OK;
+#define GS_LAUNCH(TS)                                                                          \
+  composite_bwd_kernel<TS><<<static_cast<unsigned>(num_tiles), TS * TS, 0, stream>>>(         \
+      projected_mean, inverse_covariance, projected_color, projected_opacity, gaussian_ids,    \
+      ranges, grad_image, final_transmittance, n_contributors, p, grad_projected)
+  GS_TILE_DISPATCH(p.tile_size, GS_LAUNCH)
+#undef GS_LAUNCH
+  return check_launch();
+}
+
+}  // namespace gs

@@ -1,0 +1,478 @@
+// Projection (forward) and parameter gradients (backward), one thread per
+// Gaussian.
+//
+// Forward follows _project_and_count_kernel (project.py:74-253) and backward
+// _project_bwd_kernel (project_bwd.py:8-334) operation for operation in float32
+// (the library builds with --fmad=false, so nothing is fused unless written as
+// fmaf), which keeps tile bounds and counts bit-identical with the CPU oracle.
+//
+// Both kernels are HBM-bound: per Gaussian the forward reads 44 + 12K bytes of
+// parameters (K = SH coefficients) and writes 64 bytes; the backward reads
+// 44 + 12K + 16 + 36 + 4 bytes and writes 44 + 12K bytes. The SH block is the
+// bulk (192 B at degree 3); each thread reads its own row with 16-byte
+// vector loads when the row is 16-byte aligned (K = 4, 16), scalar otherwise.
+#include "common.cuh"
+
+namespace gs {
+namespace {
+
+// SH basis function k at unit direction (x, y, z) (project.py:22-61).
+__device__ __forceinline__ float sh_basis(int k, float x, float y, float z, float xx, float yy,
+                                          float zz) {
+  switch (k) {
+    case 0: return 0.28209479177387814f;
+    case 1: return -0.4886025119029199f * y;
+    case 2: return 0.4886025119029199f * z;
+    case 3: return -0.4886025119029199f * x;
+    case 4: return 1.0925484305920792f * x * y;
+    case 5: return -1.0925484305920792f * y * z;
+    case 6: return 0.31539156525252005f * (2.0f * zz - xx - yy);
+    case 7: return -1.0925484305920792f * x * z;
+    case 8: return 0.5462742152960396f * (xx - yy);
+    case 9: return -0.5900435899266435f * y * (3.0f * xx - yy);
+    case 10: return 2.890611442640554f * x * y * z;
+    case 11: return -0.4570457994644658f * y * (4.0f * zz - xx - yy);
+    case 12: return 0.3731763325901154f * z * (2.0f * zz - 3.0f * xx - 3.0f * yy);
+    case 13: return -0.4570457994644658f * x * (4.0f * zz - xx - yy);
+    case 14: return 1.445305721320277f * z * (xx - yy);
+    case 15: return -0.5900435899266435f * x * (xx - 3.0f * yy);
+    case 16: return 2.5033429417967046f * x * y * (xx - yy);
+    case 17: return -1.7701307697799304f * y * z * (3.0f * xx - yy);
+    case 18: return 0.9461746957575601f * x * y * (7.0f * zz - 1.0f);
+    case 19: return -0.6690465435572892f * y * z * (7.0f * zz - 3.0f);
+    case 20: return 0.10578554691520431f * (zz * (35.0f * zz - 30.0f) + 3.0f);
+    case 21: return -0.6690465435572892f * x * z * (7.0f * zz - 3.0f);
+    case 22: return 0.47308734787878004f * (xx - yy) * (7.0f * zz - 1.0f);
+    case 23: return -1.7701307697799304f * x * z * (xx - 3.0f * yy);
+    default: return 0.6258357354491761f * (xx * (xx - 3.0f * yy) - yy * (3.0f * xx - yy));
+  }
+}
+
+// Loads the K x 3 SH coefficients of one Gaussian into registers.
+template <int K>
+__device__ __forceinline__ void load_sh(const float* __restrict__ row, float (&c)[K * 3]) {
+  if constexpr ((K * 3) % 4 == 0 && (K * 12) % 16 == 0) {
+    const float4* v = reinterpret_cast<const float4*>(row);
+#pragma unroll
+    for (int j = 0; j < K * 3 / 4; ++j) {
+      float4 q = __ldg(v + j);
+      c[4 * j] = q.x; c[4 * j + 1] = q.y; c[4 * j + 2] = q.z; c[4 * j + 3] = q.w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < K * 3; ++j) c[j] = __ldg(row + j);
+  }
+}
+
+struct Camera {
+  float r00, r01, r02, r10, r11, r12, r20, r21, r22, tx, ty, tz;
+};
+
+__device__ __forceinline__ Camera load_camera(const float* __restrict__ R,
+                                              const float* __restrict__ t) {
+  return Camera{__ldg(R), __ldg(R + 1), __ldg(R + 2), __ldg(R + 3), __ldg(R + 4), __ldg(R + 5),
+                __ldg(R + 6), __ldg(R + 7), __ldg(R + 8), __ldg(t), __ldg(t + 1), __ldg(t + 2)};
+}
+
+template <int K>
+__global__ void __launch_bounds__(256) project_fwd_kernel(
+    int64_t n, const float* __restrict__ mean, const float* __restrict__ rotation,
+    const float* __restrict__ scale, const float* __restrict__ opacity,
+    const float* __restrict__ color, const float* __restrict__ camera_rotation,
+    const float* __restrict__ camera_translation, const gs_params p,
+    float* __restrict__ projected_mean, float* __restrict__ inverse_covariance,
+    float* __restrict__ projected_color, float* __restrict__ projected_opacity,
+    int4* __restrict__ bounds, int32_t* __restrict__ counts) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const Camera c = load_camera(camera_rotation, camera_translation);
+  const float mx = __ldg(mean + 3 * i), my = __ldg(mean + 3 * i + 1), mz = __ldg(mean + 3 * i + 2);
+  // project.py:126-142
+  const float camera_x = mx * c.r00 + my * c.r01 + mz * c.r02 + c.tx;
+  const float camera_y = mx * c.r10 + my * c.r11 + mz * c.r12 + c.ty;
+  const float camera_z = mx * c.r20 + my * c.r21 + mz * c.r22 + c.tz;
+  const float depth = -camera_z;
+  const float safe_z = depth > 0.0f ? fmaxf(1e-4f, depth) : fminf(-1e-4f, depth);
+  const float pixel_x = p.fx * camera_x / safe_z + p.cx;
+  const float pixel_y = -p.fy * camera_y / safe_z + p.cy;
+  projected_mean[3 * i] = pixel_x;
+  projected_mean[3 * i + 1] = pixel_y;
+  projected_mean[3 * i + 2] = safe_z;
+  // project.py:144-156
+  const float4 q4 = __ldg(reinterpret_cast<const float4*>(rotation) + i);
+  float qw = q4.x, qx = q4.y, qy = q4.z, qz = q4.w;
+  const float inverse_norm = det_rsqrt(qw * qw + qx * qx + qy * qy + qz * qz);
+  qw = qw * inverse_norm; qx = qx * inverse_norm; qy = qy * inverse_norm; qz = qz * inverse_norm;
+  // project.py:158-176
+  const float cov_x = fminf(p.lim_x, fmaxf(-p.lim_x, camera_x / safe_z)) * safe_z;
+  const float cov_y = fminf(p.lim_y, fmaxf(-p.lim_y, camera_y / safe_z)) * safe_z;
+  const float inverse_z = 1.0f / safe_z;
+  const float j00 = p.fx * inverse_z;
+  const float j02 = p.fx * cov_x * inverse_z * inverse_z;
+  const float j11 = -p.fy * inverse_z;
+  const float j12 = -p.fy * cov_y * inverse_z * inverse_z;
+  const float jc00 = j00 * c.r00 + j02 * c.r20, jc01 = j00 * c.r01 + j02 * c.r21,
+              jc02 = j00 * c.r02 + j02 * c.r22;
+  const float jc10 = j11 * c.r10 + j12 * c.r20, jc11 = j11 * c.r11 + j12 * c.r21,
+              jc12 = j11 * c.r12 + j12 * c.r22;
+  // project.py:177-218
+  const float sx = det_exp(__ldg(scale + 3 * i)), sy = det_exp(__ldg(scale + 3 * i + 1)),
+              sz = det_exp(__ldg(scale + 3 * i + 2));
+  const float a0x = (1.0f - 2.0f * (qy * qy + qz * qz)) * sx;
+  const float a0y = (2.0f * (qx * qy + qw * qz)) * sx;
+  const float a0z = (2.0f * (qx * qz - qw * qy)) * sx;
+  const float a1x = (2.0f * (qx * qy - qw * qz)) * sy;
+  const float a1y = (1.0f - 2.0f * (qx * qx + qz * qz)) * sy;
+  const float a1z = (2.0f * (qy * qz + qw * qx)) * sy;
+  const float a2x = (2.0f * (qx * qz + qw * qy)) * sz;
+  const float a2y = (2.0f * (qy * qz - qw * qx)) * sz;
+  const float a2z = (1.0f - 2.0f * (qx * qx + qy * qy)) * sz;
+  const float f00 = jc00 * a0x + jc01 * a0y + jc02 * a0z;
+  const float f01 = jc00 * a1x + jc01 * a1y + jc02 * a1z;
+  const float f02 = jc00 * a2x + jc01 * a2y + jc02 * a2z;
+  const float f10 = jc10 * a0x + jc11 * a0y + jc12 * a0z;
+  const float f11 = jc10 * a1x + jc11 * a1y + jc12 * a1z;
+  const float f12 = jc10 * a2x + jc11 * a2y + jc12 * a2z;
+  const float cov00 = f00 * f00 + f01 * f01 + f02 * f02 + 0.03f;
+  const float cov01 = f00 * f10 + f01 * f11 + f02 * f12;
+  const float cov11 = f10 * f10 + f11 * f11 + f12 * f12 + 0.03f;
+  const float determinant = cov00 * cov11 - cov01 * cov01;
+  const float conic_xy = -cov01 / determinant;
+  reinterpret_cast<float4*>(inverse_covariance)[i] =
+      make_float4(cov11 / determinant, conic_xy, conic_xy, cov00 / determinant);
+  // project.py:221-228, _evaluate_sh (project.py:10-71)
+  float dx = mx + c.r00 * c.tx + c.r10 * c.ty + c.r20 * c.tz;
+  float dy = my + c.r01 * c.tx + c.r11 * c.ty + c.r21 * c.tz;
+  float dz = mz + c.r02 * c.tx + c.r12 * c.ty + c.r22 * c.tz;
+  const float direction_norm = det_rsqrt(dx * dx + dy * dy + dz * dz);
+  dx = dx * direction_norm; dy = dy * direction_norm; dz = dz * direction_norm;
+  const float xx = dx * dx, yy = dy * dy, zz = dz * dz;
+  float coefficients[K * 3];
+  load_sh<K>(color + i * (K * 3), coefficients);
+  float acc_r = 0.0f, acc_g = 0.0f, acc_b = 0.0f;
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    const float b = sh_basis(k, dx, dy, dz, xx, yy, zz);
+    acc_r = fmaf(coefficients[3 * k], b, acc_r);
+    acc_g = fmaf(coefficients[3 * k + 1], b, acc_g);
+    acc_b = fmaf(coefficients[3 * k + 2], b, acc_b);
+  }
+  projected_color[3 * i] = fmaxf(acc_r + 0.5f, 0.0f);
+  projected_color[3 * i + 1] = fmaxf(acc_g + 0.5f, 0.0f);
+  projected_color[3 * i + 2] = fmaxf(acc_b + 0.5f, 0.0f);
+  // project.py:230-253
+  const float o = det_sigmoid(__ldg(opacity + i));
+  projected_opacity[i] = o;
+  const float radius_extent = p.gaussian_mode ? 2.0f * sqrtf(det_log(o * 255.0f)) : p.extent;
+  const float radius_x = radius_extent * sqrtf(cov00);
+  const float radius_y = radius_extent * sqrtf(cov11);
+  const float ts = static_cast<float>(p.tile_size);
+  const float tiles_w = static_cast<float>(p.width / p.tile_size);
+  const float tiles_h = static_cast<float>(p.height / p.tile_size);
+  // tl.clamp (max then min); a NaN radius clamps to 0.
+  const float tmin_x = fminf(fmaxf(floorf((pixel_x - radius_x) / ts), 0.0f), tiles_w);
+  const float tmin_y = fminf(fmaxf(floorf((pixel_y - radius_y) / ts), 0.0f), tiles_h);
+  const float tmax_x = fminf(fmaxf(floorf((pixel_x + radius_x) / ts) + 1.0f, 0.0f), tiles_w);
+  const float tmax_y = fminf(fmaxf(floorf((pixel_y + radius_y) / ts) + 1.0f, 0.0f), tiles_h);
+  bounds[i] = make_int4(static_cast<int>(tmin_x), static_cast<int>(tmax_x),
+                        static_cast<int>(tmin_y), static_cast<int>(tmax_y));
+  const float count = (tmax_x - tmin_x) * (tmax_y - tmin_y);
+  counts[i] = (safe_z > p.near_plane && safe_z < p.far_plane) ? static_cast<int32_t>(count) : 0;
+}
+
+template <int K>
+__global__ void __launch_bounds__(128) project_bwd_kernel(
+    int64_t n, const float* __restrict__ mean, const float* __restrict__ rotation,
+    const float* __restrict__ scale, const float* __restrict__ opacity,
+    const float* __restrict__ color, const float* __restrict__ camera_rotation,
+    const float* __restrict__ camera_translation, const float* __restrict__ inverse_covariance,
+    const float* __restrict__ grad_projected, const int32_t* __restrict__ counts,
+    const gs_params p, float* __restrict__ grad_mean, float* __restrict__ grad_rotation,
+    float* __restrict__ grad_scale, float* __restrict__ grad_opacity,
+    float* __restrict__ grad_color) {
+  constexpr int KB = K < 16 ? K : 16;  // backward covers SH degree <= 3 (project_bwd.py:33)
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const bool visible = __ldg(counts + i) != 0;
+  const Camera c = load_camera(camera_rotation, camera_translation);
+  const float fx = p.fx, fy = p.fy, lim_x = p.bwd_lim_x, lim_y = p.bwd_lim_y;
+  const float mx = __ldg(mean + 3 * i), my = __ldg(mean + 3 * i + 1), mz = __ldg(mean + 3 * i + 2);
+  // project_bwd.py:62-94
+  const float camera_x = mx * c.r00 + my * c.r01 + mz * c.r02 + c.tx;
+  const float camera_y = mx * c.r10 + my * c.r11 + mz * c.r12 + c.ty;
+  const float camera_z = mx * c.r20 + my * c.r21 + mz * c.r22 + c.tz;
+  const float4 q4 = __ldg(reinterpret_cast<const float4*>(rotation) + i);
+  float qw = q4.x, qx = q4.y, qy = q4.z, qz = q4.w;
+  const float qnorm = sqrtf(qw * qw + qx * qx + qy * qy + qz * qz);
+  const float inverse_qnorm = 1.0f / qnorm;
+  qw = qw * inverse_qnorm; qx = qx * inverse_qnorm; qy = qy * inverse_qnorm; qz = qz * inverse_qnorm;
+  const float r00 = 1.0f - 2.0f * (qy * qy + qz * qz), r01 = 2.0f * (qx * qy - qw * qz),
+              r02 = 2.0f * (qx * qz + qw * qy);
+  const float r10 = 2.0f * (qx * qy + qw * qz), r11 = 1.0f - 2.0f * (qx * qx + qz * qz),
+              r12 = 2.0f * (qy * qz - qw * qx);
+  const float r20 = 2.0f * (qx * qz - qw * qy), r21 = 2.0f * (qy * qz + qw * qx),
+              r22 = 1.0f - 2.0f * (qx * qx + qy * qy);
+  const float depth = -camera_z;
+  const float inverse_z = 1.0f / depth;
+  const float normalized_x = camera_x * inverse_z, normalized_y = camera_y * inverse_z;
+  const float x_grad_mul = (normalized_x >= -lim_x && normalized_x <= lim_x) ? 1.0f : 0.0f;
+  const float y_grad_mul = (normalized_y >= -lim_y && normalized_y <= lim_y) ? 1.0f : 0.0f;
+  const float covariance_x = fminf(lim_x, fmaxf(-lim_x, normalized_x)) * depth;
+  const float covariance_y = fminf(lim_y, fmaxf(-lim_y, normalized_y)) * depth;
+  const float j00 = fx * inverse_z, j02 = fx * covariance_x * inverse_z * inverse_z;
+  const float j11 = -fy * inverse_z, j12 = -fy * covariance_y * inverse_z * inverse_z;
+  // project_bwd.py:96-114
+  const float jc00 = j00 * c.r00 + j02 * c.r20, jc01 = j00 * c.r01 + j02 * c.r21,
+              jc02 = j00 * c.r02 + j02 * c.r22;
+  const float jc10 = j11 * c.r10 + j12 * c.r20, jc11 = j11 * c.r11 + j12 * c.r21,
+              jc12 = j11 * c.r12 + j12 * c.r22;
+  const float sx = det_exp(__ldg(scale + 3 * i)), sy = det_exp(__ldg(scale + 3 * i + 1)),
+              sz = det_exp(__ldg(scale + 3 * i + 2));
+  const float m0x = jc00 * r00 + jc01 * r10 + jc02 * r20, m0y = jc00 * r01 + jc01 * r11 + jc02 * r21,
+              m0z = jc00 * r02 + jc01 * r12 + jc02 * r22;
+  const float m1x = jc10 * r00 + jc11 * r10 + jc12 * r20, m1y = jc10 * r01 + jc11 * r11 + jc12 * r21,
+              m1z = jc10 * r02 + jc11 * r12 + jc12 * r22;
+  const float a00 = m0x * sx, a01 = m0y * sy, a02 = m0z * sz;
+  const float a10 = m1x * sx, a11 = m1y * sy, a12 = m1z * sz;
+  // project_bwd.py:116-152
+  const float* gp = grad_projected + 9 * i;
+  const float4 inv = __ldg(reinterpret_cast<const float4*>(inverse_covariance) + i);
+  const float inv00 = inv.x, inv01 = inv.y, inv10 = inv01, inv11 = inv.w;
+  const float gi00 = __ldg(gp + 2), gi01 = __ldg(gp + 3), gi10 = gi01, gi11 = __ldg(gp + 4);
+  const float h00 = inv00 * gi00 + inv10 * gi10, h01 = inv00 * gi01 + inv10 * gi11;
+  const float h10 = inv01 * gi00 + inv11 * gi10, h11 = inv01 * gi01 + inv11 * gi11;
+  const float gcov00 = -(h00 * inv00 + h01 * inv10), gcov01 = -(h00 * inv01 + h01 * inv11);
+  const float gcov10 = -(h10 * inv00 + h11 * inv10), gcov11 = -(h10 * inv01 + h11 * inv11);
+  const float sym01 = gcov01 + gcov10;
+  const float ga00 = 2.0f * gcov00 * a00 + sym01 * a10, ga01 = 2.0f * gcov00 * a01 + sym01 * a11,
+              ga02 = 2.0f * gcov00 * a02 + sym01 * a12;
+  const float ga10 = sym01 * a00 + 2.0f * gcov11 * a10, ga11 = sym01 * a01 + 2.0f * gcov11 * a11,
+              ga12 = sym01 * a02 + 2.0f * gcov11 * a12;
+  const float gb00 = ga00 * sx, gb01 = ga01 * sy, gb02 = ga02 * sz;
+  const float gb10 = ga10 * sx, gb11 = ga11 * sy, gb12 = ga12 * sz;
+  const float grad_sx = ga00 * m0x + ga10 * m1x;
+  const float grad_sy = ga01 * m0y + ga11 * m1y;
+  const float grad_sz = ga02 * m0z + ga12 * m1z;
+  // project_bwd.py:154-189
+  const float gr00 = jc00 * gb00 + jc10 * gb10, gr01 = jc00 * gb01 + jc10 * gb11,
+              gr02 = jc00 * gb02 + jc10 * gb12;
+  const float gr10 = jc01 * gb00 + jc11 * gb10, gr11 = jc01 * gb01 + jc11 * gb11,
+              gr12 = jc01 * gb02 + jc11 * gb12;
+  const float gr20 = jc02 * gb00 + jc12 * gb10, gr21 = jc02 * gb01 + jc12 * gb11,
+              gr22 = jc02 * gb02 + jc12 * gb12;
+  float gqw = 2.0f * qz * (gr10 - gr01) + 2.0f * qy * (gr02 - gr20) + 2.0f * qx * (gr21 - gr12);
+  float gqx = 2.0f * qy * (gr01 + gr10) + 2.0f * qz * (gr02 + gr20) + 2.0f * qw * (gr21 - gr12) -
+              4.0f * qx * (gr11 + gr22);
+  float gqy = 2.0f * qx * (gr01 + gr10) + 2.0f * qw * (gr02 - gr20) + 2.0f * qz * (gr12 + gr21) -
+              4.0f * qy * (gr00 + gr22);
+  float gqz = 2.0f * qw * (gr10 - gr01) + 2.0f * qx * (gr02 + gr20) + 2.0f * qy * (gr12 + gr21) -
+              4.0f * qz * (gr00 + gr11);
+  const float dot_q = qw * gqw + qx * gqx + qy * gqy + qz * gqz;
+  const float gq_scale = 1.0f / qnorm;
+  gqw = (gqw - qw * dot_q) * gq_scale;
+  gqx = (gqx - qx * dot_q) * gq_scale;
+  gqy = (gqy - qy * dot_q) * gq_scale;
+  gqz = (gqz - qz * dot_q) * gq_scale;
+  // project_bwd.py:191-226
+  const float gpx = __ldg(gp), gpy = __ldg(gp + 1);
+  float gux = gpx * j00 + gpx * 0.0f;
+  float guy = gpy * j11;
+  float guz = -0.0f + gpx * j02 + gpy * j12;
+  const float mr0 = c.r00 * r00 + c.r01 * r10 + c.r02 * r20,
+              mr1 = c.r00 * r01 + c.r01 * r11 + c.r02 * r21,
+              mr2 = c.r00 * r02 + c.r01 * r12 + c.r02 * r22;
+  const float nr0 = c.r10 * r00 + c.r11 * r10 + c.r12 * r20,
+              nr1 = c.r10 * r01 + c.r11 * r11 + c.r12 * r21,
+              nr2 = c.r10 * r02 + c.r11 * r12 + c.r12 * r22;
+  const float kr0 = c.r20 * r00 + c.r21 * r10 + c.r22 * r20,
+              kr1 = c.r20 * r01 + c.r21 * r11 + c.r22 * r21,
+              kr2 = c.r20 * r02 + c.r21 * r12 + c.r22 * r22;
+  const float gj_j00 = gb00 * mr0 + gb01 * mr1 + gb02 * mr2;
+  const float gj_j02 = gb00 * kr0 + gb01 * kr1 + gb02 * kr2;
+  const float gj_j11 = gb10 * nr0 + gb11 * nr1 + gb12 * nr2;
+  const float gj_j12 = gb10 * kr0 + gb11 * kr1 + gb12 * kr2;
+  gux += x_grad_mul * gj_j02 * (fx * inverse_z * inverse_z);
+  guy += y_grad_mul * gj_j12 * (-fy * inverse_z * inverse_z);
+  const float inverse_z3 = inverse_z * inverse_z * inverse_z;
+  guz += gj_j00 * (fx * inverse_z * inverse_z) + gj_j02 * 2.0f * fx * covariance_x * inverse_z3;
+  guz += gj_j11 * (-fy * inverse_z * inverse_z) - gj_j12 * 2.0f * fy * covariance_y * inverse_z3;
+  float gmx = gux * c.r00 + guy * c.r10 + guz * c.r20;
+  float gmy = gux * c.r01 + guy * c.r11 + guz * c.r21;
+  float gmz = gux * c.r02 + guy * c.r12 + guz * c.r22;
+  // project_bwd.py:228-318: SH VJP for coefficients 0..15 and the view
+  // direction's contribution to the mean.
+  const float ddx = mx + c.r00 * c.tx + c.r10 * c.ty + c.r20 * c.tz;
+  const float ddy = my + c.r01 * c.tx + c.r11 * c.ty + c.r21 * c.tz;
+  const float ddz = mz + c.r02 * c.tx + c.r12 * c.ty + c.r22 * c.tz;
+  const float norm = sqrtf(ddx * ddx + ddy * ddy + ddz * ddz);
+  const float x = ddx / norm, y = ddy / norm, z = ddz / norm;
+  const float xx = x * x, yy = y * y, zz = z * z;
+  float basis[16], dbx[16], dby[16], dbz[16];
+#pragma unroll
+  for (int k = 0; k < 16; ++k) { dbx[k] = 0.0f; dby[k] = 0.0f; dbz[k] = 0.0f; }
+  basis[0] = 0.28209479177387814f;
+  basis[1] = -0.4886025119029199f * y;
+  basis[2] = 0.4886025119029199f * z;
+  basis[3] = -0.4886025119029199f * x;
+  basis[4] = 1.0925484305920792f * x * y;
+  basis[5] = -1.0925484305920792f * y * z;
+  basis[6] = 0.31539156525252005f * (2.0f * zz - xx - yy);
+  basis[7] = -1.0925484305920792f * x * z;
+  basis[8] = 0.5462742152960396f * (xx - yy);
+  basis[9] = -0.5900435899266435f * y * (3.0f * xx - yy);
+  basis[10] = 2.890611442640554f * x * y * z;
+  basis[11] = -0.4570457994644655f * y * (4.0f * zz - xx - yy);
+  basis[12] = 0.3731763325901154f * z * (2.0f * zz - 3.0f * xx - 3.0f * yy);
+  basis[13] = -0.4570457994644655f * x * (4.0f * zz - xx - yy);
+  basis[14] = 1.445305721320277f * z * (xx - yy);
+  basis[15] = -0.5900435899266435f * x * (xx - 3.0f * yy);
+  dbx[3] = -0.4886025119029199f;
+  dby[1] = -0.4886025119029199f;
+  dbz[2] = 0.4886025119029199f;
+  dbx[4] = 1.0925484305920792f * y;
+  dby[4] = 1.0925484305920792f * x;
+  dby[5] = -1.0925484305920792f * z;
+  dbz[5] = -1.0925484305920792f * y;
+  dbx[6] = -0.6307831301050401f * x;
+  dby[6] = -0.6307831301050401f * y;
+  dbz[6] = 1.2615662610100802f * z;
+  dbx[7] = -1.0925484305920792f * z;
+  dbz[7] = -1.0925484305920792f * x;
+  dbx[8] = 1.0925484305920792f * x;
+  dby[8] = -1.0925484305920792f * y;
+  dbx[9] = -3.540261539559861f * x * y;
+  dby[9] = -1.7701307697799305f * (xx - yy);
+  dbx[10] = 2.890611442640554f * y * z;
+  dby[10] = 2.890611442640554f * x * z;
+  dbz[10] = 2.890611442640554f * x * y;
+  dbx[11] = 0.914091599852931f * x * y;
+  dby[11] = -0.4570457994644655f * (4.0f * zz - xx - 3.0f * yy);
+  dbz[11] = -3.656366399411724f * y * z;
+  dbx[12] = -2.2390579955366924f * x * z;
+  dby[12] = -2.2390579955366924f * y * z;
+  dbz[12] = 0.3731763325901154f * (6.0f * zz - 3.0f * xx - 3.0f * yy);
+  dbx[13] = -0.4570457994644655f * (4.0f * zz - 3.0f * xx - yy);
+  dby[13] = 0.914091599852931f * x * y;
+  dbz[13] = -3.656366399411724f * x * z;
+  dbx[14] = 2.890611442640554f * x * z;
+  dby[14] = -2.890611442640554f * y * z;
+  dbz[14] = 1.445305721320277f * (xx - yy);
+  dbx[15] = -1.7701307697799305f * (xx - yy);
+  dby[15] = 3.540261539559861f * x * y;
+  float coefficients[K * 3];
+  load_sh<K>(color + i * (K * 3), coefficients);
+  float* gcol = grad_color + i * (K * 3);
+  float gc3[3];
+  float gdx = 0.0f, gdy = 0.0f, gdz = 0.0f;
+#pragma unroll
+  for (int ch = 0; ch < 3; ++ch) {
+    float raw = 0.0f, sdx = 0.0f, sdy = 0.0f, sdz = 0.0f;
+#pragma unroll
+    for (int k = 0; k < KB; ++k) {
+      const float coef = coefficients[3 * k + ch];
+      raw = fmaf(coef, basis[k], raw);
+      sdx = fmaf(coef, dbx[k], sdx);
+      sdy = fmaf(coef, dby[k], sdy);
+      sdz = fmaf(coef, dbz[k], sdz);
+    }
+    raw = raw + 0.5f;
+    const float gc = __ldg(gp + 5 + ch) * (raw > 0.0f ? 1.0f : 0.0f);
+    gc3[ch] = visible ? gc : 0.0f;
+    gdx += gc * sdx;
+    gdy += gc * sdy;
+    gdz += gc * sdz;
+  }
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+#pragma unroll
+    for (int ch = 0; ch < 3; ++ch)
+      gcol[3 * k + ch] = k < KB ? (visible ? gc3[ch] * basis[k < 16 ? k : 0] : 0.0f) : 0.0f;
+  }
+  const float dot_d = x * gdx + y * gdy + z * gdz;
+  gdx = (gdx - x * dot_d) / norm;
+  gdy = (gdy - y * dot_d) / norm;
+  gdz = (gdz - z * dot_d) / norm;
+  gmx += gdx; gmy += gdy; gmz += gdz;
+  // project_bwd.py:320-334
+  const float po = det_sigmoid(__ldg(opacity + i));
+  const float go = __ldg(gp + 8) * po * (1.0f - po);
+  grad_mean[3 * i] = visible ? gmx : 0.0f;
+  grad_mean[3 * i + 1] = visible ? gmy : 0.0f;
+  grad_mean[3 * i + 2] = visible ? gmz : 0.0f;
+  reinterpret_cast<float4*>(grad_rotation)[i] =
+      visible ? make_float4(gqw, gqx, gqy, gqz) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  grad_scale[3 * i] = visible ? grad_sx * sx : 0.0f;
+  grad_scale[3 * i + 1] = visible ? grad_sy * sy : 0.0f;
+  grad_scale[3 * i + 2] = visible ? grad_sz * sz : 0.0f;
+  grad_opacity[i] = visible ? go : 0.0f;
+}
+
+}  // namespace
+
+#define GS_SH_DISPATCH(num_sh, LAUNCH)        \
+  switch (num_sh) {                            \
+    case 1: LAUNCH(1); break;                  \
+    case 4: LAUNCH(4); break;                  \
+    case 9: LAUNCH(9); break;                  \
+    case 16: LAUNCH(16); break;                \
+    case 25: LAUNCH(25); break;                \
+    default: return GS_ERR_UNSUPPORTED;        \
+  }
+
+int32_t launch_project_fwd(int64_t n, int32_t num_sh, const float* mean, const float* rotation,
+                           const float* scale, const float* opacity, const float* color,
+                           const float* camera_rotation, const float* camera_translation,
+                           const gs_params& p, float* projected_mean, float* inverse_covariance,
+                           float* projected_color, float* projected_opacity, int32_t* bounds,
+                           int32_t* counts, cudaStream_t stream) {
+  if (n == 0) return GS_OK;
+  const unsigned blocks = ceil_div(n, 256);
+#define GS_LAUNCH(K)                                                                          \
+  project_fwd_kernel<K><<<blocks, 256, 0, stream>>>(                                          \
+      n, mean, rotation, scale, opacity, color, camera_rotation, camera_translation, p,       \
+      projected_mean, inverse_covariance, projected_color, projected_opacity,                 \
+      reinterpret_cast<int4*>(bounds), counts)
+  GS_SH_DISPATCH(num_sh, GS_LAUNCH)
+#undef GS_LAUNCH
+  return check_launch();
+}
+
+int32_t launch_project_bwd(int64_t n, int32_t num_sh, const float* mean, const float* rotation,
+                           const float* scale, const float* opacity, const float* color,
+                           const float* camera_rotation, const float* camera_translation,
+                           const float* inverse_covariance, const float* grad_projected,
+                           const int32_t* counts, const gs_params& p, float* grad_mean,
+                           float* grad_rotation, float* grad_scale, float* grad_opacity,
+                           float* grad_color, cudaStream_t stream) {
+  if (n == 0) return GS_OK;
+  const unsigned blocks = ceil_div(n, 128);
+#define GS_LAUNCH(K)                                                                          \
+  project_bwd_kernel<K><<<blocks, 128, 0, stream>>>(                                          \
+      n, mean, rotation, scale, opacity, color, camera_rotation, camera_translation,           \
+      inverse_covariance, grad_projected, counts, p, grad_mean, grad_rotation, grad_scale,    \
+      grad_opacity, grad_color)
+  GS_SH_DISPATCH(num_sh, GS_LAUNCH)
+#undef GS_LAUNCH
+  return check_launch();
+}
+
+__global__ void det_exp_kernel(int64_t n, const float* __restrict__ x, float* __restrict__ y) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < n) y[i] = det_exp(x[i]);
+}
+
+__global__ void det_log_kernel(int64_t n, const float* __restrict__ x, float* __restrict__ y) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < n) y[i] = det_log(x[i]);
+}
+
+int32_t launch_det_math(int which, int64_t n, const float* x, float* y, cudaStream_t stream) {
+  if (n == 0) return GS_OK;
+  if (which == 0)
+    det_exp_kernel<<<ceil_div(n, 256), 256, 0, stream>>>(n, x, y);
+  else
+    det_log_kernel<<<ceil_div(n, 256), 256, 0, stream>>>(n, x, y);
+  return check_launch();
+}
+
+}  // namespace gs

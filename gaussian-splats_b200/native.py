@@ -1,0 +1,134 @@
+"""ctypes binding of ``libgs_b200.so`` (the C ABI in ``include/gs_b200.h``).
+
+The library is built in-tree by ``__graft_entry__.build()`` (or ``make -C
+gaussian-splats_b200/csrc``). There is no fallback: if the library is missing
+or fails to load, :func:`lib` raises, and so does every rasterizer call.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+import os
+
+PACKAGE_DIR = os.path.dirname(os.path.abspath(__file__))
+LIBRARY_PATH = os.path.join(PACKAGE_DIR, "libgs_b200.so")
+
+GS_OK = 0
+STATUS_NAMES = {
+    -1: "GS_ERR_INVALID_ARGUMENT",
+    -2: "GS_ERR_CUDA",
+    -3: "GS_ERR_CAPACITY",
+    -4: "GS_ERR_UNSUPPORTED",
+    -5: "GS_ERR_MISALIGNED",
+    -6: "GS_ERR_TIMEOUT",
+}
+
+# Every symbol include/gs_b200.h declares.
+EXPORTED_SYMBOLS = (
+    "gs_version",
+    "gs_last_cuda_error",
+    "gs_project_fwd",
+    "gs_bin_count",
+    "gs_bin_count_workspace_size",
+    "gs_bin_sort",
+    "gs_bin_sort_workspace_size",
+    "gs_bin_check",
+    "gs_composite_fwd",
+    "gs_composite_bwd",
+    "gs_project_bwd",
+    "gs_det_exp",
+    "gs_det_log",
+)
+
+
+class Params(ctypes.Structure):
+    """``gs_params`` (include/gs_b200.h)."""
+
+    _fields_ = [
+        ("fx", ctypes.c_float), ("fy", ctypes.c_float), ("cx", ctypes.c_float),
+        ("cy", ctypes.c_float), ("width", ctypes.c_int32), ("height", ctypes.c_int32),
+        ("tile_size", ctypes.c_int32), ("gaussian_mode", ctypes.c_int32),
+        ("near_plane", ctypes.c_float), ("far_plane", ctypes.c_float),
+        ("lim_x", ctypes.c_float), ("lim_y", ctypes.c_float),
+        ("bwd_lim_x", ctypes.c_float), ("bwd_lim_y", ctypes.c_float),
+        ("extent", ctypes.c_float), ("cutoff", ctypes.c_float),
+        ("opacity_threshold", ctypes.c_float),
+    ]
+
+
+def make_params(fx, fy, cx, cy, width, height, tile_size, opacity_threshold, near, far,
+                rendering_mode, confidence) -> Params:
+    """Fold the op's scalars like the reference folds its Triton constexprs.
+
+    ``lim_x``/``lim_y`` (project.py:158-159), the backward limits
+    (project_bwd.py:376-377), the ellipsoid extent (project.py:308) and cutoff
+    (composite.py:226) are evaluated in Python double and rounded to float32.
+    """
+    tiles_w = width // tile_size
+    tiles_h = height // tile_size
+    ellipsoid = rendering_mode == "ellipsoid"
+    return Params(
+        fx=fx, fy=fy, cx=cx, cy=cy, width=width, height=height, tile_size=tile_size,
+        gaussian_mode=0 if ellipsoid else 1, near_plane=near, far_plane=far,
+        lim_x=1.3 * tiles_w * tile_size / (2.0 * fx),
+        lim_y=1.3 * tiles_h * tile_size / (2.0 * fy),
+        bwd_lim_x=1.3 * width / (2.0 * fx),
+        bwd_lim_y=1.3 * height / (2.0 * fy),
+        extent=math.sqrt(-2 * math.log1p(-confidence)) if ellipsoid else 3.0,
+        cutoff=-2.0 * math.log1p(-confidence),
+        opacity_threshold=opacity_threshold,
+    )
+
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded kernel library; raises if it was not built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIBRARY_PATH):
+        raise RuntimeError(
+            f"gaussian_splats_b200: {LIBRARY_PATH} is missing; build it with "
+            "`python -c 'import __graft_entry__ as g; g.build()'` or "
+            "`make -C gaussian-splats_b200/csrc` (there is no CPU fallback)"
+        )
+    handle = ctypes.CDLL(LIBRARY_PATH)
+    vp, i32, i64, u64 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_uint64
+    P = ctypes.POINTER(Params)
+    sigs = {
+        "gs_version": ([], i32),
+        "gs_last_cuda_error": ([], i32),
+        "gs_project_fwd": ([i64, i32] + [vp] * 7 + [P] + [vp] * 6 + [vp], i32),
+        "gs_bin_count": ([i64, vp, vp, vp, u64, ctypes.POINTER(i64), vp], i32),
+        "gs_bin_count_workspace_size": ([i64], u64),
+        "gs_bin_sort": ([i64, i64, vp, vp, P, vp, u64, vp, u64, vp, vp, vp], i32),
+        "gs_bin_sort_workspace_size": ([i64, i64], u64),
+        "gs_bin_check": ([vp, vp, vp], i32),
+        "gs_composite_fwd": ([vp] * 6 + [P] + [vp] * 3 + [vp], i32),
+        "gs_composite_bwd": ([i64] + [vp] * 9 + [P, vp, vp], i32),
+        "gs_project_bwd": ([i64, i32] + [vp] * 10 + [P] + [vp] * 5 + [vp], i32),
+        "gs_det_exp": ([i64, vp, vp, vp], i32),
+        "gs_det_log": ([i64, vp, vp, vp], i32),
+    }
+    for name, (args, res) in sigs.items():
+        fn = getattr(handle, name)
+        fn.argtypes = args
+        fn.restype = res
+    if handle.gs_version() != 100:
+        raise RuntimeError(f"gaussian_splats_b200: unexpected library version {handle.gs_version()}")
+    _lib = handle
+    return _lib
+
+
+def check(status: int, what: str) -> None:
+    """Raise ``RuntimeError`` for a non-zero status from the library."""
+    if status == GS_OK:
+        return
+    name = STATUS_NAMES.get(status, str(status))
+    detail = ""
+    if status == -2:
+        detail = f" (cudaError {lib().gs_last_cuda_error()})"
+    raise RuntimeError(f"gaussian_splats_b200: {what} failed with {name}{detail}")

@@ -1,0 +1,293 @@
+"""The ``gaussian_splats::rasterize`` operator on the B200 kernels.
+
+Same operator name, 19-argument schema, 10 outputs and autograd contract as
+the reference's Triton operator (kernels/rasterize/interface.py:17-244), so
+code written against ``torch.ops.gaussian_splats.rasterize`` or against the
+``rasterize(splats, camera, ...)`` helpers runs unchanged. (Registering the
+same operator name as the reference means the two cannot be imported into one
+process.)
+
+The stages run as hand-written sm_100a kernels through the C ABI of
+``libgs_b200.so`` (``include/gs_b200.h``), on the current CUDA stream:
+
+1. ``gs_project_fwd``   projection, SH colour, opacity, tile rectangle and count;
+2. ``gs_bin_count``     depth order of the visible Gaussians and the
+                        intersection total -- the one host sync, as in
+                        intersections.py:51;
+3. ``gs_bin_sort``      (tile, depth)-ordered Gaussian ids and tile ranges;
+4. ``gs_composite_fwd`` per-tile front-to-back compositing.
+Backward: ``gs_composite_bwd`` then ``gs_project_bwd`` (interface.py:176-239).
+
+Differences from the reference, all deliberate:
+* ``ranges`` is int64 in the fake (meta) kernel too, matching what the real
+  operator returns (the reference's fake declares int32, interface.py:146-153);
+* an unknown ``rendering_mode`` raises ``ValueError`` instead of mixing the
+  ellipsoid projection with Gaussian compositing;
+* SH coefficients 16..24 (degree 4) get zero gradients where the reference
+  leaves them uninitialised (project_bwd.py:33,355);
+* inputs must be CUDA tensors: there is no CPU path.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from typing import Literal
+
+import torch
+
+from . import native
+from .camera import Camera
+
+_OUTPUTS = 10
+_VALID_MODES = ("gaussian", "ellipsoid")
+
+
+def _ptr(t: torch.Tensor | None) -> ctypes.c_void_p:
+    return ctypes.c_void_p(t.data_ptr() if t is not None and t.numel() else 0)
+
+
+def _stream(device: torch.device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _check_inputs(mean: torch.Tensor, color: torch.Tensor, rendering_mode: str) -> None:
+    if not mean.is_cuda:
+        raise RuntimeError(
+            "gaussian_splats_b200 runs on CUDA devices only (there is no CPU fallback); "
+            f"got tensors on {mean.device}"
+        )
+    if color.shape[1] > 25:
+        raise NotImplementedError(
+            f"SH degrees above 4 are not implemented. Got {color.shape[1]}."
+        )
+    if rendering_mode not in _VALID_MODES:
+        raise ValueError(f"Invalid rendering mode: {rendering_mode}")
+
+
+def _f32(t: torch.Tensor) -> torch.Tensor:
+    return t.detach().to(torch.float32).contiguous()
+
+
+@torch.library.custom_op("gaussian_splats::rasterize", mutates_args=())
+def _rasterize(
+    mean: torch.Tensor,
+    rotation: torch.Tensor,
+    scale: torch.Tensor,
+    opacity: torch.Tensor,
+    color: torch.Tensor,
+    camera_rotation: torch.Tensor,
+    camera_translation: torch.Tensor,
+    fx: float,
+    fy: float,
+    cx: float,
+    cy: float,
+    image_width: int,
+    image_height: int,
+    tile_size: int,
+    opacity_threshold: float,
+    near: float,
+    far: float,
+    rendering_mode: str,
+    confidence: float,
+) -> tuple[
+    torch.Tensor,  # image [H, W, 3]
+    torch.Tensor,  # final_transmittance [H, W]
+    torch.Tensor,  # n_contributors [H, W] int32
+    torch.Tensor,  # projected_mean [N, 3] (pixel x, pixel y, depth)
+    torch.Tensor,  # inverse_covariance [N, 2, 2]
+    torch.Tensor,  # projected_color [N, 3]
+    torch.Tensor,  # projected_opacity [N, 1]
+    torch.Tensor,  # gaussian_ids [I] int32
+    torch.Tensor,  # ranges [tiles, 2] int64
+    torch.Tensor,  # counts [N] int32
+]:
+    _check_inputs(mean, color, rendering_mode)
+    lib = native.lib()
+    device = mean.device
+    mean, rotation, scale, opacity, color = map(_f32, (mean, rotation, scale, opacity, color))
+    camera_rotation, camera_translation = _f32(camera_rotation), _f32(camera_translation)
+    n, num_sh = mean.shape[0], color.shape[1]
+    params = native.make_params(fx, fy, cx, cy, image_width, image_height, tile_size,
+                                opacity_threshold, near, far, rendering_mode, confidence)
+    pref = ctypes.byref(params)
+    num_tiles = (image_width // tile_size) * (image_height // tile_size)
+    with torch.cuda.device(device):
+        stream = _stream(device)
+        projected_mean = mean.new_empty((n, 3))
+        inverse_covariance = mean.new_empty((n, 2, 2))
+        projected_color = mean.new_empty((n, 3))
+        projected_opacity = mean.new_empty((n, 1))
+        bounds = torch.empty((n, 4), dtype=torch.int32, device=device)
+        counts = torch.empty((n,), dtype=torch.int32, device=device)
+        native.check(lib.gs_project_fwd(
+            n, num_sh, _ptr(mean), _ptr(rotation), _ptr(scale), _ptr(opacity), _ptr(color),
+            _ptr(camera_rotation), _ptr(camera_translation), pref, _ptr(projected_mean),
+            _ptr(inverse_covariance), _ptr(projected_color), _ptr(projected_opacity),
+            _ptr(bounds), _ptr(counts), stream), "gs_project_fwd")
+
+        count_bytes = lib.gs_bin_count_workspace_size(n)
+        count_ws = torch.empty((count_bytes,), dtype=torch.uint8, device=device)
+        total = ctypes.c_int64(0)
+        native.check(lib.gs_bin_count(
+            n, _ptr(projected_mean), _ptr(counts), _ptr(count_ws), count_bytes,
+            ctypes.byref(total), stream), "gs_bin_count")
+        total = total.value
+
+        gaussian_ids = torch.empty((total,), dtype=torch.int32, device=device)
+        ranges = torch.empty((num_tiles, 2), dtype=torch.int64, device=device)
+        sort_bytes = lib.gs_bin_sort_workspace_size(total, num_tiles)
+        sort_ws = torch.empty((sort_bytes,), dtype=torch.uint8, device=device)
+        native.check(lib.gs_bin_sort(
+            n, total, _ptr(bounds), _ptr(counts), pref, _ptr(count_ws), count_bytes,
+            _ptr(sort_ws), sort_bytes, _ptr(gaussian_ids), _ptr(ranges), stream), "gs_bin_sort")
+        if os.environ.get("GAUSSIAN_SPLATS_B200_CHECK") == "1":
+            native.check(lib.gs_bin_check(_ptr(count_ws), _ptr(sort_ws), stream), "binning")
+
+        image = mean.new_empty((image_height, image_width, 3))
+        final_transmittance = mean.new_empty((image_height, image_width))
+        n_contributors = torch.empty((image_height, image_width), dtype=torch.int32,
+                                     device=device)
+        native.check(lib.gs_composite_fwd(
+            _ptr(projected_mean), _ptr(inverse_covariance), _ptr(projected_color),
+            _ptr(projected_opacity), _ptr(gaussian_ids), _ptr(ranges), pref, _ptr(image),
+            _ptr(final_transmittance), _ptr(n_contributors), stream), "gs_composite_fwd")
+    return (image, final_transmittance, n_contributors, projected_mean, inverse_covariance,
+            projected_color, projected_opacity, gaussian_ids, ranges, counts)
+
+
+@_rasterize.register_fake
+def _rasterize_fake(mean, rotation, scale, opacity, color, camera_rotation, camera_translation,
+                    fx, fy, cx, cy, image_width, image_height, tile_size, opacity_threshold,
+                    near, far, rendering_mode, confidence):
+    dynamic = torch.library.get_ctx().new_dynamic_size()
+    n = mean.shape[0]
+    num_tiles = (image_height // tile_size) * (image_width // tile_size)
+    i32 = dict(dtype=torch.int32, device=mean.device)
+    return (
+        mean.new_empty((image_height, image_width, 3)),
+        mean.new_empty((image_height, image_width)),
+        torch.empty((image_height, image_width), **i32),
+        mean.new_empty((n, 3)),
+        mean.new_empty((n, 2, 2)),
+        mean.new_empty((n, 3)),
+        mean.new_empty((n, 1)),
+        torch.empty((dynamic,), **i32),
+        torch.empty((num_tiles, 2), dtype=torch.int64, device=mean.device),
+        torch.empty((n,), **i32),
+    )
+
+
+def _setup_context(ctx, inputs, output) -> None:
+    # Same saved set as interface.py:158-173: the 7 tensor inputs and outputs[1:].
+    ctx.save_for_backward(*inputs[:7], *output[1:])
+    (ctx.fx, ctx.fy, ctx.cx, ctx.cy, ctx.image_width, ctx.image_height, ctx.tile_size,
+     ctx.opacity_threshold, ctx.near, ctx.far, ctx.rendering_mode, ctx.confidence) = inputs[7:]
+
+
+def _backward(ctx, *grad_outputs):
+    """Composite backward, then projection backward (interface.py:176-239)."""
+    assert ctx.rendering_mode == "gaussian", (
+        "Backward gradients are only supported for Gaussian rendering."
+    )
+    (mean, rotation, scale, opacity, color, camera_rotation, camera_translation,
+     final_transmittance, n_contributors, projected_mean, inverse_covariance, projected_color,
+     projected_opacity, gaussian_ids, ranges, counts) = ctx.saved_tensors
+    lib = native.lib()
+    device = mean.device
+    grad_image = grad_outputs[0]
+    if grad_image is None:
+        grad_image = torch.zeros((ctx.image_height, ctx.image_width, 3), device=device)
+    grad_image = _f32(grad_image)
+    mean, rotation, scale, opacity, color = map(_f32, (mean, rotation, scale, opacity, color))
+    camera_rotation, camera_translation = _f32(camera_rotation), _f32(camera_translation)
+    n, num_sh = mean.shape[0], color.shape[1]
+    params = native.make_params(ctx.fx, ctx.fy, ctx.cx, ctx.cy, ctx.image_width,
+                                ctx.image_height, ctx.tile_size, ctx.opacity_threshold,
+                                ctx.near, ctx.far, ctx.rendering_mode, ctx.confidence)
+    pref = ctypes.byref(params)
+    with torch.cuda.device(device):
+        stream = _stream(device)
+        grad_projected = mean.new_empty((n, 9))
+        native.check(lib.gs_composite_bwd(
+            n, _ptr(projected_mean), _ptr(inverse_covariance), _ptr(projected_color),
+            _ptr(projected_opacity), _ptr(gaussian_ids), _ptr(ranges), _ptr(grad_image),
+            _ptr(final_transmittance), _ptr(n_contributors), pref, _ptr(grad_projected),
+            stream), "gs_composite_bwd")
+        grad_mean = torch.empty_like(mean)
+        grad_rotation = torch.empty_like(rotation)
+        grad_scale = torch.empty_like(scale)
+        grad_opacity = torch.empty_like(opacity)
+        grad_color = torch.empty_like(color)
+        native.check(lib.gs_project_bwd(
+            n, num_sh, _ptr(mean), _ptr(rotation), _ptr(scale), _ptr(opacity), _ptr(color),
+            _ptr(camera_rotation), _ptr(camera_translation), _ptr(inverse_covariance),
+            _ptr(grad_projected), _ptr(counts), pref, _ptr(grad_mean), _ptr(grad_rotation),
+            _ptr(grad_scale), _ptr(grad_opacity), _ptr(grad_color), stream), "gs_project_bwd")
+    gradients = (grad_mean, grad_rotation, grad_scale, grad_opacity, grad_color)
+    return (*gradients, *(None,) * (19 - len(gradients)))
+
+
+torch.library.register_autograd(
+    "gaussian_splats::rasterize", _backward, setup_context=_setup_context
+)
+
+
+def rasterize_outputs(
+    splats,
+    camera: Camera,
+    tile_size: int = 4,
+    opacity_threshold: float = 0.999,
+    near: float = 0.2,
+    far: float = 100.0,
+    rendering_mode: Literal["gaussian", "ellipsoid"] = "gaussian",
+    confidence: float = 0.95,
+    indices: torch.Tensor | None = None,
+) -> tuple[torch.Tensor, ...]:
+    """All ten operator outputs for ``splats`` seen by ``camera``."""
+    fx, fy = camera.focal_length
+    cx, cy = camera.principal_point
+    image_width, image_height = camera.image_size
+    assert tile_size > 0 and tile_size & (tile_size - 1) == 0
+    assert image_width % tile_size == 0 and image_height % tile_size == 0
+    mean, rotation, scale, opacity, color = (
+        splats.mean, splats.rotation, splats.scale, splats.opacity, splats.color,
+    )
+    if indices is not None:
+        mean, rotation, scale, opacity, color = (
+            mean[indices], rotation[indices], scale[indices], opacity[indices], color[indices],
+        )
+    return torch.ops.gaussian_splats.rasterize(
+        mean, rotation, scale, opacity, color,
+        camera.rotation_matrix.to(mean.device), camera.translation.to(mean.device),
+        float(fx), float(fy), float(cx), float(cy), int(image_width), int(image_height),
+        int(tile_size), float(opacity_threshold), float(near), float(far), rendering_mode,
+        float(confidence),
+    )
+
+
+def rasterize(
+    splats,
+    camera: Camera,
+    tile_size: int = 4,
+    opacity_threshold: float = 0.999,
+    near: float = 0.2,
+    far: float = 100.0,
+    rendering_mode: Literal["gaussian", "ellipsoid"] = "gaussian",
+    confidence: float = 0.95,
+    indices: torch.Tensor | None = None,
+    backend: str | None = None,
+) -> torch.Tensor:
+    """Render ``splats`` to an ``[H, W, 3]`` float image.
+
+    Signature of the reference's ``splats.rasterize.rasterize``
+    (splats/rasterize.py:12-43) and ``kernels.rasterize.interface.rasterize``
+    (interface.py:247-303). ``backend`` exists for call-site compatibility:
+    ``None``, ``"b200"`` and ``"triton"`` (the reference's name for the kernel
+    path this library replaces) all run the B200 kernels; anything else raises
+    ``ValueError`` like the reference's dispatch.
+    """
+    if backend not in (None, "b200", "triton"):
+        raise ValueError(f"Unknown rasterization backend: {backend}")
+    return rasterize_outputs(splats, camera, tile_size, opacity_threshold, near, far,
+                             rendering_mode, confidence, indices)[0]

@@ -1,0 +1,152 @@
+/*
+ * gs_b200.h -- C ABI of the B200 (sm_100a) Gaussian-splat rasterizer.
+ *
+ * Drop-in kernels for the reference's `gaussian_splats::rasterize` operator
+ * (VikaasVarma/gaussian-splats, src/gaussian_splats/kernels/rasterize/
+ * interface.py:17-244). Each entry point below replaces one stage that the
+ * reference's Python operator launches; the host wrapper (the package's
+ * rasterize.py, or any FFI caller) chains them exactly as interface.py does.
+ *
+ * Conventions shared by every entry point:
+ *  - All array arguments are DEVICE pointers to contiguous row-major data on
+ *    the current device, except where a name ends in `_host`.
+ *  - Nothing here allocates memory. Scratch comes from the caller as
+ *    `workspace` buffers (256-byte aligned) of the sizes the matching
+ *    `*_workspace_size` queries return. rotation, inverse_covariance,
+ *    grad_rotation and bounds rows are read/written as 16-byte vectors and
+ *    must be 16-byte aligned; so must color when K is 4 or 16.
+ *  - Work is enqueued on `stream`; only gs_bin_count() synchronises it.
+ *  - Return value: GS_OK (0) or a negative GS_ERR_* code. CUDA launch errors
+ *    are reported as GS_ERR_CUDA; gs_last_cuda_error() returns the code.
+ *  - Gaussian tensors follow splats/splats.py: mean [N,3], rotation [N,4]
+ *    (w,x,y,z, any norm), scale [N,3] (log sigma), opacity [N,1] (logit),
+ *    color [N,K,3] (real SH, K = (degree+1)^2 <= 25).
+ */
+#ifndef GS_B200_H
+#define GS_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st *gs_stream_t; /* a cudaStream_t; NULL = legacy default stream */
+
+enum {
+  GS_OK = 0,
+  GS_ERR_INVALID_ARGUMENT = -1, /* sizes, tile size or mode out of range */
+  GS_ERR_CUDA = -2,             /* a CUDA runtime call or launch failed */
+  GS_ERR_CAPACITY = -3,         /* more intersections than the buffers hold */
+  GS_ERR_UNSUPPORTED = -4,      /* SH degree above 4 */
+  GS_ERR_MISALIGNED = -5,       /* a buffer misses its required alignment */
+  GS_ERR_TIMEOUT = -6           /* a bounded device-side wait gave up (results invalid) */
+};
+
+/* Scalars of one render, folded on the host the way the reference folds its
+ * Triton constexprs (in double, then rounded to float):
+ *   lim_x = 1.3 * tiles_w * tile_size / (2 fx)      project.py:158
+ *   lim_y = 1.3 * tiles_h * tile_size / (2 fy)      project.py:159
+ *   bwd_lim_x = 1.3 * width / (2 fx)                 project_bwd.py:376
+ *   bwd_lim_y = 1.3 * height / (2 fy)                project_bwd.py:377
+ *   extent = sqrt(-2 log1p(-confidence)) if ellipsoid else 3    project.py:308
+ *   cutoff = -2 log1p(-confidence)                   composite.py:226  */
+typedef struct gs_params {
+  float fx, fy, cx, cy;
+  int32_t width, height, tile_size; /* width, height: multiples of tile_size */
+  int32_t gaussian_mode;            /* 1: Gaussian falloff; 0: ellipsoid indicator */
+  float near_plane, far_plane;
+  float lim_x, lim_y, bwd_lim_x, bwd_lim_y;
+  float extent, cutoff, opacity_threshold;
+} gs_params;
+
+/* Library version, for load-time checks. */
+int32_t gs_version(void);
+
+/* cudaError_t of the last failing CUDA call made by this library. */
+int32_t gs_last_cuda_error(void);
+
+/* Projection + SH + tile counting: replaces _project_and_count_kernel and
+ * its launcher (project.py:74-345). Writes the four projected op outputs,
+ * per-Gaussian tile counts and the tile rectangles
+ * bounds [N,4] = (xmin, xmax, ymin, ymax) used by gs_bin_*. */
+int32_t gs_project_fwd(int64_t n, int32_t num_sh, const float *mean, const float *rotation,
+                       const float *scale, const float *opacity, const float *color,
+                       const float *camera_rotation, const float *camera_translation,
+                       const gs_params *params, float *projected_mean,
+                       float *inverse_covariance, float *projected_color,
+                       float *projected_opacity, int32_t *bounds, int32_t *counts,
+                       gs_stream_t stream);
+
+/* Binning, phase 1: the host sync of emit_intersections
+ * (intersections.py:51-52). Orders the Gaussians with counts > 0 by depth
+ * (stable: equal depth bits keep index order), prefix-sums their counts in
+ * that order, copies the intersection total to *total_host and synchronises
+ * `stream`. `workspace` (gs_bin_count_workspace_size(n) bytes) must be passed
+ * unchanged to the following gs_bin_sort. Fails with GS_ERR_CAPACITY if the
+ * total reaches 2^30. */
+int32_t gs_bin_count(int64_t n, const float *projected_mean, const int32_t *counts,
+                     void *workspace, uint64_t workspace_bytes, int64_t *total_host,
+                     gs_stream_t stream);
+uint64_t gs_bin_count_workspace_size(int64_t n);
+
+/* Binning, phase 2: emit + sort + tile ranges, replacing _emit_intersections
+ * (intersections.py:10-74) and sort_intersections (intersections.py:77-88).
+ * gaussian_ids [total] receives the Gaussian index of every (tile, Gaussian)
+ * intersection ordered by (tile, depth bits, Gaussian index) -- the order of
+ * the reference's stable sort of (tile << 32 | depth bits) keys emitted in
+ * Gaussian order; ranges [num_tiles, 2] receives each tile's [start, end).
+ * count_workspace is the buffer gs_bin_count filled; sort_workspace holds
+ * gs_bin_sort_workspace_size(total, num_tiles) bytes of scratch. */
+int32_t gs_bin_sort(int64_t n, int64_t total, const int32_t *bounds, const int32_t *counts,
+                    const gs_params *params, const void *count_workspace,
+                    uint64_t count_workspace_bytes, void *sort_workspace,
+                    uint64_t sort_workspace_bytes, int32_t *gaussian_ids, int64_t *ranges,
+                    gs_stream_t stream);
+uint64_t gs_bin_sort_workspace_size(int64_t total, int64_t num_tiles);
+
+/* Front-to-back compositing: replaces _composite_kernel (composite.py:25-162).
+ * image [H,W,3], final_transmittance [H,W], n_contributors [H,W] int32. */
+int32_t gs_composite_fwd(const float *projected_mean, const float *inverse_covariance,
+                         const float *projected_color, const float *projected_opacity,
+                         const int32_t *gaussian_ids, const int64_t *ranges,
+                         const gs_params *params, float *image, float *final_transmittance,
+                         int32_t *n_contributors, gs_stream_t stream);
+
+/* Back-to-front compositing gradients: replaces _composite_bwd_kernel and the
+ * index_add_ reduction (composite_bwd.py:47-277). Accumulates into
+ * grad_projected [N,9] = (d mean_x, d mean_y, d conic_xx, d conic_xy,
+ * d conic_yy, d r, d g, d b, d opacity), which this call zeroes first. */
+int32_t gs_composite_bwd(int64_t n, const float *projected_mean, const float *inverse_covariance,
+                         const float *projected_color, const float *projected_opacity,
+                         const int32_t *gaussian_ids, const int64_t *ranges,
+                         const float *grad_image, const float *final_transmittance,
+                         const int32_t *n_contributors, const gs_params *params,
+                         float *grad_projected, gs_stream_t stream);
+
+/* Parameter gradients: replaces _project_bwd_kernel (project_bwd.py:8-381).
+ * SH gradients cover coefficients 0..15; coefficients 16..24 get zero. */
+int32_t gs_project_bwd(int64_t n, int32_t num_sh, const float *mean, const float *rotation,
+                       const float *scale, const float *opacity, const float *color,
+                       const float *camera_rotation, const float *camera_translation,
+                       const float *inverse_covariance, const float *grad_projected,
+                       const int32_t *counts, const gs_params *params, float *grad_mean,
+                       float *grad_rotation, float *grad_scale, float *grad_opacity,
+                       float *grad_color, gs_stream_t stream);
+
+/* Binning error word of a count workspace (0 = fine, else some device-side
+ * bounded wait in the last gs_bin_count / gs_bin_sort on these workspaces
+ * gave up). Synchronises `stream`. */
+int32_t gs_bin_check(const void *count_workspace, const void *sort_workspace,
+                     gs_stream_t stream);
+
+/* The deterministic exp / log the kernels use, applied elementwise (test hook
+ * for bitwise agreement with the CPU oracle). */
+int32_t gs_det_exp(int64_t n, const float *x, float *y, gs_stream_t stream);
+int32_t gs_det_log(int64_t n, const float *x, float *y, gs_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GS_B200_H */

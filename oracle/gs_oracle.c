@@ -270,7 +270,9 @@ static inline float pair_d2(float dx, float dy, float xx, float xy, float yy) {
     return fmaf(xx * dx, dx, fmaf((2.0f * xy) * dx, dy, (yy * dy) * dy));
 }
 
+/* A NaN distance (only reachable from a degenerate conic) contributes nothing. */
 static inline float pair_probability(float d2, const gso_params *p) {
+    if (d2 != d2) return 0.0f;
     return p->gaussian_mode ? gso_exp(-0.5f * d2) : (d2 <= p->cutoff ? 1.0f : 0.0f);
 }
 
@@ -345,13 +347,16 @@ void gso_composite_bwd(int64_t n, const float *projected_mean, const float *inve
                        const int32_t *gaussian_ids, const int64_t *ranges, int64_t total,
                        const float *grad_image, const float *final_transmittance,
                        const int32_t *n_contributors, const gso_params *p,
-                       float *grad_projected) {
+                       const int32_t *tiles, int32_t num_listed, float *grad_projected) {
+    /* `tiles` (optional) restricts the walk to the listed tiles; the caller
+     * guarantees grad_image is zero elsewhere, where rows would be zero. */
     const int ts = p->tile_size, tiles_w = p->width / ts, W = p->width;
-    const int32_t num_tiles = (p->height / ts) * tiles_w;
+    const int32_t num_tiles = tiles ? num_listed : (p->height / ts) * tiles_w;
     const float thr = p->opacity_threshold;
     float *rows = (float *)calloc((size_t)(total ? total : 1) * 9, sizeof(float));
 #pragma omp parallel for schedule(dynamic, 1)
-    for (int32_t tile = 0; tile < num_tiles; ++tile) {
+    for (int32_t which = 0; which < num_tiles; ++which) {
+        int32_t tile = tiles ? tiles[which] : which;
         int npix = ts * ts;
         float *st = (float *)malloc(sizeof(float) * npix * 4);
         float *sc = st + npix;

@@ -68,7 +68,7 @@ def lib() -> ctypes.CDLL:
         _lib.gso_composite.argtypes = [_f32p, _f32p, _f32p, _f32p, _i32p, _i64p, P,
                                        ctypes.c_void_p, i32, _f32p, _f32p, _i32p]
         _lib.gso_composite_bwd.argtypes = [i64, _f32p, _f32p, _f32p, _f32p, _i32p, _i64p, i64,
-                                           _f32p, _f32p, _i32p, P, _f32p]
+                                           _f32p, _f32p, _i32p, P, ctypes.c_void_p, i32, _f32p]
         _lib.gso_project_bwd.argtypes = [i64, _f32p, _f32p, _f32p, _f32p, _f32p, i32, _f32p, _f32p,
                                          _f32p, _f32p, _i32p, P, _f32p, _f32p, _f32p, _f32p,
                                          _f32p]
@@ -187,16 +187,20 @@ def rasterize(mean, rotation, scale, opacity, color, camera_rotation, camera_tra
     return out
 
 
-def composite_bwd(fwd: dict, grad_image, s: Settings) -> np.ndarray:
+def composite_bwd(fwd: dict, grad_image, s: Settings, tiles=None) -> np.ndarray:
+    """grad_projected [N, 9]. With ``tiles``, only those tiles are walked; the
+    caller must pass a grad_image that is zero on every other tile."""
     n = fwd["projected_mean"].shape[0]
     grad = np.empty((n, 9), np.float32)
     p = s.params()
+    tiles_arr = None if tiles is None else _c(tiles, np.int32)
     lib().gso_composite_bwd(n, _c(fwd["projected_mean"]), _c(fwd["inverse_covariance"]),
                             _c(fwd["projected_color"]), _c(fwd["projected_opacity"]),
                             _c(fwd["gaussian_ids"], np.int32), _c(fwd["ranges"], np.int64),
                             len(fwd["gaussian_ids"]), _c(grad_image),
                             _c(fwd["final_transmittance"]), _c(fwd["n_contributors"], np.int32),
-                            ctypes.byref(p), grad)
+                            ctypes.byref(p), None if tiles_arr is None else tiles_arr.ctypes.data,
+                            0 if tiles_arr is None else len(tiles_arr), grad)
     return grad
 
 
@@ -216,9 +220,9 @@ def project_bwd(mean, rotation, scale, opacity, color, camera_rotation, camera_t
     return out
 
 
-def backward(inputs: dict, fwd: dict, grad_image, s: Settings) -> dict:
+def backward(inputs: dict, fwd: dict, grad_image, s: Settings, tiles=None) -> dict:
     """Parameter gradients for ``grad_image`` (interface.py:176-239)."""
-    grad_projected = composite_bwd(fwd, grad_image, s)
+    grad_projected = composite_bwd(fwd, grad_image, s, tiles)
     grads = project_bwd(inputs["mean"], inputs["rotation"], inputs["scale"], inputs["opacity"],
                         inputs["color"], inputs["camera_rotation"], inputs["camera_translation"],
                         fwd["inverse_covariance"], grad_projected, fwd["counts"], s)
