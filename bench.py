@@ -1,0 +1,391 @@
+"""Benchmark: config 2 -- one 1920x1080 view of 1M Gaussians (SH degree 3),
+forward + backward with an L1 loss -- per GPU.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+With N > 1 (launched by torchrun, one rank per GPU) every rank renders its own
+camera of the same replicated scene and the parameter gradients are summed
+with one NCCL all-reduce per step (view-parallel training, weak scaling).
+Rank 0 prints one JSON line. ``value`` is views/s over all ranks, timed with
+CUDA events over K steps (max over ranks). Inputs exceed the 126 MB L2
+(236 MB of Gaussian parameters are read every step), so no flush is needed.
+
+``--impl reference`` times the reference algorithm on the host CPU cores: the
+C restatement of the reference's rasterizer in ``oracle/`` (the reference is
+Python with Triton kernels and does not travel to the GPU box). Each step is a
+bounded sample of the view -- projection, binning and projection backward of
+all Gaussians, compositing forward and backward of a sample of tiles scaled to
+all tiles.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "fwd / fwd+bwd ms per 1080p view at 1M Gaussians; views/sec at 1/2/4/8 GPUs"
+UNIT = "views/s"
+WORKLOAD = "config2: 1M Gaussians SH3, 1920x1080 (rendered 1920x1088), 16x16 tiles, fwd+bwd L1"
+# Algorithmic bytes per Gaussian (K = 16 SH coefficients): projection reads
+# mean, rotation, scale, opacity (44 B) and colour (192 B) and writes
+# projected mean, conic, colour, opacity, tile rectangle, count (64 B);
+# projection backward reads the same parameters plus conic, the 9-float
+# screen-space gradient and the count (56 B) and writes 236 B of gradients.
+PROJECT_FWD_BYTES = 44 + 12 * 16 + 64
+PROJECT_BWD_BYTES = 44 + 12 * 16 + 56 + 44 + 12 * 16
+# Per evaluated (pixel, Gaussian) pair, the reference's forward arithmetic
+# (composite.py:159-186): offsets 2, distance 9, exp argument 1, exp 1,
+# alpha 4, activity test 3, weight 2, colour 6, transmittance 3.
+COMPOSITE_FWD_FLOPS = 31
+# Backward per evaluated pair (composite_bwd.py:101-195 without the dropped
+# abs-gradient): distance and alpha 16, T recovery 5, weight gradient 9,
+# alpha/opacity/distance gradients 6, mean/conic gradients 14, colour 4,
+# suffix update 10.
+COMPOSITE_BWD_FLOPS = 64
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    p.add_argument("--points", type=int, default=1_000_000)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            peaks = json.load(f)
+        return float(peaks["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_rank{index}.csv")
+
+    def __enter__(self):
+        try:
+            os.makedirs(os.path.dirname(self.path), exist_ok=True)
+            self.file = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", str(self.index), "-lms", "200"], stdout=self.file,
+                stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            self.proc.wait(timeout=10)
+            self.file.close()
+
+    def summary(self):
+        if self.proc is None:
+            return None
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) >= 9 and parts[1].replace(".", "").isdigit():
+                    rows.append(parts)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows]
+        reasons = set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for r in rows:
+            for name, flag in zip(names, r[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": float(rows[0][2]),
+                "samples": len(rows), "reasons": sorted(reasons)}
+
+
+def make_view(scene, rank):
+    """Rank 0 renders config 2's camera; other ranks a camera from the same
+    recipe (radius 5, random direction) seeded by rank."""
+    from gaussian_splats_b200 import scenes
+
+    if rank == 0:
+        return scene.cameras[0], scene.targets[0]
+    g = torch.Generator().manual_seed(1000 + rank)
+    cam = scenes.look_at_camera(5.0 * scenes.random_direction(g), fovy_degrees=50.0,
+                                width=1920, height=1080)
+    return cam, torch.rand(1080, 1920, 3, generator=g)
+
+
+def run_reference(args, rank, world):
+    """CPU restatement of the reference, timed on this host's cores (rank 0)."""
+    if rank != 0:
+        return
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+
+    from gaussian_splats_b200 import scenes
+
+    scene = scenes.config2(num_points=args.points)
+    cores = os.cpu_count() or 1
+    os.environ.setdefault("OMP_NUM_THREADS", str(cores))
+    step_s = []
+    sample = None
+    for i in range(args.warmup + args.steps):
+        seconds, sample = cpu_view_seconds(O, scene, tiles=256, seed=i)
+        if i >= args.warmup:
+            step_s.append(seconds)
+    per_view = statistics.median(step_s)
+    value = 1.0 / per_view
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_view * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": {"workload": WORKLOAD},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def cpu_view_seconds(O, scene, tiles, seed):
+    """Seconds for one config-2 view on the CPU oracle: projection, binning and
+    projection backward of all Gaussians timed in full; compositing forward and
+    backward timed on `tiles` random tiles and scaled to all tiles."""
+    inputs, s = O.scene_inputs(scene)
+    keys = ("mean", "rotation", "scale", "opacity", "color", "camera_rotation",
+            "camera_translation")
+    t0 = time.perf_counter()
+    proj = O.project(*(inputs[k] for k in keys), s)
+    t1 = time.perf_counter()
+    binned = O.bin(proj["bounds"], proj["projected_mean"][:, 2], proj["counts"], s)
+    t2 = time.perf_counter()
+    rng = np.random.default_rng(seed)
+    chosen = rng.choice(s.num_tiles, size=min(tiles, s.num_tiles), replace=False).astype(np.int32)
+    comp = O.composite(proj["projected_mean"], proj["inverse_covariance"],
+                       proj["projected_color"], proj["projected_opacity"],
+                       binned["gaussian_ids"], binned["ranges"], s, tiles=chosen)
+    t3 = time.perf_counter()
+    fwd = dict(proj, **binned, **comp)
+    grad_image = np.full((s.height, s.width, 3), 1.0 / (1920 * 1080 * 3), np.float32)
+    grad_projected = O.composite_bwd(fwd, grad_image, s, tiles=chosen)
+    t4 = time.perf_counter()
+    O.project_bwd(*(inputs[k] for k in keys), proj["inverse_covariance"], grad_projected,
+                  proj["counts"], s)
+    t5 = time.perf_counter()
+    scale = s.num_tiles / len(chosen)
+    seconds = (t1 - t0) + (t2 - t1) + (t3 - t2) * scale + (t4 - t3) * scale + (t5 - t4)
+    sample = (f"one config-2 view: projection, binning, projection backward of all "
+              f"{scene.num_points} Gaussians; composite fwd+bwd on {len(chosen)} of "
+              f"{s.num_tiles} random tiles scaled by {scale:.1f}")
+    return seconds, sample
+
+
+def main():
+    args = parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        torch.distributed.init_process_group(
+            "nccl" if args.impl == "b200" else "gloo",
+            timeout=datetime.timedelta(seconds=120))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        if world > 1:
+            torch.distributed.destroy_process_group()
+        return
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    from gaussian_splats_b200 import scenes
+    from gaussian_splats_b200.rasterize import StageTimer, rasterize_outputs
+    from gaussian_splats_b200.splats import GaussianSplat
+
+    scene = scenes.config2(num_points=args.points)
+    camera, target_cpu = make_view(scene, rank)
+    crop_w, crop_h = scene.crop
+    host = [t.contiguous() for t in scene.tensors()]
+    params = [t.to(device) for t in host]
+    splats = GaussianSplat.from_tensors(*params)
+    for p in splats.parameters():
+        p.requires_grad_(p is not splats.normals)
+    camera = camera.to(device)
+    target = target_cpu.to(device)
+    trainable = [splats.mean, splats.rotation, splats.scale, splats.opacity, splats.color]
+    settings = scene.settings
+
+    def render(s):
+        return rasterize_outputs(s, camera, settings.tile_size, settings.opacity_threshold,
+                                 settings.near, settings.far)
+
+    def train_step():
+        for p in trainable:
+            p.grad = None
+        out = render(splats)
+        loss = (out[0][:crop_h, :crop_w] - target).abs().mean()
+        loss.backward()
+        if world > 1:
+            flat = torch.cat([p.grad.reshape(-1) for p in trainable])
+            torch.distributed.all_reduce(flat)
+        return loss, out
+
+    def timed(fn, steps):
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(steps):
+            fn()
+        end.record()
+        torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+        ms = start.elapsed_time(end) / steps
+        if world > 1:
+            t = torch.tensor([ms], device=device)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            ms = float(t)
+        return ms
+
+    # Forward only.
+    with torch.no_grad():
+        for _ in range(args.warmup):
+            render(splats)
+        fwd_ms = timed(lambda: render(splats), args.steps)
+
+    # Forward + backward (+ all-reduce): the headline.
+    for _ in range(args.warmup):
+        train_step()
+    with ClockSampler(local_rank) as clocks, StageTimer() as stages:
+        ms = timed(train_step, args.steps)
+    stage_ms = stages.durations()
+    clock = clocks.summary()
+    value = world * 1000.0 / ms
+
+    # Structure of the view (for the roofline's work counts).
+    with torch.no_grad():
+        out = render(splats)
+        n_contrib = int(out[2].sum())
+        intersections = int(out[7].numel())
+        visible = int((out[9] > 0).sum())
+
+    # End to end through the public API with host buffers: each step copies the
+    # Gaussian parameters and the target from pinned host memory, renders
+    # forward + backward, and reads the loss back.
+    pinned = [t.pin_memory() for t in host]
+    target_pinned = target_cpu.pin_memory()
+    e2e_params = [torch.empty_like(p) for p in params]
+    e2e_target = torch.empty_like(target)
+    e2e_splats = GaussianSplat.from_tensors(*e2e_params)
+    e2e_trainable = [e2e_splats.mean, e2e_splats.rotation, e2e_splats.scale,
+                     e2e_splats.opacity, e2e_splats.color]
+    h2d = sum(t.numel() * t.element_size() for t in host) + target_cpu.numel() * 4
+
+    def e2e_step():
+        with torch.no_grad():
+            for dst, src in zip(e2e_params, pinned):
+                dst.copy_(src, non_blocking=True)
+            e2e_target.copy_(target_pinned, non_blocking=True)
+        for p in e2e_trainable:
+            p.grad = None
+            p.requires_grad_(True)
+        out = render(e2e_splats)
+        loss = (out[0][:crop_h, :crop_w] - e2e_target).abs().mean()
+        loss.backward()
+        if world > 1:
+            flat = torch.cat([p.grad.reshape(-1) for p in e2e_trainable])
+            torch.distributed.all_reduce(flat)
+        return loss.item()
+
+    for _ in range(max(1, args.warmup // 2)):
+        e2e_step()
+    e2e_ms = timed(e2e_step, max(3, args.steps // 2))
+
+    hbm_peak, peak_kind = load_peaks()
+    launches_per_step = 15  # 1 projection, 6 count-phase, 5 sort-phase, 2 composite, 1 proj bwd
+    n = scene.num_points
+    rooflines = {}
+    if "project_fwd" in stage_ms:
+        gbs = n * PROJECT_FWD_BYTES / (stage_ms["project_fwd"] * 1e-3) / 1e9
+        rooflines["project_fwd"] = {"bound": "hbm", "achieved": gbs, "peak": hbm_peak,
+                                    "unit": "GB/s", "frac": gbs / hbm_peak,
+                                    "ms": stage_ms["project_fwd"]}
+    if "project_bwd" in stage_ms:
+        gbs = n * PROJECT_BWD_BYTES / (stage_ms["project_bwd"] * 1e-3) / 1e9
+        rooflines["project_bwd"] = {"bound": "hbm", "achieved": gbs, "peak": hbm_peak,
+                                    "unit": "GB/s", "frac": gbs / hbm_peak,
+                                    "ms": stage_ms["project_bwd"]}
+    traffic = None
+    profile_json = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(profile_json):
+        with open(profile_json) as f:
+            traffic = json.load(f)
+    dominant = max(stage_ms, key=stage_ms.get) if stage_ms else None
+    main_roof = rooflines.get("project_fwd")
+    if main_roof is not None:
+        main_roof = dict(main_roof, kernel="project_fwd",
+                         traffic=(traffic or {}).get("project_fwd"),
+                         note=f"peak: {peak_kind} hbm_gbs")
+
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "fwd_ms": fwd_ms, "fwd_bwd_ms": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded config-2 scene, random L1 target)",
+        "config": {"workload": WORKLOAD, "gaussians": n, "image": [1920, 1080],
+                   "tile_size": settings.tile_size, "views_per_rank_per_step": 1,
+                   "parallelism": f"view-parallel x{world}, NCCL all-reduce of gradients"
+                   if world > 1 else "single GPU",
+                   "l2": "inputs larger than L2 (236 MB of parameters read per step)"},
+        "stage_ms": stage_ms, "dominant_stage": dominant,
+        "view": {"visible": visible, "intersections": intersections,
+                 "evaluated_pairs_fwd": n_contrib},
+        "roofline": main_roof, "rooflines": rooflines,
+        "e2e": {"value": world * 1000.0 / e2e_ms, "unit": UNIT, "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4},
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clock,
+    }
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle as O
+
+        cpu_scene = scenes.config2(num_points=args.points)
+        seconds, sample = cpu_view_seconds(O, cpu_scene, tiles=256, seed=0)
+        line["cpu_baseline"] = {"value": 1.0 / seconds, "unit": UNIT,
+                                "cores": os.cpu_count(), "kind": "port", "sample": sample}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -69,6 +69,48 @@ def _f32(t: torch.Tensor) -> torch.Tensor:
     return t.detach().to(torch.float32).contiguous()
 
 
+class StageTimer:
+    """Records a CUDA event on the launching stream after each stage.
+
+    Install with ``with StageTimer() as timer:``; ``timer.durations()`` then
+    returns milliseconds per stage name summed over the recorded calls. Off
+    (no events) unless installed.
+    """
+
+    active: "StageTimer | None" = None
+
+    def __init__(self):
+        self.marks: list[tuple[str, torch.cuda.Event]] = []
+
+    def __enter__(self):
+        StageTimer.active = self
+        return self
+
+    def __exit__(self, *exc):
+        StageTimer.active = None
+
+    def mark(self, name: str) -> None:
+        event = torch.cuda.Event(enable_timing=True)
+        event.record()
+        self.marks.append((name, event))
+
+    def durations(self) -> dict[str, float]:
+        torch.cuda.synchronize()
+        out: dict[str, float] = {}
+        counts: dict[str, int] = {}
+        for (_, before), (name, after) in zip(self.marks, self.marks[1:]):
+            if name.startswith("begin"):
+                continue
+            out[name] = out.get(name, 0.0) + before.elapsed_time(after)
+            counts[name] = counts.get(name, 0) + 1
+        return {k: v / counts[k] for k, v in out.items()}
+
+
+def _mark(name: str) -> None:
+    if StageTimer.active is not None:
+        StageTimer.active.mark(name)
+
+
 @torch.library.custom_op("gaussian_splats::rasterize", mutates_args=())
 def _rasterize(
     mean: torch.Tensor,
@@ -114,6 +156,7 @@ def _rasterize(
     num_tiles = (image_width // tile_size) * (image_height // tile_size)
     with torch.cuda.device(device):
         stream = _stream(device)
+        _mark("begin_forward")
         projected_mean = mean.new_empty((n, 3))
         inverse_covariance = mean.new_empty((n, 2, 2))
         projected_color = mean.new_empty((n, 3))
@@ -125,6 +168,7 @@ def _rasterize(
             _ptr(camera_rotation), _ptr(camera_translation), pref, _ptr(projected_mean),
             _ptr(inverse_covariance), _ptr(projected_color), _ptr(projected_opacity),
             _ptr(bounds), _ptr(counts), stream), "gs_project_fwd")
+        _mark("project_fwd")
 
         count_bytes = lib.gs_bin_count_workspace_size(n)
         count_ws = torch.empty((count_bytes,), dtype=torch.uint8, device=device)
@@ -133,6 +177,7 @@ def _rasterize(
             n, _ptr(projected_mean), _ptr(counts), _ptr(count_ws), count_bytes,
             ctypes.byref(total), stream), "gs_bin_count")
         total = total.value
+        _mark("bin_count")
 
         gaussian_ids = torch.empty((total,), dtype=torch.int32, device=device)
         ranges = torch.empty((num_tiles, 2), dtype=torch.int64, device=device)
@@ -141,6 +186,7 @@ def _rasterize(
         native.check(lib.gs_bin_sort(
             n, total, _ptr(bounds), _ptr(counts), pref, _ptr(count_ws), count_bytes,
             _ptr(sort_ws), sort_bytes, _ptr(gaussian_ids), _ptr(ranges), stream), "gs_bin_sort")
+        _mark("bin_sort")
         if os.environ.get("GAUSSIAN_SPLATS_B200_CHECK") == "1":
             native.check(lib.gs_bin_check(_ptr(count_ws), _ptr(sort_ws), stream), "binning")
 
@@ -152,6 +198,7 @@ def _rasterize(
             _ptr(projected_mean), _ptr(inverse_covariance), _ptr(projected_color),
             _ptr(projected_opacity), _ptr(gaussian_ids), _ptr(ranges), pref, _ptr(image),
             _ptr(final_transmittance), _ptr(n_contributors), stream), "gs_composite_fwd")
+        _mark("composite_fwd")
     return (image, final_transmittance, n_contributors, projected_mean, inverse_covariance,
             projected_color, projected_opacity, gaussian_ids, ranges, counts)
 
@@ -208,12 +255,14 @@ def _backward(ctx, *grad_outputs):
     pref = ctypes.byref(params)
     with torch.cuda.device(device):
         stream = _stream(device)
+        _mark("begin_backward")
         grad_projected = mean.new_empty((n, 9))
         native.check(lib.gs_composite_bwd(
             n, _ptr(projected_mean), _ptr(inverse_covariance), _ptr(projected_color),
             _ptr(projected_opacity), _ptr(gaussian_ids), _ptr(ranges), _ptr(grad_image),
             _ptr(final_transmittance), _ptr(n_contributors), pref, _ptr(grad_projected),
             stream), "gs_composite_bwd")
+        _mark("composite_bwd")
         grad_mean = torch.empty_like(mean)
         grad_rotation = torch.empty_like(rotation)
         grad_scale = torch.empty_like(scale)
@@ -224,6 +273,7 @@ def _backward(ctx, *grad_outputs):
             _ptr(camera_rotation), _ptr(camera_translation), _ptr(inverse_covariance),
             _ptr(grad_projected), _ptr(counts), pref, _ptr(grad_mean), _ptr(grad_rotation),
             _ptr(grad_scale), _ptr(grad_opacity), _ptr(grad_color), stream), "gs_project_bwd")
+        _mark("project_bwd")
     gradients = (grad_mean, grad_rotation, grad_scale, grad_opacity, grad_color)
     return (*gradients, *(None,) * (19 - len(gradients)))
 

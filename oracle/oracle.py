@@ -258,3 +258,21 @@ def load_golden(path: str) -> tuple[dict, Settings, dict]:
                  confidence=float(inputs["confidence"]))
     expected = {k: d[k] for k in d.files if not k.startswith("in_")}
     return inputs, s, expected
+
+
+def scene_inputs(scene, view: int = 0) -> tuple[dict, Settings]:
+    """Numpy inputs and settings for one camera of a scene object (duck-typed:
+    ``tensors()``, ``cameras``, ``settings`` as in the package's scenes)."""
+    camera = scene.cameras[view]
+    fx, fy = camera.focal_length
+    cx, cy = camera.principal_point
+    w, h = camera.image_size
+    st = scene.settings
+    names = ("mean", "rotation", "scale", "opacity", "color")
+    inputs = {k: t.detach().cpu().numpy() for k, t in zip(names, scene.tensors())}
+    inputs["camera_rotation"] = camera.rotation_matrix.cpu().numpy()
+    inputs["camera_translation"] = camera.translation.cpu().numpy()
+    settings = Settings(fx=fx, fy=fy, cx=cx, cy=cy, width=w, height=h, tile_size=st.tile_size,
+                        opacity_threshold=st.opacity_threshold, near=st.near, far=st.far,
+                        rendering_mode=st.rendering_mode, confidence=st.confidence)
+    return inputs, settings

@@ -115,18 +115,7 @@ def scene_inputs(scene, view=0):
     """Numpy operator inputs and oracle settings of a ``scenes.Scene`` view."""
     import oracle as O
 
-    camera = scene.cameras[view]
-    fx, fy = camera.focal_length
-    cx, cy = camera.principal_point
-    w, h = camera.image_size
-    st = scene.settings
-    inputs = {k: t.numpy() for k, t in zip(PARAM_NAMES, scene.tensors())}
-    inputs["camera_rotation"] = camera.rotation_matrix.numpy()
-    inputs["camera_translation"] = camera.translation.numpy()
-    settings = O.Settings(fx=fx, fy=fy, cx=cx, cy=cy, width=w, height=h, tile_size=st.tile_size,
-                          opacity_threshold=st.opacity_threshold, near=st.near, far=st.far,
-                          rendering_mode=st.rendering_mode, confidence=st.confidence)
-    return inputs, settings
+    return O.scene_inputs(scene, view)
 
 
 def l1_grad_image(image, target, crop):
@@ -143,8 +132,9 @@ def l1_grad_image(image, target, crop):
 INPUTS_ORDER = PARAM_NAMES + ("camera_rotation", "camera_translation")
 
 
-def run_binning(bounds, depths, counts, width, height, tile_size=1):
-    """gs_bin_count + gs_bin_sort through the C ABI on the GPU; numpy in/out."""
+def run_binning(bounds, depths, counts, tiles_w, tiles_h, tile_size=4):
+    """gs_bin_count + gs_bin_sort through the C ABI on the GPU; numpy in/out.
+    Bounds are in tiles; the image is tiles_w x tiles_h tiles of tile_size."""
     import ctypes
 
     import numpy as np
@@ -159,9 +149,9 @@ def run_binning(bounds, depths, counts, width, height, tile_size=1):
     d_pm = torch.from_numpy(pm).cuda()
     d_counts = torch.from_numpy(np.ascontiguousarray(counts, np.int32)).cuda()
     d_bounds = torch.from_numpy(np.ascontiguousarray(bounds, np.int32).reshape(n, 4)).cuda()
-    params = native.make_params(1.0, 1.0, 0.0, 0.0, width, height, tile_size, 0.999, 0.2, 100.0,
-                                "gaussian", 0.95)
-    num_tiles = (width // tile_size) * (height // tile_size)
+    params = native.make_params(1.0, 1.0, 0.0, 0.0, tiles_w * tile_size, tiles_h * tile_size,
+                                tile_size, 0.999, 0.2, 100.0, "gaussian", 0.95)
+    num_tiles = tiles_w * tiles_h
     stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
     ptr = lambda t: ctypes.c_void_p(t.data_ptr() if t.numel() else 0)  # noqa: E731
     cbytes = lib.gs_bin_count_workspace_size(n)

@@ -12,14 +12,14 @@ from conftest import GOLDEN, run_binning
 pytestmark = pytest.mark.gpu
 
 
-def _oracle_bin(oracle, bounds, depths, counts, width, height, tile_size=1):
-    s = oracle.Settings(fx=1, fy=1, cx=0, cy=0, width=width, height=height, tile_size=tile_size)
+def _oracle_bin(oracle, bounds, depths, counts, tiles_w, tiles_h):
+    s = oracle.Settings(fx=1, fy=1, cx=0, cy=0, width=tiles_w, height=tiles_h, tile_size=1)
     return oracle.bin(bounds, depths, counts, s)
 
 
-def _check(oracle, bounds, depths, counts, width, height, tile_size=1):
-    total, ids, ranges = run_binning(bounds, depths, counts, width, height, tile_size)
-    ref = _oracle_bin(oracle, bounds, depths, counts, width, height, tile_size)
+def _check(oracle, bounds, depths, counts, tiles_w, tiles_h, tile_size=4):
+    total, ids, ranges = run_binning(bounds, depths, counts, tiles_w, tiles_h, tile_size)
+    ref = _oracle_bin(oracle, bounds, depths, counts, tiles_w, tiles_h)
     assert total == len(ref["gaussian_ids"]) == int(np.asarray(counts, np.int64).sum())
     np.testing.assert_array_equal(ids, ref["gaussian_ids"])
     np.testing.assert_array_equal(ranges, ref["ranges"])
@@ -79,7 +79,8 @@ def test_single_tile_and_tile_sizes(oracle):
     b, d, c = _random_case(rng, 1000, 1, 1)
     _check(oracle, b, d, c, 1, 1)
     b, d, c = _random_case(rng, 1000, 4, 8, max_extent=2)
-    _check(oracle, b, d, c, 64, 128, tile_size=16)
+    _check(oracle, b, d, c, 4, 8, tile_size=16)
+    _check(oracle, b, d, c, 4, 8, tile_size=32)
 
 
 def test_nothing_visible(oracle):
