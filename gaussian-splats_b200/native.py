@@ -34,6 +34,7 @@ EXPORTED_SYMBOLS = (
     "gs_bin_sort",
     "gs_bin_sort_workspace_size",
     "gs_bin_check",
+    "gs_bin_noalloc",
     "gs_composite_fwd",
     "gs_composite_bwd",
     "gs_project_bwd",
@@ -107,6 +108,7 @@ def lib() -> ctypes.CDLL:
         "gs_bin_sort": ([i64, i64, vp, vp, P, vp, u64, vp, u64, vp, vp, vp], i32),
         "gs_bin_sort_workspace_size": ([i64, i64], u64),
         "gs_bin_check": ([vp, vp, vp], i32),
+        "gs_bin_noalloc": ([i64, vp, vp, vp, P, vp, i64, vp, ctypes.POINTER(i64), vp], i32),
         "gs_composite_fwd": ([vp] * 6 + [P] + [vp] * 3 + [vp], i32),
         "gs_composite_bwd": ([i64] + [vp] * 9 + [P, vp, vp], i32),
         "gs_project_bwd": ([i64, i32] + [vp] * 10 + [P] + [vp] * 5 + [vp], i32),

@@ -105,6 +105,32 @@ int32_t gs_bin_sort(int64_t n, int64_t total, const int32_t *bounds, const int32
                     gs_stream_t stream);
 uint64_t gs_bin_sort_workspace_size(int64_t total, int64_t num_tiles);
 
+/* Binning without any device allocation, for callers that cannot allocate
+ * (no counterpart in the reference). Some callers have no workspace to hand
+ * over: a plugin or FFI binding inside a host program that owns every device
+ * allocation, or a per-frame loop that cannot afford cudaMalloc's implicit
+ * device-wide synchronisation. This entry point does what gs_bin_count
+ * followed by gs_bin_sort do, with its scratch in a 64 MiB array inside the
+ * library (held on every GPU that loads the library until the process exits);
+ * it never calls cudaMalloc or cudaFree.
+ *  - Limit: the count-phase scratch for n Gaussians plus the sort-phase
+ *    scratch for the intersection total must fit in 64 MiB (about 21 bytes
+ *    per Gaussian plus 16.3 bytes per intersection; e.g. 1M Gaussians with
+ *    up to 2.6M intersections). Larger inputs return GS_ERR_CAPACITY, as does
+ *    a total above ids_capacity; *total_host still reports the total.
+ *  - The first call on a device looks up the array's device address
+ *    (cudaGetSymbolAddress), so make that first call before any stream
+ *    capture.
+ *  - All calls on a device share the array and it keeps the previous call's
+ *    contents (every call clears what it needs); calls whose GPU work
+ *    overlaps -- other streams, other host threads -- race on it, so
+ *    serialise them.
+ *  - Synchronises `stream` once, to read the intersection total. */
+int32_t gs_bin_noalloc(int64_t n, const float *projected_mean, const int32_t *counts,
+                       const int32_t *bounds, const gs_params *params, int32_t *gaussian_ids,
+                       int64_t ids_capacity, int64_t *ranges, int64_t *total_host,
+                       gs_stream_t stream);
+
 /* Front-to-back compositing: replaces _composite_kernel (composite.py:25-162).
  * image [H,W,3], final_transmittance [H,W], n_contributors [H,W] int32. */
 int32_t gs_composite_fwd(const float *projected_mean, const float *inverse_covariance,
