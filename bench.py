@@ -226,6 +226,8 @@ def main():
     from gaussian_splats_b200 import scenes
     from gaussian_splats_b200.rasterize import StageTimer, rasterize_outputs
     from gaussian_splats_b200.splats import GaussianSplat
+    from gaussian_splats_b200.view_parallel import GradientArena
+    from gaussian_splats_b200.view_parallel import train_step as vp_train_step
 
     scene = scenes.config2(num_points=args.points)
     camera, target_cpu = make_view(scene, rank)
@@ -235,9 +237,11 @@ def main():
     splats = GaussianSplat.from_tensors(*params)
     for p in splats.parameters():
         p.requires_grad_(p is not splats.normals)
-    camera = camera.to(device)
+    # The camera stays on the host: its 3x3 matrix is built there once per
+    # render and uploaded (48 bytes), instead of ~15 tiny device kernels.
     target = target_cpu.to(device)
     trainable = [splats.mean, splats.rotation, splats.scale, splats.opacity, splats.color]
+    arena = GradientArena(trainable)
     settings = scene.settings
 
     def render(s):
@@ -245,15 +249,11 @@ def main():
                                  settings.near, settings.far)
 
     def train_step():
-        for p in trainable:
-            p.grad = None
-        out = render(splats)
-        loss = (out[0][:crop_h, :crop_w] - target).abs().mean()
-        loss.backward()
-        if world > 1:
-            flat = torch.cat([p.grad.reshape(-1) for p in trainable])
-            torch.distributed.all_reduce(flat)
-        return loss, out
+        # One view per rank; gradients accumulate into the flat arena, which
+        # is summed over ranks with one all-reduce (view_parallel.train_step).
+        return vp_train_step(splats, [camera], [target], arena,
+                             lambda s, c: render(s)[0],
+                             lambda image, t: (image[:crop_h, :crop_w] - t).abs().mean())
 
     def timed(fn, steps):
         if world > 1:
@@ -306,6 +306,9 @@ def main():
     e2e_splats = GaussianSplat.from_tensors(*e2e_params)
     e2e_trainable = [e2e_splats.mean, e2e_splats.rotation, e2e_splats.scale,
                      e2e_splats.opacity, e2e_splats.color]
+    for p in e2e_trainable:
+        p.requires_grad_(True)
+    e2e_arena = GradientArena(e2e_trainable)
     h2d = sum(t.numel() * t.element_size() for t in host) + target_cpu.numel() * 4
 
     def e2e_step():
@@ -313,15 +316,9 @@ def main():
             for dst, src in zip(e2e_params, pinned):
                 dst.copy_(src, non_blocking=True)
             e2e_target.copy_(target_pinned, non_blocking=True)
-        for p in e2e_trainable:
-            p.grad = None
-            p.requires_grad_(True)
-        out = render(e2e_splats)
-        loss = (out[0][:crop_h, :crop_w] - e2e_target).abs().mean()
-        loss.backward()
-        if world > 1:
-            flat = torch.cat([p.grad.reshape(-1) for p in e2e_trainable])
-            torch.distributed.all_reduce(flat)
+        loss = vp_train_step(e2e_splats, [camera], [e2e_target], e2e_arena,
+                             lambda s, c: render(s)[0],
+                             lambda image, t: (image[:crop_h, :crop_w] - t).abs().mean())
         return loss.item()
 
     for _ in range(max(1, args.warmup // 2)):

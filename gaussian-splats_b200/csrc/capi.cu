@@ -181,7 +181,7 @@ int32_t gs_project_bwd(int64_t n, int32_t num_sh, const float* mean, const float
   if (!gs::valid_sh(num_sh)) return num_sh > 25 ? GS_ERR_UNSUPPORTED : GS_ERR_INVALID_ARGUMENT;
   if (!gs::aligned(rotation, 16) || !gs::aligned(inverse_covariance, 16) ||
       !gs::aligned(grad_rotation, 16) ||
-      ((num_sh == 4 || num_sh == 16) && !gs::aligned(color, 16)))
+      ((num_sh == 4 || num_sh == 16) && (!gs::aligned(color, 16) || !gs::aligned(grad_color, 16))))
     return GS_ERR_MISALIGNED;
   return gs::launch_project_bwd(n, num_sh, mean, rotation, scale, opacity, color,
                                 camera_rotation, camera_translation, inverse_covariance,

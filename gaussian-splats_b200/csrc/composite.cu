@@ -1,20 +1,29 @@
 // Per-tile alpha compositing, forward and backward.
 //
-// One CTA per tile, one thread per pixel (TS x TS threads). The tile's list
-// of Gaussians -- ids[start:end), front to back -- is staged into shared
-// memory in batches of TS*TS entries (one entry per thread: a gather of the
-// projected mean, conic, opacity and colour), and every pixel then walks the
-// batch from shared memory. The work is FP32 arithmetic per (pixel, Gaussian)
-// pair; nothing here is a dense contraction, so tensor cores have no role.
+// One CTA per tile, one thread per pixel (TS x TS threads). Each warp owns a
+// compact 8 x 4 block of the tile's pixels (4 x 4 for 4 x 4 tiles). The
+// tile's list of Gaussians -- ids[start:end), front to back -- is staged into
+// shared memory up to 256 entries at a time (one entry per thread: a gather of
+// the projected mean, conic, opacity and colour, plus two derived values), and
+// every pixel walks the batch from shared memory. The work is FP32 arithmetic
+// per (pixel, Gaussian) pair; nothing here is a dense contraction, so tensor
+// cores have no role.
 //
 // Forward (composite.py:25-107). Per pair:
 //   d2 = fmaf(xx dx, dx, fmaf(2xy dx, dy, (yy dy) dy)),  p = exp(-d2/2),
 //   alpha = min(o p, 0.99), alpha < 1/255 -> 0, C += T alpha c, T *= 1 - alpha
-// while the pixel is active ((1 - T) < threshold). Pairs with
-// d2 > skip_cutoff(o) have alpha = 0 and change nothing, so they are skipped
-// before the exp. A pixel's contributor count is the number of list entries
-// it saw while active, i.e. (index of the entry that ended it) + 1, or the
-// list length if it never ended; the tile stops once every pixel has ended
+// while the pixel is active ((1 - T) < threshold). Two exact shortcuts skip
+// pairs with alpha = 0, which change nothing:
+//  * per pixel, d2 > skip_cutoff(o) (given det_exp's < 1 ulp error);
+//  * per warp, the staged entry carries the bounding box of the ellipse
+//    d2 <= 1.0201 skip_cutoff; a warp whose 8 x 4 pixel block lies outside it
+//    skips the entry with one uniform test. For conics with condition number
+//    below ~1e3 the float32 d2 of any such pixel is provably above the cutoff
+//    (its relative rounding error is < 2 kappa * 4 ulp < 1e-3); other conics
+//    get an infinite box.
+// A pixel's contributor count is the number of list entries it saw while
+// active, i.e. (index of the entry that ended it) + 1, or the list length if
+// it never ended; the tile stops once every pixel has ended
 // (composite.py:187-188).
 //
 // Backward (composite_bwd.py:47-277). Walks the list back to front from
@@ -22,9 +31,10 @@
 // product and composited colour of the entries behind) replaces the
 // reference's chunked associative scan; T at an entry is recovered as
 // final_T / max(suffix_T (1 - alpha), 1e-4) and the termination test is
-// re-evaluated on it, as the reference does. Each warp sums its 32 pixels'
-// 9-vector per entry with shuffles (skipped when no lane contributes) and
-// adds it to grad_projected[g] with one atomic per component.
+// re-evaluated on it, as the reference does. Each warp reduces its pixels'
+// 9-vector per entry with a butterfly reduce-scatter (14 shuffles; skipped
+// when no lane contributes) that leaves one component in each of 9 lanes,
+// which add them to grad_projected[g] with one atomic instruction.
 #include "common.cuh"
 
 namespace gs {
@@ -36,13 +46,40 @@ struct TileShape {
   static constexpr int kBatch = kPixels < 256 ? kPixels : 256;  // list entries staged at once
   static constexpr int kWarpLanes = kPixels < 32 ? kPixels : 32;
   static constexpr unsigned kWarpMask = kPixels < 32 ? ((1u << kPixels) - 1u) : 0xffffffffu;
+  static constexpr int kBlockW = TS < 8 ? TS : 8;               // warp block width
+  static constexpr int kBlockH = kWarpLanes / kBlockW;          // warp block height
+  static constexpr int kBlocksPerRow = TS / kBlockW;
 };
 
-// Gathers entry k of the sorted list into the shared-memory batch slot.
+// Pixel of this thread and the pixel rectangle of its warp.
+template <int TS>
+struct PixelMap {
+  int px, py;
+  float rx0, rx1, ry0, ry1;
+  __device__ __forceinline__ PixelMap(int tile, int tiles_w, int tid) {
+    using S = TileShape<TS>;
+    const int warp = tid / S::kWarpLanes, lane = tid % S::kWarpLanes;
+    const int bx = (tile % tiles_w) * TS + (warp % S::kBlocksPerRow) * S::kBlockW;
+    const int by = (tile / tiles_w) * TS + (warp / S::kBlocksPerRow) * S::kBlockH;
+    px = bx + lane % S::kBlockW;
+    py = by + lane / S::kBlockW;
+    rx0 = static_cast<float>(bx);
+    rx1 = static_cast<float>(bx + S::kBlockW - 1);
+    ry0 = static_cast<float>(by);
+    ry1 = static_cast<float>(by + S::kBlockH - 1);
+  }
+  // True if the box (xmin, xmax, ymin, ymax) misses this warp's pixels.
+  __device__ __forceinline__ bool misses(const float4& box) const {
+    return box.x > rx1 || box.y < rx0 || box.z > ry1 || box.w < ry0;
+  }
+};
+
+// One list entry as staged in shared memory.
 struct Staged {
-  float4 a;  // mean_x, mean_y, conic_xx, 2 conic_xy
-  float4 b;  // conic_yy, opacity, skip cutoff, conic_xy
-  float4 c;  // r, g, b, gaussian id (bits)
+  float4 a;    // mean_x, mean_y, conic_xx, 2 conic_xy
+  float4 b;    // conic_yy, opacity, skip cutoff, conic_xy
+  float4 c;    // r, g, b, gaussian id (bits)
+  float4 box;  // xmin, xmax, ymin, ymax of the ellipse where alpha can reach 1/255
 };
 
 __device__ __forceinline__ Staged stage_entry(int32_t g, const float* __restrict__ projected_mean,
@@ -50,40 +87,78 @@ __device__ __forceinline__ Staged stage_entry(int32_t g, const float* __restrict
                                               const float* __restrict__ projected_color,
                                               const float* __restrict__ projected_opacity,
                                               const gs_params& p) {
-  const float mx = __ldg(projected_mean + 3 * static_cast<int64_t>(g));
-  const float my = __ldg(projected_mean + 3 * static_cast<int64_t>(g) + 1);
+  const int64_t g3 = 3 * static_cast<int64_t>(g);
+  const float mx = __ldg(projected_mean + g3), my = __ldg(projected_mean + g3 + 1);
   const float4 conic = __ldg(reinterpret_cast<const float4*>(inverse_covariance) + g);
   const float o = __ldg(projected_opacity + g);
-  const float r = __ldg(projected_color + 3 * static_cast<int64_t>(g));
-  const float gg = __ldg(projected_color + 3 * static_cast<int64_t>(g) + 1);
-  const float b = __ldg(projected_color + 3 * static_cast<int64_t>(g) + 2);
+  const float r = __ldg(projected_color + g3), gg = __ldg(projected_color + g3 + 1),
+              b = __ldg(projected_color + g3 + 2);
+  const float cutoff = skip_cutoff(o, p);
+  const float xx = conic.x, xy = conic.y, yy = conic.w;
+  const float det = xx * yy - xy * xy;
+  const float inf = __int_as_float(0x7f800000);
+  float4 box = make_float4(-inf, inf, -inf, inf);
+  if (!(cutoff >= 0.0f)) {
+    box = make_float4(inf, -inf, inf, -inf);  // no pixel can reach alpha >= 1/255
+  } else if (xx > 0.0f && yy > 0.0f && det > 0.0f && (xx + yy) * (xx + yy) < 4.0e3f * det) {
+    const float scaled = 1.0201f * cutoff / det;
+    const float hx = sqrtf(scaled * yy) * 1.001f + 0.01f;
+    const float hy = sqrtf(scaled * xx) * 1.001f + 0.01f;
+    box = make_float4(mx - hx, mx + hx, my - hy, my + hy);
+  }
   Staged s;
-  s.a = make_float4(mx, my, conic.x, 2.0f * conic.y);
-  s.b = make_float4(conic.w, o, skip_cutoff(o, p), conic.y);
+  s.a = make_float4(mx, my, xx, 2.0f * xy);
+  s.b = make_float4(yy, o, cutoff, xy);
   s.c = make_float4(r, gg, b, __int_as_float(g));
+  s.box = box;
   return s;
 }
 
+// Appends, in order, the batch entries whose box meets this warp's pixel
+// block (and, when `limit` >= 0, whose list position is below `limit`) to the
+// warp's list in shared memory; returns how many. One ballot per 32 entries
+// replaces a per-entry test inside the pixel loop.
 template <int TS>
+__device__ __forceinline__ int warp_select(const PixelMap<TS>& pm, const float4* s_box, int count,
+                                           int lane, uint16_t* list, int64_t position0,
+                                           int64_t limit) {
+  using S = TileShape<TS>;
+  int selected = 0;
+  for (int base = 0; base < count; base += S::kWarpLanes) {
+    const int j = base + lane;
+    bool hit = j < count && !pm.misses(s_box[j]);
+    if (limit >= 0) hit = hit && position0 + j < limit;
+    const unsigned mask = __ballot_sync(S::kWarpMask, hit);
+    if (hit) list[selected + __popc(mask & ((1u << lane) - 1u))] = static_cast<uint16_t>(j);
+    selected += __popc(mask);
+  }
+  __syncwarp(S::kWarpMask);
+  return selected;
+}
+
+template <int TS, bool kGaussian>
 __global__ void __launch_bounds__(TS * TS) composite_fwd_kernel(
     const float* __restrict__ projected_mean, const float* __restrict__ inverse_covariance,
     const float* __restrict__ projected_color, const float* __restrict__ projected_opacity,
     const int32_t* __restrict__ gaussian_ids, const int64_t* __restrict__ ranges,
     const gs_params p, float* __restrict__ image, float* __restrict__ final_transmittance,
     int32_t* __restrict__ n_contributors) {
-  constexpr int NB = TileShape<TS>::kBatch;
+  using S = TileShape<TS>;
+  constexpr int NB = S::kBatch;
+  constexpr int kWarps = S::kPixels / S::kWarpLanes;
   __shared__ float4 s_a[NB];
   __shared__ float4 s_b[NB];
   __shared__ float4 s_c[NB];
+  __shared__ float4 s_box[NB];
+  __shared__ uint16_t s_list[kWarps][NB];
   const int tile = blockIdx.x;
-  const int tiles_w = p.width / TS;
   const int tid = threadIdx.x;
-  const int px = (tile % tiles_w) * TS + tid % TS;
-  const int py = (tile / tiles_w) * TS + tid / TS;
-  const float fpx = static_cast<float>(px), fpy = static_cast<float>(py);
+  const int lane = tid % S::kWarpLanes, warp = tid / S::kWarpLanes;
+  const PixelMap<TS> pm(tile, p.width / TS, tid);
+  const float fpx = static_cast<float>(pm.px), fpy = static_cast<float>(pm.py);
   const int64_t start = ranges[2 * tile], end = ranges[2 * tile + 1];
   const float threshold = p.opacity_threshold;
-  const bool gaussian = p.gaussian_mode != 0;
+  uint16_t* list = s_list[warp];
 
   float T = 1.0f, cr = 0.0f, cg = 0.0f, cb = 0.0f;
   bool done = !((1.0f - T) < threshold);
@@ -96,46 +171,81 @@ __global__ void __launch_bounds__(TS * TS) composite_fwd_kernel(
       s_a[tid] = s.a;
       s_b[tid] = s.b;
       s_c[tid] = s.c;
+      s_box[tid] = s.box;
     }
     __syncthreads();
-    if (!done) {
+    if (__any_sync(S::kWarpMask, !done)) {
       const int count = static_cast<int>(end - batch < NB ? end - batch : NB);
-      for (int j = 0; j < count; ++j) {
-        const float4 a = s_a[j];
-        const float4 b = s_b[j];
-        const float dx = fpx - a.x, dy = fpy - a.y;
-        const float d2 = pair_d2(dx, dy, a.z, a.w, b.x);
-        if (!(d2 <= b.z)) continue;
-        float alpha;
-        if (gaussian) {
-          const float prob = d2 >= 0.0f ? det_exp_nonpositive(-0.5f * d2) : det_exp(-0.5f * d2);
-          alpha = fminf(b.y * prob, kAlphaMax);
-        } else {
-          alpha = fminf(b.y, kAlphaMax);
-        }
-        if (!(alpha >= kAlphaMin)) continue;
-        const float4 c = s_c[j];
-        const float weight = T * alpha;
-        cr = fmaf(weight, c.x, cr);
-        cg = fmaf(weight, c.y, cg);
-        cb = fmaf(weight, c.z, cb);
-        T = T * (1.0f - alpha);
-        if (!((1.0f - T) < threshold)) {
-          done = true;
-          contrib = batch + j + 1 - start;
-          break;
+      const int selected = warp_select<TS>(pm, s_box, count, lane, list, 0, -1);
+      if (!done) {
+        for (int i = 0; i < selected; ++i) {
+          const int j = list[i];
+          const float4 a = s_a[j];
+          const float4 b = s_b[j];
+          const float dx = fpx - a.x, dy = fpy - a.y;
+          const float d2 = pair_d2(dx, dy, a.z, a.w, b.x);
+          if (!(d2 <= b.z)) continue;
+          float alpha;
+          if constexpr (kGaussian) {
+            const float prob = d2 >= 0.0f ? det_exp_nonpositive(-0.5f * d2) : det_exp(-0.5f * d2);
+            alpha = fminf(b.y * prob, kAlphaMax);
+          } else {
+            alpha = fminf(b.y, kAlphaMax);
+          }
+          if (!(alpha >= kAlphaMin)) continue;
+          const float4 c = s_c[j];
+          const float weight = T * alpha;
+          cr = fmaf(weight, c.x, cr);
+          cg = fmaf(weight, c.y, cg);
+          cb = fmaf(weight, c.z, cb);
+          T = T * (1.0f - alpha);
+          if (!((1.0f - T) < threshold)) {
+            done = true;
+            contrib = batch + j + 1 - start;
+            break;
+          }
         }
       }
     }
     if (__syncthreads_count(!done) == 0) break;
   }
   if (!done) contrib = end - start;
-  const int64_t pix = static_cast<int64_t>(py) * p.width + px;
+  const int64_t pix = static_cast<int64_t>(pm.py) * p.width + pm.px;
   image[3 * pix] = cr;
   image[3 * pix + 1] = cg;
   image[3 * pix + 2] = cb;
   final_transmittance[pix] = T;
   n_contributors[pix] = static_cast<int32_t>(contrib);
+}
+
+// Sums v[0..8] over the 32 lanes of a warp. Values 0..7 go through a
+// butterfly reduce-scatter (each exchange halves the values a lane keeps);
+// afterwards lane 4k holds the total of value k. Value 8 is reduced plainly
+// and lands in every lane. 14 shuffles instead of 45.
+__device__ __forceinline__ void warp_reduce_scatter9(const float (&v)[9], int lane,
+                                                     float& mine, float& last) {
+  const bool h16 = lane & 16, h8 = lane & 8, h4 = lane & 4;
+  float k4[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float send = h16 ? v[i] : v[4 + i];
+    k4[i] = (h16 ? v[4 + i] : v[i]) + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+  float k2[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const float send = h8 ? k4[i] : k4[2 + i];
+    k2[i] = (h8 ? k4[2 + i] : k4[i]) + __shfl_xor_sync(0xffffffffu, send, 8);
+  }
+  {
+    const float send = h4 ? k2[0] : k2[1];
+    mine = (h4 ? k2[1] : k2[0]) + __shfl_xor_sync(0xffffffffu, send, 4);
+  }
+  mine += __shfl_xor_sync(0xffffffffu, mine, 2);
+  mine += __shfl_xor_sync(0xffffffffu, mine, 1);
+  last = v[8];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) last += __shfl_xor_sync(0xffffffffu, last, o);
 }
 
 template <int TS>
@@ -152,15 +262,15 @@ __global__ void __launch_bounds__(TS * TS) composite_bwd_kernel(
   __shared__ float4 s_a[NB];
   __shared__ float4 s_b[NB];
   __shared__ float4 s_c[NB];
+  __shared__ float4 s_box[NB];
+  __shared__ uint16_t s_list[Shape::kPixels / Shape::kWarpLanes][NB];
   __shared__ int s_max_contrib;
   const int tile = blockIdx.x;
-  const int tiles_w = p.width / TS;
   const int tid = threadIdx.x;
-  const int lane = tid & 31;
-  const int px = (tile % tiles_w) * TS + tid % TS;
-  const int py = (tile / tiles_w) * TS + tid / TS;
-  const float fpx = static_cast<float>(px), fpy = static_cast<float>(py);
-  const int64_t pix = static_cast<int64_t>(py) * p.width + px;
+  const int lane = tid % Shape::kWarpLanes, warp = tid / Shape::kWarpLanes;
+  const PixelMap<TS> pm(tile, p.width / TS, tid);
+  const float fpx = static_cast<float>(pm.px), fpy = static_cast<float>(pm.py);
+  const int64_t pix = static_cast<int64_t>(pm.py) * p.width + pm.px;
   const float threshold = p.opacity_threshold;
   const float gr = __ldg(grad_image + 3 * pix), gg = __ldg(grad_image + 3 * pix + 1),
               gb = __ldg(grad_image + 3 * pix + 2);
@@ -175,6 +285,8 @@ __global__ void __launch_bounds__(TS * TS) composite_bwd_kernel(
   int64_t end = ranges[2 * tile + 1];
   if (end > start + s_max_contrib) end = start + s_max_contrib;  // composite_bwd.py:81-83
 
+  const int warp_max_contrib = __reduce_max_sync(kMask, contrib);
+  uint16_t* list = s_list[warp];
   float st = 1.0f, sr = 0.0f, sg = 0.0f, sb = 0.0f;  // suffix behind the current entry
   for (int64_t batch_end = end; batch_end > start; batch_end -= NB) {
     const int64_t batch_start = batch_end - NB > start ? batch_end - NB : start;
@@ -185,9 +297,14 @@ __global__ void __launch_bounds__(TS * TS) composite_bwd_kernel(
       s_a[tid] = s.a;
       s_b[tid] = s.b;
       s_c[tid] = s.c;
+      s_box[tid] = s.box;
     }
     __syncthreads();
-    for (int j = static_cast<int>(batch_end - batch_start) - 1; j >= 0; --j) {
+    const int count = static_cast<int>(batch_end - batch_start);
+    const int selected = warp_select<TS>(pm, s_box, count, lane, list, batch_start - start,
+                                         warp_max_contrib);
+    for (int i = selected - 1; i >= 0; --i) {
+      const int j = list[i];
       const int64_t position = batch_start + j - start;
       float v[9];
 #pragma unroll
@@ -235,16 +352,24 @@ __global__ void __launch_bounds__(TS * TS) composite_bwd_kernel(
         }
       }
       if (__any_sync(kMask, active)) {
+        const int g = __float_as_int(s_c[j].w);
+        float* dst = grad_projected + 9 * static_cast<int64_t>(g);
+        if constexpr (Shape::kWarpLanes == 32) {
+          float mine, last;
+          warp_reduce_scatter9(v, lane, mine, last);
+          if ((lane & 3) == 0) atomicAdd(dst + (lane >> 2), mine);
+          if (lane == 1) atomicAdd(dst + 8, last);
+        } else {
 #pragma unroll
-        for (int q = 0; q < 9; ++q) {
+          for (int q = 0; q < 9; ++q) {
 #pragma unroll
-          for (int o = Shape::kWarpLanes / 2; o > 0; o >>= 1) v[q] += __shfl_xor_sync(kMask, v[q], o);
-        }
-        if (lane == 0) {
-          const int g = __float_as_int(s_c[j].w);
-          float* dst = grad_projected + 9 * static_cast<int64_t>(g);
+            for (int o = Shape::kWarpLanes / 2; o > 0; o >>= 1)
+              v[q] += __shfl_xor_sync(kMask, v[q], o);
+          }
+          if (lane == 0) {
 #pragma unroll
-          for (int q = 0; q < 9; ++q) atomicAdd(dst + q, v[q]);
+            for (int q = 0; q < 9; ++q) atomicAdd(dst + q, v[q]);
+          }
         }
       }
     }
@@ -272,9 +397,14 @@ int32_t launch_composite_fwd(const float* projected_mean, const float* inverse_c
       static_cast<int64_t>(p.width / p.tile_size) * (p.height / p.tile_size);
   if (num_tiles == 0) return GS_OK;
 #define GS_LAUNCH(TS)                                                                          \
-  composite_fwd_kernel<TS><<<static_cast<unsigned>(num_tiles), TS * TS, 0, stream>>>(         \
-      projected_mean, inverse_covariance, projected_color, projected_opacity, gaussian_ids,    \
-      ranges, p, image, final_transmittance, n_contributors)
+  if (p.gaussian_mode)                                                                         \
+    composite_fwd_kernel<TS, true><<<static_cast<unsigned>(num_tiles), TS * TS, 0, stream>>>(  \
+        projected_mean, inverse_covariance, projected_color, projected_opacity, gaussian_ids,  \
+        ranges, p, image, final_transmittance, n_contributors);                                \
+  else                                                                                         \
+    composite_fwd_kernel<TS, false><<<static_cast<unsigned>(num_tiles), TS * TS, 0, stream>>>( \
+        projected_mean, inverse_covariance, projected_color, projected_opacity, gaussian_ids,  \
+        ranges, p, image, final_transmittance, n_contributors)
   GS_TILE_DISPATCH(p.tile_size, GS_LAUNCH)
 #undef GS_LAUNCH
   return check_launch();

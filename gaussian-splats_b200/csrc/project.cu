@@ -382,11 +382,21 @@ __global__ void __launch_bounds__(128) project_bwd_kernel(
     gdy += gc * sdy;
     gdz += gc * sdz;
   }
+  float gout[K * 3];
 #pragma unroll
   for (int k = 0; k < K; ++k) {
 #pragma unroll
     for (int ch = 0; ch < 3; ++ch)
-      gcol[3 * k + ch] = k < KB ? (visible ? gc3[ch] * basis[k < 16 ? k : 0] : 0.0f) : 0.0f;
+      gout[3 * k + ch] = k < KB ? (visible ? gc3[ch] * basis[k < 16 ? k : 0] : 0.0f) : 0.0f;
+  }
+  if constexpr ((K * 12) % 16 == 0) {
+    float4* v = reinterpret_cast<float4*>(gcol);
+#pragma unroll
+    for (int j = 0; j < K * 3 / 4; ++j)
+      v[j] = make_float4(gout[4 * j], gout[4 * j + 1], gout[4 * j + 2], gout[4 * j + 3]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < K * 3; ++j) gcol[j] = gout[j];
   }
   const float dot_d = x * gdx + y * gdy + z * gdz;
   gdx = (gdx - x * dot_d) / norm;

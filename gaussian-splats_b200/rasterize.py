@@ -95,11 +95,13 @@ class StageTimer:
         self.marks.append((name, event))
 
     def durations(self) -> dict[str, float]:
+        """Mean milliseconds between each ``begin:X`` mark and the ``X`` mark
+        that follows it."""
         torch.cuda.synchronize()
         out: dict[str, float] = {}
         counts: dict[str, int] = {}
-        for (_, before), (name, after) in zip(self.marks, self.marks[1:]):
-            if name.startswith("begin"):
+        for (first, before), (name, after) in zip(self.marks, self.marks[1:]):
+            if first != "begin:" + name:
                 continue
             out[name] = out.get(name, 0.0) + before.elapsed_time(after)
             counts[name] = counts.get(name, 0) + 1
@@ -156,13 +158,13 @@ def _rasterize(
     num_tiles = (image_width // tile_size) * (image_height // tile_size)
     with torch.cuda.device(device):
         stream = _stream(device)
-        _mark("begin_forward")
         projected_mean = mean.new_empty((n, 3))
         inverse_covariance = mean.new_empty((n, 2, 2))
         projected_color = mean.new_empty((n, 3))
         projected_opacity = mean.new_empty((n, 1))
         bounds = torch.empty((n, 4), dtype=torch.int32, device=device)
         counts = torch.empty((n,), dtype=torch.int32, device=device)
+        _mark("begin:project_fwd")
         native.check(lib.gs_project_fwd(
             n, num_sh, _ptr(mean), _ptr(rotation), _ptr(scale), _ptr(opacity), _ptr(color),
             _ptr(camera_rotation), _ptr(camera_translation), pref, _ptr(projected_mean),
@@ -173,6 +175,7 @@ def _rasterize(
         count_bytes = lib.gs_bin_count_workspace_size(n)
         count_ws = torch.empty((count_bytes,), dtype=torch.uint8, device=device)
         total = ctypes.c_int64(0)
+        _mark("begin:bin_count")
         native.check(lib.gs_bin_count(
             n, _ptr(projected_mean), _ptr(counts), _ptr(count_ws), count_bytes,
             ctypes.byref(total), stream), "gs_bin_count")
@@ -183,6 +186,7 @@ def _rasterize(
         ranges = torch.empty((num_tiles, 2), dtype=torch.int64, device=device)
         sort_bytes = lib.gs_bin_sort_workspace_size(total, num_tiles)
         sort_ws = torch.empty((sort_bytes,), dtype=torch.uint8, device=device)
+        _mark("begin:bin_sort")
         native.check(lib.gs_bin_sort(
             n, total, _ptr(bounds), _ptr(counts), pref, _ptr(count_ws), count_bytes,
             _ptr(sort_ws), sort_bytes, _ptr(gaussian_ids), _ptr(ranges), stream), "gs_bin_sort")
@@ -194,6 +198,7 @@ def _rasterize(
         final_transmittance = mean.new_empty((image_height, image_width))
         n_contributors = torch.empty((image_height, image_width), dtype=torch.int32,
                                      device=device)
+        _mark("begin:composite_fwd")
         native.check(lib.gs_composite_fwd(
             _ptr(projected_mean), _ptr(inverse_covariance), _ptr(projected_color),
             _ptr(projected_opacity), _ptr(gaussian_ids), _ptr(ranges), pref, _ptr(image),
@@ -255,8 +260,8 @@ def _backward(ctx, *grad_outputs):
     pref = ctypes.byref(params)
     with torch.cuda.device(device):
         stream = _stream(device)
-        _mark("begin_backward")
         grad_projected = mean.new_empty((n, 9))
+        _mark("begin:composite_bwd")
         native.check(lib.gs_composite_bwd(
             n, _ptr(projected_mean), _ptr(inverse_covariance), _ptr(projected_color),
             _ptr(projected_opacity), _ptr(gaussian_ids), _ptr(ranges), _ptr(grad_image),
@@ -268,6 +273,7 @@ def _backward(ctx, *grad_outputs):
         grad_scale = torch.empty_like(scale)
         grad_opacity = torch.empty_like(opacity)
         grad_color = torch.empty_like(color)
+        _mark("begin:project_bwd")
         native.check(lib.gs_project_bwd(
             n, num_sh, _ptr(mean), _ptr(rotation), _ptr(scale), _ptr(opacity), _ptr(color),
             _ptr(camera_rotation), _ptr(camera_translation), _ptr(inverse_covariance),

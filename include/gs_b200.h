@@ -14,7 +14,7 @@
  *    `workspace` buffers (256-byte aligned) of the sizes the matching
  *    `*_workspace_size` queries return. rotation, inverse_covariance,
  *    grad_rotation and bounds rows are read/written as 16-byte vectors and
- *    must be 16-byte aligned; so must color when K is 4 or 16.
+ *    must be 16-byte aligned; so must color and grad_color when K is 4 or 16.
  *  - Work is enqueued on `stream`; only gs_bin_count() synchronises it.
  *  - Return value: GS_OK (0) or a negative GS_ERR_* code. CUDA launch errors
  *    are reported as GS_ERR_CUDA; gs_last_cuda_error() returns the code.

@@ -1,0 +1,104 @@
+"""Host logic of the view-parallel step on CPU ranks (gloo, world size 2).
+
+The rendering itself needs a GPU; here the backward is replaced by a
+deterministic per-rank gradient so the sharding, the arena that autograd
+accumulates into, the all-reduce and the failure path run as real separate
+processes over gloo.
+"""
+
+import os
+import socket
+import time
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from gaussian_splats_b200.view_parallel import GradientArena, shard_views
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_shard_views_covers_each_view_once():
+    for views in (1, 7, 8, 64):
+        for world in (1, 2, 3, 4, 8):
+            shards = [shard_views(views, world, r) for r in range(world)]
+            flat = [v for s in shards for v in s]
+            assert sorted(flat) == list(range(views))
+            assert max(map(len, shards)) - min(map(len, shards)) <= 1
+    with pytest.raises(ValueError):
+        shard_views(8, 2, 2)
+
+
+def test_arena_receives_autograd_accumulation():
+    params = [torch.zeros(5, 3, requires_grad=True), torch.zeros(5, 4, requires_grad=True)]
+    arena = GradientArena(params)
+    arena.attach()
+    loss = (params[0] * 2.0).sum() + (params[1] * 3.0).sum()
+    loss.backward()
+    arena.check_attached()
+    assert torch.all(arena.flat[:15] == 2.0) and torch.all(arena.flat[15:] == 3.0)
+    loss = (params[0] * 1.0).sum()
+    loss.backward()  # accumulates into the same views
+    assert torch.all(arena.flat[:15] == 3.0)
+
+
+def _worker(rank, world, port, results):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    params = [torch.zeros(100, 3, requires_grad=True), torch.zeros(100, 16, 3, requires_grad=True)]
+    arena = GradientArena(params)
+    arena.attach()
+    views = shard_views(8, world, rank)
+    # Stand-in for rendering this rank's views: gradient = view index + 1 per view.
+    loss = sum((p * float(v + 1)).sum() for v in views for p in params)
+    loss.backward()
+    arena.all_reduce()
+    results[rank] = (views, float(arena.flat[0]), float(arena.flat[-1]))
+    dist.destroy_process_group()
+
+
+def test_all_reduce_sums_every_ranks_views():
+    world = 2
+    manager = mp.Manager()
+    results = manager.dict()
+    mp.spawn(_worker, args=(world, _free_port(), results), nprocs=world, join=True)
+    expected = float(sum(v + 1 for v in range(8)))  # every view counted once
+    for rank in range(world):
+        views, first, last = results[rank]
+        assert first == expected and last == expected
+    assert sorted(results[0][0] + results[1][0]) == list(range(8))
+
+
+def _failing_worker(rank, world, port, results):
+    import datetime
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=3))
+    arena = GradientArena([torch.zeros(10, requires_grad=True)])
+    arena.attach()
+    if rank == 1:
+        # This rank fails between steps: it leaves without joining the collective.
+        results[rank] = "left"
+        return
+    start = time.time()
+    try:
+        arena.all_reduce()
+        results[rank] = "no error"
+    except Exception as error:  # the survivor must see an error, not hang
+        results[rank] = f"error after {time.time() - start:.1f}s: {type(error).__name__}"
+
+
+def test_missing_rank_ends_collective_with_error():
+    world = 2
+    manager = mp.Manager()
+    results = manager.dict()
+    mp.spawn(_failing_worker, args=(world, _free_port(), results), nprocs=world, join=True)
+    assert results[1] == "left"
+    assert results[0].startswith("error after"), results[0]
