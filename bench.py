@@ -97,10 +97,16 @@ class ClockSampler:
                 stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
+            return self
+        # nvidia-smi takes a moment to start; begin timing once it samples.
+        deadline = time.time() + 5.0
+        while time.time() < deadline and os.path.getsize(self.path) == 0:
+            time.sleep(0.02)
         return self
 
     def __exit__(self, *exc):
         if self.proc is not None:
+            time.sleep(0.25)  # one more sample covering the end of the region
             self.proc.terminate()
             self.proc.wait(timeout=10)
             self.file.close()
@@ -125,6 +131,92 @@ class ClockSampler:
                     reasons.add(name)
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": float(rows[0][2]),
                 "samples": len(rows), "reasons": sorted(reasons)}
+
+
+def fp32_peak_tflops(device):
+    """FP32 CUDA-core peak measured live: cuBLAS SGEMM 8192^3 with TF32 off.
+    MEASURED_PEAKS.json carries HBM and bf16 figures only."""
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        a = torch.randn(8192, 8192, device=device)
+        b = torch.randn(8192, 8192, device=device)
+        for _ in range(2):
+            a @ b
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        best = float("inf")
+        for _ in range(5):
+            start.record()
+            a @ b
+            end.record()
+            torch.cuda.synchronize()
+            best = min(best, start.elapsed_time(end))
+        return 2 * 8192 ** 3 / (best * 1e-3) / 1e12
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+
+
+def kernel_durations(outputs, params, camera, grad_image, settings, device, repeats=5):
+    """Per-launch milliseconds of the four main kernels, each launched through
+    the C ABI right after a 1 GiB L2 flush, with CUDA events around the launch
+    on the launching stream (the GPU is still busy with the flush when the
+    launch is enqueued, so no host gap is timed). Returns {stage: mean ms}."""
+    import ctypes
+
+    from gaussian_splats_b200 import native
+
+    lib = native.lib()
+    (image, final_t, n_contrib, pmean, conic, pcolor, popacity, ids, ranges, counts) = outputs
+    mean, rotation, scale, opacity, color = params
+    n, k = mean.shape[0], color.shape[1]
+    w, h = camera.image_size
+    fx, fy = camera.focal_length
+    cx, cy = camera.principal_point
+    prm = native.make_params(fx, fy, cx, cy, w, h, settings.tile_size,
+                             settings.opacity_threshold, settings.near, settings.far,
+                             settings.rendering_mode, settings.confidence)
+    pref = ctypes.byref(prm)
+    cam_r = camera.rotation_matrix.to(device)
+    cam_t = camera.translation.to(device)
+    P = lambda t: ctypes.c_void_p(t.data_ptr() if t.numel() else 0)  # noqa: E731
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    out_pm, out_conic = torch.empty_like(pmean), torch.empty_like(conic)
+    out_rgb, out_o = torch.empty_like(pcolor), torch.empty_like(popacity)
+    bounds = torch.empty((n, 4), dtype=torch.int32, device=device)
+    out_counts = torch.empty_like(counts)
+    out_img, out_t = torch.empty_like(image), torch.empty_like(final_t)
+    out_nc = torch.empty_like(n_contrib)
+    grad_projected = torch.empty((n, 9), device=device)
+    grads = [torch.empty_like(t) for t in params]
+    launches = {
+        "project_fwd": lambda: lib.gs_project_fwd(
+            n, k, P(mean), P(rotation), P(scale), P(opacity), P(color), P(cam_r), P(cam_t), pref,
+            P(out_pm), P(out_conic), P(out_rgb), P(out_o), P(bounds), P(out_counts), stream),
+        "composite_fwd": lambda: lib.gs_composite_fwd(
+            P(pmean), P(conic), P(pcolor), P(popacity), P(ids), P(ranges), pref, P(out_img),
+            P(out_t), P(out_nc), stream),
+        "composite_bwd": lambda: lib.gs_composite_bwd(
+            n, P(pmean), P(conic), P(pcolor), P(popacity), P(ids), P(ranges), P(grad_image),
+            P(final_t), P(n_contrib), pref, P(grad_projected), stream),
+        "project_bwd": lambda: lib.gs_project_bwd(
+            n, k, P(mean), P(rotation), P(scale), P(opacity), P(color), P(cam_r), P(cam_t),
+            P(conic), P(grad_projected), P(counts), pref, *(P(g) for g in grads), stream),
+    }
+    flush = torch.empty(1 << 28, dtype=torch.float32, device=device)  # 1 GiB > 126 MB L2
+    result = {}
+    for name, launch in launches.items():
+        events = []
+        for _ in range(repeats):
+            flush.zero_()
+            before, after = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            before.record()
+            native.check(launch(), name)
+            after.record()
+            events.append((before, after))
+        torch.cuda.synchronize()
+        result[name] = sum(b.elapsed_time(a) for b, a in events) / repeats
+    return result
 
 
 def make_view(scene, rank):
@@ -226,7 +318,6 @@ def main():
     from gaussian_splats_b200 import scenes
     from gaussian_splats_b200.rasterize import StageTimer, rasterize_outputs
     from gaussian_splats_b200.splats import GaussianSplat
-    from gaussian_splats_b200.view_parallel import GradientArena
     from gaussian_splats_b200.view_parallel import train_step as vp_train_step
 
     scene = scenes.config2(num_points=args.points)
@@ -241,7 +332,6 @@ def main():
     # render and uploaded (48 bytes), instead of ~15 tiny device kernels.
     target = target_cpu.to(device)
     trainable = [splats.mean, splats.rotation, splats.scale, splats.opacity, splats.color]
-    arena = GradientArena(trainable)
     settings = scene.settings
 
     def render(s):
@@ -249,9 +339,9 @@ def main():
                                  settings.near, settings.far)
 
     def train_step():
-        # One view per rank; gradients accumulate into the flat arena, which
-        # is summed over ranks with one all-reduce (view_parallel.train_step).
-        return vp_train_step(splats, [camera], [target], arena,
+        # One view per rank; the gradients are summed over ranks with one
+        # all-reduce per parameter tensor (view_parallel.train_step).
+        return vp_train_step(splats, [camera], [target], trainable,
                              lambda s, c: render(s)[0],
                              lambda image, t: (image[:crop_h, :crop_w] - t).abs().mean())
 
@@ -295,6 +385,19 @@ def main():
         n_contrib = int(out[2].sum())
         intersections = int(out[7].numel())
         visible = int((out[9] > 0).sum())
+        # Pairs the reference's compositing kernels evaluate: every pixel of a
+        # tile for every list entry up to the tile's largest contributor count
+        # (composite.py:148-188, composite_bwd.py:81-93).
+        ts = settings.tile_size
+        nc = out[2].reshape(out[2].shape[0] // ts, ts, out[2].shape[1] // ts, ts)
+        tile_max = nc.permute(0, 2, 1, 3).reshape(-1, ts * ts).amax(dim=1).long()
+        lengths = out[8][:, 1] - out[8][:, 0]
+        pairs = int((torch.minimum(lengths, tile_max) * ts * ts).sum())
+        grad_image = torch.zeros_like(out[0])
+        diff = out[0][:crop_h, :crop_w] - target
+        grad_image[:crop_h, :crop_w] = torch.sign(diff) / diff.numel()
+    kernel_ms = kernel_durations(out, params, camera, grad_image, settings, device)
+    fp32_peak = fp32_peak_tflops(device)
 
     # End to end through the public API with host buffers: each step copies the
     # Gaussian parameters and the target from pinned host memory, renders
@@ -308,7 +411,6 @@ def main():
                      e2e_splats.opacity, e2e_splats.color]
     for p in e2e_trainable:
         p.requires_grad_(True)
-    e2e_arena = GradientArena(e2e_trainable)
     h2d = sum(t.numel() * t.element_size() for t in host) + target_cpu.numel() * 4
 
     def e2e_step():
@@ -316,7 +418,7 @@ def main():
             for dst, src in zip(e2e_params, pinned):
                 dst.copy_(src, non_blocking=True)
             e2e_target.copy_(target_pinned, non_blocking=True)
-        loss = vp_train_step(e2e_splats, [camera], [e2e_target], e2e_arena,
+        loss = vp_train_step(e2e_splats, [camera], [e2e_target], e2e_trainable,
                              lambda s, c: render(s)[0],
                              lambda image, t: (image[:crop_h, :crop_w] - t).abs().mean())
         return loss.item()
@@ -328,28 +430,35 @@ def main():
     hbm_peak, peak_kind = load_peaks()
     launches_per_step = 15  # 1 projection, 6 count-phase, 5 sort-phase, 2 composite, 1 proj bwd
     n = scene.num_points
-    rooflines = {}
-    if "project_fwd" in stage_ms:
-        gbs = n * PROJECT_FWD_BYTES / (stage_ms["project_fwd"] * 1e-3) / 1e9
-        rooflines["project_fwd"] = {"bound": "hbm", "achieved": gbs, "peak": hbm_peak,
-                                    "unit": "GB/s", "frac": gbs / hbm_peak,
-                                    "ms": stage_ms["project_fwd"]}
-    if "project_bwd" in stage_ms:
-        gbs = n * PROJECT_BWD_BYTES / (stage_ms["project_bwd"] * 1e-3) / 1e9
-        rooflines["project_bwd"] = {"bound": "hbm", "achieved": gbs, "peak": hbm_peak,
-                                    "unit": "GB/s", "frac": gbs / hbm_peak,
-                                    "ms": stage_ms["project_bwd"]}
-    traffic = None
+    traffic = {}
     profile_json = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(profile_json):
         with open(profile_json) as f:
             traffic = json.load(f)
-    dominant = max(stage_ms, key=stage_ms.get) if stage_ms else None
-    main_roof = rooflines.get("project_fwd")
-    if main_roof is not None:
-        main_roof = dict(main_roof, kernel="project_fwd",
-                         traffic=(traffic or {}).get("project_fwd"),
-                         note=f"peak: {peak_kind} hbm_gbs")
+
+    def hbm(name, bytes_per_launch):
+        gbs = bytes_per_launch / (kernel_ms[name] * 1e-3) / 1e9
+        return {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s",
+                "frac": gbs / hbm_peak, "traffic": traffic.get(name), "ms": kernel_ms[name],
+                "algorithmic_bytes": bytes_per_launch,
+                "note": f"peak: {peak_kind} hbm_gbs (MEASURED_PEAKS.json)"}
+
+    def fp32(name, flops):
+        tflops = flops / (kernel_ms[name] * 1e-3) / 1e12
+        return {"bound": "fp32", "achieved": tflops, "peak": fp32_peak, "unit": "TFLOP/s",
+                "frac": tflops / fp32_peak, "traffic": traffic.get(name), "ms": kernel_ms[name],
+                "algorithmic_flops": flops,
+                "note": "peak: FP32 cuBLAS SGEMM measured in this run (no FP32 figure in "
+                        "MEASURED_PEAKS.json); work = reference-evaluated pairs x ops/pair"}
+
+    rooflines = {
+        "project_fwd": hbm("project_fwd", n * PROJECT_FWD_BYTES),
+        "project_bwd": hbm("project_bwd", n * PROJECT_BWD_BYTES),
+        "composite_fwd": fp32("composite_fwd", pairs * COMPOSITE_FWD_FLOPS),
+        "composite_bwd": fp32("composite_bwd", pairs * COMPOSITE_BWD_FLOPS),
+    }
+    dominant = max(kernel_ms, key=kernel_ms.get)
+    main_roof = dict(rooflines[dominant], kernel=dominant)
 
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -361,9 +470,9 @@ def main():
                    "parallelism": f"view-parallel x{world}, NCCL all-reduce of gradients"
                    if world > 1 else "single GPU",
                    "l2": "inputs larger than L2 (236 MB of parameters read per step)"},
-        "stage_ms": stage_ms, "dominant_stage": dominant,
+        "stage_ms": stage_ms, "kernel_ms": kernel_ms, "dominant_kernel": dominant,
         "view": {"visible": visible, "intersections": intersections,
-                 "evaluated_pairs_fwd": n_contrib},
+                 "active_pairs": n_contrib, "reference_pairs": pairs},
         "roofline": main_roof, "rooflines": rooflines,
         "e2e": {"value": world * 1000.0 / e2e_ms, "unit": UNIT, "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4},

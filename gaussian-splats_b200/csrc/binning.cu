@@ -377,21 +377,21 @@ __global__ void __launch_bounds__(kThreads) emit_kernel(
   }
 }
 
-// ranges[t] = [lower_bound(t), lower_bound(t + 1)) over the sorted tile keys.
+// ranges[t] = [first index with key >= t, first index with key >= t + 1)
+// over the sorted tile keys. Thread i (0 <= i <= total) looks at the step
+// between key[i-1] and key[i] (key[-1] = -1, key[total] = num_tiles): every
+// tile t in (key[i-1], key[i]] starts at i and every tile t in
+// [key[i-1], key[i]) ends at i. Each start and end is written exactly once,
+// and empty tiles get start == end.
 __global__ void ranges_kernel(const uint32_t* __restrict__ sorted_keys, int64_t total,
                               int64_t num_tiles, int64_t* __restrict__ ranges) {
-  const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (t >= num_tiles) return;
-  auto lower_bound = [&](uint64_t value) {
-    int64_t lo = 0, hi = total;
-    while (lo < hi) {
-      const int64_t mid = (lo + hi) >> 1;
-      if (sorted_keys[mid] < value) lo = mid + 1; else hi = mid;
-    }
-    return lo;
-  };
-  ranges[2 * t] = lower_bound(static_cast<uint64_t>(t));
-  ranges[2 * t + 1] = lower_bound(static_cast<uint64_t>(t) + 1);
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i > total) return;
+  const int64_t prev = i > 0 ? static_cast<int64_t>(sorted_keys[i - 1]) : -1;
+  const int64_t cur = i < total ? static_cast<int64_t>(sorted_keys[i]) : num_tiles;
+  if (cur == prev) return;
+  for (int64_t t = prev + 1; t <= cur && t < num_tiles; ++t) ranges[2 * t] = i;
+  for (int64_t t = prev < 0 ? 0 : prev; t < cur; ++t) ranges[2 * t + 1] = i;
 }
 
 // ---------------------------------------------------------------- workspaces
@@ -570,7 +570,7 @@ int32_t launch_bin_sort(int64_t n, int64_t total, const int32_t* bounds, const i
     }
   }
   if (num_tiles > 0) {
-    ranges_kernel<<<ceil_div(num_tiles, 256), 256, 0, stream>>>(sorted_keys, total, num_tiles,
+    ranges_kernel<<<ceil_div(total + 1, 256), 256, 0, stream>>>(sorted_keys, total, num_tiles,
                                                                ranges);
     GS_TRY(check_launch());
   }

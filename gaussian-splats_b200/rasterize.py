@@ -233,6 +233,9 @@ def _rasterize_fake(mean, rotation, scale, opacity, color, camera_rotation, came
 def _setup_context(ctx, inputs, output) -> None:
     # Same saved set as interface.py:158-173: the 7 tensor inputs and outputs[1:].
     ctx.save_for_backward(*inputs[:7], *output[1:])
+    # Only the image's gradient is used; do not materialise zero gradients for
+    # the nine other outputs (one fill kernel each).
+    ctx.set_materialize_grads(False)
     (ctx.fx, ctx.fy, ctx.cx, ctx.cy, ctx.image_width, ctx.image_height, ctx.tile_size,
      ctx.opacity_threshold, ctx.near, ctx.far, ctx.rendering_mode, ctx.confidence) = inputs[7:]
 

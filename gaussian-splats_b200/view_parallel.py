@@ -5,9 +5,8 @@ and the parameter gradients are summed with one all-reduce per step -- the
 only exchange. The reference is single-device (training/train.py:125-151
 renders one view per step); this is the multi-GPU shape of that step.
 
-Gradients land in one flat float32 arena: before the backward each
-parameter's ``.grad`` is made a view into the arena, so autograd accumulates
-straight into it and the all-reduce runs on the arena with no packing.
+Gradients stay in the tensors autograd creates; the exchange is one
+asynchronous all-reduce per parameter tensor, awaited together.
 """
 
 from __future__ import annotations
@@ -32,40 +31,28 @@ def shard_views(num_views: int, world_size: int, rank: int) -> list[int]:
     return list(range(start, start + base + (1 if rank < extra else 0)))
 
 
-class GradientArena:
-    """One flat buffer backing the ``.grad`` of a list of parameters."""
+def all_reduce_gradients(parameters: Sequence[torch.Tensor], group=None,
+                         average: bool = False) -> None:
+    """Sum (or average) every parameter's ``.grad`` over the process group.
 
-    def __init__(self, parameters: Sequence[torch.Tensor]):
-        self.parameters = list(parameters)
-        total = sum(p.numel() for p in self.parameters)
-        device = self.parameters[0].device
-        self.flat = torch.zeros(total, dtype=torch.float32, device=device)
-        self.views = []
-        offset = 0
-        for p in self.parameters:
-            self.views.append(self.flat[offset:offset + p.numel()].view_as(p))
-            offset += p.numel()
-
-    def attach(self) -> None:
-        """Zero the arena and point every parameter's ``.grad`` into it."""
-        self.flat.zero_()
-        for p, v in zip(self.parameters, self.views):
-            p.grad = v
-
-    def check_attached(self) -> None:
-        """Raise if autograd replaced a ``.grad`` instead of accumulating."""
-        for p, v in zip(self.parameters, self.views):
-            if p.grad is None or p.grad.data_ptr() != v.data_ptr():
-                raise RuntimeError("a parameter gradient left the arena; call attach() "
-                                   "before backward and do not reassign .grad")
-
-    def all_reduce(self, group=None, average: bool = False) -> None:
-        """Sum (or average) the arena over the process group."""
-        self.check_attached()
-        if dist.is_initialized() and dist.get_world_size(group) > 1:
-            dist.all_reduce(self.flat, op=dist.ReduceOp.SUM, group=group)
-            if average:
-                self.flat.div_(dist.get_world_size(group))
+    One all-reduce per tensor, issued back to back asynchronously and then
+    awaited: the gradients stay where autograd put them (no packing copy and no
+    pre-zeroed buffer to accumulate into). Parameters without a gradient on
+    this rank take part with zeros so every rank issues the same collectives.
+    """
+    if not (dist.is_initialized() and dist.get_world_size(group) > 1):
+        return
+    works = []
+    for p in parameters:
+        if p.grad is None:
+            p.grad = torch.zeros_like(p)
+        works.append(dist.all_reduce(p.grad, op=dist.ReduceOp.SUM, group=group, async_op=True))
+    for work in works:
+        work.wait()
+    if average:
+        size = dist.get_world_size(group)
+        for p in parameters:
+            p.grad.div_(size)
 
 
 def init_from_env(backend: str = "nccl", timeout_s: float = 120.0) -> tuple[int, int, int]:
@@ -85,21 +72,26 @@ def train_step(
     splats,
     cameras: Sequence,
     targets: Sequence[torch.Tensor],
-    arena: GradientArena,
+    parameters: Sequence[torch.Tensor],
     render: Callable,
     loss_fn: Callable[[torch.Tensor, torch.Tensor], torch.Tensor],
     group=None,
 ) -> torch.Tensor:
-    """Forward + backward of this rank's views, then one all-reduce.
+    """Forward + backward of this rank's views, then the gradient all-reduce.
 
     ``render(splats, camera)`` returns an image; ``loss_fn(image, target)`` a
-    scalar. Returns this rank's summed loss (a device tensor; no host sync).
+    scalar. Gradients of ``parameters`` start from None, accumulate over this
+    rank's views and are summed over ranks. Returns this rank's summed loss (a
+    device tensor; no host sync).
     """
-    arena.attach()
+    for p in parameters:
+        p.grad = None
     total = None
     for camera, target in zip(cameras, targets):
         loss = loss_fn(render(splats, camera), target)
         loss.backward()
         total = loss.detach() if total is None else total + loss.detach()
-    arena.all_reduce(group)
-    return total if total is not None else torch.zeros((), device=arena.flat.device)
+    all_reduce_gradients(parameters, group)
+    if total is None:
+        total = torch.zeros((), device=parameters[0].device)
+    return total

@@ -1,9 +1,8 @@
 """Host logic of the view-parallel step on CPU ranks (gloo, world size 2).
 
 The rendering itself needs a GPU; here the backward is replaced by a
-deterministic per-rank gradient so the sharding, the arena that autograd
-accumulates into, the all-reduce and the failure path run as real separate
-processes over gloo.
+deterministic per-rank gradient so the sharding, the gradient all-reduce and
+the failure path run as real separate processes over gloo.
 """
 
 import os
@@ -15,7 +14,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from gaussian_splats_b200.view_parallel import GradientArena, shard_views
+from gaussian_splats_b200.view_parallel import all_reduce_gradients, shard_views, train_step
 
 
 def _free_port():
@@ -35,31 +34,24 @@ def test_shard_views_covers_each_view_once():
         shard_views(8, 2, 2)
 
 
-def test_arena_receives_autograd_accumulation():
-    params = [torch.zeros(5, 3, requires_grad=True), torch.zeros(5, 4, requires_grad=True)]
-    arena = GradientArena(params)
-    arena.attach()
-    loss = (params[0] * 2.0).sum() + (params[1] * 3.0).sum()
-    loss.backward()
-    arena.check_attached()
-    assert torch.all(arena.flat[:15] == 2.0) and torch.all(arena.flat[15:] == 3.0)
-    loss = (params[0] * 1.0).sum()
-    loss.backward()  # accumulates into the same views
-    assert torch.all(arena.flat[:15] == 3.0)
+def test_single_process_step_keeps_local_gradients():
+    params = [torch.ones(5, 3, requires_grad=True), torch.ones(5, 4, requires_grad=True)]
+    cams, targets = [1.0, 2.0], [torch.zeros(()), torch.zeros(())]
+    render = lambda s, cam: sum((p * cam).sum() for p in params)  # noqa: E731
+    loss = train_step(None, cams, targets, params, render, lambda image, t: image - t)
+    assert float(loss) == 3.0 * (15 + 20)
+    assert torch.all(params[0].grad == 3.0) and torch.all(params[1].grad == 3.0)
 
 
 def _worker(rank, world, port, results):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     params = [torch.zeros(100, 3, requires_grad=True), torch.zeros(100, 16, 3, requires_grad=True)]
-    arena = GradientArena(params)
-    arena.attach()
     views = shard_views(8, world, rank)
-    # Stand-in for rendering this rank's views: gradient = view index + 1 per view.
-    loss = sum((p * float(v + 1)).sum() for v in views for p in params)
-    loss.backward()
-    arena.all_reduce()
-    results[rank] = (views, float(arena.flat[0]), float(arena.flat[-1]))
+    # Stand-in for rendering a view: the loss is (view index + 1) * sum(params).
+    render = lambda s, v: sum((p * float(v + 1)).sum() for p in params)  # noqa: E731
+    train_step(None, views, [0.0] * len(views), params, render, lambda image, t: image - t)
+    results[rank] = (views, float(params[0].grad[0, 0]), float(params[1].grad[-1, -1, -1]))
     dist.destroy_process_group()
 
 
@@ -81,15 +73,15 @@ def _failing_worker(rank, world, port, results):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world,
                             timeout=datetime.timedelta(seconds=3))
-    arena = GradientArena([torch.zeros(10, requires_grad=True)])
-    arena.attach()
+    params = [torch.zeros(10, requires_grad=True)]
+    params[0].grad = torch.ones(10)
     if rank == 1:
         # This rank fails between steps: it leaves without joining the collective.
         results[rank] = "left"
         return
     start = time.time()
     try:
-        arena.all_reduce()
+        all_reduce_gradients(params)
         results[rank] = "no error"
     except Exception as error:  # the survivor must see an error, not hang
         results[rank] = f"error after {time.time() - start:.1f}s: {type(error).__name__}"
