@@ -1,13 +1,19 @@
 // Per-tile alpha compositing, forward and backward.
 //
-// One CTA per tile, one thread per pixel (TS x TS threads). Each warp owns a
-// compact 8 x 4 block of the tile's pixels (4 x 4 for 4 x 4 tiles). The
-// tile's list of Gaussians -- ids[start:end), front to back -- is staged into
-// shared memory up to 256 entries at a time (one entry per thread: a gather of
-// the projected mean, conic, opacity and colour, plus two derived values), and
-// every pixel walks the batch from shared memory. The work is FP32 arithmetic
-// per (pixel, Gaussian) pair; nothing here is a dense contraction, so tensor
-// cores have no role.
+// One CTA per tile. The tile's list of Gaussians -- ids[start:end), front to
+// back -- is staged into shared memory 256 entries at a time (a gather of the
+// projected mean, conic, opacity and colour, plus two derived values), and
+// every pixel walks the batch from shared memory. Each warp owns a compact
+// block of pixels: in the forward one pixel per thread and an 8 x 4 block
+// (4 x 4 tiles: one 4 x 4 block); in the backward, for 8 x 8 and larger
+// tiles, two pixels per thread (one column, four rows apart) and an 8 x 8
+// block. Two pixels per thread halve the per-pixel cost of everything done
+// once per (warp, entry) -- the culling ballot, the loop and shared-memory
+// loads and, above all, the warp reduction and atomics of the backward; the
+// forward keeps one pixel per thread because its smaller blocks cull more
+// and its pixels stop early. The work is FP32 arithmetic per (pixel,
+// Gaussian) pair; nothing here is a dense contraction, so tensor cores have
+// no role.
 //
 // Forward (composite.py:25-107). Per pair:
 //   d2 = fmaf(xx dx, dx, fmaf(2xy dx, dy, (yy dy) dy)),  p = exp(-d2/2),
@@ -16,11 +22,12 @@
 // pairs with alpha = 0, which change nothing:
 //  * per pixel, d2 > skip_cutoff(o) (given det_exp's < 1 ulp error);
 //  * per warp, the staged entry carries the bounding box of the ellipse
-//    d2 <= 1.0201 skip_cutoff; a warp whose 8 x 4 pixel block lies outside it
-//    skips the entry with one uniform test. For conics with condition number
-//    below ~1e3 the float32 d2 of any such pixel is provably above the cutoff
-//    (its relative rounding error is < 2 kappa * 4 ulp < 1e-3); other conics
-//    get an infinite box.
+//    d2 <= 1.0201 skip_cutoff; each warp ballots the staged entries against
+//    its pixel block and walks only the ones whose box meets it (in list
+//    order). For conics with condition number below ~1e3 the float32 d2 of
+//    any pixel outside the box is provably above the cutoff (its relative
+//    rounding error is < 2 kappa * 4 ulp < 1e-3); other conics get an
+//    infinite box.
 // A pixel's contributor count is the number of list entries it saw while
 // active, i.e. (index of the entry that ended it) + 1, or the list length if
 // it never ended; the tile stops once every pixel has ended
@@ -31,43 +38,55 @@
 // product and composited colour of the entries behind) replaces the
 // reference's chunked associative scan; T at an entry is recovered as
 // final_T / max(suffix_T (1 - alpha), 1e-4) and the termination test is
-// re-evaluated on it, as the reference does. Each warp reduces its pixels'
-// 9-vector per entry with a butterfly reduce-scatter (14 shuffles; skipped
-// when no lane contributes) that leaves one component in each of 9 lanes,
-// which add them to grad_projected[g] with one atomic instruction.
+// re-evaluated on it, as the reference does. Each thread sums its pixels'
+// 9-vectors per entry, each warp reduces them with a butterfly
+// reduce-scatter (14 shuffles; skipped when no lane contributes) that leaves
+// one component in each of 9 lanes, which add them to grad_projected[g] with
+// two atomic instructions.
 #include "common.cuh"
 
 namespace gs {
 namespace {
 
-template <int TS>
+template <int TS, int PPT>
 struct TileShape {
   static constexpr int kPixels = TS * TS;
-  static constexpr int kBatch = kPixels < 256 ? kPixels : 256;  // list entries staged at once
-  static constexpr int kWarpLanes = kPixels < 32 ? kPixels : 32;
-  static constexpr unsigned kWarpMask = kPixels < 32 ? ((1u << kPixels) - 1u) : 0xffffffffu;
-  static constexpr int kBlockW = TS < 8 ? TS : 8;               // warp block width
-  static constexpr int kBlockH = kWarpLanes / kBlockW;          // warp block height
+  static constexpr int kPpt = PPT;                               // pixels per thread
+  static constexpr int kThreads = kPixels / kPpt;
+  static constexpr int kWarpLanes = kThreads < 32 ? kThreads : 32;
+  static constexpr unsigned kWarpMask = kThreads < 32 ? ((1u << kThreads) - 1u) : 0xffffffffu;
+  static constexpr int kWarps = kThreads / kWarpLanes;
+  static constexpr int kBlockW = TS < 8 ? TS : 8;                // warp block width
+  static constexpr int kLaneRows = kWarpLanes / kBlockW;         // rows one pass of lanes covers
+  static constexpr int kBlockH = kLaneRows * kPpt;               // warp block height
   static constexpr int kBlocksPerRow = TS / kBlockW;
+  static constexpr int kBatch = kPixels < 256 ? kPixels : 256;  // list entries staged at once
 };
 
-// Pixel of this thread and the pixel rectangle of its warp.
-template <int TS>
+// This thread's pixels (one column, kLaneRows apart) and its warp's block.
+// Resident CTAs of `threads` threads asked of the register allocator for the
+// backward: 32 warps per SM (at most 64 registers a thread).
+constexpr int min_blocks_for_32_warps(int threads) {
+  return 1024 / threads < 16 ? 1024 / threads : 16;
+}
+
+template <int TS, int PPT>
 struct PixelMap {
-  int px, py;
+  using S = TileShape<TS, PPT>;
+  int px, py0;
   float rx0, rx1, ry0, ry1;
   __device__ __forceinline__ PixelMap(int tile, int tiles_w, int tid) {
-    using S = TileShape<TS>;
     const int warp = tid / S::kWarpLanes, lane = tid % S::kWarpLanes;
     const int bx = (tile % tiles_w) * TS + (warp % S::kBlocksPerRow) * S::kBlockW;
     const int by = (tile / tiles_w) * TS + (warp / S::kBlocksPerRow) * S::kBlockH;
     px = bx + lane % S::kBlockW;
-    py = by + lane / S::kBlockW;
+    py0 = by + lane / S::kBlockW;
     rx0 = static_cast<float>(bx);
     rx1 = static_cast<float>(bx + S::kBlockW - 1);
     ry0 = static_cast<float>(by);
     ry1 = static_cast<float>(by + S::kBlockH - 1);
   }
+  __device__ __forceinline__ int py(int q) const { return py0 + q * S::kLaneRows; }
   // True if the box (xmin, xmax, ymin, ymax) misses this warp's pixels.
   __device__ __forceinline__ bool misses(const float4& box) const {
     return box.x > rx1 || box.y < rx0 || box.z > ry1 || box.w < ry0;
@@ -114,15 +133,39 @@ __device__ __forceinline__ Staged stage_entry(int32_t g, const float* __restrict
   return s;
 }
 
+// Stages list entries [first, last) into the batch slots 0..last-first-1.
+template <int TS, int PPT>
+__device__ __forceinline__ void stage_batch(int64_t first, int64_t last,
+                                            const int32_t* __restrict__ gaussian_ids,
+                                            const float* __restrict__ projected_mean,
+                                            const float* __restrict__ inverse_covariance,
+                                            const float* __restrict__ projected_color,
+                                            const float* __restrict__ projected_opacity,
+                                            const gs_params& p, float4* s_a, float4* s_b,
+                                            float4* s_c, float4* s_box) {
+  using S = TileShape<TS, PPT>;
+  for (int slot = threadIdx.x; slot < S::kBatch; slot += S::kThreads) {
+    const int64_t k = first + slot;
+    if (k < last) {
+      const Staged st = stage_entry(__ldg(gaussian_ids + k), projected_mean, inverse_covariance,
+                                    projected_color, projected_opacity, p);
+      s_a[slot] = st.a;
+      s_b[slot] = st.b;
+      s_c[slot] = st.c;
+      s_box[slot] = st.box;
+    }
+  }
+}
+
 // Appends, in order, the batch entries whose box meets this warp's pixel
 // block (and, when `limit` >= 0, whose list position is below `limit`) to the
 // warp's list in shared memory; returns how many. One ballot per 32 entries
 // replaces a per-entry test inside the pixel loop.
-template <int TS>
-__device__ __forceinline__ int warp_select(const PixelMap<TS>& pm, const float4* s_box, int count,
+template <int TS, int PPT>
+__device__ __forceinline__ int warp_select(const PixelMap<TS, PPT>& pm, const float4* s_box, int count,
                                            int lane, uint16_t* list, int64_t position0,
                                            int64_t limit) {
-  using S = TileShape<TS>;
+  using S = TileShape<TS, PPT>;
   int selected = 0;
   for (int base = 0; base < count; base += S::kWarpLanes) {
     const int j = base + lane;
@@ -137,15 +180,15 @@ __device__ __forceinline__ int warp_select(const PixelMap<TS>& pm, const float4*
 }
 
 template <int TS, bool kGaussian>
-__global__ void __launch_bounds__(TS * TS) composite_fwd_kernel(
+__global__ void __launch_bounds__(TileShape<TS, 1>::kThreads) composite_fwd_kernel(
     const float* __restrict__ projected_mean, const float* __restrict__ inverse_covariance,
     const float* __restrict__ projected_color, const float* __restrict__ projected_opacity,
     const int32_t* __restrict__ gaussian_ids, const int64_t* __restrict__ ranges,
     const gs_params p, float* __restrict__ image, float* __restrict__ final_transmittance,
     int32_t* __restrict__ n_contributors) {
-  using S = TileShape<TS>;
+  using S = TileShape<TS, 1>;
   constexpr int NB = S::kBatch;
-  constexpr int kWarps = S::kPixels / S::kWarpLanes;
+  constexpr int kWarps = S::kWarps;
   __shared__ float4 s_a[NB];
   __shared__ float4 s_b[NB];
   __shared__ float4 s_c[NB];
@@ -154,8 +197,8 @@ __global__ void __launch_bounds__(TS * TS) composite_fwd_kernel(
   const int tile = blockIdx.x;
   const int tid = threadIdx.x;
   const int lane = tid % S::kWarpLanes, warp = tid / S::kWarpLanes;
-  const PixelMap<TS> pm(tile, p.width / TS, tid);
-  const float fpx = static_cast<float>(pm.px), fpy = static_cast<float>(pm.py);
+  const PixelMap<TS, 1> pm(tile, p.width / TS, tid);
+  const float fpx = static_cast<float>(pm.px), fpy = static_cast<float>(pm.py0);
   const int64_t start = ranges[2 * tile], end = ranges[2 * tile + 1];
   const float threshold = p.opacity_threshold;
   uint16_t* list = s_list[warp];
@@ -176,7 +219,7 @@ __global__ void __launch_bounds__(TS * TS) composite_fwd_kernel(
     __syncthreads();
     if (__any_sync(S::kWarpMask, !done)) {
       const int count = static_cast<int>(end - batch < NB ? end - batch : NB);
-      const int selected = warp_select<TS>(pm, s_box, count, lane, list, 0, -1);
+      const int selected = warp_select<TS, 1>(pm, s_box, count, lane, list, 0, -1);
       if (!done) {
         for (int i = 0; i < selected; ++i) {
           const int j = list[i];
@@ -210,7 +253,7 @@ __global__ void __launch_bounds__(TS * TS) composite_fwd_kernel(
     if (__syncthreads_count(!done) == 0) break;
   }
   if (!done) contrib = end - start;
-  const int64_t pix = static_cast<int64_t>(pm.py) * p.width + pm.px;
+  const int64_t pix = static_cast<int64_t>(pm.py0) * p.width + pm.px;
   image[3 * pix] = cr;
   image[3 * pix + 1] = cg;
   image[3 * pix + 2] = cb;
@@ -248,127 +291,138 @@ __device__ __forceinline__ void warp_reduce_scatter9(const float (&v)[9], int la
   for (int o = 16; o > 0; o >>= 1) last += __shfl_xor_sync(0xffffffffu, last, o);
 }
 
-template <int TS>
-__global__ void __launch_bounds__(TS * TS) composite_bwd_kernel(
+template <int TS, int PPT>
+__global__ void __launch_bounds__(TileShape<TS, PPT>::kThreads,
+                                  min_blocks_for_32_warps(TileShape<TS, PPT>::kThreads))
+    composite_bwd_kernel(
     const float* __restrict__ projected_mean, const float* __restrict__ inverse_covariance,
     const float* __restrict__ projected_color, const float* __restrict__ projected_opacity,
     const int32_t* __restrict__ gaussian_ids, const int64_t* __restrict__ ranges,
     const float* __restrict__ grad_image, const float* __restrict__ final_transmittance,
     const int32_t* __restrict__ n_contributors, const gs_params p,
     float* __restrict__ grad_projected) {
-  using Shape = TileShape<TS>;
-  constexpr int NB = Shape::kBatch;
-  constexpr unsigned kMask = Shape::kWarpMask;
+  using S = TileShape<TS, PPT>;
+  constexpr int NB = S::kBatch;
+  constexpr int Q = S::kPpt;
+  constexpr unsigned kMask = S::kWarpMask;
   __shared__ float4 s_a[NB];
   __shared__ float4 s_b[NB];
   __shared__ float4 s_c[NB];
   __shared__ float4 s_box[NB];
-  __shared__ uint16_t s_list[Shape::kPixels / Shape::kWarpLanes][NB];
+  __shared__ uint16_t s_list[S::kWarps][NB];
   __shared__ int s_max_contrib;
   const int tile = blockIdx.x;
   const int tid = threadIdx.x;
-  const int lane = tid % Shape::kWarpLanes, warp = tid / Shape::kWarpLanes;
-  const PixelMap<TS> pm(tile, p.width / TS, tid);
-  const float fpx = static_cast<float>(pm.px), fpy = static_cast<float>(pm.py);
-  const int64_t pix = static_cast<int64_t>(pm.py) * p.width + pm.px;
+  const int lane = tid % S::kWarpLanes, warp = tid / S::kWarpLanes;
+  const PixelMap<TS, PPT> pm(tile, p.width / TS, tid);
+  const float fpx = static_cast<float>(pm.px);
   const float threshold = p.opacity_threshold;
-  const float gr = __ldg(grad_image + 3 * pix), gg = __ldg(grad_image + 3 * pix + 1),
-              gb = __ldg(grad_image + 3 * pix + 2);
-  const float t_final = __ldg(final_transmittance + pix);
-  const int contrib = __ldg(n_contributors + pix);
+  float fpy[Q], gr[Q], gg[Q], gb[Q], t_final[Q];
+  int contrib[Q];
+  int my_max = 0;
+#pragma unroll
+  for (int q = 0; q < Q; ++q) {
+    fpy[q] = static_cast<float>(pm.py(q));
+    const int64_t pix = static_cast<int64_t>(pm.py(q)) * p.width + pm.px;
+    gr[q] = __ldg(grad_image + 3 * pix);
+    gg[q] = __ldg(grad_image + 3 * pix + 1);
+    gb[q] = __ldg(grad_image + 3 * pix + 2);
+    t_final[q] = __ldg(final_transmittance + pix);
+    contrib[q] = __ldg(n_contributors + pix);
+    my_max = contrib[q] > my_max ? contrib[q] : my_max;
+  }
   if (tid == 0) s_max_contrib = 0;
   __syncthreads();
-  const int warp_max = __reduce_max_sync(kMask, contrib);
-  if (lane == 0) atomicMax(&s_max_contrib, warp_max);
+  const int warp_max_contrib = __reduce_max_sync(kMask, my_max);
+  if (lane == 0) atomicMax(&s_max_contrib, warp_max_contrib);
   __syncthreads();
   const int64_t start = ranges[2 * tile];
   int64_t end = ranges[2 * tile + 1];
   if (end > start + s_max_contrib) end = start + s_max_contrib;  // composite_bwd.py:81-83
 
-  const int warp_max_contrib = __reduce_max_sync(kMask, contrib);
   uint16_t* list = s_list[warp];
-  float st = 1.0f, sr = 0.0f, sg = 0.0f, sb = 0.0f;  // suffix behind the current entry
+  float st[Q], sr[Q], sg[Q], sb[Q];  // suffix behind the current entry
+#pragma unroll
+  for (int q = 0; q < Q; ++q) {
+    st[q] = 1.0f;
+    sr[q] = sg[q] = sb[q] = 0.0f;
+  }
   for (int64_t batch_end = end; batch_end > start; batch_end -= NB) {
     const int64_t batch_start = batch_end - NB > start ? batch_end - NB : start;
-    const int64_t k = batch_start + tid;
-    if (tid < NB && k < batch_end) {
-      const Staged s = stage_entry(__ldg(gaussian_ids + k), projected_mean, inverse_covariance,
-                                   projected_color, projected_opacity, p);
-      s_a[tid] = s.a;
-      s_b[tid] = s.b;
-      s_c[tid] = s.c;
-      s_box[tid] = s.box;
-    }
+    stage_batch<TS, PPT>(batch_start, batch_end, gaussian_ids, projected_mean, inverse_covariance,
+                    projected_color, projected_opacity, p, s_a, s_b, s_c, s_box);
     __syncthreads();
     const int count = static_cast<int>(batch_end - batch_start);
-    const int selected = warp_select<TS>(pm, s_box, count, lane, list, batch_start - start,
+    const int selected = warp_select<TS, PPT>(pm, s_box, count, lane, list, batch_start - start,
                                          warp_max_contrib);
     for (int i = selected - 1; i >= 0; --i) {
       const int j = list[i];
       const int64_t position = batch_start + j - start;
       float v[9];
 #pragma unroll
-      for (int q = 0; q < 9; ++q) v[q] = 0.0f;
+      for (int k = 0; k < 9; ++k) v[k] = 0.0f;
       bool active = false;
-      if (position < contrib) {
-        const float4 a = s_a[j];
-        const float4 b = s_b[j];
-        const float dx = fpx - a.x, dy = fpy - a.y;
-        const float xx = a.z, xy = b.w, yy = b.x, o = b.y;
-        const float d2 = pair_d2(dx, dy, xx, a.w, yy);
-        if (d2 <= b.z) {
-          const float prob = d2 >= 0.0f ? det_exp_nonpositive(-0.5f * d2) : det_exp(-0.5f * d2);
-          const float alpha_raw = o * prob;
-          const float alpha = fminf(alpha_raw, kAlphaMax);
-          if (alpha >= kAlphaMin) {
-            active = true;
-            const float4 c = s_c[j];
-            const float denominator = fmaxf(st * (1.0f - alpha), 1e-4f);
-            const float forward = t_final / denominator;
-            const bool still = (1.0f - forward) < threshold;
-            float weight_grad = gr * (c.x - sr);
-            weight_grad += gg * (c.y - sg);
-            weight_grad += gb * (c.z - sb);
-            float grad_alpha = still ? forward * weight_grad : 0.0f;
-            grad_alpha = alpha_raw < kAlphaMax ? grad_alpha : 0.0f;
-            const float probability_grad = grad_alpha * o;
-            const float grad_color = forward * alpha;
-            const float grad_distance = -0.5f * prob * probability_grad;
-            v[0] = -2.0f * grad_distance * (xx * dx + xy * dy);
-            v[1] = -2.0f * grad_distance * (xy * dx + yy * dy);
-            v[2] = grad_distance * dx * dx;
-            v[3] = grad_distance * dx * dy;
-            v[4] = grad_distance * dy * dy;
-            v[5] = grad_color * gr;
-            v[6] = grad_color * gg;
-            v[7] = grad_color * gb;
-            v[8] = grad_alpha * prob;
-            const float local_t = 1.0f - alpha;
-            sr = fmaf(local_t, sr, alpha * c.x);
-            sg = fmaf(local_t, sg, alpha * c.y);
-            sb = fmaf(local_t, sb, alpha * c.z);
-            st = st * local_t;
-          }
-        }
+      const float4 a = s_a[j];
+      const float4 b = s_b[j];
+      const float dx = fpx - a.x;
+      const float xx = a.z, xy = b.w, yy = b.x, o = b.y;
+      const float adx = xx * dx, bdx = a.w * dx;
+#pragma unroll
+      for (int q = 0; q < Q; ++q) {
+        if (!(position < contrib[q])) continue;
+        const float dy = fpy[q] - a.y;
+        const float d2 = fmaf(adx, dx, fmaf(bdx, dy, (yy * dy) * dy));
+        if (!(d2 <= b.z)) continue;
+        const float prob = d2 >= 0.0f ? det_exp_nonpositive(-0.5f * d2) : det_exp(-0.5f * d2);
+        const float alpha_raw = o * prob;
+        const float alpha = fminf(alpha_raw, kAlphaMax);
+        if (!(alpha >= kAlphaMin)) continue;
+        active = true;
+        const float4 c = s_c[j];
+        const float denominator = fmaxf(st[q] * (1.0f - alpha), 1e-4f);
+        const float forward = t_final[q] / denominator;
+        const bool still = (1.0f - forward) < threshold;
+        float weight_grad = gr[q] * (c.x - sr[q]);
+        weight_grad += gg[q] * (c.y - sg[q]);
+        weight_grad += gb[q] * (c.z - sb[q]);
+        float grad_alpha = still ? forward * weight_grad : 0.0f;
+        grad_alpha = alpha_raw < kAlphaMax ? grad_alpha : 0.0f;
+        const float probability_grad = grad_alpha * o;
+        const float grad_color = forward * alpha;
+        const float grad_distance = -0.5f * prob * probability_grad;
+        v[0] += -2.0f * grad_distance * (xx * dx + xy * dy);
+        v[1] += -2.0f * grad_distance * (xy * dx + yy * dy);
+        v[2] += grad_distance * dx * dx;
+        v[3] += grad_distance * dx * dy;
+        v[4] += grad_distance * dy * dy;
+        v[5] += grad_color * gr[q];
+        v[6] += grad_color * gg[q];
+        v[7] += grad_color * gb[q];
+        v[8] += grad_alpha * prob;
+        const float local_t = 1.0f - alpha;
+        sr[q] = fmaf(local_t, sr[q], alpha * c.x);
+        sg[q] = fmaf(local_t, sg[q], alpha * c.y);
+        sb[q] = fmaf(local_t, sb[q], alpha * c.z);
+        st[q] = st[q] * local_t;
       }
       if (__any_sync(kMask, active)) {
         const int g = __float_as_int(s_c[j].w);
         float* dst = grad_projected + 9 * static_cast<int64_t>(g);
-        if constexpr (Shape::kWarpLanes == 32) {
+        if constexpr (S::kWarpLanes == 32) {
           float mine, last;
           warp_reduce_scatter9(v, lane, mine, last);
           if ((lane & 3) == 0) atomicAdd(dst + (lane >> 2), mine);
           if (lane == 1) atomicAdd(dst + 8, last);
         } else {
 #pragma unroll
-          for (int q = 0; q < 9; ++q) {
+          for (int k = 0; k < 9; ++k) {
 #pragma unroll
-            for (int o = Shape::kWarpLanes / 2; o > 0; o >>= 1)
-              v[q] += __shfl_xor_sync(kMask, v[q], o);
+            for (int off = S::kWarpLanes / 2; off > 0; off >>= 1)
+              v[k] += __shfl_xor_sync(kMask, v[k], off);
           }
           if (lane == 0) {
 #pragma unroll
-            for (int q = 0; q < 9; ++q) atomicAdd(dst + q, v[q]);
+            for (int k = 0; k < 9; ++k) atomicAdd(dst + k, v[k]);
           }
         }
       }
@@ -376,6 +430,17 @@ __global__ void __launch_bounds__(TS * TS) composite_bwd_kernel(
     __syncthreads();
   }
 }
+
+// Pixels per thread of the backward: two, so one warp reduction and one set
+// of atomics per Gaussian covers an 8x8 block (the forward keeps one pixel per
+// thread; its early exit and 8x4 warp blocks cull best).
+#ifndef GS_BWD_PPT
+#define GS_BWD_PPT 2
+#endif
+template <int TS>
+struct BwdPpt {
+  static constexpr int value = TS * TS / GS_BWD_PPT >= 16 ? GS_BWD_PPT : 1;
+};
 
 }  // namespace
 
@@ -421,9 +486,12 @@ int32_t launch_composite_bwd(int64_t n, const float* projected_mean,
       static_cast<int64_t>(p.width / p.tile_size) * (p.height / p.tile_size);
   if (num_tiles == 0 || n == 0) return GS_OK;
 #define GS_LAUNCH(TS)                                                                          \
-  composite_bwd_kernel<TS><<<static_cast<unsigned>(num_tiles), TS * TS, 0, stream>>>(         \
-      projected_mean, inverse_covariance, projected_color, projected_opacity, gaussian_ids,    \
-      ranges, grad_image, final_transmittance, n_contributors, p, grad_projected)
+  composite_bwd_kernel<TS, BwdPpt<TS>::value>                                                  \
+      <<<static_cast<unsigned>(num_tiles), TileShape<TS, BwdPpt<TS>::value>::kThreads, 0,       \
+         stream>>>(                                                                            \
+          projected_mean, inverse_covariance, projected_color, projected_opacity,              \
+          gaussian_ids, ranges, grad_image, final_transmittance, n_contributors, p,            \
+          grad_projected)
   GS_TILE_DISPATCH(p.tile_size, GS_LAUNCH)
 #undef GS_LAUNCH
   return check_launch();
