@@ -14,8 +14,9 @@ CUDA events over K steps (max over ranks). Inputs exceed the 126 MB L2
 C restatement of the reference's rasterizer in ``oracle/`` (the reference is
 Python with Triton kernels and does not travel to the GPU box). Each step is a
 bounded sample of the view -- projection, binning and projection backward of
-all Gaussians, compositing forward and backward of a sample of tiles scaled to
-all tiles.
+a chunk of the Gaussians, compositing forward and backward of a sample of
+tiles, each scaled to the whole view -- sized so the run stays within about
+two minutes whatever --steps and --warmup are.
 """
 
 from __future__ import annotations
@@ -58,7 +59,7 @@ COMPOSITE_BWD_FLOPS = 64
 def parse_args():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--steps", type=int, default=100)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=("b200", "reference"), default="b200")
     p.add_argument("--points", type=int, default=1_000_000)
@@ -81,6 +82,7 @@ class ClockSampler:
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    PERIOD_MS = 50
 
     def __init__(self, index):
         self.index = index
@@ -93,7 +95,7 @@ class ClockSampler:
             self.file = open(self.path, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-i", str(self.index), "-lms", "200"], stdout=self.file,
+                 "-i", str(self.index), "-lms", str(self.PERIOD_MS)], stdout=self.file,
                 stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
@@ -102,11 +104,19 @@ class ClockSampler:
         deadline = time.time() + 5.0
         while time.time() < deadline and os.path.getsize(self.path) == 0:
             time.sleep(0.02)
+        self.lines_before = self._line_count()
         return self
+
+    def _line_count(self):
+        with open(self.path) as f:
+            return sum(1 for _ in f)
 
     def __exit__(self, *exc):
         if self.proc is not None:
-            time.sleep(0.25)  # one more sample covering the end of the region
+            # Samples written up to now (plus the one in flight) cover the
+            # region; later ones would be of an idle GPU.
+            time.sleep(self.PERIOD_MS / 1000.0)
+            self.lines_after = self._line_count()
             self.proc.terminate()
             self.proc.wait(timeout=10)
             self.file.close()
@@ -116,10 +126,15 @@ class ClockSampler:
             return None
         rows = []
         with open(self.path) as f:
-            for line in f:
-                parts = [x.strip() for x in line.split(",")]
-                if len(parts) >= 9 and parts[1].replace(".", "").isdigit():
-                    rows.append(parts)
+            lines = f.readlines()
+        # Keep the samples taken while the timed region ran (the last one
+        # before it started bounds it from below).
+        first = max(0, self.lines_before - 1)
+        window = lines[first:self.lines_after] or lines
+        for line in window:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 9 and parts[1].replace(".", "").isdigit():
+                rows.append(parts)
         if not rows:
             return None
         sm = [float(r[1]) for r in rows]
@@ -232,8 +247,26 @@ def make_view(scene, rank):
     return cam, torch.rand(1080, 1920, 3, generator=g)
 
 
+# Seconds of CPU work the reference arm may spend on its timed and warm-up
+# steps together. A step always composites at least MIN_SAMPLE_TILES tiles
+# (enough to keep every host thread busy); the chunk of Gaussians projected,
+# binned and back-projected shrinks with the time left per step.
+REFERENCE_BUDGET_S = 120.0
+MIN_SAMPLE_TILES = 128
+
+
+def sample_size(steps, warmup, num_points):
+    """(Gaussians in the chunk, tiles) of one reference-arm step."""
+    per_step = REFERENCE_BUDGET_S / max(1, steps + warmup)
+    tiles = 256 if per_step >= 2.0 else MIN_SAMPLE_TILES
+    fraction = min(1.0, max(1.0 / 64.0, (per_step - 0.6) / 4.4))
+    return max(1, int(round(num_points * fraction))), tiles
+
+
 def run_reference(args, rank, world):
-    """CPU restatement of the reference, timed on this host's cores (rank 0)."""
+    """CPU restatement of the reference, timed on this host's cores (rank 0).
+    Each step is a bounded sample of the view, sized so warm-up plus timed
+    steps stay within about REFERENCE_BUDGET_S."""
     if rank != 0:
         return
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
@@ -244,10 +277,12 @@ def run_reference(args, rank, world):
     scene = scenes.config2(num_points=args.points)
     cores = os.cpu_count() or 1
     os.environ.setdefault("OMP_NUM_THREADS", str(cores))
+    chunk, tiles = sample_size(args.steps, args.warmup, scene.num_points)
+    view = cpu_view_setup(O, scene)
     step_s = []
     sample = None
     for i in range(args.warmup + args.steps):
-        seconds, sample = cpu_view_seconds(O, scene, tiles=256, seed=i)
+        seconds, sample = cpu_view_seconds(O, view, chunk=chunk, tiles=tiles, seed=i)
         if i >= args.warmup:
             step_s.append(seconds)
     per_view = statistics.median(step_s)
@@ -264,36 +299,81 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
-def cpu_view_seconds(O, scene, tiles, seed):
-    """Seconds for one config-2 view on the CPU oracle: projection, binning and
-    projection backward of all Gaussians timed in full; compositing forward and
-    backward timed on `tiles` random tiles and scaled to all tiles."""
+def cpu_view_setup(O, scene):
+    """The whole view's projection and binning, which the sampled compositing
+    steps read, and the per-view fixed cost of the compositing calls (image
+    buffers; in the backward the [intersections, 9] row buffer and its
+    reduction per Gaussian), timed once with an empty tile list."""
     inputs, s = O.scene_inputs(scene)
     keys = ("mean", "rotation", "scale", "opacity", "color", "camera_rotation",
             "camera_translation")
-    t0 = time.perf_counter()
     proj = O.project(*(inputs[k] for k in keys), s)
-    t1 = time.perf_counter()
     binned = O.bin(proj["bounds"], proj["projected_mean"][:, 2], proj["counts"], s)
-    t2 = time.perf_counter()
-    rng = np.random.default_rng(seed)
-    chosen = rng.choice(s.num_tiles, size=min(tiles, s.num_tiles), replace=False).astype(np.int32)
+    grad_image = np.full((s.height, s.width, 3), 1.0 / (1920 * 1080 * 3), np.float32)
+    view = {"scene": scene, "inputs": inputs, "settings": s, "keys": keys, "proj": proj,
+            "binned": binned, "grad_image": grad_image}
+    none = np.zeros((0,), np.int32)
+    fixed = [composite_seconds(O, view, none) for _ in range(6)][1:]  # first call warms up
+    view["fixed_fwd"] = statistics.median(f[0] for f in fixed)
+    view["fixed_bwd"] = statistics.median(f[1] for f in fixed)
+    return view
+
+
+def composite_seconds(O, view, tiles):
+    """Seconds of the oracle's compositing forward and backward over `tiles`."""
+    s, proj, binned = view["settings"], view["proj"], view["binned"]
+    t0 = time.perf_counter()
     comp = O.composite(proj["projected_mean"], proj["inverse_covariance"],
                        proj["projected_color"], proj["projected_opacity"],
-                       binned["gaussian_ids"], binned["ranges"], s, tiles=chosen)
+                       binned["gaussian_ids"], binned["ranges"], s, tiles=tiles)
+    t1 = time.perf_counter()
+    O.composite_bwd(dict(proj, **binned, **comp), view["grad_image"], s, tiles=tiles)
+    t2 = time.perf_counter()
+    return t1 - t0, t2 - t1
+
+
+def cpu_view_seconds(O, view, chunk, tiles, seed):
+    """Seconds for one config-2 view on the CPU oracle, from a bounded sample:
+    projection, binning and projection backward of a contiguous random chunk
+    of `chunk` Gaussians scaled to all of them, plus compositing forward and
+    backward of `tiles` random tiles -- the per-view fixed cost once, the
+    per-tile remainder scaled to all tiles by list entries."""
+    s, inputs, keys = view["settings"], view["inputs"], view["keys"]
+    n = view["scene"].num_points
+    rng = np.random.default_rng(seed)
+    first = int(rng.integers(0, n - chunk + 1))
+    part = slice(first, first + chunk)
+    chunk_inputs = [inputs[k][part] if k not in ("camera_rotation", "camera_translation")
+                    else inputs[k] for k in keys]
+    chosen = rng.choice(s.num_tiles, size=min(tiles, s.num_tiles), replace=False).astype(np.int32)
+    # Longest lists first, so the host threads' dynamic schedule balances a
+    # small sample as well as it balances the whole view.
+    ranges = view["binned"]["ranges"]
+    chosen = chosen[np.argsort(-(ranges[chosen, 1] - ranges[chosen, 0]), kind="stable")]
+    t0 = time.perf_counter()
+    chunk_proj = O.project(*chunk_inputs, s)
+    t1 = time.perf_counter()
+    O.bin(chunk_proj["bounds"], chunk_proj["projected_mean"][:, 2], chunk_proj["counts"], s)
+    t2 = time.perf_counter()
+    fwd_s, bwd_s = composite_seconds(O, view, chosen)
+    grad_projected = np.zeros((chunk, 9), np.float32)
     t3 = time.perf_counter()
-    fwd = dict(proj, **binned, **comp)
-    grad_image = np.full((s.height, s.width, 3), 1.0 / (1920 * 1080 * 3), np.float32)
-    grad_projected = O.composite_bwd(fwd, grad_image, s, tiles=chosen)
+    O.project_bwd(*chunk_inputs, chunk_proj["inverse_covariance"], grad_projected,
+                  chunk_proj["counts"], s)
     t4 = time.perf_counter()
-    O.project_bwd(*(inputs[k] for k in keys), proj["inverse_covariance"], grad_projected,
-                  proj["counts"], s)
-    t5 = time.perf_counter()
-    scale = s.num_tiles / len(chosen)
-    seconds = (t1 - t0) + (t2 - t1) + (t3 - t2) * scale + (t4 - t3) * scale + (t5 - t4)
-    sample = (f"one config-2 view: projection, binning, projection backward of all "
-              f"{scene.num_points} Gaussians; composite fwd+bwd on {len(chosen)} of "
-              f"{s.num_tiles} random tiles scaled by {scale:.1f}")
+    gaussian_scale = n / chunk
+    # Ratio estimate: compositing time follows the list entries walked, so the
+    # sampled tiles' time is scaled by all entries over the sampled entries.
+    lengths = ranges[:, 1] - ranges[:, 0]
+    tile_scale = float(lengths.sum()) / max(1.0, float(lengths[chosen].sum()))
+    fixed = view["fixed_fwd"] + view["fixed_bwd"]
+    per_tile = max(0.0, fwd_s + bwd_s - fixed)
+    seconds = ((t1 - t0) + (t2 - t1) + (t4 - t3)) * gaussian_scale + fixed + per_tile * tile_scale
+    sample = (f"one config-2 view: projection, binning, projection backward of {chunk} of "
+              f"{n} Gaussians scaled by {gaussian_scale:.2f}; composite fwd+bwd on "
+              f"{len(chosen)} of {s.num_tiles} random tiles, per-tile time scaled by "
+              f"{tile_scale:.1f} (all list entries / sampled entries), per-view fixed "
+              f"time ({fixed:.2f} s) counted once")
     return seconds, sample
 
 
@@ -401,31 +481,45 @@ def main():
 
     # End to end through the public API with host buffers: each step copies the
     # Gaussian parameters and the target from pinned host memory, renders
-    # forward + backward, and reads the loss back.
-    pinned = [t.pin_memory() for t in host]
-    target_pinned = target_cpu.pin_memory()
-    e2e_params = [torch.empty_like(p) for p in params]
-    e2e_target = torch.empty_like(target)
-    e2e_splats = GaussianSplat.from_tensors(*e2e_params)
-    e2e_trainable = [e2e_splats.mean, e2e_splats.rotation, e2e_splats.scale,
-                     e2e_splats.opacity, e2e_splats.color]
-    for p in e2e_trainable:
-        p.requires_grad_(True)
-    h2d = sum(t.numel() * t.element_size() for t in host) + target_cpu.numel() * 4
+    # forward + backward, and reads the loss back. Inputs are double-buffered:
+    # the copy of step i+1 runs on a copy stream while step i computes (the
+    # buffer it overwrites was last read by step i-1, which the loss read-back
+    # has already waited for), so the step time is max(copy, compute).
+    pinned = [t.pin_memory() for t in host] + [target_cpu.pin_memory()]
+    h2d = sum(t.numel() * t.element_size() for t in pinned)
+    copy_stream = torch.cuda.Stream(device)
+    slots = []
+    for _ in range(2):
+        buffers = [torch.empty_like(p) for p in params] + [torch.empty_like(target)]
+        slot_splats = GaussianSplat.from_tensors(*buffers[:5])
+        slot_trainable = [slot_splats.mean, slot_splats.rotation, slot_splats.scale,
+                          slot_splats.opacity, slot_splats.color]
+        for p in slot_trainable:
+            p.requires_grad_(True)
+        slots.append((buffers, slot_splats, slot_trainable, torch.cuda.Event()))
 
-    def e2e_step():
-        with torch.no_grad():
-            for dst, src in zip(e2e_params, pinned):
+    def prefetch(i):
+        buffers, _, _, ready = slots[i % 2]
+        with torch.no_grad(), torch.cuda.stream(copy_stream):
+            for dst, src in zip(buffers, pinned):
                 dst.copy_(src, non_blocking=True)
-            e2e_target.copy_(target_pinned, non_blocking=True)
-        loss = vp_train_step(e2e_splats, [camera], [e2e_target], e2e_trainable,
-                             lambda s, c: render(s)[0],
-                             lambda image, t: (image[:crop_h, :crop_w] - t).abs().mean())
-        return loss.item()
+            ready.record(copy_stream)
 
-    for _ in range(max(1, args.warmup // 2)):
-        e2e_step()
-    e2e_ms = timed(e2e_step, max(3, args.steps // 2))
+    def e2e_run(steps):
+        prefetch(0)
+        for i in range(steps):
+            if i + 1 < steps:
+                prefetch(i + 1)
+            buffers, slot_splats, slot_trainable, ready = slots[i % 2]
+            torch.cuda.current_stream().wait_event(ready)
+            loss = vp_train_step(slot_splats, [camera], [buffers[-1]], slot_trainable,
+                                 lambda s, c: render(s)[0],
+                                 lambda image, t: (image[:crop_h, :crop_w] - t).abs().mean())
+            loss.item()
+
+    e2e_run(max(1, args.warmup // 2))
+    e2e_steps = max(3, args.steps // 2)
+    e2e_ms = timed(lambda: e2e_run(e2e_steps), 1) / e2e_steps
 
     hbm_peak, peak_kind = load_peaks()
     launches_per_step = 15  # 1 projection, 6 count-phase, 5 sort-phase, 2 composite, 1 proj bwd
@@ -484,7 +578,9 @@ def main():
         import oracle as O
 
         cpu_scene = scenes.config2(num_points=args.points)
-        seconds, sample = cpu_view_seconds(O, cpu_scene, tiles=256, seed=0)
+        view = cpu_view_setup(O, cpu_scene)
+        seconds, sample = cpu_view_seconds(O, view, chunk=cpu_scene.num_points, tiles=256,
+                                           seed=0)
         line["cpu_baseline"] = {"value": 1.0 / seconds, "unit": UNIT,
                                 "cores": os.cpu_count(), "kind": "port", "sample": sample}
     if rank == 0:

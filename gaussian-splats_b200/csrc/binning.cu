@@ -15,13 +15,15 @@
 //
 // Both sorts are LSD radix sorts with 8-bit digits, one kernel per pass in
 // the "onesweep" style: each CTA ranks a 4096-key tile in shared memory
-// (warp-level match_any ranking, which is stable), publishes its per-digit
-// counts, computes its global offsets by decoupled look-back over the
-// preceding CTAs, and writes the keys out digit-grouped and coalesced. CTAs
-// take their tile index from an atomic counter, so a CTA only ever waits on
-// CTAs that already started. Every spin is bounded; on expiry the CTA records
-// an error word and proceeds, so a fault costs a wrong result and an error
-// code, never a hung GPU.
+// (warp-level ranking: the lanes holding the same digit are found with one
+// ballot per digit bit, and lanes are ranked in order, which is stable),
+// publishes its per-digit counts, computes its global offsets by decoupled
+// look-back over the preceding CTAs (reading several predecessors' status
+// words per round trip), and writes the keys out digit-grouped and
+// coalesced. CTAs take their tile index from an atomic counter, so a CTA
+// only ever waits on CTAs that already started. Every spin is bounded; on
+// expiry the CTA records an error word and proceeds, so a fault costs a wrong
+// result and an error code, never a hung GPU.
 #include "common.cuh"
 
 namespace gs {
@@ -144,9 +146,56 @@ __device__ __forceinline__ uint32_t block_exclusive_scan(uint32_t v, uint32_t* s
   return warp_prefix + x - v;
 }
 
+// Decoupled look-back for one digit column of the status words: the sum of
+// the predecessors' counts from block `b` down to the nearest inclusive
+// prefix. The words of kLookback predecessors are loaded together, so a walk
+// over many blocks that are still publishing costs one L2 round trip per
+// kLookback blocks instead of one per block. Each wait is bounded; on expiry
+// the error word is set and the walk stops.
+constexpr int kLookback = 4;
+__device__ __forceinline__ uint32_t lookback_window(const uint32_t* status, int d, int64_t b,
+                                                    uint32_t* error) {
+  uint32_t exclusive = 0;
+  while (b >= 0) {
+    uint32_t words[kLookback];
+#pragma unroll
+    for (int i = 0; i < kLookback; ++i)
+      words[i] = b - i >= 0 ? ld_volatile(status + (b - i) * kRadix + d) : kFlagPrefix;
+#pragma unroll
+    for (int i = 0; i < kLookback; ++i) {
+      int spins = 0;
+      while ((words[i] >> 30) == 0) {
+        if (++spins > kSpinLimit) {
+          atomicOr(error, kErrLookbackTimeout);
+          return exclusive;
+        }
+        if (spins > 64) __nanosleep(64);
+        words[i] = ld_volatile(status + (b - i) * kRadix + d);
+      }
+      exclusive += words[i] & kValueMask;
+      if ((words[i] >> 30) != 1) return exclusive;  // inclusive prefix (or block < 0)
+    }
+    b -= kLookback;
+  }
+  return exclusive;
+}
+
+// Lanes of the warp holding the same 9-bit label as this lane (8 digit bits
+// plus the invalid marker kRadix): one ballot per bit.
+__device__ __forceinline__ unsigned match_digit(int d) {
+  unsigned peers = 0xffffffffu;
+#pragma unroll
+  for (int bit = 0; bit < 9; ++bit) {
+    const bool set = (d >> bit) & 1;
+    const unsigned vote = __ballot_sync(0xffffffffu, set);
+    peers &= set ? vote : ~vote;
+  }
+  return peers;
+}
+
 // One stable LSD pass over 8 bits at `shift`.
 template <class Source>
-__global__ void __launch_bounds__(kThreads) sort_pass_kernel(
+__global__ void __launch_bounds__(kThreads, 3) sort_pass_kernel(
     Source src, Count count, int shift, const uint32_t* __restrict__ pass_hist,
     uint32_t* __restrict__ status, uint32_t* __restrict__ tile_counter,
     uint32_t* __restrict__ keys_out, uint32_t* __restrict__ values_out,
@@ -184,7 +233,7 @@ __global__ void __launch_bounds__(kThreads) sort_pass_kernel(
 #pragma unroll
   for (int j = 0; j < kItems; ++j) {
     const int d = digits[j];
-    const unsigned peers = __match_any_sync(0xffffffffu, d);
+    const unsigned peers = match_digit(d);
     const int leader = __ffs(peers) - 1;
     uint32_t base = 0;
     if (lane == leader && d < kRadix) {
@@ -210,23 +259,7 @@ __global__ void __launch_bounds__(kThreads) sort_pass_kernel(
   st_volatile(my_status, (block == 0 ? kFlagPrefix : kFlagAggregate) | block_count);
   uint32_t exclusive = 0;
   if (block > 0) {
-    int64_t b = static_cast<int64_t>(block) - 1;
-    while (b >= 0) {
-      const uint32_t* s = status + b * kRadix + d;
-      uint32_t word = ld_volatile(s);
-      int spins = 0;
-      while ((word >> 30) == 0) {
-        if (++spins > kSpinLimit) {
-          atomicOr(error, kErrLookbackTimeout);
-          break;
-        }
-        if (spins > 64) __nanosleep(64);
-        word = ld_volatile(s);
-      }
-      exclusive += word & kValueMask;
-      if ((word >> 30) != 1) break;  // inclusive prefix found (or timed out)
-      --b;
-    }
+    exclusive = lookback_window(status, d, static_cast<int64_t>(block) - 1, error);
     st_volatile(my_status, kFlagPrefix | (exclusive + block_count));
   }
   // Global exclusive offset of digit d across the whole pass.
@@ -287,31 +320,43 @@ __global__ void __launch_bounds__(kThreads) count_scan_kernel(
   }
   uint32_t block_total;
   const uint32_t thread_prefix = block_exclusive_scan(local, s_tmp, &block_total);
-  if (threadIdx.x == 0) {
+  if (threadIdx.x < 32) {
+    // Warp-wide look-back: lane l reads the status of block b - l; the
+    // nearest inclusive prefix ends the walk, aggregates before it add up.
+    const int lane = threadIdx.x;
     uint64_t* my_status = status + block;
-    st_volatile(my_status, (block == 0 ? kScanFlagPrefix : kScanFlagAggregate) | block_total);
+    if (lane == 0)
+      st_volatile(my_status, (block == 0 ? kScanFlagPrefix : kScanFlagAggregate) | block_total);
     uint64_t exclusive = 0;
-    if (block > 0) {
-      int64_t b = static_cast<int64_t>(block) - 1;
-      while (b >= 0) {
-        uint64_t word = ld_volatile(status + b);
-        int spins = 0;
-        while ((word >> 62) == 0) {
-          if (++spins > kSpinLimit) {
-            atomicOr(error, kErrLookbackTimeout);
-            break;
-          }
-          if (spins > 64) __nanosleep(64);
-          word = ld_volatile(status + b);
+    bool timed_out = false;
+    for (int64_t b = static_cast<int64_t>(block) - 1; b >= 0 && !timed_out; b -= 32) {
+      const int64_t mine = b - lane;
+      uint64_t word = mine >= 0 ? ld_volatile(status + mine) : kScanFlagPrefix;
+      int spins = 0;
+      while ((word >> 62) == 0) {
+        if (++spins > kSpinLimit) {
+          atomicOr(error, kErrLookbackTimeout);
+          word = kScanFlagPrefix;  // stop here; the result is flagged wrong
+          timed_out = true;
+          break;
         }
-        exclusive += word & kScanValueMask;
-        if ((word >> 62) != 1) break;
-        --b;
+        if (spins > 64) __nanosleep(64);
+        word = ld_volatile(status + mine);
       }
-      st_volatile(my_status, kScanFlagPrefix | (exclusive + block_total));
+      const unsigned prefix_lanes = __ballot_sync(0xffffffffu, (word >> 62) != 1);
+      timed_out = __any_sync(0xffffffffu, timed_out);
+      // Lanes up to and including the nearest prefix contribute.
+      const int stop = prefix_lanes ? __ffs(prefix_lanes) - 1 : 31;
+      uint64_t v = lane <= stop ? (word & kScanValueMask) : 0;
+      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      exclusive += v;
+      if (prefix_lanes) break;
     }
-    s_exclusive = exclusive;
-    if (tile_start + kTile >= n) *total_out = static_cast<int64_t>(exclusive + block_total);
+    if (lane == 0) {
+      if (block > 0) st_volatile(my_status, kScanFlagPrefix | (exclusive + block_total));
+      s_exclusive = exclusive;
+      if (tile_start + kTile >= n) *total_out = static_cast<int64_t>(exclusive + block_total);
+    }
   }
   __syncthreads();
   // Offsets are stored as 32 bits; totals of 2^30 and more are rejected on
