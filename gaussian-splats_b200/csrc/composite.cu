@@ -24,7 +24,8 @@
 //  * per warp, the staged entry carries the bounding box of the ellipse
 //    d2 <= 1.0201 skip_cutoff; each warp ballots the staged entries against
 //    its pixel block and walks only the ones whose box meets it (in list
-//    order). For conics with condition number below ~1e3 the float32 d2 of
+//    order); the backward also drops entries whose ellipse itself misses
+//    the block (minimum of the conic's quadratic form over the block). For conics with condition number below ~1e3 the float32 d2 of
 //    any pixel outside the box is provably above the cutoff (its relative
 //    rounding error is < 2 kappa * 4 ulp < 1e-3); other conics get an
 //    infinite box.
@@ -157,19 +158,55 @@ __device__ __forceinline__ void stage_batch(int64_t first, int64_t last,
   }
 }
 
+// True unless the ellipse d2 <= 1.0201 cutoff provably misses the rectangle
+// [x0, x1] x [y0, y1] (which holds every pixel of a warp). The minimum of the
+// positive definite form q(u, v) = xx u^2 + 2 xy u v + yy v^2 over the
+// rectangle (u, v relative to the mean) is 0 when the mean is inside, else it
+// lies on an edge, at the edge's critical point clamped to the edge. A
+// candidate computed with rounding is still a point of the rectangle, and q
+// grows only quadratically away from the true minimiser, so the computed
+// minimum exceeds the true one by far less than the 2% margin; conics too
+// ill-conditioned for that carry an infinite box and always pass.
+__device__ __forceinline__ bool ellipse_meets_rect(const float4& a, const float4& b,
+                                                   const float4& box, float x0, float x1,
+                                                   float y0, float y1) {
+  if (box.x == -__int_as_float(0x7f800000)) return true;  // unconditioned: no exact test
+  const float xx = a.z, yy = b.x, xy = b.w;
+  const float u0 = x0 - a.x, u1 = x1 - a.x, v0 = y0 - a.y, v1 = y1 - a.y;
+  if (u0 <= 0.0f && u1 >= 0.0f && v0 <= 0.0f && v1 >= 0.0f) return true;
+  auto q = [&](float u, float v) { return xx * u * u + 2.0f * xy * u * v + yy * v * v; };
+  // Critical v per u and u per v (approximate division: any point of the
+  // rectangle is a valid candidate).
+  const float ru = __fdividef(-xy, yy), rv = __fdividef(-xy, xx);
+  float m = q(u0, fminf(fmaxf(ru * u0, v0), v1));
+  m = fminf(m, q(u1, fminf(fmaxf(ru * u1, v0), v1)));
+  m = fminf(m, q(fminf(fmaxf(rv * v0, u0), u1), v0));
+  m = fminf(m, q(fminf(fmaxf(rv * v1, u0), u1), v1));
+  return m <= 1.0201f * b.z;
+}
+
 // Appends, in order, the batch entries whose box meets this warp's pixel
-// block (and, when `limit` >= 0, whose list position is below `limit`) to the
-// warp's list in shared memory; returns how many. One ballot per 32 entries
-// replaces a per-entry test inside the pixel loop.
-template <int TS, int PPT>
-__device__ __forceinline__ int warp_select(const PixelMap<TS, PPT>& pm, const float4* s_box, int count,
+// block (with kExact, whose ellipse does) and, when `limit` >= 0, whose list
+// position is below `limit`, to the warp's list in shared memory; returns how
+// many. One ballot per 32 entries replaces a per-entry test inside the pixel
+// loop. The exact test pays in the backward, where every selected entry costs
+// a warp reduction and atomics; in the forward it costs more than it saves.
+template <int TS, int PPT, bool kExact>
+__device__ __forceinline__ int warp_select(const PixelMap<TS, PPT>& pm, const float4* s_a,
+                                           const float4* s_b, const float4* s_box, int count,
                                            int lane, uint16_t* list, int64_t position0,
                                            int64_t limit) {
   using S = TileShape<TS, PPT>;
   int selected = 0;
   for (int base = 0; base < count; base += S::kWarpLanes) {
     const int j = base + lane;
-    bool hit = j < count && !pm.misses(s_box[j]);
+    bool hit = false;
+    if (j < count) {
+      const float4 box = s_box[j];
+      hit = !pm.misses(box);
+      if (kExact && hit)
+        hit = ellipse_meets_rect(s_a[j], s_b[j], box, pm.rx0, pm.rx1, pm.ry0, pm.ry1);
+    }
     if (limit >= 0) hit = hit && position0 + j < limit;
     const unsigned mask = __ballot_sync(S::kWarpMask, hit);
     if (hit) list[selected + __popc(mask & ((1u << lane) - 1u))] = static_cast<uint16_t>(j);
@@ -219,7 +256,7 @@ __global__ void __launch_bounds__(TileShape<TS, 1>::kThreads) composite_fwd_kern
     __syncthreads();
     if (__any_sync(S::kWarpMask, !done)) {
       const int count = static_cast<int>(end - batch < NB ? end - batch : NB);
-      const int selected = warp_select<TS, 1>(pm, s_box, count, lane, list, 0, -1);
+      const int selected = warp_select<TS, 1, false>(pm, s_a, s_b, s_box, count, lane, list, 0, -1);
       if (!done) {
         for (int i = 0; i < selected; ++i) {
           const int j = list[i];
@@ -353,7 +390,7 @@ __global__ void __launch_bounds__(TileShape<TS, PPT>::kThreads,
                     projected_color, projected_opacity, p, s_a, s_b, s_c, s_box);
     __syncthreads();
     const int count = static_cast<int>(batch_end - batch_start);
-    const int selected = warp_select<TS, PPT>(pm, s_box, count, lane, list, batch_start - start,
+    const int selected = warp_select<TS, PPT, true>(pm, s_a, s_b, s_box, count, lane, list, batch_start - start,
                                          warp_max_contrib);
     for (int i = selected - 1; i >= 0; --i) {
       const int j = list[i];
