@@ -37,14 +37,42 @@ import torch  # noqa: E402
 
 METRIC = "fwd / fwd+bwd ms per 1080p view at 1M Gaussians; views/sec at 1/2/4/8 GPUs"
 UNIT = "views/s"
-WORKLOAD = "config2: 1M Gaussians SH3, 1920x1080 (rendered 1920x1088), 16x16 tiles, fwd+bwd L1"
-# Algorithmic bytes per Gaussian (K = 16 SH coefficients): projection reads
-# mean, rotation, scale, opacity (44 B) and colour (192 B) and writes
+
+# The BASELINE configs. Config 2 is the headline (the default); the others
+# are measured with --config. `views`: cameras per step over all ranks (None:
+# one camera per rank, weak scaling); `backward`: fwd+bwd with an L1 loss.
+WORKLOADS = {
+    1: dict(name="config1: 16,384 Gaussians SH0, 256x256, 16x16 tiles, fwd+bwd L1 (random "
+                 "target)", views=None, backward=True),
+    2: dict(name="config2: 1M Gaussians SH3, 1920x1080 (rendered 1920x1088), 16x16 tiles, "
+                 "fwd+bwd L1", views=None, backward=True),
+    3: dict(name="config3: 3M Gaussians SH3, 8 cameras per step split over ranks, 1600x1064 "
+                 "(rendered 1600x1072), fwd+bwd L1, gradient all-reduce", views=8,
+            backward=True),
+    4: dict(name="config4: 6M Gaussians SH3, 3840x2160, 64-camera orbit split over ranks, "
+                 "forward only", views=64, backward=False),
+    5: dict(name="config5: 500k Gaussians SH1 in one dense blob, 1920x1080 (rendered "
+                 "1920x1088), fwd+bwd L1", views=None, backward=True),
+}
+WORKLOAD = WORKLOADS[2]["name"]
+
+
+# Algorithmic bytes per Gaussian with K SH coefficients: projection reads
+# mean, rotation, scale, opacity (44 B) and colour (12K B) and writes
 # projected mean, conic, colour, opacity, tile rectangle, count (64 B);
 # projection backward reads the same parameters plus conic, the 9-float
-# screen-space gradient and the count (56 B) and writes 236 B of gradients.
-PROJECT_FWD_BYTES = 44 + 12 * 16 + 64
-PROJECT_BWD_BYTES = 44 + 12 * 16 + 56 + 44 + 12 * 16
+# screen-space gradient and the count (56 B) and writes 44 + 12K B of
+# gradients. K = 16: 300 B and 528 B.
+def project_fwd_bytes(k):
+    return 44 + 12 * k + 64
+
+
+def project_bwd_bytes(k):
+    return 44 + 12 * k + 56 + 44 + 12 * k
+
+
+PROJECT_FWD_BYTES = project_fwd_bytes(16)
+PROJECT_BWD_BYTES = project_bwd_bytes(16)
 # Per evaluated (pixel, Gaussian) pair, the reference's forward arithmetic
 # (composite.py:159-186): offsets 2, distance 9, exp argument 1, exp 1,
 # alpha 4, activity test 3, weight 2, colour 6, transmittance 3.
@@ -62,7 +90,10 @@ def parse_args():
     p.add_argument("--steps", type=int, default=100)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=("b200", "reference"), default="b200")
-    p.add_argument("--points", type=int, default=1_000_000)
+    p.add_argument("--config", type=int, choices=sorted(WORKLOADS), default=2,
+                   help="BASELINE config to run (2, the headline, by default)")
+    p.add_argument("--points", type=int, default=None,
+                   help="override the config's Gaussian count (smaller smoke runs)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     return p.parse_args()
 
@@ -173,7 +204,8 @@ def fp32_peak_tflops(device):
 
 
 def kernel_durations(outputs, params, camera, grad_image, settings, device, repeats=5):
-    """Per-launch milliseconds of the four main kernels, each launched through
+    """Per-launch milliseconds of the four main kernels (the two forward ones
+    when `grad_image` is None), each launched through
     the C ABI right after a 1 GiB L2 flush, with CUDA events around the launch
     on the launching stream (the GPU is still busy with the flush when the
     launch is enqueued, so no host gap is timed). Returns {stage: mean ms}."""
@@ -203,7 +235,7 @@ def kernel_durations(outputs, params, camera, grad_image, settings, device, repe
     out_img, out_t = torch.empty_like(image), torch.empty_like(final_t)
     out_nc = torch.empty_like(n_contrib)
     grad_projected = torch.empty((n, 9), device=device)
-    grads = [torch.empty_like(t) for t in params]
+    grads = [torch.empty_like(t) for t in params] if grad_image is not None else None
     launches = {
         "project_fwd": lambda: lib.gs_project_fwd(
             n, k, P(mean), P(rotation), P(scale), P(opacity), P(color), P(cam_r), P(cam_t), pref,
@@ -211,13 +243,14 @@ def kernel_durations(outputs, params, camera, grad_image, settings, device, repe
         "composite_fwd": lambda: lib.gs_composite_fwd(
             P(pmean), P(conic), P(pcolor), P(popacity), P(ids), P(ranges), pref, P(out_img),
             P(out_t), P(out_nc), stream),
-        "composite_bwd": lambda: lib.gs_composite_bwd(
-            n, P(pmean), P(conic), P(pcolor), P(popacity), P(ids), P(ranges), P(grad_image),
-            P(final_t), P(n_contrib), pref, P(grad_projected), stream),
-        "project_bwd": lambda: lib.gs_project_bwd(
-            n, k, P(mean), P(rotation), P(scale), P(opacity), P(color), P(cam_r), P(cam_t),
-            P(conic), P(grad_projected), P(counts), pref, *(P(g) for g in grads), stream),
     }
+    if grad_image is not None:
+        launches["composite_bwd"] = lambda: lib.gs_composite_bwd(
+            n, P(pmean), P(conic), P(pcolor), P(popacity), P(ids), P(ranges), P(grad_image),
+            P(final_t), P(n_contrib), pref, P(grad_projected), stream)
+        launches["project_bwd"] = lambda: lib.gs_project_bwd(
+            n, k, P(mean), P(rotation), P(scale), P(opacity), P(color), P(cam_r), P(cam_t),
+            P(conic), P(grad_projected), P(counts), pref, *(P(g) for g in grads), stream)
     flush = torch.empty(1 << 28, dtype=torch.float32, device=device)  # 1 GiB > 126 MB L2
     result = {}
     for name, launch in launches.items():
@@ -234,17 +267,48 @@ def kernel_durations(outputs, params, camera, grad_image, settings, device, repe
     return result
 
 
-def make_view(scene, rank):
-    """Rank 0 renders config 2's camera; other ranks a camera from the same
-    recipe (radius 5, random direction) seeded by rank."""
+def load_scene(config, points=None):
+    """The config's seeded synthetic scene (CPU tensors)."""
     from gaussian_splats_b200 import scenes
 
-    if rank == 0:
-        return scene.cameras[0], scene.targets[0]
-    g = torch.Generator().manual_seed(1000 + rank)
-    cam = scenes.look_at_camera(5.0 * scenes.random_direction(g), fovy_degrees=50.0,
-                                width=1920, height=1080)
-    return cam, torch.rand(1080, 1920, 3, generator=g)
+    make = getattr(scenes, f"config{config}")
+    return make() if points is None else make(num_points=points)
+
+
+# Camera recipe (distance from the origin, vertical FOV) of the single-view
+# configs, for the extra cameras of ranks > 0.
+_SINGLE_VIEW_RECIPE = {1: (4.0, 60.0), 2: (5.0, 50.0), 5: (2.5, 70.0)}
+
+
+def views_for_rank(scene, config, rank, world):
+    """(camera, target) pairs this rank renders each step. Single-view configs:
+    rank 0 renders the config's camera, other ranks a camera of the same recipe
+    from a direction seeded by the rank (weak scaling). Multi-view configs: the
+    config's cameras split over the ranks (strong scaling). Targets are None
+    for forward-only configs; configs without targets get uniform ones."""
+    from gaussian_splats_b200 import scenes
+    from gaussian_splats_b200.view_parallel import shard_views
+
+    width, height = scene.crop
+    backward = WORKLOADS[config]["backward"]
+
+    def target(i, g):
+        if not backward:
+            return None
+        if scene.targets and i is not None:
+            return scene.targets[i]
+        return torch.rand(height, width, 3, generator=g)
+
+    if WORKLOADS[config]["views"] is None:
+        if rank == 0:
+            return [(scene.cameras[0], target(0, torch.Generator().manual_seed(999)))]
+        g = torch.Generator().manual_seed(1000 + rank)
+        distance, fov = _SINGLE_VIEW_RECIPE[config]
+        cam = scenes.look_at_camera(distance * scenes.random_direction(g), fovy_degrees=fov,
+                                    width=width, height=height)
+        return [(cam, target(None, g))]
+    return [(scene.cameras[i], target(i, None))
+            for i in shard_views(len(scene.cameras), world, rank)]
 
 
 # Seconds of CPU work the reference arm may spend on its timed and warm-up
@@ -272,13 +336,12 @@ def run_reference(args, rank, world):
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
 
-    from gaussian_splats_b200 import scenes
-
-    scene = scenes.config2(num_points=args.points)
+    scene = load_scene(args.config, args.points)
+    backward = WORKLOADS[args.config]["backward"]
     cores = os.cpu_count() or 1
     os.environ.setdefault("OMP_NUM_THREADS", str(cores))
     chunk, tiles = sample_size(args.steps, args.warmup, scene.num_points)
-    view = cpu_view_setup(O, scene)
+    view = cpu_view_setup(O, scene, backward)
     step_s = []
     sample = None
     for i in range(args.warmup + args.steps):
@@ -291,7 +354,7 @@ def run_reference(args, rank, world):
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_view * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic", "config": {"workload": WORKLOAD},
+        "data": "synthetic", "config": {"workload": WORKLOADS[args.config]["name"]},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
                          "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -299,19 +362,21 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
-def cpu_view_setup(O, scene):
-    """The whole view's projection and binning, which the sampled compositing
-    steps read, and the per-view fixed cost of the compositing calls (image
-    buffers; in the backward the [intersections, 9] row buffer and its
-    reduction per Gaussian), timed once with an empty tile list."""
+def cpu_view_setup(O, scene, backward=True):
+    """The whole view's projection and binning (of the scene's first camera),
+    which the sampled compositing steps read, and the per-view fixed cost of
+    the compositing calls (image buffers; in the backward the [intersections,
+    9] row buffer and its reduction per Gaussian), timed once with an empty
+    tile list."""
     inputs, s = O.scene_inputs(scene)
     keys = ("mean", "rotation", "scale", "opacity", "color", "camera_rotation",
             "camera_translation")
     proj = O.project(*(inputs[k] for k in keys), s)
     binned = O.bin(proj["bounds"], proj["projected_mean"][:, 2], proj["counts"], s)
-    grad_image = np.full((s.height, s.width, 3), 1.0 / (1920 * 1080 * 3), np.float32)
+    width, height = scene.crop
+    grad_image = np.full((s.height, s.width, 3), 1.0 / (width * height * 3), np.float32)
     view = {"scene": scene, "inputs": inputs, "settings": s, "keys": keys, "proj": proj,
-            "binned": binned, "grad_image": grad_image}
+            "binned": binned, "grad_image": grad_image, "backward": backward}
     none = np.zeros((0,), np.int32)
     fixed = [composite_seconds(O, view, none) for _ in range(6)][1:]  # first call warms up
     view["fixed_fwd"] = statistics.median(f[0] for f in fixed)
@@ -327,7 +392,8 @@ def composite_seconds(O, view, tiles):
                        proj["projected_color"], proj["projected_opacity"],
                        binned["gaussian_ids"], binned["ranges"], s, tiles=tiles)
     t1 = time.perf_counter()
-    O.composite_bwd(dict(proj, **binned, **comp), view["grad_image"], s, tiles=tiles)
+    if view["backward"]:
+        O.composite_bwd(dict(proj, **binned, **comp), view["grad_image"], s, tiles=tiles)
     t2 = time.perf_counter()
     return t1 - t0, t2 - t1
 
@@ -358,8 +424,9 @@ def cpu_view_seconds(O, view, chunk, tiles, seed):
     fwd_s, bwd_s = composite_seconds(O, view, chosen)
     grad_projected = np.zeros((chunk, 9), np.float32)
     t3 = time.perf_counter()
-    O.project_bwd(*chunk_inputs, chunk_proj["inverse_covariance"], grad_projected,
-                  chunk_proj["counts"], s)
+    if view["backward"]:
+        O.project_bwd(*chunk_inputs, chunk_proj["inverse_covariance"], grad_projected,
+                      chunk_proj["counts"], s)
     t4 = time.perf_counter()
     gaussian_scale = n / chunk
     # Ratio estimate: compositing time follows the list entries walked, so the
@@ -369,12 +436,31 @@ def cpu_view_seconds(O, view, chunk, tiles, seed):
     fixed = view["fixed_fwd"] + view["fixed_bwd"]
     per_tile = max(0.0, fwd_s + bwd_s - fixed)
     seconds = ((t1 - t0) + (t2 - t1) + (t4 - t3)) * gaussian_scale + fixed + per_tile * tile_scale
-    sample = (f"one config-2 view: projection, binning, projection backward of {chunk} of "
-              f"{n} Gaussians scaled by {gaussian_scale:.2f}; composite fwd+bwd on "
+    what = "projection, binning, projection backward" if view["backward"] else \
+        "projection, binning"
+    sample = (f"one view: {what} of {chunk} of "
+              f"{n} Gaussians scaled by {gaussian_scale:.2f}; composite "
+              f"{'fwd+bwd' if view['backward'] else 'fwd'} on "
               f"{len(chosen)} of {s.num_tiles} random tiles, per-tile time scaled by "
               f"{tile_scale:.1f} (all list entries / sampled entries), per-view fixed "
               f"time ({fixed:.2f} s) counted once")
     return seconds, sample
+
+
+def sort_passes(num_tiles):
+    """8-bit radix passes of the tile sort for `num_tiles` tiles."""
+    bits = max(0, (max(1, num_tiles) - 1).bit_length())
+    return (bits + 7) // 8
+
+
+def launches_per_view(num_tiles, backward):
+    """This library's kernel launches for one view: projection; the count
+    phase (histogram, 4 depth passes, count scan); the sort phase (emit,
+    histogram when the tile sort has passes, the passes, ranges);
+    compositing; and in the backward compositing and projection backward."""
+    passes = sort_passes(num_tiles)
+    forward = 1 + 6 + (2 + (1 + passes if passes else 0)) + 1
+    return forward + (2 if backward else 0)
 
 
 def main():
@@ -395,35 +481,47 @@ def main():
         return
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
-    from gaussian_splats_b200 import scenes
     from gaussian_splats_b200.rasterize import StageTimer, rasterize_outputs
     from gaussian_splats_b200.splats import GaussianSplat
     from gaussian_splats_b200.view_parallel import train_step as vp_train_step
 
-    scene = scenes.config2(num_points=args.points)
-    camera, target_cpu = make_view(scene, rank)
+    workload = WORKLOADS[args.config]
+    backward = workload["backward"]
+    scene = load_scene(args.config, args.points)
+    views = views_for_rank(scene, args.config, rank, world)
+    cameras = [camera for camera, _ in views]
+    views_per_step = world * len(views) if workload["views"] is None else workload["views"]
     crop_w, crop_h = scene.crop
     host = [t.contiguous() for t in scene.tensors()]
     params = [t.to(device) for t in host]
     splats = GaussianSplat.from_tensors(*params)
     for p in splats.parameters():
-        p.requires_grad_(p is not splats.normals)
-    # The camera stays on the host: its 3x3 matrix is built there once per
-    # render and uploaded (48 bytes), instead of ~15 tiny device kernels.
-    target = target_cpu.to(device)
+        p.requires_grad_(backward and p is not splats.normals)
+    # Cameras stay on the host: each 3x3 matrix is built there once per render
+    # and uploaded (48 bytes), instead of ~15 tiny device kernels.
+    targets_cpu = [target for _, target in views]
+    targets = [t.to(device) if t is not None else None for t in targets_cpu]
     trainable = [splats.mean, splats.rotation, splats.scale, splats.opacity, splats.color]
     settings = scene.settings
 
-    def render(s):
+    def render(s, camera):
         return rasterize_outputs(s, camera, settings.tile_size, settings.opacity_threshold,
                                  settings.near, settings.far)
 
+    def loss_fn(image, target):
+        return (image[:crop_h, :crop_w] - target).abs().mean()
+
+    def forward_step(s=splats):
+        with torch.no_grad():
+            return [render(s, camera)[0] for camera in cameras]
+
     def train_step():
-        # One view per rank; the gradients are summed over ranks with one
-        # all-reduce per parameter tensor (view_parallel.train_step).
-        return vp_train_step(splats, [camera], [target], trainable,
-                             lambda s, c: render(s)[0],
-                             lambda image, t: (image[:crop_h, :crop_w] - t).abs().mean())
+        # This rank's views forward + backward; the gradients are summed over
+        # ranks with one all-reduce per parameter tensor (view_parallel).
+        return vp_train_step(splats, cameras, targets, trainable,
+                             lambda s, c: render(s, c)[0], loss_fn)
+
+    step = train_step if backward else forward_step
 
     def timed(fn, steps):
         if world > 1:
@@ -445,23 +543,23 @@ def main():
         return ms
 
     # Forward only.
-    with torch.no_grad():
-        for _ in range(args.warmup):
-            render(splats)
-        fwd_ms = timed(lambda: render(splats), args.steps)
-
-    # Forward + backward (+ all-reduce): the headline.
     for _ in range(args.warmup):
-        train_step()
+        forward_step()
+    fwd_ms = timed(forward_step, args.steps)
+
+    # The headline step: forward + backward (+ all-reduce), or forward only.
+    for _ in range(args.warmup):
+        step()
     with ClockSampler(local_rank) as clocks, StageTimer() as stages:
-        ms = timed(train_step, args.steps)
+        ms = timed(step, args.steps)
     stage_ms = stages.durations()
     clock = clocks.summary()
-    value = world * 1000.0 / ms
+    value = views_per_step * 1000.0 / ms
 
-    # Structure of the view (for the roofline's work counts).
+    # Structure of this rank's first view (for the roofline's work counts).
+    camera0 = cameras[0]
     with torch.no_grad():
-        out = render(splats)
+        out = render(splats, camera0)
         n_contrib = int(out[2].sum())
         intersections = int(out[7].numel())
         visible = int((out[9] > 0).sum())
@@ -472,30 +570,36 @@ def main():
         nc = out[2].reshape(out[2].shape[0] // ts, ts, out[2].shape[1] // ts, ts)
         tile_max = nc.permute(0, 2, 1, 3).reshape(-1, ts * ts).amax(dim=1).long()
         lengths = out[8][:, 1] - out[8][:, 0]
+        num_tiles = int(lengths.numel())
         pairs = int((torch.minimum(lengths, tile_max) * ts * ts).sum())
-        grad_image = torch.zeros_like(out[0])
-        diff = out[0][:crop_h, :crop_w] - target
-        grad_image[:crop_h, :crop_w] = torch.sign(diff) / diff.numel()
-    kernel_ms = kernel_durations(out, params, camera, grad_image, settings, device)
+        grad_image = None
+        if backward:
+            grad_image = torch.zeros_like(out[0])
+            diff = out[0][:crop_h, :crop_w] - targets[0]
+            grad_image[:crop_h, :crop_w] = torch.sign(diff) / diff.numel()
+    kernel_ms = kernel_durations(out, params, camera0, grad_image, settings, device)
     fp32_peak = fp32_peak_tflops(device)
 
     # End to end through the public API with host buffers: each step copies the
-    # Gaussian parameters and the target from pinned host memory, renders
-    # forward + backward, and reads the loss back. Inputs are double-buffered:
-    # the copy of step i+1 runs on a copy stream while step i computes (the
-    # buffer it overwrites was last read by step i-1, which the loss read-back
-    # has already waited for), so the step time is max(copy, compute).
-    pinned = [t.pin_memory() for t in host] + [target_cpu.pin_memory()]
+    # Gaussian parameters and this rank's targets from pinned host memory,
+    # renders, and reads the result back (the loss, or for forward-only
+    # configs one sum per image). Inputs are double-buffered: the copy of step
+    # i+1 runs on a copy stream while step i computes (the buffer it
+    # overwrites was last read by step i-1, which the read-back has already
+    # waited for), so the step time is max(copy, compute).
+    pinned = [t.pin_memory() for t in host] + \
+        [t.pin_memory() for t in targets_cpu if t is not None]
     h2d = sum(t.numel() * t.element_size() for t in pinned)
+    d2h = 4 if backward else 4 * len(cameras)
     copy_stream = torch.cuda.Stream(device)
     slots = []
     for _ in range(2):
-        buffers = [torch.empty_like(p) for p in params] + [torch.empty_like(target)]
+        buffers = [torch.empty_like(t, device=device) for t in pinned]
         slot_splats = GaussianSplat.from_tensors(*buffers[:5])
         slot_trainable = [slot_splats.mean, slot_splats.rotation, slot_splats.scale,
                           slot_splats.opacity, slot_splats.color]
         for p in slot_trainable:
-            p.requires_grad_(True)
+            p.requires_grad_(backward)
         slots.append((buffers, slot_splats, slot_trainable, torch.cuda.Event()))
 
     def prefetch(i):
@@ -512,21 +616,23 @@ def main():
                 prefetch(i + 1)
             buffers, slot_splats, slot_trainable, ready = slots[i % 2]
             torch.cuda.current_stream().wait_event(ready)
-            loss = vp_train_step(slot_splats, [camera], [buffers[-1]], slot_trainable,
-                                 lambda s, c: render(s)[0],
-                                 lambda image, t: (image[:crop_h, :crop_w] - t).abs().mean())
-            loss.item()
+            if backward:
+                loss = vp_train_step(slot_splats, cameras, buffers[5:], slot_trainable,
+                                     lambda s, c: render(s, c)[0], loss_fn)
+                loss.item()
+            else:
+                images = forward_step(slot_splats)
+                torch.stack([image.sum() for image in images]).cpu()
 
     e2e_run(max(1, args.warmup // 2))
     e2e_steps = max(3, args.steps // 2)
     e2e_ms = timed(lambda: e2e_run(e2e_steps), 1) / e2e_steps
 
     hbm_peak, peak_kind = load_peaks()
-    launches_per_step = 15  # 1 projection, 6 count-phase, 5 sort-phase, 2 composite, 1 proj bwd
-    n = scene.num_points
+    n, k = scene.num_points, host[4].shape[1]
     traffic = {}
     profile_json = os.path.join(ROOT, "profiles", "traffic.json")
-    if os.path.exists(profile_json):
+    if args.config == 2 and args.points is None and os.path.exists(profile_json):
         with open(profile_json) as f:
             traffic = json.load(f)
 
@@ -546,41 +652,49 @@ def main():
                         "MEASURED_PEAKS.json); work = reference-evaluated pairs x ops/pair"}
 
     rooflines = {
-        "project_fwd": hbm("project_fwd", n * PROJECT_FWD_BYTES),
-        "project_bwd": hbm("project_bwd", n * PROJECT_BWD_BYTES),
+        "project_fwd": hbm("project_fwd", n * project_fwd_bytes(k)),
         "composite_fwd": fp32("composite_fwd", pairs * COMPOSITE_FWD_FLOPS),
-        "composite_bwd": fp32("composite_bwd", pairs * COMPOSITE_BWD_FLOPS),
     }
+    if backward:
+        rooflines["project_bwd"] = hbm("project_bwd", n * project_bwd_bytes(k))
+        rooflines["composite_bwd"] = fp32("composite_bwd", pairs * COMPOSITE_BWD_FLOPS)
     dominant = max(kernel_ms, key=kernel_ms.get)
     main_roof = dict(rooflines[dominant], kernel=dominant)
+    per_view = len(cameras)
 
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms, "fwd_ms": fwd_ms, "fwd_bwd_ms": ms,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic (seeded config-2 scene, random L1 target)",
-        "config": {"workload": WORKLOAD, "gaussians": n, "image": [1920, 1080],
-                   "tile_size": settings.tile_size, "views_per_rank_per_step": 1,
-                   "parallelism": f"view-parallel x{world}, NCCL all-reduce of gradients"
+        "warmup": args.warmup, "ms_per_step": ms, "fwd_ms": fwd_ms / per_view,
+        "fwd_bwd_ms": ms / per_view if backward else None,
+        "higher_is_better": True,
+        "scaling": "weak" if workload["views"] is None else "strong",
+        "vs_baseline": None, "dtype": "f32",
+        "data": f"synthetic (seeded config-{args.config} scene"
+                + (", random L1 target)" if backward else ")"),
+        "config": {"workload": workload["name"], "gaussians": n,
+                   "image": [crop_w, crop_h], "tile_size": settings.tile_size,
+                   "views_per_step": views_per_step, "views_per_rank_per_step": per_view,
+                   "parallelism": (f"view-parallel x{world}" + (
+                       ", NCCL all-reduce of gradients" if backward else ", no collective"))
                    if world > 1 else "single GPU",
-                   "l2": "inputs larger than L2 (236 MB of parameters read per step)"},
+                   "l2": "inputs larger than L2 (Gaussian parameters read every view)"
+                   if n * project_fwd_bytes(k) > 126e6 else
+                   "inputs smaller than L2; each view re-reads them"},
         "stage_ms": stage_ms, "kernel_ms": kernel_ms, "dominant_kernel": dominant,
-        "view": {"visible": visible, "intersections": intersections,
+        "view": {"visible": visible, "intersections": intersections, "tiles": num_tiles,
                  "active_pairs": n_contrib, "reference_pairs": pairs},
         "roofline": main_roof, "rooflines": rooflines,
-        "e2e": {"value": world * 1000.0 / e2e_ms, "unit": UNIT, "ms_per_step": e2e_ms,
-                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4},
-        "gpu_launches": launches_per_step * args.steps,
+        "e2e": {"value": views_per_step * 1000.0 / e2e_ms, "unit": UNIT, "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": launches_per_view(num_tiles, backward) * per_view * args.steps,
         "clocks": clock,
     }
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         sys.path.insert(0, os.path.join(ROOT, "oracle"))
         import oracle as O
 
-        cpu_scene = scenes.config2(num_points=args.points)
-        view = cpu_view_setup(O, cpu_scene)
-        seconds, sample = cpu_view_seconds(O, view, chunk=cpu_scene.num_points, tiles=256,
-                                           seed=0)
+        view = cpu_view_setup(O, load_scene(args.config, args.points), backward)
+        seconds, sample = cpu_view_seconds(O, view, chunk=scene.num_points, tiles=256, seed=0)
         line["cpu_baseline"] = {"value": 1.0 / seconds, "unit": UNIT,
                                 "cores": os.cpu_count(), "kind": "port", "sample": sample}
     if rank == 0:

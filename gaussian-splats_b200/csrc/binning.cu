@@ -74,6 +74,19 @@ struct DepthSource {  // key = depth bits of projected_mean[i, 2], value = i
     return __float_as_uint(__ldg(projected_mean + 3 * i + 2));
   }
   __device__ __forceinline__ uint32_t value(int64_t i) const { return static_cast<uint32_t>(i); }
+  // Keys of elements [first, first + R) into keys[]; returns the valid mask.
+  template <int R>
+  __device__ __forceinline__ uint32_t load_run(int64_t first, int64_t n, uint32_t (&keys)[R]) const {
+    uint32_t mask = 0;
+#pragma unroll
+    for (int j = 0; j < R; ++j) {
+      const int64_t i = first + j;
+      const bool ok = i < n && valid(i);
+      keys[j] = ok ? key(i) : 0u;
+      mask |= ok ? (1u << j) : 0u;
+    }
+    return mask;
+  }
 };
 
 struct ArraySource {
@@ -82,6 +95,31 @@ struct ArraySource {
   __device__ __forceinline__ bool valid(int64_t) const { return true; }
   __device__ __forceinline__ uint32_t key(int64_t i) const { return keys[i]; }
   __device__ __forceinline__ uint32_t value(int64_t i) const { return values[i]; }
+  // Keys of elements [first, first + R) (first a multiple of R, R a multiple
+  // of 4, the array 16-byte aligned: whole runs load as 16-byte vectors).
+  template <int R>
+  __device__ __forceinline__ uint32_t load_run(int64_t first, int64_t n, uint32_t (&keys)[R]) const {
+    if (first + R <= n) {
+#pragma unroll
+      for (int j = 0; j < R; j += 4) {
+        const uint4 v = *reinterpret_cast<const uint4*>(keys_ptr() + first + j);
+        keys[j] = v.x;
+        keys[j + 1] = v.y;
+        keys[j + 2] = v.z;
+        keys[j + 3] = v.w;
+      }
+      return R == 32 ? 0xffffffffu : (1u << R) - 1u;
+    }
+    uint32_t mask = 0;
+#pragma unroll
+    for (int j = 0; j < R; ++j) {
+      const bool ok = first + j < n;
+      keys[j] = ok ? keys_ptr()[first + j] : 0u;
+      mask |= ok ? (1u << j) : 0u;
+    }
+    return mask;
+  }
+  __device__ __forceinline__ const uint32_t* keys_ptr() const { return keys; }
 };
 
 // Element count of a pass: a host value, or a device word written earlier on
@@ -93,8 +131,12 @@ struct Count {
 };
 
 // Per-digit histograms of every pass at once (the global digit offsets each
-// pass needs), plus the number of valid elements.
-template <class Source>
+// pass needs), plus the number of valid elements. Each thread walks
+// kUpsweepRun consecutive elements and adds runs of equal digits with one
+// shared-memory atomic: neighbouring keys share their high digits (a
+// Gaussian's tiles lie in few tile rows; depths share their exponent), which
+// would otherwise put whole warps on one counter.
+template <class Source, int kUpsweepRun>
 __global__ void __launch_bounds__(kThreads) upsweep_kernel(Source src, int64_t n, int num_passes,
                                                           int shift0, uint32_t* __restrict__ hist,
                                                           uint32_t* __restrict__ valid_total) {
@@ -102,12 +144,29 @@ __global__ void __launch_bounds__(kThreads) upsweep_kernel(Source src, int64_t n
   for (int i = threadIdx.x; i < 4 * kRadix; i += kThreads) (&s_hist[0][0])[i] = 0;
   __syncthreads();
   uint32_t valid_here = 0;
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; i < n;
-       i += static_cast<int64_t>(gridDim.x) * kThreads) {
-    if (!src.valid(i)) continue;
-    ++valid_here;
-    const uint32_t key = src.key(i);
-    for (int p = 0; p < num_passes; ++p) atomicAdd(&s_hist[p][(key >> (shift0 + 8 * p)) & 0xFF], 1u);
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kThreads * kUpsweepRun;
+  for (int64_t first = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) * kUpsweepRun;
+       first < n; first += stride) {
+    uint32_t keys[kUpsweepRun];
+    uint32_t valid = src.load_run(first, n, keys);  // bit j: element first + j counts
+    valid_here += __popc(valid);
+    for (int p = 0; p < num_passes; ++p) {
+      const int shift = shift0 + 8 * p;
+      int current = -1;
+      uint32_t run = 0;
+#pragma unroll
+      for (int j = 0; j < kUpsweepRun; ++j) {
+        if (!((valid >> j) & 1u)) continue;
+        const int digit = static_cast<int>((keys[j] >> shift) & 0xFFu);
+        if (digit != current) {
+          if (run) atomicAdd(&s_hist[p][current], run);
+          current = digit;
+          run = 0;
+        }
+        ++run;
+      }
+      if (run) atomicAdd(&s_hist[p][current], run);
+    }
   }
   if (valid_total) {
     for (int o = 16; o > 0; o >>= 1) valid_here += __shfl_xor_sync(0xffffffffu, valid_here, o);
@@ -423,20 +482,39 @@ __global__ void __launch_bounds__(kThreads) emit_kernel(
 }
 
 // ranges[t] = [first index with key >= t, first index with key >= t + 1)
-// over the sorted tile keys. Thread i (0 <= i <= total) looks at the step
+// over the sorted tile keys. Each index i (0 <= i <= total) looks at the step
 // between key[i-1] and key[i] (key[-1] = -1, key[total] = num_tiles): every
 // tile t in (key[i-1], key[i]] starts at i and every tile t in
 // [key[i-1], key[i]) ends at i. Each start and end is written exactly once,
-// and empty tiles get start == end.
+// and empty tiles get start == end. A thread takes kRangeItems consecutive
+// indices (two 16-byte loads when they are all inside the array).
+constexpr int kRangeItems = 8;
 __global__ void ranges_kernel(const uint32_t* __restrict__ sorted_keys, int64_t total,
                               int64_t num_tiles, int64_t* __restrict__ ranges) {
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (i > total) return;
-  const int64_t prev = i > 0 ? static_cast<int64_t>(sorted_keys[i - 1]) : -1;
-  const int64_t cur = i < total ? static_cast<int64_t>(sorted_keys[i]) : num_tiles;
-  if (cur == prev) return;
-  for (int64_t t = prev + 1; t <= cur && t < num_tiles; ++t) ranges[2 * t] = i;
-  for (int64_t t = prev < 0 ? 0 : prev; t < cur; ++t) ranges[2 * t + 1] = i;
+  const int64_t i0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * kRangeItems;
+  if (i0 > total) return;
+  uint32_t k[kRangeItems];
+  if (i0 + kRangeItems <= total) {
+    const uint4 a = *reinterpret_cast<const uint4*>(sorted_keys + i0);
+    const uint4 b = *reinterpret_cast<const uint4*>(sorted_keys + i0 + 4);
+    k[0] = a.x; k[1] = a.y; k[2] = a.z; k[3] = a.w;
+    k[4] = b.x; k[5] = b.y; k[6] = b.z; k[7] = b.w;
+  } else {
+#pragma unroll
+    for (int j = 0; j < kRangeItems; ++j) k[j] = i0 + j < total ? sorted_keys[i0 + j] : 0u;
+  }
+  int64_t prev = i0 > 0 ? static_cast<int64_t>(sorted_keys[i0 - 1]) : -1;
+#pragma unroll
+  for (int j = 0; j < kRangeItems; ++j) {
+    const int64_t i = i0 + j;
+    if (i > total) break;
+    const int64_t cur = i < total ? static_cast<int64_t>(k[j]) : num_tiles;
+    if (cur != prev) {
+      for (int64_t t = prev + 1; t <= cur && t < num_tiles; ++t) ranges[2 * t] = i;
+      for (int64_t t = prev < 0 ? 0 : prev; t < cur; ++t) ranges[2 * t + 1] = i;
+    }
+    prev = cur;
+  }
 }
 
 // ---------------------------------------------------------------- workspaces
@@ -530,7 +608,7 @@ int32_t launch_bin_count(int64_t n, const float* projected_mean, const int32_t* 
   GS_CUDA_TRY(cudaMemsetAsync(workspace, 0, L.zero_bytes, stream));
   if (n > 0) {
     const int64_t blocks = (n + kTile - 1) / kTile;
-    upsweep_kernel<<<upsweep_blocks(n), kThreads, 0, stream>>>(
+    upsweep_kernel<DepthSource, 4><<<upsweep_blocks(n), kThreads, 0, stream>>>(
         DepthSource{projected_mean, counts}, n, 4, 0, &h->hist[0][0], &h->num_valid);
     GS_TRY(check_launch());
     uint32_t* depth_status = at<uint32_t>(workspace, L.depth_status);
@@ -594,7 +672,7 @@ int32_t launch_bin_sort(int64_t n, int64_t total, const int32_t* bounds, const i
         static_cast<int>(tiles_w), kA, passes == 0 ? out_ids : vA);
     GS_TRY(check_launch());
     if (passes > 0) {
-      upsweep_kernel<<<upsweep_blocks(total), kThreads, 0, stream>>>(
+      upsweep_kernel<ArraySource, 16><<<upsweep_blocks(total), kThreads, 0, stream>>>(
           ArraySource{kA, vA}, total, passes, 0, &h->hist[0][0], nullptr);
       GS_TRY(check_launch());
       const int64_t blocks = (total + kTile - 1) / kTile;
@@ -615,8 +693,8 @@ int32_t launch_bin_sort(int64_t n, int64_t total, const int32_t* bounds, const i
     }
   }
   if (num_tiles > 0) {
-    ranges_kernel<<<ceil_div(total + 1, 256), 256, 0, stream>>>(sorted_keys, total, num_tiles,
-                                                               ranges);
+    ranges_kernel<<<ceil_div(ceil_div(total + 1, kRangeItems), 256), 256, 0, stream>>>(
+        sorted_keys, total, num_tiles, ranges);
     GS_TRY(check_launch());
   }
   return GS_OK;

@@ -34,3 +34,39 @@ def test_reference_arm_prints_one_contract_line():
     assert d["cpu_baseline"]["kind"] == "port" and d["cpu_baseline"]["value"] == d["value"]
     assert d["e2e"] == {"value": d["value"], "unit": "views/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}
+
+
+def test_launch_count_per_view():
+    # 1080p at 16x16: 8160 tiles, 13 bits, two tile-sort passes.
+    assert bench.sort_passes(8160) == 2 and bench.sort_passes(256) == 1
+    assert bench.sort_passes(1) == 0
+    assert bench.launches_per_view(8160, backward=True) == 15
+    assert bench.launches_per_view(8160, backward=False) == 13
+    assert bench.launches_per_view(256, backward=True) == 14
+    assert bench.launches_per_view(1, backward=False) == 10
+
+
+def test_views_split_over_ranks():
+    from gaussian_splats_b200 import scenes
+
+    multi = scenes.config4(num_points=64)
+    for world in (1, 2, 4, 8):
+        got = [bench.views_for_rank(multi, 4, r, world) for r in range(world)]
+        assert sum(len(v) for v in got) == 64
+        assert all(target is None for v in got for _, target in v)  # forward only
+    single = scenes.config2(num_points=64)
+    first = bench.views_for_rank(single, 2, 0, 2)
+    second = bench.views_for_rank(single, 2, 1, 2)
+    assert first[0][0] is single.cameras[0] and first[0][1] is single.targets[0]
+    assert len(second) == 1 and second[0][1].shape == (1080, 1920, 3)
+    assert not (second[0][0].position == first[0][0].position).all()
+
+
+def test_reference_arm_forward_only_config():
+    out = subprocess.run(
+        [sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--config", "4",
+         "--steps", "1", "--warmup", "0", "--points", "20000"],
+        capture_output=True, text=True, timeout=600, cwd=ROOT, check=True).stdout
+    d = json.loads([line for line in out.splitlines() if line.startswith("{")][0])
+    assert d["value"] > 0 and d["config"]["workload"].startswith("config4")
+    assert "projection backward" not in d["cpu_baseline"]["sample"]
