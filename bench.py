@@ -447,6 +447,71 @@ def cpu_view_seconds(O, view, chunk, tiles, seed):
     return seconds, sample
 
 
+# Algorithmic bytes per Gaussian of one fused optimizer step with K SH
+# coefficients: parameter, gradient and both Adam moments read (4 x (11 + 3K)
+# floats), the position noise's normal samples read (3 floats), parameter and
+# moments written (3 x (11 + 3K) floats). K = 16: 1,664 B.
+def optimizer_bytes(k):
+    return 4 * (7 * (11 + 3 * k) + 3)
+
+
+def optimizer_timings(params, grads, device, repeats=5):
+    """Milliseconds of one training-loop optimizer step on these parameters
+    and gradients: the fused step (FusedAdam with position noise) and, for
+    comparison, what the reference runs -- torch.optim.Adam (eps 1e-15) then
+    noise_splats' tensor ops (training/utils.py:50-62) -- each after a 1 GiB
+    L2 flush, timed with CUDA events."""
+    import torch.nn.functional as F
+
+    from gaussian_splats_b200.optim import GROUP_NAMES, FusedAdam
+    from gaussian_splats_b200.utils import quaternion_to_rotation_matrix
+
+    lrs = (1.6e-4, 1e-3, 5e-3, 5e-2, 2.5e-3)  # training/train.py:78-83
+
+    def copies():
+        tensors = [p.detach().clone().requires_grad_() for p in params]
+        for t, g in zip(tensors, grads):
+            t.grad = g.clone()
+        return tensors
+
+    def noise_splats(mean, rotation, scale, opacity, noise_lr, position_lr):
+        rot = quaternion_to_rotation_matrix(F.normalize(rotation, dim=-1))
+        factor = rot * scale.exp()[:, None, :]
+        covariance = factor @ factor.transpose(-1, -2)
+        gate = torch.sigmoid(100 * (1 - opacity.sigmoid() - 0.995))
+        noise = torch.randn_like(mean) * gate * noise_lr * position_lr
+        mean.add_((covariance @ noise[..., None]).squeeze(-1))
+
+    ours = copies()
+    fused = FusedAdam([{"params": [t], "name": n, "lr": lr}
+                       for t, n, lr in zip(ours, GROUP_NAMES, lrs)], eps=1e-15)
+    theirs = copies()
+    plain = torch.optim.Adam([{"params": [t], "lr": lr} for t, lr in zip(theirs, lrs)],
+                             eps=1e-15)
+
+    def reference_step():
+        plain.step()
+        with torch.no_grad():
+            noise_splats(theirs[0], theirs[1], theirs[2], theirs[3], 5e5, lrs[0])
+
+    flush = torch.empty(1 << 28, dtype=torch.float32, device=device)
+    result = {}
+    for name, fn in (("fused", lambda: fused.step(noise=(5e5, lrs[0]))),
+                     ("torch", reference_step)):
+        fn()  # first step allocates the moments
+        events = []
+        for _ in range(repeats):
+            flush.zero_()
+            before, after = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            before.record()
+            fn()
+            after.record()
+            events.append((before, after))
+        torch.cuda.synchronize()
+        result[name] = sum(b.elapsed_time(a) for b, a in events) / repeats
+    return result
+
+
 def sort_passes(num_tiles):
     """8-bit radix passes of the tile sort for `num_tiles` tiles."""
     bits = max(0, (max(1, num_tiles) - 1).bit_length())
@@ -579,6 +644,10 @@ def main():
             grad_image[:crop_h, :crop_w] = torch.sign(diff) / diff.numel()
     kernel_ms = kernel_durations(out, params, camera0, grad_image, settings, device)
     fp32_peak = fp32_peak_tflops(device)
+    optimizer_ms = None
+    if backward:
+        train_step()  # leaves this rank's summed, all-reduced gradients in .grad
+        optimizer_ms = optimizer_timings(trainable, [p.grad for p in trainable], device)
 
     # End to end through the public API with host buffers: each step copies the
     # Gaussian parameters and this rank's targets from pinned host memory,
@@ -660,6 +729,16 @@ def main():
         rooflines["composite_bwd"] = fp32("composite_bwd", pairs * COMPOSITE_BWD_FLOPS)
     dominant = max(kernel_ms, key=kernel_ms.get)
     main_roof = dict(rooflines[dominant], kernel=dominant)
+    optimizer = None
+    if optimizer_ms is not None:
+        gbs = n * optimizer_bytes(k) / (optimizer_ms["fused"] * 1e-3) / 1e9
+        optimizer = {
+            "fused_ms": optimizer_ms["fused"], "torch_adam_and_noise_ms": optimizer_ms["torch"],
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s",
+                         "frac": gbs / hbm_peak, "algorithmic_bytes": n * optimizer_bytes(k),
+                         "note": f"peak: {peak_kind} hbm_gbs (MEASURED_PEAKS.json)"},
+            "note": "one training-loop optimizer step (Adam over the five parameter groups + "
+                    "position noise), not part of the timed fwd+bwd step"}
     per_view = len(cameras)
 
     line = {
@@ -683,7 +762,7 @@ def main():
         "stage_ms": stage_ms, "kernel_ms": kernel_ms, "dominant_kernel": dominant,
         "view": {"visible": visible, "intersections": intersections, "tiles": num_tiles,
                  "active_pairs": n_contrib, "reference_pairs": pairs},
-        "roofline": main_roof, "rooflines": rooflines,
+        "roofline": main_roof, "rooflines": rooflines, "optimizer": optimizer,
         "e2e": {"value": views_per_step * 1000.0 / e2e_ms, "unit": UNIT, "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": launches_per_view(num_tiles, backward) * per_view * args.steps,

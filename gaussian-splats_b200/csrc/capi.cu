@@ -29,6 +29,9 @@ int32_t launch_composite_fwd(const float*, const float*, const float*, const flo
 int32_t launch_composite_bwd(int64_t, const float*, const float*, const float*, const float*,
                              const int32_t*, const int64_t*, const float*, const float*,
                              const int32_t*, const gs_params&, float*, cudaStream_t);
+int32_t launch_adam_step(int64_t, int32_t, const gs_splat_arrays&, const gs_splat_arrays&,
+                         const gs_splat_arrays&, const gs_splat_arrays&, const gs_adam_params&,
+                         const float*, cudaStream_t);
 
 namespace {
 thread_local int32_t g_last_cuda_error = 0;
@@ -187,6 +190,24 @@ int32_t gs_project_bwd(int64_t n, int32_t num_sh, const float* mean, const float
                                 camera_rotation, camera_translation, inverse_covariance,
                                 grad_projected, counts, *params, grad_mean, grad_rotation,
                                 grad_scale, grad_opacity, grad_color, as_cuda(stream));
+}
+
+int32_t gs_adam_step(int64_t n, int32_t num_sh, const gs_splat_arrays* params,
+                     const gs_splat_arrays* grads, const gs_splat_arrays* exp_avg,
+                     const gs_splat_arrays* exp_avg_sq, const gs_adam_params* hyper,
+                     const float* randn, gs_stream_t stream) {
+  if (!params || !grads || !exp_avg || !exp_avg_sq || !hyper) return GS_ERR_INVALID_ARGUMENT;
+  if (n < 0 || n >= gs::kMaxGaussians) return GS_ERR_INVALID_ARGUMENT;
+  if (num_sh < 1 || num_sh > 25) return GS_ERR_INVALID_ARGUMENT;
+  const gs_splat_arrays* sets[3] = {params, exp_avg, exp_avg_sq};
+  for (const gs_splat_arrays* set : sets) {
+    if (!set->mean || !set->rotation || !set->scale || !set->opacity || !set->color)
+      return GS_ERR_INVALID_ARGUMENT;
+    if (!gs::aligned(set->color, 16)) return GS_ERR_MISALIGNED;
+  }
+  if (grads->color && !gs::aligned(grads->color, 16)) return GS_ERR_MISALIGNED;
+  return gs::launch_adam_step(n, num_sh, *params, *grads, *exp_avg, *exp_avg_sq, *hyper, randn,
+                              as_cuda(stream));
 }
 
 int32_t gs_det_exp(int64_t n, const float* x, float* y, gs_stream_t stream) {

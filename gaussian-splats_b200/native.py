@@ -38,6 +38,7 @@ EXPORTED_SYMBOLS = (
     "gs_composite_fwd",
     "gs_composite_bwd",
     "gs_project_bwd",
+    "gs_adam_step",
     "gs_det_exp",
     "gs_det_log",
 )
@@ -82,6 +83,40 @@ def make_params(fx, fy, cx, cy, width, height, tile_size, opacity_threshold, nea
     )
 
 
+class SplatArrays(ctypes.Structure):
+    """``gs_splat_arrays``: device pointers of mean, rotation, scale, opacity,
+    color (NULL members allowed in a gradient set)."""
+
+    _fields_ = [(name, ctypes.c_void_p) for name in
+                ("mean", "rotation", "scale", "opacity", "color")]
+
+
+class AdamParams(ctypes.Structure):
+    """``gs_adam_params``: one Adam step's scalars (see :func:`adam_params`)."""
+
+    _fields_ = [(name, ctypes.c_float) for name in
+                ("lerp_weight", "beta2", "sq_weight", "eps")] + [
+        ("neg_step_size", ctypes.c_float * 5), ("bias2_sqrt", ctypes.c_float * 5),
+        ("noise_lr", ctypes.c_float), ("position_lr", ctypes.c_float)]
+
+
+def adam_params(steps, lrs, betas, eps, noise_lr=0.0, position_lr=0.0) -> AdamParams:
+    """Fold one Adam step for the five groups (mean, rotation, scale, opacity,
+    color) with step numbers ``steps`` (1-based) and learning rates ``lrs`` the
+    way torch.optim.Adam's foreach path folds them, in double: bias
+    corrections ``1 - beta ** step``, step size ``-(lr / bc1)``, ``sqrt(bc2)``."""
+    beta1, beta2 = betas
+    h = AdamParams()
+    h.lerp_weight, h.beta2, h.sq_weight, h.eps = 1 - beta1, beta2, 1 - beta2, eps
+    for k, (step, lr) in enumerate(zip(steps, lrs)):
+        bc1 = 1 - beta1 ** step
+        bc2 = 1 - beta2 ** step
+        h.neg_step_size[k] = (lr / bc1) * -1
+        h.bias2_sqrt[k] = bc2 ** 0.5
+    h.noise_lr, h.position_lr = noise_lr, position_lr
+    return h
+
+
 _lib = None
 
 
@@ -112,6 +147,8 @@ def lib() -> ctypes.CDLL:
         "gs_composite_fwd": ([vp] * 6 + [P] + [vp] * 3 + [vp], i32),
         "gs_composite_bwd": ([i64] + [vp] * 9 + [P, vp, vp], i32),
         "gs_project_bwd": ([i64, i32] + [vp] * 10 + [P] + [vp] * 5 + [vp], i32),
+        "gs_adam_step": ([i64, i32] + [ctypes.POINTER(SplatArrays)] * 4 +
+                         [ctypes.POINTER(AdamParams), vp, vp], i32),
         "gs_det_exp": ([i64, vp, vp, vp], i32),
         "gs_det_log": ([i64, vp, vp, vp], i32),
     }

@@ -166,6 +166,40 @@ int32_t gs_project_bwd(int64_t n, int32_t num_sh, const float *mean, const float
 int32_t gs_bin_check(const void *count_workspace, const void *sort_workspace,
                      gs_stream_t stream);
 
+/* ------------------------------------------------------------ training step */
+
+/* The five parameter arrays of a splat set (or of its gradients or Adam
+ * moments), laid out as the Gaussian tensors above. A NULL member in the
+ * gradient set skips that parameter (torch.optim.Adam skips params whose
+ * .grad is None). */
+typedef struct gs_splat_arrays {
+  float *mean, *rotation, *scale, *opacity, *color;
+} gs_splat_arrays;
+
+/* Step scalars, folded on the host in double and rounded to float the way
+ * torch.optim.Adam's foreach path folds them (t = the step number, >= 1):
+ *   lerp_weight = 1 - beta1, beta2, sq_weight = 1 - beta2, eps, and per
+ *   parameter k (mean, rotation, scale, opacity, color) with its own step t_k:
+ *   neg_step_size[k] = -(lr_k / (1 - beta1^t_k)), bias2_sqrt[k] =
+ *   sqrt(1 - beta2^t_k); noise_lr and position_lr as noise_splats takes them. */
+typedef struct gs_adam_params {
+  float lerp_weight, beta2, sq_weight, eps;
+  float neg_step_size[5];
+  float bias2_sqrt[5];
+  float noise_lr, position_lr;
+} gs_adam_params;
+
+/* One optimizer step: Adam (torch.optim.Adam as training/train.py:118,151
+ * runs it, foreach order) on every parameter with a gradient, updating
+ * `params`, `exp_avg` and `exp_avg_sq` in place; then, when `randn` [N,3] is
+ * not NULL, the position noise of noise_splats (training/utils.py:50-62)
+ * added to the updated means. Replaces optimizer.step() + noise_splats(). The
+ * colour arrays must be 16-byte aligned. */
+int32_t gs_adam_step(int64_t n, int32_t num_sh, const gs_splat_arrays *params,
+                     const gs_splat_arrays *grads, const gs_splat_arrays *exp_avg,
+                     const gs_splat_arrays *exp_avg_sq, const gs_adam_params *hyper,
+                     const float *randn, gs_stream_t stream);
+
 /* The deterministic exp / log the kernels use, applied elementwise (test hook
  * for bitwise agreement with the CPU oracle). */
 int32_t gs_det_exp(int64_t n, const float *x, float *y, gs_stream_t stream);

@@ -9,6 +9,8 @@
  *   gso_composite_bwd composite_bwd.py:47-277 (reverse compositing, per-intersection
  *                                              rows reduced per Gaussian like index_add_)
  *   gso_project_bwd   project_bwd.py:8-334    (parameter VJPs)
+ *   gso_adam_step     training/train.py:118,151 + training/utils.py:50-62
+ *                                             (torch Adam step, position noise)
  * Each function follows the reference's float32 operation order (no fused
  * multiply-adds unless written as fmaf) so that integer decisions match the
  * CUDA kernels bit for bit; exp/log come from detmath.h. Only tests, the
@@ -650,5 +652,76 @@ void gso_project_bwd(int64_t n, const float *mean, const float *rotation, const 
 }
 
 /* Deterministic exp/log exposed for the bitwise CPU/GPU agreement test. */
+/* ---------------------------------------------------------------- optimizer step */
+
+/* torch.optim.Adam's foreach step (eps 1e-15 and one group per parameter as
+ * training/train.py:111-118 builds them) followed by noise_splats
+ * (training/utils.py:50-62) on the updated parameters. Scalars arrive folded
+ * as torch folds them (double, then float). Per element, in torch's order:
+ *   m = m + w1 (g - m); v = v b2; v = v + w2 (g g);
+ *   p = p + neg_step (m / (sqrt(v) / bias2_sqrt + eps)). */
+typedef struct gso_adam_params {
+    float lerp_weight, beta2, sq_weight, eps;
+    float neg_step_size[5];
+    float bias2_sqrt[5];
+    float noise_lr, position_lr;
+} gso_adam_params;
+
+static float adam_one(float p, float g, float *m, float *v, float neg_step, float bias2_sqrt,
+                      const gso_adam_params *h) {
+    *m = *m + h->lerp_weight * (g - *m);
+    *v = *v * h->beta2;
+    *v = *v + h->sq_weight * (g * g);
+    float d = sqrtf(*v) / bias2_sqrt + h->eps;
+    return p + neg_step * (*m / d);
+}
+
+static float sigmoidf_det(float x) { return 1.0f / (1.0f + gso_exp(-x)); }
+
+/* params/grads/m/v: pointers to mean, rotation, scale, opacity, color (a NULL
+ * gradient skips that parameter); randn [N,3] or NULL for no noise. */
+void gso_adam_step(int64_t n, int32_t num_sh, float *const *params, const float *const *grads,
+                   float *const *m, float *const *v, const gso_adam_params *h,
+                   const float *randn) {
+    static const int widths[4] = {3, 4, 3, 1};
+    for (int k = 0; k < 4; ++k) {
+        if (!grads[k]) continue;
+        for (int64_t e = 0; e < n * widths[k]; ++e)
+            params[k][e] = adam_one(params[k][e], grads[k][e], &m[k][e], &v[k][e],
+                                    h->neg_step_size[k], h->bias2_sqrt[k], h);
+    }
+    if (grads[4]) {
+        for (int64_t e = 0; e < n * 3 * (int64_t)num_sh; ++e)
+            params[4][e] = adam_one(params[4][e], grads[4][e], &m[4][e], &v[4][e],
+                                    h->neg_step_size[4], h->bias2_sqrt[4], h);
+    }
+    if (!randn) return;
+    for (int64_t i = 0; i < n; ++i) {
+        const float *r4 = params[1] + 4 * i, *sc = params[2] + 3 * i;
+        float norm = sqrtf(((r4[0] * r4[0] + r4[1] * r4[1]) + r4[2] * r4[2]) + r4[3] * r4[3]);
+        float inv = fmaxf(norm, 1e-12f);
+        float w = r4[0] / inv, x = r4[1] / inv, y = r4[2] / inv, z = r4[3] / inv;
+        float r[3][3] = {
+            {1.0f - 2.0f * (y * y + z * z), 2.0f * (x * y - w * z), 2.0f * (x * z + w * y)},
+            {2.0f * (x * y + w * z), 1.0f - 2.0f * (x * x + z * z), 2.0f * (y * z - w * x)},
+            {2.0f * (x * z - w * y), 2.0f * (y * z + w * x), 1.0f - 2.0f * (x * x + y * y)}};
+        float s[3] = {gso_exp(sc[0]), gso_exp(sc[1]), gso_exp(sc[2])};
+        float f[3][3];
+        for (int a = 0; a < 3; ++a)
+            for (int b = 0; b < 3; ++b) f[a][b] = r[a][b] * s[b];
+        float gate = sigmoidf_det(100.0f * (1.0f - sigmoidf_det(params[3][i]) - 0.995f));
+        float nz[3];
+        for (int k = 0; k < 3; ++k) nz[k] = ((randn[3 * i + k] * gate) * h->noise_lr) * h->position_lr;
+        for (int a = 0; a < 3; ++a) {
+            float shift = 0.0f;
+            for (int b = 0; b < 3; ++b) {
+                float cov = (f[a][0] * f[b][0] + f[a][1] * f[b][1]) + f[a][2] * f[b][2];
+                shift = b == 0 ? cov * nz[0] : shift + cov * nz[b];
+            }
+            params[0][3 * i + a] = params[0][3 * i + a] + shift;
+        }
+    }
+}
+
 void gso_exp_array(int64_t n, const float *x, float *y) { for (int64_t i = 0; i < n; ++i) y[i] = gso_exp(x[i]); }
 void gso_log_array(int64_t n, const float *x, float *y) { for (int64_t i = 0; i < n; ++i) y[i] = gso_log(x[i]); }

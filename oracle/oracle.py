@@ -72,9 +72,20 @@ def lib() -> ctypes.CDLL:
         _lib.gso_project_bwd.argtypes = [i64, _f32p, _f32p, _f32p, _f32p, _f32p, i32, _f32p, _f32p,
                                          _f32p, _f32p, _i32p, P, _f32p, _f32p, _f32p, _f32p,
                                          _f32p]
+        ptr5 = ctypes.c_void_p * 5
+        _lib.gso_adam_step.argtypes = [i64, i32, ptr5, ptr5, ptr5, ptr5,
+                                       ctypes.POINTER(AdamParams), ctypes.c_void_p]
         _lib.gso_exp_array.argtypes = [i64, _f32p, _f32p]
         _lib.gso_log_array.argtypes = [i64, _f32p, _f32p]
     return _lib
+
+
+class AdamParams(ctypes.Structure):
+    """gso_adam_params: torch Adam's step scalars, folded as torch folds them."""
+    _fields_ = [(name, ctypes.c_float) for name in
+                ("lerp_weight", "beta2", "sq_weight", "eps")] + \
+               [("neg_step_size", ctypes.c_float * 5), ("bias2_sqrt", ctypes.c_float * 5),
+                ("noise_lr", ctypes.c_float), ("position_lr", ctypes.c_float)]
 
 
 @dataclass
@@ -276,3 +287,45 @@ def scene_inputs(scene, view: int = 0) -> tuple[dict, Settings]:
                         opacity_threshold=st.opacity_threshold, near=st.near, far=st.far,
                         rendering_mode=st.rendering_mode, confidence=st.confidence)
     return inputs, settings
+
+
+ADAM_NAMES = ("mean", "rotation", "scale", "opacity", "color")
+
+
+def adam_scalars(step: int, lrs, betas=(0.9, 0.999), eps=1e-15, noise_lr=0.0,
+                 position_lr=0.0) -> AdamParams:
+    """Scalars of Adam step ``step`` (1-based; an int for all five groups or
+    one per group) folded in double like torch.optim.Adam's foreach path
+    (torch/optim/adam.py: bias corrections 1 - beta^step, step size
+    -(lr / bc1), sqrt(bc2))."""
+    beta1, beta2 = betas
+    steps = [step] * 5 if isinstance(step, int) else list(step)
+    h = AdamParams()
+    h.lerp_weight, h.beta2, h.sq_weight, h.eps = 1 - beta1, beta2, 1 - beta2, eps
+    for k, (t, lr) in enumerate(zip(steps, lrs)):
+        bc1 = 1 - beta1 ** t
+        bc2 = 1 - beta2 ** t
+        h.neg_step_size[k] = (lr / bc1) * -1
+        h.bias2_sqrt[k] = bc2 ** 0.5
+    h.noise_lr, h.position_lr = noise_lr, position_lr
+    return h
+
+
+def adam_step(params: dict, grads: dict, exp_avg: dict, exp_avg_sq: dict, hyper: AdamParams,
+              randn=None) -> dict:
+    """One Adam step (+ position noise when ``randn`` [N,3] is given) on copies
+    of the float32 arrays; returns {"params", "exp_avg", "exp_avg_sq"} keyed by
+    ADAM_NAMES. A missing gradient skips that parameter."""
+    out = {key: {k: np.array(src[k], dtype=np.float32, copy=True) for k in ADAM_NAMES}
+           for key, src in (("params", params), ("exp_avg", exp_avg),
+                            ("exp_avg_sq", exp_avg_sq))}
+    g = {k: (_c(grads[k]) if grads.get(k) is not None else None) for k in ADAM_NAMES}
+    ptr5 = ctypes.c_void_p * 5
+    addr = lambda d: ptr5(*(None if d[k] is None else d[k].ctypes.data for k in ADAM_NAMES))  # noqa: E731
+    n = out["params"]["mean"].shape[0]
+    num_sh = out["params"]["color"].shape[1]
+    r = None if randn is None else _c(randn)
+    lib().gso_adam_step(n, num_sh, addr(out["params"]), addr(g), addr(out["exp_avg"]),
+                        addr(out["exp_avg_sq"]), ctypes.byref(hyper),
+                        None if r is None else r.ctypes.data)
+    return out

@@ -24,6 +24,12 @@ Scenes:
 * ``config1``: the full config-1 forward (16,384 Gaussians, 256x256).
 * ``intersections``: the reference's random-bounds emit/sort case
   (kernels/rasterize/tests/test_intersections.py:8-18).
+* ``adam_noise``: the training loop's optimizer step (training/train.py:
+  111-118,151: torch.optim.Adam, one group per splat tensor, eps 1e-15, the
+  default learning rates) for three steps of random gradients on a
+  GaussianSplat of 257 Gaussians, then the reference's own noise_splats
+  (training/utils.py:50-62) with a recorded seed; the normal samples it draws
+  are stored too.
 """
 
 from __future__ import annotations
@@ -201,7 +207,70 @@ def run_intersections() -> dict:
     )
 
 
-CASES = ("intersections", "fixture_degenerate", "fixture_sh1_t8", "fixture_sh0_t8",
+def run_adam_noise() -> dict:
+    """torch.optim.Adam as the reference's training loop builds it, then its
+    noise_splats, on the reference's GaussianSplat."""
+    import types
+
+    import gaussian_splats
+    from gaussian_splats.splats.splats import GaussianSplat
+
+    # training/utils.py imports torchmetrics (for its SSIM, unused here) and the
+    # package __init__ pulls in the whole training script; neither is needed
+    # for noise_splats. Stub the one and skip the other.
+    if "torchmetrics" not in sys.modules:
+        image = types.ModuleType("torchmetrics.functional.image")
+        image.structural_similarity_index_measure = None
+        functional = types.ModuleType("torchmetrics.functional")
+        functional.image = image
+        root = types.ModuleType("torchmetrics")
+        root.functional = functional
+        sys.modules.update({"torchmetrics": root, "torchmetrics.functional": functional,
+                            "torchmetrics.functional.image": image})
+    if "gaussian_splats.training" not in sys.modules:
+        package = types.ModuleType("gaussian_splats.training")
+        package.__path__ = [os.path.join(os.path.dirname(gaussian_splats.__file__), "training")]
+        sys.modules["gaussian_splats.training"] = package
+    from gaussian_splats.training.utils import noise_splats
+
+    n, lrs = 257, (1.6e-4 * 3.3, 1e-3, 5e-3, 5e-2, 2.5e-3)  # train.py:78-83 (mean lr scaled)
+    noise_lr, position_lr = 5e5, 1.6e-4 * 3.3
+    g = torch.Generator().manual_seed(11)
+    splats = GaussianSplat(n, sh_degree=3)
+    with torch.no_grad():
+        splats.mean.copy_(torch.randn(n, 3, generator=g))
+        splats.rotation.copy_(torch.randn(n, 4, generator=g))
+        splats.scale.copy_(torch.randn(n, 3, generator=g) * 0.5 - 4.0)
+        splats.opacity.copy_(torch.randn(n, 1, generator=g) * 3.0 - 4.0)
+        splats.color.copy_(torch.randn(n, 16, 3, generator=g) * 0.3)
+    params = [splats.mean, splats.rotation, splats.scale, splats.opacity, splats.color]
+    record = {f"in_{name}": p.detach().numpy().copy() for name, p in zip(PARAM_NAMES, params)}
+    groups = [{"params": [p], "name": name, "lr": lr}
+              for p, name, lr in zip(params, PARAM_NAMES, lrs)]
+    optimizer = torch.optim.Adam(groups, eps=1e-15)
+    for step in range(3):
+        for name, p in zip(PARAM_NAMES, params):
+            grad = torch.randn(p.shape, generator=g) * 10.0 ** -(1 + step)
+            record[f"in_grad{step}_{name}"] = grad.numpy().copy()
+            p.grad = grad
+        optimizer.step()
+        optimizer.zero_grad()
+    for name, p in zip(PARAM_NAMES, params):
+        record[f"adam_{name}"] = p.detach().numpy().copy()
+        state = optimizer.state[p]
+        record[f"exp_avg_{name}"] = state["exp_avg"].numpy().copy()
+        record[f"exp_avg_sq_{name}"] = state["exp_avg_sq"].numpy().copy()
+    torch.manual_seed(1234)
+    record["in_randn"] = torch.randn_like(splats.mean).numpy().copy()
+    torch.manual_seed(1234)
+    noise_splats(splats, noise_lr, position_lr)
+    record["noised_mean"] = splats.mean.detach().numpy().copy()
+    record["in_lrs"] = np.array(lrs)
+    record["in_noise"] = np.array([noise_lr, position_lr])
+    return record
+
+
+CASES = ("adam_noise", "intersections", "fixture_degenerate", "fixture_sh1_t8", "fixture_sh0_t8",
          "fixture_sh4_t8", "fixture_sh2_t8", "fixture_ellipsoid", "fixture_sh1_t4",
          "fixture_sh3_t16", "mini5", "mini2", "config1")
 
@@ -217,7 +286,12 @@ def main() -> None:
     torch.set_num_threads(os.cpu_count() or 1)
     for name in args.cases:
         t0 = time.time()
-        record = run_intersections() if name == "intersections" else run_case(name)
+        if name == "intersections":
+            record = run_intersections()
+        elif name == "adam_noise":
+            record = run_adam_noise()
+        else:
+            record = run_case(name)
         np.savez_compressed(HERE / f"{name}.npz", **record)
         print(f"{name}: {time.time() - t0:.1f}s", flush=True)
 
