@@ -164,7 +164,6 @@ int32_t gs_composite_bwd(int64_t n, const float* projected_mean, const float* in
                          float* grad_projected, gs_stream_t stream) {
   GS_TRY(gs::check_params(params));
   if (n < 0) return GS_ERR_INVALID_ARGUMENT;
-  if (!params->gaussian_mode) return GS_ERR_UNSUPPORTED;  // interface.py:184-186
   if (!gs::aligned(inverse_covariance, 16)) return GS_ERR_MISALIGNED;
   return gs::launch_composite_bwd(n, projected_mean, inverse_covariance, projected_color,
                                   projected_opacity, gaussian_ids, ranges, grad_image,

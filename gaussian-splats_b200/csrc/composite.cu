@@ -328,7 +328,7 @@ __device__ __forceinline__ void warp_reduce_scatter9(const float (&v)[9], int la
   for (int o = 16; o > 0; o >>= 1) last += __shfl_xor_sync(0xffffffffu, last, o);
 }
 
-template <int TS, int PPT>
+template <int TS, int PPT, bool kGaussian>
 __global__ void __launch_bounds__(TileShape<TS, PPT>::kThreads,
                                   min_blocks_for_32_warps(TileShape<TS, PPT>::kThreads))
     composite_bwd_kernel(
@@ -410,7 +410,12 @@ __global__ void __launch_bounds__(TileShape<TS, PPT>::kThreads,
         const float dy = fpy[q] - a.y;
         const float d2 = fmaf(adx, dx, fmaf(bdx, dy, (yy * dy) * dy));
         if (!(d2 <= b.z)) continue;
-        const float prob = d2 >= 0.0f ? det_exp_nonpositive(-0.5f * d2) : det_exp(-0.5f * d2);
+        // Ellipsoid mode: the falloff is the indicator of d2 <= cutoff (the
+        // test above), whose derivative is zero, so only colour and opacity
+        // get gradients.
+        float prob = 1.0f;
+        if constexpr (kGaussian)
+          prob = d2 >= 0.0f ? det_exp_nonpositive(-0.5f * d2) : det_exp(-0.5f * d2);
         const float alpha_raw = o * prob;
         const float alpha = fminf(alpha_raw, kAlphaMax);
         if (!(alpha >= kAlphaMin)) continue;
@@ -426,12 +431,14 @@ __global__ void __launch_bounds__(TileShape<TS, PPT>::kThreads,
         grad_alpha = alpha_raw < kAlphaMax ? grad_alpha : 0.0f;
         const float probability_grad = grad_alpha * o;
         const float grad_color = forward * alpha;
-        const float grad_distance = -0.5f * prob * probability_grad;
-        v[0] += -2.0f * grad_distance * (xx * dx + xy * dy);
-        v[1] += -2.0f * grad_distance * (xy * dx + yy * dy);
-        v[2] += grad_distance * dx * dx;
-        v[3] += grad_distance * dx * dy;
-        v[4] += grad_distance * dy * dy;
+        if constexpr (kGaussian) {
+          const float grad_distance = -0.5f * prob * probability_grad;
+          v[0] += -2.0f * grad_distance * (xx * dx + xy * dy);
+          v[1] += -2.0f * grad_distance * (xy * dx + yy * dy);
+          v[2] += grad_distance * dx * dx;
+          v[3] += grad_distance * dx * dy;
+          v[4] += grad_distance * dy * dy;
+        }
         v[5] += grad_color * gr[q];
         v[6] += grad_color * gg[q];
         v[7] += grad_color * gb[q];
@@ -523,12 +530,18 @@ int32_t launch_composite_bwd(int64_t n, const float* projected_mean,
       static_cast<int64_t>(p.width / p.tile_size) * (p.height / p.tile_size);
   if (num_tiles == 0 || n == 0) return GS_OK;
 #define GS_LAUNCH(TS)                                                                          \
-  composite_bwd_kernel<TS, BwdPpt<TS>::value>                                                  \
-      <<<static_cast<unsigned>(num_tiles), TileShape<TS, BwdPpt<TS>::value>::kThreads, 0,       \
-         stream>>>(                                                                            \
-          projected_mean, inverse_covariance, projected_color, projected_opacity,              \
-          gaussian_ids, ranges, grad_image, final_transmittance, n_contributors, p,            \
-          grad_projected)
+  if (p.gaussian_mode)                                                                         \
+    composite_bwd_kernel<TS, BwdPpt<TS>::value, true>                                          \
+        <<<static_cast<unsigned>(num_tiles), TileShape<TS, BwdPpt<TS>::value>::kThreads, 0,   \
+           stream>>>(projected_mean, inverse_covariance, projected_color, projected_opacity,   \
+                     gaussian_ids, ranges, grad_image, final_transmittance, n_contributors, p, \
+                     grad_projected);                                                          \
+  else                                                                                         \
+    composite_bwd_kernel<TS, BwdPpt<TS>::value, false>                                         \
+        <<<static_cast<unsigned>(num_tiles), TileShape<TS, BwdPpt<TS>::value>::kThreads, 0,   \
+           stream>>>(projected_mean, inverse_covariance, projected_color, projected_opacity,   \
+                     gaussian_ids, ranges, grad_image, final_transmittance, n_contributors, p, \
+                     grad_projected)
   GS_TILE_DISPATCH(p.tile_size, GS_LAUNCH)
 #undef GS_LAUNCH
   return check_launch();

@@ -190,7 +190,10 @@ __global__ void __launch_bounds__(128) project_bwd_kernel(
     const gs_params p, float* __restrict__ grad_mean, float* __restrict__ grad_rotation,
     float* __restrict__ grad_scale, float* __restrict__ grad_opacity,
     float* __restrict__ grad_color) {
-  constexpr int KB = K < 16 ? K : 16;  // backward covers SH degree <= 3 (project_bwd.py:33)
+  // SH coefficients with a gradient: all K. The reference's backward stops at 16
+  // (project_bwd.py:33); degree 4 is carried through here.
+  constexpr int KB = K;
+  constexpr int KA = K > 16 ? 25 : 16;  // basis / derivative slots
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= n) return;
   const bool visible = __ldg(counts + i) != 0;
@@ -300,16 +303,17 @@ __global__ void __launch_bounds__(128) project_bwd_kernel(
   float gmy = gux * c.r01 + guy * c.r11 + guz * c.r21;
   float gmz = gux * c.r02 + guy * c.r12 + guz * c.r22;
   // project_bwd.py:228-318: SH VJP for coefficients 0..15 and the view
-  // direction's contribution to the mean.
+  // direction's contribution to the mean; degree 4 (coefficients 16..24)
+  // differentiates the forward basis (project.py:51-61) the same way.
   const float ddx = mx + c.r00 * c.tx + c.r10 * c.ty + c.r20 * c.tz;
   const float ddy = my + c.r01 * c.tx + c.r11 * c.ty + c.r21 * c.tz;
   const float ddz = mz + c.r02 * c.tx + c.r12 * c.ty + c.r22 * c.tz;
   const float norm = sqrtf(ddx * ddx + ddy * ddy + ddz * ddz);
   const float x = ddx / norm, y = ddy / norm, z = ddz / norm;
   const float xx = x * x, yy = y * y, zz = z * z;
-  float basis[16], dbx[16], dby[16], dbz[16];
+  float basis[KA], dbx[KA], dby[KA], dbz[KA];
 #pragma unroll
-  for (int k = 0; k < 16; ++k) { dbx[k] = 0.0f; dby[k] = 0.0f; dbz[k] = 0.0f; }
+  for (int k = 0; k < KA; ++k) { dbx[k] = 0.0f; dby[k] = 0.0f; dbz[k] = 0.0f; }
   basis[0] = 0.28209479177387814f;
   basis[1] = -0.4886025119029199f * y;
   basis[2] = 0.4886025119029199f * z;
@@ -359,6 +363,38 @@ __global__ void __launch_bounds__(128) project_bwd_kernel(
   dbz[14] = 1.445305721320277f * (xx - yy);
   dbx[15] = -1.7701307697799305f * (xx - yy);
   dby[15] = 3.540261539559861f * x * y;
+  if constexpr (K > 16) {
+    basis[16] = 2.5033429417967046f * x * y * (xx - yy);
+    basis[17] = -1.7701307697799304f * y * z * (3.0f * xx - yy);
+    basis[18] = 0.9461746957575601f * x * y * (7.0f * zz - 1.0f);
+    basis[19] = -0.6690465435572892f * y * z * (7.0f * zz - 3.0f);
+    basis[20] = 0.10578554691520431f * (zz * (35.0f * zz - 30.0f) + 3.0f);
+    basis[21] = -0.6690465435572892f * x * z * (7.0f * zz - 3.0f);
+    basis[22] = 0.47308734787878004f * (xx - yy) * (7.0f * zz - 1.0f);
+    basis[23] = -1.7701307697799304f * x * z * (xx - 3.0f * yy);
+    basis[24] = 0.6258357354491761f * (xx * (xx - 3.0f * yy) - yy * (3.0f * xx - yy));
+    dbx[16] = 2.5033429417967046f * y * (3.0f * xx - yy);
+    dby[16] = 2.5033429417967046f * x * (xx - 3.0f * yy);
+    dbx[17] = -10.620784618679583f * x * y * z;
+    dby[17] = -5.310392309339791f * z * (xx - yy);
+    dbz[17] = -1.7701307697799304f * y * (3.0f * xx - yy);
+    dbx[18] = 0.9461746957575601f * y * (7.0f * zz - 1.0f);
+    dby[18] = 0.9461746957575601f * x * (7.0f * zz - 1.0f);
+    dbz[18] = 13.246445740605841f * x * y * z;
+    dby[19] = -0.6690465435572892f * z * (7.0f * zz - 3.0f);
+    dbz[19] = -0.6690465435572892f * y * (21.0f * zz - 3.0f);
+    dbz[20] = 0.10578554691520431f * z * (140.0f * zz - 60.0f);
+    dbx[21] = -0.6690465435572892f * z * (7.0f * zz - 3.0f);
+    dbz[21] = -0.6690465435572892f * x * (21.0f * zz - 3.0f);
+    dbx[22] = 0.9461746957575601f * x * (7.0f * zz - 1.0f);
+    dby[22] = -0.9461746957575601f * y * (7.0f * zz - 1.0f);
+    dbz[22] = 6.623222870302921f * z * (xx - yy);
+    dbx[23] = -5.310392309339791f * z * (xx - yy);
+    dby[23] = 10.620784618679583f * x * y * z;
+    dbz[23] = -1.7701307697799304f * x * (xx - 3.0f * yy);
+    dbx[24] = 2.5033429417967046f * x * (xx - 3.0f * yy);
+    dby[24] = 2.5033429417967046f * y * (yy - 3.0f * xx);
+  }
   float coefficients[K * 3];
   load_sh<K>(color + i * (K * 3), coefficients);
   float* gcol = grad_color + i * (K * 3);
@@ -387,7 +423,7 @@ __global__ void __launch_bounds__(128) project_bwd_kernel(
   for (int k = 0; k < K; ++k) {
 #pragma unroll
     for (int ch = 0; ch < 3; ++ch)
-      gout[3 * k + ch] = k < KB ? (visible ? gc3[ch] * basis[k < 16 ? k : 0] : 0.0f) : 0.0f;
+      gout[3 * k + ch] = visible ? gc3[ch] * basis[k] : 0.0f;
   }
   if constexpr ((K * 12) % 16 == 0) {
     float4* v = reinterpret_cast<float4*>(gcol);

@@ -23,8 +23,10 @@ Differences from the reference, all deliberate:
   operator returns (the reference's fake declares int32, interface.py:146-153);
 * an unknown ``rendering_mode`` raises ``ValueError`` instead of mixing the
   ellipsoid projection with Gaussian compositing;
-* SH coefficients 16..24 (degree 4) get zero gradients where the reference
-  leaves them uninitialised (project_bwd.py:33,355);
+* the backward covers SH degree 4 (coefficients 16..24 and their share of the
+  view-direction gradient), which the reference leaves uninitialised
+  (project_bwd.py:33,355), and ellipsoid rendering, which it refuses
+  (interface.py:184-186);
 * inputs must be CUDA tensors: there is no CPU path.
 """
 
@@ -241,10 +243,11 @@ def _setup_context(ctx, inputs, output) -> None:
 
 
 def _backward(ctx, *grad_outputs):
-    """Composite backward, then projection backward (interface.py:176-239)."""
-    assert ctx.rendering_mode == "gaussian", (
-        "Backward gradients are only supported for Gaussian rendering."
-    )
+    """Composite backward, then projection backward (interface.py:176-239).
+
+    Unlike the reference (interface.py:184-186), ellipsoid rendering has a
+    backward too: its indicator falloff passes gradients to colour and
+    opacity only."""
     (mean, rotation, scale, opacity, color, camera_rotation, camera_translation,
      final_transmittance, n_contributors, projected_mean, inverse_covariance, projected_color,
      projected_opacity, gaussian_ids, ranges, counts) = ctx.saved_tensors

@@ -151,7 +151,8 @@ int32_t gs_composite_bwd(int64_t n, const float *projected_mean, const float *in
                          float *grad_projected, gs_stream_t stream);
 
 /* Parameter gradients: replaces _project_bwd_kernel (project_bwd.py:8-381).
- * SH gradients cover coefficients 0..15; coefficients 16..24 get zero. */
+ * SH gradients cover all K coefficients: degree 4 (K = 25) differentiates the
+ * forward basis, where the reference's backward stops at 16 (project_bwd.py:33). */
 int32_t gs_project_bwd(int64_t n, int32_t num_sh, const float *mean, const float *rotation,
                        const float *scale, const float *opacity, const float *color,
                        const float *camera_rotation, const float *camera_translation,

@@ -21,8 +21,12 @@
  *  - opacity < 1/255 makes the reference's radius NaN; Triton's clamp then
  *    yields bounds 0 and count 0, which is what happens here;
  *  - the key sort is stable (ties in (tile, depth bits) keep emission order);
- *  - SH coefficients 16..24 receive a zero gradient (the reference leaves
- *    them uninitialised, project_bwd.py:33,355).
+ *  - the backward differentiates SH degree 4 too (coefficients 16..24 and
+ *    their share of the view-direction gradient), where the reference stops
+ *    at 16 and leaves the rest uninitialised (project_bwd.py:33,355);
+ *  - ellipsoid rendering has a backward (colour and opacity gradients; the
+ *    indicator falloff has none), which the reference refuses
+ *    (interface.py:184-186).
  * Pair evaluation inside compositing (shared by forward and backward):
  *    dx = x - mean_x, dy = y - mean_y (integer pixel coordinates, no +0.5)
  *    d2 = fmaf(xx*dx, dx, fmaf((2*xy)*dx, dy, (yy*dy)*dy))
@@ -403,7 +407,8 @@ void gso_composite_bwd(int64_t n, const float *projected_mean, const float *inve
                 grad_alpha = alpha_raw < 0.99f ? grad_alpha : 0.0f;
                 float probability_grad = grad_alpha * o;
                 float grad_color = forward * alpha;
-                float grad_distance = -0.5f * prob * probability_grad;
+                /* ellipsoid mode: the indicator falloff has no gradient */
+                float grad_distance = p->gaussian_mode ? -0.5f * prob * probability_grad : 0.0f;
                 row[0] += -2.0f * grad_distance * (xx * dx + xy * dy);
                 row[1] += -2.0f * grad_distance * (xy * dx + yy * dy);
                 row[2] += grad_distance * dx * dx;
@@ -538,14 +543,16 @@ static void project_bwd_one(int64_t i, const float *mean, const float *rotation,
     float gmx = gux * cr00 + guy * cr10 + guz * cr20;
     float gmy = gux * cr01 + guy * cr11 + guz * cr21;
     float gmz = gux * cr02 + guy * cr12 + guz * cr22;
-    /* project_bwd.py:228-318 (degree <= 3) */
+    /* project_bwd.py:228-318 (degree <= 3); degree 4 (coefficients 16..24)
+     * differentiates the forward basis (project.py:51-61) the same way,
+     * where the reference's backward stops at 16 (project_bwd.py:33). */
     float dx = mx + cr00 * tx + cr10 * ty + cr20 * tz;
     float dy = my + cr01 * tx + cr11 * ty + cr21 * tz;
     float dz = mz + cr02 * tx + cr12 * ty + cr22 * tz;
     float norm = sqrtf(dx * dx + dy * dy + dz * dz);
     float x = dx / norm, y = dy / norm, z = dz / norm;
     float xx = x * x, yy = y * y, zz = z * z;
-    float basis[16], dbx[16], dby[16], dbz[16];
+    float basis[25], dbx[25], dby[25], dbz[25];
     memset(dbx, 0, sizeof dbx); memset(dby, 0, sizeof dby); memset(dbz, 0, sizeof dbz);
     basis[0] = 0.28209479177387814f;
     basis[1] = -0.4886025119029199f * y;
@@ -596,7 +603,39 @@ static void project_bwd_one(int64_t i, const float *mean, const float *rotation,
     dbz[14] = 1.445305721320277f * (xx - yy);
     dbx[15] = -1.7701307697799305f * (xx - yy);
     dby[15] = 3.540261539559861f * x * y;
-    const int kmax = num_sh < 16 ? num_sh : 16;
+    if (num_sh > 16) {
+        basis[16] = 2.5033429417967046f * x * y * (xx - yy);
+        basis[17] = -1.7701307697799304f * y * z * (3.0f * xx - yy);
+        basis[18] = 0.9461746957575601f * x * y * (7.0f * zz - 1.0f);
+        basis[19] = -0.6690465435572892f * y * z * (7.0f * zz - 3.0f);
+        basis[20] = 0.10578554691520431f * (zz * (35.0f * zz - 30.0f) + 3.0f);
+        basis[21] = -0.6690465435572892f * x * z * (7.0f * zz - 3.0f);
+        basis[22] = 0.47308734787878004f * (xx - yy) * (7.0f * zz - 1.0f);
+        basis[23] = -1.7701307697799304f * x * z * (xx - 3.0f * yy);
+        basis[24] = 0.6258357354491761f * (xx * (xx - 3.0f * yy) - yy * (3.0f * xx - yy));
+        dbx[16] = 2.5033429417967046f * y * (3.0f * xx - yy);
+        dby[16] = 2.5033429417967046f * x * (xx - 3.0f * yy);
+        dbx[17] = -10.620784618679583f * x * y * z;
+        dby[17] = -5.310392309339791f * z * (xx - yy);
+        dbz[17] = -1.7701307697799304f * y * (3.0f * xx - yy);
+        dbx[18] = 0.9461746957575601f * y * (7.0f * zz - 1.0f);
+        dby[18] = 0.9461746957575601f * x * (7.0f * zz - 1.0f);
+        dbz[18] = 13.246445740605841f * x * y * z;
+        dby[19] = -0.6690465435572892f * z * (7.0f * zz - 3.0f);
+        dbz[19] = -0.6690465435572892f * y * (21.0f * zz - 3.0f);
+        dbz[20] = 0.10578554691520431f * z * (140.0f * zz - 60.0f);
+        dbx[21] = -0.6690465435572892f * z * (7.0f * zz - 3.0f);
+        dbz[21] = -0.6690465435572892f * x * (21.0f * zz - 3.0f);
+        dbx[22] = 0.9461746957575601f * x * (7.0f * zz - 1.0f);
+        dby[22] = -0.9461746957575601f * y * (7.0f * zz - 1.0f);
+        dbz[22] = 6.623222870302921f * z * (xx - yy);
+        dbx[23] = -5.310392309339791f * z * (xx - yy);
+        dby[23] = 10.620784618679583f * x * y * z;
+        dbz[23] = -1.7701307697799304f * x * (xx - 3.0f * yy);
+        dbx[24] = 2.5033429417967046f * x * (xx - 3.0f * yy);
+        dby[24] = 2.5033429417967046f * y * (yy - 3.0f * xx);
+    }
+    const int kmax = num_sh;
     const float *coefficients = color + i * (int64_t)num_sh * 3;
     float *gcol = grad_color + i * (int64_t)num_sh * 3;
     float gdx = 0.0f, gdy = 0.0f, gdz = 0.0f;
@@ -612,7 +651,6 @@ static void project_bwd_one(int64_t i, const float *mean, const float *rotation,
         raw = raw + 0.5f;
         float gc = gp[5 + c] * (raw > 0.0f ? 1.0f : 0.0f);
         for (int k = 0; k < kmax; ++k) gcol[3 * k + c] = visible ? gc * basis[k] : 0.0f;
-        for (int k = kmax; k < num_sh; ++k) gcol[3 * k + c] = 0.0f;
         gdx += gc * sdx;
         gdy += gc * sdy;
         gdz += gc * sdz;

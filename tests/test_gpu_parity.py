@@ -97,3 +97,23 @@ def test_backward_with_nothing_visible(oracle):
     got = run_operator(inputs, settings, grad_image=g)
     for key in PARAM_NAMES:
         assert np.all(got["grad_" + key] == 0), key
+
+
+@pytest.mark.parametrize("name", ["fixture_sh4_t8", "fixture_ellipsoid"])
+def test_extended_backward_vs_oracle(oracle, name):
+    """Backward paths the reference lacks: SH degree 4 and ellipsoid
+    rendering (the oracle's versions are checked against float64 autograd in
+    tests/test_extended_backward_cpu.py)."""
+    inputs, settings, _ = _load(oracle, name)
+    rng = np.random.default_rng(5)
+    grad_image = rng.standard_normal((settings.height, settings.width, 3)).astype(np.float32)
+    got = run_operator(inputs, settings, grad_image=grad_image)
+    fwd = oracle.rasterize(*(inputs[k] for k in INPUTS_ORDER), settings)
+    grads = oracle.backward(inputs, fwd, grad_image, settings)
+    for key in PARAM_NAMES:
+        np.testing.assert_allclose(got["grad_" + key], grads[key], rtol=1e-4, atol=1e-6,
+                                   err_msg=key)
+    if name == "fixture_sh4_t8":
+        assert np.abs(got["grad_color"][:, 16:]).max() > 0
+    else:
+        assert np.abs(got["grad_opacity"]).max() > 0
