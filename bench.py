@@ -512,6 +512,9 @@ def optimizer_timings(params, grads, device, repeats=5):
     return result
 
 
+BATCH_VIEWS = 16  # cameras per rasterize_batch call in forward-only multi-camera configs
+
+
 def sort_passes(num_tiles):
     """8-bit radix passes of the tile sort for `num_tiles` tiles."""
     bits = max(0, (max(1, num_tiles) - 1).bit_length())
@@ -546,7 +549,7 @@ def main():
         return
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
-    from gaussian_splats_b200.rasterize import StageTimer, rasterize_outputs
+    from gaussian_splats_b200.rasterize import StageTimer, rasterize_batch, rasterize_outputs
     from gaussian_splats_b200.splats import GaussianSplat
     from gaussian_splats_b200.view_parallel import train_step as vp_train_step
 
@@ -580,13 +583,25 @@ def main():
         with torch.no_grad():
             return [render(s, camera)[0] for camera in cameras]
 
+    # Forward-only multi-camera configs render through the batched op, 16
+    # cameras per call (one projection launch and one host wait per call).
+    batched = not backward and workload["views"] is not None
+
+    def batched_step(s=splats):
+        images = []
+        for first in range(0, len(cameras), BATCH_VIEWS):
+            images += [out[0] for out in rasterize_batch(
+                s, cameras[first:first + BATCH_VIEWS], settings.tile_size,
+                settings.opacity_threshold, settings.near, settings.far)]
+        return images
+
     def train_step():
         # This rank's views forward + backward; the gradients are summed over
         # ranks with one all-reduce per parameter tensor (view_parallel).
         return vp_train_step(splats, cameras, targets, trainable,
                              lambda s, c: render(s, c)[0], loss_fn)
 
-    step = train_step if backward else forward_step
+    step = train_step if backward else (batched_step if batched else forward_step)
 
     def timed(fn, steps):
         if world > 1:
@@ -690,7 +705,7 @@ def main():
                                      lambda s, c: render(s, c)[0], loss_fn)
                 loss.item()
             else:
-                images = forward_step(slot_splats)
+                images = (batched_step if batched else forward_step)(slot_splats)
                 torch.stack([image.sum() for image in images]).cpu()
 
     e2e_run(max(1, args.warmup // 2))
@@ -744,6 +759,7 @@ def main():
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "fwd_ms": fwd_ms / per_view,
+        "batched_fwd_ms": ms / per_view if batched else None,
         "fwd_bwd_ms": ms / per_view if backward else None,
         "higher_is_better": True,
         "scaling": "weak" if workload["views"] is None else "strong",
@@ -765,7 +781,9 @@ def main():
         "roofline": main_roof, "rooflines": rooflines, "optimizer": optimizer,
         "e2e": {"value": views_per_step * 1000.0 / e2e_ms, "unit": UNIT, "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-        "gpu_launches": launches_per_view(num_tiles, backward) * per_view * args.steps,
+        "gpu_launches": (launches_per_view(num_tiles, backward) * per_view if not batched else
+                         (launches_per_view(num_tiles, False) - 1) * per_view
+                         + -(-per_view // BATCH_VIEWS)) * args.steps,
         "clocks": clock,
     }
     if world == 1 and rank == 0 and not args.no_cpu_baseline:

@@ -600,9 +600,27 @@ uint64_t bin_sort_workspace_size(int64_t total, int64_t num_tiles) {
 // Where the depth-sorted Gaussian ids end up after the 4 passes.
 static uint64_t sorted_ids_offset(const CountLayout& L) { return L.ids_a; }
 
+// The count phase without the host wait: the intersection total and the
+// error word are copied into the caller's (pinned) host words on `stream`.
+int32_t launch_bin_count_async(int64_t n, const float* projected_mean, const int32_t* counts,
+                               void* workspace, int64_t* total_host, uint32_t* error_host,
+                               cudaStream_t stream);
+
 int32_t launch_bin_count(int64_t n, const float* projected_mean, const int32_t* counts,
                          void* workspace, int64_t* total_host, uint32_t* error_host,
                          cudaStream_t stream) {
+  int64_t total = 0;
+  uint32_t error = 0;
+  GS_TRY(launch_bin_count_async(n, projected_mean, counts, workspace, &total, &error, stream));
+  GS_CUDA_TRY(cudaStreamSynchronize(stream));
+  *total_host = total;
+  *error_host = error;
+  return GS_OK;
+}
+
+int32_t launch_bin_count_async(int64_t n, const float* projected_mean, const int32_t* counts,
+                               void* workspace, int64_t* total_host, uint32_t* error_host,
+                               cudaStream_t stream) {
   const CountLayout L(n);
   BinHeader* h = at<BinHeader>(workspace, L.header);
   GS_CUDA_TRY(cudaMemsetAsync(workspace, 0, L.zero_bytes, stream));
@@ -639,12 +657,10 @@ int32_t launch_bin_count(int64_t n, const float* projected_mean, const int32_t* 
         at<uint32_t>(workspace, L.offsets), &h->total, &h->error);
     GS_TRY(check_launch());
   }
-  int64_t result[2];
-  GS_CUDA_TRY(cudaMemcpyAsync(result, &h->total, sizeof(int64_t), cudaMemcpyDeviceToHost, stream));
+  GS_CUDA_TRY(cudaMemcpyAsync(total_host, &h->total, sizeof(int64_t), cudaMemcpyDeviceToHost,
+                              stream));
   GS_CUDA_TRY(cudaMemcpyAsync(error_host, &h->error, sizeof(uint32_t), cudaMemcpyDeviceToHost,
                               stream));
-  GS_CUDA_TRY(cudaStreamSynchronize(stream));
-  *total_host = result[0];
   return GS_OK;
 }
 

@@ -11,6 +11,12 @@ int32_t launch_project_fwd(int64_t, int32_t, const float*, const float*, const f
                            const float*, const float*, const float*, const float*,
                            const gs_params&, float*, float*, float*, float*, int32_t*, int32_t*,
                            cudaStream_t);
+int32_t launch_project_fwd_batch(int64_t, int32_t, int32_t, const float*, const float*,
+                                 const float*, const float*, const float*, const float*,
+                                 const float*, const gs_params*, float*, float*, float*, float*,
+                                 int32_t*, int32_t*, cudaStream_t);
+int32_t launch_bin_count_async(int64_t, const float*, const int32_t*, void*, int64_t*, uint32_t*,
+                               cudaStream_t);
 int32_t launch_project_bwd(int64_t, int32_t, const float*, const float*, const float*,
                            const float*, const float*, const float*, const float*, const float*,
                            const float*, const int32_t*, const gs_params&, float*, float*, float*,
@@ -86,6 +92,39 @@ int32_t gs_project_fwd(int64_t n, int32_t num_sh, const float* mean, const float
                                 camera_translation, *params, projected_mean, inverse_covariance,
                                 projected_color, projected_opacity, bounds, counts,
                                 as_cuda(stream));
+}
+
+int32_t gs_project_fwd_batch(int64_t n, int32_t num_sh, int32_t num_views, const float* mean,
+                             const float* rotation, const float* scale, const float* opacity,
+                             const float* color, const float* camera_rotations_host,
+                             const float* camera_translations_host, const gs_params* params_host,
+                             float* projected_mean, float* inverse_covariance,
+                             float* projected_color, float* projected_opacity, int32_t* bounds,
+                             int32_t* counts, gs_stream_t stream) {
+  if (n < 0 || n >= gs::kMaxGaussians || num_views < 0) return GS_ERR_INVALID_ARGUMENT;
+  if (num_views > 0 && (!camera_rotations_host || !camera_translations_host || !params_host))
+    return GS_ERR_INVALID_ARGUMENT;
+  for (int32_t v = 0; v < num_views; ++v) GS_TRY(gs::check_params(params_host + v));
+  if (!gs::valid_sh(num_sh)) return num_sh > 25 ? GS_ERR_UNSUPPORTED : GS_ERR_INVALID_ARGUMENT;
+  if (!gs::aligned(rotation, 16) || !gs::aligned(inverse_covariance, 16) ||
+      !gs::aligned(bounds, 16) || ((num_sh == 4 || num_sh == 16) && !gs::aligned(color, 16)))
+    return GS_ERR_MISALIGNED;
+  return gs::launch_project_fwd_batch(n, num_sh, num_views, mean, rotation, scale, opacity, color,
+                                      camera_rotations_host, camera_translations_host,
+                                      params_host, projected_mean, inverse_covariance,
+                                      projected_color, projected_opacity, bounds, counts,
+                                      as_cuda(stream));
+}
+
+int32_t gs_bin_count_async(int64_t n, const float* projected_mean, const int32_t* counts,
+                           void* workspace, uint64_t workspace_bytes, int64_t* total_host,
+                           uint32_t* error_host, gs_stream_t stream) {
+  if (n < 0 || n >= gs::kMaxGaussians || !total_host || !error_host)
+    return GS_ERR_INVALID_ARGUMENT;
+  if (workspace_bytes < gs::bin_count_workspace_size(n)) return GS_ERR_INVALID_ARGUMENT;
+  if (!gs::aligned(workspace, 256)) return GS_ERR_MISALIGNED;
+  return gs::launch_bin_count_async(n, projected_mean, counts, workspace, total_host, error_host,
+                                    as_cuda(stream));
 }
 
 uint64_t gs_bin_count_workspace_size(int64_t n) {

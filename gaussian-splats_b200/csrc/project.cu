@@ -68,10 +68,146 @@ struct Camera {
   float r00, r01, r02, r10, r11, r12, r20, r21, r22, tx, ty, tz;
 };
 
+constexpr int kMaxBatchViews = 16;
+
 __device__ __forceinline__ Camera load_camera(const float* __restrict__ R,
                                               const float* __restrict__ t) {
   return Camera{__ldg(R), __ldg(R + 1), __ldg(R + 2), __ldg(R + 3), __ldg(R + 4), __ldg(R + 5),
                 __ldg(R + 6), __ldg(R + 7), __ldg(R + 8), __ldg(t), __ldg(t + 1), __ldg(t + 2)};
+}
+
+// Batched projection (several cameras per launch) is built from two parts.
+// They evaluate exactly the expressions of project_fwd_kernel below, so with
+// no implicit multiply-add fusion every output is bit-identical to it; the
+// single-view kernel keeps its own ordering, which holds fewer values live.
+//
+// The view-independent part of one Gaussian's projection: world mean,
+// R(q) diag(exp(scale)) (project.py:144-156,177-199), opacity and the Gaussian
+// mode's radius multiplier 2 sqrt(log(255 o)) (project.py:230-236).
+struct GaussianTerms {
+  float mx, my, mz;
+  float a0x, a0y, a0z, a1x, a1y, a1z, a2x, a2y, a2z;
+  float o, gaussian_extent;
+};
+
+__device__ __forceinline__ GaussianTerms gaussian_terms(int64_t i, const float* __restrict__ mean,
+                                                        const float* __restrict__ rotation,
+                                                        const float* __restrict__ scale,
+                                                        const float* __restrict__ opacity) {
+  GaussianTerms g;
+  g.mx = __ldg(mean + 3 * i);
+  g.my = __ldg(mean + 3 * i + 1);
+  g.mz = __ldg(mean + 3 * i + 2);
+  // project.py:144-156
+  const float4 q4 = __ldg(reinterpret_cast<const float4*>(rotation) + i);
+  float qw = q4.x, qx = q4.y, qy = q4.z, qz = q4.w;
+  const float inverse_norm = det_rsqrt(qw * qw + qx * qx + qy * qy + qz * qz);
+  qw = qw * inverse_norm; qx = qx * inverse_norm; qy = qy * inverse_norm; qz = qz * inverse_norm;
+  // project.py:177-199
+  const float sx = det_exp(__ldg(scale + 3 * i)), sy = det_exp(__ldg(scale + 3 * i + 1)),
+              sz = det_exp(__ldg(scale + 3 * i + 2));
+  g.a0x = (1.0f - 2.0f * (qy * qy + qz * qz)) * sx;
+  g.a0y = (2.0f * (qx * qy + qw * qz)) * sx;
+  g.a0z = (2.0f * (qx * qz - qw * qy)) * sx;
+  g.a1x = (2.0f * (qx * qy - qw * qz)) * sy;
+  g.a1y = (1.0f - 2.0f * (qx * qx + qz * qz)) * sy;
+  g.a1z = (2.0f * (qy * qz + qw * qx)) * sy;
+  g.a2x = (2.0f * (qx * qz + qw * qy)) * sz;
+  g.a2y = (2.0f * (qy * qz - qw * qx)) * sz;
+  g.a2z = (1.0f - 2.0f * (qx * qx + qy * qy)) * sz;
+  // project.py:230-236
+  g.o = det_sigmoid(__ldg(opacity + i));
+  g.gaussian_extent = 2.0f * sqrtf(det_log(g.o * 255.0f));
+  return g;
+}
+
+// The view-dependent part: camera transform, 2D covariance and conic, SH
+// colour along the view direction, tile rectangle and count of Gaussian i
+// for one camera (project.py:126-142,158-176,200-253). Output pointers are
+// those of this view. The SH row is loaded where it is used, so its 3K
+// registers are not live during the covariance (a batched caller's repeated
+// loads of the row hit L1).
+template <int K>
+__device__ __forceinline__ void project_view(
+    int64_t i, const GaussianTerms& g, const float* __restrict__ sh_row, const Camera& c,
+    const gs_params& p, float* __restrict__ projected_mean, float* __restrict__ inverse_covariance,
+    float* __restrict__ projected_color, float* __restrict__ projected_opacity,
+    int4* __restrict__ bounds, int32_t* __restrict__ counts) {
+  const float mx = g.mx, my = g.my, mz = g.mz;
+  // project.py:126-142
+  const float camera_x = mx * c.r00 + my * c.r01 + mz * c.r02 + c.tx;
+  const float camera_y = mx * c.r10 + my * c.r11 + mz * c.r12 + c.ty;
+  const float camera_z = mx * c.r20 + my * c.r21 + mz * c.r22 + c.tz;
+  const float depth = -camera_z;
+  const float safe_z = depth > 0.0f ? fmaxf(1e-4f, depth) : fminf(-1e-4f, depth);
+  const float pixel_x = p.fx * camera_x / safe_z + p.cx;
+  const float pixel_y = -p.fy * camera_y / safe_z + p.cy;
+  projected_mean[3 * i] = pixel_x;
+  projected_mean[3 * i + 1] = pixel_y;
+  projected_mean[3 * i + 2] = safe_z;
+  // project.py:158-176
+  const float cov_x = fminf(p.lim_x, fmaxf(-p.lim_x, camera_x / safe_z)) * safe_z;
+  const float cov_y = fminf(p.lim_y, fmaxf(-p.lim_y, camera_y / safe_z)) * safe_z;
+  const float inverse_z = 1.0f / safe_z;
+  const float j00 = p.fx * inverse_z;
+  const float j02 = p.fx * cov_x * inverse_z * inverse_z;
+  const float j11 = -p.fy * inverse_z;
+  const float j12 = -p.fy * cov_y * inverse_z * inverse_z;
+  const float jc00 = j00 * c.r00 + j02 * c.r20, jc01 = j00 * c.r01 + j02 * c.r21,
+              jc02 = j00 * c.r02 + j02 * c.r22;
+  const float jc10 = j11 * c.r10 + j12 * c.r20, jc11 = j11 * c.r11 + j12 * c.r21,
+              jc12 = j11 * c.r12 + j12 * c.r22;
+  // project.py:200-218
+  const float f00 = jc00 * g.a0x + jc01 * g.a0y + jc02 * g.a0z;
+  const float f01 = jc00 * g.a1x + jc01 * g.a1y + jc02 * g.a1z;
+  const float f02 = jc00 * g.a2x + jc01 * g.a2y + jc02 * g.a2z;
+  const float f10 = jc10 * g.a0x + jc11 * g.a0y + jc12 * g.a0z;
+  const float f11 = jc10 * g.a1x + jc11 * g.a1y + jc12 * g.a1z;
+  const float f12 = jc10 * g.a2x + jc11 * g.a2y + jc12 * g.a2z;
+  const float cov00 = f00 * f00 + f01 * f01 + f02 * f02 + 0.03f;
+  const float cov01 = f00 * f10 + f01 * f11 + f02 * f12;
+  const float cov11 = f10 * f10 + f11 * f11 + f12 * f12 + 0.03f;
+  const float determinant = cov00 * cov11 - cov01 * cov01;
+  const float conic_xy = -cov01 / determinant;
+  reinterpret_cast<float4*>(inverse_covariance)[i] =
+      make_float4(cov11 / determinant, conic_xy, conic_xy, cov00 / determinant);
+  // project.py:221-228, _evaluate_sh (project.py:10-71)
+  float dx = mx + c.r00 * c.tx + c.r10 * c.ty + c.r20 * c.tz;
+  float dy = my + c.r01 * c.tx + c.r11 * c.ty + c.r21 * c.tz;
+  float dz = mz + c.r02 * c.tx + c.r12 * c.ty + c.r22 * c.tz;
+  const float direction_norm = det_rsqrt(dx * dx + dy * dy + dz * dz);
+  dx = dx * direction_norm; dy = dy * direction_norm; dz = dz * direction_norm;
+  const float xx = dx * dx, yy = dy * dy, zz = dz * dz;
+  float coefficients[K * 3];
+  load_sh<K>(sh_row, coefficients);
+  float acc_r = 0.0f, acc_g = 0.0f, acc_b = 0.0f;
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    const float b = sh_basis(k, dx, dy, dz, xx, yy, zz);
+    acc_r = fmaf(coefficients[3 * k], b, acc_r);
+    acc_g = fmaf(coefficients[3 * k + 1], b, acc_g);
+    acc_b = fmaf(coefficients[3 * k + 2], b, acc_b);
+  }
+  projected_color[3 * i] = fmaxf(acc_r + 0.5f, 0.0f);
+  projected_color[3 * i + 1] = fmaxf(acc_g + 0.5f, 0.0f);
+  projected_color[3 * i + 2] = fmaxf(acc_b + 0.5f, 0.0f);
+  // project.py:230-253
+  projected_opacity[i] = g.o;
+  const float radius_extent = p.gaussian_mode ? g.gaussian_extent : p.extent;
+  const float radius_x = radius_extent * sqrtf(cov00);
+  const float radius_y = radius_extent * sqrtf(cov11);
+  const float ts = static_cast<float>(p.tile_size);
+  const float tiles_w = static_cast<float>(p.width / p.tile_size);
+  const float tiles_h = static_cast<float>(p.height / p.tile_size);
+  // tl.clamp (max then min); a NaN radius clamps to 0.
+  const float tmin_x = fminf(fmaxf(floorf((pixel_x - radius_x) / ts), 0.0f), tiles_w);
+  const float tmin_y = fminf(fmaxf(floorf((pixel_y - radius_y) / ts), 0.0f), tiles_h);
+  const float tmax_x = fminf(fmaxf(floorf((pixel_x + radius_x) / ts) + 1.0f, 0.0f), tiles_w);
+  const float tmax_y = fminf(fmaxf(floorf((pixel_y + radius_y) / ts) + 1.0f, 0.0f), tiles_h);
+  bounds[i] = make_int4(static_cast<int>(tmin_x), static_cast<int>(tmax_x),
+                        static_cast<int>(tmin_y), static_cast<int>(tmax_y));
+  const float count = (tmax_x - tmin_x) * (tmax_y - tmin_y);
+  counts[i] = (safe_z > p.near_plane && safe_z < p.far_plane) ? static_cast<int32_t>(count) : 0;
 }
 
 template <int K>
@@ -178,6 +314,36 @@ __global__ void __launch_bounds__(256) project_fwd_kernel(
                         static_cast<int>(tmin_y), static_cast<int>(tmax_y));
   const float count = (tmax_x - tmin_x) * (tmax_y - tmin_y);
   counts[i] = (safe_z > p.near_plane && safe_z < p.far_plane) ? static_cast<int32_t>(count) : 0;
+}
+
+// Up to kMaxBatchViews cameras of one batched projection, passed by value.
+struct ViewBatch {
+  gs_params p[kMaxBatchViews];
+  Camera c[kMaxBatchViews];
+  int views;
+};
+
+// Batched projection: each thread reads its Gaussian's parameters once,
+// computes the view-independent terms once, and projects into every view of
+// the batch (its SH row comes from HBM once; the later views' loads hit L1).
+// View b writes at offset b * n of each output.
+template <int K>
+__global__ void __launch_bounds__(256) project_fwd_batch_kernel(
+    int64_t n, const float* __restrict__ mean, const float* __restrict__ rotation,
+    const float* __restrict__ scale, const float* __restrict__ opacity,
+    const float* __restrict__ color, const __grid_constant__ ViewBatch batch,
+    float* __restrict__ projected_mean, float* __restrict__ inverse_covariance,
+    float* __restrict__ projected_color, float* __restrict__ projected_opacity,
+    int4* __restrict__ bounds, int32_t* __restrict__ counts) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const GaussianTerms g = gaussian_terms(i, mean, rotation, scale, opacity);
+  for (int b = 0; b < batch.views; ++b) {
+    const int64_t o = static_cast<int64_t>(b) * n;
+    project_view<K>(i, g, color + i * (K * 3), batch.c[b], batch.p[b], projected_mean + 3 * o,
+                    inverse_covariance + 4 * o, projected_color + 3 * o, projected_opacity + o,
+                    bounds + o, counts + o);
+  }
 }
 
 template <int K>
@@ -481,6 +647,38 @@ int32_t launch_project_fwd(int64_t n, int32_t num_sh, const float* mean, const f
   GS_SH_DISPATCH(num_sh, GS_LAUNCH)
 #undef GS_LAUNCH
   return check_launch();
+}
+
+int32_t launch_project_fwd_batch(int64_t n, int32_t num_sh, int32_t num_views, const float* mean,
+                                 const float* rotation, const float* scale, const float* opacity,
+                                 const float* color, const float* camera_rotations_host,
+                                 const float* camera_translations_host,
+                                 const gs_params* params_host, float* projected_mean,
+                                 float* inverse_covariance, float* projected_color,
+                                 float* projected_opacity, int32_t* bounds, int32_t* counts,
+                                 cudaStream_t stream) {
+  if (n == 0 || num_views == 0) return GS_OK;
+  const unsigned blocks = ceil_div(n, 256);
+  for (int first = 0; first < num_views; first += kMaxBatchViews) {
+    ViewBatch batch{};
+    batch.views = num_views - first < kMaxBatchViews ? num_views - first : kMaxBatchViews;
+    for (int b = 0; b < batch.views; ++b) {
+      const float* R = camera_rotations_host + 9 * (first + b);
+      const float* t = camera_translations_host + 3 * (first + b);
+      batch.c[b] = Camera{R[0], R[1], R[2], R[3], R[4], R[5], R[6], R[7], R[8], t[0], t[1], t[2]};
+      batch.p[b] = params_host[first + b];
+    }
+    const int64_t o = static_cast<int64_t>(first) * n;
+#define GS_LAUNCH(K)                                                                          \
+  project_fwd_batch_kernel<K><<<blocks, 256, 0, stream>>>(                                    \
+      n, mean, rotation, scale, opacity, color, batch, projected_mean + 3 * o,                 \
+      inverse_covariance + 4 * o, projected_color + 3 * o, projected_opacity + o,              \
+      reinterpret_cast<int4*>(bounds) + o, counts + o)
+    GS_SH_DISPATCH(num_sh, GS_LAUNCH)
+#undef GS_LAUNCH
+    GS_TRY(check_launch());
+  }
+  return GS_OK;
 }
 
 int32_t launch_project_bwd(int64_t n, int32_t num_sh, const float* mean, const float* rotation,

@@ -29,7 +29,9 @@ EXPORTED_SYMBOLS = (
     "gs_version",
     "gs_last_cuda_error",
     "gs_project_fwd",
+    "gs_project_fwd_batch",
     "gs_bin_count",
+    "gs_bin_count_async",
     "gs_bin_count_workspace_size",
     "gs_bin_sort",
     "gs_bin_sort_workspace_size",
@@ -138,7 +140,9 @@ def lib() -> ctypes.CDLL:
         "gs_version": ([], i32),
         "gs_last_cuda_error": ([], i32),
         "gs_project_fwd": ([i64, i32] + [vp] * 7 + [P] + [vp] * 6 + [vp], i32),
+        "gs_project_fwd_batch": ([i64, i32, i32] + [vp] * 7 + [P] + [vp] * 6 + [vp], i32),
         "gs_bin_count": ([i64, vp, vp, vp, u64, ctypes.POINTER(i64), vp], i32),
+        "gs_bin_count_async": ([i64, vp, vp, vp, u64, vp, vp, vp], i32),
         "gs_bin_count_workspace_size": ([i64], u64),
         "gs_bin_sort": ([i64, i64, vp, vp, P, vp, u64, vp, u64, vp, vp, vp], i32),
         "gs_bin_sort_workspace_size": ([i64, i64], u64),

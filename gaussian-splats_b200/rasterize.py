@@ -353,3 +353,109 @@ def rasterize(
         raise ValueError(f"Unknown rasterization backend: {backend}")
     return rasterize_outputs(splats, camera, tile_size, opacity_threshold, near, far,
                              rendering_mode, confidence, indices)[0]
+
+
+def rasterize_batch(
+    splats,
+    cameras: list[Camera],
+    tile_size: int = 4,
+    opacity_threshold: float = 0.999,
+    near: float = 0.2,
+    far: float = 100.0,
+    rendering_mode: Literal["gaussian", "ellipsoid"] = "gaussian",
+    confidence: float = 0.95,
+) -> list[tuple[torch.Tensor, ...]]:
+    """Forward render of one scene from several cameras (no autograd).
+
+    Returns, per camera, the ten outputs of ``gaussian_splats::rasterize`` --
+    bit-identical to rendering that camera alone. The work is shared where
+    views allow it: one launch projects every Gaussian into up to 16 cameras
+    (its parameters are read once, the view-independent terms computed once);
+    the binning count phases of all views run back to back with one host wait
+    for all their intersection totals (instead of one wait per view); then
+    every view's sort and compositing are enqueued without further waits.
+    The reference renders one camera per call (visualize/gaussian/backend.py:48).
+    """
+    mean, rotation, scale, opacity, color = map(
+        _f32, (splats.mean.detach(), splats.rotation.detach(), splats.scale.detach(),
+               splats.opacity.detach(), splats.color.detach()))
+    _check_inputs(mean, color, rendering_mode)
+    assert tile_size > 0 and tile_size & (tile_size - 1) == 0
+    lib = native.lib()
+    device = mean.device
+    n, num_sh, views = mean.shape[0], color.shape[1], len(cameras)
+    if views == 0:
+        return []
+    params = (native.Params * views)()
+    rotations = torch.empty((views, 3, 3), dtype=torch.float32)
+    translations = torch.empty((views, 3), dtype=torch.float32)
+    sizes = []
+    for v, camera in enumerate(cameras):
+        fx, fy = camera.focal_length
+        cx, cy = camera.principal_point
+        width, height = camera.image_size
+        assert width % tile_size == 0 and height % tile_size == 0
+        params[v] = native.make_params(float(fx), float(fy), float(cx), float(cy), int(width),
+                                       int(height), tile_size, opacity_threshold, near, far,
+                                       rendering_mode, confidence)
+        rotations[v] = camera.rotation_matrix.detach().float().cpu()
+        translations[v] = camera.translation.detach().float().cpu()
+        sizes.append((int(width), int(height)))
+    with torch.cuda.device(device), torch.no_grad():
+        stream = _stream(device)
+        projected_mean = mean.new_empty((views, n, 3))
+        inverse_covariance = mean.new_empty((views, n, 2, 2))
+        projected_color = mean.new_empty((views, n, 3))
+        projected_opacity = mean.new_empty((views, n, 1))
+        bounds = torch.empty((views, n, 4), dtype=torch.int32, device=device)
+        counts = torch.empty((views, n), dtype=torch.int32, device=device)
+        native.check(lib.gs_project_fwd_batch(
+            n, num_sh, views, _ptr(mean), _ptr(rotation), _ptr(scale), _ptr(opacity),
+            _ptr(color), ctypes.c_void_p(rotations.data_ptr()),
+            ctypes.c_void_p(translations.data_ptr()), params, _ptr(projected_mean),
+            _ptr(inverse_covariance), _ptr(projected_color), _ptr(projected_opacity),
+            _ptr(bounds), _ptr(counts), stream), "gs_project_fwd_batch")
+
+        count_bytes = lib.gs_bin_count_workspace_size(n)
+        count_ws = torch.empty((views, count_bytes), dtype=torch.uint8, device=device)
+        stride = count_ws.stride(0)
+        if stride % 256:
+            raise RuntimeError("gaussian_splats_b200: count workspace rows are not 256-byte "
+                               "aligned")
+        totals = torch.zeros(views, dtype=torch.int64).pin_memory()
+        errors = torch.zeros(views, dtype=torch.int32).pin_memory()
+        for v in range(views):
+            native.check(lib.gs_bin_count_async(
+                n, _ptr(projected_mean[v]), _ptr(counts[v]), _ptr(count_ws[v]), count_bytes,
+                ctypes.c_void_p(totals.data_ptr() + 8 * v),
+                ctypes.c_void_p(errors.data_ptr() + 4 * v), stream), "gs_bin_count_async")
+        torch.cuda.current_stream(device).synchronize()
+        outputs = []
+        for v in range(views):
+            if int(errors[v]):
+                native.check(-6, "gs_bin_count_async")
+            total = int(totals[v])
+            if total >= 1 << 30:
+                native.check(-3, "gs_bin_count_async")
+            width, height = sizes[v]
+            num_tiles = (width // tile_size) * (height // tile_size)
+            pref = ctypes.byref(params[v])
+            gaussian_ids = torch.empty((total,), dtype=torch.int32, device=device)
+            ranges = torch.empty((num_tiles, 2), dtype=torch.int64, device=device)
+            sort_bytes = lib.gs_bin_sort_workspace_size(total, num_tiles)
+            sort_ws = torch.empty((sort_bytes,), dtype=torch.uint8, device=device)
+            native.check(lib.gs_bin_sort(
+                n, total, _ptr(bounds[v]), _ptr(counts[v]), pref, _ptr(count_ws[v]),
+                count_bytes, _ptr(sort_ws), sort_bytes, _ptr(gaussian_ids), _ptr(ranges),
+                stream), "gs_bin_sort")
+            image = mean.new_empty((height, width, 3))
+            final_transmittance = mean.new_empty((height, width))
+            n_contributors = torch.empty((height, width), dtype=torch.int32, device=device)
+            native.check(lib.gs_composite_fwd(
+                _ptr(projected_mean[v]), _ptr(inverse_covariance[v]), _ptr(projected_color[v]),
+                _ptr(projected_opacity[v]), _ptr(gaussian_ids), _ptr(ranges), pref, _ptr(image),
+                _ptr(final_transmittance), _ptr(n_contributors), stream), "gs_composite_fwd")
+            outputs.append((image, final_transmittance, n_contributors, projected_mean[v],
+                            inverse_covariance[v], projected_color[v], projected_opacity[v],
+                            gaussian_ids, ranges, counts[v]))
+    return outputs

@@ -78,6 +78,22 @@ int32_t gs_project_fwd(int64_t n, int32_t num_sh, const float *mean, const float
                        float *projected_opacity, int32_t *bounds, int32_t *counts,
                        gs_stream_t stream);
 
+/* Projection of one scene into `num_views` cameras at once (the batched
+ * multi-camera form of gs_project_fwd; no counterpart in the reference, which
+ * projects one view per call). Each thread reads its Gaussian's parameters
+ * and SH coefficients once, computes the view-independent terms once and
+ * projects into every camera; per view the outputs are bit-identical to
+ * gs_project_fwd's. Cameras and scalars are HOST arrays:
+ * camera_rotations_host [V,3,3], camera_translations_host [V,3],
+ * params_host [V]. Outputs are [V, N, ...]: view v starts at v * N rows. */
+int32_t gs_project_fwd_batch(int64_t n, int32_t num_sh, int32_t num_views, const float *mean,
+                             const float *rotation, const float *scale, const float *opacity,
+                             const float *color, const float *camera_rotations_host,
+                             const float *camera_translations_host, const gs_params *params_host,
+                             float *projected_mean, float *inverse_covariance,
+                             float *projected_color, float *projected_opacity, int32_t *bounds,
+                             int32_t *counts, gs_stream_t stream);
+
 /* Binning, phase 1: the host sync of emit_intersections
  * (intersections.py:51-52). Orders the Gaussians with counts > 0 by depth
  * (stable: equal depth bits keep index order), prefix-sums their counts in
@@ -89,6 +105,16 @@ int32_t gs_bin_count(int64_t n, const float *projected_mean, const int32_t *coun
                      void *workspace, uint64_t workspace_bytes, int64_t *total_host,
                      gs_stream_t stream);
 uint64_t gs_bin_count_workspace_size(int64_t n);
+
+/* Binning, phase 1 without the host wait (for several views in flight):
+ * enqueues what gs_bin_count does and copies the intersection total and the
+ * device error word into *total_host and *error_host on `stream` (use pinned
+ * memory for a truly asynchronous copy). Read them after synchronising the
+ * stream: a non-zero error word means a bounded wait gave up (as
+ * GS_ERR_TIMEOUT), and a total of 2^30 or more exceeds the sort's capacity. */
+int32_t gs_bin_count_async(int64_t n, const float *projected_mean, const int32_t *counts,
+                           void *workspace, uint64_t workspace_bytes, int64_t *total_host,
+                           uint32_t *error_host, gs_stream_t stream);
 
 /* Binning, phase 2: emit + sort + tile ranges, replacing _emit_intersections
  * (intersections.py:10-74) and sort_intersections (intersections.py:77-88).

@@ -94,3 +94,13 @@ def test_wrapper_argument_errors():
         R.rasterize(splats, camera, tile_size=32)
     with pytest.raises(ValueError, match="backend"):
         R.rasterize(splats, camera, tile_size=8, backend="torch")
+
+
+def test_batch_has_no_cpu_path():
+    from gaussian_splats_b200.rasterize import rasterize_batch
+
+    splats = GaussianSplat(10, sh_degree=0)
+    camera = PinholeCamera(image_size=(16, 16), focal_length=(10.0, 10.0),
+                           principal_point=(8.0, 8.0))
+    with pytest.raises(RuntimeError, match="no CPU"):
+        rasterize_batch(splats, [camera], tile_size=8)
