@@ -123,11 +123,21 @@ struct ArraySource {
 };
 
 // Element count of a pass: a host value, or a device word written earlier on
-// the stream (the number of visible Gaussians).
+// the stream (the number of visible Gaussians), or the smaller of a host
+// capacity and a device total (the intersection total, when the buffers were
+// sized before the host knew it).
 struct Count {
   int64_t host;
   const uint32_t* device;
-  __device__ __forceinline__ int64_t get() const { return device ? *device : host; }
+  const int64_t* device_total = nullptr;
+  __device__ __forceinline__ int64_t get() const {
+    if (device) return *device;
+    if (device_total) {
+      const int64_t t = *device_total;
+      return t < host ? t : host;
+    }
+    return host;
+  }
 };
 
 // Per-digit histograms of every pass at once (the global digit offsets each
@@ -137,10 +147,11 @@ struct Count {
 // Gaussian's tiles lie in few tile rows; depths share their exponent), which
 // would otherwise put whole warps on one counter.
 template <class Source, int kUpsweepRun>
-__global__ void __launch_bounds__(kThreads) upsweep_kernel(Source src, int64_t n, int num_passes,
+__global__ void __launch_bounds__(kThreads) upsweep_kernel(Source src, Count count, int num_passes,
                                                           int shift0, uint32_t* __restrict__ hist,
                                                           uint32_t* __restrict__ valid_total) {
   __shared__ uint32_t s_hist[4][kRadix];
+  const int64_t n = count.get();
   for (int i = threadIdx.x; i < 4 * kRadix; i += kThreads) (&s_hist[0][0])[i] = 0;
   __syncthreads();
   uint32_t valid_here = 0;
@@ -437,8 +448,8 @@ __global__ void __launch_bounds__(kThreads) count_scan_kernel(
 __global__ void __launch_bounds__(kThreads) emit_kernel(
     const uint32_t* __restrict__ sorted_ids, const uint32_t* __restrict__ num_valid,
     const uint32_t* __restrict__ offsets, const int32_t* __restrict__ counts,
-    const int4* __restrict__ bounds, int tiles_w, uint32_t* __restrict__ tile_keys,
-    uint32_t* __restrict__ values) {
+    const int4* __restrict__ bounds, int tiles_w, int64_t capacity,
+    uint32_t* __restrict__ tile_keys, uint32_t* __restrict__ values) {
   const int lane = threadIdx.x & 31;
   const int64_t warp_first = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) - lane;
   const int64_t n = *num_valid;
@@ -472,7 +483,7 @@ __global__ void __launch_bounds__(kThreads) emit_kernel(
     const int src_xmin = __shfl_sync(0xffffffffu, b.x, s);
     const int src_ymin = __shfl_sync(0xffffffffu, b.z, s);
     const int src_width = __shfl_sync(0xffffffffu, width, s);
-    if (o < total) {
+    if (o < total && static_cast<int64_t>(out0) + o < capacity) {
       const int local = static_cast<int>(o - src_excl);
       const int tile = (src_ymin + local / src_width) * tiles_w + src_xmin + local % src_width;
       tile_keys[out0 + o] = static_cast<uint32_t>(tile);
@@ -489,8 +500,9 @@ __global__ void __launch_bounds__(kThreads) emit_kernel(
 // and empty tiles get start == end. A thread takes kRangeItems consecutive
 // indices (two 16-byte loads when they are all inside the array).
 constexpr int kRangeItems = 8;
-__global__ void ranges_kernel(const uint32_t* __restrict__ sorted_keys, int64_t total,
+__global__ void ranges_kernel(const uint32_t* __restrict__ sorted_keys, Count count,
                               int64_t num_tiles, int64_t* __restrict__ ranges) {
+  const int64_t total = count.get();
   const int64_t i0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * kRangeItems;
   if (i0 > total) return;
   uint32_t k[kRangeItems];
@@ -606,28 +618,50 @@ int32_t launch_bin_count_async(int64_t n, const float* projected_mean, const int
                                void* workspace, int64_t* total_host, uint32_t* error_host,
                                cudaStream_t stream);
 
+int32_t launch_bin_count_kernels(int64_t n, const float* projected_mean, const int32_t* counts,
+                                 void* workspace, cudaStream_t stream);
+
 int32_t launch_bin_count(int64_t n, const float* projected_mean, const int32_t* counts,
                          void* workspace, int64_t* total_host, uint32_t* error_host,
                          cudaStream_t stream) {
-  int64_t total = 0;
-  uint32_t error = 0;
-  GS_TRY(launch_bin_count_async(n, projected_mean, counts, workspace, &total, &error, stream));
+  GS_TRY(launch_bin_count_kernels(n, projected_mean, counts, workspace, stream));
+  // error, pad and total are adjacent in the header: one copy brings both back.
+  struct {
+    uint32_t error, pad;
+    int64_t total;
+  } tail;
+  static_assert(offsetof(BinHeader, total) == offsetof(BinHeader, error) + 8,
+                "error and total must be adjacent");
+  const BinHeader* h = at<BinHeader>(workspace, CountLayout(n).header);
+  GS_CUDA_TRY(cudaMemcpyAsync(&tail, &h->error, sizeof(tail), cudaMemcpyDeviceToHost, stream));
   GS_CUDA_TRY(cudaStreamSynchronize(stream));
-  *total_host = total;
-  *error_host = error;
+  *total_host = tail.total;
+  *error_host = tail.error;
   return GS_OK;
 }
 
 int32_t launch_bin_count_async(int64_t n, const float* projected_mean, const int32_t* counts,
                                void* workspace, int64_t* total_host, uint32_t* error_host,
                                cudaStream_t stream) {
+  GS_TRY(launch_bin_count_kernels(n, projected_mean, counts, workspace, stream));
+  const BinHeader* h = at<BinHeader>(workspace, CountLayout(n).header);
+  GS_CUDA_TRY(cudaMemcpyAsync(total_host, &h->total, sizeof(int64_t), cudaMemcpyDeviceToHost,
+                              stream));
+  GS_CUDA_TRY(cudaMemcpyAsync(error_host, &h->error, sizeof(uint32_t), cudaMemcpyDeviceToHost,
+                              stream));
+  return GS_OK;
+}
+
+int32_t launch_bin_count_kernels(int64_t n, const float* projected_mean, const int32_t* counts,
+                                 void* workspace, cudaStream_t stream) {
   const CountLayout L(n);
   BinHeader* h = at<BinHeader>(workspace, L.header);
   GS_CUDA_TRY(cudaMemsetAsync(workspace, 0, L.zero_bytes, stream));
   if (n > 0) {
     const int64_t blocks = (n + kTile - 1) / kTile;
     upsweep_kernel<DepthSource, 4><<<upsweep_blocks(n), kThreads, 0, stream>>>(
-        DepthSource{projected_mean, counts}, n, 4, 0, &h->hist[0][0], &h->num_valid);
+        DepthSource{projected_mean, counts}, Count{n, nullptr}, 4, 0, &h->hist[0][0],
+        &h->num_valid);
     GS_TRY(check_launch());
     uint32_t* depth_status = at<uint32_t>(workspace, L.depth_status);
     uint32_t* kA = at<uint32_t>(workspace, L.keys_a);
@@ -657,13 +691,13 @@ int32_t launch_bin_count_async(int64_t n, const float* projected_mean, const int
         at<uint32_t>(workspace, L.offsets), &h->total, &h->error);
     GS_TRY(check_launch());
   }
-  GS_CUDA_TRY(cudaMemcpyAsync(total_host, &h->total, sizeof(int64_t), cudaMemcpyDeviceToHost,
-                              stream));
-  GS_CUDA_TRY(cudaMemcpyAsync(error_host, &h->error, sizeof(uint32_t), cudaMemcpyDeviceToHost,
-                              stream));
   return GS_OK;
 }
 
+// `total` is the capacity the buffers were sized for: the intersection total
+// itself, or more when the caller sized them before reading it. The kernels
+// read the true total from the count workspace and clamp it to the capacity
+// (an overflow leaves a wrong but in-bounds result, for the caller to redo).
 int32_t launch_bin_sort(int64_t n, int64_t total, const int32_t* bounds, const int32_t* counts,
                         const gs_params& p, const void* count_workspace, void* sort_workspace,
                         int32_t* gaussian_ids, int64_t* ranges, cudaStream_t stream) {
@@ -680,16 +714,17 @@ int32_t launch_bin_sort(int64_t n, int64_t total, const int32_t* bounds, const i
   uint32_t* vB = at<uint32_t>(sort_workspace, L.values_b);
   uint32_t* out_ids = reinterpret_cast<uint32_t*>(gaussian_ids);
   const uint32_t* sorted_keys = kA;
+  const Count live{total, nullptr, &ch->total};
   if (total > 0) {
     const int passes = L.passes;
     emit_kernel<<<ceil_div(n, kThreads), kThreads, 0, stream>>>(
         at<uint32_t>(count_workspace, sorted_ids_offset(C)), &ch->num_valid,
         at<uint32_t>(count_workspace, C.offsets), counts, reinterpret_cast<const int4*>(bounds),
-        static_cast<int>(tiles_w), kA, passes == 0 ? out_ids : vA);
+        static_cast<int>(tiles_w), total, kA, passes == 0 ? out_ids : vA);
     GS_TRY(check_launch());
     if (passes > 0) {
       upsweep_kernel<ArraySource, 16><<<upsweep_blocks(total), kThreads, 0, stream>>>(
-          ArraySource{kA, vA}, total, passes, 0, &h->hist[0][0], nullptr);
+          ArraySource{kA, vA}, live, passes, 0, &h->hist[0][0], nullptr);
       GS_TRY(check_launch());
       const int64_t blocks = (total + kTile - 1) / kTile;
       uint32_t* src_k = kA;
@@ -698,7 +733,7 @@ int32_t launch_bin_sort(int64_t n, int64_t total, const int32_t* bounds, const i
         uint32_t* dst_k = (pass % 2 == 0) ? kB : kA;
         uint32_t* dst_v = (pass == passes - 1) ? out_ids : ((pass % 2 == 0) ? vB : vA);
         sort_pass_kernel<<<blocks, kThreads, 0, stream>>>(
-            ArraySource{src_k, src_v}, Count{total, nullptr}, 8 * pass, &h->hist[pass][0],
+            ArraySource{src_k, src_v}, live, 8 * pass, &h->hist[pass][0],
             at<uint32_t>(sort_workspace, L.status) + static_cast<int64_t>(pass) * blocks * kRadix,
             &h->pass_counters[pass], dst_k, dst_v, &h->error);
         GS_TRY(check_launch());
@@ -710,7 +745,7 @@ int32_t launch_bin_sort(int64_t n, int64_t total, const int32_t* bounds, const i
   }
   if (num_tiles > 0) {
     ranges_kernel<<<ceil_div(ceil_div(total + 1, kRangeItems), 256), 256, 0, stream>>>(
-        sorted_keys, total, num_tiles, ranges);
+        sorted_keys, live, num_tiles, ranges);
     GS_TRY(check_launch());
   }
   return GS_OK;

@@ -115,6 +115,18 @@ def _mark(name: str) -> None:
         StageTimer.active.mark(name)
 
 
+# Intersection total of the last render per (Gaussians, tiles, device): later
+# renders size their sort buffers from it (plus headroom) and enqueue the sort
+# before their own total reaches the host.
+_LAST_TOTAL: dict[tuple[int, int, int | None], int] = {}
+
+
+def _pinned_words() -> torch.Tensor:
+    """Two zeroed pinned int64 host words (intersection total, error word) for
+    one render; torch's pinned-memory cache makes them cheap to allocate."""
+    return torch.zeros(2, dtype=torch.int64, pin_memory=True)
+
+
 @torch.library.custom_op("gaussian_splats::rasterize", mutates_args=())
 def _rasterize(
     mean: torch.Tensor,
@@ -176,36 +188,69 @@ def _rasterize(
 
         count_bytes = lib.gs_bin_count_workspace_size(n)
         count_ws = torch.empty((count_bytes,), dtype=torch.uint8, device=device)
-        total = ctypes.c_int64(0)
-        _mark("begin:bin_count")
-        native.check(lib.gs_bin_count(
-            n, _ptr(projected_mean), _ptr(counts), _ptr(count_ws), count_bytes,
-            ctypes.byref(total), stream), "gs_bin_count")
-        total = total.value
-        _mark("bin_count")
-
-        gaussian_ids = torch.empty((total,), dtype=torch.int32, device=device)
         ranges = torch.empty((num_tiles, 2), dtype=torch.int64, device=device)
-        sort_bytes = lib.gs_bin_sort_workspace_size(total, num_tiles)
-        sort_ws = torch.empty((sort_bytes,), dtype=torch.uint8, device=device)
-        _mark("begin:bin_sort")
-        native.check(lib.gs_bin_sort(
-            n, total, _ptr(bounds), _ptr(counts), pref, _ptr(count_ws), count_bytes,
-            _ptr(sort_ws), sort_bytes, _ptr(gaussian_ids), _ptr(ranges), stream), "gs_bin_sort")
-        _mark("bin_sort")
-        if os.environ.get("GAUSSIAN_SPLATS_B200_CHECK") == "1":
-            native.check(lib.gs_bin_check(_ptr(count_ws), _ptr(sort_ws), stream), "binning")
-
         image = mean.new_empty((image_height, image_width, 3))
         final_transmittance = mean.new_empty((image_height, image_width))
         n_contributors = torch.empty((image_height, image_width), dtype=torch.int32,
                                      device=device)
-        _mark("begin:composite_fwd")
-        native.check(lib.gs_composite_fwd(
-            _ptr(projected_mean), _ptr(inverse_covariance), _ptr(projected_color),
-            _ptr(projected_opacity), _ptr(gaussian_ids), _ptr(ranges), pref, _ptr(image),
-            _ptr(final_transmittance), _ptr(n_contributors), stream), "gs_composite_fwd")
-        _mark("composite_fwd")
+
+        def sort_and_composite(capacity):
+            gaussian_ids = torch.empty((capacity,), dtype=torch.int32, device=device)
+            sort_bytes = lib.gs_bin_sort_workspace_size(capacity, num_tiles)
+            sort_ws = torch.empty((sort_bytes,), dtype=torch.uint8, device=device)
+            _mark("begin:bin_sort")
+            native.check(lib.gs_bin_sort(
+                n, capacity, _ptr(bounds), _ptr(counts), pref, _ptr(count_ws), count_bytes,
+                _ptr(sort_ws), sort_bytes, _ptr(gaussian_ids), _ptr(ranges), stream),
+                "gs_bin_sort")
+            _mark("bin_sort")
+            if os.environ.get("GAUSSIAN_SPLATS_B200_CHECK") == "1":
+                native.check(lib.gs_bin_check(_ptr(count_ws), _ptr(sort_ws), stream), "binning")
+            _mark("begin:composite_fwd")
+            native.check(lib.gs_composite_fwd(
+                _ptr(projected_mean), _ptr(inverse_covariance), _ptr(projected_color),
+                _ptr(projected_opacity), _ptr(gaussian_ids), _ptr(ranges), pref, _ptr(image),
+                _ptr(final_transmittance), _ptr(n_contributors), stream), "gs_composite_fwd")
+            _mark("composite_fwd")
+            return gaussian_ids
+
+        key = (n, num_tiles, device.index)
+        last = _LAST_TOTAL.get(key)
+        _mark("begin:bin_count")
+        if last is None:
+            # First render of this shape: wait for the total, size exactly.
+            total = ctypes.c_int64(0)
+            native.check(lib.gs_bin_count(
+                n, _ptr(projected_mean), _ptr(counts), _ptr(count_ws), count_bytes,
+                ctypes.byref(total), stream), "gs_bin_count")
+            total = total.value
+            _mark("bin_count")
+            gaussian_ids = sort_and_composite(total)
+        else:
+            # Enqueue the sort and compositing at a capacity sized from the
+            # last total, read this total when the count phase is done (the
+            # GPU keeps working meanwhile), and redo if it did not fit.
+            words = _pinned_words()
+            native.check(lib.gs_bin_count_async(
+                n, _ptr(projected_mean), _ptr(counts), _ptr(count_ws), count_bytes,
+                ctypes.c_void_p(words.data_ptr()), ctypes.c_void_p(words.data_ptr() + 8),
+                stream), "gs_bin_count_async")
+            counted = torch.cuda.Event()
+            counted.record(torch.cuda.current_stream(device))
+            _mark("bin_count")
+            capacity = last + last // 4 + 4096
+            gaussian_ids = sort_and_composite(capacity)
+            counted.synchronize()
+            total, error = int(words[0]), int(words[1]) & 0xFFFFFFFF
+            if error:
+                native.check(-6, "gs_bin_count_async")
+            if total >= 1 << 30:
+                native.check(-3, "gs_bin_count_async")
+            if total > capacity:
+                gaussian_ids = sort_and_composite(total)
+            else:
+                gaussian_ids.resize_(total)  # same storage, no copy
+        _LAST_TOTAL[key] = total
     return (image, final_transmittance, n_contributors, projected_mean, inverse_covariance,
             projected_color, projected_opacity, gaussian_ids, ranges, counts)
 

@@ -122,8 +122,14 @@ int32_t gs_bin_count_async(int64_t n, const float *projected_mean, const int32_t
  * intersection ordered by (tile, depth bits, Gaussian index) -- the order of
  * the reference's stable sort of (tile << 32 | depth bits) keys emitted in
  * Gaussian order; ranges [num_tiles, 2] receives each tile's [start, end).
- * count_workspace is the buffer gs_bin_count filled; sort_workspace holds
- * gs_bin_sort_workspace_size(total, num_tiles) bytes of scratch. */
+ * count_workspace is the buffer gs_bin_count (or gs_bin_count_async) filled;
+ * sort_workspace holds gs_bin_sort_workspace_size(total, num_tiles) bytes of
+ * scratch. `total` may be any capacity at least the intersection total: the
+ * kernels read the true total from count_workspace, so the call can be
+ * enqueued before the total reaches the host; gaussian_ids then holds its
+ * first (true total) entries. If the true total exceeds the capacity the
+ * result is wrong but every access stays inside the buffers -- redo with the
+ * true total. */
 int32_t gs_bin_sort(int64_t n, int64_t total, const int32_t *bounds, const int32_t *counts,
                     const gs_params *params, const void *count_workspace,
                     uint64_t count_workspace_bytes, void *sort_workspace,

@@ -117,3 +117,23 @@ def test_extended_backward_vs_oracle(oracle, name):
         assert np.abs(got["grad_color"][:, 16:]).max() > 0
     else:
         assert np.abs(got["grad_opacity"]).max() > 0
+
+
+def test_capacity_overflow_redoes_the_sort(oracle):
+    """Renders after the first size the sort from the last intersection
+    total; a total above that capacity must redo the sort and compositing and
+    give exactly the outputs of an exactly sized render."""
+    import gaussian_splats_b200.rasterize as R
+
+    inputs, settings, _ = _load(oracle, "mini2")
+    exact = run_operator(inputs, settings)  # first render of this shape: exact sizes
+    keys = [k for k in R._LAST_TOTAL if k[0] == inputs["mean"].shape[0]]
+    assert keys and R._LAST_TOTAL[keys[0]] == exact["gaussian_ids"].shape[0]
+    for key in keys:
+        R._LAST_TOTAL[key] = 0  # capacity 4096, far below the total
+    small = run_operator(inputs, settings)
+    assert exact["gaussian_ids"].shape[0] > 4096
+    again = run_operator(inputs, settings)  # capacity from the true total
+    for got in (small, again):
+        for key in EXACT:
+            np.testing.assert_array_equal(got[key], exact[key], err_msg=key)
