@@ -33,6 +33,7 @@ Differences from the reference, all deliberate:
 from __future__ import annotations
 
 import ctypes
+import math
 import os
 from typing import Literal
 
@@ -287,6 +288,16 @@ def _setup_context(ctx, inputs, output) -> None:
      ctx.opacity_threshold, ctx.near, ctx.far, ctx.rendering_mode, ctx.confidence) = inputs[7:]
 
 
+def _carve(flat: torch.Tensor, n: int, shapes) -> list[torch.Tensor]:
+    """Consecutive views [n, *shape] of a flat buffer."""
+    views, offset = [], 0
+    for shape in shapes:
+        size = n * math.prod(shape)
+        views.append(flat[offset:offset + size].view(n, *shape))
+        offset += size
+    return views
+
+
 def _backward(ctx, *grad_outputs):
     """Composite backward, then projection backward (interface.py:176-239).
 
@@ -319,11 +330,12 @@ def _backward(ctx, *grad_outputs):
             _ptr(final_transmittance), _ptr(n_contributors), pref, _ptr(grad_projected),
             stream), "gs_composite_bwd")
         _mark("composite_bwd")
-        grad_mean = torch.empty_like(mean)
-        grad_rotation = torch.empty_like(rotation)
-        grad_scale = torch.empty_like(scale)
-        grad_opacity = torch.empty_like(opacity)
-        grad_color = torch.empty_like(color)
+        # The five gradients are carved out of one buffer (rotation and colour
+        # first, keeping their 16-byte rows aligned), so a view-parallel step
+        # can all-reduce them as one flat tensor without a packing copy.
+        grad_rotation, grad_color, grad_mean, grad_scale, grad_opacity = _carve(
+            mean.new_empty((n * (11 + 3 * num_sh),)), n,
+            ((4,), (num_sh, 3), (3,), (3,), (1,)))
         _mark("begin:project_bwd")
         native.check(lib.gs_project_bwd(
             n, num_sh, _ptr(mean), _ptr(rotation), _ptr(scale), _ptr(opacity), _ptr(color),

@@ -137,3 +137,25 @@ def test_capacity_overflow_redoes_the_sort(oracle):
     for got in (small, again):
         for key in EXACT:
             np.testing.assert_array_equal(got[key], exact[key], err_msg=key)
+
+
+def test_backward_gradients_share_one_buffer(oracle):
+    """The op's backward returns the five gradients as views of one buffer and
+    autograd adopts them as .grad without copying, so the view-parallel
+    exchange all-reduces one flat tensor."""
+    import torch
+
+    from gaussian_splats_b200 import scenes
+    from gaussian_splats_b200.rasterize import rasterize_outputs
+    from gaussian_splats_b200.splats import GaussianSplat
+    from gaussian_splats_b200.view_parallel import _shared_flat
+
+    scene = scenes.config2(num_points=3000, width=96, height=60, log_scale=(-3.5, 0.7))
+    splats = GaussianSplat.from_tensors(*(t.cuda() for t in scene.tensors()))
+    params = [splats.mean, splats.rotation, splats.scale, splats.opacity, splats.color]
+    for p in params:
+        p.requires_grad_(True)
+    image = rasterize_outputs(splats, scene.cameras[0], 16)[0]
+    image.sum().backward()
+    flat = _shared_flat([p.grad for p in params])
+    assert flat is not None and flat.numel() == 3000 * (11 + 3 * 16)

@@ -94,3 +94,37 @@ def test_missing_rank_ends_collective_with_error():
     mp.spawn(_failing_worker, args=(world, _free_port(), results), nprocs=world, join=True)
     assert results[1] == "left"
     assert results[0].startswith("error after"), results[0]
+
+
+def test_shared_flat_detection():
+    from gaussian_splats_b200.view_parallel import _shared_flat
+
+    flat = torch.arange(20, dtype=torch.float32)
+    views = [flat[0:8].view(2, 4), flat[8:14].view(2, 3), flat[14:20].view(2, 3)]
+    got = _shared_flat(views)
+    assert got is not None and got.numel() == 20 and got.data_ptr() == flat.data_ptr()
+    assert _shared_flat(views[:2]) is None  # does not cover the storage
+    assert _shared_flat([torch.zeros(3), torch.zeros(4)]) is None  # separate storages
+    assert _shared_flat([flat[0:10], flat[5:20]]) is None  # overlapping
+
+
+def _flat_worker(rank, world, port, results):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    params = [torch.zeros(5, 4, requires_grad=True), torch.zeros(5, 3, requires_grad=True)]
+    flat = torch.full((35,), float(rank + 1))
+    params[0].grad, params[1].grad = flat[:20].view(5, 4), flat[20:].view(5, 3)
+    all_reduce_gradients(params)
+    results[rank] = (float(params[0].grad.sum()), float(params[1].grad.sum()),
+                     params[0].grad.data_ptr() == flat.data_ptr())
+    dist.destroy_process_group()
+
+
+def test_flat_all_reduce_of_views():
+    world = 2
+    manager = mp.Manager()
+    results = manager.dict()
+    mp.spawn(_flat_worker, args=(world, _free_port(), results), nprocs=world, join=True)
+    for rank in range(world):
+        first, second, in_place = results[rank]
+        assert first == 20 * 3.0 and second == 15 * 3.0 and in_place
