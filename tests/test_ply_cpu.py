@@ -97,3 +97,15 @@ def test_rejects_bad_files(tmp_path):
         load_ply(tmp_path / "y.ply")
     with pytest.raises(ValueError):
         save_ply(dict(_state(), color=torch.zeros(7, 5, 3)), tmp_path / "z.ply")
+
+
+def test_convert_round_trip(tmp_path):
+    from gaussian_splats_b200.convert import ply_to_pt, pt_to_ply
+
+    splats = GaussianSplat(11, sh_degree=2)
+    splats.save_checkpoint(tmp_path / "s.pt")
+    ply = pt_to_ply(tmp_path / "s.pt")
+    assert ply == tmp_path / "s.ply" and ply.exists()
+    back = GaussianSplat.from_checkpoint(ply_to_pt(ply, tmp_path / "t.pt"))
+    for name in ("mean", "rotation", "scale", "opacity", "color", "normals"):
+        torch.testing.assert_close(getattr(back, name), getattr(splats, name), rtol=0, atol=0)
