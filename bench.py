@@ -595,11 +595,14 @@ def main():
                 settings.opacity_threshold, settings.near, settings.far)]
         return images
 
+    # One view per rank: the ranks exchange screen-space gradients and each
+    # sums the projection backward over all views (view_parallel); several
+    # views per rank: the parameter gradients are all-reduced once per step.
+    screen = world > 1 and len(cameras) == 1
+
     def train_step():
-        # This rank's views forward + backward; the gradients are summed over
-        # ranks with one all-reduce per parameter tensor (view_parallel).
         return vp_train_step(splats, cameras, targets, trainable,
-                             lambda s, c: render(s, c)[0], loss_fn)
+                             lambda s, c: render(s, c)[0], loss_fn, screen_exchange=screen)
 
     step = train_step if backward else (batched_step if batched else forward_step)
 
@@ -702,7 +705,8 @@ def main():
             torch.cuda.current_stream().wait_event(ready)
             if backward:
                 loss = vp_train_step(slot_splats, cameras, buffers[5:], slot_trainable,
-                                     lambda s, c: render(s, c)[0], loss_fn)
+                                     lambda s, c: render(s, c)[0], loss_fn,
+                                     screen_exchange=screen)
                 loss.item()
             else:
                 images = (batched_step if batched else forward_step)(slot_splats)
@@ -770,7 +774,9 @@ def main():
                    "image": [crop_w, crop_h], "tile_size": settings.tile_size,
                    "views_per_step": views_per_step, "views_per_rank_per_step": per_view,
                    "parallelism": (f"view-parallel x{world}" + (
-                       ", NCCL all-reduce of gradients" if backward else ", no collective"))
+                       (", NCCL all-gather of screen-space gradients + projection backward "
+                        "summed over all ranks' views" if screen else
+                        ", NCCL all-reduce of gradients") if backward else ", no collective"))
                    if world > 1 else "single GPU",
                    "l2": "inputs larger than L2 (Gaussian parameters read every view)"
                    if n * project_fwd_bytes(k) > 126e6 else

@@ -17,6 +17,10 @@ int32_t launch_project_fwd_batch(int64_t, int32_t, int32_t, const float*, const 
                                  int32_t*, int32_t*, cudaStream_t);
 int32_t launch_bin_count_async(int64_t, const float*, const int32_t*, void*, int64_t*, uint32_t*,
                                cudaStream_t);
+int32_t launch_project_bwd_views(int64_t, int32_t, int32_t, const float*, const float*,
+                                 const float*, const float*, const float*, const void*,
+                                 const float*, const int32_t*, float*, float*, float*, float*,
+                                 float*, cudaStream_t);
 int32_t launch_project_bwd(int64_t, int32_t, const float*, const float*, const float*,
                            const float*, const float*, const float*, const float*, const float*,
                            const float*, const int32_t*, const gs_params&, float*, float*, float*,
@@ -246,6 +250,23 @@ int32_t gs_adam_step(int64_t n, int32_t num_sh, const gs_splat_arrays* params,
   if (grads->color && !gs::aligned(grads->color, 16)) return GS_ERR_MISALIGNED;
   return gs::launch_adam_step(n, num_sh, *params, *grads, *exp_avg, *exp_avg_sq, *hyper, randn,
                               as_cuda(stream));
+}
+
+int32_t gs_project_bwd_views(int64_t n, int32_t num_sh, int32_t num_views, const float* mean,
+                             const float* rotation, const float* scale, const float* opacity,
+                             const float* color, const void* views, const float* grad_projected,
+                             const int32_t* counts, float* grad_mean, float* grad_rotation,
+                             float* grad_scale, float* grad_opacity, float* grad_color,
+                             gs_stream_t stream) {
+  if (n < 0 || n >= gs::kMaxGaussians || num_views < 0 || (num_views > 0 && !views))
+    return GS_ERR_INVALID_ARGUMENT;
+  if (!gs::valid_sh(num_sh)) return num_sh > 25 ? GS_ERR_UNSUPPORTED : GS_ERR_INVALID_ARGUMENT;
+  if (!gs::aligned(rotation, 16) || !gs::aligned(grad_rotation, 16) || !gs::aligned(views, 4) ||
+      ((num_sh == 4 || num_sh == 16) && (!gs::aligned(color, 16) || !gs::aligned(grad_color, 16))))
+    return GS_ERR_MISALIGNED;
+  return gs::launch_project_bwd_views(n, num_sh, num_views, mean, rotation, scale, opacity, color,
+                                      views, grad_projected, counts, grad_mean, grad_rotation,
+                                      grad_scale, grad_opacity, grad_color, as_cuda(stream));
 }
 
 int32_t gs_det_exp(int64_t n, const float* x, float* y, gs_stream_t stream) {

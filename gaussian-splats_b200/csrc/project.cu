@@ -316,6 +316,41 @@ __global__ void __launch_bounds__(256) project_fwd_kernel(
   counts[i] = (safe_z > p.near_plane && safe_z < p.far_plane) ? static_cast<int32_t>(count) : 0;
 }
 
+// One view's conic as the forward computes it (project.py:126-142,158-218):
+// the expressions of project_fwd_kernel, so the same bits as the conic the
+// forward wrote.
+__device__ __forceinline__ float4 view_conic(const GaussianTerms& g, const Camera& c,
+                                             const gs_params& p) {
+  const float camera_x = g.mx * c.r00 + g.my * c.r01 + g.mz * c.r02 + c.tx;
+  const float camera_y = g.mx * c.r10 + g.my * c.r11 + g.mz * c.r12 + c.ty;
+  const float camera_z = g.mx * c.r20 + g.my * c.r21 + g.mz * c.r22 + c.tz;
+  const float depth = -camera_z;
+  const float safe_z = depth > 0.0f ? fmaxf(1e-4f, depth) : fminf(-1e-4f, depth);
+  const float cov_x = fminf(p.lim_x, fmaxf(-p.lim_x, camera_x / safe_z)) * safe_z;
+  const float cov_y = fminf(p.lim_y, fmaxf(-p.lim_y, camera_y / safe_z)) * safe_z;
+  const float inverse_z = 1.0f / safe_z;
+  const float j00 = p.fx * inverse_z;
+  const float j02 = p.fx * cov_x * inverse_z * inverse_z;
+  const float j11 = -p.fy * inverse_z;
+  const float j12 = -p.fy * cov_y * inverse_z * inverse_z;
+  const float jc00 = j00 * c.r00 + j02 * c.r20, jc01 = j00 * c.r01 + j02 * c.r21,
+              jc02 = j00 * c.r02 + j02 * c.r22;
+  const float jc10 = j11 * c.r10 + j12 * c.r20, jc11 = j11 * c.r11 + j12 * c.r21,
+              jc12 = j11 * c.r12 + j12 * c.r22;
+  const float f00 = jc00 * g.a0x + jc01 * g.a0y + jc02 * g.a0z;
+  const float f01 = jc00 * g.a1x + jc01 * g.a1y + jc02 * g.a1z;
+  const float f02 = jc00 * g.a2x + jc01 * g.a2y + jc02 * g.a2z;
+  const float f10 = jc10 * g.a0x + jc11 * g.a0y + jc12 * g.a0z;
+  const float f11 = jc10 * g.a1x + jc11 * g.a1y + jc12 * g.a1z;
+  const float f12 = jc10 * g.a2x + jc11 * g.a2y + jc12 * g.a2z;
+  const float cov00 = f00 * f00 + f01 * f01 + f02 * f02 + 0.03f;
+  const float cov01 = f00 * f10 + f01 * f11 + f02 * f12;
+  const float cov11 = f10 * f10 + f11 * f11 + f12 * f12 + 0.03f;
+  const float determinant = cov00 * cov11 - cov01 * cov01;
+  const float conic_xy = -cov01 / determinant;
+  return make_float4(cov11 / determinant, conic_xy, conic_xy, cov00 / determinant);
+}
+
 // Up to kMaxBatchViews cameras of one batched projection, passed by value.
 struct ViewBatch {
   gs_params p[kMaxBatchViews];
@@ -346,35 +381,59 @@ __global__ void __launch_bounds__(256) project_fwd_batch_kernel(
   }
 }
 
-template <int K>
-__global__ void __launch_bounds__(128) project_bwd_kernel(
-    int64_t n, const float* __restrict__ mean, const float* __restrict__ rotation,
-    const float* __restrict__ scale, const float* __restrict__ opacity,
-    const float* __restrict__ color, const float* __restrict__ camera_rotation,
-    const float* __restrict__ camera_translation, const float* __restrict__ inverse_covariance,
-    const float* __restrict__ grad_projected, const int32_t* __restrict__ counts,
-    const gs_params p, float* __restrict__ grad_mean, float* __restrict__ grad_rotation,
-    float* __restrict__ grad_scale, float* __restrict__ grad_opacity,
-    float* __restrict__ grad_color) {
+// The view-independent terms of one Gaussian's projection backward
+// (project_bwd.py:62-94,320-334): its mean, normalised quaternion and the
+// reciprocal of the quaternion's norm, activated scales and opacity. A
+// backward over several views computes them once.
+struct BwdTerms {
+  float mx, my, mz;
+  float qw, qx, qy, qz, inverse_qnorm;
+  float sx, sy, sz, po;
+};
+
+__device__ __forceinline__ BwdTerms bwd_terms(int64_t i, const float* __restrict__ mean,
+                                              const float* __restrict__ rotation,
+                                              const float* __restrict__ scale,
+                                              const float* __restrict__ opacity) {
+  BwdTerms b;
+  b.mx = __ldg(mean + 3 * i);
+  b.my = __ldg(mean + 3 * i + 1);
+  b.mz = __ldg(mean + 3 * i + 2);
+  const float4 q4 = __ldg(reinterpret_cast<const float4*>(rotation) + i);
+  const float qnorm = sqrtf(q4.x * q4.x + q4.y * q4.y + q4.z * q4.z + q4.w * q4.w);
+  b.inverse_qnorm = 1.0f / qnorm;
+  b.qw = q4.x * b.inverse_qnorm;
+  b.qx = q4.y * b.inverse_qnorm;
+  b.qy = q4.z * b.inverse_qnorm;
+  b.qz = q4.w * b.inverse_qnorm;
+  b.sx = det_exp(__ldg(scale + 3 * i));
+  b.sy = det_exp(__ldg(scale + 3 * i + 1));
+  b.sz = det_exp(__ldg(scale + 3 * i + 2));
+  b.po = det_sigmoid(__ldg(opacity + i));
+  return b;
+}
+
+// Gradients of one Gaussian's parameters from its screen-space gradient in
+// one view (project_bwd.py:8-334), handed to `sink`: sink.color(g[3K]) with
+// the SH coefficient gradients, then sink.rest(mean xyz, rotation, scale xyz,
+// opacity). `b` holds the Gaussian's view-independent terms, `inv` is the
+// view's conic as the forward computed it and `gp` the view's 9-float
+// screen-space gradient of the Gaussian.
+template <int K, class Sink>
+__device__ __forceinline__ void project_bwd_view(
+    int64_t i, bool visible, const Camera& c, const gs_params& p, const BwdTerms& b,
+    const float* __restrict__ color, float4 inv, const float* __restrict__ gp, Sink& sink) {
   // SH coefficients with a gradient: all K. The reference's backward stops at 16
   // (project_bwd.py:33); degree 4 is carried through here.
   constexpr int KB = K;
   constexpr int KA = K > 16 ? 25 : 16;  // basis / derivative slots
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (i >= n) return;
-  const bool visible = __ldg(counts + i) != 0;
-  const Camera c = load_camera(camera_rotation, camera_translation);
   const float fx = p.fx, fy = p.fy, lim_x = p.bwd_lim_x, lim_y = p.bwd_lim_y;
-  const float mx = __ldg(mean + 3 * i), my = __ldg(mean + 3 * i + 1), mz = __ldg(mean + 3 * i + 2);
+  const float mx = b.mx, my = b.my, mz = b.mz;
   // project_bwd.py:62-94
   const float camera_x = mx * c.r00 + my * c.r01 + mz * c.r02 + c.tx;
   const float camera_y = mx * c.r10 + my * c.r11 + mz * c.r12 + c.ty;
   const float camera_z = mx * c.r20 + my * c.r21 + mz * c.r22 + c.tz;
-  const float4 q4 = __ldg(reinterpret_cast<const float4*>(rotation) + i);
-  float qw = q4.x, qx = q4.y, qy = q4.z, qz = q4.w;
-  const float qnorm = sqrtf(qw * qw + qx * qx + qy * qy + qz * qz);
-  const float inverse_qnorm = 1.0f / qnorm;
-  qw = qw * inverse_qnorm; qx = qx * inverse_qnorm; qy = qy * inverse_qnorm; qz = qz * inverse_qnorm;
+  const float qw = b.qw, qx = b.qx, qy = b.qy, qz = b.qz;
   const float r00 = 1.0f - 2.0f * (qy * qy + qz * qz), r01 = 2.0f * (qx * qy - qw * qz),
               r02 = 2.0f * (qx * qz + qw * qy);
   const float r10 = 2.0f * (qx * qy + qw * qz), r11 = 1.0f - 2.0f * (qx * qx + qz * qz),
@@ -395,8 +454,7 @@ __global__ void __launch_bounds__(128) project_bwd_kernel(
               jc02 = j00 * c.r02 + j02 * c.r22;
   const float jc10 = j11 * c.r10 + j12 * c.r20, jc11 = j11 * c.r11 + j12 * c.r21,
               jc12 = j11 * c.r12 + j12 * c.r22;
-  const float sx = det_exp(__ldg(scale + 3 * i)), sy = det_exp(__ldg(scale + 3 * i + 1)),
-              sz = det_exp(__ldg(scale + 3 * i + 2));
+  const float sx = b.sx, sy = b.sy, sz = b.sz;
   const float m0x = jc00 * r00 + jc01 * r10 + jc02 * r20, m0y = jc00 * r01 + jc01 * r11 + jc02 * r21,
               m0z = jc00 * r02 + jc01 * r12 + jc02 * r22;
   const float m1x = jc10 * r00 + jc11 * r10 + jc12 * r20, m1y = jc10 * r01 + jc11 * r11 + jc12 * r21,
@@ -404,8 +462,6 @@ __global__ void __launch_bounds__(128) project_bwd_kernel(
   const float a00 = m0x * sx, a01 = m0y * sy, a02 = m0z * sz;
   const float a10 = m1x * sx, a11 = m1y * sy, a12 = m1z * sz;
   // project_bwd.py:116-152
-  const float* gp = grad_projected + 9 * i;
-  const float4 inv = __ldg(reinterpret_cast<const float4*>(inverse_covariance) + i);
   const float inv00 = inv.x, inv01 = inv.y, inv10 = inv01, inv11 = inv.w;
   const float gi00 = __ldg(gp + 2), gi01 = __ldg(gp + 3), gi10 = gi01, gi11 = __ldg(gp + 4);
   const float h00 = inv00 * gi00 + inv10 * gi10, h01 = inv00 * gi01 + inv10 * gi11;
@@ -437,7 +493,7 @@ __global__ void __launch_bounds__(128) project_bwd_kernel(
   float gqz = 2.0f * qw * (gr10 - gr01) + 2.0f * qx * (gr02 + gr20) + 2.0f * qy * (gr12 + gr21) -
               4.0f * qz * (gr00 + gr11);
   const float dot_q = qw * gqw + qx * gqx + qy * gqy + qz * gqz;
-  const float gq_scale = 1.0f / qnorm;
+  const float gq_scale = b.inverse_qnorm;  // 1 / |q|
   gqw = (gqw - qw * dot_q) * gq_scale;
   gqx = (gqx - qx * dot_q) * gq_scale;
   gqy = (gqy - qy * dot_q) * gq_scale;
@@ -563,7 +619,6 @@ __global__ void __launch_bounds__(128) project_bwd_kernel(
   }
   float coefficients[K * 3];
   load_sh<K>(color + i * (K * 3), coefficients);
-  float* gcol = grad_color + i * (K * 3);
   float gc3[3];
   float gdx = 0.0f, gdy = 0.0f, gdz = 0.0f;
 #pragma unroll
@@ -591,32 +646,149 @@ __global__ void __launch_bounds__(128) project_bwd_kernel(
     for (int ch = 0; ch < 3; ++ch)
       gout[3 * k + ch] = visible ? gc3[ch] * basis[k] : 0.0f;
   }
-  if constexpr ((K * 12) % 16 == 0) {
-    float4* v = reinterpret_cast<float4*>(gcol);
-#pragma unroll
-    for (int j = 0; j < K * 3 / 4; ++j)
-      v[j] = make_float4(gout[4 * j], gout[4 * j + 1], gout[4 * j + 2], gout[4 * j + 3]);
-  } else {
-#pragma unroll
-    for (int j = 0; j < K * 3; ++j) gcol[j] = gout[j];
-  }
+  sink.color(gout);
   const float dot_d = x * gdx + y * gdy + z * gdz;
   gdx = (gdx - x * dot_d) / norm;
   gdy = (gdy - y * dot_d) / norm;
   gdz = (gdz - z * dot_d) / norm;
   gmx += gdx; gmy += gdy; gmz += gdz;
   // project_bwd.py:320-334
-  const float po = det_sigmoid(__ldg(opacity + i));
+  const float po = b.po;
   const float go = __ldg(gp + 8) * po * (1.0f - po);
-  grad_mean[3 * i] = visible ? gmx : 0.0f;
-  grad_mean[3 * i + 1] = visible ? gmy : 0.0f;
-  grad_mean[3 * i + 2] = visible ? gmz : 0.0f;
-  reinterpret_cast<float4*>(grad_rotation)[i] =
-      visible ? make_float4(gqw, gqx, gqy, gqz) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-  grad_scale[3 * i] = visible ? grad_sx * sx : 0.0f;
-  grad_scale[3 * i + 1] = visible ? grad_sy * sy : 0.0f;
-  grad_scale[3 * i + 2] = visible ? grad_sz * sz : 0.0f;
-  grad_opacity[i] = visible ? go : 0.0f;
+  sink.rest(visible ? gmx : 0.0f, visible ? gmy : 0.0f, visible ? gmz : 0.0f,
+            visible ? make_float4(gqw, gqx, gqy, gqz) : make_float4(0.0f, 0.0f, 0.0f, 0.0f),
+            visible ? grad_sx * sx : 0.0f, visible ? grad_sy * sy : 0.0f,
+            visible ? grad_sz * sz : 0.0f, visible ? go : 0.0f);
+}
+
+// Stores one view's gradients (the single-view backward).
+template <int K>
+struct StoreGradients {
+  int64_t i;
+  float *grad_mean, *grad_rotation, *grad_scale, *grad_opacity, *grad_color;
+  __device__ __forceinline__ void color(const float (&g)[K * 3]) {
+    float* gcol = grad_color + i * (K * 3);
+    if constexpr ((K * 12) % 16 == 0) {
+      float4* v = reinterpret_cast<float4*>(gcol);
+#pragma unroll
+      for (int j = 0; j < K * 3 / 4; ++j)
+        v[j] = make_float4(g[4 * j], g[4 * j + 1], g[4 * j + 2], g[4 * j + 3]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < K * 3; ++j) gcol[j] = g[j];
+    }
+  }
+  __device__ __forceinline__ void rest(float gmx, float gmy, float gmz, float4 grot, float gsx,
+                                       float gsy, float gsz, float go) {
+    grad_mean[3 * i] = gmx;
+    grad_mean[3 * i + 1] = gmy;
+    grad_mean[3 * i + 2] = gmz;
+    reinterpret_cast<float4*>(grad_rotation)[i] = grot;
+    grad_scale[3 * i] = gsx;
+    grad_scale[3 * i + 1] = gsy;
+    grad_scale[3 * i + 2] = gsz;
+    grad_opacity[i] = go;
+  }
+};
+
+// Sums the gradients of several views: the 3K colour sums in shared memory
+// (one column per thread of a 128-thread block, so a warp's accesses fall in
+// distinct banks), the rest in registers. Keeping the colour sums out of
+// registers lets four blocks share an SM without spills at K = 16.
+template <int K>
+struct SharedAccumulateGradients {
+  float (*c)[128];
+  int t;
+  float m[3], s[3], o;
+  float4 r;
+  __device__ __forceinline__ void zero() {
+#pragma unroll
+    for (int j = 0; j < K * 3; ++j) c[j][t] = 0.0f;
+    m[0] = m[1] = m[2] = s[0] = s[1] = s[2] = o = 0.0f;
+    r = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  }
+  __device__ __forceinline__ void color(const float (&g)[K * 3]) {
+#pragma unroll
+    for (int j = 0; j < K * 3; ++j) c[j][t] = c[j][t] + g[j];
+  }
+  __device__ __forceinline__ void rest(float gmx, float gmy, float gmz, float4 grot, float gsx,
+                                       float gsy, float gsz, float go) {
+    m[0] = m[0] + gmx; m[1] = m[1] + gmy; m[2] = m[2] + gmz;
+    r = make_float4(r.x + grot.x, r.y + grot.y, r.z + grot.z, r.w + grot.w);
+    s[0] = s[0] + gsx; s[1] = s[1] + gsy; s[2] = s[2] + gsz;
+    o = o + go;
+  }
+};
+
+// One view of gs_project_bwd_views as it lies in device memory: the
+// render's gs_params, then the camera rotation (row-major) and translation.
+struct ViewRecord {
+  gs_params p;
+  float R[9];
+  float t[3];
+};
+static_assert(sizeof(ViewRecord) == 29 * 4, "29 32-bit words per view");
+
+// Projection backward summed over views: each thread reads its Gaussian's
+// parameters once, recomputes each view's conic with the forward's
+// expressions, runs the single-view backward per view on that view's
+// screen-space gradient (grad_projected / counts: [views, n, ...]) and writes
+// the sum over views in view order. The views' cameras are read from device
+// memory, so a collective can deliver them without a host round trip. A view
+// where the Gaussian is not visible contributes zero, as in the single-view
+// backward.
+template <int K>
+__global__ void __launch_bounds__(128, K > 16 ? 3 : 4) project_bwd_views_kernel(
+    int64_t n, int num_views, const float* __restrict__ mean, const float* __restrict__ rotation,
+    const float* __restrict__ scale, const float* __restrict__ opacity,
+    const float* __restrict__ color, const ViewRecord* __restrict__ views,
+    const float* __restrict__ grad_projected, const int32_t* __restrict__ counts,
+    float* __restrict__ grad_mean, float* __restrict__ grad_rotation,
+    float* __restrict__ grad_scale, float* __restrict__ grad_opacity,
+    float* __restrict__ grad_color) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const GaussianTerms g = gaussian_terms(i, mean, rotation, scale, opacity);
+  const BwdTerms b = bwd_terms(i, mean, rotation, scale, opacity);
+  __shared__ float color_acc[K * 3][128];
+  SharedAccumulateGradients<K> acc{color_acc, static_cast<int>(threadIdx.x)};
+  acc.zero();
+  for (int v = 0; v < num_views; ++v) {
+    const int64_t o = static_cast<int64_t>(v) * n + i;
+    if (__ldg(counts + o) == 0) continue;
+    const gs_params p = views[v].p;
+    const float* R = views[v].R;
+    const float* t = views[v].t;
+    const Camera c{R[0], R[1], R[2], R[3], R[4], R[5], R[6], R[7], R[8], t[0], t[1], t[2]};
+    const float4 inv = view_conic(g, c, p);
+    project_bwd_view<K>(i, true, c, p, b, color, inv, grad_projected + 9 * o, acc);
+  }
+  float sum[K * 3];
+#pragma unroll
+  for (int j = 0; j < K * 3; ++j) sum[j] = color_acc[j][threadIdx.x];
+  StoreGradients<K> out{i, grad_mean, grad_rotation, grad_scale, grad_opacity, grad_color};
+  out.color(sum);
+  out.rest(acc.m[0], acc.m[1], acc.m[2], acc.r, acc.s[0], acc.s[1], acc.s[2], acc.o);
+}
+
+template <int K>
+__global__ void __launch_bounds__(128) project_bwd_kernel(
+    int64_t n, const float* __restrict__ mean, const float* __restrict__ rotation,
+    const float* __restrict__ scale, const float* __restrict__ opacity,
+    const float* __restrict__ color, const float* __restrict__ camera_rotation,
+    const float* __restrict__ camera_translation, const float* __restrict__ inverse_covariance,
+    const float* __restrict__ grad_projected, const int32_t* __restrict__ counts,
+    const gs_params p, float* __restrict__ grad_mean, float* __restrict__ grad_rotation,
+    float* __restrict__ grad_scale, float* __restrict__ grad_opacity,
+    float* __restrict__ grad_color) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const bool visible = __ldg(counts + i) != 0;
+  const Camera c = load_camera(camera_rotation, camera_translation);
+  const float4 inv = __ldg(reinterpret_cast<const float4*>(inverse_covariance) + i);
+  StoreGradients<K> sink{i, grad_mean, grad_rotation, grad_scale, grad_opacity, grad_color};
+  project_bwd_view<K>(i, visible, c, p, bwd_terms(i, mean, rotation, scale, opacity), color,
+                      inv, grad_projected + 9 * i, sink);
 }
 
 }  // namespace
@@ -679,6 +851,24 @@ int32_t launch_project_fwd_batch(int64_t n, int32_t num_sh, int32_t num_views, c
     GS_TRY(check_launch());
   }
   return GS_OK;
+}
+
+int32_t launch_project_bwd_views(int64_t n, int32_t num_sh, int32_t num_views,
+                                 const float* mean, const float* rotation, const float* scale,
+                                 const float* opacity, const float* color, const void* views,
+                                 const float* grad_projected, const int32_t* counts,
+                                 float* grad_mean, float* grad_rotation, float* grad_scale,
+                                 float* grad_opacity, float* grad_color, cudaStream_t stream) {
+  if (n == 0) return GS_OK;
+  const unsigned blocks = ceil_div(n, 128);
+#define GS_LAUNCH(K)                                                                          \
+  project_bwd_views_kernel<K><<<blocks, 128, 0, stream>>>(                                    \
+      n, num_views, mean, rotation, scale, opacity, color,                                    \
+      static_cast<const ViewRecord*>(views), grad_projected, counts, grad_mean, grad_rotation, \
+      grad_scale, grad_opacity, grad_color)
+  GS_SH_DISPATCH(num_sh, GS_LAUNCH)
+#undef GS_LAUNCH
+  return check_launch();
 }
 
 int32_t launch_project_bwd(int64_t n, int32_t num_sh, const float* mean, const float* rotation,

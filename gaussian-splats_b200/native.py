@@ -40,6 +40,7 @@ EXPORTED_SYMBOLS = (
     "gs_composite_fwd",
     "gs_composite_bwd",
     "gs_project_bwd",
+    "gs_project_bwd_views",
     "gs_adam_step",
     "gs_det_exp",
     "gs_det_log",
@@ -119,6 +120,27 @@ def adam_params(steps, lrs, betas, eps, noise_lr=0.0, position_lr=0.0) -> AdamPa
     return h
 
 
+VIEW_RECORD_WORDS = 29  # gs_params (17 words) + camera rotation (9) + translation (3)
+
+
+def view_record(params: Params, camera_rotation, camera_translation):
+    """The 29-word record of one view for ``gs_project_bwd_views``: the
+    render's ``gs_params`` bytes, then the camera rotation and translation as
+    float32 (an int32 tensor holding those bits), on the camera tensors'
+    device. For CUDA cameras the record is assembled on the device without a
+    host wait: the parameter words go up from pinned memory (non-blocking),
+    the camera words are concatenated on the device."""
+    import torch
+
+    device = camera_rotation.device
+    header = torch.empty(ctypes.sizeof(Params) // 4, dtype=torch.int32,
+                         pin_memory=device.type == "cuda")
+    ctypes.memmove(header.data_ptr(), ctypes.addressof(params), ctypes.sizeof(Params))
+    camera = torch.cat((camera_rotation.detach().reshape(9).float(),
+                        camera_translation.detach().reshape(3).to(device).float()))
+    return torch.cat((header.to(device, non_blocking=True), camera.view(torch.int32)))
+
+
 _lib = None
 
 
@@ -151,6 +173,7 @@ def lib() -> ctypes.CDLL:
         "gs_composite_fwd": ([vp] * 6 + [P] + [vp] * 3 + [vp], i32),
         "gs_composite_bwd": ([i64] + [vp] * 9 + [P, vp, vp], i32),
         "gs_project_bwd": ([i64, i32] + [vp] * 10 + [P] + [vp] * 5 + [vp], i32),
+        "gs_project_bwd_views": ([i64, i32, i32] + [vp] * 13 + [vp], i32),
         "gs_adam_step": ([i64, i32] + [ctypes.POINTER(SplatArrays)] * 4 +
                          [ctypes.POINTER(AdamParams), vp, vp], i32),
         "gs_det_exp": ([i64, vp, vp, vp], i32),

@@ -39,7 +39,7 @@ from typing import Literal
 
 import torch
 
-from . import native
+from . import native, view_parallel
 from .camera import Camera
 
 _OUTPUTS = 10
@@ -336,13 +336,29 @@ def _backward(ctx, *grad_outputs):
         grad_rotation, grad_color, grad_mean, grad_scale, grad_opacity = _carve(
             mean.new_empty((n * (11 + 3 * num_sh),)), n,
             ((4,), (num_sh, 3), (3,), (3,), (1,)))
-        _mark("begin:project_bwd")
-        native.check(lib.gs_project_bwd(
-            n, num_sh, _ptr(mean), _ptr(rotation), _ptr(scale), _ptr(opacity), _ptr(color),
-            _ptr(camera_rotation), _ptr(camera_translation), _ptr(inverse_covariance),
-            _ptr(grad_projected), _ptr(counts), pref, _ptr(grad_mean), _ptr(grad_rotation),
-            _ptr(grad_scale), _ptr(grad_opacity), _ptr(grad_color), stream), "gs_project_bwd")
-        _mark("project_bwd")
+        group = view_parallel.active_exchange()
+        if group is not None:
+            # View-parallel step: gather every rank's screen-space gradient
+            # and camera, and sum the projection backward over all views.
+            record = native.view_record(params, camera_rotation, camera_translation)
+            all_gp, all_counts, all_views = view_parallel.exchange_screen_gradients(
+                grad_projected, counts, record, group)
+            _mark("begin:project_bwd")
+            native.check(lib.gs_project_bwd_views(
+                n, num_sh, all_views.shape[0], _ptr(mean), _ptr(rotation), _ptr(scale),
+                _ptr(opacity), _ptr(color), _ptr(all_views), _ptr(all_gp), _ptr(all_counts),
+                _ptr(grad_mean), _ptr(grad_rotation), _ptr(grad_scale), _ptr(grad_opacity),
+                _ptr(grad_color), stream), "gs_project_bwd_views")
+            _mark("project_bwd")
+        else:
+            _mark("begin:project_bwd")
+            native.check(lib.gs_project_bwd(
+                n, num_sh, _ptr(mean), _ptr(rotation), _ptr(scale), _ptr(opacity), _ptr(color),
+                _ptr(camera_rotation), _ptr(camera_translation), _ptr(inverse_covariance),
+                _ptr(grad_projected), _ptr(counts), pref, _ptr(grad_mean), _ptr(grad_rotation),
+                _ptr(grad_scale), _ptr(grad_opacity), _ptr(grad_color), stream),
+                "gs_project_bwd")
+            _mark("project_bwd")
     gradients = (grad_mean, grad_rotation, grad_scale, grad_opacity, grad_color)
     return (*gradients, *(None,) * (19 - len(gradients)))
 

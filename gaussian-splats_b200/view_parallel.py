@@ -12,6 +12,7 @@ that buffer (no packing copy).
 
 from __future__ import annotations
 
+import contextlib
 import datetime
 import os
 from collections.abc import Callable, Sequence
@@ -20,6 +21,69 @@ import torch
 import torch.distributed as dist
 
 PARAMETER_NAMES = ("mean", "rotation", "scale", "opacity", "color")
+
+# The group of the enclosing screen_space_exchange. Process-wide rather than
+# thread-local: autograd runs CUDA backward functions on its own device
+# thread, not on the thread that entered the context and called backward().
+_EXCHANGE_GROUP = None
+
+
+@contextlib.contextmanager
+def screen_space_exchange(group=None):
+    """Inside this context the rasterizer's backward returns the parameter
+    gradients summed over every rank's view, computed without exchanging them.
+
+    Each rank all-gathers the other ranks' screen-space gradients -- the 9
+    floats per Gaussian that compositing backward produces -- with their tile
+    counts and cameras, and runs one projection backward over all views
+    (``gs_project_bwd_views``: parameters read once, each view's conic
+    recomputed). That moves 40 bytes per Gaussian per rank instead of the 236
+    bytes of parameter gradients an all-reduce moves at SH degree 3, for one
+    extra pass of cheap per-view arithmetic.
+
+    Preconditions: every rank runs the rasterizer's backward the same number
+    of times inside the context (once per step in ``train_step``), and the
+    loss reaches the Gaussian parameters only through rendered images (a
+    regulariser on the parameters themselves would stay rank-local).
+    """
+    global _EXCHANGE_GROUP
+    previous = _EXCHANGE_GROUP
+    _EXCHANGE_GROUP = group if group is not None else dist.group.WORLD
+    try:
+        yield
+    finally:
+        _EXCHANGE_GROUP = previous
+
+
+def active_exchange():
+    """The process group of the enclosing :func:`screen_space_exchange`, or None."""
+    group = _EXCHANGE_GROUP
+    if group is None or not dist.is_initialized():
+        return None
+    return group
+
+
+def exchange_screen_gradients(grad_projected: torch.Tensor, counts: torch.Tensor,
+                              record: torch.Tensor, group) -> tuple[torch.Tensor, ...]:
+    """All-gather every rank's screen-space gradient [N, 9], tile counts [N]
+    and 29-word view record; returns ([W, N, 9], [W, N], [W, 29]) on the
+    gradients' device, in rank order."""
+    world = dist.get_world_size(group)
+    device = grad_projected.device
+    n = grad_projected.shape[0]
+    all_gp = grad_projected.new_empty((world, n, 9))
+    all_counts = counts.new_empty((world, n))
+    all_views = torch.empty((world, record.numel()), dtype=torch.int32, device=device)
+    local_view = record.to(device).contiguous()
+    # Three collectives, not one coalesced group: the tensors differ in dtype.
+    works = [dist.all_gather_into_tensor(all_gp, grad_projected.contiguous(), group=group,
+                                         async_op=True),
+             dist.all_gather_into_tensor(all_counts, counts.contiguous(), group=group,
+                                         async_op=True),
+             dist.all_gather_into_tensor(all_views, local_view, group=group, async_op=True)]
+    for work in works:
+        work.wait()
+    return all_gp, all_counts, all_views
 
 
 def shard_views(num_views: int, world_size: int, rank: int) -> list[int]:
@@ -107,22 +171,32 @@ def train_step(
     render: Callable,
     loss_fn: Callable[[torch.Tensor, torch.Tensor], torch.Tensor],
     group=None,
+    screen_exchange: bool = False,
 ) -> torch.Tensor:
-    """Forward + backward of this rank's views, then the gradient all-reduce.
+    """Forward + backward of this rank's views, then the gradient exchange.
 
     ``render(splats, camera)`` returns an image; ``loss_fn(image, target)`` a
     scalar. Gradients of ``parameters`` start from None, accumulate over this
-    rank's views and are summed over ranks. Returns this rank's summed loss (a
-    device tensor; no host sync).
+    rank's views and are summed over ranks: by all-reducing them, or, with
+    ``screen_exchange`` (one view per rank, image losses only; see
+    :func:`screen_space_exchange`), inside the rasterizer's backward. Returns
+    this rank's summed loss (a device tensor; no host sync).
     """
     for p in parameters:
         p.grad = None
+    distributed = dist.is_initialized() and dist.get_world_size(group) > 1
+    if screen_exchange and distributed and len(cameras) != 1:
+        raise ValueError("screen_exchange needs exactly one view per rank and step")
+    exchange = screen_space_exchange(group) if screen_exchange and distributed \
+        else contextlib.nullcontext()
     total = None
     for camera, target in zip(cameras, targets):
         loss = loss_fn(render(splats, camera), target)
-        loss.backward()
+        with exchange:
+            loss.backward()
         total = loss.detach() if total is None else total + loss.detach()
-    all_reduce_gradients(parameters, group)
+    if not (screen_exchange and distributed):
+        all_reduce_gradients(parameters, group)
     if total is None:
         total = torch.zeros((), device=parameters[0].device)
     return total

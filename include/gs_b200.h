@@ -193,6 +193,26 @@ int32_t gs_project_bwd(int64_t n, int32_t num_sh, const float *mean, const float
                        float *grad_rotation, float *grad_scale, float *grad_opacity,
                        float *grad_color, gs_stream_t stream);
 
+/* Projection backward summed over several views (no counterpart in the
+ * reference): the parameter gradients of sum_v (rasterize(view v) . grad_v),
+ * given each view's screen-space gradient grad_projected [V,N,9] (what
+ * gs_composite_bwd writes) and tile counts [V,N]. Each thread reads its
+ * Gaussian's parameters once, recomputes each view's conic exactly as
+ * gs_project_fwd computed it, and adds the per-view gradients of
+ * gs_project_bwd in view order. `views` is a DEVICE array of V records of 29
+ * 32-bit words: the view's gs_params (its 17 words as laid out above), the
+ * camera rotation (9 floats, row-major) and translation (3 floats) -- so a
+ * collective can deliver them without a host round trip. For view-parallel
+ * training this replaces all-reducing the parameter gradients (59 floats per
+ * Gaussian at SH degree 3) with all-gathering the screen-space ones (9 floats
+ * and a count). */
+int32_t gs_project_bwd_views(int64_t n, int32_t num_sh, int32_t num_views, const float *mean,
+                             const float *rotation, const float *scale, const float *opacity,
+                             const float *color, const void *views, const float *grad_projected,
+                             const int32_t *counts, float *grad_mean, float *grad_rotation,
+                             float *grad_scale, float *grad_opacity, float *grad_color,
+                             gs_stream_t stream);
+
 /* Binning error word of a count workspace (0 = fine, else some device-side
  * bounded wait in the last gs_bin_count / gs_bin_sort on these workspaces
  * gave up). Synchronises `stream`. */

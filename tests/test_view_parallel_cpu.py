@@ -128,3 +128,48 @@ def test_flat_all_reduce_of_views():
     for rank in range(world):
         first, second, in_place = results[rank]
         assert first == 20 * 3.0 and second == 15 * 3.0 and in_place
+
+
+def test_view_record_layout():
+    import ctypes
+
+    from gaussian_splats_b200 import native
+
+    params = native.make_params(500.0, 510.0, 320.0, 240.0, 640, 480, 16, 0.999, 0.2, 100.0,
+                                "gaussian", 0.95)
+    R = torch.arange(9, dtype=torch.float32).reshape(3, 3)
+    t = torch.tensor([1.5, -2.0, 3.25])
+    words = native.view_record(params, R, t)
+    assert words.dtype == torch.int32 and words.numel() == native.VIEW_RECORD_WORDS == 29
+    assert ctypes.sizeof(native.Params) == 17 * 4
+    back = native.Params.from_buffer_copy(words[:17].numpy().tobytes())
+    assert (back.fx, back.width, back.tile_size, back.opacity_threshold) == \
+        (params.fx, params.width, params.tile_size, params.opacity_threshold)
+    assert torch.equal(words[17:].view(torch.float32), torch.cat((R.reshape(9), t)))
+
+
+def test_screen_exchange_needs_one_view(monkeypatch):
+    monkeypatch.setattr(dist, "is_initialized", lambda: True)
+    monkeypatch.setattr(dist, "get_world_size", lambda group=None: 2)
+    params = [torch.zeros(3, requires_grad=True)]
+    with pytest.raises(ValueError, match="one view"):
+        train_step(None, [1, 2], [0, 0], params, lambda s, c: params[0].sum(),
+                   lambda image, t: image, screen_exchange=True)
+
+
+def test_screen_exchange_is_seen_from_other_threads(monkeypatch):
+    # autograd runs CUDA backward functions on its own device thread, so the
+    # context set on the caller's thread must be visible there
+    import threading
+
+    from gaussian_splats_b200 import view_parallel
+
+    monkeypatch.setattr(dist, "is_initialized", lambda: True)
+    group = object()
+    seen = []
+    with view_parallel.screen_space_exchange(group):
+        worker = threading.Thread(target=lambda: seen.append(view_parallel.active_exchange()))
+        worker.start()
+        worker.join()
+    assert seen == [group]
+    assert view_parallel.active_exchange() is None
