@@ -95,6 +95,9 @@ def parse_args():
     p.add_argument("--points", type=int, default=None,
                    help="override the config's Gaussian count (smaller smoke runs)")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--exchange", choices=("auto", "screen", "all-reduce"), default="auto",
+                   help="how ranks sum gradients with one view per rank (auto: "
+                        "view_parallel.screen_exchange_pays)")
     return p.parse_args()
 
 
@@ -551,6 +554,7 @@ def main():
     device = torch.device("cuda", local_rank)
     from gaussian_splats_b200.rasterize import StageTimer, rasterize_batch, rasterize_outputs
     from gaussian_splats_b200.splats import GaussianSplat
+    from gaussian_splats_b200.view_parallel import screen_exchange_pays
     from gaussian_splats_b200.view_parallel import train_step as vp_train_step
 
     workload = WORKLOADS[args.config]
@@ -595,10 +599,12 @@ def main():
                 settings.opacity_threshold, settings.near, settings.far)]
         return images
 
-    # One view per rank: the ranks exchange screen-space gradients and each
-    # sums the projection backward over all views (view_parallel); several
-    # views per rank: the parameter gradients are all-reduced once per step.
-    screen = world > 1 and len(cameras) == 1
+    # One view per rank: the ranks can exchange screen-space gradients, each
+    # summing the projection backward over all views (view_parallel), where
+    # that beats all-reducing the parameter gradients; several views per rank:
+    # the parameter gradients are all-reduced once per step.
+    screen = world > 1 and len(cameras) == 1 and (
+        args.exchange == "screen" or (args.exchange == "auto" and screen_exchange_pays(world)))
 
     def train_step():
         return vp_train_step(splats, cameras, targets, trainable,

@@ -63,6 +63,21 @@ def active_exchange():
     return group
 
 
+# Largest world size at which the screen-space exchange beats the all-reduce
+# for one view per rank. At 1M Gaussians, SH3, on B200 + NVLink 5: the
+# all-reduce moves 236 MB (0.47 ms at 2 GPUs, 0.63 ms at 4); the exchange
+# all-gathers 40 MB per rank and grows the projection backward by ~55 us per
+# extra view (0.10 ms at 2 views, 0.20 ms at 4, 0.42 ms at 8), so at 8 ranks
+# its W-fold gather plus that arithmetic overtakes the all-reduce.
+SCREEN_EXCHANGE_MAX_WORLD = 4
+
+
+def screen_exchange_pays(world_size: int) -> bool:
+    """Whether ``train_step`` with one view per rank should use the
+    screen-space exchange rather than the parameter-gradient all-reduce."""
+    return 1 < world_size <= SCREEN_EXCHANGE_MAX_WORLD
+
+
 def exchange_screen_gradients(grad_projected: torch.Tensor, counts: torch.Tensor,
                               record: torch.Tensor, group) -> tuple[torch.Tensor, ...]:
     """All-gather every rank's screen-space gradient [N, 9], tile counts [N]

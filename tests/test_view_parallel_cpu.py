@@ -173,3 +173,9 @@ def test_screen_exchange_is_seen_from_other_threads(monkeypatch):
         worker.join()
     assert seen == [group]
     assert view_parallel.active_exchange() is None
+
+
+def test_screen_exchange_choice():
+    from gaussian_splats_b200.view_parallel import screen_exchange_pays
+
+    assert [screen_exchange_pays(w) for w in (1, 2, 4, 8)] == [False, True, True, False]
