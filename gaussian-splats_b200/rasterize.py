@@ -72,6 +72,18 @@ def _f32(t: torch.Tensor) -> torch.Tensor:
     return t.detach().to(torch.float32).contiguous()
 
 
+def _to_device(t: torch.Tensor, device: torch.device) -> torch.Tensor:
+    """``t`` on ``device``. A host tensor goes up through pinned memory with a
+    non-blocking copy: a plain ``.to`` from pageable memory synchronises the
+    stream, so the host would wait for all queued GPU work on every render and
+    the GPU would then idle while the next kernels are launched."""
+    if t.device == device or device.type != "cuda" or t.requires_grad:
+        return t.to(device)
+    staged = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+    staged.copy_(t)
+    return staged.to(device, non_blocking=True)
+
+
 class StageTimer:
     """Records a CUDA event on the launching stream after each stage.
 
@@ -394,7 +406,8 @@ def rasterize_outputs(
         )
     return torch.ops.gaussian_splats.rasterize(
         mean, rotation, scale, opacity, color,
-        camera.rotation_matrix.to(mean.device), camera.translation.to(mean.device),
+        _to_device(camera.rotation_matrix, mean.device),
+        _to_device(camera.translation, mean.device),
         float(fx), float(fy), float(cx), float(cy), int(image_width), int(image_height),
         int(tile_size), float(opacity_threshold), float(near), float(far), rendering_mode,
         float(confidence),
