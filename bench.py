@@ -515,6 +515,96 @@ def optimizer_timings(params, grads, device, repeats=5):
     return result
 
 
+DEAD_FRACTION = 0.03  # rows made dead for the relocation timing
+
+
+def relocation_timings(params, device, repeats=3):
+    """Milliseconds of one splat relocation as the reference's training loop
+    runs it once the count has reached max_splats (density factor 1.0: dead
+    rows replaced by copies of live ones sampled by opacity, the Adam moments
+    of every touched row zeroed): gaussian_splats_b200.relocate with FusedAdam
+    state, and for comparison the reference's tensor ops (training/utils.py:
+    83-193, restated with torch) on torch.optim.Adam state. The parameters are
+    these, with a seeded DEAD_FRACTION of rows given opacity logit -8. Both
+    draw the same copies (same seed). CUDA events around the whole call (its
+    host waits included), after a 1 GiB L2 flush; mean over ``repeats``."""
+    import math
+
+    from gaussian_splats_b200 import relocate as R
+    from gaussian_splats_b200.optim import GROUP_NAMES, FusedAdam
+    from gaussian_splats_b200.splats import GaussianSplat
+
+    n = len(params[0])
+    order = torch.randperm(n, generator=torch.Generator().manual_seed(77))
+    dead_rows = order[: int(DEAD_FRACTION * n)].to(device)
+    degree = torch.arange(1, 52, device=device)
+    table = torch.tensor([[math.comb(m, d) if d <= m else 0 for d in range(1, 52)]
+                          for m in range(52)], dtype=torch.float32, device=device)
+    table = table * ((-1.0) ** (degree - 1) / degree.sqrt())
+
+    def fresh(optimizer_class):
+        tensors = [p.detach().clone() for p in params]
+        tensors[3][dead_rows] = -8.0
+        splats = GaussianSplat.from_tensors(*tensors)
+        opt = optimizer_class([{"params": [getattr(splats, k)], "name": k, "lr": 1e-3}
+                               for k in GROUP_NAMES], eps=1e-15)
+        for k in GROUP_NAMES:
+            p = getattr(splats, k)
+            opt.state[p] = {"step": torch.tensor(1.0), "exp_avg": torch.full_like(p, 0.1),
+                            "exp_avg_sq": torch.full_like(p, 0.01)}
+        return splats, opt
+
+    @torch.no_grad()
+    def torch_relocate(splats, opt):
+        opacity = splats.opacity.sigmoid().squeeze(-1)
+        dead_mask = opacity < 0.005
+        dead = dead_mask.nonzero().squeeze(-1)
+        drawn = torch.multinomial(opacity.masked_fill(dead_mask, 0), len(dead), replacement=True)
+        counts = torch.bincount(drawn, minlength=n).cpu()
+        parent_rows = counts.nonzero().squeeze(-1)
+        copies = counts[parent_rows].to(device)
+        parent_rows = parent_rows.to(device)
+        source = parent_rows.repeat_interleave(copies)
+        o = opacity[parent_rows]
+        total = (copies + 1).clamp(1, 51)
+        o_new = 1 - (1 - o).pow(1 / total)
+        series = table[total] * o_new[:, None].pow(degree) * (degree <= total[:, None])
+        s_new = splats.scale[parent_rows].exp() * (o / series.sum(-1))[:, None]
+        o_new = o_new.clamp(0.005, 1 - 1e-6)
+        for name in ("mean", "rotation", "color", "normals"):
+            value = getattr(splats, name)
+            value.index_copy_(0, dead, value[source])
+        splats.opacity.index_copy_(0, parent_rows, torch.logit(o_new)[:, None])
+        splats.opacity.index_copy_(0, dead, torch.logit(o_new.repeat_interleave(copies))[:, None])
+        splats.scale.index_copy_(0, parent_rows, s_new.log())
+        splats.scale.index_copy_(0, dead, s_new.repeat_interleave(copies, dim=0).log())
+        rows = torch.cat((parent_rows, dead)).unique()
+        for state in opt.state.values():
+            for key in ("exp_avg", "exp_avg_sq"):
+                state[key][rows] = 0
+
+    flush = torch.empty(1 << 28, dtype=torch.float32, device=device)
+    result = {}
+    for name, optimizer_class, fn in (
+            ("fused", FusedAdam, lambda s, o: R.relocate_splats(s, o, 1.0)),
+            ("torch", torch.optim.Adam, torch_relocate)):
+        times = []
+        for _ in range(repeats + 1):  # the first run warms up
+            splats, opt = fresh(optimizer_class)
+            flush.zero_()
+            torch.manual_seed(2024)
+            before, after = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            before.record()
+            fn(splats, opt)
+            after.record()
+            torch.cuda.synchronize()
+            times.append(before.elapsed_time(after))
+            del splats, opt
+        result[name] = sum(times[1:]) / repeats
+    result["dead_rows"] = len(dead_rows)
+    return result
+
+
 BATCH_VIEWS = 16  # cameras per rasterize_batch call in forward-only multi-camera configs
 
 
@@ -672,6 +762,7 @@ def main():
     if backward:
         train_step()  # leaves this rank's summed, all-reduced gradients in .grad
         optimizer_ms = optimizer_timings(trainable, [p.grad for p in trainable], device)
+        relocation_ms = relocation_timings(trainable, device)
 
     # End to end through the public API with host buffers: each step copies the
     # Gaussian parameters and this rank's targets from pinned host memory,
@@ -762,6 +853,12 @@ def main():
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s",
                          "frac": gbs / hbm_peak, "algorithmic_bytes": n * optimizer_bytes(k),
                          "note": f"peak: {peak_kind} hbm_gbs (MEASURED_PEAKS.json)"},
+            "relocation": {
+                "fused_ms": relocation_ms["fused"], "torch_ms": relocation_ms["torch"],
+                "dead_rows": relocation_ms["dead_rows"],
+                "note": "relocate_splats at density 1.0 (dead rows replaced, moments reset), "
+                        "FusedAdam state; torch = the reference's tensor ops; every 100 steps "
+                        "in the reference's loop"},
             "note": "one training-loop optimizer step (Adam over the five parameter groups + "
                     "position noise), not part of the timed fwd+bwd step"}
     per_view = len(cameras)

@@ -42,6 +42,11 @@ int32_t launch_composite_bwd(int64_t, const float*, const float*, const float*, 
 int32_t launch_adam_step(int64_t, int32_t, const gs_splat_arrays&, const gs_splat_arrays&,
                          const gs_splat_arrays&, const gs_splat_arrays&, const gs_adam_params&,
                          const float*, cudaStream_t);
+size_t relocate_workspace_size(int64_t);
+int32_t launch_relocate(int64_t, int64_t, int32_t, const int64_t*, int64_t, const int64_t*,
+                        int64_t, const gs_splat_arrays&, float*, const gs_splat_arrays*,
+                        const gs_splat_arrays*, void*, size_t, cudaStream_t);
+int32_t relocate_status(const void*, cudaStream_t);
 
 namespace {
 thread_local int32_t g_last_cuda_error = 0;
@@ -267,6 +272,39 @@ int32_t gs_project_bwd_views(int64_t n, int32_t num_sh, int32_t num_views, const
   return gs::launch_project_bwd_views(n, num_sh, num_views, mean, rotation, scale, opacity, color,
                                       views, grad_projected, counts, grad_mean, grad_rotation,
                                       grad_scale, grad_opacity, grad_color, as_cuda(stream));
+}
+
+uint64_t gs_relocate_workspace_size(int64_t n_src) {
+  return n_src < 0 ? 0 : gs::relocate_workspace_size(n_src);
+}
+
+int32_t gs_relocate(int64_t n_src, int64_t n_rows, int32_t num_sh, const int64_t* counts,
+                    int64_t num_outputs, const int64_t* output_indices, int64_t output_base,
+                    const gs_splat_arrays* splats, float* normals, const gs_splat_arrays* exp_avg,
+                    const gs_splat_arrays* exp_avg_sq, void* workspace, uint64_t workspace_size,
+                    gs_stream_t stream) {
+  if (!splats || !workspace || (n_src > 0 && !counts)) return GS_ERR_INVALID_ARGUMENT;
+  if (n_src < 0 || n_rows < n_src || n_rows >= gs::kMaxGaussians || num_outputs < 0)
+    return GS_ERR_INVALID_ARGUMENT;
+  if (!output_indices &&
+      (num_outputs > 0 && (output_base < 0 || output_base > n_rows - num_outputs)))
+    return GS_ERR_INVALID_ARGUMENT;
+  if (!gs::valid_sh(num_sh)) return num_sh > 25 ? GS_ERR_UNSUPPORTED : GS_ERR_INVALID_ARGUMENT;
+  if (!splats->mean || !splats->rotation || !splats->scale || !splats->opacity || !splats->color)
+    return GS_ERR_INVALID_ARGUMENT;
+  if (!gs::aligned(splats->rotation, 16) || !gs::aligned(workspace, 16) ||
+      !gs::aligned(counts, 8) || !gs::aligned(output_indices, 8))
+    return GS_ERR_MISALIGNED;
+  for (const gs_splat_arrays* m : {exp_avg, exp_avg_sq})
+    if (m && m->rotation && !gs::aligned(m->rotation, 16)) return GS_ERR_MISALIGNED;
+  return gs::launch_relocate(n_src, n_rows, num_sh, counts, num_outputs, output_indices,
+                             output_base, *splats, normals, exp_avg, exp_avg_sq, workspace,
+                             workspace_size, as_cuda(stream));
+}
+
+int32_t gs_relocate_status(const void* workspace, gs_stream_t stream) {
+  if (!workspace) return GS_ERR_INVALID_ARGUMENT;
+  return gs::relocate_status(workspace, as_cuda(stream));
 }
 
 int32_t gs_det_exp(int64_t n, const float* x, float* y, gs_stream_t stream) {

@@ -42,6 +42,9 @@ EXPORTED_SYMBOLS = (
     "gs_project_bwd",
     "gs_project_bwd_views",
     "gs_adam_step",
+    "gs_relocate",
+    "gs_relocate_status",
+    "gs_relocate_workspace_size",
     "gs_det_exp",
     "gs_det_log",
 )
@@ -176,6 +179,11 @@ def lib() -> ctypes.CDLL:
         "gs_project_bwd_views": ([i64, i32, i32] + [vp] * 13 + [vp], i32),
         "gs_adam_step": ([i64, i32] + [ctypes.POINTER(SplatArrays)] * 4 +
                          [ctypes.POINTER(AdamParams), vp, vp], i32),
+        "gs_relocate": ([i64, i64, i32, vp, i64, vp, i64, ctypes.POINTER(SplatArrays), vp,
+                         ctypes.POINTER(SplatArrays), ctypes.POINTER(SplatArrays), vp,
+                         ctypes.c_uint64, vp], i32),
+        "gs_relocate_status": ([vp, vp], i32),
+        "gs_relocate_workspace_size": ([i64], ctypes.c_uint64),
         "gs_det_exp": ([i64, vp, vp, vp], i32),
         "gs_det_log": ([i64, vp, vp, vp], i32),
     }

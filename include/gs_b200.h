@@ -253,6 +253,37 @@ int32_t gs_adam_step(int64_t n, int32_t num_sh, const gs_splat_arrays *params,
                      const gs_splat_arrays *exp_avg_sq, const gs_adam_params *hyper,
                      const float *randn, gs_stream_t stream);
 
+/* Workspace bytes gs_relocate needs for `n_src` counts (16-byte aligned). */
+uint64_t gs_relocate_workspace_size(int64_t n_src);
+
+/* Splat relocation: replaces copy_splats (training/utils.py:120-145) with its
+ * normalize_copies (training/utils.py:94-101), and the Adam-moment reset of
+ * relocate_splats (training/utils.py:187-193), in one pass. `counts` [n_src]
+ * (int64, what sample_counts draws) gives each parent row's number of copies;
+ * they must add up to `num_outputs`. Output slot j goes to row
+ * output_indices[j] (int64), or output_base + j when output_indices is NULL,
+ * and receives a copy of the parent whose run of counts covers j, parents in
+ * index order (parents.repeat_interleave(copies)). Each parent and its copies
+ * get the renormalised opacity logit and log scale of normalize_copies with
+ * copies = count + 1 (clamped to 51), computed in double precision; mean,
+ * rotation, colour and `normals` (may be NULL) are copied. Moment rows of the
+ * parents and outputs are zeroed in `exp_avg` / `exp_avg_sq` (either set, or
+ * any member, may be NULL). Rows are those of `splats` (n_rows >= n_src);
+ * output rows must be distinct and not parents (as sampled in the reference:
+ * parents have opacity >= 0.005, outputs are dead or new rows). Bad counts or
+ * output rows are skipped and recorded; gs_relocate_status reports them.
+ * rotation arrays 16-byte aligned. */
+int32_t gs_relocate(int64_t n_src, int64_t n_rows, int32_t num_sh, const int64_t *counts,
+                    int64_t num_outputs, const int64_t *output_indices, int64_t output_base,
+                    const gs_splat_arrays *splats, float *normals, const gs_splat_arrays *exp_avg,
+                    const gs_splat_arrays *exp_avg_sq, void *workspace, uint64_t workspace_size,
+                    gs_stream_t stream);
+
+/* GS_OK, or GS_ERR_INVALID_ARGUMENT if the last gs_relocate on this
+ * workspace met negative counts, counts not adding up to num_outputs, or an
+ * output row outside [0, n_rows). Synchronises `stream`. */
+int32_t gs_relocate_status(const void *workspace, gs_stream_t stream);
+
 /* The deterministic exp / log the kernels use, applied elementwise (test hook
  * for bitwise agreement with the CPU oracle). */
 int32_t gs_det_exp(int64_t n, const float *x, float *y, gs_stream_t stream);

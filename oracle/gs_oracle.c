@@ -11,6 +11,9 @@
  *   gso_project_bwd   project_bwd.py:8-334    (parameter VJPs)
  *   gso_adam_step     training/train.py:118,151 + training/utils.py:50-62
  *                                             (torch Adam step, position noise)
+ *   gso_relocate      training/utils.py:94-101,120-145,187-193
+ *                                             (copy_splats with normalize_copies,
+ *                                              moment reset of relocate_splats)
  * Each function follows the reference's float32 operation order (no fused
  * multiply-adds unless written as fmaf) so that integer decisions match the
  * CUDA kernels bit for bit; exp/log come from detmath.h. Only tests, the
@@ -759,6 +762,86 @@ void gso_adam_step(int64_t n, int32_t num_sh, float *const *params, const float 
             params[0][3 * i + a] = params[0][3 * i + a] + shift;
         }
     }
+}
+
+/* Relocation (training/utils.py:120-145 with :94-101 and the moment reset of
+ * :187-193). Parents in index order take consecutive output slots
+ * (parents.repeat_interleave(copies)); slot j writes row output_indices[j], or
+ * output_base + j when output_indices is NULL. normalize_copies with copies =
+ * count + 1 clamped to 51: o' = 1 - (1 - o)^(1/copies), sum = sum over d of
+ * C(copies, d) (-1)^(d-1) o'^d / sqrt(d), scale' = scale o / sum, opacity' =
+ * clamp(o', 0.005, 1 - 1e-6) -- evaluated in double, each output rounded to
+ * float once (the reference chains float32 operations; its results differ
+ * from these by its rounding). moments[10] = exp_avg then exp_avg_sq of mean,
+ * rotation, scale, opacity, colour (NULL entries skipped). Returns error bits:
+ * 1 negative count, 2 counts not adding up to num_outputs, 4 output row out
+ * of range (those slots are skipped). */
+static void zero_moment_row(float *const *moments, int64_t row, int32_t num_sh) {
+  static const int widths[5] = {3, 4, 3, 1, 0};
+  for (int set = 0; set < 2; ++set)
+    for (int k = 0; k < 5; ++k) {
+      float *m = moments[5 * set + k];
+      if (!m) continue;
+      const int w = k == 4 ? 3 * num_sh : widths[k];
+      for (int e = 0; e < w; ++e) m[row * w + e] = 0.0f;
+    }
+}
+
+int gso_relocate(int64_t n_src, int64_t n_rows, int32_t num_sh, const int64_t *counts,
+                 int64_t num_outputs, const int64_t *output_indices, int64_t output_base,
+                 float *mean, float *rotation, float *scale, float *opacity, float *color,
+                 float *normals, float *const *moments) {
+  int error = 0;
+  int64_t total = 0;
+  for (int64_t i = 0; i < n_src; ++i) {
+    if (counts[i] < 0) error |= 1;
+    total += counts[i] > 0 ? counts[i] : 0;
+  }
+  if (total != num_outputs) error |= 2;
+  const int w = 3 * num_sh;
+  int64_t slot = 0;
+  for (int64_t parent = 0; parent < n_src; ++parent) {
+    const int64_t count = counts[parent] > 0 ? counts[parent] : 0;
+    if (count == 0) continue;
+    const int copies = count + 1 < 51 ? (int)(count + 1) : 51;
+    const double o = 1.0 / (1.0 + exp(-(double)opacity[parent]));
+    const double new_opacity = 1.0 - pow(1.0 - o, 1.0 / copies);
+    double sum = 0.0, binomial = 1.0, power = 1.0;
+    for (int d = 1; d <= copies; ++d) {
+      binomial = binomial * (copies - d + 1) / d;
+      power = power * new_opacity;
+      const double term = binomial * power / sqrt((double)d);
+      sum = (d & 1) ? sum + term : sum - term;
+    }
+    const double ratio = o / sum;
+    const double p = fmin(fmax(new_opacity, (double)0.005f), (double)(float)(1.0 - 1e-6));
+    const float logit = (float)log(p / (1.0 - p));
+    float log_scale[3];
+    for (int a = 0; a < 3; ++a) log_scale[a] = (float)log(exp((double)scale[3 * parent + a]) * ratio);
+    for (int64_t j = slot; j < slot + count; ++j) {
+      if (j >= num_outputs) {
+        error |= 2;
+        break;
+      }
+      const int64_t row = output_indices ? output_indices[j] : output_base + j;
+      if (row < 0 || row >= n_rows) {
+        error |= 4;
+        continue;
+      }
+      memcpy(mean + 3 * row, mean + 3 * parent, 3 * sizeof(float));
+      memcpy(rotation + 4 * row, rotation + 4 * parent, 4 * sizeof(float));
+      memcpy(color + row * w, color + parent * w, (size_t)w * sizeof(float));
+      if (normals) memcpy(normals + 3 * row, normals + 3 * parent, 3 * sizeof(float));
+      opacity[row] = logit;
+      for (int a = 0; a < 3; ++a) scale[3 * row + a] = log_scale[a];
+      zero_moment_row(moments, row, num_sh);
+    }
+    slot += count;
+    opacity[parent] = logit;
+    for (int a = 0; a < 3; ++a) scale[3 * parent + a] = log_scale[a];
+    zero_moment_row(moments, parent, num_sh);
+  }
+  return error;
 }
 
 void gso_exp_array(int64_t n, const float *x, float *y) { for (int64_t i = 0; i < n; ++i) y[i] = gso_exp(x[i]); }

@@ -75,6 +75,10 @@ def lib() -> ctypes.CDLL:
         ptr5 = ctypes.c_void_p * 5
         _lib.gso_adam_step.argtypes = [i64, i32, ptr5, ptr5, ptr5, ptr5,
                                        ctypes.POINTER(AdamParams), ctypes.c_void_p]
+        _lib.gso_relocate.argtypes = [i64, i64, i32, ctypes.c_void_p, i64, ctypes.c_void_p, i64,
+                                      _f32p, _f32p, _f32p, _f32p, _f32p, ctypes.c_void_p,
+                                      ctypes.c_void_p * 10]
+        _lib.gso_relocate.restype = ctypes.c_int
         _lib.gso_exp_array.argtypes = [i64, _f32p, _f32p]
         _lib.gso_log_array.argtypes = [i64, _f32p, _f32p]
     return _lib
@@ -329,3 +333,32 @@ def adam_step(params: dict, grads: dict, exp_avg: dict, exp_avg_sq: dict, hyper:
                         addr(out["exp_avg_sq"]), ctypes.byref(hyper),
                         None if r is None else r.ctypes.data)
     return out
+
+
+def relocate(state: dict, counts, output_indices=None, output_base: int = 0,
+             exp_avg: dict | None = None, exp_avg_sq: dict | None = None) -> dict:
+    """copy_splats + normalize_copies + the moment reset of relocate_splats
+    (training/utils.py:94-101,120-145,187-193) on copies of the float32 arrays.
+
+    ``state`` holds mean, rotation, scale, opacity, color and optionally
+    normals (all rows, including the output rows); ``counts`` [n_src] int64;
+    output slot j writes row ``output_indices[j]`` or ``output_base + j``.
+    Returns {"state", "exp_avg", "exp_avg_sq", "error"} (error bits as
+    gso_relocate returns them)."""
+    out = {k: np.array(v, dtype=np.float32, copy=True) for k, v in state.items()}
+    moments = [None if m is None else {k: np.array(v, dtype=np.float32, copy=True)
+                                       for k, v in m.items()} for m in (exp_avg, exp_avg_sq)]
+    counts = np.ascontiguousarray(counts, dtype=np.int64)
+    rows = out["mean"].shape[0]
+    idx = None if output_indices is None else np.ascontiguousarray(output_indices, np.int64)
+    num_outputs = int(np.maximum(counts, 0).sum()) if idx is None else len(idx)
+    ptrs = (ctypes.c_void_p * 10)(*(
+        None if m is None or m.get(k) is None else m[k].ctypes.data
+        for m in moments for k in ADAM_NAMES))
+    normals = out.get("normals")
+    error = lib().gso_relocate(
+        len(counts), rows, out["color"].shape[1], counts.ctypes.data, num_outputs,
+        None if idx is None else idx.ctypes.data, output_base, out["mean"], out["rotation"],
+        out["scale"], out["opacity"], out["color"],
+        None if normals is None else normals.ctypes.data, ptrs)
+    return {"state": out, "exp_avg": moments[0], "exp_avg_sq": moments[1], "error": error}

@@ -28,7 +28,7 @@ def golden_cases(kind: str = "all") -> list[str]:
     names = sorted(f[:-4] for f in os.listdir(GOLDEN) if f.endswith(".npz"))
     out = []
     for name in names:
-        if name == "adam_noise":  # the optimizer-step fixture (tests/test_*optim*.py)
+        if name in ("adam_noise", "relocate"):  # training-step fixtures (optim, relocate tests)
             continue
         if name == "intersections":
             if kind == "all":

@@ -30,6 +30,9 @@ Scenes:
   GaussianSplat of 257 Gaussians, then the reference's own noise_splats
   (training/utils.py:50-62) with a recorded seed; the normal samples it draws
   are stored too.
+* ``relocate``: the training loop's splat relocation (training/utils.py:
+  120-210): copy_splats with chosen counts, and relocate_splats with an Adam
+  optimizer and densification, with the counts it sampled.
 """
 
 from __future__ import annotations
@@ -207,17 +210,16 @@ def run_intersections() -> dict:
     )
 
 
-def run_adam_noise() -> dict:
-    """torch.optim.Adam as the reference's training loop builds it, then its
-    noise_splats, on the reference's GaussianSplat."""
+def _training_utils():
+    """The reference's training/utils.py module. It imports torchmetrics (for
+    its SSIM, unused here) and the package __init__ pulls in the whole
+    training script; neither is needed for the splat helpers. Stub the one and
+    skip the other."""
+    import importlib
     import types
 
     import gaussian_splats
-    from gaussian_splats.splats.splats import GaussianSplat
 
-    # training/utils.py imports torchmetrics (for its SSIM, unused here) and the
-    # package __init__ pulls in the whole training script; neither is needed
-    # for noise_splats. Stub the one and skip the other.
     if "torchmetrics" not in sys.modules:
         image = types.ModuleType("torchmetrics.functional.image")
         image.structural_similarity_index_measure = None
@@ -231,7 +233,15 @@ def run_adam_noise() -> dict:
         package = types.ModuleType("gaussian_splats.training")
         package.__path__ = [os.path.join(os.path.dirname(gaussian_splats.__file__), "training")]
         sys.modules["gaussian_splats.training"] = package
-    from gaussian_splats.training.utils import noise_splats
+    return importlib.import_module("gaussian_splats.training.utils")
+
+
+def run_adam_noise() -> dict:
+    """torch.optim.Adam as the reference's training loop builds it, then its
+    noise_splats, on the reference's GaussianSplat."""
+    from gaussian_splats.splats.splats import GaussianSplat
+
+    noise_splats = _training_utils().noise_splats
 
     n, lrs = 257, (1.6e-4 * 3.3, 1e-3, 5e-3, 5e-2, 2.5e-3)  # train.py:78-83 (mean lr scaled)
     noise_lr, position_lr = 5e5, 1.6e-4 * 3.3
@@ -270,7 +280,91 @@ def run_adam_noise() -> dict:
     return record
 
 
-CASES = ("adam_noise", "intersections", "fixture_degenerate", "fixture_sh1_t8", "fixture_sh0_t8",
+def run_relocate() -> dict:
+    """The reference's copy_splats and relocate_splats on CPU.
+
+    copy_*: copy_splats (training/utils.py:120-145) with chosen counts -- one
+    parent with 55 copies (normalize_copies clamps copies at 51), three with 1
+    to 3 -- into 61 non-parent rows listed in random order.
+    reloc_*: relocate_splats (training/utils.py:147-210) with a
+    torch.optim.Adam that has taken one step, densification factor 1.05 and
+    torch seed 5; the counts its sample_counts drew (dead rows, then
+    densification) are recorded so a test can replay them."""
+    from gaussian_splats.splats.splats import GaussianSplat
+
+    utils = _training_utils()
+    names = PARAM_NAMES + ("normals",)
+    n = 300
+    g = torch.Generator().manual_seed(21)
+
+    def make():
+        splats = GaussianSplat(n, sh_degree=1)
+        with torch.no_grad():
+            splats.mean.copy_(torch.randn(n, 3, generator=g))
+            splats.rotation.copy_(torch.randn(n, 4, generator=g))
+            splats.scale.copy_(torch.randn(n, 3, generator=g) * 0.5 - 4.0)
+            splats.opacity.copy_(torch.randn(n, 1, generator=g) * 2.5 - 2.0)
+            splats.color.copy_(torch.randn(n, 4, 3, generator=g) * 0.3)
+            splats.normals.copy_(torch.randn(n, 3, generator=g))
+        return splats
+
+    record = {}
+    splats = make()
+    for name in names:
+        record[f"copy_in_{name}"] = getattr(splats, name).detach().numpy().copy()
+    alive = (splats.opacity.sigmoid().squeeze(-1) >= 0.005).nonzero().squeeze(-1)
+    parents = alive[torch.randperm(len(alive), generator=g)[:4]]
+    counts = torch.zeros(n, dtype=torch.int64)
+    counts[parents] = torch.tensor([55, 1, 2, 3])
+    others = torch.ones(n, dtype=torch.bool)
+    others[parents] = False
+    candidates = others.nonzero().squeeze(-1)
+    outputs = candidates[torch.randperm(len(candidates), generator=g)[:61]]
+    reset = utils.copy_splats(splats, counts, outputs)
+    record["copy_counts"] = counts.numpy()
+    record["copy_outputs"] = outputs.numpy()
+    record["copy_reset"] = reset.numpy()
+    for name in names:
+        record[f"copy_out_{name}"] = getattr(splats, name).detach().numpy().copy()
+
+    splats = make()
+    params = [getattr(splats, name) for name in PARAM_NAMES]
+    optimizer = torch.optim.Adam([{"params": [p], "name": name, "lr": 1e-3}
+                                  for p, name in zip(params, PARAM_NAMES)], eps=1e-15)
+    for p in params:
+        p.grad = torch.randn(p.shape, generator=g) * 0.1
+    optimizer.step()
+    for name, p in zip(PARAM_NAMES, params):
+        record[f"reloc_in_exp_avg_{name}"] = optimizer.state[p]["exp_avg"].numpy().copy()
+        record[f"reloc_in_exp_avg_sq_{name}"] = optimizer.state[p]["exp_avg_sq"].numpy().copy()
+    for name in names:
+        record[f"reloc_in_{name}"] = getattr(splats, name).detach().numpy().copy()
+    drawn = []
+    sample = utils.sample_counts
+
+    def recording(weights, count):
+        out = sample(weights, count)
+        drawn.append(out.numpy().copy())
+        return out
+
+    utils.sample_counts = recording
+    try:
+        torch.manual_seed(5)
+        utils.relocate_splats(splats, optimizer, densification_factor=1.05)
+    finally:
+        utils.sample_counts = sample
+    assert len(drawn) == 2, "expected a dead-row and a densification draw"
+    record["reloc_counts_dead"], record["reloc_counts_densify"] = drawn
+    for name in names:
+        record[f"reloc_out_{name}"] = getattr(splats, name).detach().numpy().copy()
+    for group in optimizer.param_groups:
+        state = optimizer.state[group["params"][0]]
+        record[f"reloc_out_exp_avg_{group['name']}"] = state["exp_avg"].numpy().copy()
+        record[f"reloc_out_exp_avg_sq_{group['name']}"] = state["exp_avg_sq"].numpy().copy()
+    return record
+
+
+CASES = ("relocate", "adam_noise", "intersections", "fixture_degenerate", "fixture_sh1_t8", "fixture_sh0_t8",
          "fixture_sh4_t8", "fixture_sh2_t8", "fixture_ellipsoid", "fixture_sh1_t4",
          "fixture_sh3_t16", "mini5", "mini2", "config1")
 
@@ -290,6 +384,8 @@ def main() -> None:
             record = run_intersections()
         elif name == "adam_noise":
             record = run_adam_noise()
+        elif name == "relocate":
+            record = run_relocate()
         else:
             record = run_case(name)
         np.savez_compressed(HERE / f"{name}.npz", **record)
