@@ -424,25 +424,27 @@ __global__ void __launch_bounds__(TileShape<TS, PPT>::kThreads,
         const float denominator = fmaxf(st[q] * (1.0f - alpha), 1e-4f);
         const float forward = t_final[q] / denominator;
         const bool still = (1.0f - forward) < threshold;
+        // Gradient arithmetic (tolerance-checked, unlike the decisions above)
+        // contracts multiply-adds explicitly.
         float weight_grad = gr[q] * (c.x - sr[q]);
-        weight_grad += gg[q] * (c.y - sg[q]);
-        weight_grad += gb[q] * (c.z - sb[q]);
+        weight_grad = fmaf(gg[q], c.y - sg[q], weight_grad);
+        weight_grad = fmaf(gb[q], c.z - sb[q], weight_grad);
         float grad_alpha = still ? forward * weight_grad : 0.0f;
         grad_alpha = alpha_raw < kAlphaMax ? grad_alpha : 0.0f;
-        const float probability_grad = grad_alpha * o;
         const float grad_color = forward * alpha;
         if constexpr (kGaussian) {
-          const float grad_distance = -0.5f * prob * probability_grad;
-          v[0] += -2.0f * grad_distance * (xx * dx + xy * dy);
-          v[1] += -2.0f * grad_distance * (xy * dx + yy * dy);
-          v[2] += grad_distance * dx * dx;
-          v[3] += grad_distance * dx * dy;
-          v[4] += grad_distance * dy * dy;
+          const float grad_distance = -0.5f * prob * (grad_alpha * o);
+          const float gdx = grad_distance * dx, gdy = grad_distance * dy;
+          v[0] = fmaf(-2.0f * grad_distance, fmaf(xy, dy, adx), v[0]);
+          v[1] = fmaf(-2.0f * grad_distance, fmaf(yy, dy, xy * dx), v[1]);
+          v[2] = fmaf(gdx, dx, v[2]);
+          v[3] = fmaf(gdx, dy, v[3]);
+          v[4] = fmaf(gdy, dy, v[4]);
         }
-        v[5] += grad_color * gr[q];
-        v[6] += grad_color * gg[q];
-        v[7] += grad_color * gb[q];
-        v[8] += grad_alpha * prob;
+        v[5] = fmaf(grad_color, gr[q], v[5]);
+        v[6] = fmaf(grad_color, gg[q], v[6]);
+        v[7] = fmaf(grad_color, gb[q], v[7]);
+        v[8] = fmaf(grad_alpha, prob, v[8]);
         const float local_t = 1.0f - alpha;
         sr[q] = fmaf(local_t, sr[q], alpha * c.x);
         sg[q] = fmaf(local_t, sg[q], alpha * c.y);

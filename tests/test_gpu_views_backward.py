@@ -94,7 +94,8 @@ def test_exchange_plumbing_on_one_rank():
     views) must give the ordinary backward's gradients. The two backward
     passes each run compositing backward, whose float atomics add in
     scheduling order, so they agree to rounding, not bit for bit (the summed
-    backward itself is bit-exact: test above)."""
+    backward itself is bit-exact: test above); a component that is a sum with
+    cancellation can differ by that rounding relative to the tensor's scale."""
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
@@ -115,7 +116,9 @@ def test_exchange_plumbing_on_one_rank():
                 (image * weights).sum().backward()
             grads.append([p.grad.clone() for p in params])
         for a, b in zip(*grads):
-            torch.testing.assert_close(a, b, rtol=1e-4, atol=1e-6)
+            # summation order noise of the atomics, on sums with cancellation:
+            # absolute, on the scale of the gradient tensor
+            torch.testing.assert_close(a, b, rtol=1e-4, atol=1e-5 * float(b.abs().max()))
     finally:
         dist.destroy_process_group()
 
