@@ -25,10 +25,28 @@ class Camera:
     translation: torch.Tensor = field(default_factory=lambda: torch.zeros(3))
     image_size: tuple[int, int] = (640, 480)
 
+    # (quaternion tensor, its version, matrix, the matrix's version) of the
+    # last rotation_matrix computed without autograd
+    _matrix_cache: tuple | None = field(default=None, init=False, repr=False, compare=False)
+
     @property
     def rotation_matrix(self) -> torch.Tensor:
-        """World-to-camera 3x3 matrix of the normalised quaternion."""
-        return quaternion_to_rotation_matrix(F.normalize(self.rotation, dim=-1))
+        """World-to-camera 3x3 matrix of the normalised quaternion.
+
+        Remembered while the quaternion tensor is the same object with the same
+        version counter (so in-place edits and reassignment recompute it): a
+        render then pays no per-call torch ops for an unchanged camera.
+        Quaternions that require grad are never cached."""
+        q = self.rotation
+        if q.requires_grad:
+            return quaternion_to_rotation_matrix(F.normalize(q, dim=-1))
+        cache = self._matrix_cache
+        if cache is not None and cache[0] is q and cache[1] == q._version and \
+                cache[3] == cache[2]._version:
+            return cache[2]
+        matrix = quaternion_to_rotation_matrix(F.normalize(q, dim=-1))
+        self._matrix_cache = (q, q._version, matrix, matrix._version)
+        return matrix
 
     @property
     def position(self) -> torch.Tensor:

@@ -38,6 +38,7 @@ import os
 from typing import Literal
 
 import torch
+from torch.utils.weak import WeakIdKeyDictionary
 
 from . import native, view_parallel
 from .camera import Camera
@@ -72,16 +73,28 @@ def _f32(t: torch.Tensor) -> torch.Tensor:
     return t.detach().to(torch.float32).contiguous()
 
 
+# Device copies of host camera tensors: host tensor -> (its version, device,
+# copy). Entries die with the host tensor.
+_DEVICE_COPIES = WeakIdKeyDictionary()
+
+
 def _to_device(t: torch.Tensor, device: torch.device) -> torch.Tensor:
     """``t`` on ``device``. A host tensor goes up through pinned memory with a
     non-blocking copy: a plain ``.to`` from pageable memory synchronises the
     stream, so the host would wait for all queued GPU work on every render and
-    the GPU would then idle while the next kernels are launched."""
+    the GPU would then idle while the next kernels are launched. The copy is
+    kept while the host tensor is unchanged (same object and version), so
+    re-rendering a camera copies nothing."""
     if t.device == device or device.type != "cuda" or t.requires_grad:
         return t.to(device)
+    cached = _DEVICE_COPIES.get(t)
+    if cached is not None and cached[0] == t._version and cached[1] == device:
+        return cached[2]
     staged = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
     staged.copy_(t)
-    return staged.to(device, non_blocking=True)
+    copy = staged.to(device, non_blocking=True)
+    _DEVICE_COPIES[t] = (t._version, device, copy)
+    return copy
 
 
 class StageTimer:
