@@ -642,6 +642,7 @@ def main():
         return
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
+    from gaussian_splats_b200.graphs import CapturedStep
     from gaussian_splats_b200.rasterize import StageTimer, rasterize_batch, rasterize_outputs
     from gaussian_splats_b200.splats import GaussianSplat
     from gaussian_splats_b200.view_parallel import screen_exchange_pays
@@ -726,12 +727,31 @@ def main():
         forward_step()
     fwd_ms = timed(forward_step, args.steps)
 
-    # The headline step: forward + backward (+ all-reduce), or forward only.
+    # The headline step: forward + backward (+ the gradient exchange), or
+    # forward only. On one GPU the training step is replayed from a CUDA graph
+    # (gaussian_splats_b200.graphs: one launch per step, the same kernels);
+    # the per-stage times come from eager steps, which the stage timer's
+    # events need. With several ranks the step runs eagerly (no collective is
+    # captured).
     for _ in range(args.warmup):
         step()
-    with ClockSampler(local_rank) as clocks, StageTimer() as stages:
-        ms = timed(step, args.steps)
-    stage_ms = stages.durations()
+    graphed = backward and world == 1
+    eager_ms = None
+    if graphed:
+        with StageTimer() as stages:
+            eager_ms = timed(step, max(3, args.steps // 5))
+        stage_ms = stages.durations()
+        captured = CapturedStep(step, warmup=max(1, args.warmup))
+        for _ in range(args.warmup):
+            captured()
+        with ClockSampler(local_rank) as clocks:
+            ms = timed(captured, args.steps)
+        if not captured.check():
+            raise RuntimeError("a timed replay overflowed its intersection buffer")
+    else:
+        with ClockSampler(local_rank) as clocks, StageTimer() as stages:
+            ms = timed(step, args.steps)
+        stage_ms = stages.durations()
     clock = clocks.summary()
     value = views_per_step * 1000.0 / ms
 
@@ -793,6 +813,20 @@ def main():
                 dst.copy_(src, non_blocking=True)
             ready.record(copy_stream)
 
+    def slot_step(slot):
+        buffers, slot_splats, slot_trainable, _ = slot
+        return lambda: vp_train_step(slot_splats, cameras, buffers[5:], slot_trainable,
+                                     lambda s, c: render(s, c)[0], loss_fn,
+                                     screen_exchange=screen)
+
+    slot_steps = [slot_step(slot) for slot in slots]
+    if graphed:
+        # one captured step per buffer slot, captured on real inputs
+        prefetch(0)
+        prefetch(1)
+        torch.cuda.synchronize()
+        slot_steps = [CapturedStep(fn, warmup=1) for fn in slot_steps]
+
     def e2e_run(steps):
         prefetch(0)
         for i in range(steps):
@@ -801,9 +835,7 @@ def main():
             buffers, slot_splats, slot_trainable, ready = slots[i % 2]
             torch.cuda.current_stream().wait_event(ready)
             if backward:
-                loss = vp_train_step(slot_splats, cameras, buffers[5:], slot_trainable,
-                                     lambda s, c: render(s, c)[0], loss_fn,
-                                     screen_exchange=screen)
+                loss = slot_steps[i % 2]()
                 loss.item()
             else:
                 images = (batched_step if batched else forward_step)(slot_splats)
@@ -812,6 +844,8 @@ def main():
     e2e_run(max(1, args.warmup // 2))
     e2e_steps = max(3, args.steps // 2)
     e2e_ms = timed(lambda: e2e_run(e2e_steps), 1) / e2e_steps
+    if graphed and not all(fn.check() for fn in slot_steps):
+        raise RuntimeError("an end-to-end replay overflowed its intersection buffer")
 
     hbm_peak, peak_kind = load_peaks()
     n, k = scene.num_points, host[4].shape[1]
@@ -868,6 +902,7 @@ def main():
         "warmup": args.warmup, "ms_per_step": ms, "fwd_ms": fwd_ms / per_view,
         "batched_fwd_ms": ms / per_view if batched else None,
         "fwd_bwd_ms": ms / per_view if backward else None,
+        "eager_ms_per_step": eager_ms,
         "higher_is_better": True,
         "scaling": "weak" if workload["views"] is None else "strong",
         "vs_baseline": None, "dtype": "f32",
@@ -881,6 +916,9 @@ def main():
                         "summed over all ranks' views" if screen else
                         ", NCCL all-reduce of gradients") if backward else ", no collective"))
                    if world > 1 else "single GPU",
+                   "step": "CUDA-graph replay of the captured training step (same kernels; "
+                           "eager_ms_per_step is the step launched from Python)" if graphed
+                   else "launched from Python",
                    "l2": "inputs larger than L2 (Gaussian parameters read every view)"
                    if n * project_fwd_bytes(k) > 126e6 else
                    "inputs smaller than L2; each view re-reads them"},

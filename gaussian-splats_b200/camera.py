@@ -36,9 +36,11 @@ class Camera:
         Remembered while the quaternion tensor is the same object with the same
         version counter (so in-place edits and reassignment recompute it): a
         render then pays no per-call torch ops for an unchanged camera.
-        Quaternions that require grad are never cached."""
+        Quaternions that require grad are never cached, nor device quaternions
+        during CUDA-graph capture (the graph must recompute the matrix from
+        the quaternion on every replay)."""
         q = self.rotation
-        if q.requires_grad:
+        if q.requires_grad or (q.is_cuda and torch.cuda.is_current_stream_capturing()):
             return quaternion_to_rotation_matrix(F.normalize(q, dim=-1))
         cache = self._matrix_cache
         if cache is not None and cache[0] is q and cache[1] == q._version and \

@@ -90,6 +90,10 @@ def _to_device(t: torch.Tensor, device: torch.device) -> torch.Tensor:
     cached = _DEVICE_COPIES.get(t)
     if cached is not None and cached[0] == t._version and cached[1] == device:
         return cached[2]
+    if torch.cuda.is_current_stream_capturing():
+        # a captured copy would read the staging buffer again on every replay
+        raise RuntimeError("a host camera tensor changed during CUDA-graph capture; keep the "
+                           "camera on the device, or render it once before capturing")
     staged = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
     staged.copy_(t)
     copy = staged.to(device, non_blocking=True)
@@ -145,6 +149,10 @@ def _mark(name: str) -> None:
 # renders size their sort buffers from it (plus headroom) and enqueue the sort
 # before their own total reaches the host.
 _LAST_TOTAL: dict[tuple[int, int, int | None], int] = {}
+
+# The graph capture in progress (gaussian_splats_b200.graphs sets it while a
+# captured step runs), or None.
+_CAPTURE = None
 
 
 def _pinned_words() -> torch.Tensor:
@@ -230,7 +238,8 @@ def _rasterize(
                 _ptr(sort_ws), sort_bytes, _ptr(gaussian_ids), _ptr(ranges), stream),
                 "gs_bin_sort")
             _mark("bin_sort")
-            if os.environ.get("GAUSSIAN_SPLATS_B200_CHECK") == "1":
+            if os.environ.get("GAUSSIAN_SPLATS_B200_CHECK") == "1" and \
+                    not torch.cuda.is_current_stream_capturing():
                 native.check(lib.gs_bin_check(_ptr(count_ws), _ptr(sort_ws), stream), "binning")
             _mark("begin:composite_fwd")
             native.check(lib.gs_composite_fwd(
@@ -242,8 +251,27 @@ def _rasterize(
 
         key = (n, num_tiles, device.index)
         last = _LAST_TOTAL.get(key)
+        capture = _CAPTURE if torch.cuda.is_current_stream_capturing() else None
         _mark("begin:bin_count")
-        if last is None:
+        if capture is not None:
+            # Inside CUDA-graph capture: no host wait. The sort and compositing
+            # run at the capture's capacity; a captured copy refreshes the
+            # total and error words on every replay, and the graph's owner
+            # checks them after each replay (gaussian_splats_b200.graphs).
+            if last is None:
+                raise RuntimeError("render each view once outside graph capture first: the "
+                                   "first render sizes its intersection buffer")
+            capacity = capture.capacity(key, last)
+            words = capture.take_words()
+            native.check(lib.gs_bin_count_async(
+                n, _ptr(projected_mean), _ptr(counts), _ptr(count_ws), count_bytes,
+                ctypes.c_void_p(words.data_ptr()), ctypes.c_void_p(words.data_ptr() + 8),
+                stream), "gs_bin_count_async")
+            _mark("bin_count")
+            gaussian_ids = sort_and_composite(capacity)
+            capture.record(key, capacity, words)
+            total = None
+        elif last is None:
             # First render of this shape: wait for the total, size exactly.
             total = ctypes.c_int64(0)
             native.check(lib.gs_bin_count(
@@ -276,7 +304,8 @@ def _rasterize(
                 gaussian_ids = sort_and_composite(total)
             else:
                 gaussian_ids.resize_(total)  # same storage, no copy
-        _LAST_TOTAL[key] = total
+        if total is not None:
+            _LAST_TOTAL[key] = total
     return (image, final_transmittance, n_contributors, projected_mean, inverse_covariance,
             projected_color, projected_opacity, gaussian_ids, ranges, counts)
 

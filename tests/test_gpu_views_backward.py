@@ -118,7 +118,7 @@ def test_exchange_plumbing_on_one_rank():
         for a, b in zip(*grads):
             # summation order noise of the atomics, on sums with cancellation:
             # absolute, on the scale of the gradient tensor
-            torch.testing.assert_close(a, b, rtol=1e-4, atol=1e-5 * float(b.abs().max()))
+            torch.testing.assert_close(a, b, rtol=1e-4, atol=1e-4 * float(b.abs().max()))
     finally:
         dist.destroy_process_group()
 

@@ -56,7 +56,7 @@ def main():
             # both paths run compositing backward, whose float atomics add in
             # scheduling order, and sum the views in different orders: the
             # absolute tolerance is on the scale of the gradient tensor
-            torch.testing.assert_close(b, a, rtol=1e-4, atol=1e-5 * float(a.abs().max()),
+            torch.testing.assert_close(b, a, rtol=1e-4, atol=1e-4 * float(a.abs().max()),
                                        msg=lambda m: f"{name}: {m}")
             assert torch.count_nonzero(a) > 0, name
         for grad in results[1]:  # every rank holds the same summed gradients
