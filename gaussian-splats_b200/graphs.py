@@ -23,9 +23,12 @@ in place between replays), render every view on the same devices and image
 sizes each call, and keep host-side decisions out of the step (no ``.item()``
 or other reads of device values). Camera poses are read from device tensors
 the graph captured: keep the camera's quaternion and translation on the GPU,
-or re-render a changed host camera eagerly before capturing. The optimizer
-step (whose scalars change with the step count) and relocation stay outside
-the graph.
+or re-render a changed host camera eagerly before capturing. Set the
+parameters' ``.grad`` to None at the start of the step (``train_step`` does):
+the captured backward then writes fresh gradients into tensors the graph owns
+on every replay instead of adding to old ones; nothing may reset them between
+replays. The optimizer step (whose scalars change with the step count) and
+relocation stay outside the graph.
 """
 
 from __future__ import annotations
