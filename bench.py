@@ -95,6 +95,9 @@ def parse_args():
     p.add_argument("--points", type=int, default=None,
                    help="override the config's Gaussian count (smaller smoke runs)")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-graph", action="store_true",
+                   help="launch the training step from Python instead of replaying it from "
+                        "a CUDA graph")
     p.add_argument("--exchange", choices=("auto", "screen", "all-reduce"), default="auto",
                    help="how ranks sum gradients with one view per rank (auto: "
                         "view_parallel.screen_exchange_pays)")
@@ -729,13 +732,13 @@ def main():
 
     # The headline step: forward + backward (+ the gradient exchange), or
     # forward only. On one GPU the training step is replayed from a CUDA graph
-    # (gaussian_splats_b200.graphs: one launch per step, the same kernels);
-    # the per-stage times come from eager steps, which the stage timer's
-    # events need. With several ranks the step runs eagerly (no collective is
-    # captured).
+    # (gaussian_splats_b200.graphs: one launch per step, the same kernels); the
+    # per-stage times come from steps launched from Python, which the stage
+    # timer's events need. With several ranks the step is launched from Python:
+    # no collective is captured into a graph.
     for _ in range(args.warmup):
         step()
-    graphed = backward and world == 1
+    graphed = backward and world == 1 and not args.no_graph
     eager_ms = None
     if graphed:
         with StageTimer() as stages:

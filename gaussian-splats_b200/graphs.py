@@ -28,7 +28,9 @@ parameters' ``.grad`` to None at the start of the step (``train_step`` does):
 the captured backward then writes fresh gradients into tensors the graph owns
 on every replay instead of adding to old ones; nothing may reset them between
 replays. The optimizer step (whose scalars change with the step count) and
-relocation stay outside the graph.
+relocation stay outside the graph, and so do collectives: a step that
+exchanges gradients across ranks (``view_parallel``) is refused after its
+warm-up and stays launched from Python.
 """
 
 from __future__ import annotations
@@ -38,6 +40,7 @@ from collections.abc import Callable
 import torch
 
 from . import rasterize as _rasterize
+from . import view_parallel
 
 _HEADROOM_SLACK = 4096  # intersections added to every capacity
 
@@ -51,6 +54,11 @@ class _Capture:
         self.words = words
         self.headroom = headroom
         self.renders: list[tuple[tuple, int, torch.Tensor]] = []
+        self.kept: list[torch.Tensor] = []
+
+    def keep(self, host_buffer: torch.Tensor) -> None:
+        """Hold a pinned host buffer a captured copy reads on every replay."""
+        self.kept.append(host_buffer)
 
     def capacity(self, key, last: int) -> int:
         if key not in self.capacities:
@@ -99,11 +107,25 @@ class CapturedStep:
     def _capture(self, warmup: int) -> None:
         side = torch.cuda.Stream()
         side.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(side):
-            for _ in range(warmup):
-                self.fn()
+        collectives = view_parallel.COLLECTIVE_CALLS
+        seen: dict = {}
+        previous_seen, _rasterize._SEEN_TOTALS = _rasterize._SEEN_TOTALS, seen
+        try:
+            with torch.cuda.stream(side):
+                for _ in range(warmup):
+                    self.fn()
+        finally:
+            _rasterize._SEEN_TOTALS = previous_seen
         torch.cuda.current_stream().wait_stream(side)
         torch.cuda.synchronize()
+        if view_parallel.COLLECTIVE_CALLS != collectives:
+            # Decided from the eager warm-up, the same on every rank: capturing
+            # the step's NCCL collectives into a graph hung on two GPUs here.
+            raise RuntimeError("the step exchanges gradients across ranks; launch it from "
+                               "Python (collectives are not captured into CUDA graphs)")
+        # every render of a shape gets room for the largest one seen
+        for key, total in seen.items():
+            self._grow(key, total)
         self.graph = None  # release the previous graph's memory first
         graph = torch.cuda.CUDAGraph()
         capture = _Capture(self.capacities, self.words, self.headroom)
@@ -114,7 +136,12 @@ class CapturedStep:
         finally:
             _rasterize._CAPTURE = previous
         self.graph, self.output, self.renders = graph, output, capture.renders
+        self._kept = capture.kept  # host buffers the graph's copies read
         self.captures += 1
+
+    def _grow(self, key, total: int) -> None:
+        want = total + int(total * self.headroom) + _HEADROOM_SLACK
+        self.capacities[key] = max(want, self.capacities.get(key, 0))
 
     def __call__(self) -> torch.Tensor:
         self.graph.replay()
@@ -137,7 +164,7 @@ class CapturedStep:
                     raise RuntimeError(f"{total} intersections exceed the sort's capacity")
                 if total > capacity:
                     overflow = True
-                    self.capacities[key] = total + int(total * self.headroom) + _HEADROOM_SLACK
+                    self._grow(key, total)
             if not overflow:
                 return fitted
             fitted = False

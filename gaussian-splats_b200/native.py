@@ -126,19 +126,23 @@ def adam_params(steps, lrs, betas, eps, noise_lr=0.0, position_lr=0.0) -> AdamPa
 VIEW_RECORD_WORDS = 29  # gs_params (17 words) + camera rotation (9) + translation (3)
 
 
-def view_record(params: Params, camera_rotation, camera_translation):
+def view_record(params: Params, camera_rotation, camera_translation, keep=None):
     """The 29-word record of one view for ``gs_project_bwd_views``: the
     render's ``gs_params`` bytes, then the camera rotation and translation as
     float32 (an int32 tensor holding those bits), on the camera tensors'
     device. For CUDA cameras the record is assembled on the device without a
     host wait: the parameter words go up from pinned memory (non-blocking),
-    the camera words are concatenated on the device."""
+    the camera words are concatenated on the device. ``keep``, if given, is
+    called with the pinned host buffer the copy reads (a CUDA-graph capture
+    must keep it alive and unchanged for as long as the graph replays)."""
     import torch
 
     device = camera_rotation.device
     header = torch.empty(ctypes.sizeof(Params) // 4, dtype=torch.int32,
                          pin_memory=device.type == "cuda")
     ctypes.memmove(header.data_ptr(), ctypes.addressof(params), ctypes.sizeof(Params))
+    if keep is not None:
+        keep(header)
     camera = torch.cat((camera_rotation.detach().reshape(9).float(),
                         camera_translation.detach().reshape(3).to(device).float()))
     return torch.cat((header.to(device, non_blocking=True), camera.view(torch.int32)))

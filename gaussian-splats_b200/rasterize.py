@@ -151,8 +151,10 @@ def _mark(name: str) -> None:
 _LAST_TOTAL: dict[tuple[int, int, int | None], int] = {}
 
 # The graph capture in progress (gaussian_splats_b200.graphs sets it while a
-# captured step runs), or None.
+# captured step runs), or None; and, while a step is warmed up for capture, the
+# largest intersection total seen per key.
 _CAPTURE = None
+_SEEN_TOTALS: dict | None = None
 
 
 def _pinned_words() -> torch.Tensor:
@@ -306,6 +308,8 @@ def _rasterize(
                 gaussian_ids.resize_(total)  # same storage, no copy
         if total is not None:
             _LAST_TOTAL[key] = total
+            if _SEEN_TOTALS is not None:
+                _SEEN_TOTALS[key] = max(total, _SEEN_TOTALS.get(key, 0))
     return (image, final_transmittance, n_contributors, projected_mean, inverse_covariance,
             projected_color, projected_opacity, gaussian_ids, ranges, counts)
 
@@ -394,7 +398,9 @@ def _backward(ctx, *grad_outputs):
         if group is not None:
             # View-parallel step: gather every rank's screen-space gradient
             # and camera, and sum the projection backward over all views.
-            record = native.view_record(params, camera_rotation, camera_translation)
+            capture = _CAPTURE if torch.cuda.is_current_stream_capturing() else None
+            record = native.view_record(params, camera_rotation, camera_translation,
+                                        keep=capture.keep if capture is not None else None)
             all_gp, all_counts, all_views = view_parallel.exchange_screen_gradients(
                 grad_projected, counts, record, group)
             _mark("begin:project_bwd")

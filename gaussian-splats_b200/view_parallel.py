@@ -28,6 +28,16 @@ PARAMETER_NAMES = ("mean", "rotation", "scale", "opacity", "color")
 _EXCHANGE_GROUP = None
 
 
+# Collectives this process has issued through this module; a CUDA-graph
+# capture (gaussian_splats_b200.graphs) refuses steps that issue any.
+COLLECTIVE_CALLS = 0
+
+
+def _count_collective() -> None:
+    global COLLECTIVE_CALLS
+    COLLECTIVE_CALLS += 1
+
+
 @contextlib.contextmanager
 def screen_space_exchange(group=None):
     """Inside this context the rasterizer's backward returns the parameter
@@ -83,6 +93,7 @@ def exchange_screen_gradients(grad_projected: torch.Tensor, counts: torch.Tensor
     """All-gather every rank's screen-space gradient [N, 9], tile counts [N]
     and 29-word view record; returns ([W, N, 9], [W, N], [W, 29]) on the
     gradients' device, in rank order."""
+    _count_collective()
     world = dist.get_world_size(group)
     device = grad_projected.device
     n = grad_projected.shape[0]
@@ -146,6 +157,7 @@ def all_reduce_gradients(parameters: Sequence[torch.Tensor], group=None,
     """
     if not (dist.is_initialized() and dist.get_world_size(group) > 1):
         return
+    _count_collective()
     grads = []
     for p in parameters:
         if p.grad is None:

@@ -179,3 +179,17 @@ def test_screen_exchange_choice():
     from gaussian_splats_b200.view_parallel import screen_exchange_pays
 
     assert [screen_exchange_pays(w) for w in (1, 2, 4, 8)] == [False, True, True, False]
+
+
+def test_collectives_are_counted_for_the_graph_guard(monkeypatch):
+    from gaussian_splats_b200 import view_parallel
+
+    monkeypatch.setattr(dist, "is_initialized", lambda: True)
+    monkeypatch.setattr(dist, "get_world_size", lambda group=None: 2)
+    monkeypatch.setattr(dist, "all_reduce", lambda *a, **k: None)
+    before = view_parallel.COLLECTIVE_CALLS
+    grads = [torch.zeros(3)]
+    for g in grads:
+        g.grad = torch.ones(3)
+    all_reduce_gradients(grads)
+    assert view_parallel.COLLECTIVE_CALLS == before + 1
