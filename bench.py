@@ -98,7 +98,8 @@ def parse_args():
     p.add_argument("--no-graph", action="store_true",
                    help="launch the training step from Python instead of replaying it from "
                         "a CUDA graph")
-    p.add_argument("--exchange", choices=("auto", "screen", "all-reduce"), default="auto",
+    p.add_argument("--exchange", choices=("auto", "screen", "screen-nccl", "all-reduce"),
+                   default="auto",
                    help="how ranks sum gradients with one view per rank (auto: "
                         "view_parallel.screen_exchange_pays)")
     return p.parse_args()
@@ -648,6 +649,7 @@ def main():
     from gaussian_splats_b200.graphs import CapturedStep
     from gaussian_splats_b200.rasterize import StageTimer, rasterize_batch, rasterize_outputs
     from gaussian_splats_b200.splats import GaussianSplat
+    from gaussian_splats_b200 import view_parallel
     from gaussian_splats_b200.view_parallel import screen_exchange_pays
     from gaussian_splats_b200.view_parallel import train_step as vp_train_step
 
@@ -698,7 +700,11 @@ def main():
     # that beats all-reducing the parameter gradients; several views per rank:
     # the parameter gradients are all-reduced once per step.
     screen = world > 1 and len(cameras) == 1 and (
-        args.exchange == "screen" or (args.exchange == "auto" and screen_exchange_pays(world)))
+        args.exchange in ("screen", "screen-nccl") or
+        (args.exchange == "auto" and screen_exchange_pays(world)))
+    # screen-space gradients read from peer memory (default) or all-gathered by NCCL
+    view_parallel.EXCHANGE_TRANSPORT = "nccl" if args.exchange == "screen-nccl" else "p2p"
+    peers = screen and view_parallel.EXCHANGE_TRANSPORT == "p2p"
 
     def train_step():
         return vp_train_step(splats, cameras, targets, trainable,
@@ -731,14 +737,15 @@ def main():
     fwd_ms = timed(forward_step, args.steps)
 
     # The headline step: forward + backward (+ the gradient exchange), or
-    # forward only. On one GPU the training step is replayed from a CUDA graph
-    # (gaussian_splats_b200.graphs: one launch per step, the same kernels); the
+    # forward only. The training step is replayed from a CUDA graph
+    # (gaussian_splats_b200.graphs: one launch per step, the same kernels) on
+    # one GPU, and on several when the ranks exchange through peer memory; the
     # per-stage times come from steps launched from Python, which the stage
-    # timer's events need. With several ranks the step is launched from Python:
-    # no collective is captured into a graph.
+    # timer's events need. A step with an NCCL collective is launched from
+    # Python: no collective is captured into a graph.
     for _ in range(args.warmup):
         step()
-    graphed = backward and world == 1 and not args.no_graph
+    graphed = backward and not args.no_graph and (world == 1 or peers)
     eager_ms = None
     if graphed:
         with StageTimer() as stages:
@@ -751,6 +758,8 @@ def main():
             ms = timed(captured, args.steps)
         if not captured.check():
             raise RuntimeError("a timed replay overflowed its intersection buffer")
+        if peers:
+            view_parallel.check_exchange()
     else:
         with ClockSampler(local_rank) as clocks, StageTimer() as stages:
             ms = timed(step, args.steps)
@@ -849,6 +858,8 @@ def main():
     e2e_ms = timed(lambda: e2e_run(e2e_steps), 1) / e2e_steps
     if graphed and not all(fn.check() for fn in slot_steps):
         raise RuntimeError("an end-to-end replay overflowed its intersection buffer")
+    if peers:
+        view_parallel.check_exchange()
 
     hbm_peak, peak_kind = load_peaks()
     n, k = scene.num_points, host[4].shape[1]
@@ -915,7 +926,10 @@ def main():
                    "image": [crop_w, crop_h], "tile_size": settings.tile_size,
                    "views_per_step": views_per_step, "views_per_rank_per_step": per_view,
                    "parallelism": (f"view-parallel x{world}" + (
-                       (", NCCL all-gather of screen-space gradients + projection backward "
+                       (", projection backward summed over all ranks' views, reading their "
+                        "screen-space gradients from peer memory (symmetric memory, NVLink)"
+                        if peers else
+                        ", NCCL all-gather of screen-space gradients + projection backward "
                         "summed over all ranks' views" if screen else
                         ", NCCL all-reduce of gradients") if backward else ", no collective"))
                    if world > 1 else "single GPU",

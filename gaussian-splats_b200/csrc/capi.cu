@@ -42,6 +42,16 @@ int32_t launch_composite_bwd(int64_t, const float*, const float*, const float*, 
 int32_t launch_adam_step(int64_t, int32_t, const gs_splat_arrays&, const gs_splat_arrays&,
                          const gs_splat_arrays&, const gs_splat_arrays&, const gs_adam_params&,
                          const float*, cudaStream_t);
+int32_t launch_project_bwd_peers(int64_t, int32_t, int32_t, const float*, const float*,
+                                 const float*, const float*, const float*, const void*,
+                                 const float* const*, const int32_t* const*, float*, float*,
+                                 float*, float*, float*, cudaStream_t);
+int32_t exchange_layout(int64_t, int32_t, gs_exchange_layout*);
+int32_t launch_exchange_begin(const gs_peer_group&, cudaStream_t);
+int32_t launch_exchange_publish(const gs_peer_group&, int64_t, cudaStream_t);
+int32_t launch_exchange_finish(const gs_peer_group&, cudaStream_t);
+int32_t exchange_gather(const gs_peer_group&, int64_t, float*, int32_t*, cudaStream_t);
+int32_t exchange_status(const gs_peer_group&, cudaStream_t);
 size_t relocate_workspace_size(int64_t);
 int32_t launch_relocate(int64_t, int64_t, int32_t, const int64_t*, int64_t, const int64_t*,
                         int64_t, const gs_splat_arrays&, float*, const gs_splat_arrays*,
@@ -271,6 +281,69 @@ int32_t gs_project_bwd_views(int64_t n, int32_t num_sh, int32_t num_views, const
     return GS_ERR_MISALIGNED;
   return gs::launch_project_bwd_views(n, num_sh, num_views, mean, rotation, scale, opacity, color,
                                       views, grad_projected, counts, grad_mean, grad_rotation,
+                                      grad_scale, grad_opacity, grad_color, as_cuda(stream));
+}
+
+int32_t gs_exchange_layout_for(int64_t n, int32_t world, gs_exchange_layout* out) {
+  return gs::exchange_layout(n, world, out);
+}
+
+int32_t gs_exchange_begin(const gs_peer_group* group, gs_stream_t stream) {
+  if (!group) return GS_ERR_INVALID_ARGUMENT;
+  return gs::launch_exchange_begin(*group, as_cuda(stream));
+}
+
+int32_t gs_exchange_publish(const gs_peer_group* group, int64_t n, gs_stream_t stream) {
+  if (!group || n < 0 || n >= gs::kMaxGaussians) return GS_ERR_INVALID_ARGUMENT;
+  return gs::launch_exchange_publish(*group, n, as_cuda(stream));
+}
+
+int32_t gs_exchange_gather(const gs_peer_group* group, int64_t n, float* grad_projected,
+                           int32_t* counts, gs_stream_t stream) {
+  if (!group || n < 0 || n >= gs::kMaxGaussians) return GS_ERR_INVALID_ARGUMENT;
+  return gs::exchange_gather(*group, n, grad_projected, counts, as_cuda(stream));
+}
+
+int32_t gs_exchange_finish(const gs_peer_group* group, gs_stream_t stream) {
+  if (!group) return GS_ERR_INVALID_ARGUMENT;
+  return gs::launch_exchange_finish(*group, as_cuda(stream));
+}
+
+int32_t gs_exchange_status(const gs_peer_group* group, gs_stream_t stream) {
+  if (!group) return GS_ERR_INVALID_ARGUMENT;
+  return gs::exchange_status(*group, as_cuda(stream));
+}
+
+int32_t gs_project_bwd_peers(int64_t n, int32_t num_sh, const gs_peer_group* group,
+                             const float* gathered_grad, const int32_t* gathered_counts,
+                             const float* mean, const float* rotation, const float* scale,
+                             const float* opacity, const float* color, float* grad_mean,
+                             float* grad_rotation, float* grad_scale, float* grad_opacity,
+                             float* grad_color, gs_stream_t stream) {
+  if (!group || n < 0 || n >= gs::kMaxGaussians) return GS_ERR_INVALID_ARGUMENT;
+  if (group->world < 1 || group->world > GS_MAX_PEERS || group->rank < 0 ||
+      group->rank >= group->world)
+    return GS_ERR_INVALID_ARGUMENT;
+  if (!gs::valid_sh(num_sh)) return num_sh > 25 ? GS_ERR_UNSUPPORTED : GS_ERR_INVALID_ARGUMENT;
+  if (!gs::aligned(rotation, 16) || !gs::aligned(grad_rotation, 16) ||
+      ((num_sh == 4 || num_sh == 16) && (!gs::aligned(color, 16) || !gs::aligned(grad_color, 16))))
+    return GS_ERR_MISALIGNED;
+  gs_exchange_layout layout;
+  GS_TRY(gs::exchange_layout(n, group->world, &layout));
+  const float* grads[GS_MAX_PEERS] = {};
+  const int32_t* counts[GS_MAX_PEERS] = {};
+  for (int p = 0; p < group->world; ++p) {
+    if (!group->arena[p] || !gs::aligned(group->arena[p], 256)) return GS_ERR_MISALIGNED;
+    const char* base = static_cast<const char*>(group->arena[p]);
+    const bool local = p == group->rank || !gathered_grad || !gathered_counts;
+    grads[p] = local ? reinterpret_cast<const float*>(base + layout.grad_projected)
+                     : gathered_grad + 9 * n * p;
+    counts[p] = local ? reinterpret_cast<const int32_t*>(base + layout.counts)
+                      : gathered_counts + n * p;
+  }
+  const void* records = static_cast<const char*>(group->arena[group->rank]) + layout.gathered;
+  return gs::launch_project_bwd_peers(n, num_sh, group->world, mean, rotation, scale, opacity,
+                                      color, records, grads, counts, grad_mean, grad_rotation,
                                       grad_scale, grad_opacity, grad_color, as_cuda(stream));
 }
 

@@ -13,6 +13,7 @@ namespace gs {
 constexpr float kAlphaMin = 1.0f / 255.0f;  // composite.py:170, composite_bwd.py:121
 constexpr float kAlphaMax = 0.99f;           // composite.py:169
 constexpr int kSmCount = 148;                // B200: 2 dies x 74 SMs
+constexpr int kMaxPeers = GS_MAX_PEERS;      // ranks of a view-parallel exchange
 
 // Records the last CUDA error for gs_last_cuda_error(); defined in capi.cu.
 void set_cuda_error(cudaError_t err);

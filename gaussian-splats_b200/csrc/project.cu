@@ -419,7 +419,17 @@ __device__ __forceinline__ BwdTerms bwd_terms(int64_t i, const float* __restrict
 // opacity). `b` holds the Gaussian's view-independent terms, `inv` is the
 // view's conic as the forward computed it and `gp` the view's 9-float
 // screen-space gradient of the Gaussian.
-template <int K, class Sink>
+// How a view's screen-space gradient is read: through the read-only cache
+// (written on this GPU by an earlier kernel), or at L2 only (written by
+// another GPU, behind a flag).
+struct LoadReadOnly {
+  static __device__ __forceinline__ float get(const float* p) { return __ldg(p); }
+};
+struct LoadPeer {
+  static __device__ __forceinline__ float get(const float* p) { return __ldcg(p); }
+};
+
+template <int K, class Sink, class Load = LoadReadOnly>
 __device__ __forceinline__ void project_bwd_view(
     int64_t i, bool visible, const Camera& c, const gs_params& p, const BwdTerms& b,
     const float* __restrict__ color, float4 inv, const float* __restrict__ gp, Sink& sink) {
@@ -463,7 +473,8 @@ __device__ __forceinline__ void project_bwd_view(
   const float a10 = m1x * sx, a11 = m1y * sy, a12 = m1z * sz;
   // project_bwd.py:116-152
   const float inv00 = inv.x, inv01 = inv.y, inv10 = inv01, inv11 = inv.w;
-  const float gi00 = __ldg(gp + 2), gi01 = __ldg(gp + 3), gi10 = gi01, gi11 = __ldg(gp + 4);
+  const float gi00 = Load::get(gp + 2), gi01 = Load::get(gp + 3), gi10 = gi01,
+              gi11 = Load::get(gp + 4);
   const float h00 = inv00 * gi00 + inv10 * gi10, h01 = inv00 * gi01 + inv10 * gi11;
   const float h10 = inv01 * gi00 + inv11 * gi10, h11 = inv01 * gi01 + inv11 * gi11;
   const float gcov00 = -(h00 * inv00 + h01 * inv10), gcov01 = -(h00 * inv01 + h01 * inv11);
@@ -499,7 +510,7 @@ __device__ __forceinline__ void project_bwd_view(
   gqy = (gqy - qy * dot_q) * gq_scale;
   gqz = (gqz - qz * dot_q) * gq_scale;
   // project_bwd.py:191-226
-  const float gpx = __ldg(gp), gpy = __ldg(gp + 1);
+  const float gpx = Load::get(gp), gpy = Load::get(gp + 1);
   float gux = gpx * j00 + gpx * 0.0f;
   float guy = gpy * j11;
   float guz = -0.0f + gpx * j02 + gpy * j12;
@@ -633,7 +644,7 @@ __device__ __forceinline__ void project_bwd_view(
       sdz = fmaf(coef, dbz[k], sdz);
     }
     raw = raw + 0.5f;
-    const float gc = __ldg(gp + 5 + ch) * (raw > 0.0f ? 1.0f : 0.0f);
+    const float gc = Load::get(gp + 5 + ch) * (raw > 0.0f ? 1.0f : 0.0f);
     gc3[ch] = visible ? gc : 0.0f;
     gdx += gc * sdx;
     gdy += gc * sdy;
@@ -654,7 +665,7 @@ __device__ __forceinline__ void project_bwd_view(
   gmx += gdx; gmy += gdy; gmz += gdz;
   // project_bwd.py:320-334
   const float po = b.po;
-  const float go = __ldg(gp + 8) * po * (1.0f - po);
+  const float go = Load::get(gp + 8) * po * (1.0f - po);
   sink.rest(visible ? gmx : 0.0f, visible ? gmy : 0.0f, visible ? gmz : 0.0f,
             visible ? make_float4(gqw, gqx, gqy, gqz) : make_float4(0.0f, 0.0f, 0.0f, 0.0f),
             visible ? grad_sx * sx : 0.0f, visible ? grad_sy * sy : 0.0f,
@@ -729,23 +740,50 @@ struct ViewRecord {
 };
 static_assert(sizeof(ViewRecord) == 29 * 4, "29 32-bit words per view");
 
+// Where the views of gs_project_bwd_views live: [views, n, ...] arrays in this
+// GPU's memory.
+struct ContiguousViews {
+  const float* grad_projected;
+  const int32_t* counts;
+  int64_t n;
+  using Load = LoadReadOnly;
+  __device__ __forceinline__ int32_t count(int v, int64_t i) const {
+    return __ldg(counts + static_cast<int64_t>(v) * n + i);
+  }
+  __device__ __forceinline__ const float* grad(int v, int64_t i) const {
+    return grad_projected + 9 * (static_cast<int64_t>(v) * n + i);
+  }
+};
+
+// ... or one [n, 9] gradient and [n] count array per view, each in the memory
+// of the GPU that rendered the view (peer-mapped; read at L2 only).
+struct PeerViews {
+  const float* grad_projected[kMaxPeers];
+  const int32_t* counts[kMaxPeers];
+  using Load = LoadPeer;
+  __device__ __forceinline__ int32_t count(int v, int64_t i) const {
+    return __ldcg(counts[v] + i);
+  }
+  __device__ __forceinline__ const float* grad(int v, int64_t i) const {
+    return grad_projected[v] + 9 * i;
+  }
+};
+
 // Projection backward summed over views: each thread reads its Gaussian's
 // parameters once, recomputes each view's conic with the forward's
 // expressions, runs the single-view backward per view on that view's
-// screen-space gradient (grad_projected / counts: [views, n, ...]) and writes
-// the sum over views in view order. The views' cameras are read from device
-// memory, so a collective can deliver them without a host round trip. A view
-// where the Gaussian is not visible contributes zero, as in the single-view
-// backward.
-template <int K>
+// screen-space gradient and writes the sum over views in view order. The
+// views' cameras are read from device memory, so a collective (or a peer
+// handshake) can deliver them without a host round trip. A view where the
+// Gaussian is not visible contributes zero, as in the single-view backward.
+template <int K, class Source>
 __global__ void __launch_bounds__(128, K > 16 ? 3 : 4) project_bwd_views_kernel(
     int64_t n, int num_views, const float* __restrict__ mean, const float* __restrict__ rotation,
     const float* __restrict__ scale, const float* __restrict__ opacity,
     const float* __restrict__ color, const ViewRecord* __restrict__ views,
-    const float* __restrict__ grad_projected, const int32_t* __restrict__ counts,
-    float* __restrict__ grad_mean, float* __restrict__ grad_rotation,
-    float* __restrict__ grad_scale, float* __restrict__ grad_opacity,
-    float* __restrict__ grad_color) {
+    const __grid_constant__ Source src, float* __restrict__ grad_mean,
+    float* __restrict__ grad_rotation, float* __restrict__ grad_scale,
+    float* __restrict__ grad_opacity, float* __restrict__ grad_color) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= n) return;
   const GaussianTerms g = gaussian_terms(i, mean, rotation, scale, opacity);
@@ -754,14 +792,14 @@ __global__ void __launch_bounds__(128, K > 16 ? 3 : 4) project_bwd_views_kernel(
   SharedAccumulateGradients<K> acc{color_acc, static_cast<int>(threadIdx.x)};
   acc.zero();
   for (int v = 0; v < num_views; ++v) {
-    const int64_t o = static_cast<int64_t>(v) * n + i;
-    if (__ldg(counts + o) == 0) continue;
+    if (src.count(v, i) == 0) continue;
     const gs_params p = views[v].p;
     const float* R = views[v].R;
     const float* t = views[v].t;
     const Camera c{R[0], R[1], R[2], R[3], R[4], R[5], R[6], R[7], R[8], t[0], t[1], t[2]};
     const float4 inv = view_conic(g, c, p);
-    project_bwd_view<K>(i, true, c, p, b, color, inv, grad_projected + 9 * o, acc);
+    project_bwd_view<K, SharedAccumulateGradients<K>, typename Source::Load>(
+        i, true, c, p, b, color, inv, src.grad(v, i), acc);
   }
   float sum[K * 3];
 #pragma unroll
@@ -861,11 +899,36 @@ int32_t launch_project_bwd_views(int64_t n, int32_t num_sh, int32_t num_views,
                                  float* grad_opacity, float* grad_color, cudaStream_t stream) {
   if (n == 0) return GS_OK;
   const unsigned blocks = ceil_div(n, 128);
+  const ContiguousViews src{grad_projected, counts, n};
 #define GS_LAUNCH(K)                                                                          \
-  project_bwd_views_kernel<K><<<blocks, 128, 0, stream>>>(                                    \
+  project_bwd_views_kernel<K, ContiguousViews><<<blocks, 128, 0, stream>>>(                   \
       n, num_views, mean, rotation, scale, opacity, color,                                    \
-      static_cast<const ViewRecord*>(views), grad_projected, counts, grad_mean, grad_rotation, \
-      grad_scale, grad_opacity, grad_color)
+      static_cast<const ViewRecord*>(views), src, grad_mean, grad_rotation, grad_scale,       \
+      grad_opacity, grad_color)
+  GS_SH_DISPATCH(num_sh, GS_LAUNCH)
+#undef GS_LAUNCH
+  return check_launch();
+}
+
+int32_t launch_project_bwd_peers(int64_t n, int32_t num_sh, int32_t num_views,
+                                 const float* mean, const float* rotation, const float* scale,
+                                 const float* opacity, const float* color, const void* views,
+                                 const float* const* grad_projected, const int32_t* const* counts,
+                                 float* grad_mean, float* grad_rotation, float* grad_scale,
+                                 float* grad_opacity, float* grad_color, cudaStream_t stream) {
+  if (n == 0) return GS_OK;
+  if (num_views < 0 || num_views > kMaxPeers) return GS_ERR_INVALID_ARGUMENT;
+  PeerViews src{};
+  for (int v = 0; v < num_views; ++v) {
+    src.grad_projected[v] = grad_projected[v];
+    src.counts[v] = counts[v];
+  }
+  const unsigned blocks = ceil_div(n, 128);
+#define GS_LAUNCH(K)                                                                          \
+  project_bwd_views_kernel<K, PeerViews><<<blocks, 128, 0, stream>>>(                         \
+      n, num_views, mean, rotation, scale, opacity, color,                                    \
+      static_cast<const ViewRecord*>(views), src, grad_mean, grad_rotation, grad_scale,       \
+      grad_opacity, grad_color)
   GS_SH_DISPATCH(num_sh, GS_LAUNCH)
 #undef GS_LAUNCH
   return check_launch();

@@ -42,6 +42,13 @@ EXPORTED_SYMBOLS = (
     "gs_project_bwd",
     "gs_project_bwd_views",
     "gs_adam_step",
+    "gs_exchange_layout_for",
+    "gs_exchange_begin",
+    "gs_exchange_publish",
+    "gs_exchange_gather",
+    "gs_project_bwd_peers",
+    "gs_exchange_finish",
+    "gs_exchange_status",
     "gs_relocate",
     "gs_relocate_status",
     "gs_relocate_workspace_size",
@@ -95,6 +102,24 @@ class SplatArrays(ctypes.Structure):
 
     _fields_ = [(name, ctypes.c_void_p) for name in
                 ("mean", "rotation", "scale", "opacity", "color")]
+
+
+GS_MAX_PEERS = 8  # ranks of one peer exchange (include/gs_b200.h)
+
+
+class PeerGroup(ctypes.Structure):
+    """``gs_peer_group``: this rank, the number of ranks, and every rank's
+    exchange arena as mapped in this process."""
+
+    _fields_ = [("rank", ctypes.c_int32), ("world", ctypes.c_int32),
+                ("arena", ctypes.c_void_p * GS_MAX_PEERS)]
+
+
+class ExchangeLayout(ctypes.Structure):
+    """``gs_exchange_layout``: byte offsets inside an exchange arena."""
+
+    _fields_ = [(name, ctypes.c_uint64) for name in
+                ("grad_projected", "counts", "record", "gathered", "bytes")]
 
 
 class AdamParams(ctypes.Structure):
@@ -183,6 +208,13 @@ def lib() -> ctypes.CDLL:
         "gs_project_bwd_views": ([i64, i32, i32] + [vp] * 13 + [vp], i32),
         "gs_adam_step": ([i64, i32] + [ctypes.POINTER(SplatArrays)] * 4 +
                          [ctypes.POINTER(AdamParams), vp, vp], i32),
+        "gs_exchange_layout_for": ([i64, i32, ctypes.POINTER(ExchangeLayout)], i32),
+        "gs_exchange_begin": ([ctypes.POINTER(PeerGroup), vp], i32),
+        "gs_exchange_publish": ([ctypes.POINTER(PeerGroup), i64, vp], i32),
+        "gs_exchange_gather": ([ctypes.POINTER(PeerGroup), i64, vp, vp, vp], i32),
+        "gs_project_bwd_peers": ([i64, i32, ctypes.POINTER(PeerGroup)] + [vp] * 12 + [vp], i32),
+        "gs_exchange_finish": ([ctypes.POINTER(PeerGroup), vp], i32),
+        "gs_exchange_status": ([ctypes.POINTER(PeerGroup), vp], i32),
         "gs_relocate": ([i64, i64, i32, vp, i64, vp, i64, ctypes.POINTER(SplatArrays), vp,
                          ctypes.POINTER(SplatArrays), ctypes.POINTER(SplatArrays), vp,
                          ctypes.c_uint64, vp], i32),

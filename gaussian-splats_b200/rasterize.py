@@ -378,9 +378,19 @@ def _backward(ctx, *grad_outputs):
                                 ctx.image_height, ctx.tile_size, ctx.opacity_threshold,
                                 ctx.near, ctx.far, ctx.rendering_mode, ctx.confidence)
     pref = ctypes.byref(params)
+    group = view_parallel.active_exchange()
+    peers = group is not None and view_parallel.EXCHANGE_TRANSPORT == "p2p"
     with torch.cuda.device(device):
         stream = _stream(device)
-        grad_projected = mean.new_empty((n, 9))
+        if peers:
+            # Peer exchange: the screen-space gradient goes straight into
+            # this rank's arena, once every peer has finished reading it.
+            arena = view_parallel.peer_arena(n, device, group)
+            group_ref = ctypes.byref(arena.group)
+            native.check(lib.gs_exchange_begin(group_ref, stream), "gs_exchange_begin")
+            grad_projected = arena.grad_projected
+        else:
+            grad_projected = mean.new_empty((n, 9))
         _mark("begin:composite_bwd")
         native.check(lib.gs_composite_bwd(
             n, _ptr(projected_mean), _ptr(inverse_covariance), _ptr(projected_color),
@@ -394,13 +404,30 @@ def _backward(ctx, *grad_outputs):
         grad_rotation, grad_color, grad_mean, grad_scale, grad_opacity = _carve(
             mean.new_empty((n * (11 + 3 * num_sh),)), n,
             ((4,), (num_sh, 3), (3,), (3,), (1,)))
-        group = view_parallel.active_exchange()
         if group is not None:
-            # View-parallel step: gather every rank's screen-space gradient
-            # and camera, and sum the projection backward over all views.
+            # View-parallel step: every rank's screen-space gradient and
+            # camera, and the projection backward summed over all views.
             capture = _CAPTURE if torch.cuda.is_current_stream_capturing() else None
             record = native.view_record(params, camera_rotation, camera_translation,
                                         keep=capture.keep if capture is not None else None)
+        if peers:
+            arena.counts.copy_(counts)
+            arena.record.copy_(record)
+            native.check(lib.gs_exchange_publish(group_ref, n, stream), "gs_exchange_publish")
+            # bulk copies of the peers' gradients over NVLink; the peers may
+            # overwrite theirs as soon as the copies are done
+            native.check(lib.gs_exchange_gather(group_ref, n, _ptr(arena.gathered_grad),
+                                                _ptr(arena.gathered_counts), stream),
+                         "gs_exchange_gather")
+            native.check(lib.gs_exchange_finish(group_ref, stream), "gs_exchange_finish")
+            _mark("begin:project_bwd")
+            native.check(lib.gs_project_bwd_peers(
+                n, num_sh, group_ref, _ptr(arena.gathered_grad), _ptr(arena.gathered_counts),
+                _ptr(mean), _ptr(rotation), _ptr(scale), _ptr(opacity), _ptr(color),
+                _ptr(grad_mean), _ptr(grad_rotation), _ptr(grad_scale), _ptr(grad_opacity),
+                _ptr(grad_color), stream), "gs_project_bwd_peers")
+            _mark("project_bwd")
+        elif group is not None:
             all_gp, all_counts, all_views = view_parallel.exchange_screen_gradients(
                 grad_projected, counts, record, group)
             _mark("begin:project_bwd")

@@ -13,6 +13,7 @@ that buffer (no packing copy).
 from __future__ import annotations
 
 import contextlib
+import ctypes
 import datetime
 import os
 from collections.abc import Callable, Sequence
@@ -86,6 +87,95 @@ def screen_exchange_pays(world_size: int) -> bool:
     """Whether ``train_step`` with one view per rank should use the
     screen-space exchange rather than the parameter-gradient all-reduce."""
     return 1 < world_size <= SCREEN_EXCHANGE_MAX_WORLD
+
+
+# How the screen-space exchange moves the gradients: "p2p" -- the projection
+# backward reads every rank's screen-space gradients straight from its memory
+# (symmetric memory, peer-mapped over NVLink; one node, one GPU per rank) --
+# or "nccl" -- three NCCL all-gathers.
+EXCHANGE_TRANSPORT = "p2p"
+
+
+class PeerArena:
+    """This rank's exchange arena in symmetric memory and every rank's arena
+    as mapped here (``gs_peer_group``), for one Gaussian count.
+
+    Holds the screen-space gradient [n, 9] that compositing backward writes,
+    the tile counts [n], this rank's 29-word view record and the step flags
+    of the peer handshake (see ``gs_exchange_publish``). Created once per
+    (count, device, group) by all ranks together, outside graph capture."""
+
+    def __init__(self, n: int, device: torch.device, group):
+        import torch.distributed._symmetric_memory as symm_mem
+
+        from . import native
+
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("the peer exchange arena is created by an eager step, not "
+                               "inside graph capture")
+        world = dist.get_world_size(group)
+        if world > native.GS_MAX_PEERS:
+            raise ValueError(f"the peer exchange takes at most {native.GS_MAX_PEERS} ranks")
+        # one GPU per rank: the handshake kernels of two ranks must never share one
+        gpus = [None] * world
+        dist.all_gather_object(gpus, (os.uname().nodename, str(torch.cuda.get_device_properties(
+            device).uuid)), group=group)
+        if len(set(gpus)) != world or len({host for host, _ in gpus}) != 1:
+            raise RuntimeError("the peer exchange needs one GPU per rank on one node")
+        lib = native.lib()
+        layout = native.ExchangeLayout()
+        native.check(lib.gs_exchange_layout_for(n, world, ctypes.byref(layout)),
+                     "gs_exchange_layout_for")
+        buffer = symm_mem.empty(int(layout.bytes), dtype=torch.uint8, device=device)
+        buffer.zero_()
+        torch.cuda.synchronize(device)
+        handle = symm_mem.rendezvous(buffer, group)
+        if handle.world_size != world:
+            raise RuntimeError("symmetric memory group does not match the process group")
+        offset = buffer.data_ptr() - handle.buffer_ptrs[handle.rank]
+        if offset < 0 or offset + int(layout.bytes) > handle.buffer_size:
+            raise RuntimeError("exchange arena lies outside its symmetric buffer")
+        arenas = [int(base) + offset for base in handle.buffer_ptrs]
+        if any(address % 256 for address in arenas):
+            raise RuntimeError("exchange arenas must be 256-byte aligned")
+        self.n, self.layout, self.buffer, self.handle = n, layout, buffer, handle
+        slots = arenas + [None] * (native.GS_MAX_PEERS - world)
+        self.group = native.PeerGroup(handle.rank, world,
+                                      (ctypes.c_void_p * native.GS_MAX_PEERS)(*slots))
+        self.grad_projected = buffer[layout.grad_projected:layout.grad_projected + 36 * n] \
+            .view(torch.float32).view(n, 9)
+        self.counts = buffer[layout.counts:layout.counts + 4 * n].view(torch.int32)
+        self.record = buffer[layout.record:layout.record + 4 * native.VIEW_RECORD_WORDS] \
+            .view(torch.int32)
+        # the peers' gradients and counts, bulk-copied here each step
+        self.gathered_grad = torch.empty((world, n, 9), dtype=torch.float32, device=device)
+        self.gathered_counts = torch.empty((world, n), dtype=torch.int32, device=device)
+
+
+_ARENAS: dict = {}
+
+
+def peer_arena(n: int, device: torch.device, group) -> PeerArena:
+    """The exchange arena for ``n`` Gaussians on ``device`` in ``group``
+    (created on first use, by every rank of the group in the same step)."""
+    key = (n, device.index, id(group))
+    arena = _ARENAS.get(key)
+    if arena is None:
+        arena = _ARENAS[key] = PeerArena(n, device, group)
+    return arena
+
+
+def check_exchange() -> None:
+    """Raise if any bounded wait of this rank's peer exchanges gave up (a
+    peer that did not reach the same step within about a second).
+    Synchronises the current stream."""
+    from . import native
+
+    for arena in _ARENAS.values():
+        with torch.cuda.device(arena.buffer.device):
+            stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+            native.check(native.lib().gs_exchange_status(ctypes.byref(arena.group), stream),
+                         "peer exchange (a rank did not reach the same step)")
 
 
 def exchange_screen_gradients(grad_projected: torch.Tensor, counts: torch.Tensor,

@@ -213,6 +213,63 @@ int32_t gs_project_bwd_views(int64_t n, int32_t num_sh, int32_t num_views, const
                              float *grad_scale, float *grad_opacity, float *grad_color,
                              gs_stream_t stream);
 
+/* ------------------------------------------- view-parallel exchange, peers */
+
+#define GS_MAX_PEERS 8
+
+/* A group of ranks (one process per GPU on one node) exchanging screen-space
+ * gradients through peer memory: this rank, the number of ranks, and every
+ * rank's exchange arena as mapped in this process (arena[rank] is this GPU's
+ * own; each 256-byte aligned, all gs_exchange_layout(n).bytes long, zeroed
+ * before first use). */
+typedef struct gs_peer_group {
+  int32_t rank, world;
+  void *arena[GS_MAX_PEERS];
+} gs_peer_group;
+
+/* Byte offsets inside an arena for n Gaussians: the screen-space gradient
+ * [n, 9] float, tile counts [n] int32, this rank's 29-word view record (as
+ * gs_project_bwd_views takes them) and the gathered records of all ranks. */
+typedef struct gs_exchange_layout {
+  uint64_t grad_projected, counts, record, gathered, bytes;
+} gs_exchange_layout;
+
+int32_t gs_exchange_layout_for(int64_t n, int32_t world, gs_exchange_layout *out);
+
+/* One view-parallel backward step, in stream order (all bounded waits; a wait
+ * that gives up sets an error bit that gs_exchange_status reports):
+ *   gs_exchange_begin     wait until every peer finished reading this rank's
+ *                         arena of the previous step;
+ *   (compositing backward into the arena's gradient, counts and record
+ *    copied into it)
+ *   gs_exchange_publish   publish this rank's step, wait for every peer's,
+ *                         gather the view records;
+ *   gs_project_bwd_peers  projection backward summed over every rank's view,
+ *                         reading their gradients and counts from peer memory;
+ *   gs_exchange_finish    tell every peer this rank is done reading.
+ * Step counters live in the arenas, so the sequence replays from a CUDA
+ * graph. No counterpart in the reference (it is single-device). */
+int32_t gs_exchange_begin(const gs_peer_group *group, gs_stream_t stream);
+int32_t gs_exchange_publish(const gs_peer_group *group, int64_t n, gs_stream_t stream);
+/* Optional, after gs_exchange_publish: bulk-copy every peer's gradient and
+ * counts into this GPU's [world, n, 9] / [world, n] buffers (slot p = rank p;
+ * this rank's slot untouched), for gs_project_bwd_peers to read locally. */
+int32_t gs_exchange_gather(const gs_peer_group *group, int64_t n, float *grad_projected,
+                           int32_t *counts, gs_stream_t stream);
+/* Reads each peer's gradient and counts from the gathered buffers when they
+ * are given (NULL: straight from peer memory), this rank's from its arena. */
+int32_t gs_project_bwd_peers(int64_t n, int32_t num_sh, const gs_peer_group *group,
+                             const float *gathered_grad, const int32_t *gathered_counts,
+                             const float *mean, const float *rotation, const float *scale,
+                             const float *opacity, const float *color, float *grad_mean,
+                             float *grad_rotation, float *grad_scale, float *grad_opacity,
+                             float *grad_color, gs_stream_t stream);
+int32_t gs_exchange_finish(const gs_peer_group *group, gs_stream_t stream);
+
+/* GS_OK, or GS_ERR_TIMEOUT if any wait of this rank's exchanges gave up
+ * (sticky). Synchronises `stream`. */
+int32_t gs_exchange_status(const gs_peer_group *group, gs_stream_t stream);
+
 /* Binning error word of a count workspace (0 = fine, else some device-side
  * bounded wait in the last gs_bin_count / gs_bin_sort on these workspaces
  * gave up). Synchronises `stream`. */

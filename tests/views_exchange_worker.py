@@ -4,7 +4,9 @@ by tests/test_gpu_views_backward.py when two or more GPUs are present.
 Each rank renders its own camera of one shared scene; ``train_step`` with the
 screen-space exchange (all-gather of screen-space gradients, one projection
 backward over every rank's view) must give the gradients of ``train_step``
-with the parameter-gradient all-reduce, on every rank.
+with the parameter-gradient all-reduce, on every rank -- with the screen-space
+gradients all-gathered by NCCL, and read from peer memory (also replayed from a
+CUDA graph, which that path allows: it issues no collective).
 """
 
 import datetime
@@ -18,6 +20,8 @@ import torch.distributed as dist
 sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
 from gaussian_splats_b200 import scenes  # noqa: E402
+from gaussian_splats_b200 import view_parallel as VP  # noqa: E402
+from gaussian_splats_b200.graphs import CapturedStep  # noqa: E402
 from gaussian_splats_b200.rasterize import rasterize_outputs  # noqa: E402
 from gaussian_splats_b200.splats import GaussianSplat  # noqa: E402
 from gaussian_splats_b200.view_parallel import train_step  # noqa: E402
@@ -47,29 +51,45 @@ def main():
         def loss_fn(image, t):
             return (image[:240, :320] - t).abs().mean()
 
-        results = []
-        for exchange in (False, True):
+        # gradients summed by all-reducing them, and inside the backward by
+        # the screen-space exchange over NCCL and over peer memory
+        results = {}
+        for mode in ("all-reduce", "nccl", "p2p"):
+            VP.EXCHANGE_TRANSPORT = "nccl" if mode == "nccl" else "p2p"
             train_step(splats, [camera], [target], params, render, loss_fn,
-                       screen_exchange=exchange)
-            results.append([p.grad.clone() for p in params])
-        for name, a, b in zip(("mean", "rotation", "scale", "opacity", "color"), *results):
-            # both paths run compositing backward, whose float atomics add in
-            # scheduling order, and sum the views in different orders: the
-            # absolute tolerance is on the scale of the gradient tensor
-            torch.testing.assert_close(b, a, rtol=1e-4, atol=1e-4 * float(a.abs().max()),
-                                       msg=lambda m: f"{name}: {m}")
-            assert torch.count_nonzero(a) > 0, name
-        for grad in results[1]:  # every rank holds the same summed gradients
-            ref = grad.clone()
-            dist.broadcast(ref, 0)
-            assert torch.equal(ref, grad)
+                       screen_exchange=mode != "all-reduce")
+            results[mode] = [p.grad.clone() for p in params]
+        names = ("mean", "rotation", "scale", "opacity", "color")
+        for mode in ("nccl", "p2p"):
+            for name, a, b in zip(names, results["all-reduce"], results[mode]):
+                # compositing backward's float atomics add in scheduling order,
+                # and the paths sum the views in different orders: the
+                # absolute tolerance is on the scale of the gradient tensor
+                torch.testing.assert_close(b, a, rtol=1e-4, atol=1e-4 * float(a.abs().max()),
+                                           msg=lambda m: f"{mode} {name}: {m}")
+                assert torch.count_nonzero(a) > 0, name
+            for grad in results[mode]:  # every rank holds the same summed gradients
+                ref = grad.clone()
+                dist.broadcast(ref, 0)
+                assert torch.equal(ref, grad), mode
+        # the peer-memory step replayed from a CUDA graph (it issues no collective)
+        VP.EXCHANGE_TRANSPORT = "p2p"
+        step = CapturedStep(lambda: train_step(splats, [camera], [target], params, render,
+                                               loss_fn, screen_exchange=True))
+        for _ in range(3):
+            step()
+        assert step.check()
+        VP.check_exchange()
+        for name, a, p in zip(names, results["p2p"], params):
+            torch.testing.assert_close(p.grad, a, rtol=1e-4, atol=1e-4 * float(a.abs().max()),
+                                       msg=lambda m: f"graph {name}: {m}")
         # the other ranks' views really were added in: the summed gradient
         # differs from this rank's own view alone
         for p in params:
             p.grad = None
         loss_fn(render(splats, camera), target).backward()
         own = params[0].grad
-        assert (own - results[1][0]).abs().max() > 10 * own.abs().max() * 1e-4
+        assert (own - results["p2p"][0]).abs().max() > 10 * own.abs().max() * 1e-4
         dist.barrier()
         if rank == 0:
             print(f"exchange ok at world {world}", flush=True)
