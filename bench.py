@@ -618,14 +618,16 @@ def sort_passes(num_tiles):
     return (bits + 7) // 8
 
 
-def launches_per_view(num_tiles, backward):
+def launches_per_view(num_tiles, backward, peers=False):
     """This library's kernel launches for one view: projection; the count
     phase (histogram, 4 depth passes, count scan); the sort phase (emit,
     histogram when the tile sort has passes, the passes, ranges);
-    compositing; and in the backward compositing and projection backward."""
+    compositing; in a training step the L1 loss (partial sums, total,
+    gradient), compositing backward and projection backward; and with the
+    peer exchange its three handshake kernels."""
     passes = sort_passes(num_tiles)
     forward = 1 + 6 + (2 + (1 + passes if passes else 0)) + 1
-    return forward + (2 if backward else 0)
+    return forward + (5 if backward else 0) + (3 if peers else 0)
 
 
 def main():
@@ -647,6 +649,7 @@ def main():
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
     from gaussian_splats_b200.graphs import CapturedStep
+    from gaussian_splats_b200.losses import l1_loss
     from gaussian_splats_b200.rasterize import StageTimer, rasterize_batch, rasterize_outputs
     from gaussian_splats_b200.splats import GaussianSplat
     from gaussian_splats_b200 import view_parallel
@@ -677,7 +680,8 @@ def main():
                                  settings.near, settings.far)
 
     def loss_fn(image, target):
-        return (image[:crop_h, :crop_w] - target).abs().mean()
+        # (image[:crop_h, :crop_w] - target).abs().mean(), fused
+        return l1_loss(image, target)
 
     def forward_step(s=splats):
         with torch.no_grad():
@@ -945,7 +949,8 @@ def main():
         "roofline": main_roof, "rooflines": rooflines, "optimizer": optimizer,
         "e2e": {"value": views_per_step * 1000.0 / e2e_ms, "unit": UNIT, "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-        "gpu_launches": (launches_per_view(num_tiles, backward) * per_view if not batched else
+        "gpu_launches": (launches_per_view(num_tiles, backward, peers) * per_view
+                         if not batched else
                          (launches_per_view(num_tiles, False) - 1) * per_view
                          + -(-per_view // BATCH_VIEWS)) * args.steps,
         "clocks": clock,

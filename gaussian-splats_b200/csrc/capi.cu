@@ -52,6 +52,11 @@ int32_t launch_exchange_publish(const gs_peer_group&, int64_t, cudaStream_t);
 int32_t launch_exchange_finish(const gs_peer_group&, cudaStream_t);
 int32_t exchange_gather(const gs_peer_group&, int64_t, float*, int32_t*, cudaStream_t);
 int32_t exchange_status(const gs_peer_group&, cudaStream_t);
+int32_t launch_l1_fwd(const float*, int64_t, int64_t, int64_t, const float*, int64_t, int64_t,
+                      float*, float*, cudaStream_t);
+int32_t launch_l1_bwd(const float*, int64_t, int64_t, int64_t, const float*, int64_t, int64_t,
+                      const float*, float*, cudaStream_t);
+int64_t l1_partials();
 size_t relocate_workspace_size(int64_t);
 int32_t launch_relocate(int64_t, int64_t, int32_t, const int64_t*, int64_t, const int64_t*,
                         int64_t, const gs_splat_arrays&, float*, const gs_splat_arrays*,
@@ -378,6 +383,24 @@ int32_t gs_relocate(int64_t n_src, int64_t n_rows, int32_t num_sh, const int64_t
 int32_t gs_relocate_status(const void* workspace, gs_stream_t stream) {
   if (!workspace) return GS_ERR_INVALID_ARGUMENT;
   return gs::relocate_status(workspace, as_cuda(stream));
+}
+
+int64_t gs_l1_loss_scratch_floats(void) { return gs::l1_partials(); }
+
+int32_t gs_l1_loss(const float* image, int64_t height, int64_t width, int64_t channels,
+                   const float* target, int64_t target_height, int64_t target_width,
+                   float* scratch, float* loss, gs_stream_t stream) {
+  if (height < 0 || width < 0) return GS_ERR_INVALID_ARGUMENT;
+  return gs::launch_l1_fwd(image, height, width, channels, target, target_height, target_width,
+                           scratch, loss, as_cuda(stream));
+}
+
+int32_t gs_l1_loss_backward(const float* image, int64_t height, int64_t width, int64_t channels,
+                            const float* target, int64_t target_height, int64_t target_width,
+                            const float* grad_loss, float* grad_image, gs_stream_t stream) {
+  if (height < 0 || width < 0) return GS_ERR_INVALID_ARGUMENT;
+  return gs::launch_l1_bwd(image, height, width, channels, target, target_height, target_width,
+                           grad_loss, grad_image, as_cuda(stream));
 }
 
 int32_t gs_det_exp(int64_t n, const float* x, float* y, gs_stream_t stream) {

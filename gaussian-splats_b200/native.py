@@ -49,6 +49,9 @@ EXPORTED_SYMBOLS = (
     "gs_project_bwd_peers",
     "gs_exchange_finish",
     "gs_exchange_status",
+    "gs_l1_loss_scratch_floats",
+    "gs_l1_loss",
+    "gs_l1_loss_backward",
     "gs_relocate",
     "gs_relocate_status",
     "gs_relocate_workspace_size",
@@ -215,6 +218,9 @@ def lib() -> ctypes.CDLL:
         "gs_project_bwd_peers": ([i64, i32, ctypes.POINTER(PeerGroup)] + [vp] * 12 + [vp], i32),
         "gs_exchange_finish": ([ctypes.POINTER(PeerGroup), vp], i32),
         "gs_exchange_status": ([ctypes.POINTER(PeerGroup), vp], i32),
+        "gs_l1_loss_scratch_floats": ([], i64),
+        "gs_l1_loss": ([vp, i64, i64, i64, vp, i64, i64, vp, vp, vp], i32),
+        "gs_l1_loss_backward": ([vp, i64, i64, i64, vp, i64, i64, vp, vp, vp], i32),
         "gs_relocate": ([i64, i64, i32, vp, i64, vp, i64, ctypes.POINTER(SplatArrays), vp,
                          ctypes.POINTER(SplatArrays), ctypes.POINTER(SplatArrays), vp,
                          ctypes.c_uint64, vp], i32),

@@ -341,6 +341,29 @@ int32_t gs_relocate(int64_t n_src, int64_t n_rows, int32_t num_sh, const int64_t
  * output row outside [0, n_rows). Synchronises `stream`. */
 int32_t gs_relocate_status(const void *workspace, gs_stream_t stream);
 
+/* ----------------------------------------------------------- training loss */
+
+/* Float words of scratch gs_l1_loss needs (per-block partial sums). */
+int64_t gs_l1_loss_scratch_floats(void);
+
+/* L1 photometric loss (training/train.py:140: (image - target).abs().mean())
+ * over the target's extent: image [height, width, channels] float32, target
+ * [target_height, target_width, channels] covering the image's top-left
+ * corner (the rendered image is padded to whole tiles). Writes the mean to
+ * the device scalar `loss` (deterministic order; not bit-identical to
+ * torch's mean). */
+int32_t gs_l1_loss(const float *image, int64_t height, int64_t width, int64_t channels,
+                   const float *target, int64_t target_height, int64_t target_width,
+                   float *scratch, float *loss, gs_stream_t stream);
+
+/* Its gradient for the whole image, padding included: sign(image - target)
+ * times (*grad_loss x the float reciprocal of the element count) inside the
+ * target's extent, zero outside -- the values of torch's abs / mean / slice
+ * backward chain, bit for bit. */
+int32_t gs_l1_loss_backward(const float *image, int64_t height, int64_t width, int64_t channels,
+                            const float *target, int64_t target_height, int64_t target_width,
+                            const float *grad_loss, float *grad_image, gs_stream_t stream);
+
 /* The deterministic exp / log the kernels use, applied elementwise (test hook
  * for bitwise agreement with the CPU oracle). */
 int32_t gs_det_exp(int64_t n, const float *x, float *y, gs_stream_t stream);

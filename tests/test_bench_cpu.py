@@ -40,9 +40,10 @@ def test_launch_count_per_view():
     # 1080p at 16x16: 8160 tiles, 13 bits, two tile-sort passes.
     assert bench.sort_passes(8160) == 2 and bench.sort_passes(256) == 1
     assert bench.sort_passes(1) == 0
-    assert bench.launches_per_view(8160, backward=True) == 15
+    assert bench.launches_per_view(8160, backward=True) == 18
+    assert bench.launches_per_view(8160, backward=True, peers=True) == 21
     assert bench.launches_per_view(8160, backward=False) == 13
-    assert bench.launches_per_view(256, backward=True) == 14
+    assert bench.launches_per_view(256, backward=True) == 17
     assert bench.launches_per_view(1, backward=False) == 10
 
 
