@@ -244,11 +244,14 @@ int32_t gs_exchange_layout_for(int64_t n, int32_t world, gs_exchange_layout *out
  *    copied into it)
  *   gs_exchange_publish   publish this rank's step, wait for every peer's,
  *                         gather the view records;
- *   gs_project_bwd_peers  projection backward summed over every rank's view,
- *                         reading their gradients and counts from peer memory;
- *   gs_exchange_finish    tell every peer this rank is done reading.
- * Step counters live in the arenas, so the sequence replays from a CUDA
- * graph. No counterpart in the reference (it is single-device). */
+ *   gs_exchange_gather    bulk-copy the peers' gradients and counts here;
+ *   gs_exchange_finish    tell every peer this rank is done reading (right
+ *                         after the gather: nothing reads peer memory later);
+ *   gs_project_bwd_peers  projection backward summed over every rank's view.
+ * Without the gather, gs_project_bwd_peers reads the peers' arenas directly
+ * and gs_exchange_finish must come after it. Step counters live in the
+ * arenas, so the sequence replays from a CUDA graph. No counterpart in the
+ * reference (it is single-device). */
 int32_t gs_exchange_begin(const gs_peer_group *group, gs_stream_t stream);
 int32_t gs_exchange_publish(const gs_peer_group *group, int64_t n, gs_stream_t stream);
 /* Optional, after gs_exchange_publish: bulk-copy every peer's gradient and
