@@ -71,6 +71,12 @@ constexpr int min_blocks_for_32_warps(int threads) {
   return 1024 / threads < 16 ? 1024 / threads : 16;
 }
 
+// Resident CTAs the forward compositor is compiled for: six 256-thread CTAs
+// (48 warps) fit its state in 39 registers without spills, against five at
+// its natural 48. Tiles whose six CTAs would not fit an SM's 2048 threads
+// (32x32) keep the unconstrained allocation.
+constexpr int forward_min_blocks(int threads) { return threads * 6 <= 2048 ? 6 : 1; }
+
 template <int TS, int PPT>
 struct PixelMap {
   using S = TileShape<TS, PPT>;
@@ -217,7 +223,9 @@ __device__ __forceinline__ int warp_select(const PixelMap<TS, PPT>& pm, const fl
 }
 
 template <int TS, bool kGaussian>
-__global__ void __launch_bounds__(TileShape<TS, 1>::kThreads) composite_fwd_kernel(
+__global__ void __launch_bounds__(TileShape<TS, 1>::kThreads,
+                                  forward_min_blocks(TileShape<TS, 1>::kThreads))
+    composite_fwd_kernel(
     const float* __restrict__ projected_mean, const float* __restrict__ inverse_covariance,
     const float* __restrict__ projected_color, const float* __restrict__ projected_opacity,
     const int32_t* __restrict__ gaussian_ids, const int64_t* __restrict__ ranges,
