@@ -52,7 +52,11 @@ __device__ __forceinline__ float det_exp(float x) {
 // (n >= -126), so det_exp's step for subnormal results is left out. Same bits
 // as det_exp on that domain.
 __device__ __forceinline__ float det_exp_nonpositive(float x) {
-  float n = rintf(x * kLog2e);
+  // rintf(x log2e) without a conversion instruction: adding 1.5 * 2^23 to a
+  // value below 2^22 in magnitude rounds it to the nearest integer, ties to
+  // even, as rintf does; the integer is then also the sum's low bits.
+  const float shifted = x * kLog2e + 12582912.0f;
+  const float n = shifted - 12582912.0f;
   float r = fmaf(-n, kLn2Hi, x);
   r = fmaf(-n, kLn2Lo, r);
   float p = 1.98412698e-4f;
@@ -63,7 +67,7 @@ __device__ __forceinline__ float det_exp_nonpositive(float x) {
   p = fmaf(p, r, 0.5f);
   p = fmaf(p, r, 1.0f);
   p = fmaf(p, r, 1.0f);
-  const int e = static_cast<int>(n);
+  const int e = __float_as_int(shifted) - 0x4B400000;  // n as an integer
   return p * __uint_as_float(static_cast<uint32_t>(e + 127) << 23);
 }
 
