@@ -68,7 +68,9 @@ __device__ __forceinline__ float det_exp_nonpositive(float x) {
   p = fmaf(p, r, 1.0f);
   p = fmaf(p, r, 1.0f);
   const int e = __float_as_int(shifted) - 0x4B400000;  // n as an integer
-  return p * __uint_as_float(static_cast<uint32_t>(e + 127) << 23);
+  // p * 2^n: p lies in [0.7, 1.42] and n >= -126 keeps the product normal,
+  // where the scaling is exact -- an add to p's exponent field.
+  return __int_as_float(__float_as_int(p) + (e << 23));
 }
 
 __device__ __forceinline__ float det_log(float x) {
