@@ -158,7 +158,8 @@ _ARENAS: dict = {}
 def peer_arena(n: int, device: torch.device, group) -> PeerArena:
     """The exchange arena for ``n`` Gaussians on ``device`` in ``group``
     (created on first use, by every rank of the group in the same step)."""
-    key = (n, device.index, id(group))
+    # by group name: a destroyed group's id() can come back for a new group
+    key = (n, device.index, getattr(group, "group_name", None) or id(group))
     arena = _ARENAS.get(key)
     if arena is None:
         arena = _ARENAS[key] = PeerArena(n, device, group)
