@@ -74,18 +74,6 @@ bool valid_sh(int32_t num_sh) {
   return num_sh == 1 || num_sh == 4 || num_sh == 9 || num_sh == 16 || num_sh == 25;
 }
 
-int32_t check_params(const gs_params* p) {
-  if (!p) return GS_ERR_INVALID_ARGUMENT;
-  const int ts = p->tile_size;
-  if (ts != 4 && ts != 8 && ts != 16 && ts != 32) return GS_ERR_INVALID_ARGUMENT;
-  if (p->width < 0 || p->height < 0 || p->width % ts || p->height % ts)
-    return GS_ERR_INVALID_ARGUMENT;
-  return GS_OK;
-}
-
-// Gaussian index and intersection offsets are 32-bit in the binning kernels.
-constexpr int64_t kMaxGaussians = int64_t{1} << 30;
-constexpr int64_t kMaxIntersections = int64_t{1} << 30;
 }  // namespace
 
 void set_cuda_error(cudaError_t err) { g_last_cuda_error = static_cast<int32_t>(err); }

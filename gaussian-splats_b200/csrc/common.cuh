@@ -46,6 +46,21 @@ inline cudaStream_t as_cuda(gs_stream_t s) { return reinterpret_cast<cudaStream_
 
 inline unsigned ceil_div(int64_t a, int64_t b) { return static_cast<unsigned>((a + b - 1) / b); }
 
+// Gaussian index and intersection offsets are 32-bit in the binning kernels.
+constexpr int64_t kMaxGaussians = int64_t{1} << 30;
+constexpr int64_t kMaxIntersections = int64_t{1} << 30;
+
+// Render scalars every entry point validates the same way: a tile size the
+// kernels are instantiated for, and an image of whole tiles.
+inline int32_t check_params(const gs_params* p) {
+  if (!p) return GS_ERR_INVALID_ARGUMENT;
+  const int ts = p->tile_size;
+  if (ts != 4 && ts != 8 && ts != 16 && ts != 32) return GS_ERR_INVALID_ARGUMENT;
+  if (p->width < 0 || p->height < 0 || p->width % ts || p->height % ts)
+    return GS_ERR_INVALID_ARGUMENT;
+  return GS_OK;
+}
+
 // Pair evaluation shared by the forward and backward compositors:
 // d^2 = xx dx^2 + 2 xy dx dy + yy dy^2 with integer pixel coordinates
 // (composite.py:159-161), evaluated as fmaf(xx*dx, dx, fmaf((2xy)*dx, dy, (yy*dy)*dy)).

@@ -31,6 +31,7 @@ int32_t launch_bin_sort(int64_t, int64_t, const int32_t*, const int32_t*, const 
                         const void*, void*, int32_t*, int64_t*, cudaStream_t);
 uint64_t bin_count_workspace_size(int64_t);
 uint64_t bin_sort_workspace_size(int64_t, int64_t);
+uint64_t bin_error_word_offset();
 
 namespace {
 
@@ -66,10 +67,9 @@ extern "C" int32_t gs_bin_noalloc(int64_t n, const float* projected_mean, const 
                                   const int32_t* bounds, const gs_params* params,
                                   int32_t* gaussian_ids, int64_t ids_capacity, int64_t* ranges,
                                   int64_t* total_host, gs_stream_t stream) {
-  if (!params || !total_host || n < 0 || ids_capacity < 0) return GS_ERR_INVALID_ARGUMENT;
-  const int ts = params->tile_size;
-  if ((ts != 4 && ts != 8 && ts != 16 && ts != 32) || params->width < 0 ||
-      params->height < 0 || params->width % ts || params->height % ts)
+  // The same checks as gs_bin_count + gs_bin_sort.
+  GS_TRY(gs::check_params(params));
+  if (!total_host || n < 0 || n >= gs::kMaxGaussians || ids_capacity < 0)
     return GS_ERR_INVALID_ARGUMENT;
   if (reinterpret_cast<uintptr_t>(bounds) % 16) return GS_ERR_MISALIGNED;
   *total_host = 0;
@@ -83,12 +83,20 @@ extern "C" int32_t gs_bin_noalloc(int64_t n, const float* projected_mean, const 
   GS_TRY(gs::launch_bin_count(n, projected_mean, counts, scratch, &total, &error, s));
   *total_host = total;
   if (error) return GS_ERR_TIMEOUT;
+  const int ts = params->tile_size;
   const int64_t num_tiles =
       static_cast<int64_t>(params->width / ts) * (params->height / ts);
-  if (total > ids_capacity || total >= (int64_t{1} << 30) ||
+  if (total > ids_capacity || total >= gs::kMaxIntersections ||
       count_bytes + gs::bin_sort_workspace_size(total, num_tiles) > gs::kScratchBytes)
     return GS_ERR_CAPACITY;  // *total_host says how many intersections there were
-  void* sort_scratch = static_cast<char*>(scratch) + count_bytes;
-  return gs::launch_bin_sort(n, total, bounds, counts, *params, scratch, sort_scratch,
-                             gaussian_ids, ranges, s);
+  char* sort_scratch = static_cast<char*>(scratch) + count_bytes;
+  GS_TRY(gs::launch_bin_sort(n, total, bounds, counts, *params, scratch, sort_scratch,
+                             gaussian_ids, ranges, s));
+  // The tile sort's look-back waits report into the sort scratch's error
+  // word, which only this library can reach: read it back before returning.
+  uint32_t sort_error = 0;
+  GS_CUDA_TRY(cudaMemcpyAsync(&sort_error, sort_scratch + gs::bin_error_word_offset(),
+                              sizeof(sort_error), cudaMemcpyDeviceToHost, s));
+  GS_CUDA_TRY(cudaStreamSynchronize(s));
+  return sort_error ? GS_ERR_TIMEOUT : GS_OK;
 }

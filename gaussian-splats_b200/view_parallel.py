@@ -152,18 +152,41 @@ class PeerArena:
         self.gathered_counts = torch.empty((world, n), dtype=torch.int32, device=device)
 
 
+# Exchange arenas by (Gaussian count, device, id of the process group). Each
+# entry holds its group object, so that id cannot be handed to another group
+# while the entry lives: a group created after destroy_process_group() --
+# even one with the same name, which torch reuses after a re-initialisation --
+# is a different object and gets an arena of its own.
 _ARENAS: dict = {}
+
+
+def _resolve(group):
+    return group if group is not None else dist.group.WORLD
 
 
 def peer_arena(n: int, device: torch.device, group) -> PeerArena:
     """The exchange arena for ``n`` Gaussians on ``device`` in ``group``
     (created on first use, by every rank of the group in the same step)."""
-    # by group name: a destroyed group's id() can come back for a new group
-    key = (n, device.index, getattr(group, "group_name", None) or id(group))
-    arena = _ARENAS.get(key)
-    if arena is None:
-        arena = _ARENAS[key] = PeerArena(n, device, group)
-    return arena
+    group = _resolve(group)
+    key = (n, device.index, id(group))
+    entry = _ARENAS.get(key)
+    if entry is None or entry[0] is not group:
+        entry = _ARENAS[key] = (group, PeerArena(n, device, group))
+    return entry[1]
+
+
+def release_arenas(group=None) -> int:
+    """Free this process's exchange arenas of ``group`` (of every group when
+    None) and return how many were dropped. Call it before
+    ``destroy_process_group``: an arena belongs to its group (its symmetric
+    memory handle, peer mappings and step counters), and the group's ranks
+    must not use it again. Every rank of the group calls it at the same point,
+    with nothing of the exchange in flight."""
+    doomed = [key for key, (owner, _) in _ARENAS.items()
+              if group is None or owner is _resolve(group)]
+    for key in doomed:
+        del _ARENAS[key]
+    return len(doomed)
 
 
 def check_exchange() -> None:
@@ -172,7 +195,7 @@ def check_exchange() -> None:
     Synchronises the current stream."""
     from . import native
 
-    for arena in _ARENAS.values():
+    for _, arena in _ARENAS.values():
         with torch.cuda.device(arena.buffer.device):
             stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
             native.check(native.lib().gs_exchange_status(ctypes.byref(arena.group), stream),

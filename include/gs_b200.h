@@ -157,7 +157,11 @@ uint64_t gs_bin_sort_workspace_size(int64_t total, int64_t num_tiles);
  *    contents (every call clears what it needs); calls whose GPU work
  *    overlaps -- other streams, other host threads -- race on it, so
  *    serialise them.
- *  - Synchronises `stream` once, to read the intersection total. */
+ *  - Synchronises `stream` twice: after the count phase, to read the
+ *    intersection total, and at the end, to read the error word of the sort
+ *    phase, which lives in the library's array where gs_bin_check cannot
+ *    reach it. GS_ERR_TIMEOUT means a bounded wait of either phase gave up
+ *    (the ids and ranges are then invalid). */
 int32_t gs_bin_noalloc(int64_t n, const float *projected_mean, const int32_t *counts,
                        const int32_t *bounds, const gs_params *params, int32_t *gaussian_ids,
                        int64_t ids_capacity, int64_t *ranges, int64_t *total_host,

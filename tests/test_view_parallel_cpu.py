@@ -193,3 +193,41 @@ def test_collectives_are_counted_for_the_graph_guard(monkeypatch):
         g.grad = torch.ones(3)
     all_reduce_gradients(grads)
     assert view_parallel.COLLECTIVE_CALLS == before + 1
+
+
+def _arena_worker(rank, world, port, results):
+    """Arena bookkeeping across a destroyed and re-created process group (the
+    symmetric-memory arena itself is replaced by a stand-in: no GPU here)."""
+    from gaussian_splats_b200 import view_parallel as vp
+
+    made = []
+
+    class FakeArena:
+        def __init__(self, n, device, group):
+            made.append((n, group))
+
+    vp.PeerArena = FakeArena
+    device = torch.device("cpu")
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    first = vp.peer_arena(10, device, None)
+    assert vp.peer_arena(10, device, None) is first  # cached while the group lives
+    dist.destroy_process_group()  # without release_arenas: the stale entry stays
+    os.environ["MASTER_PORT"] = str(port + 1)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    second = vp.peer_arena(10, device, None)  # a new group gets a new arena
+    released = vp.release_arenas(None)  # every group's arenas
+    third = vp.peer_arena(10, device, None)
+    assert vp.release_arenas(dist.group.WORLD) == 1
+    dist.destroy_process_group()
+    results[rank] = (second is not first, third is not second, released, len(made))
+
+
+def test_arenas_are_rebuilt_for_a_recreated_group():
+    world = 2
+    manager = mp.Manager()
+    results = manager.dict()
+    port = _free_port()
+    mp.spawn(_arena_worker, args=(world, port, results), nprocs=world, join=True)
+    for rank in range(world):
+        assert results[rank] == (True, True, 2, 3)

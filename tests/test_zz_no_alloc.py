@@ -119,3 +119,78 @@ def test_noalloc_refuses_what_does_not_fit():
     status = lib.gs_bin_noalloc(n_big, None, None, None, ctypes.byref(params), None, 0, None,
                                 ctypes.byref(total), None)
     assert status == GS_ERR_CAPACITY
+
+
+SCRATCH_BYTES = 64 << 20  # the library's fixed scratch array
+
+
+def _synthetic_tiles(n, tiles_w, tiles_h, total, seed):
+    """n Gaussians as the binning reads them -- depths, per-Gaussian tile
+    counts and tile rectangles with count == area -- whose counts add up to
+    exactly `total` (rows of 1 x w rectangles take up the remainder)."""
+    rng = np.random.default_rng(seed)
+    widths = rng.integers(1, 17, n)
+    heights = rng.integers(1, 9, n)
+    heights[::2] = 1  # half the rows stay one tile high, to take the remainder
+    area = widths * heights
+    # Scale the random rectangles down until they leave room for the rest.
+    keep = np.cumsum(area) <= total - (n - np.arange(1, n + 1))
+    widths[~keep], heights[~keep] = 1, 1
+    remainder = total - int((widths * heights).sum())
+    row = 0
+    while remainder > 0:  # widen single-row rectangles, up to a full row each
+        if heights[row] == 1:
+            add = min(remainder, tiles_w - int(widths[row]))
+            widths[row] += add
+            remainder -= add
+        row += 1
+    assert int((widths * heights).sum()) == total
+    x0 = rng.integers(0, tiles_w - widths + 1)
+    y0 = rng.integers(0, tiles_h - heights + 1)
+    bounds = np.stack([x0, x0 + widths, y0, y0 + heights], 1).astype(np.int32)
+    counts = (widths * heights).astype(np.int32)
+    pm = np.zeros((n, 3), np.float32)
+    pm[:, 2] = rng.uniform(0.5, 50.0, n).astype(np.float32)
+    return (torch.from_numpy(pm).cuda(), torch.from_numpy(counts).cuda(),
+            torch.from_numpy(bounds).cuda())
+
+
+def test_noalloc_limit_is_the_documented_scratch_size():
+    """Just under the 64 MiB limit (count-phase scratch for n Gaussians plus
+    sort-phase scratch for the total, as the workspace-size queries report
+    them) the call is accepted and matches the regular path; one intersection
+    more is refused with GS_ERR_CAPACITY and the total still reported."""
+    from gaussian_splats_b200 import native
+
+    lib = native.lib()
+    n, tile, tiles_w, tiles_h = 100_000, 16, 64, 64
+    params = native.make_params(500.0, 500.0, 512.0, 512.0, tiles_w * tile, tiles_h * tile,
+                                tile, 0.999, 0.2, 100.0, "gaussian", 0.95)
+    num_tiles = tiles_w * tiles_h
+    count_bytes = (lib.gs_bin_count_workspace_size(n) + 255) // 256 * 256
+
+    def fits(t):
+        return count_bytes + lib.gs_bin_sort_workspace_size(t, num_tiles) <= SCRATCH_BYTES
+
+    lo, hi = 0, SCRATCH_BYTES // 4
+    while lo + 1 < hi:  # largest total that fits
+        mid = (lo + hi) // 2
+        lo, hi = (mid, hi) if fits(mid) else (lo, mid)
+    limit = lo
+    assert fits(limit) and not fits(limit + 1)
+    assert 3_000_000 < limit < 4_100_000  # ~16.3 B per intersection after ~2 MB for n
+
+    pm, counts, bounds = _synthetic_tiles(n, tiles_w, tiles_h, limit, seed=5)
+    ref_ids, ref_ranges = _regular(lib, native, params, pm, counts, bounds)
+    assert len(ref_ids) == limit
+    status, total, ids, ranges = _noalloc(lib, native, params, pm, counts, bounds,
+                                          capacity=limit)
+    native.check(status, "gs_bin_noalloc at its limit")
+    assert total == limit
+    np.testing.assert_array_equal(ids, ref_ids)
+    np.testing.assert_array_equal(ranges, ref_ranges)
+
+    pm, counts, bounds = _synthetic_tiles(n, tiles_w, tiles_h, limit + 1, seed=6)
+    status, total, _, _ = _noalloc(lib, native, params, pm, counts, bounds,
+                                   capacity=limit + 1)
+    assert status == GS_ERR_CAPACITY and total == limit + 1
