@@ -25,7 +25,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import time
 
@@ -74,14 +73,18 @@ def project_bwd_bytes(k):
 PROJECT_FWD_BYTES = project_fwd_bytes(16)
 PROJECT_BWD_BYTES = project_bwd_bytes(16)
 # Per evaluated (pixel, Gaussian) pair, the reference's forward arithmetic
-# (composite.py:159-186): offsets 2, distance 9, exp argument 1, exp 1,
-# alpha 4, activity test 3, weight 2, colour 6, transmittance 3.
-COMPOSITE_FWD_FLOPS = 31
+# (composite.py:159-186): offsets 2, distance 9, exp argument 1, exp 13 (the
+# FP32 operations of the deterministic exp: range reduction 5, degree-7
+# polynomial 8), alpha 4, activity test 3, weight 2, colour 6, transmittance 3.
+COMPOSITE_FWD_FLOPS = 43
 # Backward per evaluated pair (composite_bwd.py:101-195 without the dropped
-# abs-gradient): distance and alpha 16, T recovery 5, weight gradient 9,
-# alpha/opacity/distance gradients 6, mean/conic gradients 14, colour 4,
-# suffix update 10.
-COMPOSITE_BWD_FLOPS = 64
+# abs-gradient): distance and alpha 28 (exp 13 as above), T recovery 5, weight
+# gradient 9, alpha/opacity/distance gradients 6, mean/conic gradients 14,
+# colour 4, suffix update 10.
+COMPOSITE_BWD_FLOPS = 76
+# Warp schedulers per SM (one instruction issued per scheduler per cycle) and
+# SMs of a B200: the issue roof of the compositors.
+SCHEDULERS_PER_SM, SM_COUNT = 4, 148
 
 
 def parse_args():
@@ -115,75 +118,79 @@ def load_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    """SM clock, power and throttle reasons of this rank's GPU, sampled every
+    PERIOD_S while the timed region runs, through NVML (the library behind
+    nvidia-smi) from a background thread. The timed loop spends its time in
+    ``torch.cuda.synchronize()``, which releases the GIL, so a millisecond-scale
+    period yields a few samples per millisecond of timed GPU work."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
-    PERIOD_MS = 50
+    PERIOD_S = 0.001
+    # NVML clock-event reason bits (nvml.h: nvmlClocksEventReason*)
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown"}
 
-    def __init__(self, index):
-        self.index = index
-        self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_rank{index}.csv")
+    def __init__(self, device_index):
+        self.device_index = device_index
+        self.samples = []
+        self.thread = None
+        self.max_mhz = None
+
+    def _handle(self, nvml):
+        uuid = str(torch.cuda.get_device_properties(self.device_index).uuid)
+        for i in range(nvml.nvmlDeviceGetCount()):
+            handle = nvml.nvmlDeviceGetHandleByIndex(i)
+            name = nvml.nvmlDeviceGetUUID(handle)
+            name = name.decode() if isinstance(name, bytes) else name
+            if name.endswith(uuid):
+                return handle
+        return None
 
     def __enter__(self):
+        import threading
+
         try:
-            os.makedirs(os.path.dirname(self.path), exist_ok=True)
-            self.file = open(self.path, "w")
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-i", str(self.index), "-lms", str(self.PERIOD_MS)], stdout=self.file,
-                stderr=subprocess.DEVNULL)
-        except (OSError, FileNotFoundError):
-            self.proc = None
+            import pynvml as nvml
+
+            nvml.nvmlInit()
+            handle = self._handle(nvml)
+        except Exception:  # no NVML: the line carries no clock record
             return self
-        # nvidia-smi takes a moment to start; begin timing once it samples.
-        deadline = time.time() + 5.0
-        while time.time() < deadline and os.path.getsize(self.path) == 0:
-            time.sleep(0.02)
-        self.lines_before = self._line_count()
+        if handle is None:
+            return self
+        self.max_mhz = float(nvml.nvmlDeviceGetMaxClockInfo(handle, nvml.NVML_CLOCK_SM))
+        reasons = getattr(nvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nvml.nvmlDeviceGetCurrentClocksThrottleReasons
+        self.stop = threading.Event()
+
+        def sample():
+            while not self.stop.is_set():
+                self.samples.append((float(nvml.nvmlDeviceGetClockInfo(handle, nvml.NVML_CLOCK_SM)),
+                                     int(reasons(handle)),
+                                     nvml.nvmlDeviceGetPowerUsage(handle) / 1000.0))
+                time.sleep(self.PERIOD_S)
+
+        self.thread = threading.Thread(target=sample, daemon=True)
+        self.thread.start()
+        deadline = time.time() + 2.0
+        while not self.samples and time.time() < deadline:
+            time.sleep(self.PERIOD_S)
+        self.samples.clear()  # keep what the timed region saw
         return self
 
-    def _line_count(self):
-        with open(self.path) as f:
-            return sum(1 for _ in f)
-
     def __exit__(self, *exc):
-        if self.proc is not None:
-            # Samples written up to now (plus the one in flight) cover the
-            # region; later ones would be of an idle GPU.
-            time.sleep(self.PERIOD_MS / 1000.0)
-            self.lines_after = self._line_count()
-            self.proc.terminate()
-            self.proc.wait(timeout=10)
-            self.file.close()
+        if self.thread is not None:
+            self.stop.set()
+            self.thread.join(timeout=5)
 
     def summary(self):
-        if self.proc is None:
+        if not self.samples:
             return None
-        rows = []
-        with open(self.path) as f:
-            lines = f.readlines()
-        # Keep the samples taken while the timed region ran (the last one
-        # before it started bounds it from below).
-        first = max(0, self.lines_before - 1)
-        window = lines[first:self.lines_after] or lines
-        for line in window:
-            parts = [x.strip() for x in line.split(",")]
-            if len(parts) >= 9 and parts[1].replace(".", "").isdigit():
-                rows.append(parts)
-        if not rows:
-            return None
-        sm = [float(r[1]) for r in rows]
-        reasons = set()
-        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        for r in rows:
-            for name, flag in zip(names, r[5:9]):
-                if flag.lower() == "active":
-                    reasons.add(name)
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": float(rows[0][2]),
-                "samples": len(rows), "reasons": sorted(reasons)}
+        reasons = sorted({name for _, bits, _ in self.samples
+                          for bit, name in self.REASONS.items() if bits & bit})
+        return {"sm_mhz": statistics.median(mhz for mhz, _, _ in self.samples),
+                "sm_max_mhz": self.max_mhz, "samples": len(self.samples),
+                "power_w_max": max(w for _, _, w in self.samples), "reasons": reasons,
+                "source": f"NVML every {self.PERIOD_S * 1e3:g} ms during the timed region"}
 
 
 def fp32_peak_tflops(device):
@@ -208,6 +215,43 @@ def fp32_peak_tflops(device):
         return 2 * 8192 ** 3 / (best * 1e-3) / 1e12
     finally:
         torch.backends.cuda.matmul.allow_tf32 = prev
+
+
+PARITY_RTOL, PARITY_ATOL = 1e-4, 1e-6  # the parameter-gradient tolerance of the contract
+
+
+def gradient_parity(step, local_view, trainable, device):
+    """Checks the multi-GPU step's summed gradients on every rank.
+
+    ``step()`` is the timed step (graph replay or Python launch, with its
+    exchange: peer memory or all-reduce), which leaves the summed parameter
+    gradients in ``.grad``. The check recomputes them the plain way: this
+    rank's views forward and backward with no exchange (``local_view``), then
+    one NCCL all-reduce per parameter. Tolerance: |a - b| <= atol + rtol |b|
+    elementwise. Returns the worst figures over ranks; every rank gets the
+    same answer."""
+    step()
+    torch.cuda.synchronize()
+    got = [p.grad.detach().clone() for p in trainable]
+    local_view()
+    for p in trainable:
+        torch.distributed.all_reduce(p.grad)
+    max_abs = ratio = max_rel = 0.0
+    for a, p in zip(got, trainable):
+        b = p.grad
+        err = (a - b).abs()
+        max_abs = max(max_abs, float(err.max()))
+        ratio = max(ratio, float((err / (PARITY_ATOL + PARITY_RTOL * b.abs())).max()))
+        beyond_atol = err > PARITY_ATOL
+        if bool(beyond_atol.any()):
+            max_rel = max(max_rel, float((err[beyond_atol] / b.abs()[beyond_atol]).max()))
+    worst = torch.tensor([max_abs, ratio, max_rel], device=device)
+    torch.distributed.all_reduce(worst, op=torch.distributed.ReduceOp.MAX)
+    max_abs, ratio, max_rel = worst.tolist()
+    return {"max_abs": max_abs, "max_rel": max_rel, "max_tol_ratio": ratio,
+            "rtol": PARITY_RTOL, "atol": PARITY_ATOL, "ok": ratio <= 1.0,
+            "against": "rank-local backward of each rank's views + NCCL all-reduce of the "
+                       "parameter gradients"}
 
 
 def kernel_durations(outputs, params, camera, grad_image, settings, device, repeats=5):
@@ -318,140 +362,104 @@ def views_for_rank(scene, config, rank, world):
             for i in shard_views(len(scene.cameras), world, rank)]
 
 
-# Seconds of CPU work the reference arm may spend on its timed and warm-up
-# steps together. A step always composites at least MIN_SAMPLE_TILES tiles
-# (enough to keep every host thread busy); the chunk of Gaussians projected,
-# binned and back-projected shrinks with the time left per step.
-REFERENCE_BUDGET_S = 120.0
-MIN_SAMPLE_TILES = 128
+def host_cores():
+    """Host CPU cores this process may run on."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
 
 
-def sample_size(steps, warmup, num_points):
-    """(Gaussians in the chunk, tiles) of one reference-arm step."""
-    per_step = REFERENCE_BUDGET_S / max(1, steps + warmup)
-    tiles = 256 if per_step >= 2.0 else MIN_SAMPLE_TILES
-    fraction = min(1.0, max(1.0 / 64.0, (per_step - 0.6) / 4.4))
-    return max(1, int(round(num_points * fraction))), tiles
+def workload_config(config, scene):
+    """The ``config`` object of the JSON line: what the workload is, the same
+    for both arms and every N (how a run executes it -- ranks, graphs,
+    exchange -- is reported under ``run``)."""
+    n = scene.num_points
+    k = scene.color.shape[1]
+    return {"workload": WORKLOADS[config]["name"], "gaussians": n,
+            "image": list(scene.crop), "tile_size": scene.settings.tile_size,
+            "l2": "inputs larger than L2 (Gaussian parameters read every view)"
+            if n * project_fwd_bytes(k) > 126e6 else
+            "inputs smaller than L2; each view re-reads them"}
 
 
-def run_reference(args, rank, world):
-    """CPU restatement of the reference, timed on this host's cores (rank 0).
-    Each step is a bounded sample of the view, sized so warm-up plus timed
-    steps stay within about REFERENCE_BUDGET_S."""
-    if rank != 0:
-        return
+class ReferenceView:
+    """One whole view of a config through the CPU restatement of the
+    reference (``oracle/``): projection, binning and compositing of the
+    config's first camera and, for the training configs, the L1 loss gradient
+    against that camera's target (the one rank 0 of the GPU arm uses),
+    compositing backward and projection backward. Nothing is sampled or
+    extrapolated: ``run()`` times the whole view."""
+
+    def __init__(self, O, scene, config):
+        self.O = O
+        self.inputs, self.settings = O.scene_inputs(scene)
+        self.backward = WORKLOADS[config]["backward"]
+        self.crop = scene.crop
+        self.target = None
+        if self.backward:
+            _, target = views_for_rank(scene, config, 0, 1)[0]
+            self.target = target.numpy()
+        self.what = ("projection, binning, compositing, L1 loss gradient, compositing backward, "
+                     "projection backward" if self.backward else
+                     "projection, binning, compositing")
+
+    def run(self):
+        O, s, inputs = self.O, self.settings, self.inputs
+        t0 = time.perf_counter()
+        fwd = O.rasterize(*(inputs[k] for k in REFERENCE_KEYS), s)
+        if self.backward:
+            width, height = self.crop
+            diff = fwd["image"][:height, :width] - self.target
+            grad_image = np.zeros_like(fwd["image"])
+            grad_image[:height, :width] = np.sign(diff) / np.float32(diff.size)
+            O.backward(inputs, fwd, grad_image, s)
+        return time.perf_counter() - t0
+
+
+REFERENCE_KEYS = ("mean", "rotation", "scale", "opacity", "color", "camera_rotation",
+                  "camera_translation")
+
+
+def load_oracle(threads):
+    """The CPU restatement, its parallel loops set to ``threads`` host threads
+    (explicitly: torchrun exports OMP_NUM_THREADS=1). Returns (module, threads
+    in effect)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
 
+    return O, O.set_threads(threads)
+
+
+def run_reference(args, rank, world):
+    """The reference's algorithm on this host's cores (rank 0 only; other
+    ranks exit at once): W warm-up views, then K whole views timed back to
+    back. value = K / seconds."""
+    if rank != 0:
+        return
+    O, threads = load_oracle(host_cores())
     scene = load_scene(args.config, args.points)
-    backward = WORKLOADS[args.config]["backward"]
-    cores = os.cpu_count() or 1
-    os.environ.setdefault("OMP_NUM_THREADS", str(cores))
-    chunk, tiles = sample_size(args.steps, args.warmup, scene.num_points)
-    view = cpu_view_setup(O, scene, backward)
-    step_s = []
-    sample = None
-    for i in range(args.warmup + args.steps):
-        seconds, sample = cpu_view_seconds(O, view, chunk=chunk, tiles=tiles, seed=i)
-        if i >= args.warmup:
-            step_s.append(seconds)
-    per_view = statistics.median(step_s)
-    value = 1.0 / per_view
+    view = ReferenceView(O, scene, args.config)
+    for _ in range(args.warmup):
+        view.run()
+    seconds = sum(view.run() for _ in range(args.steps))
+    value = args.steps / seconds
+    sample = (f"{args.steps} whole views of the config's first camera ({view.what}), "
+              f"timed back to back after {args.warmup} warm-up views; nothing sampled or scaled")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_view * 1e3,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": seconds * 1e3 / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic", "config": {"workload": WORKLOADS[args.config]["name"]},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+        "data": f"synthetic (seeded config-{args.config} scene"
+                + (", random L1 target)" if view.backward else ")"),
+        "config": workload_config(args.config, scene),
+        "run": {"host": "CPU restatement of the reference's kernels (oracle/gs_oracle.c, "
+                        "OpenMP)", "threads": threads, "ranks_working": 1},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
                          "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
-
-
-def cpu_view_setup(O, scene, backward=True):
-    """The whole view's projection and binning (of the scene's first camera),
-    which the sampled compositing steps read, and the per-view fixed cost of
-    the compositing calls (image buffers; in the backward the [intersections,
-    9] row buffer and its reduction per Gaussian), timed once with an empty
-    tile list."""
-    inputs, s = O.scene_inputs(scene)
-    keys = ("mean", "rotation", "scale", "opacity", "color", "camera_rotation",
-            "camera_translation")
-    proj = O.project(*(inputs[k] for k in keys), s)
-    binned = O.bin(proj["bounds"], proj["projected_mean"][:, 2], proj["counts"], s)
-    width, height = scene.crop
-    grad_image = np.full((s.height, s.width, 3), 1.0 / (width * height * 3), np.float32)
-    view = {"scene": scene, "inputs": inputs, "settings": s, "keys": keys, "proj": proj,
-            "binned": binned, "grad_image": grad_image, "backward": backward}
-    none = np.zeros((0,), np.int32)
-    fixed = [composite_seconds(O, view, none) for _ in range(6)][1:]  # first call warms up
-    view["fixed_fwd"] = statistics.median(f[0] for f in fixed)
-    view["fixed_bwd"] = statistics.median(f[1] for f in fixed)
-    return view
-
-
-def composite_seconds(O, view, tiles):
-    """Seconds of the oracle's compositing forward and backward over `tiles`."""
-    s, proj, binned = view["settings"], view["proj"], view["binned"]
-    t0 = time.perf_counter()
-    comp = O.composite(proj["projected_mean"], proj["inverse_covariance"],
-                       proj["projected_color"], proj["projected_opacity"],
-                       binned["gaussian_ids"], binned["ranges"], s, tiles=tiles)
-    t1 = time.perf_counter()
-    if view["backward"]:
-        O.composite_bwd(dict(proj, **binned, **comp), view["grad_image"], s, tiles=tiles)
-    t2 = time.perf_counter()
-    return t1 - t0, t2 - t1
-
-
-def cpu_view_seconds(O, view, chunk, tiles, seed):
-    """Seconds for one config-2 view on the CPU oracle, from a bounded sample:
-    projection, binning and projection backward of a contiguous random chunk
-    of `chunk` Gaussians scaled to all of them, plus compositing forward and
-    backward of `tiles` random tiles -- the per-view fixed cost once, the
-    per-tile remainder scaled to all tiles by list entries."""
-    s, inputs, keys = view["settings"], view["inputs"], view["keys"]
-    n = view["scene"].num_points
-    rng = np.random.default_rng(seed)
-    first = int(rng.integers(0, n - chunk + 1))
-    part = slice(first, first + chunk)
-    chunk_inputs = [inputs[k][part] if k not in ("camera_rotation", "camera_translation")
-                    else inputs[k] for k in keys]
-    chosen = rng.choice(s.num_tiles, size=min(tiles, s.num_tiles), replace=False).astype(np.int32)
-    # Longest lists first, so the host threads' dynamic schedule balances a
-    # small sample as well as it balances the whole view.
-    ranges = view["binned"]["ranges"]
-    chosen = chosen[np.argsort(-(ranges[chosen, 1] - ranges[chosen, 0]), kind="stable")]
-    t0 = time.perf_counter()
-    chunk_proj = O.project(*chunk_inputs, s)
-    t1 = time.perf_counter()
-    O.bin(chunk_proj["bounds"], chunk_proj["projected_mean"][:, 2], chunk_proj["counts"], s)
-    t2 = time.perf_counter()
-    fwd_s, bwd_s = composite_seconds(O, view, chosen)
-    grad_projected = np.zeros((chunk, 9), np.float32)
-    t3 = time.perf_counter()
-    if view["backward"]:
-        O.project_bwd(*chunk_inputs, chunk_proj["inverse_covariance"], grad_projected,
-                      chunk_proj["counts"], s)
-    t4 = time.perf_counter()
-    gaussian_scale = n / chunk
-    # Ratio estimate: compositing time follows the list entries walked, so the
-    # sampled tiles' time is scaled by all entries over the sampled entries.
-    lengths = ranges[:, 1] - ranges[:, 0]
-    tile_scale = float(lengths.sum()) / max(1.0, float(lengths[chosen].sum()))
-    fixed = view["fixed_fwd"] + view["fixed_bwd"]
-    per_tile = max(0.0, fwd_s + bwd_s - fixed)
-    seconds = ((t1 - t0) + (t2 - t1) + (t4 - t3)) * gaussian_scale + fixed + per_tile * tile_scale
-    what = "projection, binning, projection backward" if view["backward"] else \
-        "projection, binning"
-    sample = (f"one view: {what} of {chunk} of "
-              f"{n} Gaussians scaled by {gaussian_scale:.2f}; composite "
-              f"{'fwd+bwd' if view['backward'] else 'fwd'} on "
-              f"{len(chosen)} of {s.num_tiles} random tiles, per-tile time scaled by "
-              f"{tile_scale:.1f} (all list entries / sampled entries), per-view fixed "
-              f"time ({fixed:.2f} s) counted once")
-    return seconds, sample
 
 
 # Algorithmic bytes per Gaussian of one fused optimizer step with K SH
@@ -609,6 +617,8 @@ def relocation_timings(params, device, repeats=3):
     return result
 
 
+CPU_BASELINE_VIEWS = 3  # whole views timed for the GPU arm's cpu_baseline
+
 BATCH_VIEWS = 16  # cameras per rasterize_batch call in forward-only multi-camera configs
 
 
@@ -635,17 +645,14 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        # host CPU work on rank 0 only: no process group, no collective
+        run_reference(args, rank, world)
+        return
     if world > 1:
         import datetime
 
-        torch.distributed.init_process_group(
-            "nccl" if args.impl == "b200" else "gloo",
-            timeout=datetime.timedelta(seconds=120))
-    if args.impl == "reference":
-        run_reference(args, rank, world)
-        if world > 1:
-            torch.distributed.destroy_process_group()
-        return
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
     from gaussian_splats_b200.graphs import CapturedStep
@@ -729,11 +736,16 @@ def main():
         if world > 1:
             torch.distributed.barrier()
         ms = start.elapsed_time(end) / steps
+        rank_ms[fn] = [ms]
         if world > 1:
-            t = torch.tensor([ms], device=device)
-            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-            ms = float(t)
+            every = torch.zeros(world, device=device)
+            every[rank] = ms
+            torch.distributed.all_reduce(every)  # each rank's own time, for the record
+            rank_ms[fn] = every.tolist()
+            ms = max(rank_ms[fn])
         return ms
+
+    rank_ms = {}
 
     # Forward only.
     for _ in range(args.warmup):
@@ -770,6 +782,24 @@ def main():
         stage_ms = stages.durations()
     clock = clocks.summary()
     value = views_per_step * 1000.0 / ms
+    headline_rank_ms = rank_ms[captured if graphed else step]
+    parity = None
+    rank_view_ms = None
+    if world > 1 and backward:
+        # Each rank's own view, forward + backward without any exchange
+        # (launched from Python): how much of the multi-GPU step is camera
+        # imbalance rather than exchange cost.
+        def local_view():
+            for p in trainable:
+                p.grad = None
+            for camera, target in zip(cameras, targets):
+                loss_fn(render(splats, camera), target).backward()
+
+        for _ in range(2):
+            local_view()
+        timed(local_view, 5)
+        rank_view_ms = rank_ms[local_view]
+        parity = gradient_parity(captured if graphed else step, local_view, trainable, device)
 
     # Structure of this rank's first view (for the roofline's work counts).
     camera0 = cameras[0]
@@ -880,21 +910,53 @@ def main():
                 "algorithmic_bytes": bytes_per_launch,
                 "note": f"peak: {peak_kind} hbm_gbs (MEASURED_PEAKS.json)"}
 
-    def fp32(name, flops):
+    pipes = {}
+    pipes_json = os.path.join(ROOT, "profiles", "pipes.json")
+    if args.config == 2 and args.points is None and os.path.exists(pipes_json):
+        with open(pipes_json) as f:
+            pipes = json.load(f)
+    clock_mhz = (clock or {}).get("sm_mhz") or 1965.0
+
+    def issue(name, flops):
+        """The compositors are bound by instruction issue (no tensor work, DRAM
+        a few % busy): achieved = warp instructions per launch (counted by ncu
+        on this workload) / live launch time, against one instruction per
+        scheduler per cycle at the clock measured during the timed region.
+        The reference-work FP32 rate is kept beside it, labelled by its basis."""
         tflops = flops / (kernel_ms[name] * 1e-3) / 1e12
-        return {"bound": "fp32", "achieved": tflops, "peak": fp32_peak, "unit": "TFLOP/s",
-                "frac": tflops / fp32_peak, "traffic": traffic.get(name), "ms": kernel_ms[name],
-                "algorithmic_flops": flops,
-                "note": "peak: FP32 cuBLAS SGEMM measured in this run (no FP32 figure in "
-                        "MEASURED_PEAKS.json); work = reference-evaluated pairs x ops/pair"}
+        work = {"basis": "reference-evaluated (pixel, Gaussian) pairs x FP32 ops per pair of the "
+                         "reference's arithmetic: a rate of reference work, not pipe "
+                         "utilisation (the kernel culls pairs the reference evaluates)",
+                "achieved": tflops, "unit": "TFLOP/s", "fp32_sgemm_peak": fp32_peak,
+                "vs_sgemm": tflops / fp32_peak, "algorithmic_flops": flops}
+        entry = {"bound": "issue", "achieved": None, "peak": None, "unit": "Ginst/s",
+                 "frac": None, "traffic": traffic.get(name), "ms": kernel_ms[name],
+                 "reference_work": work}
+        counters = pipes.get(name)
+        if counters:
+            inst = counters["inst_executed"]
+            achieved = inst / (kernel_ms[name] * 1e-3) / 1e9
+            peak = SCHEDULERS_PER_SM * SM_COUNT * clock_mhz * 1e6 / 1e9
+            entry.update(
+                achieved=achieved, peak=peak, frac=achieved / peak,
+                inst_executed=inst, fma_pipe_pct=counters["fma_pipe_pct"],
+                alu_pipe_pct=counters["alu_pipe_pct"],
+                threads_per_warp_inst=counters["threads_per_warp_inst"],
+                warp_inst_per_active_pair=inst / max(1, n_contrib),
+                thread_inst_per_active_pair=inst * counters["threads_per_warp_inst"]
+                / max(1, n_contrib),
+                note="warp instructions from ncu (profiles/pipes.json, same workload); time "
+                     "live (CUDA events, L2 flushed); peak = 4 schedulers x 148 SMs x the "
+                     "median SM clock of the timed region")
+        return entry
 
     rooflines = {
         "project_fwd": hbm("project_fwd", n * project_fwd_bytes(k)),
-        "composite_fwd": fp32("composite_fwd", pairs * COMPOSITE_FWD_FLOPS),
+        "composite_fwd": issue("composite_fwd", pairs * COMPOSITE_FWD_FLOPS),
     }
     if backward:
         rooflines["project_bwd"] = hbm("project_bwd", n * project_bwd_bytes(k))
-        rooflines["composite_bwd"] = fp32("composite_bwd", pairs * COMPOSITE_BWD_FLOPS)
+        rooflines["composite_bwd"] = issue("composite_bwd", pairs * COMPOSITE_BWD_FLOPS)
     dominant = max(kernel_ms, key=kernel_ms.get)
     main_roof = dict(rooflines[dominant], kernel=dominant)
     optimizer = None
@@ -926,23 +988,19 @@ def main():
         "vs_baseline": None, "dtype": "f32",
         "data": f"synthetic (seeded config-{args.config} scene"
                 + (", random L1 target)" if backward else ")"),
-        "config": {"workload": workload["name"], "gaussians": n,
-                   "image": [crop_w, crop_h], "tile_size": settings.tile_size,
-                   "views_per_step": views_per_step, "views_per_rank_per_step": per_view,
-                   "parallelism": (f"view-parallel x{world}" + (
-                       (", projection backward summed over all ranks' views, reading their "
-                        "screen-space gradients from peer memory (symmetric memory, NVLink)"
-                        if peers else
-                        ", NCCL all-gather of screen-space gradients + projection backward "
-                        "summed over all ranks' views" if screen else
-                        ", NCCL all-reduce of gradients") if backward else ", no collective"))
-                   if world > 1 else "single GPU",
-                   "step": "CUDA-graph replay of the captured training step (same kernels; "
-                           "eager_ms_per_step is the step launched from Python)" if graphed
-                   else "launched from Python",
-                   "l2": "inputs larger than L2 (Gaussian parameters read every view)"
-                   if n * project_fwd_bytes(k) > 126e6 else
-                   "inputs smaller than L2; each view re-reads them"},
+        "config": workload_config(args.config, scene),
+        "run": {"views_per_step": views_per_step, "views_per_rank_per_step": per_view,
+                "parallelism": (f"view-parallel x{world}" + (
+                    (", projection backward summed over all ranks' views, reading their "
+                     "screen-space gradients from peer memory (symmetric memory, NVLink)"
+                     if peers else
+                     ", NCCL all-gather of screen-space gradients + projection backward "
+                     "summed over all ranks' views" if screen else
+                     ", NCCL all-reduce of gradients") if backward else ", no collective"))
+                if world > 1 else "single GPU",
+                "step": "CUDA-graph replay of the captured training step (same kernels; "
+                        "eager_ms_per_step is the step launched from Python)" if graphed
+                else "launched from Python"},
         "stage_ms": stage_ms, "kernel_ms": kernel_ms, "dominant_kernel": dominant,
         "view": {"visible": visible, "intersections": intersections, "tiles": num_tiles,
                  "active_pairs": n_contrib, "reference_pairs": pairs},
@@ -954,19 +1012,29 @@ def main():
                          (launches_per_view(num_tiles, False) - 1) * per_view
                          + -(-per_view // BATCH_VIEWS)) * args.steps,
         "clocks": clock,
+        "rank_ms_per_step": headline_rank_ms,
+        "rank_view_ms": rank_view_ms,
+        "parity": parity,
     }
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
-        sys.path.insert(0, os.path.join(ROOT, "oracle"))
-        import oracle as O
-
-        view = cpu_view_setup(O, load_scene(args.config, args.points), backward)
-        seconds, sample = cpu_view_seconds(O, view, chunk=scene.num_points, tiles=256, seed=0)
-        line["cpu_baseline"] = {"value": 1.0 / seconds, "unit": UNIT,
-                                "cores": os.cpu_count(), "kind": "port", "sample": sample}
+        O, threads = load_oracle(host_cores())
+        cpu_view = ReferenceView(O, load_scene(args.config, args.points), args.config)
+        cpu_view.run()  # warm-up
+        cpu_s = [cpu_view.run() for _ in range(CPU_BASELINE_VIEWS)]
+        line["cpu_baseline"] = {
+            "value": CPU_BASELINE_VIEWS / sum(cpu_s), "unit": UNIT, "cores": threads,
+            "kind": "port",
+            "sample": f"{CPU_BASELINE_VIEWS} whole views of the config's first camera "
+                      f"({cpu_view.what}) after one warm-up view, CPU restatement of the "
+                      f"reference's kernels on {threads} host threads"}
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
+        view_parallel.release_arenas()
         torch.distributed.destroy_process_group()
+    if parity is not None and not parity["ok"]:
+        sys.exit(f"multi-GPU gradients outside rtol {PARITY_RTOL} / atol {PARITY_ATOL} of the "
+                 f"plain all-reduce: {parity}")
 
 
 if __name__ == "__main__":

@@ -43,6 +43,29 @@
 
 #include "detmath.h"
 
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+/* Host threads of the parallel loops below. Set explicitly by the benchmark:
+ * launchers such as torchrun export OMP_NUM_THREADS=1, which would otherwise
+ * leave a timed run on one core while reporting all of them. */
+void gso_set_threads(int32_t threads) {
+#ifdef _OPENMP
+    if (threads > 0) omp_set_num_threads(threads);
+#else
+    (void)threads;
+#endif
+}
+
+int32_t gso_max_threads(void) {
+#ifdef _OPENMP
+    return omp_get_max_threads();
+#else
+    return 1;
+#endif
+}
+
 typedef struct gso_params {
     float fx, fy, cx, cy;
     int32_t width, height, tile_size;

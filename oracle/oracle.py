@@ -61,6 +61,8 @@ def lib() -> ctypes.CDLL:
         i64, i32 = ctypes.c_int64, ctypes.c_int32
         _lib.gso_project.argtypes = [i64, _f32p, _f32p, _f32p, _f32p, _f32p, i32, _f32p, _f32p, P,
                                      _f32p, _f32p, _f32p, _f32p, _i32p, _i32p]
+        _lib.gso_set_threads.argtypes = [i32]
+        _lib.gso_max_threads.restype = i32
         _lib.gso_total.argtypes = [i64, _i32p]
         _lib.gso_total.restype = i64
         _lib.gso_bin.argtypes = [i64, _i32p, _f32p, _i32p, i32, i32, ctypes.c_void_p,
@@ -132,6 +134,13 @@ class Settings:
             cutoff=-2.0 * math.log1p(-self.confidence),
             opacity_threshold=self.opacity_threshold,
         )
+
+
+def set_threads(threads: int) -> int:
+    """Run the parallel loops on ``threads`` host threads (whatever
+    OMP_NUM_THREADS says); returns the thread count now in effect."""
+    lib().gso_set_threads(int(threads))
+    return int(lib().gso_max_threads())
 
 
 def _c(a, dtype=np.float32):

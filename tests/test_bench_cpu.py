@@ -1,5 +1,6 @@
 """bench.py's reference arm (the CPU oracle on the host cores): one JSON line
-with the contract's keys, a bounded per-step sample, and the sample sizing."""
+with the contract's keys, whole views timed on an explicit thread count, and
+the workload description both arms share."""
 
 import json
 import os
@@ -12,20 +13,23 @@ sys.path.insert(0, ROOT)
 import bench  # noqa: E402
 
 
-def test_sample_size_shrinks_with_steps():
-    full = bench.sample_size(steps=3, warmup=1, num_points=1_000_000)
-    small = bench.sample_size(steps=100, warmup=5, num_points=1_000_000)
-    tiny = bench.sample_size(steps=10_000, warmup=5, num_points=1_000_000)
-    assert full == (1_000_000, 256)
-    assert small[0] < full[0] and small[1] == bench.MIN_SAMPLE_TILES
-    assert tiny[0] == round(1_000_000 / 64)
+def test_both_arms_describe_the_workload_alike():
+    from gaussian_splats_b200 import scenes
+
+    scene = scenes.config2(num_points=64)
+    config = bench.workload_config(2, scene)
+    assert config["workload"].startswith("config2") and config["gaussians"] == 64
+    assert config["image"] == [1920, 1080] and config["tile_size"] == 16
+    # nothing about ranks or launch mode: that goes under "run"
+    assert not {"parallelism", "step", "views_per_step"} & set(config)
 
 
 def test_reference_arm_prints_one_contract_line():
     out = subprocess.run(
         [sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--steps", "2",
          "--warmup", "1", "--points", "20000"],
-        capture_output=True, text=True, timeout=600, cwd=ROOT, check=True).stdout
+        capture_output=True, text=True, timeout=600, cwd=ROOT, check=True,
+        env=dict(os.environ, OMP_NUM_THREADS="1")).stdout
     lines = [line for line in out.splitlines() if line.startswith("{")]
     assert len(lines) == 1
     d = json.loads(lines[0])
@@ -34,6 +38,13 @@ def test_reference_arm_prints_one_contract_line():
     assert d["cpu_baseline"]["kind"] == "port" and d["cpu_baseline"]["value"] == d["value"]
     assert d["e2e"] == {"value": d["value"], "unit": "views/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}
+    # the whole timed region is K whole views, on every host core despite OMP_NUM_THREADS=1
+    assert abs(d["ms_per_step"] * d["steps"] / 1e3 - d["steps"] / d["value"]) < 1e-6
+    assert d["cpu_baseline"]["cores"] == bench.host_cores()
+    assert "whole views" in d["cpu_baseline"]["sample"]
+    from gaussian_splats_b200 import scenes
+
+    assert d["config"] == bench.workload_config(2, scenes.config2(num_points=20000))
 
 
 def test_launch_count_per_view():
