@@ -101,9 +101,11 @@ def parse_args():
     p.add_argument("--no-graph", action="store_true",
                    help="launch the training step from Python instead of replaying it from "
                         "a CUDA graph")
-    p.add_argument("--exchange", choices=("auto", "screen", "screen-nccl", "all-reduce"),
+    p.add_argument("--exchange", choices=("auto", "shard", "screen", "screen-nccl", "all-reduce"),
                    default="auto",
-                   help="how ranks sum gradients with one view per rank (auto: "
+                   help="how ranks sum gradients with one view per rank: the sharded peer "
+                        "exchange, the whole-gradient peer exchange, its NCCL all-gather form, "
+                        "or the parameter-gradient all-reduce (auto: the sharded exchange where "
                         "view_parallel.screen_exchange_pays)")
     return p.parse_args()
 
@@ -628,16 +630,18 @@ def sort_passes(num_tiles):
     return (bits + 7) // 8
 
 
-def launches_per_view(num_tiles, backward, peers=False):
+def launches_per_view(num_tiles, backward, peers=False, sharded=False):
     """This library's kernel launches for one view: projection; the count
     phase (histogram, 4 depth passes, count scan); the sort phase (emit,
     histogram when the tile sort has passes, the passes, ranges);
     compositing; in a training step the L1 loss (partial sums, total,
-    gradient), compositing backward and projection backward; and with the
-    peer exchange its three handshake kernels."""
+    gradient), compositing backward and projection backward; and with a peer
+    exchange its handshake kernels (begin, publish, finish; the sharded form
+    also its shard release)."""
     passes = sort_passes(num_tiles)
     forward = 1 + 6 + (2 + (1 + passes if passes else 0)) + 1
-    return forward + (5 if backward else 0) + (3 if peers else 0)
+    handshakes = 4 if sharded else (3 if peers else 0)
+    return forward + (5 if backward else 0) + handshakes
 
 
 def main():
@@ -710,12 +714,12 @@ def main():
     # summing the projection backward over all views (view_parallel), where
     # that beats all-reducing the parameter gradients; several views per rank:
     # the parameter gradients are all-reduced once per step.
+    transport = {"screen": "p2p", "screen-nccl": "nccl"}.get(args.exchange, "p2p-shard")
     screen = world > 1 and len(cameras) == 1 and (
-        args.exchange in ("screen", "screen-nccl") or
-        (args.exchange == "auto" and screen_exchange_pays(world)))
-    # screen-space gradients read from peer memory (default) or all-gathered by NCCL
-    view_parallel.EXCHANGE_TRANSPORT = "nccl" if args.exchange == "screen-nccl" else "p2p"
-    peers = screen and view_parallel.EXCHANGE_TRANSPORT == "p2p"
+        args.exchange in ("shard", "screen", "screen-nccl") or
+        (args.exchange == "auto" and screen_exchange_pays(world, transport)))
+    view_parallel.EXCHANGE_TRANSPORT = transport
+    peers = screen and transport in view_parallel.PEER_TRANSPORTS
 
     def train_step():
         return vp_train_step(splats, cameras, targets, trainable,
@@ -991,7 +995,11 @@ def main():
         "config": workload_config(args.config, scene),
         "run": {"views_per_step": views_per_step, "views_per_rank_per_step": per_view,
                 "parallelism": (f"view-parallel x{world}" + (
-                    (", projection backward summed over all ranks' views, reading their "
+                    (", sharded peer exchange: each rank copies its shard's screen-space "
+                     "gradient rows from every rank (symmetric memory, NVLink), sums the "
+                     "projection backward of its shard over all ranks' views, and copies the "
+                     "other shards' parameter gradients" if transport == "p2p-shard" and peers
+                     else ", projection backward summed over all ranks' views, reading their "
                      "screen-space gradients from peer memory (symmetric memory, NVLink)"
                      if peers else
                      ", NCCL all-gather of screen-space gradients + projection backward "
@@ -1007,7 +1015,8 @@ def main():
         "roofline": main_roof, "rooflines": rooflines, "optimizer": optimizer,
         "e2e": {"value": views_per_step * 1000.0 / e2e_ms, "unit": UNIT, "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-        "gpu_launches": (launches_per_view(num_tiles, backward, peers) * per_view
+        "gpu_launches": (launches_per_view(num_tiles, backward, peers,
+                                           peers and transport == "p2p-shard") * per_view
                          if not batched else
                          (launches_per_view(num_tiles, False) - 1) * per_view
                          + -(-per_view // BATCH_VIEWS)) * args.steps,

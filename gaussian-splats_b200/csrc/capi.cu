@@ -52,6 +52,14 @@ int32_t launch_exchange_publish(const gs_peer_group&, int64_t, cudaStream_t);
 int32_t launch_exchange_finish(const gs_peer_group&, cudaStream_t);
 int32_t exchange_gather(const gs_peer_group&, int64_t, float*, int32_t*, cudaStream_t);
 int32_t exchange_status(const gs_peer_group&, cudaStream_t);
+int32_t exchange_shard_layout(int64_t, int32_t, int32_t, gs_shard_layout*);
+int32_t exchange_gather_rows(const gs_peer_group&, int64_t, float*, int32_t*, cudaStream_t);
+int32_t launch_project_bwd_shard(int64_t, int32_t, const gs_peer_group&, const float*,
+                                 const int32_t*, const float*, const float*, const float*,
+                                 const float*, const float*, cudaStream_t);
+int32_t launch_exchange_publish_shard(const gs_peer_group&, cudaStream_t);
+int32_t exchange_gather_shards(const gs_peer_group&, int64_t, int32_t, float*, float*, float*,
+                               float*, float*, cudaStream_t);
 int32_t launch_l1_fwd(const float*, int64_t, int64_t, int64_t, const float*, int64_t, int64_t,
                       float*, float*, cudaStream_t);
 int32_t launch_l1_bwd(const float*, int64_t, int64_t, int64_t, const float*, int64_t, int64_t,
@@ -338,6 +346,44 @@ int32_t gs_project_bwd_peers(int64_t n, int32_t num_sh, const gs_peer_group* gro
   return gs::launch_project_bwd_peers(n, num_sh, group->world, mean, rotation, scale, opacity,
                                       color, records, grads, counts, grad_mean, grad_rotation,
                                       grad_scale, grad_opacity, grad_color, as_cuda(stream));
+}
+
+int32_t gs_exchange_shard_layout(int64_t n, int32_t world, int32_t num_sh,
+                                 gs_shard_layout* out) {
+  if (!gs::valid_sh(num_sh)) return num_sh > 25 ? GS_ERR_UNSUPPORTED : GS_ERR_INVALID_ARGUMENT;
+  return gs::exchange_shard_layout(n, world, num_sh, out);
+}
+
+int32_t gs_exchange_gather_rows(const gs_peer_group* group, int64_t n, float* grad_rows,
+                                int32_t* count_rows, gs_stream_t stream) {
+  if (!group || n < 0 || n >= gs::kMaxGaussians) return GS_ERR_INVALID_ARGUMENT;
+  return gs::exchange_gather_rows(*group, n, grad_rows, count_rows, as_cuda(stream));
+}
+
+int32_t gs_project_bwd_shard(int64_t n, int32_t num_sh, const gs_peer_group* group,
+                             const float* grad_rows, const int32_t* count_rows, const float* mean,
+                             const float* rotation, const float* scale, const float* opacity,
+                             const float* color, gs_stream_t stream) {
+  if (!group || n < 0 || n >= gs::kMaxGaussians) return GS_ERR_INVALID_ARGUMENT;
+  if (!gs::valid_sh(num_sh)) return num_sh > 25 ? GS_ERR_UNSUPPORTED : GS_ERR_INVALID_ARGUMENT;
+  if (!gs::aligned(rotation, 16) || ((num_sh == 4 || num_sh == 16) && !gs::aligned(color, 16)))
+    return GS_ERR_MISALIGNED;
+  return gs::launch_project_bwd_shard(n, num_sh, *group, grad_rows, count_rows, mean, rotation,
+                                      scale, opacity, color, as_cuda(stream));
+}
+
+int32_t gs_exchange_publish_shard(const gs_peer_group* group, gs_stream_t stream) {
+  if (!group) return GS_ERR_INVALID_ARGUMENT;
+  return gs::launch_exchange_publish_shard(*group, as_cuda(stream));
+}
+
+int32_t gs_exchange_gather_shards(const gs_peer_group* group, int64_t n, int32_t num_sh,
+                                  float* grad_rotation, float* grad_color, float* grad_mean,
+                                  float* grad_scale, float* grad_opacity, gs_stream_t stream) {
+  if (!group || n < 0 || n >= gs::kMaxGaussians) return GS_ERR_INVALID_ARGUMENT;
+  if (!gs::valid_sh(num_sh)) return num_sh > 25 ? GS_ERR_UNSUPPORTED : GS_ERR_INVALID_ARGUMENT;
+  return gs::exchange_gather_shards(*group, n, num_sh, grad_rotation, grad_color, grad_mean,
+                                    grad_scale, grad_opacity, as_cuda(stream));
 }
 
 uint64_t gs_relocate_workspace_size(int64_t n_src) {

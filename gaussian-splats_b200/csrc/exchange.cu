@@ -20,6 +20,16 @@
 // Reading the gradients straight from peer memory inside the projection
 // backward (gs_project_bwd_peers without gathered buffers) also works, but its
 // scattered 36-byte rows over NVLink cost more than the bulk copy.
+// Sharded variant (gs_exchange_gather_rows .. gs_exchange_gather_shards): rank
+// r owns Gaussians [r*rows, (r+1)*rows). After the publish it copies only its
+// shard's rows of every rank's gradient and counts, runs the projection
+// backward over all views for its shard alone into the arena's shard region,
+// releases `shard_ready` to the peers, waits for theirs and copies every
+// rank's finished shard of parameter gradients; then gs_exchange_finish. Per
+// rank that moves rows x 40 B from each peer plus the other shards' gradients
+// (7/8 of 59 floats per Gaussian at 8 ranks, SH degree 3), and the per-view
+// arithmetic of the summed backward is split W ways instead of repeated on
+// every rank.
 // The epochs live in device memory, so the sequence replays from a CUDA graph.
 // Each wait is bounded (about a second): on expiry it records an error bit in
 // the header and returns; gs_exchange_status reports it.
@@ -35,6 +45,21 @@ int32_t launch_exchange_finish(const gs_peer_group& g, cudaStream_t stream);
 int32_t exchange_gather(const gs_peer_group& g, int64_t n, float* grad_projected,
                         int32_t* counts, cudaStream_t stream);
 int32_t exchange_status(const gs_peer_group& g, cudaStream_t stream);
+int32_t exchange_shard_layout(int64_t n, int32_t world, int32_t num_sh, gs_shard_layout* out);
+int32_t exchange_gather_rows(const gs_peer_group& g, int64_t n, float* grad_rows,
+                             int32_t* count_rows, cudaStream_t stream);
+int32_t launch_exchange_publish_shard(const gs_peer_group& g, cudaStream_t stream);
+int32_t exchange_gather_shards(const gs_peer_group& g, int64_t n, int32_t num_sh,
+                               float* grad_rotation, float* grad_color, float* grad_mean,
+                               float* grad_scale, float* grad_opacity, cudaStream_t stream);
+int32_t launch_project_bwd_peers(int64_t, int32_t, int32_t, const float*, const float*,
+                                 const float*, const float*, const float*, const void*,
+                                 const float* const*, const int32_t* const*, float*, float*,
+                                 float*, float*, float*, cudaStream_t);
+int32_t launch_project_bwd_shard(int64_t n, int32_t num_sh, const gs_peer_group& g,
+                                 const float* grad_rows, const int32_t* count_rows,
+                                 const float* mean, const float* rotation, const float* scale,
+                                 const float* opacity, const float* color, cudaStream_t stream);
 
 namespace {
 
@@ -44,11 +69,13 @@ struct ArenaHeader {
   unsigned int pad;
   unsigned long long ready[GS_MAX_PEERS];  // [p]: last epoch rank p published
   unsigned long long done[GS_MAX_PEERS];   // [p]: last epoch rank p finished reading
+  unsigned long long shard_ready[GS_MAX_PEERS];  // [p]: last epoch rank p finished its shard
 };
 static_assert(sizeof(ArenaHeader) <= 256, "header fits its 256 bytes");
 
 constexpr unsigned kErrReadyTimeout = 1u;
 constexpr unsigned kErrDoneTimeout = 2u;
+constexpr unsigned kErrShardTimeout = 4u;
 constexpr long long kWaitCycles = 2000000000LL;  // ~1 s at the B200's clocks
 constexpr int kRecordWords = 29;
 
@@ -113,7 +140,29 @@ __global__ void exchange_finish_kernel(gs_peer_group g) {
   if (p < g.world && p != g.rank) st_release_sys(&header(g.arena[p])->done[g.rank], me->epoch);
 }
 
+// After this rank's shard of parameter gradients is in its arena (earlier
+// work on the stream): release `shard_ready` to every peer and wait for
+// theirs. One warp; lane p deals with peer p.
+__global__ void exchange_publish_shard_kernel(gs_peer_group g) {
+  ArenaHeader* me = header(g.arena[g.rank]);
+  const int p = threadIdx.x;
+  const unsigned long long epoch = me->epoch;  // bumped by this step's publish
+  __threadfence_system();
+  if (p < g.world && p != g.rank) {
+    st_release_sys(&header(g.arena[p])->shard_ready[g.rank], epoch);
+    if (!wait_at_least(&me->shard_ready[p], epoch)) atomicOr(&me->error, kErrShardTimeout);
+  }
+}
+
 uint64_t align256(uint64_t x) { return (x + 255) & ~uint64_t{255}; }
+
+// Gaussians of rank p's shard: [first, first + count).
+void shard_span(int64_t n, int64_t rows, int p, int64_t* first, int64_t* count) {
+  const int64_t lo = rows * p < n ? rows * p : n;
+  const int64_t hi = rows * (p + 1) < n ? rows * (p + 1) : n;
+  *first = lo;
+  *count = hi - lo;
+}
 
 bool valid_group(const gs_peer_group& g) {
   if (g.world < 1 || g.world > GS_MAX_PEERS || g.rank < 0 || g.rank >= g.world) return false;
@@ -176,6 +225,121 @@ int32_t exchange_gather(const gs_peer_group& g, int64_t n, float* grad_projected
                                 36 * static_cast<size_t>(n), cudaMemcpyDeviceToDevice, stream));
     GS_CUDA_TRY(cudaMemcpyAsync(counts + n * p, base + layout.counts,
                                 4 * static_cast<size_t>(n), cudaMemcpyDeviceToDevice, stream));
+  }
+  return GS_OK;
+}
+
+int32_t exchange_shard_layout(int64_t n, int32_t world, int32_t num_sh, gs_shard_layout* out) {
+  if (!out || num_sh < 1 || num_sh > 25) return GS_ERR_INVALID_ARGUMENT;
+  gs_exchange_layout base;
+  GS_TRY(exchange_layout(n, world, &base));
+  const uint64_t rows = static_cast<uint64_t>((n + world - 1) / world);
+  uint64_t at = align256(base.bytes);
+  out->rotation = at;
+  at = align256(at + 16 * rows);
+  out->color = at;
+  at = align256(at + 12 * static_cast<uint64_t>(num_sh) * rows);
+  out->mean = at;
+  at = align256(at + 12 * rows);
+  out->scale = at;
+  at = align256(at + 12 * rows);
+  out->opacity = at;
+  at = align256(at + 4 * rows);
+  out->bytes = at;
+  out->rows = static_cast<int64_t>(rows);
+  return GS_OK;
+}
+
+// Copies this rank's shard rows of every rank's screen-space gradient and
+// counts (this rank's own too) into [world, rows, 9] / [world, rows] local
+// buffers: one contiguous block of each array per rank.
+int32_t exchange_gather_rows(const gs_peer_group& g, int64_t n, float* grad_rows,
+                             int32_t* count_rows, cudaStream_t stream) {
+  if (!valid_group(g) || !grad_rows || !count_rows) return GS_ERR_INVALID_ARGUMENT;
+  gs_exchange_layout layout;
+  GS_TRY(exchange_layout(n, g.world, &layout));
+  const int64_t rows = (n + g.world - 1) / g.world;
+  int64_t first, count;
+  shard_span(n, rows, g.rank, &first, &count);
+  if (count <= 0) return GS_OK;
+  for (int p = 0; p < g.world; ++p) {
+    const char* base = static_cast<const char*>(g.arena[p]);
+    GS_CUDA_TRY(cudaMemcpyAsync(grad_rows + 9 * rows * p,
+                                base + layout.grad_projected + 36 * static_cast<size_t>(first),
+                                36 * static_cast<size_t>(count), cudaMemcpyDeviceToDevice,
+                                stream));
+    GS_CUDA_TRY(cudaMemcpyAsync(count_rows + rows * p,
+                                base + layout.counts + 4 * static_cast<size_t>(first),
+                                4 * static_cast<size_t>(count), cudaMemcpyDeviceToDevice,
+                                stream));
+  }
+  return GS_OK;
+}
+
+// The summed projection backward of this rank's shard, over every rank's
+// view, into the shard region of this rank's arena.
+int32_t launch_project_bwd_shard(int64_t n, int32_t num_sh, const gs_peer_group& g,
+                                 const float* grad_rows, const int32_t* count_rows,
+                                 const float* mean, const float* rotation, const float* scale,
+                                 const float* opacity, const float* color, cudaStream_t stream) {
+  if (!valid_group(g) || !grad_rows || !count_rows) return GS_ERR_INVALID_ARGUMENT;
+  gs_exchange_layout layout;
+  gs_shard_layout shard;
+  GS_TRY(exchange_layout(n, g.world, &layout));
+  GS_TRY(exchange_shard_layout(n, g.world, num_sh, &shard));
+  int64_t first, count;
+  shard_span(n, shard.rows, g.rank, &first, &count);
+  if (count <= 0) return GS_OK;
+  const float* grads[GS_MAX_PEERS] = {};
+  const int32_t* counts[GS_MAX_PEERS] = {};
+  for (int v = 0; v < g.world; ++v) {
+    grads[v] = grad_rows + 9 * shard.rows * v;
+    counts[v] = count_rows + shard.rows * v;
+  }
+  char* me = static_cast<char*>(g.arena[g.rank]);
+  const int64_t k3 = 3 * static_cast<int64_t>(num_sh);
+  return launch_project_bwd_peers(
+      count, num_sh, g.world, mean + 3 * first, rotation + 4 * first, scale + 3 * first,
+      opacity + first, color + k3 * first, me + layout.gathered, grads, counts,
+      reinterpret_cast<float*>(me + shard.mean), reinterpret_cast<float*>(me + shard.rotation),
+      reinterpret_cast<float*>(me + shard.scale), reinterpret_cast<float*>(me + shard.opacity),
+      reinterpret_cast<float*>(me + shard.color), stream);
+}
+
+int32_t launch_exchange_publish_shard(const gs_peer_group& g, cudaStream_t stream) {
+  if (!valid_group(g)) return GS_ERR_INVALID_ARGUMENT;
+  exchange_publish_shard_kernel<<<1, 32, 0, stream>>>(g);
+  return check_launch();
+}
+
+// Copies every rank's finished shard of parameter gradients (this rank's from
+// its own arena) into the full gradient arrays.
+int32_t exchange_gather_shards(const gs_peer_group& g, int64_t n, int32_t num_sh,
+                               float* grad_rotation, float* grad_color, float* grad_mean,
+                               float* grad_scale, float* grad_opacity, cudaStream_t stream) {
+  if (!valid_group(g) || !grad_rotation || !grad_color || !grad_mean || !grad_scale ||
+      !grad_opacity)
+    return GS_ERR_INVALID_ARGUMENT;
+  gs_shard_layout shard;
+  GS_TRY(exchange_shard_layout(n, g.world, num_sh, &shard));
+  const size_t k3 = 3 * static_cast<size_t>(num_sh);
+  for (int step = 1; step <= g.world; ++step) {
+    const int p = (g.rank + step) % g.world;  // peers first (staggered), this rank last
+    int64_t first, count;
+    shard_span(n, shard.rows, p, &first, &count);
+    if (count <= 0) continue;
+    const char* base = static_cast<const char*>(g.arena[p]);
+    const size_t f = static_cast<size_t>(first), c = static_cast<size_t>(count);
+    struct {
+      float* dst;
+      uint64_t offset;
+      size_t width;
+    } parts[5] = {{grad_rotation, shard.rotation, 4}, {grad_color, shard.color, k3},
+                  {grad_mean, shard.mean, 3}, {grad_scale, shard.scale, 3},
+                  {grad_opacity, shard.opacity, 1}};
+    for (const auto& part : parts)
+      GS_CUDA_TRY(cudaMemcpyAsync(part.dst + part.width * f, base + part.offset,
+                                  4 * part.width * c, cudaMemcpyDeviceToDevice, stream));
   }
   return GS_OK;
 }

@@ -49,6 +49,11 @@ EXPORTED_SYMBOLS = (
     "gs_project_bwd_peers",
     "gs_exchange_finish",
     "gs_exchange_status",
+    "gs_exchange_shard_layout",
+    "gs_exchange_gather_rows",
+    "gs_project_bwd_shard",
+    "gs_exchange_publish_shard",
+    "gs_exchange_gather_shards",
     "gs_l1_loss_scratch_floats",
     "gs_l1_loss",
     "gs_l1_loss_backward",
@@ -123,6 +128,15 @@ class ExchangeLayout(ctypes.Structure):
 
     _fields_ = [(name, ctypes.c_uint64) for name in
                 ("grad_projected", "counts", "record", "gathered", "bytes")]
+
+
+class ShardLayout(ctypes.Structure):
+    """``gs_shard_layout``: the shard of parameter gradients inside a sharded
+    exchange arena (byte offsets), the arena size, and Gaussians per shard."""
+
+    _fields_ = [(name, ctypes.c_uint64) for name in
+                ("rotation", "color", "mean", "scale", "opacity", "bytes")] + [
+        ("rows", ctypes.c_int64)]
 
 
 class AdamParams(ctypes.Structure):
@@ -218,6 +232,12 @@ def lib() -> ctypes.CDLL:
         "gs_project_bwd_peers": ([i64, i32, ctypes.POINTER(PeerGroup)] + [vp] * 12 + [vp], i32),
         "gs_exchange_finish": ([ctypes.POINTER(PeerGroup), vp], i32),
         "gs_exchange_status": ([ctypes.POINTER(PeerGroup), vp], i32),
+        "gs_exchange_shard_layout": ([i64, i32, i32, ctypes.POINTER(ShardLayout)], i32),
+        "gs_exchange_gather_rows": ([ctypes.POINTER(PeerGroup), i64, vp, vp, vp], i32),
+        "gs_project_bwd_shard": ([i64, i32, ctypes.POINTER(PeerGroup)] + [vp] * 7 + [vp], i32),
+        "gs_exchange_publish_shard": ([ctypes.POINTER(PeerGroup), vp], i32),
+        "gs_exchange_gather_shards": ([ctypes.POINTER(PeerGroup), i64, i32] + [vp] * 5 + [vp],
+                                      i32),
         "gs_l1_loss_scratch_floats": ([], i64),
         "gs_l1_loss": ([vp, i64, i64, i64, vp, i64, i64, vp, vp, vp], i32),
         "gs_l1_loss_backward": ([vp, i64, i64, i64, vp, i64, i64, vp, vp, vp], i32),

@@ -379,13 +379,15 @@ def _backward(ctx, *grad_outputs):
                                 ctx.near, ctx.far, ctx.rendering_mode, ctx.confidence)
     pref = ctypes.byref(params)
     group = view_parallel.active_exchange()
-    peers = group is not None and view_parallel.EXCHANGE_TRANSPORT == "p2p"
+    transport = view_parallel.EXCHANGE_TRANSPORT
+    peers = group is not None and transport in view_parallel.PEER_TRANSPORTS
+    sharded = peers and transport == "p2p-shard"
     with torch.cuda.device(device):
         stream = _stream(device)
         if peers:
             # Peer exchange: the screen-space gradient goes straight into
             # this rank's arena, once every peer has finished reading it.
-            arena = view_parallel.peer_arena(n, device, group)
+            arena = view_parallel.peer_arena(n, device, group, num_sh if sharded else None)
             group_ref = ctypes.byref(arena.group)
             native.check(lib.gs_exchange_begin(group_ref, stream), "gs_exchange_begin")
             grad_projected = arena.grad_projected
@@ -414,6 +416,25 @@ def _backward(ctx, *grad_outputs):
             arena.counts.copy_(counts)
             arena.record.copy_(record)
             native.check(lib.gs_exchange_publish(group_ref, n, stream), "gs_exchange_publish")
+        if sharded:
+            # this rank's rows of every rank's gradient, the summed backward of
+            # this rank's shard, then every rank's finished shard
+            native.check(lib.gs_exchange_gather_rows(group_ref, n, _ptr(arena.gathered_grad),
+                                                     _ptr(arena.gathered_counts), stream),
+                         "gs_exchange_gather_rows")
+            _mark("begin:project_bwd")
+            native.check(lib.gs_project_bwd_shard(
+                n, num_sh, group_ref, _ptr(arena.gathered_grad), _ptr(arena.gathered_counts),
+                _ptr(mean), _ptr(rotation), _ptr(scale), _ptr(opacity), _ptr(color), stream),
+                "gs_project_bwd_shard")
+            _mark("project_bwd")
+            native.check(lib.gs_exchange_publish_shard(group_ref, stream),
+                         "gs_exchange_publish_shard")
+            native.check(lib.gs_exchange_gather_shards(
+                group_ref, n, num_sh, _ptr(grad_rotation), _ptr(grad_color), _ptr(grad_mean),
+                _ptr(grad_scale), _ptr(grad_opacity), stream), "gs_exchange_gather_shards")
+            native.check(lib.gs_exchange_finish(group_ref, stream), "gs_exchange_finish")
+        elif peers:
             # bulk copies of the peers' gradients over NVLink; the peers may
             # overwrite theirs as soon as the copies are done
             native.check(lib.gs_exchange_gather(group_ref, n, _ptr(arena.gathered_grad),

@@ -75,25 +75,34 @@ def active_exchange():
 
 
 # Largest world size at which the screen-space exchange beats the all-reduce
-# for one view per rank. At 1M Gaussians, SH3, on B200 + NVLink 5: the
-# all-reduce moves 236 MB (0.47 ms at 2 GPUs, 0.63 ms at 4); the exchange
-# all-gathers 40 MB per rank and grows the projection backward by ~55 us per
-# extra view (0.10 ms at 2 views, 0.20 ms at 4, 0.42 ms at 8), so at 8 ranks
-# its W-fold gather plus that arithmetic overtakes the all-reduce.
-SCREEN_EXCHANGE_MAX_WORLD = 4
+# for one view per rank, per transport. Copying every rank's whole gradient
+# (40 B per Gaussian from each peer) and summing all W views on every rank
+# grows by ~55 us of arithmetic per extra view at 1M Gaussians, SH3, so past 4
+# ranks the 236 MB all-reduce wins; the sharded form moves 40 B per Gaussian of
+# its own shard from each peer plus the other shards' gradients and splits
+# the arithmetic W ways, so it takes every world size the exchange supports.
+SCREEN_EXCHANGE_MAX_WORLD = {"p2p": 4, "nccl": 4, "p2p-shard": 8}
 
 
-def screen_exchange_pays(world_size: int) -> bool:
+def screen_exchange_pays(world_size: int, transport: str | None = None) -> bool:
     """Whether ``train_step`` with one view per rank should use the
-    screen-space exchange rather than the parameter-gradient all-reduce."""
-    return 1 < world_size <= SCREEN_EXCHANGE_MAX_WORLD
+    screen-space exchange (over ``transport``, by default the module's) rather
+    than the parameter-gradient all-reduce."""
+    limit = SCREEN_EXCHANGE_MAX_WORLD[transport or EXCHANGE_TRANSPORT]
+    return 1 < world_size <= limit
 
 
-# How the screen-space exchange moves the gradients: "p2p" -- the projection
-# backward reads every rank's screen-space gradients straight from its memory
-# (symmetric memory, peer-mapped over NVLink; one node, one GPU per rank) --
-# or "nccl" -- three NCCL all-gathers.
-EXCHANGE_TRANSPORT = "p2p"
+# How the screen-space exchange moves the gradients, all through symmetric
+# memory peer-mapped over NVLink (one node, one GPU per rank) except "nccl":
+# "p2p-shard" -- each rank copies its shard's rows of every rank's gradient,
+#     computes the summed projection backward of its shard, and copies the
+#     other ranks' finished shards (gs_exchange_gather_rows ..
+#     gs_exchange_gather_shards);
+# "p2p" -- each rank copies every rank's whole screen-space gradient and
+#     computes the summed projection backward of all Gaussians;
+# "nccl" -- three NCCL all-gathers, then as "p2p".
+EXCHANGE_TRANSPORT = "p2p-shard"
+PEER_TRANSPORTS = ("p2p", "p2p-shard")
 
 
 class PeerArena:
@@ -105,7 +114,7 @@ class PeerArena:
     of the peer handshake (see ``gs_exchange_publish``). Created once per
     (count, device, group) by all ranks together, outside graph capture."""
 
-    def __init__(self, n: int, device: torch.device, group):
+    def __init__(self, n: int, device: torch.device, group, num_sh: int | None = None):
         import torch.distributed._symmetric_memory as symm_mem
 
         from . import native
@@ -126,14 +135,22 @@ class PeerArena:
         layout = native.ExchangeLayout()
         native.check(lib.gs_exchange_layout_for(n, world, ctypes.byref(layout)),
                      "gs_exchange_layout_for")
-        buffer = symm_mem.empty(int(layout.bytes), dtype=torch.uint8, device=device)
+        # sharded: the arena also holds this rank's shard of parameter gradients
+        self.sharded = num_sh is not None
+        total = int(layout.bytes)
+        if self.sharded:
+            self.shard = native.ShardLayout()
+            native.check(lib.gs_exchange_shard_layout(n, world, num_sh, ctypes.byref(self.shard)),
+                         "gs_exchange_shard_layout")
+            total = int(self.shard.bytes)
+        buffer = symm_mem.empty(total, dtype=torch.uint8, device=device)
         buffer.zero_()
         torch.cuda.synchronize(device)
         handle = symm_mem.rendezvous(buffer, group)
         if handle.world_size != world:
             raise RuntimeError("symmetric memory group does not match the process group")
         offset = buffer.data_ptr() - handle.buffer_ptrs[handle.rank]
-        if offset < 0 or offset + int(layout.bytes) > handle.buffer_size:
+        if offset < 0 or offset + total > handle.buffer_size:
             raise RuntimeError("exchange arena lies outside its symmetric buffer")
         arenas = [int(base) + offset for base in handle.buffer_ptrs]
         if any(address % 256 for address in arenas):
@@ -147,9 +164,11 @@ class PeerArena:
         self.counts = buffer[layout.counts:layout.counts + 4 * n].view(torch.int32)
         self.record = buffer[layout.record:layout.record + 4 * native.VIEW_RECORD_WORDS] \
             .view(torch.int32)
-        # the peers' gradients and counts, bulk-copied here each step
-        self.gathered_grad = torch.empty((world, n, 9), dtype=torch.float32, device=device)
-        self.gathered_counts = torch.empty((world, n), dtype=torch.int32, device=device)
+        # the gradients and counts copied here each step: every rank's rows of
+        # this rank's shard (sharded), or the peers' whole arrays
+        rows = int(self.shard.rows) if self.sharded else n
+        self.gathered_grad = torch.empty((world, rows, 9), dtype=torch.float32, device=device)
+        self.gathered_counts = torch.empty((world, rows), dtype=torch.int32, device=device)
 
 
 # Exchange arenas by (Gaussian count, device, id of the process group). Each
@@ -164,14 +183,16 @@ def _resolve(group):
     return group if group is not None else dist.group.WORLD
 
 
-def peer_arena(n: int, device: torch.device, group) -> PeerArena:
-    """The exchange arena for ``n`` Gaussians on ``device`` in ``group``
-    (created on first use, by every rank of the group in the same step)."""
+def peer_arena(n: int, device: torch.device, group, num_sh: int | None = None) -> PeerArena:
+    """The exchange arena for ``n`` Gaussians on ``device`` in ``group`` --
+    sharded, with room for a shard of parameter gradients with ``num_sh`` SH
+    coefficients, when ``num_sh`` is given -- created on first use, by every
+    rank of the group in the same step."""
     group = _resolve(group)
-    key = (n, device.index, id(group))
+    key = (n, num_sh, device.index, id(group))
     entry = _ARENAS.get(key)
     if entry is None or entry[0] is not group:
-        entry = _ARENAS[key] = (group, PeerArena(n, device, group))
+        entry = _ARENAS[key] = (group, PeerArena(n, device, group, num_sh))
     return entry[1]
 
 

@@ -273,6 +273,43 @@ int32_t gs_project_bwd_peers(int64_t n, int32_t num_sh, const gs_peer_group *gro
                              float *grad_color, gs_stream_t stream);
 int32_t gs_exchange_finish(const gs_peer_group *group, gs_stream_t stream);
 
+/* Sharded exchange: the same step with the summed projection backward split
+ * over the ranks (no counterpart in the reference). Rank p owns Gaussians
+ * [p*rows, min(n, (p+1)*rows)), rows = ceil(n / world). The arena is then
+ * gs_shard_layout(...).bytes long (the plain layout followed by this rank's
+ * shard of parameter gradients, each array 256-byte aligned). A step is:
+ *   gs_exchange_begin, (compositing backward, counts and record into the
+ *   arena), gs_exchange_publish as above; then
+ *   gs_exchange_gather_rows    copy this rank's shard rows of every rank's
+ *                              gradient and counts into [world, rows, 9] /
+ *                              [world, rows] buffers on this GPU;
+ *   gs_project_bwd_shard       the projection backward of the shard summed
+ *                              over every rank's view, into the arena;
+ *   gs_exchange_publish_shard  release this rank's shard, wait for every
+ *                              peer's (bounded);
+ *   gs_exchange_gather_shards  copy every rank's shard into the full gradient
+ *                              arrays (grad_color 16-byte aligned);
+ *   gs_exchange_finish.
+ * Each rank moves rows x 40 B from every peer plus the other ranks' shards of
+ * parameter gradients, and computes 1/world of the summed backward. */
+typedef struct gs_shard_layout {
+  uint64_t rotation, color, mean, scale, opacity; /* byte offsets of the shard's gradients */
+  uint64_t bytes;                                 /* arena bytes, shard included */
+  int64_t rows;                                   /* Gaussians per shard */
+} gs_shard_layout;
+
+int32_t gs_exchange_shard_layout(int64_t n, int32_t world, int32_t num_sh, gs_shard_layout *out);
+int32_t gs_exchange_gather_rows(const gs_peer_group *group, int64_t n, float *grad_rows,
+                                int32_t *count_rows, gs_stream_t stream);
+int32_t gs_project_bwd_shard(int64_t n, int32_t num_sh, const gs_peer_group *group,
+                             const float *grad_rows, const int32_t *count_rows,
+                             const float *mean, const float *rotation, const float *scale,
+                             const float *opacity, const float *color, gs_stream_t stream);
+int32_t gs_exchange_publish_shard(const gs_peer_group *group, gs_stream_t stream);
+int32_t gs_exchange_gather_shards(const gs_peer_group *group, int64_t n, int32_t num_sh,
+                                  float *grad_rotation, float *grad_color, float *grad_mean,
+                                  float *grad_scale, float *grad_opacity, gs_stream_t stream);
+
 /* GS_OK, or GS_ERR_TIMEOUT if any wait of this rank's exchanges gave up
  * (sticky). Synchronises `stream`. */
 int32_t gs_exchange_status(const gs_peer_group *group, gs_stream_t stream);

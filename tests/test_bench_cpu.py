@@ -53,6 +53,7 @@ def test_launch_count_per_view():
     assert bench.sort_passes(1) == 0
     assert bench.launches_per_view(8160, backward=True) == 18
     assert bench.launches_per_view(8160, backward=True, peers=True) == 21
+    assert bench.launches_per_view(8160, backward=True, peers=True, sharded=True) == 22
     assert bench.launches_per_view(8160, backward=False) == 13
     assert bench.launches_per_view(256, backward=True) == 17
     assert bench.launches_per_view(1, backward=False) == 10

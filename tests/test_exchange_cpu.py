@@ -35,3 +35,24 @@ def test_peer_group_struct_matches_the_header():
     # int32 rank, int32 world, then GS_MAX_PEERS pointers
     assert ctypes.sizeof(native.PeerGroup) == 8 + 8 * native.GS_MAX_PEERS
     assert ctypes.sizeof(native.ExchangeLayout) == 5 * 8
+
+
+def test_shard_layout_follows_the_plain_arena():
+    lib = native.lib()
+    for n, world, k in ((1_000_000, 8, 16), (60_000, 2, 16), (7, 3, 1), (0, 4, 25)):
+        base = _layout(n, world)[1]
+        out = native.ShardLayout()
+        assert lib.gs_exchange_shard_layout(n, world, k, ctypes.byref(out)) == 0
+        rows = -(-n // world)
+        assert out.rows == rows
+        offsets = [out.rotation, out.color, out.mean, out.scale, out.opacity, out.bytes]
+        assert all(o % 256 == 0 for o in offsets)
+        assert out.rotation >= base.bytes  # the shard follows the plain arena
+        assert out.color >= out.rotation + 16 * rows
+        assert out.mean >= out.color + 12 * k * rows
+        assert out.scale >= out.mean + 12 * rows
+        assert out.opacity >= out.scale + 12 * rows
+        assert out.bytes >= out.opacity + 4 * rows
+    out = native.ShardLayout()
+    assert lib.gs_exchange_shard_layout(10, 2, 26, ctypes.byref(out)) != 0
+    assert lib.gs_exchange_shard_layout(10, native.GS_MAX_PEERS + 1, 16, ctypes.byref(out)) != 0

@@ -125,9 +125,10 @@ def test_exchange_plumbing_on_one_rank():
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
                     reason="needs two GPUs")
-def test_exchange_matches_all_reduce_on_two_gpus():
-    """Two NCCL ranks, one camera each: train_step with the screen-space
-    exchange gives the all-reduce path's gradients on every rank."""
+def test_exchange_matches_all_reduce_on_several_gpus():
+    """One NCCL rank per GPU (up to eight), one camera each: train_step with
+    every screen-space exchange gives the all-reduce path's gradients on every
+    rank."""
     import subprocess
     import sys
 
@@ -135,10 +136,11 @@ def test_exchange_matches_all_reduce_on_two_gpus():
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
     worker = os.path.join(os.path.dirname(os.path.abspath(__file__)), "views_exchange_worker.py")
+    world = min(torch.cuda.device_count(), 8)
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     run = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
-                          "--nproc-per-node=2", "--master-addr=127.0.0.1",
+                          f"--nproc-per-node={world}", "--master-addr=127.0.0.1",
                           f"--master-port={port}", worker],
                          env=env, capture_output=True, text=True, timeout=300)
     assert run.returncode == 0, run.stdout[-3000:] + run.stderr[-3000:]
-    assert "exchange ok at world 2" in run.stdout
+    assert f"exchange ok at world {world}" in run.stdout

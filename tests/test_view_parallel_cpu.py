@@ -178,7 +178,9 @@ def test_screen_exchange_is_seen_from_other_threads(monkeypatch):
 def test_screen_exchange_choice():
     from gaussian_splats_b200.view_parallel import screen_exchange_pays
 
-    assert [screen_exchange_pays(w) for w in (1, 2, 4, 8)] == [False, True, True, False]
+    assert [screen_exchange_pays(w, "p2p") for w in (1, 2, 4, 8)] == [False, True, True, False]
+    assert [screen_exchange_pays(w, "p2p-shard") for w in (1, 2, 4, 8)] == [False, True, True,
+                                                                           True]
 
 
 def test_collectives_are_counted_for_the_graph_guard(monkeypatch):
@@ -203,7 +205,7 @@ def _arena_worker(rank, world, port, results):
     made = []
 
     class FakeArena:
-        def __init__(self, n, device, group):
+        def __init__(self, n, device, group, num_sh=None):
             made.append((n, group))
 
     vp.PeerArena = FakeArena

@@ -5,8 +5,11 @@ Each rank renders its own camera of one shared scene; ``train_step`` with the
 screen-space exchange (all-gather of screen-space gradients, one projection
 backward over every rank's view) must give the gradients of ``train_step``
 with the parameter-gradient all-reduce, on every rank -- with the screen-space
-gradients all-gathered by NCCL, and read from peer memory (also replayed from a
-CUDA graph, which that path allows: it issues no collective).
+gradients all-gathered by NCCL, copied whole from peer memory, and sharded
+(each rank computing the summed projection backward of its own shard of
+Gaussians and copying the others' finished shards) -- the two peer-memory
+forms also replayed from a CUDA graph, which they allow: they issue no
+collective.
 """
 
 import datetime
@@ -54,13 +57,14 @@ def main():
         # gradients summed by all-reducing them, and inside the backward by
         # the screen-space exchange over NCCL and over peer memory
         results = {}
-        for mode in ("all-reduce", "nccl", "p2p"):
-            VP.EXCHANGE_TRANSPORT = "nccl" if mode == "nccl" else "p2p"
+        exchanges = ("nccl", "p2p", "p2p-shard")
+        for mode in ("all-reduce",) + exchanges:
+            VP.EXCHANGE_TRANSPORT = "p2p" if mode == "all-reduce" else mode
             train_step(splats, [camera], [target], params, render, loss_fn,
                        screen_exchange=mode != "all-reduce")
             results[mode] = [p.grad.clone() for p in params]
         names = ("mean", "rotation", "scale", "opacity", "color")
-        for mode in ("nccl", "p2p"):
+        for mode in exchanges:
             for name, a, b in zip(names, results["all-reduce"], results[mode]):
                 # compositing backward's float atomics add in scheduling order,
                 # and the paths sum the views in different orders: the
@@ -72,17 +76,20 @@ def main():
                 ref = grad.clone()
                 dist.broadcast(ref, 0)
                 assert torch.equal(ref, grad), mode
-        # the peer-memory step replayed from a CUDA graph (it issues no collective)
-        VP.EXCHANGE_TRANSPORT = "p2p"
-        step = CapturedStep(lambda: train_step(splats, [camera], [target], params, render,
-                                               loss_fn, screen_exchange=True))
-        for _ in range(3):
-            step()
-        assert step.check()
-        VP.check_exchange()
-        for name, a, p in zip(names, results["p2p"], params):
-            torch.testing.assert_close(p.grad, a, rtol=1e-4, atol=1e-4 * float(a.abs().max()),
-                                       msg=lambda m: f"graph {name}: {m}")
+        # the peer-memory steps replayed from a CUDA graph (they issue no collective)
+        for mode in ("p2p", "p2p-shard"):
+            VP.EXCHANGE_TRANSPORT = mode
+            step = CapturedStep(lambda: train_step(splats, [camera], [target], params, render,
+                                                   loss_fn, screen_exchange=True))
+            for _ in range(3):
+                step()
+            assert step.check()
+            VP.check_exchange()
+            for name, a, p in zip(names, results[mode], params):
+                torch.testing.assert_close(p.grad, a, rtol=1e-4,
+                                           atol=1e-4 * float(a.abs().max()),
+                                           msg=lambda m: f"graph {mode} {name}: {m}")
+            del step
         # the other ranks' views really were added in: the summed gradient
         # differs from this rank's own view alone
         for p in params:
@@ -94,6 +101,7 @@ def main():
         if rank == 0:
             print(f"exchange ok at world {world}", flush=True)
     finally:
+        VP.release_arenas()
         dist.destroy_process_group()
 
 
