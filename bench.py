@@ -225,16 +225,15 @@ PARITY_RTOL, PARITY_ATOL = 1e-4, 1e-6  # the parameter-gradient tolerance of the
 def gradient_parity(step, local_view, trainable, device):
     """Checks the multi-GPU step's summed gradients on every rank.
 
-    ``step()`` is the timed step (graph replay or Python launch, with its
-    exchange: peer memory or all-reduce), which leaves the summed parameter
-    gradients in ``.grad``. The check recomputes them the plain way: this
+    ``step()`` runs the timed step (graph replay or Python launch, with its
+    exchange: peer memory or all-reduce) and returns the summed parameter
+    gradients it produced. The check recomputes them the plain way: this
     rank's views forward and backward with no exchange (``local_view``), then
     one NCCL all-reduce per parameter. Tolerance: |a - b| <= atol + rtol |b|
     elementwise. Returns the worst figures over ranks; every rank gets the
     same answer."""
-    step()
+    got = [g.detach().clone() for g in step()]
     torch.cuda.synchronize()
-    got = [p.grad.detach().clone() for p in trainable]
     local_view()
     for p in trainable:
         torch.distributed.all_reduce(p.grad)
@@ -776,6 +775,9 @@ def main():
             captured()
         with ClockSampler(local_rank) as clocks:
             ms = timed(captured, args.steps)
+        # the gradient tensors the graph writes on every replay (bound to .grad
+        # during capture; later eager steps rebind .grad to other tensors)
+        step_grads = [p.grad for p in trainable]
         if not captured.check():
             raise RuntimeError("a timed replay overflowed its intersection buffer")
         if peers:
@@ -797,13 +799,21 @@ def main():
             for p in trainable:
                 p.grad = None
             for camera, target in zip(cameras, targets):
-                loss_fn(render(splats, camera), target).backward()
+                loss_fn(render(splats, camera)[0], target).backward()
 
         for _ in range(2):
             local_view()
         timed(local_view, 5)
         rank_view_ms = rank_ms[local_view]
-        parity = gradient_parity(captured if graphed else step, local_view, trainable, device)
+        if graphed:
+            def replay():
+                captured()
+                return step_grads
+        else:
+            def replay():
+                step()
+                return [p.grad for p in trainable]
+        parity = gradient_parity(replay, local_view, trainable, device)
 
     # Structure of this rank's first view (for the roofline's work counts).
     camera0 = cameras[0]

@@ -156,6 +156,78 @@ __global__ void exchange_publish_shard_kernel(gs_peer_group g) {
 
 uint64_t align256(uint64_t x) { return (x + 255) & ~uint64_t{255}; }
 
+// Byte ranges one copy launch moves (from peers' arenas or this GPU's own),
+// in order. Sources and destinations start on 16-byte boundaries.
+constexpr int kMaxSegments = 5 * GS_MAX_PEERS;
+struct CopySegment {
+  const char* src;
+  char* dst;
+  uint64_t bytes;
+};
+struct CopyPlan {
+  CopySegment seg[kMaxSegments];
+  int count;
+};
+
+// Copies `bytes` from src to dst as words of type W (both aligned to W),
+// every thread of the grid `kCopyUnroll` words in flight; loads read at L2.
+constexpr int kCopyThreads = 256;
+constexpr int kCopyUnroll = 4;
+template <class W>
+__device__ __forceinline__ void copy_words(const char* src_bytes, char* dst_bytes,
+                                           uint64_t bytes, uint64_t tid, uint64_t threads) {
+  const uint64_t words = bytes / sizeof(W);
+  const W* src = reinterpret_cast<const W*>(src_bytes);
+  W* dst = reinterpret_cast<W*>(dst_bytes);
+  uint64_t i = tid;
+  for (; i + (kCopyUnroll - 1) * threads < words; i += kCopyUnroll * threads) {
+    W v[kCopyUnroll];
+#pragma unroll
+    for (int u = 0; u < kCopyUnroll; ++u) v[u] = __ldcg(src + i + u * threads);
+#pragma unroll
+    for (int u = 0; u < kCopyUnroll; ++u) dst[i + u * threads] = v[u];
+  }
+  for (; i < words; i += threads) dst[i] = __ldcg(src + i);
+  for (uint64_t b = words * sizeof(W) + tid; b < bytes; b += threads)
+    dst_bytes[b] = __ldcg(reinterpret_cast<const signed char*>(src_bytes) + b);
+}
+
+// Every CTA of the grid walks every segment: 16-byte words where both ends
+// allow, else 4-byte words (every segment holds whole floats or ints). The
+// data came from other GPUs this step, so loads read at L2. Peer reads go
+// over NVLink from the SMs -- all links of this GPU at once -- instead of one
+// copy-engine transfer after another.
+__global__ void __launch_bounds__(kCopyThreads) peer_copy_kernel(const __grid_constant__ CopyPlan plan) {
+  const uint64_t tid = static_cast<uint64_t>(blockIdx.x) * kCopyThreads + threadIdx.x;
+  const uint64_t threads = static_cast<uint64_t>(gridDim.x) * kCopyThreads;
+  for (int s = 0; s < plan.count; ++s) {
+    const CopySegment seg = plan.seg[s];
+    const uintptr_t ends = reinterpret_cast<uintptr_t>(seg.src) | reinterpret_cast<uintptr_t>(seg.dst);
+    if (ends % 16 == 0)
+      copy_words<uint4>(seg.src, seg.dst, seg.bytes, tid, threads);
+    else
+      copy_words<uint32_t>(seg.src, seg.dst, seg.bytes, tid, threads);
+  }
+}
+
+int32_t launch_copy(const CopyPlan& plan, uint64_t bytes, cudaStream_t stream) {
+  if (plan.count == 0 || bytes == 0) return GS_OK;
+  // enough CTAs to keep every link busy, no more than the work needs
+  const uint64_t want = (bytes / 16 + kCopyThreads * kCopyUnroll - 1) / (kCopyThreads * kCopyUnroll);
+  const unsigned blocks = static_cast<unsigned>(want < 4 * kSmCount ? (want ? want : 1)
+                                                                    : 4 * kSmCount);
+  peer_copy_kernel<<<blocks, kCopyThreads, 0, stream>>>(plan);
+  return check_launch();
+}
+
+// Gaussians per shard: ceil(n / world) rounded up to a multiple of 64, so
+// every shard starts at a 16-byte boundary of every per-Gaussian array (the
+// copies below move 16-byte words).
+int64_t shard_rows(int64_t n, int world) {
+  const int64_t rows = (n + world - 1) / world;
+  return (rows + 63) / 64 * 64;
+}
+
 // Gaussians of rank p's shard: [first, first + count).
 void shard_span(int64_t n, int64_t rows, int p, int64_t* first, int64_t* count) {
   const int64_t lo = rows * p < n ? rows * p : n;
@@ -233,7 +305,7 @@ int32_t exchange_shard_layout(int64_t n, int32_t world, int32_t num_sh, gs_shard
   if (!out || num_sh < 1 || num_sh > 25) return GS_ERR_INVALID_ARGUMENT;
   gs_exchange_layout base;
   GS_TRY(exchange_layout(n, world, &base));
-  const uint64_t rows = static_cast<uint64_t>((n + world - 1) / world);
+  const uint64_t rows = static_cast<uint64_t>(shard_rows(n, world));
   uint64_t at = align256(base.bytes);
   out->rotation = at;
   at = align256(at + 16 * rows);
@@ -256,24 +328,27 @@ int32_t exchange_shard_layout(int64_t n, int32_t world, int32_t num_sh, gs_shard
 int32_t exchange_gather_rows(const gs_peer_group& g, int64_t n, float* grad_rows,
                              int32_t* count_rows, cudaStream_t stream) {
   if (!valid_group(g) || !grad_rows || !count_rows) return GS_ERR_INVALID_ARGUMENT;
+  if (reinterpret_cast<uintptr_t>(grad_rows) % 4 || reinterpret_cast<uintptr_t>(count_rows) % 4)
+    return GS_ERR_MISALIGNED;
   gs_exchange_layout layout;
   GS_TRY(exchange_layout(n, g.world, &layout));
-  const int64_t rows = (n + g.world - 1) / g.world;
+  const int64_t rows = shard_rows(n, g.world);
   int64_t first, count;
   shard_span(n, rows, g.rank, &first, &count);
   if (count <= 0) return GS_OK;
-  for (int p = 0; p < g.world; ++p) {
+  CopyPlan plan{};
+  uint64_t bytes = 0;
+  for (int step = 1; step <= g.world; ++step) {
+    const int p = (g.rank + step) % g.world;  // peers first (staggered), this rank last
     const char* base = static_cast<const char*>(g.arena[p]);
-    GS_CUDA_TRY(cudaMemcpyAsync(grad_rows + 9 * rows * p,
-                                base + layout.grad_projected + 36 * static_cast<size_t>(first),
-                                36 * static_cast<size_t>(count), cudaMemcpyDeviceToDevice,
-                                stream));
-    GS_CUDA_TRY(cudaMemcpyAsync(count_rows + rows * p,
-                                base + layout.counts + 4 * static_cast<size_t>(first),
-                                4 * static_cast<size_t>(count), cudaMemcpyDeviceToDevice,
-                                stream));
+    const size_t f = static_cast<size_t>(first), c = static_cast<size_t>(count);
+    plan.seg[plan.count++] = {base + layout.grad_projected + 36 * f,
+                              reinterpret_cast<char*>(grad_rows + 9 * rows * p), 36 * c};
+    plan.seg[plan.count++] = {base + layout.counts + 4 * f,
+                              reinterpret_cast<char*>(count_rows + rows * p), 4 * c};
+    bytes += 40 * c;
   }
-  return GS_OK;
+  return launch_copy(plan, bytes, stream);
 }
 
 // The summed projection backward of this rank's shard, over every rank's
@@ -290,7 +365,7 @@ int32_t launch_project_bwd_shard(int64_t n, int32_t num_sh, const gs_peer_group&
   int64_t first, count;
   shard_span(n, shard.rows, g.rank, &first, &count);
   if (count <= 0) return GS_OK;
-  const float* grads[GS_MAX_PEERS] = {};
+  const float* grads[GS_MAX_PEERS] = {};  // rows of view v: [v * shard.rows, +count)
   const int32_t* counts[GS_MAX_PEERS] = {};
   for (int v = 0; v < g.world; ++v) {
     grads[v] = grad_rows + 9 * shard.rows * v;
@@ -320,9 +395,13 @@ int32_t exchange_gather_shards(const gs_peer_group& g, int64_t n, int32_t num_sh
   if (!valid_group(g) || !grad_rotation || !grad_color || !grad_mean || !grad_scale ||
       !grad_opacity)
     return GS_ERR_INVALID_ARGUMENT;
+  for (const float* ptr : {grad_rotation, grad_color, grad_mean, grad_scale, grad_opacity})
+    if (reinterpret_cast<uintptr_t>(ptr) % 4) return GS_ERR_MISALIGNED;
   gs_shard_layout shard;
   GS_TRY(exchange_shard_layout(n, g.world, num_sh, &shard));
   const size_t k3 = 3 * static_cast<size_t>(num_sh);
+  CopyPlan plan{};
+  uint64_t bytes = 0;
   for (int step = 1; step <= g.world; ++step) {
     const int p = (g.rank + step) % g.world;  // peers first (staggered), this rank last
     int64_t first, count;
@@ -337,11 +416,14 @@ int32_t exchange_gather_shards(const gs_peer_group& g, int64_t n, int32_t num_sh
     } parts[5] = {{grad_rotation, shard.rotation, 4}, {grad_color, shard.color, k3},
                   {grad_mean, shard.mean, 3}, {grad_scale, shard.scale, 3},
                   {grad_opacity, shard.opacity, 1}};
-    for (const auto& part : parts)
-      GS_CUDA_TRY(cudaMemcpyAsync(part.dst + part.width * f, base + part.offset,
-                                  4 * part.width * c, cudaMemcpyDeviceToDevice, stream));
+    for (const auto& part : parts) {
+      plan.seg[plan.count++] = {base + part.offset,
+                                reinterpret_cast<char*>(part.dst + part.width * f),
+                                4 * part.width * c};
+      bytes += 4 * part.width * c;
+    }
   }
-  return GS_OK;
+  return launch_copy(plan, bytes, stream);
 }
 
 int32_t exchange_status(const gs_peer_group& g, cudaStream_t stream) {

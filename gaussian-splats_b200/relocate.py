@@ -143,6 +143,28 @@ def copy_splats(splats: GaussianSplat, counts: torch.Tensor,
 
 
 @torch.no_grad()
+def _move_optimizer_state(optimizer, replacement: dict, extra_rows: int) -> None:
+    """Hands each replaced parameter's optimizer state to its replacement.
+
+    ``replacement`` maps id(old parameter) to the new, ``extra_rows`` longer
+    parameter. The state dict is re-keyed to the new tensor with both Adam
+    moments padded by zero rows, and every parameter group is rebuilt to refer
+    to the new tensors (training/utils.py:195-209 does the same bookkeeping)."""
+    for old_id, new in replacement.items():
+        old = next((p for p in optimizer.state if id(p) == old_id), None)
+        if old is None:
+            continue
+        state = optimizer.state.pop(old)
+
+        def padded(value):
+            return torch.cat((value, value.new_zeros((extra_rows, *value.shape[1:]))))
+
+        optimizer.state[new] = {key: padded(value) if key in ("exp_avg", "exp_avg_sq") else value
+                                for key, value in state.items()}
+    for group in optimizer.param_groups:
+        group["params"] = [replacement.get(id(p), p) for p in group["params"]]
+
+
 def relocate_splats(splats: GaussianSplat, optimizer: torch.optim.Optimizer | None = None,
                     densification_factor: float = 1.0) -> None:
     """Replace dead splats with sampled copies of live ones, densify to
@@ -180,19 +202,8 @@ def relocate_splats(splats: GaussianSplat, optimizer: torch.optim.Optimizer | No
         if optimizer is not None:
             # Grow the moments first (zero rows for the new splats), so the
             # kernel resets the parents' rows in the grown state.
-            for name in _ALL_NAMES:
-                old, new = getattr(splats, name), getattr(extended, name)
-                state = optimizer.state.pop(old, None)
-                if state is not None:
-                    for key in ("exp_avg", "exp_avg_sq"):
-                        if key in state:
-                            state[key] = torch.cat((state[key], torch.zeros_like(new[-diff:])))
-                    optimizer.state[new] = state
-                for group in optimizer.param_groups:
-                    for index, parameter in enumerate(group["params"]):
-                        if parameter is old:
-                            group["params"][index] = new
-                            break
+            _move_optimizer_state(optimizer, {id(getattr(splats, name)): getattr(extended, name)
+                                              for name in _ALL_NAMES}, diff)
         new_params = [getattr(extended, name) for name in PARAMETER_NAMES]
         workspaces.append(_relocate(extended, counts, None, n, diff,
                                     _moments(optimizer, new_params)))

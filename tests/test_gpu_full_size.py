@@ -1,5 +1,6 @@
-"""Full benchmark-size parity: configs 2 (1M Gaussians, 1080p) and 5 (dense
-blob, ~57M intersections) at their real sizes.
+"""Full benchmark-size parity: configs 2 (1M Gaussians, 1080p), 3 (3M
+Gaussians, 1600x1064), 4 (6M Gaussians, 4K, the batched 16-camera forward)
+and 5 (dense blob, ~57M intersections) at their real sizes.
 
 The oracle checks what it can finish in seconds at this size: projection and
 binning of every Gaussian (bit-exact), compositing of a sample of tiles that
@@ -8,7 +9,11 @@ pixel gradient is kept only on the sampled tiles (so the oracle only needs to
 walk those tiles; 1e-4 relative / 1e-6 absolute). Size-independent properties
 cover the rest of the image: ranges tile the id list, lists are in (depth, id)
 order, every listed Gaussian's rectangle covers its tile, transmittance lies
-in [0, 1].
+in [0, 1]. Where the oracle composites the whole view in seconds (configs 2
+and 3) the whole image, transmittance and contributor counts are compared
+too. Config 4 checks its batched launch: every one of 16 cameras' ten outputs
+bit-identical to rendering that camera alone, and the first camera against
+the oracle as above (forward only: config 4 has no backward).
 """
 
 import numpy as np
@@ -37,7 +42,7 @@ def _tile_mask(settings, tiles):
     return mask
 
 
-def _check_config(oracle, scene, sample, seed):
+def _check_config(oracle, scene, sample, seed, whole_image=False, backward=True):
     inputs, s = scene_inputs(scene)
     got = run_operator(inputs, s)
     proj = oracle.project(*(inputs[k] for k in INPUTS_ORDER), s)
@@ -71,6 +76,14 @@ def _check_config(oracle, scene, sample, seed):
     mask = _tile_mask(s, tiles)
     for key in ("image", "final_transmittance", "n_contributors"):
         np.testing.assert_array_equal(got[key][mask], comp[key][mask], err_msg=key)
+    if whole_image:
+        comp = oracle.composite(proj["projected_mean"], proj["inverse_covariance"],
+                                proj["projected_color"], proj["projected_opacity"], ids, ranges,
+                                s)
+        for key in ("image", "final_transmittance", "n_contributors"):
+            np.testing.assert_array_equal(got[key], comp[key], err_msg="whole view " + key)
+    if not backward:
+        return got
 
     # Gradients with the loss restricted to the sampled tiles.
     grad_image = l1_grad_image(got["image"], scene.targets[0].numpy(), scene.crop)
@@ -88,8 +101,51 @@ def _check_config(oracle, scene, sample, seed):
 def test_config2_full_size(oracle):
     from gaussian_splats_b200 import scenes
 
-    got = _check_config(oracle, scenes.config2(), sample=192, seed=0)
+    got = _check_config(oracle, scenes.config2(), sample=192, seed=0, whole_image=True)
     assert len(got["gaussian_ids"]) > 1_000_000
+
+
+def test_config3_full_size(oracle):
+    from gaussian_splats_b200 import scenes
+
+    scene = scenes.config3()
+    assert scene.num_points == 3_000_000 and scene.crop == (1600, 1064)
+    got = _check_config(oracle, scene, sample=128, seed=2, whole_image=True)
+    assert len(got["gaussian_ids"]) > 3_000_000
+
+
+def test_config4_batched_full_size(oracle):
+    """The bench's config-4 launch shape: 16 cameras of the 4K orbit per
+    rasterize_batch call over 6M Gaussians."""
+    import torch
+
+    from gaussian_splats_b200 import scenes
+    from gaussian_splats_b200.rasterize import rasterize_batch, rasterize_outputs
+    from gaussian_splats_b200.splats import GaussianSplat
+
+    scene = scenes.config4()
+    assert scene.num_points == 6_000_000 and scene.crop == (3840, 2160)
+    splats = GaussianSplat.from_tensors(*(t.cuda() for t in scene.tensors()))
+    cameras = scene.cameras[:16]
+    st = scene.settings
+    with torch.no_grad():
+        batch = rasterize_batch(splats, cameras, st.tile_size, st.opacity_threshold, st.near,
+                                st.far)
+        for camera, got in zip(cameras, batch):
+            want = rasterize_outputs(splats, camera, st.tile_size, st.opacity_threshold,
+                                     st.near, st.far)
+            for name, a, b in zip(("image", "final_transmittance", "n_contributors",
+                                   "projected_mean", "inverse_covariance", "projected_color",
+                                   "projected_opacity", "gaussian_ids", "ranges", "counts"),
+                                  got, want):
+                assert a.dtype == b.dtype and a.shape == b.shape, name
+                assert torch.equal(a, b), name
+            del want
+    first = batch[0]
+    del batch, splats
+    torch.cuda.empty_cache()
+    got = _check_config(oracle, scene, sample=96, seed=3, backward=False)
+    assert np.array_equal(got["image"], first[0].cpu().numpy())
 
 
 def test_config5_full_size(oracle):
