@@ -105,8 +105,8 @@ def parse_args():
                    default="auto",
                    help="how ranks sum gradients with one view per rank: the sharded peer "
                         "exchange, the whole-gradient peer exchange, its NCCL all-gather form, "
-                        "or the parameter-gradient all-reduce (auto: the sharded exchange where "
-                        "view_parallel.screen_exchange_pays)")
+                        "or the parameter-gradient all-reduce (auto: view_parallel's choice "
+                        "for the world size)")
     return p.parse_args()
 
 
@@ -713,11 +713,14 @@ def main():
     # summing the projection backward over all views (view_parallel), where
     # that beats all-reducing the parameter gradients; several views per rank:
     # the parameter gradients are all-reduced once per step.
-    transport = {"screen": "p2p", "screen-nccl": "nccl"}.get(args.exchange, "p2p-shard")
+    transport = {"screen": "p2p", "screen-nccl": "nccl", "shard": "p2p-shard"}.get(
+        args.exchange, "auto")
     screen = world > 1 and len(cameras) == 1 and (
         args.exchange in ("shard", "screen", "screen-nccl") or
         (args.exchange == "auto" and screen_exchange_pays(world, transport)))
     view_parallel.EXCHANGE_TRANSPORT = transport
+    if world > 1:
+        transport = view_parallel.transport_for()
     peers = screen and transport in view_parallel.PEER_TRANSPORTS
 
     def train_step():

@@ -379,7 +379,7 @@ def _backward(ctx, *grad_outputs):
                                 ctx.near, ctx.far, ctx.rendering_mode, ctx.confidence)
     pref = ctypes.byref(params)
     group = view_parallel.active_exchange()
-    transport = view_parallel.EXCHANGE_TRANSPORT
+    transport = view_parallel.transport_for(group) if group is not None else None
     peers = group is not None and transport in view_parallel.PEER_TRANSPORTS
     sharded = peers and transport == "p2p-shard"
     with torch.cuda.device(device):
@@ -389,7 +389,9 @@ def _backward(ctx, *grad_outputs):
             # this rank's arena, once every peer has finished reading it.
             arena = view_parallel.peer_arena(n, device, group, num_sh if sharded else None)
             group_ref = ctypes.byref(arena.group)
+            _mark("begin:exchange_wait")
             native.check(lib.gs_exchange_begin(group_ref, stream), "gs_exchange_begin")
+            _mark("exchange_wait")
             grad_projected = arena.grad_projected
         else:
             grad_projected = mean.new_empty((n, 9))
@@ -415,31 +417,41 @@ def _backward(ctx, *grad_outputs):
         if peers:
             arena.counts.copy_(counts)
             arena.record.copy_(record)
+            _mark("begin:exchange_publish")
             native.check(lib.gs_exchange_publish(group_ref, n, stream), "gs_exchange_publish")
+            _mark("exchange_publish")
         if sharded:
             # this rank's rows of every rank's gradient, the summed backward of
             # this rank's shard, then every rank's finished shard
+            _mark("begin:exchange_rows")
             native.check(lib.gs_exchange_gather_rows(group_ref, n, _ptr(arena.gathered_grad),
                                                      _ptr(arena.gathered_counts), stream),
                          "gs_exchange_gather_rows")
+            _mark("exchange_rows")
             _mark("begin:project_bwd")
             native.check(lib.gs_project_bwd_shard(
                 n, num_sh, group_ref, _ptr(arena.gathered_grad), _ptr(arena.gathered_counts),
                 _ptr(mean), _ptr(rotation), _ptr(scale), _ptr(opacity), _ptr(color), stream),
                 "gs_project_bwd_shard")
             _mark("project_bwd")
+            _mark("begin:exchange_shard_wait")
             native.check(lib.gs_exchange_publish_shard(group_ref, stream),
                          "gs_exchange_publish_shard")
+            _mark("exchange_shard_wait")
+            _mark("begin:exchange_shards")
             native.check(lib.gs_exchange_gather_shards(
                 group_ref, n, num_sh, _ptr(grad_rotation), _ptr(grad_color), _ptr(grad_mean),
                 _ptr(grad_scale), _ptr(grad_opacity), stream), "gs_exchange_gather_shards")
+            _mark("exchange_shards")
             native.check(lib.gs_exchange_finish(group_ref, stream), "gs_exchange_finish")
         elif peers:
             # bulk copies of the peers' gradients over NVLink; the peers may
             # overwrite theirs as soon as the copies are done
+            _mark("begin:exchange_rows")
             native.check(lib.gs_exchange_gather(group_ref, n, _ptr(arena.gathered_grad),
                                                 _ptr(arena.gathered_counts), stream),
                          "gs_exchange_gather")
+            _mark("exchange_rows")
             native.check(lib.gs_exchange_finish(group_ref, stream), "gs_exchange_finish")
             _mark("begin:project_bwd")
             native.check(lib.gs_project_bwd_peers(

@@ -81,7 +81,7 @@ def active_exchange():
 # ranks the 236 MB all-reduce wins; the sharded form moves 40 B per Gaussian of
 # its own shard from each peer plus the other shards' gradients and splits
 # the arithmetic W ways, so it takes every world size the exchange supports.
-SCREEN_EXCHANGE_MAX_WORLD = {"p2p": 4, "nccl": 4, "p2p-shard": 8}
+SCREEN_EXCHANGE_MAX_WORLD = {"p2p": 4, "nccl": 4, "p2p-shard": 8, "auto": 8}
 
 
 def screen_exchange_pays(world_size: int, transport: str | None = None) -> bool:
@@ -100,9 +100,22 @@ def screen_exchange_pays(world_size: int, transport: str | None = None) -> bool:
 #     gs_exchange_gather_shards);
 # "p2p" -- each rank copies every rank's whole screen-space gradient and
 #     computes the summed projection backward of all Gaussians;
-# "nccl" -- three NCCL all-gathers, then as "p2p".
-EXCHANGE_TRANSPORT = "p2p-shard"
+# "nccl" -- three NCCL all-gathers, then as "p2p";
+# "auto" -- "p2p" for two ranks, "p2p-shard" for more. On B200s with 1M
+# Gaussians, SH3 (steps replayed from CUDA graphs): 2 ranks 1.88 ms per step
+# whole vs 1.96 sharded (each rank has only one peer to copy 40 MB from, while
+# the shard exchange copies 118 MB of parameter gradients); 4 ranks 2.29 ms
+# whole vs 2.10 sharded.
+EXCHANGE_TRANSPORT = "auto"
 PEER_TRANSPORTS = ("p2p", "p2p-shard")
+
+
+def transport_for(group=None) -> str:
+    """The transport the screen-space exchange uses in ``group``."""
+    if EXCHANGE_TRANSPORT != "auto":
+        return EXCHANGE_TRANSPORT
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    return "p2p" if world <= 2 else "p2p-shard"
 
 
 class PeerArena:

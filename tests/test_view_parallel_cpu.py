@@ -181,6 +181,7 @@ def test_screen_exchange_choice():
     assert [screen_exchange_pays(w, "p2p") for w in (1, 2, 4, 8)] == [False, True, True, False]
     assert [screen_exchange_pays(w, "p2p-shard") for w in (1, 2, 4, 8)] == [False, True, True,
                                                                            True]
+    assert [screen_exchange_pays(w, "auto") for w in (1, 2, 4, 8)] == [False, True, True, True]
 
 
 def test_collectives_are_counted_for_the_graph_guard(monkeypatch):
