@@ -61,6 +61,39 @@ inline int32_t check_params(const gs_params* p) {
   return GS_OK;
 }
 
+// Starts moving the 16-byte-aligned interior of [ptr, ptr + bytes) from DRAM
+// into L2 and returns at once (TMA bulk prefetch: no registers, shared memory
+// or barrier, nothing to wait for). One thread of a CTA calls it for the
+// CTA's contiguous block of an input array, so the whole block is requested
+// at the CTA's start instead of load by load behind the thread's dependent
+// arithmetic; the threads' own loads then find it in L2. Only addresses
+// inside the range are touched.
+__device__ __forceinline__ void prefetch_l2(const void* ptr, uint64_t bytes) {
+  constexpr uint64_t kChunk = 1 << 16;  // bytes per instruction
+  uint64_t begin = (reinterpret_cast<uint64_t>(ptr) + 15) & ~uint64_t{15};
+  const uint64_t end = (reinterpret_cast<uint64_t>(ptr) + bytes) & ~uint64_t{15};
+  for (; begin < end; begin += kChunk) {
+    const uint64_t size = end - begin < kChunk ? end - begin : kChunk;
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(begin),
+                 "r"(static_cast<uint32_t>(size))
+                 : "memory");
+  }
+}
+
+// Prefetches a CTA's rows [first, first + rows) of the Gaussian parameter
+// arrays (mean, rotation, scale, opacity, K SH coefficients) into L2.
+__device__ __forceinline__ void prefetch_gaussian_rows(int64_t first, int64_t rows, int k,
+                                                       const float* mean, const float* rotation,
+                                                       const float* scale, const float* opacity,
+                                                       const float* color) {
+  const uint64_t r = static_cast<uint64_t>(rows);
+  prefetch_l2(color + first * 3 * k, r * 12 * k);
+  prefetch_l2(mean + first * 3, r * 12);
+  prefetch_l2(rotation + first * 4, r * 16);
+  prefetch_l2(scale + first * 3, r * 12);
+  prefetch_l2(opacity + first, r * 4);
+}
+
 // Pair evaluation shared by the forward and backward compositors:
 // d^2 = xx dx^2 + 2 xy dx dy + yy dy^2 with integer pixel coordinates
 // (composite.py:159-161), evaluated as fmaf(xx*dx, dx, fmaf((2xy)*dx, dy, (yy*dy)*dy)).

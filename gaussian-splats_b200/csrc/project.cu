@@ -221,6 +221,11 @@ __global__ void __launch_bounds__(256) project_fwd_kernel(
     int4* __restrict__ bounds, int32_t* __restrict__ counts) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= n) return;
+  if (threadIdx.x == 0) {
+    const int64_t first = static_cast<int64_t>(blockIdx.x) * blockDim.x;
+    prefetch_gaussian_rows(first, n - first < blockDim.x ? n - first : blockDim.x, K, mean,
+                           rotation, scale, opacity, color);
+  }
   const Camera c = load_camera(camera_rotation, camera_translation);
   const float mx = __ldg(mean + 3 * i), my = __ldg(mean + 3 * i + 1), mz = __ldg(mean + 3 * i + 2);
   // project.py:126-142
@@ -372,6 +377,11 @@ __global__ void __launch_bounds__(256) project_fwd_batch_kernel(
     int4* __restrict__ bounds, int32_t* __restrict__ counts) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= n) return;
+  if (threadIdx.x == 0) {
+    const int64_t first = static_cast<int64_t>(blockIdx.x) * blockDim.x;
+    prefetch_gaussian_rows(first, n - first < blockDim.x ? n - first : blockDim.x, K, mean,
+                           rotation, scale, opacity, color);
+  }
   const GaussianTerms g = gaussian_terms(i, mean, rotation, scale, opacity);
   for (int b = 0; b < batch.views; ++b) {
     const int64_t o = static_cast<int64_t>(b) * n;
@@ -786,6 +796,11 @@ __global__ void __launch_bounds__(128, K > 16 ? 3 : 4) project_bwd_views_kernel(
     float* __restrict__ grad_opacity, float* __restrict__ grad_color) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= n) return;
+  if (threadIdx.x == 0) {
+    const int64_t first = static_cast<int64_t>(blockIdx.x) * blockDim.x;
+    prefetch_gaussian_rows(first, n - first < blockDim.x ? n - first : blockDim.x, K, mean,
+                           rotation, scale, opacity, color);
+  }
   const GaussianTerms g = gaussian_terms(i, mean, rotation, scale, opacity);
   const BwdTerms b = bwd_terms(i, mean, rotation, scale, opacity);
   __shared__ float color_acc[K * 3][128];
@@ -821,6 +836,14 @@ __global__ void __launch_bounds__(128) project_bwd_kernel(
     float* __restrict__ grad_color) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= n) return;
+  if (threadIdx.x == 0) {
+    const int64_t first = static_cast<int64_t>(blockIdx.x) * blockDim.x;
+    const int64_t rows = n - first < blockDim.x ? n - first : blockDim.x;
+    prefetch_gaussian_rows(first, rows, K, mean, rotation, scale, opacity, color);
+    prefetch_l2(inverse_covariance + 4 * first, 16 * static_cast<uint64_t>(rows));
+    prefetch_l2(grad_projected + 9 * first, 36 * static_cast<uint64_t>(rows));
+    prefetch_l2(counts + first, 4 * static_cast<uint64_t>(rows));
+  }
   const bool visible = __ldg(counts + i) != 0;
   const Camera c = load_camera(camera_rotation, camera_translation);
   const float4 inv = __ldg(reinterpret_cast<const float4*>(inverse_covariance) + i);

@@ -111,7 +111,8 @@ def banded_view(ref, splats, camera, settings, target, backward, band_rows):
                 # this band's share of the L1 mean over the cropped image
                 rows = slice(row0 * ts, min(tiles_h, row0 + band_rows) * ts)
                 crop = band[:target.shape[0], :target.shape[1]][rows]
-                ((crop - target[rows]).abs().sum() / count).backward()
+                # retain_graph: the bands share project's cached inverse covariance
+                ((crop - target[rows]).abs().sum() / count).backward(retain_graph=True)
             image += band.detach()
         if backward:
             torch.autograd.backward(
