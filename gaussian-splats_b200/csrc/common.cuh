@@ -4,8 +4,6 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
-#include <mutex>
-#include <unordered_map>
 
 #include "../../include/gs_b200.h"
 #include "detmath.cuh"
@@ -61,40 +59,6 @@ inline int32_t check_params(const gs_params* p) {
   if (p->width < 0 || p->height < 0 || p->width % ts || p->height % ts)
     return GS_ERR_INVALID_ARGUMENT;
   return GS_OK;
-}
-
-// Grid of a persistent kernel: as many CTAs of `threads` threads as fit on
-// the device at once (resident CTAs per SM from the occupancy calculator,
-// cached per kernel and device), and no more than `blocks_needed`. Each CTA
-// then strides over blocks of work, so there is no partial last wave and a
-// CTA can prefetch its next block while it works on the current one.
-inline unsigned persistent_grid(const void* kernel, int threads, int64_t blocks_needed) {
-  static std::mutex mutex;
-  static std::unordered_map<const void*, int> per_sm[64];
-  int device = 0;
-  if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= 64) device = 0;
-  int resident = 0, sms = kSmCount;
-  {
-    std::lock_guard<std::mutex> lock(mutex);
-    auto found = per_sm[device].find(kernel);
-    if (found == per_sm[device].end()) {
-      int blocks = 0;
-      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kernel, threads, 0) !=
-          cudaSuccess) {
-        cudaGetLastError();  // not a launch error: fall back to one CTA per SM
-        blocks = 1;
-      }
-      found = per_sm[device].emplace(kernel, blocks > 0 ? blocks : 1).first;
-    }
-    resident = found->second;
-  }
-  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) {
-    cudaGetLastError();
-    sms = kSmCount;
-  }
-  const int64_t grid = static_cast<int64_t>(resident) * (sms > 0 ? sms : kSmCount);
-  return static_cast<unsigned>(blocks_needed < grid ? (blocks_needed > 0 ? blocks_needed : 1)
-                                                    : grid);
 }
 
 // Starts moving the 16-byte-aligned interior of [ptr, ptr + bytes) from DRAM

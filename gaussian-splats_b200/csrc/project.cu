@@ -210,15 +210,23 @@ __device__ __forceinline__ void project_view(
   counts[i] = (safe_z > p.near_plane && safe_z < p.far_plane) ? static_cast<int32_t>(count) : 0;
 }
 
-// Projection of Gaussian i into camera c (the body of project_fwd_kernel).
 template <int K>
-__device__ __forceinline__ void project_fwd_gaussian(
-    int64_t i, const Camera& c, const float* __restrict__ mean,
-    const float* __restrict__ rotation, const float* __restrict__ scale,
-    const float* __restrict__ opacity, const float* __restrict__ color, const gs_params& p,
+__global__ void __launch_bounds__(256) project_fwd_kernel(
+    int64_t n, const float* __restrict__ mean, const float* __restrict__ rotation,
+    const float* __restrict__ scale, const float* __restrict__ opacity,
+    const float* __restrict__ color, const float* __restrict__ camera_rotation,
+    const float* __restrict__ camera_translation, const gs_params p,
     float* __restrict__ projected_mean, float* __restrict__ inverse_covariance,
     float* __restrict__ projected_color, float* __restrict__ projected_opacity,
     int4* __restrict__ bounds, int32_t* __restrict__ counts) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  if (threadIdx.x == 0) {
+    const int64_t first = static_cast<int64_t>(blockIdx.x) * blockDim.x;
+    prefetch_gaussian_rows(first, n - first < blockDim.x ? n - first : blockDim.x, K, mean,
+                           rotation, scale, opacity, color);
+  }
+  const Camera c = load_camera(camera_rotation, camera_translation);
   const float mx = __ldg(mean + 3 * i), my = __ldg(mean + 3 * i + 1), mz = __ldg(mean + 3 * i + 2);
   // project.py:126-142
   const float camera_x = mx * c.r00 + my * c.r01 + mz * c.r02 + c.tx;
@@ -313,40 +321,6 @@ __device__ __forceinline__ void project_fwd_gaussian(
   counts[i] = (safe_z > p.near_plane && safe_z < p.far_plane) ? static_cast<int32_t>(count) : 0;
 }
 
-// Persistent projection: each CTA strides over blocks of kProjectThreads
-// Gaussians and, while it projects one block, has the next block's parameter
-// rows brought into L2 (TMA bulk prefetch), so the loads of every block after
-// the first find their data in L2.
-constexpr int kProjectThreads = 256;
-
-template <int K>
-__global__ void __launch_bounds__(kProjectThreads, 5) project_fwd_kernel(
-    int64_t n, const float* __restrict__ mean, const float* __restrict__ rotation,
-    const float* __restrict__ scale, const float* __restrict__ opacity,
-    const float* __restrict__ color, const float* __restrict__ camera_rotation,
-    const float* __restrict__ camera_translation, const gs_params p,
-    float* __restrict__ projected_mean, float* __restrict__ inverse_covariance,
-    float* __restrict__ projected_color, float* __restrict__ projected_opacity,
-    int4* __restrict__ bounds, int32_t* __restrict__ counts) {
-  const Camera c = load_camera(camera_rotation, camera_translation);
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * kProjectThreads;
-  int64_t base = static_cast<int64_t>(blockIdx.x) * kProjectThreads;
-  if (threadIdx.x == 0 && base < n)
-    prefetch_gaussian_rows(base, n - base < kProjectThreads ? n - base : kProjectThreads, K,
-                           mean, rotation, scale, opacity, color);
-  for (; base < n; base += stride) {
-    const int64_t next = base + stride;
-    if (threadIdx.x == 0 && next < n)
-      prefetch_gaussian_rows(next, n - next < kProjectThreads ? n - next : kProjectThreads, K,
-                             mean, rotation, scale, opacity, color);
-    const int64_t i = base + threadIdx.x;
-    if (i < n)
-      project_fwd_gaussian<K>(i, c, mean, rotation, scale, opacity, color, p, projected_mean,
-                              inverse_covariance, projected_color, projected_opacity, bounds,
-                              counts);
-  }
-}
-
 // One view's conic as the forward computes it (project.py:126-142,158-218):
 // the expressions of project_fwd_kernel, so the same bits as the conic the
 // forward wrote.
@@ -394,32 +368,26 @@ struct ViewBatch {
 // the batch (its SH row comes from HBM once; the later views' loads hit L1).
 // View b writes at offset b * n of each output.
 template <int K>
-__global__ void __launch_bounds__(kProjectThreads) project_fwd_batch_kernel(
+__global__ void __launch_bounds__(256) project_fwd_batch_kernel(
     int64_t n, const float* __restrict__ mean, const float* __restrict__ rotation,
     const float* __restrict__ scale, const float* __restrict__ opacity,
     const float* __restrict__ color, const __grid_constant__ ViewBatch batch,
     float* __restrict__ projected_mean, float* __restrict__ inverse_covariance,
     float* __restrict__ projected_color, float* __restrict__ projected_opacity,
     int4* __restrict__ bounds, int32_t* __restrict__ counts) {
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * kProjectThreads;
-  int64_t base = static_cast<int64_t>(blockIdx.x) * kProjectThreads;
-  if (threadIdx.x == 0 && base < n)
-    prefetch_gaussian_rows(base, n - base < kProjectThreads ? n - base : kProjectThreads, K,
-                           mean, rotation, scale, opacity, color);
-  for (; base < n; base += stride) {
-    const int64_t next = base + stride;
-    if (threadIdx.x == 0 && next < n)
-      prefetch_gaussian_rows(next, n - next < kProjectThreads ? n - next : kProjectThreads, K,
-                             mean, rotation, scale, opacity, color);
-    const int64_t i = base + threadIdx.x;
-    if (i >= n) continue;
-    const GaussianTerms g = gaussian_terms(i, mean, rotation, scale, opacity);
-    for (int b = 0; b < batch.views; ++b) {
-      const int64_t o = static_cast<int64_t>(b) * n;
-      project_view<K>(i, g, color + i * (K * 3), batch.c[b], batch.p[b],
-                      projected_mean + 3 * o, inverse_covariance + 4 * o,
-                      projected_color + 3 * o, projected_opacity + o, bounds + o, counts + o);
-    }
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  if (threadIdx.x == 0) {
+    const int64_t first = static_cast<int64_t>(blockIdx.x) * blockDim.x;
+    prefetch_gaussian_rows(first, n - first < blockDim.x ? n - first : blockDim.x, K, mean,
+                           rotation, scale, opacity, color);
+  }
+  const GaussianTerms g = gaussian_terms(i, mean, rotation, scale, opacity);
+  for (int b = 0; b < batch.views; ++b) {
+    const int64_t o = static_cast<int64_t>(b) * n;
+    project_view<K>(i, g, color + i * (K * 3), batch.c[b], batch.p[b], projected_mean + 3 * o,
+                    inverse_covariance + 4 * o, projected_color + 3 * o, projected_opacity + o,
+                    bounds + o, counts + o);
   }
 }
 
@@ -826,62 +794,38 @@ __global__ void __launch_bounds__(128, K > 16 ? 3 : 4) project_bwd_views_kernel(
     const __grid_constant__ Source src, float* __restrict__ grad_mean,
     float* __restrict__ grad_rotation, float* __restrict__ grad_scale,
     float* __restrict__ grad_opacity, float* __restrict__ grad_color) {
-  __shared__ float color_acc[K * 3][128];
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * 128;
-  int64_t base = static_cast<int64_t>(blockIdx.x) * 128;
-  if (threadIdx.x == 0 && base < n)
-    prefetch_gaussian_rows(base, n - base < 128 ? n - base : 128, K, mean, rotation, scale,
-                           opacity, color);
-  for (; base < n; base += stride) {
-    const int64_t next = base + stride;
-    if (threadIdx.x == 0 && next < n)
-      prefetch_gaussian_rows(next, n - next < 128 ? n - next : 128, K, mean, rotation, scale,
-                             opacity, color);
-    const int64_t i = base + threadIdx.x;
-    if (i >= n) continue;
-    const GaussianTerms g = gaussian_terms(i, mean, rotation, scale, opacity);
-    const BwdTerms b = bwd_terms(i, mean, rotation, scale, opacity);
-    SharedAccumulateGradients<K> acc{color_acc, static_cast<int>(threadIdx.x)};
-    acc.zero();
-    for (int v = 0; v < num_views; ++v) {
-      if (src.count(v, i) == 0) continue;
-      const gs_params p = views[v].p;
-      const float* R = views[v].R;
-      const float* t = views[v].t;
-      const Camera c{R[0], R[1], R[2], R[3], R[4], R[5], R[6], R[7], R[8], t[0], t[1], t[2]};
-      const float4 inv = view_conic(g, c, p);
-      project_bwd_view<K, SharedAccumulateGradients<K>, typename Source::Load>(
-          i, true, c, p, b, color, inv, src.grad(v, i), acc);
-    }
-    float sum[K * 3];
-#pragma unroll
-    for (int j = 0; j < K * 3; ++j) sum[j] = color_acc[j][threadIdx.x];
-    StoreGradients<K> out{i, grad_mean, grad_rotation, grad_scale, grad_opacity, grad_color};
-    out.color(sum);
-    out.rest(acc.m[0], acc.m[1], acc.m[2], acc.r, acc.s[0], acc.s[1], acc.s[2], acc.o);
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  if (threadIdx.x == 0) {
+    const int64_t first = static_cast<int64_t>(blockIdx.x) * blockDim.x;
+    prefetch_gaussian_rows(first, n - first < blockDim.x ? n - first : blockDim.x, K, mean,
+                           rotation, scale, opacity, color);
   }
+  const GaussianTerms g = gaussian_terms(i, mean, rotation, scale, opacity);
+  const BwdTerms b = bwd_terms(i, mean, rotation, scale, opacity);
+  __shared__ float color_acc[K * 3][128];
+  SharedAccumulateGradients<K> acc{color_acc, static_cast<int>(threadIdx.x)};
+  acc.zero();
+  for (int v = 0; v < num_views; ++v) {
+    if (src.count(v, i) == 0) continue;
+    const gs_params p = views[v].p;
+    const float* R = views[v].R;
+    const float* t = views[v].t;
+    const Camera c{R[0], R[1], R[2], R[3], R[4], R[5], R[6], R[7], R[8], t[0], t[1], t[2]};
+    const float4 inv = view_conic(g, c, p);
+    project_bwd_view<K, SharedAccumulateGradients<K>, typename Source::Load>(
+        i, true, c, p, b, color, inv, src.grad(v, i), acc);
+  }
+  float sum[K * 3];
+#pragma unroll
+  for (int j = 0; j < K * 3; ++j) sum[j] = color_acc[j][threadIdx.x];
+  StoreGradients<K> out{i, grad_mean, grad_rotation, grad_scale, grad_opacity, grad_color};
+  out.color(sum);
+  out.rest(acc.m[0], acc.m[1], acc.m[2], acc.r, acc.s[0], acc.s[1], acc.s[2], acc.o);
 }
 
-// The CTA's block [first, first + rows) of every input of the single-view
-// projection backward, requested into L2.
 template <int K>
-__device__ __forceinline__ void prefetch_bwd_rows(int64_t first, int64_t rows,
-                                                  const float* mean, const float* rotation,
-                                                  const float* scale, const float* opacity,
-                                                  const float* color,
-                                                  const float* inverse_covariance,
-                                                  const float* grad_projected,
-                                                  const int32_t* counts) {
-  prefetch_gaussian_rows(first, rows, K, mean, rotation, scale, opacity, color);
-  prefetch_l2(inverse_covariance + 4 * first, 16 * static_cast<uint64_t>(rows));
-  prefetch_l2(grad_projected + 9 * first, 36 * static_cast<uint64_t>(rows));
-  prefetch_l2(counts + first, 4 * static_cast<uint64_t>(rows));
-}
-
-// Persistent like the forward: each CTA strides over blocks of 128
-// Gaussians, the next block's inputs prefetched into L2 while it works.
-template <int K>
-__global__ void __launch_bounds__(128, K > 16 ? 1 : 6) project_bwd_kernel(
+__global__ void __launch_bounds__(128) project_bwd_kernel(
     int64_t n, const float* __restrict__ mean, const float* __restrict__ rotation,
     const float* __restrict__ scale, const float* __restrict__ opacity,
     const float* __restrict__ color, const float* __restrict__ camera_rotation,
@@ -890,25 +834,22 @@ __global__ void __launch_bounds__(128, K > 16 ? 1 : 6) project_bwd_kernel(
     const gs_params p, float* __restrict__ grad_mean, float* __restrict__ grad_rotation,
     float* __restrict__ grad_scale, float* __restrict__ grad_opacity,
     float* __restrict__ grad_color) {
-  const Camera c = load_camera(camera_rotation, camera_translation);
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * 128;
-  int64_t base = static_cast<int64_t>(blockIdx.x) * 128;
-  if (threadIdx.x == 0 && base < n)
-    prefetch_bwd_rows<K>(base, n - base < 128 ? n - base : 128, mean, rotation, scale, opacity,
-                         color, inverse_covariance, grad_projected, counts);
-  for (; base < n; base += stride) {
-    const int64_t next = base + stride;
-    if (threadIdx.x == 0 && next < n)
-      prefetch_bwd_rows<K>(next, n - next < 128 ? n - next : 128, mean, rotation, scale,
-                           opacity, color, inverse_covariance, grad_projected, counts);
-    const int64_t i = base + threadIdx.x;
-    if (i >= n) continue;
-    const bool visible = __ldg(counts + i) != 0;
-    const float4 inv = __ldg(reinterpret_cast<const float4*>(inverse_covariance) + i);
-    StoreGradients<K> sink{i, grad_mean, grad_rotation, grad_scale, grad_opacity, grad_color};
-    project_bwd_view<K>(i, visible, c, p, bwd_terms(i, mean, rotation, scale, opacity), color,
-                        inv, grad_projected + 9 * i, sink);
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  if (threadIdx.x == 0) {
+    const int64_t first = static_cast<int64_t>(blockIdx.x) * blockDim.x;
+    const int64_t rows = n - first < blockDim.x ? n - first : blockDim.x;
+    prefetch_gaussian_rows(first, rows, K, mean, rotation, scale, opacity, color);
+    prefetch_l2(inverse_covariance + 4 * first, 16 * static_cast<uint64_t>(rows));
+    prefetch_l2(grad_projected + 9 * first, 36 * static_cast<uint64_t>(rows));
+    prefetch_l2(counts + first, 4 * static_cast<uint64_t>(rows));
   }
+  const bool visible = __ldg(counts + i) != 0;
+  const Camera c = load_camera(camera_rotation, camera_translation);
+  const float4 inv = __ldg(reinterpret_cast<const float4*>(inverse_covariance) + i);
+  StoreGradients<K> sink{i, grad_mean, grad_rotation, grad_scale, grad_opacity, grad_color};
+  project_bwd_view<K>(i, visible, c, p, bwd_terms(i, mean, rotation, scale, opacity), color,
+                      inv, grad_projected + 9 * i, sink);
 }
 
 }  // namespace
@@ -930,10 +871,9 @@ int32_t launch_project_fwd(int64_t n, int32_t num_sh, const float* mean, const f
                            float* projected_color, float* projected_opacity, int32_t* bounds,
                            int32_t* counts, cudaStream_t stream) {
   if (n == 0) return GS_OK;
+  const unsigned blocks = ceil_div(n, 256);
 #define GS_LAUNCH(K)                                                                          \
-  project_fwd_kernel<K><<<persistent_grid(reinterpret_cast<const void*>(project_fwd_kernel<K>), \
-                                          kProjectThreads, ceil_div(n, kProjectThreads)),      \
-                          kProjectThreads, 0, stream>>>(                                      \
+  project_fwd_kernel<K><<<blocks, 256, 0, stream>>>(                                          \
       n, mean, rotation, scale, opacity, color, camera_rotation, camera_translation, p,       \
       projected_mean, inverse_covariance, projected_color, projected_opacity,                 \
       reinterpret_cast<int4*>(bounds), counts)
@@ -951,6 +891,7 @@ int32_t launch_project_fwd_batch(int64_t n, int32_t num_sh, int32_t num_views, c
                                  float* projected_opacity, int32_t* bounds, int32_t* counts,
                                  cudaStream_t stream) {
   if (n == 0 || num_views == 0) return GS_OK;
+  const unsigned blocks = ceil_div(n, 256);
   for (int first = 0; first < num_views; first += kMaxBatchViews) {
     ViewBatch batch{};
     batch.views = num_views - first < kMaxBatchViews ? num_views - first : kMaxBatchViews;
@@ -962,10 +903,7 @@ int32_t launch_project_fwd_batch(int64_t n, int32_t num_sh, int32_t num_views, c
     }
     const int64_t o = static_cast<int64_t>(first) * n;
 #define GS_LAUNCH(K)                                                                          \
-  project_fwd_batch_kernel<K><<<persistent_grid(                                             \
-                                   reinterpret_cast<const void*>(project_fwd_batch_kernel<K>), \
-                                   kProjectThreads, ceil_div(n, kProjectThreads)),             \
-                                kProjectThreads, 0, stream>>>(                                \
+  project_fwd_batch_kernel<K><<<blocks, 256, 0, stream>>>(                                    \
       n, mean, rotation, scale, opacity, color, batch, projected_mean + 3 * o,                 \
       inverse_covariance + 4 * o, projected_color + 3 * o, projected_opacity + o,              \
       reinterpret_cast<int4*>(bounds) + o, counts + o)
@@ -983,13 +921,10 @@ int32_t launch_project_bwd_views(int64_t n, int32_t num_sh, int32_t num_views,
                                  float* grad_mean, float* grad_rotation, float* grad_scale,
                                  float* grad_opacity, float* grad_color, cudaStream_t stream) {
   if (n == 0) return GS_OK;
+  const unsigned blocks = ceil_div(n, 128);
   const ContiguousViews src{grad_projected, counts, n};
 #define GS_LAUNCH(K)                                                                          \
-  project_bwd_views_kernel<K, ContiguousViews>                                                \
-      <<<persistent_grid(reinterpret_cast<const void*>(                                       \
-                             project_bwd_views_kernel<K, ContiguousViews>),                   \
-                         128, ceil_div(n, 128)),                                              \
-         128, 0, stream>>>(                                                                   \
+  project_bwd_views_kernel<K, ContiguousViews><<<blocks, 128, 0, stream>>>(                   \
       n, num_views, mean, rotation, scale, opacity, color,                                    \
       static_cast<const ViewRecord*>(views), src, grad_mean, grad_rotation, grad_scale,       \
       grad_opacity, grad_color)
@@ -1011,11 +946,9 @@ int32_t launch_project_bwd_peers(int64_t n, int32_t num_sh, int32_t num_views,
     src.grad_projected[v] = grad_projected[v];
     src.counts[v] = counts[v];
   }
+  const unsigned blocks = ceil_div(n, 128);
 #define GS_LAUNCH(K)                                                                          \
-  project_bwd_views_kernel<K, PeerViews>                                                      \
-      <<<persistent_grid(reinterpret_cast<const void*>(project_bwd_views_kernel<K, PeerViews>), \
-                         128, ceil_div(n, 128)),                                              \
-         128, 0, stream>>>(                                                                   \
+  project_bwd_views_kernel<K, PeerViews><<<blocks, 128, 0, stream>>>(                         \
       n, num_views, mean, rotation, scale, opacity, color,                                    \
       static_cast<const ViewRecord*>(views), src, grad_mean, grad_rotation, grad_scale,       \
       grad_opacity, grad_color)
@@ -1032,10 +965,9 @@ int32_t launch_project_bwd(int64_t n, int32_t num_sh, const float* mean, const f
                            float* grad_rotation, float* grad_scale, float* grad_opacity,
                            float* grad_color, cudaStream_t stream) {
   if (n == 0) return GS_OK;
+  const unsigned blocks = ceil_div(n, 128);
 #define GS_LAUNCH(K)                                                                          \
-  project_bwd_kernel<K><<<persistent_grid(reinterpret_cast<const void*>(project_bwd_kernel<K>), \
-                                          128, ceil_div(n, 128)),                             \
-                          128, 0, stream>>>(                                                  \
+  project_bwd_kernel<K><<<blocks, 128, 0, stream>>>(                                          \
       n, mean, rotation, scale, opacity, color, camera_rotation, camera_translation,           \
       inverse_covariance, grad_projected, counts, p, grad_mean, grad_rotation, grad_scale,    \
       grad_opacity, grad_color)
