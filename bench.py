@@ -288,18 +288,23 @@ def kernel_durations(outputs, params, camera, grad_image, settings, device, repe
     out_nc = torch.empty_like(n_contrib)
     grad_projected = torch.empty((n, 9), device=device)
     grads = [torch.empty_like(t) for t in params] if grad_image is not None else None
+    # the compositors' records of this view (what the timed projection rewrites)
+    records = torch.empty((n, 16), device=device)
+    native.check(lib.gs_pack_records(n, P(pmean), P(conic), P(pcolor), P(popacity), pref,
+                                     P(records), stream), "gs_pack_records")
+    out_records = torch.empty_like(records)
     launches = {
         "project_fwd": lambda: lib.gs_project_fwd(
             n, k, P(mean), P(rotation), P(scale), P(opacity), P(color), P(cam_r), P(cam_t), pref,
-            P(out_pm), P(out_conic), P(out_rgb), P(out_o), P(bounds), P(out_counts), stream),
+            P(out_pm), P(out_conic), P(out_rgb), P(out_o), P(bounds), P(out_counts),
+            P(out_records), stream),
         "composite_fwd": lambda: lib.gs_composite_fwd(
-            P(pmean), P(conic), P(pcolor), P(popacity), P(ids), P(ranges), pref, P(out_img),
-            P(out_t), P(out_nc), stream),
+            P(records), P(ids), P(ranges), pref, P(out_img), P(out_t), P(out_nc), stream),
     }
     if grad_image is not None:
         launches["composite_bwd"] = lambda: lib.gs_composite_bwd(
-            n, P(pmean), P(conic), P(pcolor), P(popacity), P(ids), P(ranges), P(grad_image),
-            P(final_t), P(n_contrib), pref, P(grad_projected), stream)
+            n, P(records), P(ids), P(ranges), P(grad_image), P(final_t), P(n_contrib), pref,
+            P(grad_projected), stream)
         launches["project_bwd"] = lambda: lib.gs_project_bwd(
             n, k, P(mean), P(rotation), P(scale), P(opacity), P(color), P(cam_r), P(cam_t),
             P(conic), P(grad_projected), P(counts), pref, *(P(g) for g in grads), stream)

@@ -10,11 +10,13 @@ namespace gs {
 int32_t launch_project_fwd(int64_t, int32_t, const float*, const float*, const float*,
                            const float*, const float*, const float*, const float*,
                            const gs_params&, float*, float*, float*, float*, int32_t*, int32_t*,
-                           cudaStream_t);
+                           float*, cudaStream_t);
 int32_t launch_project_fwd_batch(int64_t, int32_t, int32_t, const float*, const float*,
                                  const float*, const float*, const float*, const float*,
                                  const float*, const gs_params*, float*, float*, float*, float*,
-                                 int32_t*, int32_t*, cudaStream_t);
+                                 int32_t*, int32_t*, float*, cudaStream_t);
+int32_t launch_pack_records(int64_t, const float*, const float*, const float*, const float*,
+                            const gs_params&, float*, cudaStream_t);
 int32_t launch_bin_count_async(int64_t, const float*, const int32_t*, void*, int64_t*, uint32_t*,
                                cudaStream_t);
 int32_t launch_project_bwd_views(int64_t, int32_t, int32_t, const float*, const float*,
@@ -33,12 +35,10 @@ int32_t launch_bin_count(int64_t, const float*, const int32_t*, void*, int64_t*,
                          cudaStream_t);
 int32_t launch_bin_sort(int64_t, int64_t, const int32_t*, const int32_t*, const gs_params&,
                         const void*, void*, int32_t*, int64_t*, cudaStream_t);
-int32_t launch_composite_fwd(const float*, const float*, const float*, const float*,
-                             const int32_t*, const int64_t*, const gs_params&, float*, float*,
-                             int32_t*, cudaStream_t);
-int32_t launch_composite_bwd(int64_t, const float*, const float*, const float*, const float*,
-                             const int32_t*, const int64_t*, const float*, const float*,
-                             const int32_t*, const gs_params&, float*, cudaStream_t);
+int32_t launch_composite_fwd(const float*, const int32_t*, const int64_t*, const gs_params&,
+                             float*, float*, int32_t*, cudaStream_t);
+int32_t launch_composite_bwd(int64_t, const float*, const int32_t*, const int64_t*, const float*,
+                             const float*, const int32_t*, const gs_params&, float*, cudaStream_t);
 int32_t launch_adam_step(int64_t, int32_t, const gs_splat_arrays&, const gs_splat_arrays&,
                          const gs_splat_arrays&, const gs_splat_arrays&, const gs_adam_params&,
                          const float*, cudaStream_t);
@@ -101,16 +101,17 @@ int32_t gs_project_fwd(int64_t n, int32_t num_sh, const float* mean, const float
                        const float* camera_rotation, const float* camera_translation,
                        const gs_params* params, float* projected_mean, float* inverse_covariance,
                        float* projected_color, float* projected_opacity, int32_t* bounds,
-                       int32_t* counts, gs_stream_t stream) {
+                       int32_t* counts, float* records, gs_stream_t stream) {
   GS_TRY(gs::check_params(params));
   if (n < 0 || n >= gs::kMaxGaussians) return GS_ERR_INVALID_ARGUMENT;
   if (!gs::valid_sh(num_sh)) return num_sh > 25 ? GS_ERR_UNSUPPORTED : GS_ERR_INVALID_ARGUMENT;
   if (!gs::aligned(rotation, 16) || !gs::aligned(inverse_covariance, 16) ||
-      !gs::aligned(bounds, 16) || ((num_sh == 4 || num_sh == 16) && !gs::aligned(color, 16)))
+      !gs::aligned(bounds, 16) || !gs::aligned(records, 16) ||
+      ((num_sh == 4 || num_sh == 16) && !gs::aligned(color, 16)))
     return GS_ERR_MISALIGNED;
   return gs::launch_project_fwd(n, num_sh, mean, rotation, scale, opacity, color, camera_rotation,
                                 camera_translation, *params, projected_mean, inverse_covariance,
-                                projected_color, projected_opacity, bounds, counts,
+                                projected_color, projected_opacity, bounds, counts, records,
                                 as_cuda(stream));
 }
 
@@ -120,20 +121,31 @@ int32_t gs_project_fwd_batch(int64_t n, int32_t num_sh, int32_t num_views, const
                              const float* camera_translations_host, const gs_params* params_host,
                              float* projected_mean, float* inverse_covariance,
                              float* projected_color, float* projected_opacity, int32_t* bounds,
-                             int32_t* counts, gs_stream_t stream) {
+                             int32_t* counts, float* records, gs_stream_t stream) {
   if (n < 0 || n >= gs::kMaxGaussians || num_views < 0) return GS_ERR_INVALID_ARGUMENT;
   if (num_views > 0 && (!camera_rotations_host || !camera_translations_host || !params_host))
     return GS_ERR_INVALID_ARGUMENT;
   for (int32_t v = 0; v < num_views; ++v) GS_TRY(gs::check_params(params_host + v));
   if (!gs::valid_sh(num_sh)) return num_sh > 25 ? GS_ERR_UNSUPPORTED : GS_ERR_INVALID_ARGUMENT;
   if (!gs::aligned(rotation, 16) || !gs::aligned(inverse_covariance, 16) ||
-      !gs::aligned(bounds, 16) || ((num_sh == 4 || num_sh == 16) && !gs::aligned(color, 16)))
+      !gs::aligned(bounds, 16) || !gs::aligned(records, 16) ||
+      ((num_sh == 4 || num_sh == 16) && !gs::aligned(color, 16)))
     return GS_ERR_MISALIGNED;
   return gs::launch_project_fwd_batch(n, num_sh, num_views, mean, rotation, scale, opacity, color,
                                       camera_rotations_host, camera_translations_host,
                                       params_host, projected_mean, inverse_covariance,
-                                      projected_color, projected_opacity, bounds, counts,
+                                      projected_color, projected_opacity, bounds, counts, records,
                                       as_cuda(stream));
+}
+
+int32_t gs_pack_records(int64_t n, const float* projected_mean, const float* inverse_covariance,
+                        const float* projected_color, const float* projected_opacity,
+                        const gs_params* params, float* records, gs_stream_t stream) {
+  GS_TRY(gs::check_params(params));
+  if (n < 0 || n >= gs::kMaxGaussians || (n > 0 && !records)) return GS_ERR_INVALID_ARGUMENT;
+  if (!gs::aligned(inverse_covariance, 16) || !gs::aligned(records, 16)) return GS_ERR_MISALIGNED;
+  return gs::launch_pack_records(n, projected_mean, inverse_covariance, projected_color,
+                                 projected_opacity, *params, records, as_cuda(stream));
 }
 
 int32_t gs_bin_count_async(int64_t n, const float* projected_mean, const int32_t* counts,
@@ -203,29 +215,24 @@ int32_t gs_bin_check(const void* count_workspace, const void* sort_workspace,
   return (words[0] | words[1]) ? GS_ERR_TIMEOUT : GS_OK;
 }
 
-int32_t gs_composite_fwd(const float* projected_mean, const float* inverse_covariance,
-                         const float* projected_color, const float* projected_opacity,
-                         const int32_t* gaussian_ids, const int64_t* ranges,
-                         const gs_params* params, float* image, float* final_transmittance,
-                         int32_t* n_contributors, gs_stream_t stream) {
+int32_t gs_composite_fwd(const float* records, const int32_t* gaussian_ids,
+                         const int64_t* ranges, const gs_params* params, float* image,
+                         float* final_transmittance, int32_t* n_contributors,
+                         gs_stream_t stream) {
   GS_TRY(gs::check_params(params));
-  if (!gs::aligned(inverse_covariance, 16)) return GS_ERR_MISALIGNED;
-  return gs::launch_composite_fwd(projected_mean, inverse_covariance, projected_color,
-                                  projected_opacity, gaussian_ids, ranges, *params, image,
+  if (!gs::aligned(records, 16)) return GS_ERR_MISALIGNED;
+  return gs::launch_composite_fwd(records, gaussian_ids, ranges, *params, image,
                                   final_transmittance, n_contributors, as_cuda(stream));
 }
 
-int32_t gs_composite_bwd(int64_t n, const float* projected_mean, const float* inverse_covariance,
-                         const float* projected_color, const float* projected_opacity,
-                         const int32_t* gaussian_ids, const int64_t* ranges,
-                         const float* grad_image, const float* final_transmittance,
-                         const int32_t* n_contributors, const gs_params* params,
-                         float* grad_projected, gs_stream_t stream) {
+int32_t gs_composite_bwd(int64_t n, const float* records, const int32_t* gaussian_ids,
+                         const int64_t* ranges, const float* grad_image,
+                         const float* final_transmittance, const int32_t* n_contributors,
+                         const gs_params* params, float* grad_projected, gs_stream_t stream) {
   GS_TRY(gs::check_params(params));
   if (n < 0) return GS_ERR_INVALID_ARGUMENT;
-  if (!gs::aligned(inverse_covariance, 16)) return GS_ERR_MISALIGNED;
-  return gs::launch_composite_bwd(n, projected_mean, inverse_covariance, projected_color,
-                                  projected_opacity, gaussian_ids, ranges, grad_image,
+  if (!gs::aligned(records, 16)) return GS_ERR_MISALIGNED;
+  return gs::launch_composite_bwd(n, records, gaussian_ids, ranges, grad_image,
                                   final_transmittance, n_contributors, *params, grad_projected,
                                   as_cuda(stream));
 }

@@ -109,4 +109,51 @@ __device__ __forceinline__ float skip_cutoff(float opacity, const gs_params& p) 
   return p.gaussian_mode ? fmaf(2.0f, det_log(opacity * 255.0f), 1e-3f) : p.cutoff;
 }
 
+// One Gaussian as the compositors stage it: 64 bytes, written once per view
+// by the projection (or gs_pack_records) and gathered per tile with four
+// 16-byte asynchronous copies. The skip cutoff and the bounding box of the
+// ellipse d2 <= 1.0201 cutoff are derived here once per Gaussian instead of
+// once per (tile, list entry).
+//   a   = (mean_x, mean_y, conic_xx, 2 conic_xy)
+//   b   = (conic_yy, opacity, skip cutoff, conic_xy)
+//   c   = (r, g, b, Gaussian index as float bits)
+//   box = (xmin, xmax, ymin, ymax) where alpha can reach 1/255: +-inf
+//         everywhere for conics whose rounding the box does not bound (condition
+//         number above ~1e3), empty when no pixel can reach 1/255.
+struct PairRecord {
+  float4 a, b, c, box;
+};
+
+__device__ __forceinline__ PairRecord make_record(int32_t g, float mx, float my, float4 conic,
+                                                  float o, float r, float gg, float b,
+                                                  const gs_params& p) {
+  const float cutoff = skip_cutoff(o, p);
+  const float xx = conic.x, xy = conic.y, yy = conic.w;
+  const float det = xx * yy - xy * xy;
+  const float inf = __int_as_float(0x7f800000);
+  float4 box = make_float4(-inf, inf, -inf, inf);
+  if (!(cutoff >= 0.0f)) {
+    box = make_float4(inf, -inf, inf, -inf);  // no pixel can reach alpha >= 1/255
+  } else if (xx > 0.0f && yy > 0.0f && det > 0.0f && (xx + yy) * (xx + yy) < 4.0e3f * det) {
+    const float scaled = 1.0201f * cutoff / det;
+    const float hx = sqrtf(scaled * yy) * 1.001f + 0.01f;
+    const float hy = sqrtf(scaled * xx) * 1.001f + 0.01f;
+    box = make_float4(mx - hx, mx + hx, my - hy, my + hy);
+  }
+  PairRecord rec;
+  rec.a = make_float4(mx, my, xx, 2.0f * xy);
+  rec.b = make_float4(yy, o, cutoff, xy);
+  rec.c = make_float4(r, gg, b, __int_as_float(g));
+  rec.box = box;
+  return rec;
+}
+
+__device__ __forceinline__ void store_record(float4* records, int64_t g, const PairRecord& rec) {
+  float4* dst = records + 4 * g;
+  dst[0] = rec.a;
+  dst[1] = rec.b;
+  dst[2] = rec.c;
+  dst[3] = rec.box;
+}
+
 }  // namespace gs

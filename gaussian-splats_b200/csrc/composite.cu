@@ -1,9 +1,12 @@
 // Per-tile alpha compositing, forward and backward.
 //
 // One CTA per tile. The tile's list of Gaussians -- ids[start:end), front to
-// back -- is staged into shared memory 256 entries at a time (a gather of the
-// projected mean, conic, opacity and colour, plus two derived values), and
-// every pixel walks the batch from shared memory. Each warp owns a compact
+// back -- is staged into shared memory a batch of entries at a time: each
+// entry's 64-byte record (projected mean, conic, opacity, colour, skip cutoff
+// and box, built once per Gaussian by the projection) arrives by four 16-byte
+// asynchronous copies (cp.async, L2 only), double-buffered, so the records of
+// batch k+1 are in flight while batch k is composited and each batch costs one
+// CTA barrier. Every pixel walks the batch from shared memory. Each warp owns a compact
 // block of pixels: in the forward one pixel per thread and an 8 x 4 block
 // (4 x 4 tiles: one 4 x 4 block); in the backward, for 8 x 8 and larger
 // tiles, two pixels per thread (one column, four rows apart) and an 8 x 8
@@ -100,68 +103,34 @@ struct PixelMap {
   }
 };
 
-// One list entry as staged in shared memory.
-struct Staged {
-  float4 a;    // mean_x, mean_y, conic_xx, 2 conic_xy
-  float4 b;    // conic_yy, opacity, skip cutoff, conic_xy
-  float4 c;    // r, g, b, gaussian id (bits)
-  float4 box;  // xmin, xmax, ymin, ymax of the ellipse where alpha can reach 1/255
+// One buffer of staged list entries: the four float4 of each entry's record
+// in separate arrays, so lanes reading consecutive entries' boxes hit
+// distinct banks.
+template <int NB>
+struct StageBuffer {
+  float4 a[NB], b[NB], c[NB], box[NB];
 };
 
-__device__ __forceinline__ Staged stage_entry(int32_t g, const float* __restrict__ projected_mean,
-                                              const float* __restrict__ inverse_covariance,
-                                              const float* __restrict__ projected_color,
-                                              const float* __restrict__ projected_opacity,
-                                              const gs_params& p) {
-  const int64_t g3 = 3 * static_cast<int64_t>(g);
-  const float mx = __ldg(projected_mean + g3), my = __ldg(projected_mean + g3 + 1);
-  const float4 conic = __ldg(reinterpret_cast<const float4*>(inverse_covariance) + g);
-  const float o = __ldg(projected_opacity + g);
-  const float r = __ldg(projected_color + g3), gg = __ldg(projected_color + g3 + 1),
-              b = __ldg(projected_color + g3 + 2);
-  const float cutoff = skip_cutoff(o, p);
-  const float xx = conic.x, xy = conic.y, yy = conic.w;
-  const float det = xx * yy - xy * xy;
-  const float inf = __int_as_float(0x7f800000);
-  float4 box = make_float4(-inf, inf, -inf, inf);
-  if (!(cutoff >= 0.0f)) {
-    box = make_float4(inf, -inf, inf, -inf);  // no pixel can reach alpha >= 1/255
-  } else if (xx > 0.0f && yy > 0.0f && det > 0.0f && (xx + yy) * (xx + yy) < 4.0e3f * det) {
-    const float scaled = 1.0201f * cutoff / det;
-    const float hx = sqrtf(scaled * yy) * 1.001f + 0.01f;
-    const float hy = sqrtf(scaled * xx) * 1.001f + 0.01f;
-    box = make_float4(mx - hx, mx + hx, my - hy, my + hy);
-  }
-  Staged s;
-  s.a = make_float4(mx, my, xx, 2.0f * xy);
-  s.b = make_float4(yy, o, cutoff, xy);
-  s.c = make_float4(r, gg, b, __int_as_float(g));
-  s.box = box;
-  return s;
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const uint32_t dst = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
 }
 
-// Stages list entries [first, last) into the batch slots 0..last-first-1.
-template <int TS, int PPT>
-__device__ __forceinline__ void stage_batch(int64_t first, int64_t last,
-                                            const int32_t* __restrict__ gaussian_ids,
-                                            const float* __restrict__ projected_mean,
-                                            const float* __restrict__ inverse_covariance,
-                                            const float* __restrict__ projected_color,
-                                            const float* __restrict__ projected_opacity,
-                                            const gs_params& p, float4* s_a, float4* s_b,
-                                            float4* s_c, float4* s_box) {
-  using S = TileShape<TS, PPT>;
-  for (int slot = threadIdx.x; slot < S::kBatch; slot += S::kThreads) {
-    const int64_t k = first + slot;
-    if (k < last) {
-      const Staged st = stage_entry(__ldg(gaussian_ids + k), projected_mean, inverse_covariance,
-                                    projected_color, projected_opacity, p);
-      s_a[slot] = st.a;
-      s_b[slot] = st.b;
-      s_c[slot] = st.c;
-      s_box[slot] = st.box;
-    }
-  }
+// Starts copying Gaussian g's record into `slot` of `buf`.
+template <int NB>
+__device__ __forceinline__ void stage_async(const float4* __restrict__ records, int32_t g,
+                                            StageBuffer<NB>& buf, int slot) {
+  const float4* src = records + 4 * static_cast<int64_t>(g);
+  cp_async16(&buf.a[slot], src);
+  cp_async16(&buf.b[slot], src + 1);
+  cp_async16(&buf.c[slot], src + 2);
+  cp_async16(&buf.box[slot], src + 3);
 }
 
 // True unless the ellipse d2 <= 1.0201 cutoff provably misses the rectangle
@@ -197,21 +166,20 @@ __device__ __forceinline__ bool ellipse_meets_rect(const float4& a, const float4
 // many. One ballot per 32 entries replaces a per-entry test inside the pixel
 // loop. The exact test pays in the backward, where every selected entry costs
 // a warp reduction and atomics; in the forward it costs more than it saves.
-template <int TS, int PPT, bool kExact>
-__device__ __forceinline__ int warp_select(const PixelMap<TS, PPT>& pm, const float4* s_a,
-                                           const float4* s_b, const float4* s_box, int count,
-                                           int lane, uint16_t* list, int64_t position0,
-                                           int64_t limit) {
+template <int TS, int PPT, bool kExact, int NB>
+__device__ __forceinline__ int warp_select(const PixelMap<TS, PPT>& pm, const StageBuffer<NB>& buf,
+                                           int count, int lane, uint16_t* list,
+                                           int64_t position0, int64_t limit) {
   using S = TileShape<TS, PPT>;
   int selected = 0;
   for (int base = 0; base < count; base += S::kWarpLanes) {
     const int j = base + lane;
     bool hit = false;
     if (j < count) {
-      const float4 box = s_box[j];
+      const float4 box = buf.box[j];
       hit = !pm.misses(box);
       if (kExact && hit)
-        hit = ellipse_meets_rect(s_a[j], s_b[j], box, pm.rx0, pm.rx1, pm.ry0, pm.ry1);
+        hit = ellipse_meets_rect(buf.a[j], buf.b[j], box, pm.rx0, pm.rx1, pm.ry0, pm.ry1);
     }
     if (limit >= 0) hit = hit && position0 + j < limit;
     const unsigned mask = __ballot_sync(S::kWarpMask, hit);
@@ -225,19 +193,15 @@ __device__ __forceinline__ int warp_select(const PixelMap<TS, PPT>& pm, const fl
 template <int TS, bool kGaussian>
 __global__ void __launch_bounds__(TileShape<TS, 1>::kThreads,
                                   forward_min_blocks(TileShape<TS, 1>::kThreads))
-    composite_fwd_kernel(
-    const float* __restrict__ projected_mean, const float* __restrict__ inverse_covariance,
-    const float* __restrict__ projected_color, const float* __restrict__ projected_opacity,
-    const int32_t* __restrict__ gaussian_ids, const int64_t* __restrict__ ranges,
-    const gs_params p, float* __restrict__ image, float* __restrict__ final_transmittance,
-    int32_t* __restrict__ n_contributors) {
+    composite_fwd_kernel(const float4* __restrict__ records,
+                         const int32_t* __restrict__ gaussian_ids,
+                         const int64_t* __restrict__ ranges, const gs_params p,
+                         float* __restrict__ image, float* __restrict__ final_transmittance,
+                         int32_t* __restrict__ n_contributors) {
   using S = TileShape<TS, 1>;
   constexpr int NB = S::kBatch;
   constexpr int kWarps = S::kWarps;
-  __shared__ float4 s_a[NB];
-  __shared__ float4 s_b[NB];
-  __shared__ float4 s_c[NB];
-  __shared__ float4 s_box[NB];
+  __shared__ StageBuffer<NB> s_buf[2];
   __shared__ uint16_t s_list[kWarps][NB];
   const int tile = blockIdx.x;
   const int tid = threadIdx.x;
@@ -248,28 +212,38 @@ __global__ void __launch_bounds__(TileShape<TS, 1>::kThreads,
   const float threshold = p.opacity_threshold;
   uint16_t* list = s_list[warp];
 
+  // Thread tid stages entry tid of every batch; the id of its next batch's
+  // entry is loaded one batch ahead, so issuing a batch's copies never waits.
+  int32_t next_id = 0;
+  if (tid < NB) {
+    if (start + tid < end) stage_async(records, __ldg(gaussian_ids + start + tid), s_buf[0], tid);
+    if (start + NB + tid < end) next_id = __ldg(gaussian_ids + start + NB + tid);
+  }
+  cp_async_commit();
+  cp_async_wait_all();
+  __syncthreads();
+
   float T = 1.0f, cr = 0.0f, cg = 0.0f, cb = 0.0f;
   bool done = !((1.0f - T) < threshold);
   int64_t contrib = 0;
-  for (int64_t batch = start; batch < end; batch += NB) {
-    const int64_t k = batch + tid;
-    if (tid < NB && k < end) {
-      const Staged s = stage_entry(__ldg(gaussian_ids + k), projected_mean, inverse_covariance,
-                                   projected_color, projected_opacity, p);
-      s_a[tid] = s.a;
-      s_b[tid] = s.b;
-      s_c[tid] = s.c;
-      s_box[tid] = s.box;
+  int buf = 0;
+  for (int64_t batch = start; batch < end; batch += NB, buf ^= 1) {
+    // The next batch's records fill the other buffer while this one is used.
+    const int64_t next = batch + NB;
+    if (tid < NB && next + tid < end) {
+      stage_async(records, next_id, s_buf[buf ^ 1], tid);
+      if (next + NB + tid < end) next_id = __ldg(gaussian_ids + next + NB + tid);
     }
-    __syncthreads();
+    cp_async_commit();
+    const StageBuffer<NB>& cur = s_buf[buf];
     if (__any_sync(S::kWarpMask, !done)) {
       const int count = static_cast<int>(end - batch < NB ? end - batch : NB);
-      const int selected = warp_select<TS, 1, false>(pm, s_a, s_b, s_box, count, lane, list, 0, -1);
+      const int selected = warp_select<TS, 1, false>(pm, cur, count, lane, list, 0, -1);
       if (!done) {
         for (int i = 0; i < selected; ++i) {
           const int j = list[i];
-          const float4 a = s_a[j];
-          const float4 b = s_b[j];
+          const float4 a = cur.a[j];
+          const float4 b = cur.b[j];
           const float dx = fpx - a.x, dy = fpy - a.y;
           const float d2 = pair_d2(dx, dy, a.z, a.w, b.x);
           if (!(d2 <= b.z)) continue;
@@ -281,7 +255,7 @@ __global__ void __launch_bounds__(TileShape<TS, 1>::kThreads,
             alpha = fminf(b.y, kAlphaMax);
           }
           if (!(alpha >= kAlphaMin)) continue;
-          const float4 c = s_c[j];
+          const float4 c = cur.c[j];
           const float weight = T * alpha;
           cr = fmaf(weight, c.x, cr);
           cg = fmaf(weight, c.y, cg);
@@ -295,6 +269,9 @@ __global__ void __launch_bounds__(TileShape<TS, 1>::kThreads,
         }
       }
     }
+    // This thread's copies of the next batch have landed; the barrier makes
+    // every thread's visible and frees the current buffer for refilling.
+    cp_async_wait_all();
     if (__syncthreads_count(!done) == 0) break;
   }
   if (!done) contrib = end - start;
@@ -336,24 +313,29 @@ __device__ __forceinline__ void warp_reduce_scatter9(const float (&v)[9], int la
   for (int o = 16; o > 0; o >>= 1) last += __shfl_xor_sync(0xffffffffu, last, o);
 }
 
+// List entries per staging batch of the backward: double-buffered records
+// of 128 entries keep the CTA's shared memory within the eight CTAs per SM
+// its register bound allows.
+template <int TS, int PPT>
+struct BackwardBatch {
+  static constexpr int value = TileShape<TS, PPT>::kBatch < 128 ? TileShape<TS, PPT>::kBatch : 128;
+};
+
 template <int TS, int PPT, bool kGaussian>
 __global__ void __launch_bounds__(TileShape<TS, PPT>::kThreads,
                                   min_blocks_for_32_warps(TileShape<TS, PPT>::kThreads))
-    composite_bwd_kernel(
-    const float* __restrict__ projected_mean, const float* __restrict__ inverse_covariance,
-    const float* __restrict__ projected_color, const float* __restrict__ projected_opacity,
-    const int32_t* __restrict__ gaussian_ids, const int64_t* __restrict__ ranges,
-    const float* __restrict__ grad_image, const float* __restrict__ final_transmittance,
-    const int32_t* __restrict__ n_contributors, const gs_params p,
-    float* __restrict__ grad_projected) {
+    composite_bwd_kernel(const float4* __restrict__ records,
+                         const int32_t* __restrict__ gaussian_ids,
+                         const int64_t* __restrict__ ranges, const float* __restrict__ grad_image,
+                         const float* __restrict__ final_transmittance,
+                         const int32_t* __restrict__ n_contributors, const gs_params p,
+                         float* __restrict__ grad_projected) {
   using S = TileShape<TS, PPT>;
-  constexpr int NB = S::kBatch;
+  constexpr int NB = BackwardBatch<TS, PPT>::value;
   constexpr int Q = S::kPpt;
+  constexpr int kStage = (NB + S::kThreads - 1) / S::kThreads;  // entries staged per thread
   constexpr unsigned kMask = S::kWarpMask;
-  __shared__ float4 s_a[NB];
-  __shared__ float4 s_b[NB];
-  __shared__ float4 s_c[NB];
-  __shared__ float4 s_box[NB];
+  __shared__ StageBuffer<NB> s_buf[2];
   __shared__ uint16_t s_list[S::kWarps][NB];
   __shared__ int s_max_contrib;
   const int tile = blockIdx.x;
@@ -385,6 +367,25 @@ __global__ void __launch_bounds__(TileShape<TS, PPT>::kThreads,
   int64_t end = ranges[2 * tile + 1];
   if (end > start + s_max_contrib) end = start + s_max_contrib;  // composite_bwd.py:81-83
 
+  // Batches walk back to front: [max(start, batch_end - NB), batch_end). Slot
+  // tid + s * kThreads of each batch is this thread's to stage; the ids of its
+  // next batch's slots are loaded one batch ahead.
+  int32_t next_id[kStage];
+  {
+    const int64_t first = end - NB > start ? end - NB : start;
+#pragma unroll
+    for (int s = 0; s < kStage; ++s) {
+      const int slot = tid + s * S::kThreads;
+      if (slot < NB && first + slot < end)
+        stage_async(records, __ldg(gaussian_ids + first + slot), s_buf[0], slot);
+      const int64_t first2 = first - NB > start ? first - NB : start;
+      next_id[s] = slot < NB && first2 + slot < first ? __ldg(gaussian_ids + first2 + slot) : 0;
+    }
+  }
+  cp_async_commit();
+  cp_async_wait_all();
+  __syncthreads();
+
   uint16_t* list = s_list[warp];
   float st[Q], sr[Q], sg[Q], sb[Q];  // suffix behind the current entry
 #pragma unroll
@@ -392,14 +393,28 @@ __global__ void __launch_bounds__(TileShape<TS, PPT>::kThreads,
     st[q] = 1.0f;
     sr[q] = sg[q] = sb[q] = 0.0f;
   }
-  for (int64_t batch_end = end; batch_end > start; batch_end -= NB) {
+  int buf = 0;
+  for (int64_t batch_end = end; batch_end > start; batch_end -= NB, buf ^= 1) {
     const int64_t batch_start = batch_end - NB > start ? batch_end - NB : start;
-    stage_batch<TS, PPT>(batch_start, batch_end, gaussian_ids, projected_mean, inverse_covariance,
-                    projected_color, projected_opacity, p, s_a, s_b, s_c, s_box);
-    __syncthreads();
+    // the next (earlier) batch's records fill the other buffer meanwhile
+    if (batch_start > start) {
+      const int64_t next_start = batch_start - NB > start ? batch_start - NB : start;
+      const int64_t after_start = next_start - NB > start ? next_start - NB : start;
+#pragma unroll
+      for (int s = 0; s < kStage; ++s) {
+        const int slot = tid + s * S::kThreads;
+        if (slot < NB && next_start + slot < batch_start) {
+          stage_async(records, next_id[s], s_buf[buf ^ 1], slot);
+          if (after_start + slot < next_start)
+            next_id[s] = __ldg(gaussian_ids + after_start + slot);
+        }
+      }
+    }
+    cp_async_commit();
+    const StageBuffer<NB>& cur = s_buf[buf];
     const int count = static_cast<int>(batch_end - batch_start);
-    const int selected = warp_select<TS, PPT, true>(pm, s_a, s_b, s_box, count, lane, list, batch_start - start,
-                                         warp_max_contrib);
+    const int selected = warp_select<TS, PPT, true>(pm, cur, count, lane, list,
+                                                    batch_start - start, warp_max_contrib);
     for (int i = selected - 1; i >= 0; --i) {
       const int j = list[i];
       const int64_t position = batch_start + j - start;
@@ -407,8 +422,8 @@ __global__ void __launch_bounds__(TileShape<TS, PPT>::kThreads,
 #pragma unroll
       for (int k = 0; k < 9; ++k) v[k] = 0.0f;
       bool active = false;
-      const float4 a = s_a[j];
-      const float4 b = s_b[j];
+      const float4 a = cur.a[j];
+      const float4 b = cur.b[j];
       const float dx = fpx - a.x;
       const float xx = a.z, xy = b.w, yy = b.x, o = b.y;
       const float adx = xx * dx, bdx = a.w * dx;
@@ -428,7 +443,7 @@ __global__ void __launch_bounds__(TileShape<TS, PPT>::kThreads,
         const float alpha = fminf(alpha_raw, kAlphaMax);
         if (!(alpha >= kAlphaMin)) continue;
         active = true;
-        const float4 c = s_c[j];
+        const float4 c = cur.c[j];
         const float denominator = fmaxf(st[q] * (1.0f - alpha), 1e-4f);
         const float forward = t_final[q] / denominator;
         const bool still = (1.0f - forward) < threshold;
@@ -460,7 +475,7 @@ __global__ void __launch_bounds__(TileShape<TS, PPT>::kThreads,
         st[q] = st[q] * local_t;
       }
       if (__any_sync(kMask, active)) {
-        const int g = __float_as_int(s_c[j].w);
+        const int g = __float_as_int(cur.c[j].w);
         float* dst = grad_projected + 9 * static_cast<int64_t>(g);
         if constexpr (S::kWarpLanes == 32) {
           float mine, last;
@@ -481,6 +496,7 @@ __global__ void __launch_bounds__(TileShape<TS, PPT>::kThreads,
         }
       }
     }
+    cp_async_wait_all();
     __syncthreads();
   }
 }
@@ -507,31 +523,56 @@ struct BwdPpt {
     default: return GS_ERR_INVALID_ARGUMENT; \
   }
 
-int32_t launch_composite_fwd(const float* projected_mean, const float* inverse_covariance,
-                             const float* projected_color, const float* projected_opacity,
-                             const int32_t* gaussian_ids, const int64_t* ranges,
-                             const gs_params& p, float* image, float* final_transmittance,
-                             int32_t* n_contributors, cudaStream_t stream) {
+// Records [n, 4] float4 of the projected Gaussians (the compositors' staged
+// form), from the four projected arrays: for callers that have only the
+// operator's outputs.
+__global__ void __launch_bounds__(256) pack_records_kernel(
+    int64_t n, const float* __restrict__ projected_mean,
+    const float* __restrict__ inverse_covariance, const float* __restrict__ projected_color,
+    const float* __restrict__ projected_opacity, const gs_params p, float4* __restrict__ records) {
+  const int64_t g = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (g >= n) return;
+  const float4 conic = __ldg(reinterpret_cast<const float4*>(inverse_covariance) + g);
+  store_record(records, g,
+               make_record(static_cast<int32_t>(g), __ldg(projected_mean + 3 * g),
+                           __ldg(projected_mean + 3 * g + 1), conic,
+                           __ldg(projected_opacity + g), __ldg(projected_color + 3 * g),
+                           __ldg(projected_color + 3 * g + 1), __ldg(projected_color + 3 * g + 2),
+                           p));
+}
+
+int32_t launch_pack_records(int64_t n, const float* projected_mean,
+                            const float* inverse_covariance, const float* projected_color,
+                            const float* projected_opacity, const gs_params& p, float* records,
+                            cudaStream_t stream) {
+  if (n == 0) return GS_OK;
+  pack_records_kernel<<<ceil_div(n, 256), 256, 0, stream>>>(
+      n, projected_mean, inverse_covariance, projected_color, projected_opacity, p,
+      reinterpret_cast<float4*>(records));
+  return check_launch();
+}
+
+int32_t launch_composite_fwd(const float* records, const int32_t* gaussian_ids,
+                             const int64_t* ranges, const gs_params& p, float* image,
+                             float* final_transmittance, int32_t* n_contributors,
+                             cudaStream_t stream) {
   const int64_t num_tiles =
       static_cast<int64_t>(p.width / p.tile_size) * (p.height / p.tile_size);
   if (num_tiles == 0) return GS_OK;
+  const float4* rec = reinterpret_cast<const float4*>(records);
 #define GS_LAUNCH(TS)                                                                          \
   if (p.gaussian_mode)                                                                         \
     composite_fwd_kernel<TS, true><<<static_cast<unsigned>(num_tiles), TS * TS, 0, stream>>>(  \
-        projected_mean, inverse_covariance, projected_color, projected_opacity, gaussian_ids,  \
-        ranges, p, image, final_transmittance, n_contributors);                                \
+        rec, gaussian_ids, ranges, p, image, final_transmittance, n_contributors);             \
   else                                                                                         \
     composite_fwd_kernel<TS, false><<<static_cast<unsigned>(num_tiles), TS * TS, 0, stream>>>( \
-        projected_mean, inverse_covariance, projected_color, projected_opacity, gaussian_ids,  \
-        ranges, p, image, final_transmittance, n_contributors)
+        rec, gaussian_ids, ranges, p, image, final_transmittance, n_contributors)
   GS_TILE_DISPATCH(p.tile_size, GS_LAUNCH)
 #undef GS_LAUNCH
   return check_launch();
 }
 
-int32_t launch_composite_bwd(int64_t n, const float* projected_mean,
-                             const float* inverse_covariance, const float* projected_color,
-                             const float* projected_opacity, const int32_t* gaussian_ids,
+int32_t launch_composite_bwd(int64_t n, const float* records, const int32_t* gaussian_ids,
                              const int64_t* ranges, const float* grad_image,
                              const float* final_transmittance, const int32_t* n_contributors,
                              const gs_params& p, float* grad_projected, cudaStream_t stream) {
@@ -539,19 +580,18 @@ int32_t launch_composite_bwd(int64_t n, const float* projected_mean,
   const int64_t num_tiles =
       static_cast<int64_t>(p.width / p.tile_size) * (p.height / p.tile_size);
   if (num_tiles == 0 || n == 0) return GS_OK;
+  const float4* rec = reinterpret_cast<const float4*>(records);
 #define GS_LAUNCH(TS)                                                                          \
   if (p.gaussian_mode)                                                                         \
     composite_bwd_kernel<TS, BwdPpt<TS>::value, true>                                          \
         <<<static_cast<unsigned>(num_tiles), TileShape<TS, BwdPpt<TS>::value>::kThreads, 0,   \
-           stream>>>(projected_mean, inverse_covariance, projected_color, projected_opacity,   \
-                     gaussian_ids, ranges, grad_image, final_transmittance, n_contributors, p, \
-                     grad_projected);                                                          \
+           stream>>>(rec, gaussian_ids, ranges, grad_image, final_transmittance,               \
+                     n_contributors, p, grad_projected);                                       \
   else                                                                                         \
     composite_bwd_kernel<TS, BwdPpt<TS>::value, false>                                         \
         <<<static_cast<unsigned>(num_tiles), TileShape<TS, BwdPpt<TS>::value>::kThreads, 0,   \
-           stream>>>(projected_mean, inverse_covariance, projected_color, projected_opacity,   \
-                     gaussian_ids, ranges, grad_image, final_transmittance, n_contributors, p, \
-                     grad_projected)
+           stream>>>(rec, gaussian_ids, ranges, grad_image, final_transmittance,               \
+                     n_contributors, p, grad_projected)
   GS_TILE_DISPATCH(p.tile_size, GS_LAUNCH)
 #undef GS_LAUNCH
   return check_launch();

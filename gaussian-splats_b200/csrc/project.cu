@@ -132,7 +132,7 @@ __device__ __forceinline__ void project_view(
     int64_t i, const GaussianTerms& g, const float* __restrict__ sh_row, const Camera& c,
     const gs_params& p, float* __restrict__ projected_mean, float* __restrict__ inverse_covariance,
     float* __restrict__ projected_color, float* __restrict__ projected_opacity,
-    int4* __restrict__ bounds, int32_t* __restrict__ counts) {
+    int4* __restrict__ bounds, int32_t* __restrict__ counts, float4* __restrict__ records) {
   const float mx = g.mx, my = g.my, mz = g.mz;
   // project.py:126-142
   const float camera_x = mx * c.r00 + my * c.r01 + mz * c.r02 + c.tx;
@@ -169,8 +169,8 @@ __device__ __forceinline__ void project_view(
   const float cov11 = f10 * f10 + f11 * f11 + f12 * f12 + 0.03f;
   const float determinant = cov00 * cov11 - cov01 * cov01;
   const float conic_xy = -cov01 / determinant;
-  reinterpret_cast<float4*>(inverse_covariance)[i] =
-      make_float4(cov11 / determinant, conic_xy, conic_xy, cov00 / determinant);
+  const float4 conic = make_float4(cov11 / determinant, conic_xy, conic_xy, cov00 / determinant);
+  reinterpret_cast<float4*>(inverse_covariance)[i] = conic;
   // project.py:221-228, _evaluate_sh (project.py:10-71)
   float dx = mx + c.r00 * c.tx + c.r10 * c.ty + c.r20 * c.tz;
   float dy = my + c.r01 * c.tx + c.r11 * c.ty + c.r21 * c.tz;
@@ -188,9 +188,11 @@ __device__ __forceinline__ void project_view(
     acc_g = fmaf(coefficients[3 * k + 1], b, acc_g);
     acc_b = fmaf(coefficients[3 * k + 2], b, acc_b);
   }
-  projected_color[3 * i] = fmaxf(acc_r + 0.5f, 0.0f);
-  projected_color[3 * i + 1] = fmaxf(acc_g + 0.5f, 0.0f);
-  projected_color[3 * i + 2] = fmaxf(acc_b + 0.5f, 0.0f);
+  const float red = fmaxf(acc_r + 0.5f, 0.0f), green = fmaxf(acc_g + 0.5f, 0.0f),
+              blue = fmaxf(acc_b + 0.5f, 0.0f);
+  projected_color[3 * i] = red;
+  projected_color[3 * i + 1] = green;
+  projected_color[3 * i + 2] = blue;
   // project.py:230-253
   projected_opacity[i] = g.o;
   const float radius_extent = p.gaussian_mode ? g.gaussian_extent : p.extent;
@@ -207,7 +209,13 @@ __device__ __forceinline__ void project_view(
   bounds[i] = make_int4(static_cast<int>(tmin_x), static_cast<int>(tmax_x),
                         static_cast<int>(tmin_y), static_cast<int>(tmax_y));
   const float count = (tmax_x - tmin_x) * (tmax_y - tmin_y);
-  counts[i] = (safe_z > p.near_plane && safe_z < p.far_plane) ? static_cast<int32_t>(count) : 0;
+  const int32_t visible_count =
+      (safe_z > p.near_plane && safe_z < p.far_plane) ? static_cast<int32_t>(count) : 0;
+  counts[i] = visible_count;
+  // the compositors' staged form; Gaussians in no tile are never staged
+  if (records != nullptr && visible_count > 0)
+    store_record(records, i, make_record(static_cast<int32_t>(i), pixel_x, pixel_y, conic, g.o,
+                                         red, green, blue, p));
 }
 
 template <int K>
@@ -218,7 +226,7 @@ __global__ void __launch_bounds__(256) project_fwd_kernel(
     const float* __restrict__ camera_translation, const gs_params p,
     float* __restrict__ projected_mean, float* __restrict__ inverse_covariance,
     float* __restrict__ projected_color, float* __restrict__ projected_opacity,
-    int4* __restrict__ bounds, int32_t* __restrict__ counts) {
+    int4* __restrict__ bounds, int32_t* __restrict__ counts, float4* __restrict__ records) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= n) return;
   if (threadIdx.x == 0) {
@@ -279,8 +287,8 @@ __global__ void __launch_bounds__(256) project_fwd_kernel(
   const float cov11 = f10 * f10 + f11 * f11 + f12 * f12 + 0.03f;
   const float determinant = cov00 * cov11 - cov01 * cov01;
   const float conic_xy = -cov01 / determinant;
-  reinterpret_cast<float4*>(inverse_covariance)[i] =
-      make_float4(cov11 / determinant, conic_xy, conic_xy, cov00 / determinant);
+  const float4 conic = make_float4(cov11 / determinant, conic_xy, conic_xy, cov00 / determinant);
+  reinterpret_cast<float4*>(inverse_covariance)[i] = conic;
   // project.py:221-228, _evaluate_sh (project.py:10-71)
   float dx = mx + c.r00 * c.tx + c.r10 * c.ty + c.r20 * c.tz;
   float dy = my + c.r01 * c.tx + c.r11 * c.ty + c.r21 * c.tz;
@@ -298,9 +306,11 @@ __global__ void __launch_bounds__(256) project_fwd_kernel(
     acc_g = fmaf(coefficients[3 * k + 1], b, acc_g);
     acc_b = fmaf(coefficients[3 * k + 2], b, acc_b);
   }
-  projected_color[3 * i] = fmaxf(acc_r + 0.5f, 0.0f);
-  projected_color[3 * i + 1] = fmaxf(acc_g + 0.5f, 0.0f);
-  projected_color[3 * i + 2] = fmaxf(acc_b + 0.5f, 0.0f);
+  const float red = fmaxf(acc_r + 0.5f, 0.0f), green = fmaxf(acc_g + 0.5f, 0.0f),
+              blue = fmaxf(acc_b + 0.5f, 0.0f);
+  projected_color[3 * i] = red;
+  projected_color[3 * i + 1] = green;
+  projected_color[3 * i + 2] = blue;
   // project.py:230-253
   const float o = det_sigmoid(__ldg(opacity + i));
   projected_opacity[i] = o;
@@ -318,7 +328,13 @@ __global__ void __launch_bounds__(256) project_fwd_kernel(
   bounds[i] = make_int4(static_cast<int>(tmin_x), static_cast<int>(tmax_x),
                         static_cast<int>(tmin_y), static_cast<int>(tmax_y));
   const float count = (tmax_x - tmin_x) * (tmax_y - tmin_y);
-  counts[i] = (safe_z > p.near_plane && safe_z < p.far_plane) ? static_cast<int32_t>(count) : 0;
+  const int32_t visible_count =
+      (safe_z > p.near_plane && safe_z < p.far_plane) ? static_cast<int32_t>(count) : 0;
+  counts[i] = visible_count;
+  // the compositors' staged form; Gaussians in no tile are never staged
+  if (records != nullptr && visible_count > 0)
+    store_record(records, i, make_record(static_cast<int32_t>(i), pixel_x, pixel_y, conic, o,
+                                         red, green, blue, p));
 }
 
 // One view's conic as the forward computes it (project.py:126-142,158-218):
@@ -374,7 +390,7 @@ __global__ void __launch_bounds__(256) project_fwd_batch_kernel(
     const float* __restrict__ color, const __grid_constant__ ViewBatch batch,
     float* __restrict__ projected_mean, float* __restrict__ inverse_covariance,
     float* __restrict__ projected_color, float* __restrict__ projected_opacity,
-    int4* __restrict__ bounds, int32_t* __restrict__ counts) {
+    int4* __restrict__ bounds, int32_t* __restrict__ counts, float4* __restrict__ records) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= n) return;
   if (threadIdx.x == 0) {
@@ -387,7 +403,7 @@ __global__ void __launch_bounds__(256) project_fwd_batch_kernel(
     const int64_t o = static_cast<int64_t>(b) * n;
     project_view<K>(i, g, color + i * (K * 3), batch.c[b], batch.p[b], projected_mean + 3 * o,
                     inverse_covariance + 4 * o, projected_color + 3 * o, projected_opacity + o,
-                    bounds + o, counts + o);
+                    bounds + o, counts + o, records ? records + 4 * o : nullptr);
   }
 }
 
@@ -869,14 +885,14 @@ int32_t launch_project_fwd(int64_t n, int32_t num_sh, const float* mean, const f
                            const float* camera_rotation, const float* camera_translation,
                            const gs_params& p, float* projected_mean, float* inverse_covariance,
                            float* projected_color, float* projected_opacity, int32_t* bounds,
-                           int32_t* counts, cudaStream_t stream) {
+                           int32_t* counts, float* records, cudaStream_t stream) {
   if (n == 0) return GS_OK;
   const unsigned blocks = ceil_div(n, 256);
 #define GS_LAUNCH(K)                                                                          \
   project_fwd_kernel<K><<<blocks, 256, 0, stream>>>(                                          \
       n, mean, rotation, scale, opacity, color, camera_rotation, camera_translation, p,       \
       projected_mean, inverse_covariance, projected_color, projected_opacity,                 \
-      reinterpret_cast<int4*>(bounds), counts)
+      reinterpret_cast<int4*>(bounds), counts, reinterpret_cast<float4*>(records))
   GS_SH_DISPATCH(num_sh, GS_LAUNCH)
 #undef GS_LAUNCH
   return check_launch();
@@ -889,7 +905,7 @@ int32_t launch_project_fwd_batch(int64_t n, int32_t num_sh, int32_t num_views, c
                                  const gs_params* params_host, float* projected_mean,
                                  float* inverse_covariance, float* projected_color,
                                  float* projected_opacity, int32_t* bounds, int32_t* counts,
-                                 cudaStream_t stream) {
+                                 float* records, cudaStream_t stream) {
   if (n == 0 || num_views == 0) return GS_OK;
   const unsigned blocks = ceil_div(n, 256);
   for (int first = 0; first < num_views; first += kMaxBatchViews) {
@@ -906,7 +922,8 @@ int32_t launch_project_fwd_batch(int64_t n, int32_t num_sh, int32_t num_views, c
   project_fwd_batch_kernel<K><<<blocks, 256, 0, stream>>>(                                    \
       n, mean, rotation, scale, opacity, color, batch, projected_mean + 3 * o,                 \
       inverse_covariance + 4 * o, projected_color + 3 * o, projected_opacity + o,              \
-      reinterpret_cast<int4*>(bounds) + o, counts + o)
+      reinterpret_cast<int4*>(bounds) + o, counts + o,                                        \
+      records ? reinterpret_cast<float4*>(records) + 4 * o : nullptr)
     GS_SH_DISPATCH(num_sh, GS_LAUNCH)
 #undef GS_LAUNCH
     GS_TRY(check_launch());

@@ -30,6 +30,7 @@ EXPORTED_SYMBOLS = (
     "gs_last_cuda_error",
     "gs_project_fwd",
     "gs_project_fwd_batch",
+    "gs_pack_records",
     "gs_bin_count",
     "gs_bin_count_async",
     "gs_bin_count_workspace_size",
@@ -210,8 +211,9 @@ def lib() -> ctypes.CDLL:
     sigs = {
         "gs_version": ([], i32),
         "gs_last_cuda_error": ([], i32),
-        "gs_project_fwd": ([i64, i32] + [vp] * 7 + [P] + [vp] * 6 + [vp], i32),
-        "gs_project_fwd_batch": ([i64, i32, i32] + [vp] * 7 + [P] + [vp] * 6 + [vp], i32),
+        "gs_project_fwd": ([i64, i32] + [vp] * 7 + [P] + [vp] * 7 + [vp], i32),
+        "gs_project_fwd_batch": ([i64, i32, i32] + [vp] * 7 + [P] + [vp] * 7 + [vp], i32),
+        "gs_pack_records": ([i64] + [vp] * 4 + [P, vp, vp], i32),
         "gs_bin_count": ([i64, vp, vp, vp, u64, ctypes.POINTER(i64), vp], i32),
         "gs_bin_count_async": ([i64, vp, vp, vp, u64, vp, vp, vp], i32),
         "gs_bin_count_workspace_size": ([i64], u64),
@@ -219,8 +221,8 @@ def lib() -> ctypes.CDLL:
         "gs_bin_sort_workspace_size": ([i64, i64], u64),
         "gs_bin_check": ([vp, vp, vp], i32),
         "gs_bin_noalloc": ([i64, vp, vp, vp, P, vp, i64, vp, ctypes.POINTER(i64), vp], i32),
-        "gs_composite_fwd": ([vp] * 6 + [P] + [vp] * 3 + [vp], i32),
-        "gs_composite_bwd": ([i64] + [vp] * 9 + [P, vp, vp], i32),
+        "gs_composite_fwd": ([vp] * 3 + [P] + [vp] * 3 + [vp], i32),
+        "gs_composite_bwd": ([i64] + [vp] * 6 + [P, vp, vp], i32),
         "gs_project_bwd": ([i64, i32] + [vp] * 10 + [P] + [vp] * 5 + [vp], i32),
         "gs_project_bwd_views": ([i64, i32, i32] + [vp] * 13 + [vp], i32),
         "gs_adam_step": ([i64, i32] + [ctypes.POINTER(SplatArrays)] * 4 +

@@ -10,13 +10,15 @@ process.)
 The stages run as hand-written sm_100a kernels through the C ABI of
 ``libgs_b200.so`` (``include/gs_b200.h``), on the current CUDA stream:
 
-1. ``gs_project_fwd``   projection, SH colour, opacity, tile rectangle and count;
+1. ``gs_project_fwd``   projection, SH colour, opacity, tile rectangle and count,
+                        and each Gaussian's 64-byte record for the compositors;
 2. ``gs_bin_count``     depth order of the visible Gaussians and the
                         intersection total -- the one host sync, as in
                         intersections.py:51;
 3. ``gs_bin_sort``      (tile, depth)-ordered Gaussian ids and tile ranges;
 4. ``gs_composite_fwd`` per-tile front-to-back compositing.
-Backward: ``gs_composite_bwd`` then ``gs_project_bwd`` (interface.py:176-239).
+Backward: ``gs_pack_records`` (the records again, from the saved outputs),
+``gs_composite_bwd``, then ``gs_project_bwd`` (interface.py:176-239).
 
 Differences from the reference, all deliberate:
 * ``ranges`` is int64 in the fake (meta) kernel too, matching what the real
@@ -214,12 +216,13 @@ def _rasterize(
         projected_opacity = mean.new_empty((n, 1))
         bounds = torch.empty((n, 4), dtype=torch.int32, device=device)
         counts = torch.empty((n,), dtype=torch.int32, device=device)
+        records = mean.new_empty((n, 16))  # the compositors' staged form, internal
         _mark("begin:project_fwd")
         native.check(lib.gs_project_fwd(
             n, num_sh, _ptr(mean), _ptr(rotation), _ptr(scale), _ptr(opacity), _ptr(color),
             _ptr(camera_rotation), _ptr(camera_translation), pref, _ptr(projected_mean),
             _ptr(inverse_covariance), _ptr(projected_color), _ptr(projected_opacity),
-            _ptr(bounds), _ptr(counts), stream), "gs_project_fwd")
+            _ptr(bounds), _ptr(counts), _ptr(records), stream), "gs_project_fwd")
         _mark("project_fwd")
 
         count_bytes = lib.gs_bin_count_workspace_size(n)
@@ -245,8 +248,7 @@ def _rasterize(
                 native.check(lib.gs_bin_check(_ptr(count_ws), _ptr(sort_ws), stream), "binning")
             _mark("begin:composite_fwd")
             native.check(lib.gs_composite_fwd(
-                _ptr(projected_mean), _ptr(inverse_covariance), _ptr(projected_color),
-                _ptr(projected_opacity), _ptr(gaussian_ids), _ptr(ranges), pref, _ptr(image),
+                _ptr(records), _ptr(gaussian_ids), _ptr(ranges), pref, _ptr(image),
                 _ptr(final_transmittance), _ptr(n_contributors), stream), "gs_composite_fwd")
             _mark("composite_fwd")
             return gaussian_ids
@@ -395,10 +397,15 @@ def _backward(ctx, *grad_outputs):
             grad_projected = arena.grad_projected
         else:
             grad_projected = mean.new_empty((n, 9))
+        # The compositors' staged records, rebuilt from the saved projection
+        # outputs (the operator's saved set is the reference's).
+        records = mean.new_empty((n, 16))
         _mark("begin:composite_bwd")
-        native.check(lib.gs_composite_bwd(
+        native.check(lib.gs_pack_records(
             n, _ptr(projected_mean), _ptr(inverse_covariance), _ptr(projected_color),
-            _ptr(projected_opacity), _ptr(gaussian_ids), _ptr(ranges), _ptr(grad_image),
+            _ptr(projected_opacity), pref, _ptr(records), stream), "gs_pack_records")
+        native.check(lib.gs_composite_bwd(
+            n, _ptr(records), _ptr(gaussian_ids), _ptr(ranges), _ptr(grad_image),
             _ptr(final_transmittance), _ptr(n_contributors), pref, _ptr(grad_projected),
             stream), "gs_composite_bwd")
         _mark("composite_bwd")
@@ -603,12 +610,13 @@ def rasterize_batch(
         projected_opacity = mean.new_empty((views, n, 1))
         bounds = torch.empty((views, n, 4), dtype=torch.int32, device=device)
         counts = torch.empty((views, n), dtype=torch.int32, device=device)
+        records = mean.new_empty((views, n, 16))
         native.check(lib.gs_project_fwd_batch(
             n, num_sh, views, _ptr(mean), _ptr(rotation), _ptr(scale), _ptr(opacity),
             _ptr(color), ctypes.c_void_p(rotations.data_ptr()),
             ctypes.c_void_p(translations.data_ptr()), params, _ptr(projected_mean),
             _ptr(inverse_covariance), _ptr(projected_color), _ptr(projected_opacity),
-            _ptr(bounds), _ptr(counts), stream), "gs_project_fwd_batch")
+            _ptr(bounds), _ptr(counts), _ptr(records), stream), "gs_project_fwd_batch")
 
         count_bytes = lib.gs_bin_count_workspace_size(n)
         count_ws = torch.empty((views, count_bytes), dtype=torch.uint8, device=device)
@@ -646,8 +654,7 @@ def rasterize_batch(
             final_transmittance = mean.new_empty((height, width))
             n_contributors = torch.empty((height, width), dtype=torch.int32, device=device)
             native.check(lib.gs_composite_fwd(
-                _ptr(projected_mean[v]), _ptr(inverse_covariance[v]), _ptr(projected_color[v]),
-                _ptr(projected_opacity[v]), _ptr(gaussian_ids), _ptr(ranges), pref, _ptr(image),
+                _ptr(records[v]), _ptr(gaussian_ids), _ptr(ranges), pref, _ptr(image),
                 _ptr(final_transmittance), _ptr(n_contributors), stream), "gs_composite_fwd")
             outputs.append((image, final_transmittance, n_contributors, projected_mean[v],
                             inverse_covariance[v], projected_color[v], projected_opacity[v],

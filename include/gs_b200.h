@@ -69,14 +69,27 @@ int32_t gs_last_cuda_error(void);
 /* Projection + SH + tile counting: replaces _project_and_count_kernel and
  * its launcher (project.py:74-345). Writes the four projected op outputs,
  * per-Gaussian tile counts and the tile rectangles
- * bounds [N,4] = (xmin, xmax, ymin, ymax) used by gs_bin_*. */
+ * bounds [N,4] = (xmin, xmax, ymin, ymax) used by gs_bin_*. When `records`
+ * is not NULL it also writes the compositors' staged form of every Gaussian
+ * with a non-zero count, records [N,16] float (16-byte aligned): per
+ * Gaussian (mean_x, mean_y, conic_xx, 2 conic_xy), (conic_yy, opacity, skip
+ * cutoff, conic_xy), (r, g, b, index as float bits) and the bounding box of
+ * the pixels where alpha can reach 1/255. gs_composite_fwd/bwd read them. */
 int32_t gs_project_fwd(int64_t n, int32_t num_sh, const float *mean, const float *rotation,
                        const float *scale, const float *opacity, const float *color,
                        const float *camera_rotation, const float *camera_translation,
                        const gs_params *params, float *projected_mean,
                        float *inverse_covariance, float *projected_color,
                        float *projected_opacity, int32_t *bounds, int32_t *counts,
-                       gs_stream_t stream);
+                       float *records, gs_stream_t stream);
+
+/* The records gs_project_fwd writes, built from the four projected arrays
+ * (the op's outputs) of n Gaussians: for a caller that kept only those, e.g.
+ * before a backward pass. No counterpart in the reference, whose compositing
+ * kernels gather the four arrays per pixel tile. */
+int32_t gs_pack_records(int64_t n, const float *projected_mean, const float *inverse_covariance,
+                        const float *projected_color, const float *projected_opacity,
+                        const gs_params *params, float *records, gs_stream_t stream);
 
 /* Projection of one scene into `num_views` cameras at once (the batched
  * multi-camera form of gs_project_fwd; no counterpart in the reference, which
@@ -85,14 +98,15 @@ int32_t gs_project_fwd(int64_t n, int32_t num_sh, const float *mean, const float
  * projects into every camera; per view the outputs are bit-identical to
  * gs_project_fwd's. Cameras and scalars are HOST arrays:
  * camera_rotations_host [V,3,3], camera_translations_host [V,3],
- * params_host [V]. Outputs are [V, N, ...]: view v starts at v * N rows. */
+ * params_host [V]. Outputs are [V, N, ...]: view v starts at v * N rows
+ * (records, when not NULL, [V, N, 16]). */
 int32_t gs_project_fwd_batch(int64_t n, int32_t num_sh, int32_t num_views, const float *mean,
                              const float *rotation, const float *scale, const float *opacity,
                              const float *color, const float *camera_rotations_host,
                              const float *camera_translations_host, const gs_params *params_host,
                              float *projected_mean, float *inverse_covariance,
                              float *projected_color, float *projected_opacity, int32_t *bounds,
-                             int32_t *counts, gs_stream_t stream);
+                             int32_t *counts, float *records, gs_stream_t stream);
 
 /* Binning, phase 1: the host sync of emit_intersections
  * (intersections.py:51-52). Orders the Gaussians with counts > 0 by depth
@@ -168,10 +182,9 @@ int32_t gs_bin_noalloc(int64_t n, const float *projected_mean, const int32_t *co
                        gs_stream_t stream);
 
 /* Front-to-back compositing: replaces _composite_kernel (composite.py:25-162).
+ * records: what gs_project_fwd (or gs_pack_records) wrote for the view.
  * image [H,W,3], final_transmittance [H,W], n_contributors [H,W] int32. */
-int32_t gs_composite_fwd(const float *projected_mean, const float *inverse_covariance,
-                         const float *projected_color, const float *projected_opacity,
-                         const int32_t *gaussian_ids, const int64_t *ranges,
+int32_t gs_composite_fwd(const float *records, const int32_t *gaussian_ids, const int64_t *ranges,
                          const gs_params *params, float *image, float *final_transmittance,
                          int32_t *n_contributors, gs_stream_t stream);
 
@@ -179,12 +192,10 @@ int32_t gs_composite_fwd(const float *projected_mean, const float *inverse_covar
  * index_add_ reduction (composite_bwd.py:47-277). Accumulates into
  * grad_projected [N,9] = (d mean_x, d mean_y, d conic_xx, d conic_xy,
  * d conic_yy, d r, d g, d b, d opacity), which this call zeroes first. */
-int32_t gs_composite_bwd(int64_t n, const float *projected_mean, const float *inverse_covariance,
-                         const float *projected_color, const float *projected_opacity,
-                         const int32_t *gaussian_ids, const int64_t *ranges,
-                         const float *grad_image, const float *final_transmittance,
-                         const int32_t *n_contributors, const gs_params *params,
-                         float *grad_projected, gs_stream_t stream);
+int32_t gs_composite_bwd(int64_t n, const float *records, const int32_t *gaussian_ids,
+                         const int64_t *ranges, const float *grad_image,
+                         const float *final_transmittance, const int32_t *n_contributors,
+                         const gs_params *params, float *grad_projected, gs_stream_t stream);
 
 /* Parameter gradients: replaces _project_bwd_kernel (project_bwd.py:8-381).
  * SH gradients cover all K coefficients: degree 4 (K = 25) differentiates the

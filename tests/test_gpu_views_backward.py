@@ -49,9 +49,12 @@ def _screen_gradients(splats, camera, seed):
     gp = torch.empty((n, 9), device="cuda")
     P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
     stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
-    native.check(lib.gs_composite_bwd(n, P(pm), P(conic), P(rgb), P(op), P(ids), P(ranges),
-                                      P(grad_image), P(final_t), P(n_contrib),
-                                      ctypes.byref(params), P(gp), stream), "composite_bwd")
+    records = torch.empty((n, 16), device="cuda")
+    native.check(lib.gs_pack_records(n, P(pm), P(conic), P(rgb), P(op), ctypes.byref(params),
+                                     P(records), stream), "pack_records")
+    native.check(lib.gs_composite_bwd(n, P(records), P(ids), P(ranges), P(grad_image),
+                                      P(final_t), P(n_contrib), ctypes.byref(params), P(gp),
+                                      stream), "composite_bwd")
     return params, conic, counts, gp, grad_image
 
 

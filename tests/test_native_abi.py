@@ -66,10 +66,10 @@ def test_argument_checks_without_gpu(lib):
 
     p = native.make_params(10.0, 10.0, 8.0, 8.0, 16, 16, 3, 0.999, 0.2, 100.0, "gaussian", 0.95)
     null = ctypes.c_void_p(0)
-    status = lib.gs_project_fwd(1, 1, *([null] * 7), ctypes.byref(p), *([null] * 6), null)
+    status = lib.gs_project_fwd(1, 1, *([null] * 7), ctypes.byref(p), *([null] * 7), null)
     assert status == -1  # tile size 3
     p = native.make_params(10.0, 10.0, 8.0, 8.0, 16, 16, 8, 0.999, 0.2, 100.0, "gaussian", 0.95)
-    status = lib.gs_project_fwd(1, 36, *([null] * 7), ctypes.byref(p), *([null] * 6), null)
+    status = lib.gs_project_fwd(1, 36, *([null] * 7), ctypes.byref(p), *([null] * 7), null)
     assert status == -4  # SH degree 5
     total = ctypes.c_int64(0)
     status = lib.gs_bin_count(10, null, null, null, 0, ctypes.byref(total), null)

@@ -49,7 +49,7 @@ def _project(lib, native, scene):
     native.check(lib.gs_project_fwd(n, k, _ptr(mean), _ptr(rotation), _ptr(scale), _ptr(opacity),
                                     _ptr(color), _ptr(cam_r), _ptr(cam_t), ctypes.byref(params),
                                     _ptr(pm), _ptr(conic), _ptr(rgb), _ptr(o), _ptr(bounds),
-                                    _ptr(counts), stream), "gs_project_fwd")
+                                    _ptr(counts), None, stream), "gs_project_fwd")
     return params, pm, counts, bounds
 
 
