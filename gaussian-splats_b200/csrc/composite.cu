@@ -313,12 +313,19 @@ __device__ __forceinline__ void warp_reduce_scatter9(const float (&v)[9], int la
   for (int o = 16; o > 0; o >>= 1) last += __shfl_xor_sync(0xffffffffu, last, o);
 }
 
-// List entries per staging batch of the backward: double-buffered records
-// of 128 entries keep the CTA's shared memory within the eight CTAs per SM
-// its register bound allows.
+// Staging of the backward: double-buffered batches of 128 records (the next
+// batch in flight while one is used; 17 KB of shared memory, so the eight
+// CTAs per SM its register bound allows still fit), or with
+// GS_BWD_DOUBLE=0 single-buffered batches of 256 (two barriers per batch).
+#ifndef GS_BWD_DOUBLE
+#define GS_BWD_DOUBLE 1
+#endif
+constexpr bool kBackwardDoubleBuffer = GS_BWD_DOUBLE != 0;
 template <int TS, int PPT>
 struct BackwardBatch {
-  static constexpr int value = TileShape<TS, PPT>::kBatch < 128 ? TileShape<TS, PPT>::kBatch : 128;
+  static constexpr int kMax = kBackwardDoubleBuffer ? 128 : 256;
+  static constexpr int value =
+      TileShape<TS, PPT>::kBatch < kMax ? TileShape<TS, PPT>::kBatch : kMax;
 };
 
 template <int TS, int PPT, bool kGaussian>
@@ -335,7 +342,8 @@ __global__ void __launch_bounds__(TileShape<TS, PPT>::kThreads,
   constexpr int Q = S::kPpt;
   constexpr int kStage = (NB + S::kThreads - 1) / S::kThreads;  // entries staged per thread
   constexpr unsigned kMask = S::kWarpMask;
-  __shared__ StageBuffer<NB> s_buf[2];
+  constexpr int kBuffers = kBackwardDoubleBuffer ? 2 : 1;
+  __shared__ StageBuffer<NB> s_buf[kBuffers];
   __shared__ uint16_t s_list[S::kWarps][NB];
   __shared__ int s_max_contrib;
   const int tile = blockIdx.x;
@@ -394,10 +402,11 @@ __global__ void __launch_bounds__(TileShape<TS, PPT>::kThreads,
     sr[q] = sg[q] = sb[q] = 0.0f;
   }
   int buf = 0;
-  for (int64_t batch_end = end; batch_end > start; batch_end -= NB, buf ^= 1) {
+  for (int64_t batch_end = end; batch_end > start;
+       batch_end -= NB, buf = kBackwardDoubleBuffer ? buf ^ 1 : 0) {
     const int64_t batch_start = batch_end - NB > start ? batch_end - NB : start;
     // the next (earlier) batch's records fill the other buffer meanwhile
-    if (batch_start > start) {
+    if (kBackwardDoubleBuffer && batch_start > start) {
       const int64_t next_start = batch_start - NB > start ? batch_start - NB : start;
       const int64_t after_start = next_start - NB > start ? next_start - NB : start;
 #pragma unroll
@@ -496,8 +505,29 @@ __global__ void __launch_bounds__(TileShape<TS, PPT>::kThreads,
         }
       }
     }
-    cp_async_wait_all();
-    __syncthreads();
+    if constexpr (kBackwardDoubleBuffer) {
+      cp_async_wait_all();
+      __syncthreads();
+    } else {
+      // one buffer: refill it once every warp is done with it
+      __syncthreads();
+      if (batch_start > start) {
+        const int64_t next_start = batch_start - NB > start ? batch_start - NB : start;
+        const int64_t after_start = next_start - NB > start ? next_start - NB : start;
+#pragma unroll
+        for (int s = 0; s < kStage; ++s) {
+          const int slot = tid + s * S::kThreads;
+          if (slot < NB && next_start + slot < batch_start) {
+            stage_async(records, next_id[s], s_buf[0], slot);
+            if (after_start + slot < next_start)
+              next_id[s] = __ldg(gaussian_ids + after_start + slot);
+          }
+        }
+      }
+      cp_async_commit();
+      cp_async_wait_all();
+      __syncthreads();
+    }
   }
 }
 

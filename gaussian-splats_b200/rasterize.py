@@ -17,8 +17,8 @@ The stages run as hand-written sm_100a kernels through the C ABI of
                         intersections.py:51;
 3. ``gs_bin_sort``      (tile, depth)-ordered Gaussian ids and tile ranges;
 4. ``gs_composite_fwd`` per-tile front-to-back compositing.
-Backward: ``gs_pack_records`` (the records again, from the saved outputs),
-``gs_composite_bwd``, then ``gs_project_bwd`` (interface.py:176-239).
+Backward: ``gs_composite_bwd`` (on the forward's records, or on records
+rebuilt by ``gs_pack_records``), then ``gs_project_bwd`` (interface.py:176-239).
 
 Differences from the reference, all deliberate:
 * ``ranges`` is int64 in the fake (meta) kernel too, matching what the real
@@ -159,6 +159,25 @@ _CAPTURE = None
 _SEEN_TOTALS: dict | None = None
 
 
+# Records of renders whose backward has not run yet, by (counts storage
+# address, Gaussian count): the operator's saved set is the reference's, so
+# the forward's records ride along here instead. The address identifies the
+# render: its counts tensor is saved for the backward, so no later render can
+# reuse that storage while the backward is still to come. A backward that
+# finds no entry (a second backward, or one beyond the last few renders)
+# rebuilds the records from the saved outputs (gs_pack_records).
+_PENDING_RECORDS: dict = {}
+_MAX_PENDING_RECORDS = 4
+
+
+def _keep_records(counts: torch.Tensor, records: torch.Tensor) -> None:
+    key = (counts.data_ptr(), counts.numel())
+    _PENDING_RECORDS.pop(key, None)
+    _PENDING_RECORDS[key] = records
+    while len(_PENDING_RECORDS) > _MAX_PENDING_RECORDS:
+        _PENDING_RECORDS.pop(next(iter(_PENDING_RECORDS)))
+
+
 def _pinned_words() -> torch.Tensor:
     """Two zeroed pinned int64 host words (intersection total, error word) for
     one render; torch's pinned-memory cache makes them cheap to allocate."""
@@ -201,6 +220,7 @@ def _rasterize(
     _check_inputs(mean, color, rendering_mode)
     lib = native.lib()
     device = mean.device
+    backward_possible = any(t.requires_grad for t in (mean, rotation, scale, opacity, color))
     mean, rotation, scale, opacity, color = map(_f32, (mean, rotation, scale, opacity, color))
     camera_rotation, camera_translation = _f32(camera_rotation), _f32(camera_translation)
     n, num_sh = mean.shape[0], color.shape[1]
@@ -312,6 +332,8 @@ def _rasterize(
             _LAST_TOTAL[key] = total
             if _SEEN_TOTALS is not None:
                 _SEEN_TOTALS[key] = max(total, _SEEN_TOTALS.get(key, 0))
+        if backward_possible:
+            _keep_records(counts, records)
     return (image, final_transmittance, n_contributors, projected_mean, inverse_covariance,
             projected_color, projected_opacity, gaussian_ids, ranges, counts)
 
@@ -397,13 +419,15 @@ def _backward(ctx, *grad_outputs):
             grad_projected = arena.grad_projected
         else:
             grad_projected = mean.new_empty((n, 9))
-        # The compositors' staged records, rebuilt from the saved projection
-        # outputs (the operator's saved set is the reference's).
-        records = mean.new_empty((n, 16))
+        # The compositors' records of this render: kept by its forward, or
+        # rebuilt from the saved projection outputs.
+        records = _PENDING_RECORDS.pop((counts.data_ptr(), counts.numel()), None)
         _mark("begin:composite_bwd")
-        native.check(lib.gs_pack_records(
-            n, _ptr(projected_mean), _ptr(inverse_covariance), _ptr(projected_color),
-            _ptr(projected_opacity), pref, _ptr(records), stream), "gs_pack_records")
+        if records is None:
+            records = mean.new_empty((n, 16))
+            native.check(lib.gs_pack_records(
+                n, _ptr(projected_mean), _ptr(inverse_covariance), _ptr(projected_color),
+                _ptr(projected_opacity), pref, _ptr(records), stream), "gs_pack_records")
         native.check(lib.gs_composite_bwd(
             n, _ptr(records), _ptr(gaussian_ids), _ptr(ranges), _ptr(grad_image),
             _ptr(final_transmittance), _ptr(n_contributors), pref, _ptr(grad_projected),
