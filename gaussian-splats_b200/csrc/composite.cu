@@ -190,12 +190,6 @@ __device__ __forceinline__ int warp_select(const PixelMap<TS, PPT>& pm, const St
   return selected;
 }
 
-// Forward: every warp walks the tile's list on its own, kWarpLanes entries
-// (a chunk) at a time -- lane l stages entry l of each chunk into the warp's
-// double buffer and tests its box against the warp's pixel block; the warp
-// then composites the hits in list order, iterating the ballot's set bits.
-// No CTA barrier: a warp whose pixels are all done stops, whatever the
-// others do, and warps never wait for one another's staging.
 template <int TS, bool kGaussian>
 __global__ void __launch_bounds__(TileShape<TS, 1>::kThreads,
                                   forward_min_blocks(TileShape<TS, 1>::kThreads))
@@ -205,76 +199,80 @@ __global__ void __launch_bounds__(TileShape<TS, 1>::kThreads,
                          float* __restrict__ image, float* __restrict__ final_transmittance,
                          int32_t* __restrict__ n_contributors) {
   using S = TileShape<TS, 1>;
-  constexpr int L = S::kWarpLanes;
-  constexpr unsigned kMask = S::kWarpMask;
-  // [warps][2] stage buffers (dynamic: 32 x 32 tiles need 128 KB)
-  extern __shared__ float4 s_dynamic[];
-  StageBuffer<L>(*s_stage)[2] = reinterpret_cast<StageBuffer<L>(*)[2]>(s_dynamic);
+  constexpr int NB = S::kBatch;
+  constexpr int kWarps = S::kWarps;
+  __shared__ StageBuffer<NB> s_buf[2];
+  __shared__ uint16_t s_list[kWarps][NB];
   const int tile = blockIdx.x;
   const int tid = threadIdx.x;
-  const int lane = tid % L, warp = tid / L;
+  const int lane = tid % S::kWarpLanes, warp = tid / S::kWarpLanes;
   const PixelMap<TS, 1> pm(tile, p.width / TS, tid);
   const float fpx = static_cast<float>(pm.px), fpy = static_cast<float>(pm.py0);
   const int64_t start = ranges[2 * tile], end = ranges[2 * tile + 1];
   const float threshold = p.opacity_threshold;
-  StageBuffer<L>* stage = s_stage[warp];
+  uint16_t* list = s_list[warp];
 
-  // Lane l stages entry l of every chunk; the id of its entry in the chunk
-  // after next is loaded a chunk ahead, so issuing a chunk's copies never waits.
+  // Thread tid stages entry tid of every batch; the id of its next batch's
+  // entry is loaded one batch ahead, so issuing a batch's copies never waits.
   int32_t next_id = 0;
-  if (start + lane < end) stage_async(records, __ldg(gaussian_ids + start + lane), stage[0], lane);
-  if (start + L + lane < end) next_id = __ldg(gaussian_ids + start + L + lane);
+  if (tid < NB) {
+    if (start + tid < end) stage_async(records, __ldg(gaussian_ids + start + tid), s_buf[0], tid);
+    if (start + NB + tid < end) next_id = __ldg(gaussian_ids + start + NB + tid);
+  }
   cp_async_commit();
   cp_async_wait_all();
-  __syncwarp(kMask);
+  __syncthreads();
 
   float T = 1.0f, cr = 0.0f, cg = 0.0f, cb = 0.0f;
   bool done = !((1.0f - T) < threshold);
   int64_t contrib = 0;
   int buf = 0;
-  for (int64_t chunk = start; chunk < end && __any_sync(kMask, !done); chunk += L, buf ^= 1) {
-    const int64_t next = chunk + L;
-    if (next + lane < end) {  // the next chunk lands in the other buffer meanwhile
-      stage_async(records, next_id, stage[buf ^ 1], lane);
-      if (next + L + lane < end) next_id = __ldg(gaussian_ids + next + L + lane);
+  for (int64_t batch = start; batch < end; batch += NB, buf ^= 1) {
+    // The next batch's records fill the other buffer while this one is used.
+    const int64_t next = batch + NB;
+    if (tid < NB && next + tid < end) {
+      stage_async(records, next_id, s_buf[buf ^ 1], tid);
+      if (next + NB + tid < end) next_id = __ldg(gaussian_ids + next + NB + tid);
     }
     cp_async_commit();
-    const StageBuffer<L>& cur = stage[buf];
-    unsigned hits = __ballot_sync(kMask, chunk + lane < end && !pm.misses(cur.box[lane]));
-    if (!done) {
-      while (hits) {
-        const int j = __ffs(hits) - 1;
-        hits &= hits - 1;
-        const float4 a = cur.a[j];
-        const float4 b = cur.b[j];
-        const float dx = fpx - a.x, dy = fpy - a.y;
-        const float d2 = pair_d2(dx, dy, a.z, a.w, b.x);
-        if (!(d2 <= b.z)) continue;
-        float alpha;
-        if constexpr (kGaussian) {
-          const float prob = d2 >= 0.0f ? det_exp_nonpositive(-0.5f * d2) : det_exp(-0.5f * d2);
-          alpha = fminf(b.y * prob, kAlphaMax);
-        } else {
-          alpha = fminf(b.y, kAlphaMax);
-        }
-        if (!(alpha >= kAlphaMin)) continue;
-        const float4 c = cur.c[j];
-        const float weight = T * alpha;
-        cr = fmaf(weight, c.x, cr);
-        cg = fmaf(weight, c.y, cg);
-        cb = fmaf(weight, c.z, cb);
-        T = T * (1.0f - alpha);
-        if (!((1.0f - T) < threshold)) {
-          done = true;
-          contrib = chunk + j + 1 - start;
-          break;
+    const StageBuffer<NB>& cur = s_buf[buf];
+    if (__any_sync(S::kWarpMask, !done)) {
+      const int count = static_cast<int>(end - batch < NB ? end - batch : NB);
+      const int selected = warp_select<TS, 1, false>(pm, cur, count, lane, list, 0, -1);
+      if (!done) {
+        for (int i = 0; i < selected; ++i) {
+          const int j = list[i];
+          const float4 a = cur.a[j];
+          const float4 b = cur.b[j];
+          const float dx = fpx - a.x, dy = fpy - a.y;
+          const float d2 = pair_d2(dx, dy, a.z, a.w, b.x);
+          if (!(d2 <= b.z)) continue;
+          float alpha;
+          if constexpr (kGaussian) {
+            const float prob = d2 >= 0.0f ? det_exp_nonpositive(-0.5f * d2) : det_exp(-0.5f * d2);
+            alpha = fminf(b.y * prob, kAlphaMax);
+          } else {
+            alpha = fminf(b.y, kAlphaMax);
+          }
+          if (!(alpha >= kAlphaMin)) continue;
+          const float4 c = cur.c[j];
+          const float weight = T * alpha;
+          cr = fmaf(weight, c.x, cr);
+          cg = fmaf(weight, c.y, cg);
+          cb = fmaf(weight, c.z, cb);
+          T = T * (1.0f - alpha);
+          if (!((1.0f - T) < threshold)) {
+            done = true;
+            contrib = batch + j + 1 - start;
+            break;
+          }
         }
       }
     }
-    // this lane's copies of the next chunk have landed; the warp barrier
-    // shows them to every lane and frees the current buffer for refilling
+    // This thread's copies of the next batch have landed; the barrier makes
+    // every thread's visible and frees the current buffer for refilling.
     cp_async_wait_all();
-    __syncwarp(kMask);
+    if (__syncthreads_count(!done) == 0) break;
   }
   if (!done) contrib = end - start;
   const int64_t pix = static_cast<int64_t>(pm.py0) * p.width + pm.px;
@@ -593,17 +591,12 @@ int32_t launch_composite_fwd(const float* records, const int32_t* gaussian_ids,
   if (num_tiles == 0) return GS_OK;
   const float4* rec = reinterpret_cast<const float4*>(records);
 #define GS_LAUNCH(TS)                                                                          \
-  {                                                                                            \
-    using S = TileShape<TS, 1>;                                                                \
-    const size_t smem = sizeof(StageBuffer<S::kWarpLanes>) * 2 * S::kWarps;                   \
-    auto kernel = p.gaussian_mode ? composite_fwd_kernel<TS, true>                             \
-                                  : composite_fwd_kernel<TS, false>;                           \
-    if (smem > 48 * 1024)                                                                      \
-      GS_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,    \
-                                       static_cast<int>(smem)));                               \
-    kernel<<<static_cast<unsigned>(num_tiles), S::kThreads, smem, stream>>>(                   \
+  if (p.gaussian_mode)                                                                         \
+    composite_fwd_kernel<TS, true><<<static_cast<unsigned>(num_tiles), TS * TS, 0, stream>>>(  \
         rec, gaussian_ids, ranges, p, image, final_transmittance, n_contributors);             \
-  }
+  else                                                                                         \
+    composite_fwd_kernel<TS, false><<<static_cast<unsigned>(num_tiles), TS * TS, 0, stream>>>( \
+        rec, gaussian_ids, ranges, p, image, final_transmittance, n_contributors)
   GS_TILE_DISPATCH(p.tile_size, GS_LAUNCH)
 #undef GS_LAUNCH
   return check_launch();
