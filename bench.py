@@ -70,6 +70,9 @@ def project_bwd_bytes(k):
     return 44 + 12 * k + 56 + 44 + 12 * k
 
 
+# The projection also writes each visible Gaussian's 64-byte compositing
+# record (the compositors' staged form).
+RECORD_BYTES = 64
 PROJECT_FWD_BYTES = project_fwd_bytes(16)
 PROJECT_BWD_BYTES = project_bwd_bytes(16)
 # Per evaluated (pixel, Gaussian) pair, the reference's forward arithmetic
@@ -973,7 +976,7 @@ def main():
         return entry
 
     rooflines = {
-        "project_fwd": hbm("project_fwd", n * project_fwd_bytes(k)),
+        "project_fwd": hbm("project_fwd", n * project_fwd_bytes(k) + visible * RECORD_BYTES),
         "composite_fwd": issue("composite_fwd", pairs * COMPOSITE_FWD_FLOPS),
     }
     if backward:

@@ -12,9 +12,10 @@ config scenes the benchmark uses, and prints one JSON line per case:
   intermediates, beyond host memory for a whole 1080p view, so ``project``,
   ``cull`` and ``tile`` run on the whole scene and ``render`` over bands of
   tile rows, each band's list re-based and the band images summed (exactly
-  the whole image: every tile belongs to one band). With ``--backward`` the
-  band losses' gradients w.r.t. the projected tensors are accumulated and
-  back-propagated through project once. Labelled "band-summed".
+  the whole image: every tile belongs to one band). For fwd+bwd (timed
+  unless ``--forward-only``) the band losses' gradients w.r.t. the projected
+  tensors are accumulated and back-propagated through project once.
+  Labelled "band-summed".
 
 Times are the median of ``--repeats`` runs after one warm-up, with
 ``torch.set_num_threads(<all host cores>)``.
