@@ -122,6 +122,19 @@ struct ArraySource {
   __device__ __forceinline__ const uint32_t* keys_ptr() const { return keys; }
 };
 
+// Positions 0..n-1 keyed by keys[i]: the first pass of the deterministic
+// backward's grouping of list positions by Gaussian.
+struct PositionSource {
+  const uint32_t* keys;
+  __device__ __forceinline__ bool valid(int64_t) const { return true; }
+  __device__ __forceinline__ uint32_t key(int64_t i) const { return keys[i]; }
+  __device__ __forceinline__ uint32_t value(int64_t i) const { return static_cast<uint32_t>(i); }
+  template <int R>
+  __device__ __forceinline__ uint32_t load_run(int64_t first, int64_t n, uint32_t (&out)[R]) const {
+    return ArraySource{keys, nullptr}.load_run<R>(first, n, out);
+  }
+};
+
 // Element count of a pass: a host value, or a device word written earlier on
 // the stream (the number of visible Gaussians), or the smaller of a host
 // capacity and a device total (the intersection total, when the buffers were
@@ -746,6 +759,57 @@ int32_t launch_bin_sort(int64_t n, int64_t total, const int32_t* bounds, const i
   if (num_tiles > 0) {
     ranges_kernel<<<ceil_div(ceil_div(total + 1, kRangeItems), 256), 256, 0, stream>>>(
         sorted_keys, live, num_tiles, ranges);
+    GS_TRY(check_launch());
+  }
+  return GS_OK;
+}
+
+// Stable sort of the positions 0..total-1 by keys[position] (< num_keys):
+// `order` receives the positions grouped by key, increasing within a key, and
+// segments [num_keys, 2] each key's [start, end) in `order`. The sort phase's
+// machinery on other keys: the deterministic backward groups the per-entry
+// gradient rows of each Gaussian this way. `workspace` holds
+// bin_sort_workspace_size(total, num_keys) bytes.
+int32_t launch_sort_positions(int64_t total, int64_t num_keys, const int32_t* keys,
+                              void* workspace, uint32_t* order, int64_t* segments,
+                              cudaStream_t stream) {
+  const SortLayout L(total, num_keys);
+  BinHeader* h = at<BinHeader>(workspace, L.header);
+  GS_CUDA_TRY(cudaMemsetAsync(workspace, 0, L.zero_bytes, stream));
+  uint32_t* kA = at<uint32_t>(workspace, L.keys_a);
+  uint32_t* kB = at<uint32_t>(workspace, L.keys_b);
+  uint32_t* vA = at<uint32_t>(workspace, L.values_a);
+  uint32_t* vB = at<uint32_t>(workspace, L.values_b);
+  const uint32_t* in_keys = reinterpret_cast<const uint32_t*>(keys);
+  const Count all{total, nullptr};
+  const uint32_t* sorted_keys = in_keys;
+  const int passes = L.passes > 0 ? L.passes : 1;
+  if (L.passes == 0 && num_keys > 1) return GS_ERR_INVALID_ARGUMENT;
+  if (total > 0) {
+    upsweep_kernel<PositionSource, 16><<<upsweep_blocks(total), kThreads, 0, stream>>>(
+        PositionSource{in_keys}, all, passes, 0, &h->hist[0][0], nullptr);
+    GS_TRY(check_launch());
+    const int64_t blocks = (total + kTile - 1) / kTile;
+    uint32_t* status = at<uint32_t>(workspace, L.status);
+    for (int pass = 0; pass < passes; ++pass) {
+      uint32_t* dst_k = (pass % 2 == 0) ? kB : kA;
+      uint32_t* dst_v = (pass == passes - 1) ? order : ((pass % 2 == 0) ? vB : vA);
+      uint32_t* pass_status = status + static_cast<int64_t>(pass) * blocks * kRadix;
+      if (pass == 0)
+        sort_pass_kernel<<<blocks, kThreads, 0, stream>>>(
+            PositionSource{in_keys}, all, 0, &h->hist[0][0], pass_status, &h->pass_counters[0],
+            dst_k, dst_v, &h->error);
+      else
+        sort_pass_kernel<<<blocks, kThreads, 0, stream>>>(
+            ArraySource{pass % 2 ? kB : kA, pass % 2 ? vB : vA}, all, 8 * pass,
+            &h->hist[pass][0], pass_status, &h->pass_counters[pass], dst_k, dst_v, &h->error);
+      GS_TRY(check_launch());
+      sorted_keys = dst_k;
+    }
+  }
+  if (num_keys > 0) {
+    ranges_kernel<<<ceil_div(ceil_div(total + 1, kRangeItems), 256), 256, 0, stream>>>(
+        sorted_keys, all, num_keys, segments);
     GS_TRY(check_launch());
   }
   return GS_OK;

@@ -39,6 +39,11 @@ int32_t launch_composite_fwd(const float*, const int32_t*, const int64_t*, const
                              float*, float*, int32_t*, cudaStream_t);
 int32_t launch_composite_bwd(int64_t, const float*, const int32_t*, const int64_t*, const float*,
                              const float*, const int32_t*, const gs_params&, float*, cudaStream_t);
+uint64_t composite_bwd_deterministic_workspace_size(int64_t, int64_t);
+int32_t launch_composite_bwd_deterministic(int64_t, int64_t, const float*, const int32_t*,
+                                           const int64_t*, const float*, const float*,
+                                           const int32_t*, const gs_params&, void*, float*,
+                                           cudaStream_t);
 int32_t launch_adam_step(int64_t, int32_t, const gs_splat_arrays&, const gs_splat_arrays&,
                          const gs_splat_arrays&, const gs_splat_arrays&, const gs_adam_params&,
                          const float*, cudaStream_t);
@@ -235,6 +240,29 @@ int32_t gs_composite_bwd(int64_t n, const float* records, const int32_t* gaussia
   return gs::launch_composite_bwd(n, records, gaussian_ids, ranges, grad_image,
                                   final_transmittance, n_contributors, *params, grad_projected,
                                   as_cuda(stream));
+}
+
+uint64_t gs_composite_bwd_deterministic_workspace_size(int64_t n, int64_t total) {
+  return gs::composite_bwd_deterministic_workspace_size(n < 0 ? 0 : n, total < 0 ? 0 : total);
+}
+
+int32_t gs_composite_bwd_deterministic(int64_t n, int64_t total, const float* records,
+                                       const int32_t* gaussian_ids, const int64_t* ranges,
+                                       const float* grad_image, const float* final_transmittance,
+                                       const int32_t* n_contributors, const gs_params* params,
+                                       void* workspace, uint64_t workspace_bytes,
+                                       float* grad_projected, gs_stream_t stream) {
+  GS_TRY(gs::check_params(params));
+  if (n < 0 || n >= gs::kMaxGaussians || total < 0 || total >= gs::kMaxIntersections)
+    return GS_ERR_INVALID_ARGUMENT;
+  if (workspace_bytes < gs::composite_bwd_deterministic_workspace_size(n, total))
+    return GS_ERR_INVALID_ARGUMENT;
+  if (!gs::aligned(records, 16) || !gs::aligned(workspace, 256) || !gs::aligned(gaussian_ids, 16))
+    return GS_ERR_MISALIGNED;
+  return gs::launch_composite_bwd_deterministic(n, total, records, gaussian_ids, ranges,
+                                                grad_image, final_transmittance, n_contributors,
+                                                *params, workspace, grad_projected,
+                                                as_cuda(stream));
 }
 
 int32_t gs_project_bwd(int64_t n, int32_t num_sh, const float* mean, const float* rotation,

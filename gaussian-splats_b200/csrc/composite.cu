@@ -50,6 +50,11 @@
 #include "common.cuh"
 
 namespace gs {
+
+uint64_t bin_sort_workspace_size(int64_t, int64_t);
+int32_t launch_sort_positions(int64_t, int64_t, const int32_t*, void*, uint32_t*, int64_t*,
+                              cudaStream_t);
+
 namespace {
 
 template <int TS, int PPT>
@@ -328,7 +333,14 @@ struct BackwardBatch {
       TileShape<TS, PPT>::kBatch < kMax ? TileShape<TS, PPT>::kBatch : kMax;
 };
 
-template <int TS, int PPT, bool kGaussian>
+// kRows: the deterministic form. Instead of adding each warp's reduced
+// 9-vector into grad_projected[g] with atomics, every warp leaves it in shared
+// memory, and after each batch the CTA sums the warps' vectors in warp order
+// into one row per list position, rows [position, 9] (positions the tile never
+// reaches stay as the caller zeroed them). reduce_rows_kernel then adds each
+// Gaussian's rows in list-position order. No float addition depends on
+// scheduling, so the gradients are the same bits on every run.
+template <int TS, int PPT, bool kGaussian, bool kRows = false>
 __global__ void __launch_bounds__(TileShape<TS, PPT>::kThreads,
                                   min_blocks_for_32_warps(TileShape<TS, PPT>::kThreads))
     composite_bwd_kernel(const float4* __restrict__ records,
@@ -338,7 +350,14 @@ __global__ void __launch_bounds__(TileShape<TS, PPT>::kThreads,
                          const int32_t* __restrict__ n_contributors, const gs_params p,
                          float* __restrict__ grad_projected) {
   using S = TileShape<TS, PPT>;
-  constexpr int NB = BackwardBatch<TS, PPT>::value;
+  // (the deterministic form's per-warp vectors of 32 x 32 tiles take smaller batches
+  // to stay within 48 KB of shared memory)
+  constexpr int NB = kRows && S::kWarps > 8 ? 64 : BackwardBatch<TS, PPT>::value;
+  // per (warp, batch entry) reduced vectors of the deterministic form
+  __shared__ float s_part[kRows ? S::kWarps : 1][kRows ? NB : 1][9];
+  if constexpr (kRows) {
+    for (int i = threadIdx.x; i < S::kWarps * NB * 9; i += S::kThreads) (&s_part[0][0][0])[i] = 0.0f;
+  }
   constexpr int Q = S::kPpt;
   constexpr int kStage = (NB + S::kThreads - 1) / S::kThreads;  // entries staged per thread
   constexpr unsigned kMask = S::kWarpMask;
@@ -485,12 +504,18 @@ __global__ void __launch_bounds__(TileShape<TS, PPT>::kThreads,
       }
       if (__any_sync(kMask, active)) {
         const int g = __float_as_int(cur.c[j].w);
-        float* dst = grad_projected + 9 * static_cast<int64_t>(g);
+        float* dst = kRows ? s_part[kRows ? warp : 0][kRows ? j : 0]
+                           : grad_projected + 9 * static_cast<int64_t>(g);
         if constexpr (S::kWarpLanes == 32) {
           float mine, last;
           warp_reduce_scatter9(v, lane, mine, last);
-          if ((lane & 3) == 0) atomicAdd(dst + (lane >> 2), mine);
-          if (lane == 1) atomicAdd(dst + 8, last);
+          if constexpr (kRows) {
+            if ((lane & 3) == 0) dst[lane >> 2] = mine;
+            if (lane == 1) dst[8] = last;
+          } else {
+            if ((lane & 3) == 0) atomicAdd(dst + (lane >> 2), mine);
+            if (lane == 1) atomicAdd(dst + 8, last);
+          }
         } else {
 #pragma unroll
           for (int k = 0; k < 9; ++k) {
@@ -500,9 +525,29 @@ __global__ void __launch_bounds__(TileShape<TS, PPT>::kThreads,
           }
           if (lane == 0) {
 #pragma unroll
-            for (int k = 0; k < 9; ++k) atomicAdd(dst + k, v[k]);
+            for (int k = 0; k < 9; ++k) {
+              if constexpr (kRows)
+                dst[k] = v[k];
+              else
+                atomicAdd(dst + k, v[k]);
+            }
           }
         }
+      }
+    }
+    if constexpr (kRows) {
+      // every warp's vectors of this batch are in; one row per position, the
+      // warps added in order, then the slots cleared for the next batch
+      __syncthreads();
+      for (int i = threadIdx.x; i < count * 9; i += S::kThreads) {
+        const int j = i / 9, k = i % 9;
+        float sum = 0.0f;
+#pragma unroll
+        for (int w = 0; w < S::kWarps; ++w) {
+          sum += s_part[w][j][k];
+          s_part[w][j][k] = 0.0f;
+        }
+        grad_projected[9 * (batch_start + j) + k] = sum;
       }
     }
     if constexpr (kBackwardDoubleBuffer) {
@@ -582,6 +627,25 @@ int32_t launch_pack_records(int64_t n, const float* projected_mean,
   return check_launch();
 }
 
+// Deterministic backward, second step: grad_projected[g] = the sum of g's
+// rows in increasing list position (order: positions grouped by Gaussian;
+// segments: each Gaussian's [start, end) in order).
+__global__ void __launch_bounds__(256) reduce_rows_kernel(
+    int64_t n, const uint32_t* __restrict__ order, const int64_t* __restrict__ segments,
+    const float* __restrict__ rows, float* __restrict__ grad_projected) {
+  const int64_t g = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (g >= n) return;
+  float acc[9] = {};
+  const int64_t end = segments[2 * g + 1];
+  for (int64_t k = segments[2 * g]; k < end; ++k) {
+    const float* row = rows + 9 * static_cast<int64_t>(__ldg(order + k));
+#pragma unroll
+    for (int c = 0; c < 9; ++c) acc[c] += __ldg(row + c);
+  }
+#pragma unroll
+  for (int c = 0; c < 9; ++c) grad_projected[9 * g + c] = acc[c];
+}
+
 int32_t launch_composite_fwd(const float* records, const int32_t* gaussian_ids,
                              const int64_t* ranges, const gs_params& p, float* image,
                              float* final_transmittance, int32_t* n_contributors,
@@ -624,6 +688,64 @@ int32_t launch_composite_bwd(int64_t n, const float* records, const int32_t* gau
                      n_contributors, p, grad_projected)
   GS_TILE_DISPATCH(p.tile_size, GS_LAUNCH)
 #undef GS_LAUNCH
+  return check_launch();
+}
+
+// Deterministic backward workspace: rows [total, 9] float, order [total]
+// uint32, segments [n, 2] int64, then the position sort's scratch.
+struct DeterministicLayout {
+  uint64_t rows, order, segments, sort, bytes;
+  DeterministicLayout(int64_t n, int64_t total) {
+    auto align = [](uint64_t x) { return (x + 255) / 256 * 256; };
+    uint64_t at = 0;
+    rows = at; at = align(at + 36 * static_cast<uint64_t>(total));
+    order = at; at = align(at + 4 * static_cast<uint64_t>(total));
+    segments = at; at = align(at + 16 * static_cast<uint64_t>(n));
+    sort = at; at = align(at + bin_sort_workspace_size(total, n));
+    bytes = at;
+  }
+};
+
+uint64_t composite_bwd_deterministic_workspace_size(int64_t n, int64_t total) {
+  return DeterministicLayout(n, total).bytes;
+}
+
+int32_t launch_composite_bwd_deterministic(int64_t n, int64_t total, const float* records,
+                                           const int32_t* gaussian_ids, const int64_t* ranges,
+                                           const float* grad_image,
+                                           const float* final_transmittance,
+                                           const int32_t* n_contributors, const gs_params& p,
+                                           void* workspace, float* grad_projected,
+                                           cudaStream_t stream) {
+  const DeterministicLayout L(n, total);
+  char* base = static_cast<char*>(workspace);
+  float* rows = reinterpret_cast<float*>(base + L.rows);
+  uint32_t* order = reinterpret_cast<uint32_t*>(base + L.order);
+  int64_t* segments = reinterpret_cast<int64_t*>(base + L.segments);
+  GS_CUDA_TRY(cudaMemsetAsync(rows, 0, 36 * static_cast<size_t>(total), stream));
+  const int64_t num_tiles =
+      static_cast<int64_t>(p.width / p.tile_size) * (p.height / p.tile_size);
+  const float4* rec = reinterpret_cast<const float4*>(records);
+  if (num_tiles > 0 && total > 0) {
+#define GS_LAUNCH(TS)                                                                          \
+  if (p.gaussian_mode)                                                                         \
+    composite_bwd_kernel<TS, BwdPpt<TS>::value, true, true>                                    \
+        <<<static_cast<unsigned>(num_tiles), TileShape<TS, BwdPpt<TS>::value>::kThreads, 0,   \
+           stream>>>(rec, gaussian_ids, ranges, grad_image, final_transmittance,               \
+                     n_contributors, p, rows);                                                 \
+  else                                                                                         \
+    composite_bwd_kernel<TS, BwdPpt<TS>::value, false, true>                                   \
+        <<<static_cast<unsigned>(num_tiles), TileShape<TS, BwdPpt<TS>::value>::kThreads, 0,   \
+           stream>>>(rec, gaussian_ids, ranges, grad_image, final_transmittance,               \
+                     n_contributors, p, rows)
+    GS_TILE_DISPATCH(p.tile_size, GS_LAUNCH)
+#undef GS_LAUNCH
+    GS_TRY(check_launch());
+  }
+  GS_TRY(launch_sort_positions(total, n, gaussian_ids, base + L.sort, order, segments, stream));
+  if (n == 0) return GS_OK;
+  reduce_rows_kernel<<<ceil_div(n, 256), 256, 0, stream>>>(n, order, segments, rows,
+                                                           grad_projected);
   return check_launch();
 }
 

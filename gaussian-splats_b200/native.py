@@ -40,6 +40,8 @@ EXPORTED_SYMBOLS = (
     "gs_bin_noalloc",
     "gs_composite_fwd",
     "gs_composite_bwd",
+    "gs_composite_bwd_deterministic",
+    "gs_composite_bwd_deterministic_workspace_size",
     "gs_project_bwd",
     "gs_project_bwd_views",
     "gs_adam_step",
@@ -223,6 +225,8 @@ def lib() -> ctypes.CDLL:
         "gs_bin_noalloc": ([i64, vp, vp, vp, P, vp, i64, vp, ctypes.POINTER(i64), vp], i32),
         "gs_composite_fwd": ([vp] * 3 + [P] + [vp] * 3 + [vp], i32),
         "gs_composite_bwd": ([i64] + [vp] * 6 + [P, vp, vp], i32),
+        "gs_composite_bwd_deterministic": ([i64, i64] + [vp] * 6 + [P, vp, u64, vp, vp], i32),
+        "gs_composite_bwd_deterministic_workspace_size": ([i64, i64], u64),
         "gs_project_bwd": ([i64, i32] + [vp] * 10 + [P] + [vp] * 5 + [vp], i32),
         "gs_project_bwd_views": ([i64, i32, i32] + [vp] * 13 + [vp], i32),
         "gs_adam_step": ([i64, i32] + [ctypes.POINTER(SplatArrays)] * 4 +

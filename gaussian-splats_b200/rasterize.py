@@ -170,6 +170,17 @@ _PENDING_RECORDS: dict = {}
 _MAX_PENDING_RECORDS = 4
 
 
+def deterministic_backward() -> bool:
+    """Whether the backward uses its order-fixed form (the same gradient bits
+    on every run): with ``GAUSSIAN_SPLATS_B200_DETERMINISTIC=1`` in the
+    environment, or under ``torch.use_deterministic_algorithms(True)``. The
+    default adds each tile's contributions with float atomics, whose order
+    varies from run to run in the last bits (the reference selects between its
+    two forms with GAUSSIAN_SPLATS_ATOMIC_BACKWARD, interface.py:218)."""
+    return (os.environ.get("GAUSSIAN_SPLATS_B200_DETERMINISTIC") == "1"
+            or torch.are_deterministic_algorithms_enabled())
+
+
 def _keep_records(counts: torch.Tensor, records: torch.Tensor) -> None:
     key = (counts.data_ptr(), counts.numel())
     _PENDING_RECORDS.pop(key, None)
@@ -428,10 +439,23 @@ def _backward(ctx, *grad_outputs):
             native.check(lib.gs_pack_records(
                 n, _ptr(projected_mean), _ptr(inverse_covariance), _ptr(projected_color),
                 _ptr(projected_opacity), pref, _ptr(records), stream), "gs_pack_records")
-        native.check(lib.gs_composite_bwd(
-            n, _ptr(records), _ptr(gaussian_ids), _ptr(ranges), _ptr(grad_image),
-            _ptr(final_transmittance), _ptr(n_contributors), pref, _ptr(grad_projected),
-            stream), "gs_composite_bwd")
+        if deterministic_backward():
+            # order-fixed form: the same gradient bits on every run
+            if torch.cuda.is_current_stream_capturing():
+                raise RuntimeError("the deterministic backward runs eagerly (a captured render's "
+                                   "gaussian_ids is longer than its intersection total)")
+            total = gaussian_ids.numel()
+            ws_bytes = lib.gs_composite_bwd_deterministic_workspace_size(n, total)
+            workspace = torch.empty((ws_bytes,), dtype=torch.uint8, device=device)
+            native.check(lib.gs_composite_bwd_deterministic(
+                n, total, _ptr(records), _ptr(gaussian_ids), _ptr(ranges), _ptr(grad_image),
+                _ptr(final_transmittance), _ptr(n_contributors), pref, _ptr(workspace),
+                ws_bytes, _ptr(grad_projected), stream), "gs_composite_bwd_deterministic")
+        else:
+            native.check(lib.gs_composite_bwd(
+                n, _ptr(records), _ptr(gaussian_ids), _ptr(ranges), _ptr(grad_image),
+                _ptr(final_transmittance), _ptr(n_contributors), pref, _ptr(grad_projected),
+                stream), "gs_composite_bwd")
         _mark("composite_bwd")
         # The five gradients are carved out of one buffer (rotation and colour
         # first, keeping their 16-byte rows aligned), so a view-parallel step

@@ -197,6 +197,24 @@ int32_t gs_composite_bwd(int64_t n, const float *records, const int32_t *gaussia
                          const float *final_transmittance, const int32_t *n_contributors,
                          const gs_params *params, float *grad_projected, gs_stream_t stream);
 
+/* The same gradients, the same bits on every run: the reference's
+ * per-intersection form (composite_bwd.py:237-277, its non-atomic default,
+ * interface.py:218) made order-fixed. Each tile writes one 9-float row per
+ * list position (its warps' contributions added in warp order), the positions
+ * are grouped by Gaussian with a stable sort, and each Gaussian's rows are
+ * added in list order -- no float addition depends on scheduling. `total` is
+ * the length of gaussian_ids (every entry a valid index); the workspace holds
+ * gs_composite_bwd_deterministic_workspace_size(n, total) bytes, 256-byte
+ * aligned (rows, order, segments and the sort's scratch). Writes
+ * grad_projected [N,9] (no zeroing needed). */
+uint64_t gs_composite_bwd_deterministic_workspace_size(int64_t n, int64_t total);
+int32_t gs_composite_bwd_deterministic(int64_t n, int64_t total, const float *records,
+                                       const int32_t *gaussian_ids, const int64_t *ranges,
+                                       const float *grad_image, const float *final_transmittance,
+                                       const int32_t *n_contributors, const gs_params *params,
+                                       void *workspace, uint64_t workspace_bytes,
+                                       float *grad_projected, gs_stream_t stream);
+
 /* Parameter gradients: replaces _project_bwd_kernel (project_bwd.py:8-381).
  * SH gradients cover all K coefficients: degree 4 (K = 25) differentiates the
  * forward basis, where the reference's backward stops at 16 (project_bwd.py:33). */
