@@ -473,7 +473,12 @@ __global__ void __launch_bounds__(TileShape<TS, PPT>::kThreads,
         active = true;
         const float4 c = cur.c[j];
         const float denominator = fmaxf(st[q] * (1.0f - alpha), 1e-4f);
-        const float forward = t_final[q] / denominator;
+        // T in front of the entry. The quotient only feeds gradients and the
+        // termination re-test of the gradient path (tolerance-checked), so it
+        // takes the approximate divide (<= 2 ulp, as a Triton fp32 `/` without
+        // IEEE rounding does on the reference's GPU path) instead of the
+        // IEEE one's ~10 instructions; denominator >= 1e-4 keeps it in range.
+        const float forward = __fdividef(t_final[q], denominator);
         const bool still = (1.0f - forward) < threshold;
         // Gradient arithmetic (tolerance-checked, unlike the decisions above)
         // contracts multiply-adds explicitly.
