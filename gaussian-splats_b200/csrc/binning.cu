@@ -278,7 +278,7 @@ __device__ __forceinline__ unsigned match_digit(int d) {
 
 // One stable LSD pass over 8 bits at `shift`.
 template <class Source>
-__global__ void __launch_bounds__(kThreads, 3) sort_pass_kernel(
+__global__ void __launch_bounds__(kThreads, 4) sort_pass_kernel(
     Source src, Count count, int shift, const uint32_t* __restrict__ pass_hist,
     uint32_t* __restrict__ status, uint32_t* __restrict__ tile_counter,
     uint32_t* __restrict__ keys_out, uint32_t* __restrict__ values_out,
@@ -301,21 +301,23 @@ __global__ void __launch_bounds__(kThreads, 3) sort_pass_kernel(
   if (tile_start >= n) return;  // uniform: every later tile is empty too
 
   // Rank: warp w owns keys [w*512, w*512+512) of the tile, 32 per step in
-  // order, so (step, lane) order is input order and ranks are stable.
-  uint32_t keys[kItems], values[kItems], ranks[kItems];
-  int digits[kItems];
+  // order, so (step, lane) order is input order and ranks are stable. Only
+  // the keys are held while ranking (the values are read when they are
+  // scattered), which keeps the pass at 64 registers and four CTAs per SM.
+  uint32_t keys[kItems], ranks[kItems];
+  uint32_t valid = 0;  // bit j: element j of this thread exists (and passes the filter)
   const unsigned lt = lanemask_lt();
+  const int64_t thread_first = tile_start + warp * (kItems * 32) + lane;
 #pragma unroll
   for (int j = 0; j < kItems; ++j) {
-    const int64_t idx = tile_start + warp * (kItems * 32) + j * 32 + lane;
+    const int64_t idx = thread_first + j * 32;
     const bool ok = idx < n && src.valid(idx);
     keys[j] = ok ? src.key(idx) : 0u;
-    values[j] = ok ? src.value(idx) : 0u;
-    digits[j] = ok ? static_cast<int>((keys[j] >> shift) & 0xFF) : kRadix;
+    valid |= ok ? (1u << j) : 0u;
   }
 #pragma unroll
   for (int j = 0; j < kItems; ++j) {
-    const int d = digits[j];
+    const int d = (valid >> j) & 1u ? static_cast<int>((keys[j] >> shift) & 0xFF) : kRadix;
     const unsigned peers = match_digit(d);
     const int leader = __ffs(peers) - 1;
     uint32_t base = 0;
@@ -354,11 +356,11 @@ __global__ void __launch_bounds__(kThreads, 3) sort_pass_kernel(
   // Reorder the tile in shared memory by digit, then write runs coalesced.
 #pragma unroll
   for (int j = 0; j < kItems; ++j) {
-    const int dj = digits[j];
-    if (dj < kRadix) {
+    if ((valid >> j) & 1u) {
+      const int dj = static_cast<int>((keys[j] >> shift) & 0xFF);
       const uint32_t pos = s_local_start[dj] + s_warp_hist[warp][dj] + ranks[j];
       s_keys[pos] = keys[j];
-      s_values[pos] = values[j];
+      s_values[pos] = src.value(thread_first + j * 32);
     }
   }
   __syncthreads();
