@@ -80,6 +80,92 @@ __device__ __forceinline__ void prefetch_l2(const void* ptr, uint64_t bytes) {
   }
 }
 
+// Asynchronous global -> shared copies (cp.async): 16 bytes at L2 only, or 4
+// bytes through L1. A thread's copies complete at cp_async_wait_*; a CTA
+// barrier after that makes every thread's copies visible.
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const uint32_t dst = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
+  const uint32_t dst = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+}
+// Waits for all but the most recently committed group.
+__device__ __forceinline__ void cp_async_wait_all_but_last() {
+  asm volatile("cp.async.wait_group 1;" ::: "memory");
+}
+
+// Starts copying rows [0, rows) of a row-major float array (kRow floats a
+// row, `src` at row 0) into shared memory at kPitch floats a row (kPitch >
+// kRow pads rows so that lanes reading consecutive rows hit distinct banks).
+// The copies are spread over the CTA's kThreads threads in address order, so
+// each warp's requests are coalesced; a CTA's block of Gaussian rows is one
+// contiguous range of every parameter array. 16-byte copies when the source
+// block starts on a 16-byte boundary, is a whole number of 16-byte words and
+// no word straddles two rows of a padded layout (dst 16-byte aligned, kPitch
+// a multiple of 4 when padded); 4-byte copies otherwise (a ragged last block
+// or an unaligned caller tensor). Only addresses inside the block are read.
+template <int kRow, int kPitch, int kThreads>
+__device__ __forceinline__ void stage_rows_async(float* dst, const float* src, int rows, int tid) {
+  static_assert(kPitch == kRow || (kRow % 4 == 0 && kPitch % 4 == 0), "padded rows of 16-byte words");
+  const int words = rows * kRow;
+  const bool vec = (reinterpret_cast<uint64_t>(src) & 15) == 0 && (words & 3) == 0;
+  if (vec) {
+    for (int q = tid; q < words / 4; q += kThreads) {
+      int d = 4 * q;
+      if constexpr (kPitch != kRow) {
+        const int r = q / (kRow / 4);
+        d = r * kPitch + 4 * (q - r * (kRow / 4));
+      }
+      cp_async16(dst + d, src + 4 * q);
+    }
+  } else {
+    for (int w = tid; w < words; w += kThreads) {
+      int d = w;
+      if constexpr (kPitch != kRow) {
+        const int r = w / kRow;
+        d = r * kPitch + (w - r * kRow);
+      }
+      cp_async4(dst + d, src + w);
+    }
+  }
+}
+
+// Shared-memory pitch (floats) of a CTA's staged SH rows (3K floats each):
+// rows of an even number of 16-byte words are padded by one word, so the 8
+// lanes of a quarter-warp reading word j of consecutive rows touch 8
+// distinct 4-bank groups (an odd word stride); other rows are read as
+// scalars at an odd stride or as 16-byte words at an odd word stride already.
+template <int K>
+struct ShPitch {
+  static constexpr int kRow = 3 * K;
+  static constexpr int value = (kRow % 4 == 0 && (kRow / 4) % 2 == 0) ? kRow + 4 : kRow;
+};
+
+// Loads the 3K SH coefficients of one Gaussian from its staged shared-memory
+// row (16-byte words when the row is made of them, scalars otherwise).
+template <int K>
+__device__ __forceinline__ void load_sh_shared(const float* row, float (&c)[K * 3]) {
+  if constexpr ((K * 3) % 4 == 0) {
+    const float4* v = reinterpret_cast<const float4*>(row);
+#pragma unroll
+    for (int j = 0; j < K * 3 / 4; ++j) {
+      const float4 q = v[j];
+      c[4 * j] = q.x; c[4 * j + 1] = q.y; c[4 * j + 2] = q.z; c[4 * j + 3] = q.w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < K * 3; ++j) c[j] = row[j];
+  }
+}
+
 // Prefetches a CTA's rows [first, first + rows) of the Gaussian parameter
 // arrays (mean, rotation, scale, opacity, K SH coefficients) into L2.
 __device__ __forceinline__ void prefetch_gaussian_rows(int64_t first, int64_t rows, int k,

@@ -116,17 +116,6 @@ struct StageBuffer {
   float4 a[NB], b[NB], c[NB], box[NB];
 };
 
-__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
-  const uint32_t dst = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(gmem) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() {
-  asm volatile("cp.async.commit_group;" ::: "memory");
-}
-__device__ __forceinline__ void cp_async_wait_all() {
-  asm volatile("cp.async.wait_group 0;" ::: "memory");
-}
-
 // Starts copying Gaussian g's record into `slot` of `buf`.
 template <int NB>
 __device__ __forceinline__ void stage_async(const float4* __restrict__ records, int32_t g,

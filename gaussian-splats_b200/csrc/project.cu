@@ -218,8 +218,26 @@ __device__ __forceinline__ void project_view(
                                          red, green, blue, p));
 }
 
+// A CTA's Gaussian rows as project_fwd_kernel stages them in shared memory.
+constexpr int kProjectThreads = 128;
 template <int K>
-__global__ void __launch_bounds__(256) project_fwd_kernel(
+struct FwdRows {
+  float sh[kProjectThreads * ShPitch<K>::value];
+  float4 rotation[kProjectThreads];
+  float mean[kProjectThreads * 3];
+  float scale[kProjectThreads * 3];
+  float opacity[kProjectThreads];
+};
+
+// One thread per Gaussian, 128 per CTA. The CTA's rows of the five parameter
+// arrays are contiguous ranges, so they are staged into shared memory with
+// coalesced asynchronous copies issued all at once -- about 30 KB per CTA
+// in flight without holding a register, which a thread's own dependent loads
+// could not keep up -- the geometry's rows first (their own copy group, so
+// the covariance starts while the SH rows are still arriving), then the SH
+// rows.
+template <int K>
+__global__ void __launch_bounds__(kProjectThreads) project_fwd_kernel(
     int64_t n, const float* __restrict__ mean, const float* __restrict__ rotation,
     const float* __restrict__ scale, const float* __restrict__ opacity,
     const float* __restrict__ color, const float* __restrict__ camera_rotation,
@@ -227,15 +245,24 @@ __global__ void __launch_bounds__(256) project_fwd_kernel(
     float* __restrict__ projected_mean, float* __restrict__ inverse_covariance,
     float* __restrict__ projected_color, float* __restrict__ projected_opacity,
     int4* __restrict__ bounds, int32_t* __restrict__ counts, float4* __restrict__ records) {
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (i >= n) return;
-  if (threadIdx.x == 0) {
-    const int64_t first = static_cast<int64_t>(blockIdx.x) * blockDim.x;
-    prefetch_gaussian_rows(first, n - first < blockDim.x ? n - first : blockDim.x, K, mean,
-                           rotation, scale, opacity, color);
-  }
+  constexpr int kPitch = ShPitch<K>::value;
+  __shared__ __align__(16) FwdRows<K> s;
+  const int tid = threadIdx.x;
+  const int64_t first = static_cast<int64_t>(blockIdx.x) * kProjectThreads;
+  const int rows = n - first < kProjectThreads ? static_cast<int>(n - first) : kProjectThreads;
+  stage_rows_async<3, 3, kProjectThreads>(s.mean, mean + 3 * first, rows, tid);
+  stage_rows_async<4, 4, kProjectThreads>(&s.rotation[0].x, rotation + 4 * first, rows, tid);
+  stage_rows_async<3, 3, kProjectThreads>(s.scale, scale + 3 * first, rows, tid);
+  stage_rows_async<1, 1, kProjectThreads>(s.opacity, opacity + first, rows, tid);
+  cp_async_commit();
+  stage_rows_async<3 * K, kPitch, kProjectThreads>(s.sh, color + first * (3 * K), rows, tid);
+  cp_async_commit();
   const Camera c = load_camera(camera_rotation, camera_translation);
-  const float mx = __ldg(mean + 3 * i), my = __ldg(mean + 3 * i + 1), mz = __ldg(mean + 3 * i + 2);
+  cp_async_wait_all_but_last();
+  __syncthreads();
+  const bool live = tid < rows;  // every thread stays for the second barrier
+  const int64_t i = first + tid;
+  const float mx = s.mean[3 * tid], my = s.mean[3 * tid + 1], mz = s.mean[3 * tid + 2];
   // project.py:126-142
   const float camera_x = mx * c.r00 + my * c.r01 + mz * c.r02 + c.tx;
   const float camera_y = mx * c.r10 + my * c.r11 + mz * c.r12 + c.ty;
@@ -244,11 +271,13 @@ __global__ void __launch_bounds__(256) project_fwd_kernel(
   const float safe_z = depth > 0.0f ? fmaxf(1e-4f, depth) : fminf(-1e-4f, depth);
   const float pixel_x = p.fx * camera_x / safe_z + p.cx;
   const float pixel_y = -p.fy * camera_y / safe_z + p.cy;
-  projected_mean[3 * i] = pixel_x;
-  projected_mean[3 * i + 1] = pixel_y;
-  projected_mean[3 * i + 2] = safe_z;
+  if (live) {
+    projected_mean[3 * i] = pixel_x;
+    projected_mean[3 * i + 1] = pixel_y;
+    projected_mean[3 * i + 2] = safe_z;
+  }
   // project.py:144-156
-  const float4 q4 = __ldg(reinterpret_cast<const float4*>(rotation) + i);
+  const float4 q4 = s.rotation[tid];
   float qw = q4.x, qx = q4.y, qy = q4.z, qz = q4.w;
   const float inverse_norm = det_rsqrt(qw * qw + qx * qx + qy * qy + qz * qz);
   qw = qw * inverse_norm; qx = qx * inverse_norm; qy = qy * inverse_norm; qz = qz * inverse_norm;
@@ -265,8 +294,8 @@ __global__ void __launch_bounds__(256) project_fwd_kernel(
   const float jc10 = j11 * c.r10 + j12 * c.r20, jc11 = j11 * c.r11 + j12 * c.r21,
               jc12 = j11 * c.r12 + j12 * c.r22;
   // project.py:177-218
-  const float sx = det_exp(__ldg(scale + 3 * i)), sy = det_exp(__ldg(scale + 3 * i + 1)),
-              sz = det_exp(__ldg(scale + 3 * i + 2));
+  const float sx = det_exp(s.scale[3 * tid]), sy = det_exp(s.scale[3 * tid + 1]),
+              sz = det_exp(s.scale[3 * tid + 2]);
   const float a0x = (1.0f - 2.0f * (qy * qy + qz * qz)) * sx;
   const float a0y = (2.0f * (qx * qy + qw * qz)) * sx;
   const float a0z = (2.0f * (qx * qz - qw * qy)) * sx;
@@ -288,7 +317,29 @@ __global__ void __launch_bounds__(256) project_fwd_kernel(
   const float determinant = cov00 * cov11 - cov01 * cov01;
   const float conic_xy = -cov01 / determinant;
   const float4 conic = make_float4(cov11 / determinant, conic_xy, conic_xy, cov00 / determinant);
-  reinterpret_cast<float4*>(inverse_covariance)[i] = conic;
+  if (live) reinterpret_cast<float4*>(inverse_covariance)[i] = conic;
+  // project.py:230-253
+  const float o = det_sigmoid(s.opacity[tid]);
+  const float radius_extent = p.gaussian_mode ? 2.0f * sqrtf(det_log(o * 255.0f)) : p.extent;
+  const float radius_x = radius_extent * sqrtf(cov00);
+  const float radius_y = radius_extent * sqrtf(cov11);
+  const float ts = static_cast<float>(p.tile_size);
+  const float tiles_w = static_cast<float>(p.width / p.tile_size);
+  const float tiles_h = static_cast<float>(p.height / p.tile_size);
+  // tl.clamp (max then min); a NaN radius clamps to 0.
+  const float tmin_x = fminf(fmaxf(floorf((pixel_x - radius_x) / ts), 0.0f), tiles_w);
+  const float tmin_y = fminf(fmaxf(floorf((pixel_y - radius_y) / ts), 0.0f), tiles_h);
+  const float tmax_x = fminf(fmaxf(floorf((pixel_x + radius_x) / ts) + 1.0f, 0.0f), tiles_w);
+  const float tmax_y = fminf(fmaxf(floorf((pixel_y + radius_y) / ts) + 1.0f, 0.0f), tiles_h);
+  const float count = (tmax_x - tmin_x) * (tmax_y - tmin_y);
+  const int32_t visible_count =
+      (safe_z > p.near_plane && safe_z < p.far_plane) ? static_cast<int32_t>(count) : 0;
+  if (live) {
+    projected_opacity[i] = o;
+    bounds[i] = make_int4(static_cast<int>(tmin_x), static_cast<int>(tmax_x),
+                          static_cast<int>(tmin_y), static_cast<int>(tmax_y));
+    counts[i] = visible_count;
+  }
   // project.py:221-228, _evaluate_sh (project.py:10-71)
   float dx = mx + c.r00 * c.tx + c.r10 * c.ty + c.r20 * c.tz;
   float dy = my + c.r01 * c.tx + c.r11 * c.ty + c.r21 * c.tz;
@@ -296,8 +347,11 @@ __global__ void __launch_bounds__(256) project_fwd_kernel(
   const float direction_norm = det_rsqrt(dx * dx + dy * dy + dz * dz);
   dx = dx * direction_norm; dy = dy * direction_norm; dz = dz * direction_norm;
   const float xx = dx * dx, yy = dy * dy, zz = dz * dz;
+  cp_async_wait_all();
+  __syncthreads();
+  if (!live) return;
   float coefficients[K * 3];
-  load_sh<K>(color + i * (K * 3), coefficients);
+  load_sh_shared<K>(s.sh + tid * kPitch, coefficients);
   float acc_r = 0.0f, acc_g = 0.0f, acc_b = 0.0f;
 #pragma unroll
   for (int k = 0; k < K; ++k) {
@@ -311,26 +365,6 @@ __global__ void __launch_bounds__(256) project_fwd_kernel(
   projected_color[3 * i] = red;
   projected_color[3 * i + 1] = green;
   projected_color[3 * i + 2] = blue;
-  // project.py:230-253
-  const float o = det_sigmoid(__ldg(opacity + i));
-  projected_opacity[i] = o;
-  const float radius_extent = p.gaussian_mode ? 2.0f * sqrtf(det_log(o * 255.0f)) : p.extent;
-  const float radius_x = radius_extent * sqrtf(cov00);
-  const float radius_y = radius_extent * sqrtf(cov11);
-  const float ts = static_cast<float>(p.tile_size);
-  const float tiles_w = static_cast<float>(p.width / p.tile_size);
-  const float tiles_h = static_cast<float>(p.height / p.tile_size);
-  // tl.clamp (max then min); a NaN radius clamps to 0.
-  const float tmin_x = fminf(fmaxf(floorf((pixel_x - radius_x) / ts), 0.0f), tiles_w);
-  const float tmin_y = fminf(fmaxf(floorf((pixel_y - radius_y) / ts), 0.0f), tiles_h);
-  const float tmax_x = fminf(fmaxf(floorf((pixel_x + radius_x) / ts) + 1.0f, 0.0f), tiles_w);
-  const float tmax_y = fminf(fmaxf(floorf((pixel_y + radius_y) / ts) + 1.0f, 0.0f), tiles_h);
-  bounds[i] = make_int4(static_cast<int>(tmin_x), static_cast<int>(tmax_x),
-                        static_cast<int>(tmin_y), static_cast<int>(tmax_y));
-  const float count = (tmax_x - tmin_x) * (tmax_y - tmin_y);
-  const int32_t visible_count =
-      (safe_z > p.near_plane && safe_z < p.far_plane) ? static_cast<int32_t>(count) : 0;
-  counts[i] = visible_count;
   // the compositors' staged form; Gaussians in no tile are never staged
   if (records != nullptr && visible_count > 0)
     store_record(records, i, make_record(static_cast<int32_t>(i), pixel_x, pixel_y, conic, o,
@@ -417,48 +451,60 @@ struct BwdTerms {
   float sx, sy, sz, po;
 };
 
-__device__ __forceinline__ BwdTerms bwd_terms(int64_t i, const float* __restrict__ mean,
-                                              const float* __restrict__ rotation,
-                                              const float* __restrict__ scale,
-                                              const float* __restrict__ opacity) {
+__device__ __forceinline__ BwdTerms bwd_terms_of(float mx, float my, float mz, float4 q4,
+                                                 float log_sx, float log_sy, float log_sz,
+                                                 float logit) {
   BwdTerms b;
-  b.mx = __ldg(mean + 3 * i);
-  b.my = __ldg(mean + 3 * i + 1);
-  b.mz = __ldg(mean + 3 * i + 2);
-  const float4 q4 = __ldg(reinterpret_cast<const float4*>(rotation) + i);
+  b.mx = mx;
+  b.my = my;
+  b.mz = mz;
   const float qnorm = sqrtf(q4.x * q4.x + q4.y * q4.y + q4.z * q4.z + q4.w * q4.w);
   b.inverse_qnorm = 1.0f / qnorm;
   b.qw = q4.x * b.inverse_qnorm;
   b.qx = q4.y * b.inverse_qnorm;
   b.qy = q4.z * b.inverse_qnorm;
   b.qz = q4.w * b.inverse_qnorm;
-  b.sx = det_exp(__ldg(scale + 3 * i));
-  b.sy = det_exp(__ldg(scale + 3 * i + 1));
-  b.sz = det_exp(__ldg(scale + 3 * i + 2));
-  b.po = det_sigmoid(__ldg(opacity + i));
+  b.sx = det_exp(log_sx);
+  b.sy = det_exp(log_sy);
+  b.sz = det_exp(log_sz);
+  b.po = det_sigmoid(logit);
   return b;
+}
+
+__device__ __forceinline__ BwdTerms bwd_terms(int64_t i, const float* __restrict__ mean,
+                                              const float* __restrict__ rotation,
+                                              const float* __restrict__ scale,
+                                              const float* __restrict__ opacity) {
+  return bwd_terms_of(__ldg(mean + 3 * i), __ldg(mean + 3 * i + 1), __ldg(mean + 3 * i + 2),
+                      __ldg(reinterpret_cast<const float4*>(rotation) + i),
+                      __ldg(scale + 3 * i), __ldg(scale + 3 * i + 1), __ldg(scale + 3 * i + 2),
+                      __ldg(opacity + i));
 }
 
 // Gradients of one Gaussian's parameters from its screen-space gradient in
 // one view (project_bwd.py:8-334), handed to `sink`: sink.color(g[3K]) with
 // the SH coefficient gradients, then sink.rest(mean xyz, rotation, scale xyz,
-// opacity). `b` holds the Gaussian's view-independent terms, `inv` is the
-// view's conic as the forward computed it and `gp` the view's 9-float
-// screen-space gradient of the Gaussian.
+// opacity). `b` holds the Gaussian's view-independent terms, `sh_row` its
+// 3K SH coefficients (global memory, or a staged shared-memory row with
+// kShShared), `inv` is the view's conic as the forward computed it and `gp`
+// the view's 9-float screen-space gradient of the Gaussian.
 // How a view's screen-space gradient is read: through the read-only cache
 // (written on this GPU by an earlier kernel), or at L2 only (written by
-// another GPU, behind a flag).
+// another GPU, behind a flag), or from a row staged in shared memory.
 struct LoadReadOnly {
   static __device__ __forceinline__ float get(const float* p) { return __ldg(p); }
+};
+struct LoadShared {
+  static __device__ __forceinline__ float get(const float* p) { return *p; }
 };
 struct LoadPeer {
   static __device__ __forceinline__ float get(const float* p) { return __ldcg(p); }
 };
 
-template <int K, class Sink, class Load = LoadReadOnly>
+template <int K, class Sink, class Load = LoadReadOnly, bool kShShared = false>
 __device__ __forceinline__ void project_bwd_view(
-    int64_t i, bool visible, const Camera& c, const gs_params& p, const BwdTerms& b,
-    const float* __restrict__ color, float4 inv, const float* __restrict__ gp, Sink& sink) {
+    bool visible, const Camera& c, const gs_params& p, const BwdTerms& b,
+    const float* __restrict__ sh_row, float4 inv, const float* __restrict__ gp, Sink& sink) {
   // SH coefficients with a gradient: all K. The reference's backward stops at 16
   // (project_bwd.py:33); degree 4 is carried through here.
   constexpr int KB = K;
@@ -655,7 +701,10 @@ __device__ __forceinline__ void project_bwd_view(
     dby[24] = 2.5033429417967046f * y * (yy - 3.0f * xx);
   }
   float coefficients[K * 3];
-  load_sh<K>(color + i * (K * 3), coefficients);
+  if constexpr (kShShared)
+    load_sh_shared<K>(sh_row, coefficients);
+  else
+    load_sh<K>(sh_row, coefficients);
   float gc3[3];
   float gdx = 0.0f, gdy = 0.0f, gdz = 0.0f;
 #pragma unroll
@@ -830,7 +879,7 @@ __global__ void __launch_bounds__(128, K > 16 ? 3 : 4) project_bwd_views_kernel(
     const Camera c{R[0], R[1], R[2], R[3], R[4], R[5], R[6], R[7], R[8], t[0], t[1], t[2]};
     const float4 inv = view_conic(g, c, p);
     project_bwd_view<K, SharedAccumulateGradients<K>, typename Source::Load>(
-        i, true, c, p, b, color, inv, src.grad(v, i), acc);
+        true, c, p, b, color + i * (K * 3), inv, src.grad(v, i), acc);
   }
   float sum[K * 3];
 #pragma unroll
@@ -840,8 +889,95 @@ __global__ void __launch_bounds__(128, K > 16 ? 3 : 4) project_bwd_views_kernel(
   out.rest(acc.m[0], acc.m[1], acc.m[2], acc.r, acc.s[0], acc.s[1], acc.s[2], acc.o);
 }
 
+// Threads (one per Gaussian) of a project_bwd_kernel CTA: its staged rows
+// stay within 48 KB of static shared memory.
+constexpr int project_bwd_threads(int k) { return k > 16 ? 64 : 128; }
+
+// A CTA's rows of every input of the single-view backward, staged in shared
+// memory; the SH rows are overwritten in place by their gradients.
+template <int K, int T>
+struct BwdRows {
+  float sh[T * ShPitch<K>::value];
+  float4 rotation[T];
+  float4 conic[T];
+  float mean[T * 3];
+  float scale[T * 3];
+  float grad[T * 9];
+  float opacity[T];
+  int32_t counts[T];
+};
+
+// Sink of the staged backward: the SH gradients replace the thread's own SH
+// row in shared memory (the CTA writes them out together, coalesced), the
+// rest goes straight to global memory.
 template <int K>
-__global__ void __launch_bounds__(128) project_bwd_kernel(
+struct StagedStoreGradients {
+  int64_t i;
+  float* row;
+  float *grad_mean, *grad_rotation, *grad_scale, *grad_opacity;
+  __device__ __forceinline__ void color(const float (&g)[K * 3]) {
+    if constexpr ((K * 3) % 4 == 0) {
+      float4* v = reinterpret_cast<float4*>(row);
+#pragma unroll
+      for (int j = 0; j < K * 3 / 4; ++j)
+        v[j] = make_float4(g[4 * j], g[4 * j + 1], g[4 * j + 2], g[4 * j + 3]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < K * 3; ++j) row[j] = g[j];
+    }
+  }
+  __device__ __forceinline__ void rest(float gmx, float gmy, float gmz, float4 grot, float gsx,
+                                       float gsy, float gsz, float go) {
+    grad_mean[3 * i] = gmx;
+    grad_mean[3 * i + 1] = gmy;
+    grad_mean[3 * i + 2] = gmz;
+    reinterpret_cast<float4*>(grad_rotation)[i] = grot;
+    grad_scale[3 * i] = gsx;
+    grad_scale[3 * i + 1] = gsy;
+    grad_scale[3 * i + 2] = gsz;
+    grad_opacity[i] = go;
+  }
+};
+
+// Writes rows [0, rows) staged at kPitch floats a row back to a row-major
+// global array of kRow floats a row, spread over the CTA's threads in global
+// address order (16-byte stores where the block allows, as in
+// stage_rows_async).
+template <int kRow, int kPitch, int kThreads>
+__device__ __forceinline__ void store_rows(float* __restrict__ dst, const float* src, int rows,
+                                           int tid) {
+  const int words = rows * kRow;
+  const bool vec = (reinterpret_cast<uint64_t>(dst) & 15) == 0 && (words & 3) == 0 &&
+                   (kPitch == kRow || kRow % 4 == 0);
+  if (vec) {
+    for (int q = tid; q < words / 4; q += kThreads) {
+      int d = 4 * q;
+      if constexpr (kPitch != kRow) {
+        const int r = q / (kRow / 4);
+        d = r * kPitch + 4 * (q - r * (kRow / 4));
+      }
+      reinterpret_cast<float4*>(dst)[q] = *reinterpret_cast<const float4*>(src + d);
+    }
+  } else {
+    for (int w = tid; w < words; w += kThreads) {
+      int d = w;
+      if constexpr (kPitch != kRow) {
+        const int r = w / kRow;
+        d = r * kPitch + (w - r * kRow);
+      }
+      dst[w] = src[d];
+    }
+  }
+}
+
+// Single-view projection backward, one thread per Gaussian. As in the
+// forward, the CTA stages its contiguous block of every input (parameters,
+// conic, screen-space gradient, count: 292 bytes a Gaussian at SH degree 3)
+// into shared memory with coalesced asynchronous copies issued at once, and
+// the SH gradients (the bulk of the writes) leave through shared memory as
+// coalesced 16-byte stores.
+template <int K>
+__global__ void __launch_bounds__(project_bwd_threads(K)) project_bwd_kernel(
     int64_t n, const float* __restrict__ mean, const float* __restrict__ rotation,
     const float* __restrict__ scale, const float* __restrict__ opacity,
     const float* __restrict__ color, const float* __restrict__ camera_rotation,
@@ -850,22 +986,37 @@ __global__ void __launch_bounds__(128) project_bwd_kernel(
     const gs_params p, float* __restrict__ grad_mean, float* __restrict__ grad_rotation,
     float* __restrict__ grad_scale, float* __restrict__ grad_opacity,
     float* __restrict__ grad_color) {
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (i >= n) return;
-  if (threadIdx.x == 0) {
-    const int64_t first = static_cast<int64_t>(blockIdx.x) * blockDim.x;
-    const int64_t rows = n - first < blockDim.x ? n - first : blockDim.x;
-    prefetch_gaussian_rows(first, rows, K, mean, rotation, scale, opacity, color);
-    prefetch_l2(inverse_covariance + 4 * first, 16 * static_cast<uint64_t>(rows));
-    prefetch_l2(grad_projected + 9 * first, 36 * static_cast<uint64_t>(rows));
-    prefetch_l2(counts + first, 4 * static_cast<uint64_t>(rows));
-  }
-  const bool visible = __ldg(counts + i) != 0;
+  constexpr int T = project_bwd_threads(K);
+  constexpr int kPitch = ShPitch<K>::value;
+  __shared__ __align__(16) BwdRows<K, T> s;
+  const int tid = threadIdx.x;
+  const int64_t first = static_cast<int64_t>(blockIdx.x) * T;
+  const int rows = n - first < T ? static_cast<int>(n - first) : T;
+  stage_rows_async<3 * K, kPitch, T>(s.sh, color + first * (3 * K), rows, tid);
+  stage_rows_async<4, 4, T>(&s.rotation[0].x, rotation + 4 * first, rows, tid);
+  stage_rows_async<4, 4, T>(&s.conic[0].x, inverse_covariance + 4 * first, rows, tid);
+  stage_rows_async<3, 3, T>(s.mean, mean + 3 * first, rows, tid);
+  stage_rows_async<3, 3, T>(s.scale, scale + 3 * first, rows, tid);
+  stage_rows_async<9, 9, T>(s.grad, grad_projected + 9 * first, rows, tid);
+  stage_rows_async<1, 1, T>(s.opacity, opacity + first, rows, tid);
+  stage_rows_async<1, 1, T>(reinterpret_cast<float*>(s.counts),
+                            reinterpret_cast<const float*>(counts + first), rows, tid);
+  cp_async_commit();
   const Camera c = load_camera(camera_rotation, camera_translation);
-  const float4 inv = __ldg(reinterpret_cast<const float4*>(inverse_covariance) + i);
-  StoreGradients<K> sink{i, grad_mean, grad_rotation, grad_scale, grad_opacity, grad_color};
-  project_bwd_view<K>(i, visible, c, p, bwd_terms(i, mean, rotation, scale, opacity), color,
-                      inv, grad_projected + 9 * i, sink);
+  cp_async_wait_all();
+  __syncthreads();
+  if (tid < rows) {
+    const int64_t i = first + tid;
+    const BwdTerms b = bwd_terms_of(s.mean[3 * tid], s.mean[3 * tid + 1], s.mean[3 * tid + 2],
+                                    s.rotation[tid], s.scale[3 * tid], s.scale[3 * tid + 1],
+                                    s.scale[3 * tid + 2], s.opacity[tid]);
+    float* row = s.sh + tid * kPitch;
+    StagedStoreGradients<K> sink{i, row, grad_mean, grad_rotation, grad_scale, grad_opacity};
+    project_bwd_view<K, StagedStoreGradients<K>, LoadShared, true>(
+        s.counts[tid] != 0, c, p, b, row, s.conic[tid], s.grad + 9 * tid, sink);
+  }
+  __syncthreads();
+  store_rows<3 * K, kPitch, T>(grad_color + first * (3 * K), s.sh, rows, tid);
 }
 
 }  // namespace
@@ -887,9 +1038,9 @@ int32_t launch_project_fwd(int64_t n, int32_t num_sh, const float* mean, const f
                            float* projected_color, float* projected_opacity, int32_t* bounds,
                            int32_t* counts, float* records, cudaStream_t stream) {
   if (n == 0) return GS_OK;
-  const unsigned blocks = ceil_div(n, 256);
+  const unsigned blocks = ceil_div(n, kProjectThreads);
 #define GS_LAUNCH(K)                                                                          \
-  project_fwd_kernel<K><<<blocks, 256, 0, stream>>>(                                          \
+  project_fwd_kernel<K><<<blocks, kProjectThreads, 0, stream>>>(                                          \
       n, mean, rotation, scale, opacity, color, camera_rotation, camera_translation, p,       \
       projected_mean, inverse_covariance, projected_color, projected_opacity,                 \
       reinterpret_cast<int4*>(bounds), counts, reinterpret_cast<float4*>(records))
@@ -982,9 +1133,9 @@ int32_t launch_project_bwd(int64_t n, int32_t num_sh, const float* mean, const f
                            float* grad_rotation, float* grad_scale, float* grad_opacity,
                            float* grad_color, cudaStream_t stream) {
   if (n == 0) return GS_OK;
-  const unsigned blocks = ceil_div(n, 128);
 #define GS_LAUNCH(K)                                                                          \
-  project_bwd_kernel<K><<<blocks, 128, 0, stream>>>(                                          \
+  project_bwd_kernel<K><<<ceil_div(n, project_bwd_threads(K)), project_bwd_threads(K), 0,       \
+                          stream>>>(                                          \
       n, mean, rotation, scale, opacity, color, camera_rotation, camera_translation,           \
       inverse_covariance, grad_projected, counts, p, grad_mean, grad_rotation, grad_scale,    \
       grad_opacity, grad_color)
