@@ -296,18 +296,28 @@ def kernel_durations(outputs, params, camera, grad_image, settings, device, repe
     native.check(lib.gs_pack_records(n, P(pmean), P(conic), P(pcolor), P(popacity), pref,
                                      P(records), stream), "gs_pack_records")
     out_records = torch.empty_like(records)
+    # the compositors' heavy-first tile orders, as the operator computes them per view
+    fwd_order = torch.empty((ranges.shape[0],), dtype=torch.int32, device=device)
+    bwd_order = torch.empty_like(fwd_order)
+    tile_work = torch.empty_like(fwd_order)
+    native.check(lib.gs_tile_order(P(ranges), None, pref, P(fwd_order), None, stream),
+                 "gs_tile_order")
+    if grad_image is not None:
+        native.check(lib.gs_tile_order(P(ranges), P(n_contrib), pref, P(bwd_order),
+                                       P(tile_work), stream), "gs_tile_order")
     launches = {
         "project_fwd": lambda: lib.gs_project_fwd(
             n, k, P(mean), P(rotation), P(scale), P(opacity), P(color), P(cam_r), P(cam_t), pref,
             P(out_pm), P(out_conic), P(out_rgb), P(out_o), P(bounds), P(out_counts),
             P(out_records), stream),
         "composite_fwd": lambda: lib.gs_composite_fwd(
-            P(records), P(ids), P(ranges), pref, P(out_img), P(out_t), P(out_nc), stream),
+            P(records), P(ids), P(ranges), pref, P(out_img), P(out_t), P(out_nc), P(fwd_order),
+            stream),
     }
     if grad_image is not None:
         launches["composite_bwd"] = lambda: lib.gs_composite_bwd(
             n, P(records), P(ids), P(ranges), P(grad_image), P(final_t), P(n_contrib), pref,
-            P(grad_projected), stream)
+            P(grad_projected), P(bwd_order), stream)
         launches["project_bwd"] = lambda: lib.gs_project_bwd(
             n, k, P(mean), P(rotation), P(scale), P(opacity), P(color), P(cam_r), P(cam_t),
             P(conic), P(grad_projected), P(counts), pref, *(P(g) for g in grads), stream)

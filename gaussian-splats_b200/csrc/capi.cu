@@ -36,14 +36,17 @@ int32_t launch_bin_count(int64_t, const float*, const int32_t*, void*, int64_t*,
 int32_t launch_bin_sort(int64_t, int64_t, const int32_t*, const int32_t*, const gs_params&,
                         const void*, void*, int32_t*, int64_t*, cudaStream_t);
 int32_t launch_composite_fwd(const float*, const int32_t*, const int64_t*, const gs_params&,
-                             float*, float*, int32_t*, cudaStream_t);
+                             float*, float*, int32_t*, const int32_t*, cudaStream_t);
 int32_t launch_composite_bwd(int64_t, const float*, const int32_t*, const int64_t*, const float*,
-                             const float*, const int32_t*, const gs_params&, float*, cudaStream_t);
+                             const float*, const int32_t*, const gs_params&, float*,
+                             const int32_t*, cudaStream_t);
+int32_t launch_tile_order(const int64_t*, const int32_t*, const gs_params&, int32_t*, uint32_t*,
+                          cudaStream_t);
 uint64_t composite_bwd_deterministic_workspace_size(int64_t, int64_t);
 int32_t launch_composite_bwd_deterministic(int64_t, int64_t, const float*, const int32_t*,
                                            const int64_t*, const float*, const float*,
                                            const int32_t*, const gs_params&, void*, float*,
-                                           cudaStream_t);
+                                           const int32_t*, cudaStream_t);
 int32_t launch_adam_step(int64_t, int32_t, const gs_splat_arrays&, const gs_splat_arrays&,
                          const gs_splat_arrays&, const gs_splat_arrays&, const gs_adam_params&,
                          const float*, cudaStream_t);
@@ -220,26 +223,38 @@ int32_t gs_bin_check(const void* count_workspace, const void* sort_workspace,
   return (words[0] | words[1]) ? GS_ERR_TIMEOUT : GS_OK;
 }
 
+int32_t gs_tile_order(const int64_t* ranges, const int32_t* n_contributors,
+                      const gs_params* params, int32_t* tile_order, uint32_t* tile_work,
+                      gs_stream_t stream) {
+  GS_TRY(gs::check_params(params));
+  if (!tile_order || (n_contributors && !tile_work) || (!n_contributors && !ranges))
+    return GS_ERR_INVALID_ARGUMENT;
+  return gs::launch_tile_order(ranges, n_contributors, *params, tile_order, tile_work,
+                               as_cuda(stream));
+}
+
 int32_t gs_composite_fwd(const float* records, const int32_t* gaussian_ids,
                          const int64_t* ranges, const gs_params* params, float* image,
                          float* final_transmittance, int32_t* n_contributors,
-                         gs_stream_t stream) {
+                         const int32_t* tile_order, gs_stream_t stream) {
   GS_TRY(gs::check_params(params));
   if (!gs::aligned(records, 16)) return GS_ERR_MISALIGNED;
   return gs::launch_composite_fwd(records, gaussian_ids, ranges, *params, image,
-                                  final_transmittance, n_contributors, as_cuda(stream));
+                                  final_transmittance, n_contributors, tile_order,
+                                  as_cuda(stream));
 }
 
 int32_t gs_composite_bwd(int64_t n, const float* records, const int32_t* gaussian_ids,
                          const int64_t* ranges, const float* grad_image,
                          const float* final_transmittance, const int32_t* n_contributors,
-                         const gs_params* params, float* grad_projected, gs_stream_t stream) {
+                         const gs_params* params, float* grad_projected,
+                         const int32_t* tile_order, gs_stream_t stream) {
   GS_TRY(gs::check_params(params));
   if (n < 0) return GS_ERR_INVALID_ARGUMENT;
   if (!gs::aligned(records, 16)) return GS_ERR_MISALIGNED;
   return gs::launch_composite_bwd(n, records, gaussian_ids, ranges, grad_image,
                                   final_transmittance, n_contributors, *params, grad_projected,
-                                  as_cuda(stream));
+                                  tile_order, as_cuda(stream));
 }
 
 uint64_t gs_composite_bwd_deterministic_workspace_size(int64_t n, int64_t total) {
@@ -251,7 +266,8 @@ int32_t gs_composite_bwd_deterministic(int64_t n, int64_t total, const float* re
                                        const float* grad_image, const float* final_transmittance,
                                        const int32_t* n_contributors, const gs_params* params,
                                        void* workspace, uint64_t workspace_bytes,
-                                       float* grad_projected, gs_stream_t stream) {
+                                       float* grad_projected, const int32_t* tile_order,
+                                       gs_stream_t stream) {
   GS_TRY(gs::check_params(params));
   if (n < 0 || n >= gs::kMaxGaussians || total < 0 || total >= gs::kMaxIntersections)
     return GS_ERR_INVALID_ARGUMENT;
@@ -262,7 +278,7 @@ int32_t gs_composite_bwd_deterministic(int64_t n, int64_t total, const float* re
   return gs::launch_composite_bwd_deterministic(n, total, records, gaussian_ids, ranges,
                                                 grad_image, final_transmittance, n_contributors,
                                                 *params, workspace, grad_projected,
-                                                as_cuda(stream));
+                                                tile_order, as_cuda(stream));
 }
 
 int32_t gs_project_bwd(int64_t n, int32_t num_sh, const float* mean, const float* rotation,

@@ -116,6 +116,18 @@ struct StageBuffer {
   float4 a[NB], b[NB], c[NB], box[NB];
 };
 
+// The tile this CTA composites: CTA b takes tile_order[b] (the tiles by
+// decreasing work, so the longest lists start first instead of whenever their
+// row comes up), or tile b without an order. -1 (the CTA exits) for an entry
+// that is not a tile of the image.
+__device__ __forceinline__ int visit_tile(const int32_t* __restrict__ tile_order,
+                                          const gs_params& p) {
+  if (tile_order == nullptr) return static_cast<int>(blockIdx.x);
+  const int tile = __ldg(tile_order + blockIdx.x);
+  const int num_tiles = (p.width / p.tile_size) * (p.height / p.tile_size);
+  return tile >= 0 && tile < num_tiles ? tile : -1;
+}
+
 // Starts copying Gaussian g's record into `slot` of `buf`.
 template <int NB>
 __device__ __forceinline__ void stage_async(const float4* __restrict__ records, int32_t g,
@@ -191,13 +203,15 @@ __global__ void __launch_bounds__(TileShape<TS, 1>::kThreads,
                          const int32_t* __restrict__ gaussian_ids,
                          const int64_t* __restrict__ ranges, const gs_params p,
                          float* __restrict__ image, float* __restrict__ final_transmittance,
-                         int32_t* __restrict__ n_contributors) {
+                         int32_t* __restrict__ n_contributors,
+                         const int32_t* __restrict__ tile_order) {
   using S = TileShape<TS, 1>;
   constexpr int NB = S::kBatch;
   constexpr int kWarps = S::kWarps;
   __shared__ StageBuffer<NB> s_buf[2];
   __shared__ uint16_t s_list[kWarps][NB];
-  const int tile = blockIdx.x;
+  const int tile = visit_tile(tile_order, p);
+  if (tile < 0) return;
   const int tid = threadIdx.x;
   const int lane = tid % S::kWarpLanes, warp = tid / S::kWarpLanes;
   const PixelMap<TS, 1> pm(tile, p.width / TS, tid);
@@ -337,7 +351,8 @@ __global__ void __launch_bounds__(TileShape<TS, PPT>::kThreads,
                          const int64_t* __restrict__ ranges, const float* __restrict__ grad_image,
                          const float* __restrict__ final_transmittance,
                          const int32_t* __restrict__ n_contributors, const gs_params p,
-                         float* __restrict__ grad_projected) {
+                         float* __restrict__ grad_projected,
+                         const int32_t* __restrict__ tile_order) {
   using S = TileShape<TS, PPT>;
   // (the deterministic form's per-warp vectors of 32 x 32 tiles take smaller batches
   // to stay within 48 KB of shared memory)
@@ -354,7 +369,8 @@ __global__ void __launch_bounds__(TileShape<TS, PPT>::kThreads,
   __shared__ StageBuffer<NB> s_buf[kBuffers];
   __shared__ uint16_t s_list[S::kWarps][NB];
   __shared__ int s_max_contrib;
-  const int tile = blockIdx.x;
+  const int tile = visit_tile(tile_order, p);
+  if (tile < 0) return;
   const int tid = threadIdx.x;
   const int lane = tid % S::kWarpLanes, warp = tid / S::kWarpLanes;
   const PixelMap<TS, PPT> pm(tile, p.width / TS, tid);
@@ -643,7 +659,7 @@ __global__ void __launch_bounds__(256) reduce_rows_kernel(
 int32_t launch_composite_fwd(const float* records, const int32_t* gaussian_ids,
                              const int64_t* ranges, const gs_params& p, float* image,
                              float* final_transmittance, int32_t* n_contributors,
-                             cudaStream_t stream) {
+                             const int32_t* tile_order, cudaStream_t stream) {
   const int64_t num_tiles =
       static_cast<int64_t>(p.width / p.tile_size) * (p.height / p.tile_size);
   if (num_tiles == 0) return GS_OK;
@@ -651,10 +667,10 @@ int32_t launch_composite_fwd(const float* records, const int32_t* gaussian_ids,
 #define GS_LAUNCH(TS)                                                                          \
   if (p.gaussian_mode)                                                                         \
     composite_fwd_kernel<TS, true><<<static_cast<unsigned>(num_tiles), TS * TS, 0, stream>>>(  \
-        rec, gaussian_ids, ranges, p, image, final_transmittance, n_contributors);             \
+        rec, gaussian_ids, ranges, p, image, final_transmittance, n_contributors, tile_order); \
   else                                                                                         \
     composite_fwd_kernel<TS, false><<<static_cast<unsigned>(num_tiles), TS * TS, 0, stream>>>( \
-        rec, gaussian_ids, ranges, p, image, final_transmittance, n_contributors)
+        rec, gaussian_ids, ranges, p, image, final_transmittance, n_contributors, tile_order)
   GS_TILE_DISPATCH(p.tile_size, GS_LAUNCH)
 #undef GS_LAUNCH
   return check_launch();
@@ -663,7 +679,8 @@ int32_t launch_composite_fwd(const float* records, const int32_t* gaussian_ids,
 int32_t launch_composite_bwd(int64_t n, const float* records, const int32_t* gaussian_ids,
                              const int64_t* ranges, const float* grad_image,
                              const float* final_transmittance, const int32_t* n_contributors,
-                             const gs_params& p, float* grad_projected, cudaStream_t stream) {
+                             const gs_params& p, float* grad_projected,
+                             const int32_t* tile_order, cudaStream_t stream) {
   GS_CUDA_TRY(cudaMemsetAsync(grad_projected, 0, sizeof(float) * 9 * n, stream));
   const int64_t num_tiles =
       static_cast<int64_t>(p.width / p.tile_size) * (p.height / p.tile_size);
@@ -674,12 +691,12 @@ int32_t launch_composite_bwd(int64_t n, const float* records, const int32_t* gau
     composite_bwd_kernel<TS, BwdPpt<TS>::value, true>                                          \
         <<<static_cast<unsigned>(num_tiles), TileShape<TS, BwdPpt<TS>::value>::kThreads, 0,   \
            stream>>>(rec, gaussian_ids, ranges, grad_image, final_transmittance,               \
-                     n_contributors, p, grad_projected);                                       \
+                     n_contributors, p, grad_projected, tile_order);                           \
   else                                                                                         \
     composite_bwd_kernel<TS, BwdPpt<TS>::value, false>                                         \
         <<<static_cast<unsigned>(num_tiles), TileShape<TS, BwdPpt<TS>::value>::kThreads, 0,   \
            stream>>>(rec, gaussian_ids, ranges, grad_image, final_transmittance,               \
-                     n_contributors, p, grad_projected)
+                     n_contributors, p, grad_projected, tile_order)
   GS_TILE_DISPATCH(p.tile_size, GS_LAUNCH)
 #undef GS_LAUNCH
   return check_launch();
@@ -710,7 +727,7 @@ int32_t launch_composite_bwd_deterministic(int64_t n, int64_t total, const float
                                            const float* final_transmittance,
                                            const int32_t* n_contributors, const gs_params& p,
                                            void* workspace, float* grad_projected,
-                                           cudaStream_t stream) {
+                                           const int32_t* tile_order, cudaStream_t stream) {
   const DeterministicLayout L(n, total);
   char* base = static_cast<char*>(workspace);
   float* rows = reinterpret_cast<float*>(base + L.rows);
@@ -726,12 +743,12 @@ int32_t launch_composite_bwd_deterministic(int64_t n, int64_t total, const float
     composite_bwd_kernel<TS, BwdPpt<TS>::value, true, true>                                    \
         <<<static_cast<unsigned>(num_tiles), TileShape<TS, BwdPpt<TS>::value>::kThreads, 0,   \
            stream>>>(rec, gaussian_ids, ranges, grad_image, final_transmittance,               \
-                     n_contributors, p, rows);                                                 \
+                     n_contributors, p, rows, tile_order);                                     \
   else                                                                                         \
     composite_bwd_kernel<TS, BwdPpt<TS>::value, false, true>                                   \
         <<<static_cast<unsigned>(num_tiles), TileShape<TS, BwdPpt<TS>::value>::kThreads, 0,   \
            stream>>>(rec, gaussian_ids, ranges, grad_image, final_transmittance,               \
-                     n_contributors, p, rows)
+                     n_contributors, p, rows, tile_order)
     GS_TILE_DISPATCH(p.tile_size, GS_LAUNCH)
 #undef GS_LAUNCH
     GS_TRY(check_launch());
@@ -740,6 +757,113 @@ int32_t launch_composite_bwd_deterministic(int64_t n, int64_t total, const float
   if (n == 0) return GS_OK;
   reduce_rows_kernel<<<ceil_div(n, 256), 256, 0, stream>>>(n, order, segments, rows,
                                                            grad_projected);
+  return check_launch();
+}
+
+// ------------------------------------------------------ heavy-first tile order
+//
+// The compositors take a tile per CTA in CTA order. Tile costs are very
+// uneven (config 5's densest tile walks 850k pixel-Gaussian pairs, the mean
+// 47k; alone it takes half the backward's time), and in row-major order the
+// heavy central tiles start mid-launch on SMs already full of other tiles, so
+// they finish last. Visiting tiles by decreasing work starts them first.
+// Work classes are a quarter octave wide; order within a class is arbitrary
+// (no result depends on which CTA composites a tile).
+
+constexpr int kOrderThreads = 1024;
+constexpr int kWorkClasses = 64;
+
+// 0 for no work, else 1 + 4 floor(log2 w) + the two bits of w below its
+// leading one, capped at 63.
+__device__ __forceinline__ int work_class(uint32_t w) {
+  if (w == 0) return 0;
+  const int b = 31 - __clz(w);
+  const int frac = b >= 2 ? static_cast<int>((w >> (b - 2)) & 3u) : static_cast<int>((w << (2 - b)) & 3u);
+  const int c = 1 + 4 * b + frac;
+  return c < kWorkClasses - 1 ? c : kWorkClasses - 1;
+}
+
+__device__ __forceinline__ uint32_t tile_work(const int64_t* __restrict__ ranges,
+                                              const uint32_t* __restrict__ work, int64_t t) {
+  if (work) return __ldg(work + t);
+  const int64_t len = ranges[2 * t + 1] - ranges[2 * t];
+  return len <= 0 ? 0u : (len >= 0xffffffffLL ? 0xffffffffu : static_cast<uint32_t>(len));
+}
+
+// One CTA: a counting sort of the tiles by decreasing work class. The lanes
+// of a warp holding the same class are found with one match, and their
+// leader adds them with one shared-memory atomic (all tiles fall into a few
+// classes, so per-tile atomics would serialise on a handful of counters).
+__global__ void __launch_bounds__(kOrderThreads) order_tiles_kernel(
+    const int64_t* __restrict__ ranges, const uint32_t* __restrict__ work, int64_t num_tiles,
+    int32_t* __restrict__ order) {
+  __shared__ uint32_t s_next[kWorkClasses];
+  const int lane = threadIdx.x & 31;
+  const int64_t warp_first = threadIdx.x & ~31;
+  const unsigned lower = (1u << lane) - 1u;
+  if (threadIdx.x < kWorkClasses) s_next[threadIdx.x] = 0;
+  __syncthreads();
+  for (int64_t t0 = warp_first; t0 < num_tiles; t0 += kOrderThreads) {  // warp-uniform
+    const int64_t t = t0 + lane;
+    const int c = t < num_tiles ? work_class(tile_work(ranges, work, t)) : kWorkClasses;
+    const unsigned peers = __match_any_sync(0xffffffffu, c);
+    if (c < kWorkClasses && (peers & lower) == 0) atomicAdd(&s_next[c], __popc(peers));
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {  // exclusive offsets, heaviest class first
+    uint32_t run = 0;
+    for (int c = kWorkClasses - 1; c >= 0; --c) {
+      const uint32_t k = s_next[c];
+      s_next[c] = run;
+      run += k;
+    }
+  }
+  __syncthreads();
+  for (int64_t t0 = warp_first; t0 < num_tiles; t0 += kOrderThreads) {
+    const int64_t t = t0 + lane;
+    const int c = t < num_tiles ? work_class(tile_work(ranges, work, t)) : kWorkClasses;
+    const unsigned peers = __match_any_sync(0xffffffffu, c);
+    const int leader = __ffs(peers) - 1;
+    uint32_t base = 0;
+    if (c < kWorkClasses && lane == leader) base = atomicAdd(&s_next[c], __popc(peers));
+    base = __shfl_sync(0xffffffffu, base, leader);
+    if (c < kWorkClasses) order[base + __popc(peers & lower)] = static_cast<int32_t>(t);
+  }
+}
+
+// The backward's work per tile: its largest contributor count (the backward
+// walks each tile's list that far). One warp per tile.
+__global__ void __launch_bounds__(256) tile_max_contrib_kernel(
+    const int32_t* __restrict__ n_contributors, int width, int tile_size, int tiles_w,
+    int64_t num_tiles, uint32_t* __restrict__ work) {
+  const int64_t t = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (t >= num_tiles) return;
+  const int x0 = static_cast<int>(t % tiles_w) * tile_size;
+  const int y0 = static_cast<int>(t / tiles_w) * tile_size;
+  int m = 0;
+  for (int k = lane; k < tile_size * tile_size; k += 32) {
+    const int v = __ldg(n_contributors + static_cast<int64_t>(y0 + k / tile_size) * width + x0 +
+                        k % tile_size);
+    m = v > m ? v : m;
+  }
+  m = __reduce_max_sync(0xffffffffu, m);
+  if (lane == 0) work[t] = static_cast<uint32_t>(m);
+}
+
+int32_t launch_tile_order(const int64_t* ranges, const int32_t* n_contributors,
+                          const gs_params& p, int32_t* order, uint32_t* work,
+                          cudaStream_t stream) {
+  const int tiles_w = p.width / p.tile_size;
+  const int64_t num_tiles = static_cast<int64_t>(tiles_w) * (p.height / p.tile_size);
+  if (num_tiles == 0) return GS_OK;
+  if (n_contributors != nullptr) {
+    tile_max_contrib_kernel<<<ceil_div(num_tiles * 32, 256), 256, 0, stream>>>(
+        n_contributors, p.width, p.tile_size, tiles_w, num_tiles, work);
+    GS_TRY(check_launch());
+  }
+  order_tiles_kernel<<<1, kOrderThreads, 0, stream>>>(
+      ranges, n_contributors != nullptr ? work : nullptr, num_tiles, order);
   return check_launch();
 }
 

@@ -38,6 +38,7 @@ EXPORTED_SYMBOLS = (
     "gs_bin_sort_workspace_size",
     "gs_bin_check",
     "gs_bin_noalloc",
+    "gs_tile_order",
     "gs_composite_fwd",
     "gs_composite_bwd",
     "gs_composite_bwd_deterministic",
@@ -223,9 +224,11 @@ def lib() -> ctypes.CDLL:
         "gs_bin_sort_workspace_size": ([i64, i64], u64),
         "gs_bin_check": ([vp, vp, vp], i32),
         "gs_bin_noalloc": ([i64, vp, vp, vp, P, vp, i64, vp, ctypes.POINTER(i64), vp], i32),
-        "gs_composite_fwd": ([vp] * 3 + [P] + [vp] * 3 + [vp], i32),
-        "gs_composite_bwd": ([i64] + [vp] * 6 + [P, vp, vp], i32),
-        "gs_composite_bwd_deterministic": ([i64, i64] + [vp] * 6 + [P, vp, u64, vp, vp], i32),
+        "gs_tile_order": ([vp, vp, P, vp, vp, vp], i32),
+        "gs_composite_fwd": ([vp] * 3 + [P] + [vp] * 4 + [vp], i32),
+        "gs_composite_bwd": ([i64] + [vp] * 6 + [P, vp, vp, vp], i32),
+        "gs_composite_bwd_deterministic": ([i64, i64] + [vp] * 6 + [P, vp, u64, vp, vp, vp],
+                                           i32),
         "gs_composite_bwd_deterministic_workspace_size": ([i64, i64], u64),
         "gs_project_bwd": ([i64, i32] + [vp] * 10 + [P] + [vp] * 5 + [vp], i32),
         "gs_project_bwd_views": ([i64, i32, i32] + [vp] * 13 + [vp], i32),

@@ -57,6 +57,20 @@ def _stream(device: torch.device) -> ctypes.c_void_p:
     return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
 
 
+def _tile_order(ranges: torch.Tensor, n_contributors: torch.Tensor | None, pref,
+                stream: ctypes.c_void_p) -> torch.Tensor:
+    """The compositors' heavy-first visiting order of the view's tiles
+    (gs_tile_order): by list length for the forward, by largest contributor
+    count (``n_contributors`` given) for the backward."""
+    num_tiles = ranges.shape[0]
+    order = torch.empty((num_tiles,), dtype=torch.int32, device=ranges.device)
+    work = (torch.empty((num_tiles,), dtype=torch.int32, device=ranges.device)
+            if n_contributors is not None else None)
+    native.check(native.lib().gs_tile_order(_ptr(ranges), _ptr(n_contributors), pref,
+                                            _ptr(order), _ptr(work), stream), "gs_tile_order")
+    return order
+
+
 def _check_inputs(mean: torch.Tensor, color: torch.Tensor, rendering_mode: str) -> None:
     if not mean.is_cuda:
         raise RuntimeError(
@@ -278,9 +292,11 @@ def _rasterize(
                     not torch.cuda.is_current_stream_capturing():
                 native.check(lib.gs_bin_check(_ptr(count_ws), _ptr(sort_ws), stream), "binning")
             _mark("begin:composite_fwd")
+            order = _tile_order(ranges, None, pref, stream)
             native.check(lib.gs_composite_fwd(
                 _ptr(records), _ptr(gaussian_ids), _ptr(ranges), pref, _ptr(image),
-                _ptr(final_transmittance), _ptr(n_contributors), stream), "gs_composite_fwd")
+                _ptr(final_transmittance), _ptr(n_contributors), _ptr(order), stream),
+                "gs_composite_fwd")
             _mark("composite_fwd")
             return gaussian_ids
 
@@ -439,6 +455,7 @@ def _backward(ctx, *grad_outputs):
             native.check(lib.gs_pack_records(
                 n, _ptr(projected_mean), _ptr(inverse_covariance), _ptr(projected_color),
                 _ptr(projected_opacity), pref, _ptr(records), stream), "gs_pack_records")
+        order = _tile_order(ranges, n_contributors, pref, stream)
         if deterministic_backward():
             # order-fixed form: the same gradient bits on every run
             if torch.cuda.is_current_stream_capturing():
@@ -450,12 +467,13 @@ def _backward(ctx, *grad_outputs):
             native.check(lib.gs_composite_bwd_deterministic(
                 n, total, _ptr(records), _ptr(gaussian_ids), _ptr(ranges), _ptr(grad_image),
                 _ptr(final_transmittance), _ptr(n_contributors), pref, _ptr(workspace),
-                ws_bytes, _ptr(grad_projected), stream), "gs_composite_bwd_deterministic")
+                ws_bytes, _ptr(grad_projected), _ptr(order), stream),
+                "gs_composite_bwd_deterministic")
         else:
             native.check(lib.gs_composite_bwd(
                 n, _ptr(records), _ptr(gaussian_ids), _ptr(ranges), _ptr(grad_image),
                 _ptr(final_transmittance), _ptr(n_contributors), pref, _ptr(grad_projected),
-                stream), "gs_composite_bwd")
+                _ptr(order), stream), "gs_composite_bwd")
         _mark("composite_bwd")
         # The five gradients are carved out of one buffer (rotation and colour
         # first, keeping their 16-byte rows aligned), so a view-parallel step
@@ -701,9 +719,11 @@ def rasterize_batch(
             image = mean.new_empty((height, width, 3))
             final_transmittance = mean.new_empty((height, width))
             n_contributors = torch.empty((height, width), dtype=torch.int32, device=device)
+            order = _tile_order(ranges, None, pref, stream)
             native.check(lib.gs_composite_fwd(
                 _ptr(records[v]), _ptr(gaussian_ids), _ptr(ranges), pref, _ptr(image),
-                _ptr(final_transmittance), _ptr(n_contributors), stream), "gs_composite_fwd")
+                _ptr(final_transmittance), _ptr(n_contributors), _ptr(order), stream),
+                "gs_composite_fwd")
             outputs.append((image, final_transmittance, n_contributors, projected_mean[v],
                             inverse_covariance[v], projected_color[v], projected_opacity[v],
                             gaussian_ids, ranges, counts[v]))

@@ -181,21 +181,39 @@ int32_t gs_bin_noalloc(int64_t n, const float *projected_mean, const int32_t *co
                        int64_t ids_capacity, int64_t *ranges, int64_t *total_host,
                        gs_stream_t stream);
 
+/* The order in which the compositors visit the view's tiles: the tiles by
+ * decreasing work (quarter-octave classes), so the longest lists start first
+ * instead of whenever their row of tiles comes up. No counterpart in the
+ * reference, whose Triton launches take tiles in grid order (composite.py:140,
+ * composite_bwd.py:248). Work is each tile's list length (from ranges) for
+ * the forward, or with n_contributors [H,W] its largest contributor count for
+ * the backward (then tile_work, [num_tiles] uint32, is scratch). tile_order receives
+ * [num_tiles] int32, a permutation of the tile indices. */
+int32_t gs_tile_order(const int64_t *ranges, const int32_t *n_contributors,
+                      const gs_params *params, int32_t *tile_order, uint32_t *tile_work,
+                      gs_stream_t stream);
+
 /* Front-to-back compositing: replaces _composite_kernel (composite.py:25-162).
  * records: what gs_project_fwd (or gs_pack_records) wrote for the view.
- * image [H,W,3], final_transmittance [H,W], n_contributors [H,W] int32. */
+ * image [H,W,3], final_transmittance [H,W], n_contributors [H,W] int32.
+ * tile_order: gs_tile_order's permutation, or NULL for row-major order (the
+ * results are the same either way). */
 int32_t gs_composite_fwd(const float *records, const int32_t *gaussian_ids, const int64_t *ranges,
                          const gs_params *params, float *image, float *final_transmittance,
-                         int32_t *n_contributors, gs_stream_t stream);
+                         int32_t *n_contributors, const int32_t *tile_order,
+                         gs_stream_t stream);
 
 /* Back-to-front compositing gradients: replaces _composite_bwd_kernel and the
  * index_add_ reduction (composite_bwd.py:47-277). Accumulates into
  * grad_projected [N,9] = (d mean_x, d mean_y, d conic_xx, d conic_xy,
- * d conic_yy, d r, d g, d b, d opacity), which this call zeroes first. */
+ * d conic_yy, d r, d g, d b, d opacity), which this call zeroes first.
+ * tile_order as for gs_composite_fwd (for the backward, gs_tile_order with
+ * n_contributors). */
 int32_t gs_composite_bwd(int64_t n, const float *records, const int32_t *gaussian_ids,
                          const int64_t *ranges, const float *grad_image,
                          const float *final_transmittance, const int32_t *n_contributors,
-                         const gs_params *params, float *grad_projected, gs_stream_t stream);
+                         const gs_params *params, float *grad_projected,
+                         const int32_t *tile_order, gs_stream_t stream);
 
 /* The same gradients, the same bits on every run: the reference's
  * per-intersection form (composite_bwd.py:237-277, its non-atomic default,
@@ -213,7 +231,8 @@ int32_t gs_composite_bwd_deterministic(int64_t n, int64_t total, const float *re
                                        const float *grad_image, const float *final_transmittance,
                                        const int32_t *n_contributors, const gs_params *params,
                                        void *workspace, uint64_t workspace_bytes,
-                                       float *grad_projected, gs_stream_t stream);
+                                       float *grad_projected, const int32_t *tile_order,
+                                       gs_stream_t stream);
 
 /* Parameter gradients: replaces _project_bwd_kernel (project_bwd.py:8-381).
  * SH gradients cover all K coefficients: degree 4 (K = 25) differentiates the

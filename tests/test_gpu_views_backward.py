@@ -54,7 +54,7 @@ def _screen_gradients(splats, camera, seed):
                                      P(records), stream), "pack_records")
     native.check(lib.gs_composite_bwd(n, P(records), P(ids), P(ranges), P(grad_image),
                                       P(final_t), P(n_contrib), ctypes.byref(params), P(gp),
-                                      stream), "composite_bwd")
+                                      None, stream), "composite_bwd")
     return params, conic, counts, gp, grad_image
 
 
