@@ -69,6 +69,10 @@ __device__ __forceinline__ unsigned lanemask_lt() {
 struct DepthSource {  // key = depth bits of projected_mean[i, 2], value = i
   const float* projected_mean;
   const int32_t* counts;
+  static constexpr bool kWeighted = true;  // the upsweep also totals the tile counts
+  __device__ __forceinline__ uint32_t weight(int64_t i) const {
+    return static_cast<uint32_t>(__ldg(counts + i));
+  }
   __device__ __forceinline__ bool valid(int64_t i) const { return __ldg(counts + i) > 0; }
   __device__ __forceinline__ uint32_t key(int64_t i) const {
     return __float_as_uint(__ldg(projected_mean + 3 * i + 2));
@@ -92,6 +96,7 @@ struct DepthSource {  // key = depth bits of projected_mean[i, 2], value = i
 struct ArraySource {
   const uint32_t* keys;
   const uint32_t* values;
+  static constexpr bool kWeighted = false;
   __device__ __forceinline__ bool valid(int64_t) const { return true; }
   __device__ __forceinline__ uint32_t key(int64_t i) const { return keys[i]; }
   __device__ __forceinline__ uint32_t value(int64_t i) const { return values[i]; }
@@ -126,6 +131,7 @@ struct ArraySource {
 // backward's grouping of list positions by Gaussian.
 struct PositionSource {
   const uint32_t* keys;
+  static constexpr bool kWeighted = false;
   __device__ __forceinline__ bool valid(int64_t) const { return true; }
   __device__ __forceinline__ uint32_t key(int64_t i) const { return keys[i]; }
   __device__ __forceinline__ uint32_t value(int64_t i) const { return static_cast<uint32_t>(i); }
@@ -162,18 +168,25 @@ struct Count {
 template <class Source, int kUpsweepRun>
 __global__ void __launch_bounds__(kThreads) upsweep_kernel(Source src, Count count, int num_passes,
                                                           int shift0, uint32_t* __restrict__ hist,
-                                                          uint32_t* __restrict__ valid_total) {
+                                                          uint32_t* __restrict__ valid_total,
+                                                          unsigned long long* __restrict__ weight_total) {
   __shared__ uint32_t s_hist[4][kRadix];
   const int64_t n = count.get();
   for (int i = threadIdx.x; i < 4 * kRadix; i += kThreads) (&s_hist[0][0])[i] = 0;
   __syncthreads();
   uint32_t valid_here = 0;
+  unsigned long long weight_here = 0;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * kThreads * kUpsweepRun;
   for (int64_t first = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) * kUpsweepRun;
        first < n; first += stride) {
     uint32_t keys[kUpsweepRun];
     uint32_t valid = src.load_run(first, n, keys);  // bit j: element first + j counts
     valid_here += __popc(valid);
+    if constexpr (Source::kWeighted) {
+#pragma unroll
+      for (int j = 0; j < kUpsweepRun; ++j)
+        if ((valid >> j) & 1u) weight_here += src.weight(first + j);
+    }
     for (int p = 0; p < num_passes; ++p) {
       const int shift = shift0 + 8 * p;
       int current = -1;
@@ -195,6 +208,10 @@ __global__ void __launch_bounds__(kThreads) upsweep_kernel(Source src, Count cou
   if (valid_total) {
     for (int o = 16; o > 0; o >>= 1) valid_here += __shfl_xor_sync(0xffffffffu, valid_here, o);
     if ((threadIdx.x & 31) == 0 && valid_here) atomicAdd(valid_total, valid_here);
+  }
+  if (weight_total) {
+    for (int o = 16; o > 0; o >>= 1) weight_here += __shfl_xor_sync(0xffffffffu, weight_here, o);
+    if ((threadIdx.x & 31) == 0 && weight_here) atomicAdd(weight_total, weight_here);
   }
   __syncthreads();
   for (int i = threadIdx.x; i < num_passes * kRadix; i += kThreads) {
@@ -237,13 +254,13 @@ __device__ __forceinline__ uint32_t block_exclusive_scan(uint32_t v, uint32_t* s
 // the error word is set and the walk stops.
 constexpr int kLookback = 4;
 __device__ __forceinline__ uint32_t lookback_window(const uint32_t* status, int d, int64_t b,
-                                                    uint32_t* error) {
+                                                    uint32_t* error, int64_t stride = kRadix) {
   uint32_t exclusive = 0;
   while (b >= 0) {
     uint32_t words[kLookback];
 #pragma unroll
     for (int i = 0; i < kLookback; ++i)
-      words[i] = b - i >= 0 ? ld_volatile(status + (b - i) * kRadix + d) : kFlagPrefix;
+      words[i] = b - i >= 0 ? ld_volatile(status + (b - i) * stride + d) : kFlagPrefix;
 #pragma unroll
     for (int i = 0; i < kLookback; ++i) {
       int spins = 0;
@@ -253,7 +270,7 @@ __device__ __forceinline__ uint32_t lookback_window(const uint32_t* status, int 
           return exclusive;
         }
         if (spins > 64) __nanosleep(64);
-        words[i] = ld_volatile(status + (b - i) * kRadix + d);
+        words[i] = ld_volatile(status + (b - i) * stride + d);
       }
       exclusive += words[i] & kValueMask;
       if ((words[i] >> 30) != 1) return exclusive;  // inclusive prefix (or block < 0)
@@ -544,6 +561,385 @@ __global__ void ranges_kernel(const uint32_t* __restrict__ sorted_keys, Count co
   }
 }
 
+// ------------------------------------------------------- row/column binning
+//
+// The list order (tile, depth bits, Gaussian index) is, with tile = row *
+// tiles_w + column: by tile row, then tile column, then depth order. Each
+// visible Gaussian covers a rectangle of tiles: h row segments of w
+// consecutive tiles. So instead of emitting all w*h (tile, Gaussian) pairs and
+// radix-sorting them by tile id (two passes over every pair):
+//   pass A  scatters the depth-ordered Gaussians into per-row lists of
+//           segments (stable: each row's segments stay in depth order);
+//   pass B  scatters each row's segments into the row's tile lists (stable:
+//           each tile's Gaussians stay in depth order) and writes the ids.
+// A config-2 view has 5.15M pairs but 2.2M segments, a config-5 view 56.8M
+// pairs but 5M segments.
+//
+// Each pass is three kernels and no CTA ever waits on another: count (per
+// chunk of items, how many land in each bucket -- row or column), scan (per
+// bucket, the chunks' exclusive prefix, and the bucket starts), scatter (each
+// chunk writes its items from its prefix on). Within a chunk an item's place
+// is its stable rank among the chunk's items covering the same bucket: items
+// are taken in batches of one per thread, each warp ORs its lanes into a
+// bitmask per bucket, and the rank is the popcount of the lanes and warps
+// before it -- an interval covers each of its buckets once, so no digit
+// ranking is needed. (A decoupled look-back across the thousands of small
+// chunks measured 150 us on the config-2 view: every chunk publishes at
+// once and the prefix front advances a few chunks per round trip.)
+
+constexpr int kChunkBatches = 4;                         // batches of kThreads items per chunk
+constexpr int kChunkItems = kChunkBatches * kThreads;   // 1024
+constexpr int kMaxTileRows = 512;       // pass A keeps bitmasks per (warp, row)
+constexpr int kMaxTileCols = kThreads;  // pass B keeps bitmasks per (warp, column)
+constexpr int kScanThreads = 1024;
+
+// A Gaussian's tile rectangle (xmin, xmax, ymin, ymax) clamped to the grid.
+// The projection's rectangles are inside it already, and non-empty wherever
+// the count is non-zero; the clamp keeps any other caller's input in bounds.
+__device__ __forceinline__ int4 clamp_rect(int4 b, int cols, int rows) {
+  const int x0 = min(max(b.x, 0), cols), y0 = min(max(b.z, 0), rows);
+  return make_int4(x0, min(max(b.y, x0), cols), y0, min(max(b.w, y0), rows));
+}
+
+// Exclusive scan of one value per thread over a CTA of kScanThreads; the
+// total goes to *total (every thread).
+__device__ __forceinline__ uint32_t wide_exclusive_scan(uint32_t v, uint32_t* s_tmp,
+                                                        uint32_t* total) {
+  constexpr int kScanWarps = kScanThreads / 32;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint32_t x = v;
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) s_tmp[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    uint32_t w = lane < kScanWarps ? s_tmp[lane] : 0;
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    s_tmp[lane] = w;  // inclusive warp totals
+  }
+  __syncthreads();
+  const uint32_t prefix = warp ? s_tmp[warp - 1] : 0;
+  *total = s_tmp[kScanWarps - 1];
+  __syncthreads();
+  return prefix + x - v;
+}
+
+// The ranks of one batch (one item per thread) among the batch's items that
+// cover the same bucket, on top of s_run[bucket], and s_run advanced past the
+// batch. Item [lo, hi) covers buckets lo..hi-1; `emit(bucket, position)` is
+// called once per covered bucket. s_cover [kWarps][buckets] must be zero on
+// entry and is zero again on return; s_base [kWarps][buckets] is scratch.
+template <class Emit>
+__device__ __forceinline__ void scatter_batch(int lo, int hi, int buckets, uint32_t* s_cover,
+                                              uint32_t* s_base, uint32_t* s_run, int stride,
+                                              Emit emit) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int k = lo; k < hi; ++k) atomicOr(&s_cover[warp * stride + k], 1u << lane);
+  __syncthreads();
+  for (int k = threadIdx.x; k < buckets; k += kThreads) {
+    uint32_t run = s_run[k];
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      s_base[w * stride + k] = run;
+      run += __popc(s_cover[w * stride + k]);
+    }
+    s_run[k] = run;
+  }
+  __syncthreads();
+  const unsigned lower = lanemask_lt();
+  for (int k = lo; k < hi; ++k)
+    emit(k, s_base[warp * stride + k] + __popc(s_cover[warp * stride + k] & lower));
+  __syncthreads();
+  for (int k = threadIdx.x; k < buckets; k += kThreads) {
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) s_cover[w * stride + k] = 0;
+  }
+  __syncthreads();
+}
+
+// Pass A, count: per chunk of kChunkItems depth-ordered Gaussians, the
+// segments (Gaussians) and the pairs (Gaussians x width) each tile row gets,
+// by difference arrays over rows: seg_counts / pair_counts [rows][chunks].
+__global__ void __launch_bounds__(kThreads) row_count_kernel(
+    const uint32_t* __restrict__ sorted_ids, const uint32_t* __restrict__ num_valid,
+    const int4* __restrict__ bounds, int rows, int cols, int64_t chunks_pitch,
+    uint32_t* __restrict__ seg_counts, uint32_t* __restrict__ pair_counts) {
+  __shared__ int32_t s_seg[kMaxTileRows + 1];
+  __shared__ int32_t s_pair[kMaxTileRows + 1];
+  __shared__ uint32_t s_tmp[kWarps];
+  const int64_t v = *num_valid;
+  const int64_t first = static_cast<int64_t>(blockIdx.x) * kChunkItems;
+  if (first >= v) return;  // uniform
+  for (int y = threadIdx.x; y <= rows; y += kThreads) s_seg[y] = s_pair[y] = 0;
+  __syncthreads();
+#pragma unroll
+  for (int bt = 0; bt < kChunkBatches; ++bt) {
+    const int64_t j = first + bt * kThreads + threadIdx.x;
+    if (j < v) {
+      const int4 b = clamp_rect(__ldg(bounds + sorted_ids[j]), cols, rows);
+      atomicAdd(&s_seg[b.z], 1);
+      atomicAdd(&s_seg[b.w], -1);
+      atomicAdd(&s_pair[b.z], b.y - b.x);
+      atomicAdd(&s_pair[b.w], b.x - b.y);
+    }
+  }
+  __syncthreads();
+  // prefix over rows (rows <= 2 kThreads: two rows per thread)
+  const int y0 = 2 * threadIdx.x;
+  const int32_t a0 = y0 < rows ? s_seg[y0] : 0, a1 = y0 + 1 < rows ? s_seg[y0 + 1] : 0;
+  const int32_t p0 = y0 < rows ? s_pair[y0] : 0, p1 = y0 + 1 < rows ? s_pair[y0 + 1] : 0;
+  const int32_t sa = static_cast<int32_t>(
+      block_exclusive_scan(static_cast<uint32_t>(a0 + a1), s_tmp, nullptr));
+  const int32_t sp = static_cast<int32_t>(
+      block_exclusive_scan(static_cast<uint32_t>(p0 + p1), s_tmp, nullptr));
+  if (y0 < rows) {
+    seg_counts[y0 * chunks_pitch + blockIdx.x] = static_cast<uint32_t>(sa + a0);
+    pair_counts[y0 * chunks_pitch + blockIdx.x] = static_cast<uint32_t>(sp + p0);
+  }
+  if (y0 + 1 < rows) {
+    seg_counts[(y0 + 1) * chunks_pitch + blockIdx.x] = static_cast<uint32_t>(sa + a0 + a1);
+    pair_counts[(y0 + 1) * chunks_pitch + blockIdx.x] = static_cast<uint32_t>(sp + p0 + p1);
+  }
+}
+
+// Pass A, scan: CTA y turns row y's per-chunk segment counts into exclusive
+// prefixes (in place) and totals the row's segments and pairs.
+__global__ void __launch_bounds__(kScanThreads) row_scan_kernel(
+    const uint32_t* __restrict__ num_valid, int64_t chunks_pitch,
+    uint32_t* __restrict__ seg_counts, const uint32_t* __restrict__ pair_counts,
+    uint32_t* __restrict__ row_segs, uint32_t* __restrict__ row_pairs) {
+  __shared__ uint32_t s_tmp[32];
+  const int y = blockIdx.x;
+  const int64_t chunks = (static_cast<int64_t>(*num_valid) + kChunkItems - 1) / kChunkItems;
+  uint32_t* counts = seg_counts + y * chunks_pitch;
+  const uint32_t* pairs = pair_counts + y * chunks_pitch;
+  // thread t owns a contiguous run of chunks
+  const int64_t per = (chunks + kScanThreads - 1) / kScanThreads;
+  const int64_t c0 = threadIdx.x * per;
+  const int64_t c1 = c0 + per < chunks ? c0 + per : chunks;
+  uint32_t mine = 0, my_pairs = 0;
+  for (int64_t c = c0; c < c1; ++c) {
+    mine += counts[c];
+    my_pairs += pairs[c];
+  }
+  uint32_t total, total_pairs;
+  uint32_t run = wide_exclusive_scan(mine, s_tmp, &total);
+  wide_exclusive_scan(my_pairs, s_tmp, &total_pairs);
+  for (int64_t c = c0; c < c1; ++c) {
+    const uint32_t k = counts[c];
+    counts[c] = run;
+    run += k;
+  }
+  if (threadIdx.x == 0) {
+    row_segs[y] = total;
+    row_pairs[y] = total_pairs;
+  }
+}
+
+// One CTA: the start of each row's segments (those past `seg_capacity` are
+// dropped) and pairs, and pass B's chunks (kChunkItems segments of one row
+// each): the first chunk of each row and the row of each chunk.
+__global__ void __launch_bounds__(kScanThreads) row_layout_kernel(
+    const uint32_t* __restrict__ row_segs, const uint32_t* __restrict__ row_pairs, int rows,
+    uint32_t seg_capacity, uint32_t* __restrict__ row_seg_start,
+    uint32_t* __restrict__ row_pair_start, uint32_t* __restrict__ row_chunk_start,
+    uint32_t* __restrict__ chunk_row) {
+  __shared__ uint32_t s_tmp[32];
+  const int y = threadIdx.x;  // rows <= kScanThreads
+  const uint32_t segs = y < rows ? row_segs[y] : 0u;
+  uint32_t total, total_pairs;
+  const uint32_t start = wide_exclusive_scan(segs, s_tmp, &total);
+  const uint32_t pair_start = wide_exclusive_scan(y < rows ? row_pairs[y] : 0u, s_tmp,
+                                                  &total_pairs);
+  const uint32_t lo = start < seg_capacity ? start : seg_capacity;
+  const uint32_t end = start + segs;
+  const uint32_t hi = end < seg_capacity ? end : seg_capacity;
+  const uint32_t chunks = (hi - lo + kChunkItems - 1) / kChunkItems;
+  uint32_t num_chunks;
+  const uint32_t first_chunk = wide_exclusive_scan(chunks, s_tmp, &num_chunks);
+  if (y < rows) {
+    row_seg_start[y] = lo;
+    row_pair_start[y] = pair_start;
+    row_chunk_start[y] = first_chunk;
+    for (uint32_t k = 0; k < chunks; ++k) chunk_row[first_chunk + k] = static_cast<uint32_t>(y);
+  }
+  if (y == 0) {
+    row_seg_start[rows] = total < seg_capacity ? total : seg_capacity;
+    row_pair_start[rows] = total_pairs;
+    row_chunk_start[rows] = num_chunks;
+  }
+}
+
+// Pass A, scatter: chunk c of the depth order writes each Gaussian's id into
+// its rows' segment lists, from the row start plus the chunk's prefix.
+__global__ void __launch_bounds__(kThreads) row_scatter_kernel(
+    const uint32_t* __restrict__ sorted_ids, const uint32_t* __restrict__ num_valid,
+    const int4* __restrict__ bounds, int rows, int cols, int64_t chunks_pitch,
+    const uint32_t* __restrict__ seg_prefix, const uint32_t* __restrict__ row_seg_start,
+    uint32_t seg_capacity, uint32_t* __restrict__ segs) {
+  __shared__ uint32_t s_cover[kWarps * kMaxTileRows];
+  __shared__ uint32_t s_base[kWarps * kMaxTileRows];
+  __shared__ uint32_t s_run[kMaxTileRows];
+  const int64_t v = *num_valid;
+  const int64_t first = static_cast<int64_t>(blockIdx.x) * kChunkItems;
+  if (first >= v) return;  // uniform
+  for (int i = threadIdx.x; i < kWarps * rows; i += kThreads) s_cover[(i / rows) * rows + i % rows] = 0;
+  for (int y = threadIdx.x; y < rows; y += kThreads)
+    s_run[y] = row_seg_start[y] + seg_prefix[y * chunks_pitch + blockIdx.x];
+  __syncthreads();
+  for (int bt = 0; bt < kChunkBatches; ++bt) {
+    const int64_t j = first + bt * kThreads + threadIdx.x;
+    uint32_t g = 0;
+    int4 b = make_int4(0, 0, 0, 0);
+    if (j < v) {
+      g = sorted_ids[j];
+      b = clamp_rect(__ldg(bounds + g), cols, rows);
+    }
+    scatter_batch(b.z, b.w, rows, s_cover, s_base, s_run, rows, [&](int, uint32_t pos) {
+      if (pos < seg_capacity) segs[pos] = g;
+    });
+  }
+}
+
+// Pass B, count: per chunk of one row's segments, the pairs each tile column
+// gets (a difference array over columns): col_counts [chunks][cols].
+__global__ void __launch_bounds__(kThreads) col_count_kernel(
+    const uint32_t* __restrict__ segs, const int4* __restrict__ bounds, int rows, int cols,
+    const uint32_t* __restrict__ row_seg_start, const uint32_t* __restrict__ row_chunk_start,
+    const uint32_t* __restrict__ chunk_row, uint32_t* __restrict__ col_counts) {
+  __shared__ int32_t s_diff[kMaxTileCols + 1];
+  __shared__ uint32_t s_tmp[kWarps];
+  const uint32_t num_chunks = row_chunk_start[rows];
+  for (uint32_t c = blockIdx.x; c < num_chunks; c += gridDim.x) {  // uniform
+    for (int x = threadIdx.x; x <= cols; x += kThreads) s_diff[x] = 0;
+    __syncthreads();
+    const uint32_t y = chunk_row[c];
+    const uint32_t s0 = row_seg_start[y] + (c - row_chunk_start[y]) * kChunkItems;
+    const uint32_t end = row_seg_start[y + 1];
+#pragma unroll
+    for (int bt = 0; bt < kChunkBatches; ++bt) {
+      const uint32_t si = s0 + bt * kThreads + threadIdx.x;
+      if (si < end && si < s0 + kChunkItems) {
+        const int2 span = __ldg(reinterpret_cast<const int2*>(bounds + segs[si]));
+        const int x0 = min(max(span.x, 0), cols);  // as clamp_rect
+        const int x1 = min(max(span.y, x0), cols);
+        atomicAdd(&s_diff[x0], 1);
+        atomicAdd(&s_diff[x1], -1);
+      }
+    }
+    __syncthreads();
+    const int x = threadIdx.x;  // cols <= kThreads
+    const int32_t d = x < cols ? s_diff[x] : 0;
+    const int32_t count = static_cast<int32_t>(
+        block_exclusive_scan(static_cast<uint32_t>(d), s_tmp, nullptr)) + d;
+    if (x < cols) col_counts[static_cast<int64_t>(c) * cols + x] = static_cast<uint32_t>(count);
+    __syncthreads();
+  }
+}
+
+// Pass B, scan: CTA y totals each column of row y over the row's chunks,
+// writes the row's tile ranges (start: the row's first pair plus the columns
+// before; clamped to the id capacity) and turns the chunks' column counts
+// into their first positions (in place). Four threads per column, each over a
+// quarter of the row's chunks.
+__global__ void __launch_bounds__(kScanThreads) col_scan_kernel(
+    int cols, const uint32_t* __restrict__ row_chunk_start,
+    const uint32_t* __restrict__ row_pair_start, int64_t id_capacity,
+    uint32_t* __restrict__ col_counts, int64_t* __restrict__ ranges) {
+  constexpr int kParts = kScanThreads / kMaxTileCols;  // 4
+  __shared__ uint32_t s_part[kParts][kMaxTileCols];
+  __shared__ uint32_t s_tmp[32];
+  const int y = blockIdx.x;
+  const int x = threadIdx.x % kMaxTileCols, part = threadIdx.x / kMaxTileCols;
+  const uint32_t c_begin = row_chunk_start[y], c_end = row_chunk_start[y + 1];
+  const uint32_t per = (c_end - c_begin + kParts - 1) / kParts;
+  const uint32_t c0 = c_begin + part * per < c_end ? c_begin + part * per : c_end;
+  const uint32_t c1 = c0 + per < c_end ? c0 + per : c_end;
+  uint32_t mine = 0;
+  if (x < cols)
+    for (uint32_t c = c0; c < c1; ++c) mine += col_counts[static_cast<int64_t>(c) * cols + x];
+  s_part[part][x] = mine;
+  __syncthreads();
+  // the row's pairs per column (threads of part 0, which come first in thread
+  // order, so the CTA-wide scan of their totals is the scan over columns)
+  uint32_t total = 0;
+  if (part == 0 && x < cols) {
+#pragma unroll
+    for (int q = 0; q < kParts; ++q) total += s_part[q][x];
+  }
+  uint32_t all;
+  const uint32_t before = wide_exclusive_scan(total, s_tmp, &all);
+  if (part == 0) {
+    const int64_t start = static_cast<int64_t>(row_pair_start[y]) + before;
+    const int64_t end = start + total;
+    if (x < cols) {
+      const int64_t t = static_cast<int64_t>(y) * cols + x;
+      ranges[2 * t] = start < id_capacity ? start : id_capacity;
+      ranges[2 * t + 1] = end < id_capacity ? end : id_capacity;
+    }
+    // each part's first position in the column's tile
+    uint32_t run = static_cast<uint32_t>(start);
+#pragma unroll
+    for (int q = 0; q < kParts; ++q) {
+      const uint32_t k = s_part[q][x];
+      s_part[q][x] = run;
+      run += k;
+    }
+  }
+  __syncthreads();
+  if (x < cols) {
+    uint32_t run = s_part[part][x];
+    for (uint32_t c = c0; c < c1; ++c) {
+      uint32_t* p = col_counts + static_cast<int64_t>(c) * cols + x;
+      const uint32_t k = *p;
+      *p = run;
+      run += k;
+    }
+  }
+}
+
+// Pass B, scatter: each chunk of one row's segments writes, for every tile
+// column a segment spans, its Gaussian id from the chunk's first position in
+// that tile on.
+__global__ void __launch_bounds__(kThreads) col_scatter_kernel(
+    const uint32_t* __restrict__ segs, const int4* __restrict__ bounds, int rows, int cols,
+    const uint32_t* __restrict__ row_seg_start, const uint32_t* __restrict__ row_chunk_start,
+    const uint32_t* __restrict__ chunk_row, const uint32_t* __restrict__ col_first,
+    int64_t id_capacity, int32_t* __restrict__ ids) {
+  __shared__ uint32_t s_cover[kWarps * kMaxTileCols];
+  __shared__ uint32_t s_base[kWarps * kMaxTileCols];
+  __shared__ uint32_t s_run[kMaxTileCols];
+  for (int i = threadIdx.x; i < kWarps * kMaxTileCols; i += kThreads) s_cover[i] = 0;
+  const uint32_t num_chunks = row_chunk_start[rows];
+  for (uint32_t c = blockIdx.x; c < num_chunks; c += gridDim.x) {  // uniform
+    for (int x = threadIdx.x; x < cols; x += kThreads)
+      s_run[x] = col_first[static_cast<int64_t>(c) * cols + x];
+    __syncthreads();
+    const uint32_t y = chunk_row[c];
+    const uint32_t s0 = row_seg_start[y] + (c - row_chunk_start[y]) * kChunkItems;
+    const uint32_t end = row_seg_start[y + 1];
+    for (int bt = 0; bt < kChunkBatches; ++bt) {
+      const uint32_t si = s0 + bt * kThreads + threadIdx.x;
+      uint32_t g = 0;
+      int x0 = 0, x1 = 0;
+      if (si < end && si < s0 + kChunkItems) {
+        g = segs[si];
+        const int2 span = __ldg(reinterpret_cast<const int2*>(bounds + g));
+        x0 = min(max(span.x, 0), cols);  // as clamp_rect
+        x1 = min(max(span.y, x0), cols);
+      }
+      scatter_batch(x0, x1, cols, s_cover, s_base, s_run, kMaxTileCols, [&](int, uint32_t pos) {
+        if (pos < id_capacity) ids[pos] = static_cast<int32_t>(g);
+      });
+    }
+  }
+}
+
 // ---------------------------------------------------------------- workspaces
 
 constexpr uint64_t kAlign = 256;
@@ -561,20 +957,18 @@ struct BinHeader {
 };
 
 struct CountLayout {
-  uint64_t header, depth_status, scan_status, zero_bytes;
-  uint64_t keys_a, keys_b, ids_a, ids_b, offsets, bytes;
+  uint64_t header, depth_status, zero_bytes;
+  uint64_t keys_a, keys_b, ids_a, ids_b, bytes;
   explicit CountLayout(int64_t n) {
     const uint64_t blocks = (n + kTile - 1) / kTile;
     uint64_t at = 0;
     header = at; at = align_up(at + sizeof(BinHeader));
     depth_status = at; at = align_up(at + blocks * kRadix * 4 * 4);
-    scan_status = at; at = align_up(at + blocks * 8);
     zero_bytes = at;
     keys_a = at; at = align_up(at + 4 * static_cast<uint64_t>(n));
     keys_b = at; at = align_up(at + 4 * static_cast<uint64_t>(n));
     ids_a = at; at = align_up(at + 4 * static_cast<uint64_t>(n));
     ids_b = at; at = align_up(at + 4 * static_cast<uint64_t>(n));
-    offsets = at; at = align_up(at + 4 * static_cast<uint64_t>(n));
     bytes = at;
   }
 };
@@ -585,11 +979,13 @@ inline int tile_bits(int64_t num_tiles) {
   return bits;
 }
 
-struct SortLayout {
+// Scratch of an LSD radix sort of `total` keys below num_keys (the tile sort
+// of the fallback path, and the deterministic backward's position sort).
+struct RadixLayout {
   uint64_t header, status, zero_bytes, keys_a, keys_b, values_a, values_b, bytes;
   int passes;
-  SortLayout(int64_t total, int64_t num_tiles) {
-    passes = (tile_bits(num_tiles) + 7) / 8;
+  RadixLayout(int64_t total, int64_t num_keys) {
+    passes = (tile_bits(num_keys) + 7) / 8;
     const uint64_t blocks = (total + kTile - 1) / kTile;
     uint64_t at = 0;
     header = at; at = align_up(at + sizeof(BinHeader));
@@ -599,6 +995,53 @@ struct SortLayout {
     keys_b = at; at = align_up(at + 4 * static_cast<uint64_t>(total));
     values_a = at; at = align_up(at + 4 * static_cast<uint64_t>(total));
     values_b = at; at = align_up(at + 4 * static_cast<uint64_t>(total));
+    bytes = at;
+  }
+};
+
+// Sort-phase scratch for n Gaussians, `total` intersections (the capacity)
+// and a tiles_w x tiles_h grid. The row/column path when the grid fits its
+// shared-memory tables, else the emit + tile radix sort path (which also
+// takes the count scan's offsets here).
+struct SortLayout {
+  bool rowcol;
+  int rows, cols;
+  uint64_t header, zero_bytes, bytes;
+  // row/column path
+  uint64_t chunks_a, max_chunks_b;
+  uint64_t seg_counts, pair_counts, row_segs, row_pairs, row_seg_start, row_pair_start,
+      row_chunk_start, chunk_row, col_counts, segs;
+  // radix path
+  uint64_t scan_status, offsets, radix;
+  RadixLayout lsd;
+  SortLayout(int64_t n, int64_t total, int tiles_w, int tiles_h)
+      : rows(tiles_h), cols(tiles_w), lsd(total, static_cast<int64_t>(tiles_w) * tiles_h) {
+    rowcol = tiles_h <= kMaxTileRows && tiles_w <= kMaxTileCols;
+    const uint64_t un = static_cast<uint64_t>(n), ut = static_cast<uint64_t>(total);
+    const uint64_t ur = static_cast<uint64_t>(rows), uc = static_cast<uint64_t>(cols);
+    uint64_t at = 0;
+    header = at; at = align_up(at + sizeof(BinHeader));
+    zero_bytes = at;
+    if (rowcol) {
+      chunks_a = (un + kChunkItems - 1) / kChunkItems;
+      max_chunks_b = (ut + kChunkItems - 1) / kChunkItems + ur;
+      seg_counts = at; at = align_up(at + 4 * ur * chunks_a);
+      pair_counts = at; at = align_up(at + 4 * ur * chunks_a);
+      row_segs = at; at = align_up(at + 4 * ur);
+      row_pairs = at; at = align_up(at + 4 * ur);
+      row_seg_start = at; at = align_up(at + 4 * (ur + 1));
+      row_pair_start = at; at = align_up(at + 4 * (ur + 1));
+      row_chunk_start = at; at = align_up(at + 4 * (ur + 1));
+      chunk_row = at; at = align_up(at + 4 * max_chunks_b);
+      col_counts = at; at = align_up(at + 4 * max_chunks_b * uc);
+      segs = at; at = align_up(at + 4 * ut);
+    } else {
+      chunks_a = max_chunks_b = 0;
+      scan_status = at; at = align_up(at + 8 * ((un + kTile - 1) / kTile));
+      zero_bytes = at;
+      offsets = at; at = align_up(at + 4 * un);
+      radix = at; at = align_up(at + lsd.bytes);
+    }
     bytes = at;
   }
 };
@@ -620,8 +1063,11 @@ inline unsigned upsweep_blocks(int64_t n) {
 }  // namespace
 
 uint64_t bin_count_workspace_size(int64_t n) { return CountLayout(n).bytes; }
-uint64_t bin_sort_workspace_size(int64_t total, int64_t num_tiles) {
-  return SortLayout(total, num_tiles).bytes;
+uint64_t bin_sort_workspace_size(int64_t n, int64_t total, const gs_params& p) {
+  return SortLayout(n, total, p.width / p.tile_size, p.height / p.tile_size).bytes;
+}
+uint64_t radix_sort_workspace_size(int64_t total, int64_t num_keys) {
+  return RadixLayout(total, num_keys).bytes;
 }
 
 // Where the depth-sorted Gaussian ids end up after the 4 passes.
@@ -667,6 +1113,9 @@ int32_t launch_bin_count_async(int64_t n, const float* projected_mean, const int
   return GS_OK;
 }
 
+// Depth order of the visible Gaussians (four stable 8-bit passes over the
+// depth bits) and, from the histogram upsweep, their number and the
+// intersection total (the sum of their tile counts).
 int32_t launch_bin_count_kernels(int64_t n, const float* projected_mean, const int32_t* counts,
                                  void* workspace, cudaStream_t stream) {
   const CountLayout L(n);
@@ -674,9 +1123,10 @@ int32_t launch_bin_count_kernels(int64_t n, const float* projected_mean, const i
   GS_CUDA_TRY(cudaMemsetAsync(workspace, 0, L.zero_bytes, stream));
   if (n > 0) {
     const int64_t blocks = (n + kTile - 1) / kTile;
+    static_assert(sizeof(h->total) == sizeof(unsigned long long), "64-bit total");
     upsweep_kernel<DepthSource, 4><<<upsweep_blocks(n), kThreads, 0, stream>>>(
         DepthSource{projected_mean, counts}, Count{n, nullptr}, 4, 0, &h->hist[0][0],
-        &h->num_valid);
+        &h->num_valid, reinterpret_cast<unsigned long long*>(&h->total));
     GS_TRY(check_launch());
     uint32_t* depth_status = at<uint32_t>(workspace, L.depth_status);
     uint32_t* kA = at<uint32_t>(workspace, L.keys_a);
@@ -700,46 +1150,109 @@ int32_t launch_bin_count_kernels(int64_t n, const float* projected_mean, const i
           &h->pass_counters[p], outs_k[p - 1], outs_v[p - 1], &h->error);
       GS_TRY(check_launch());
     }
-    count_scan_kernel<<<blocks, kThreads, 0, stream>>>(
-        at<uint32_t>(workspace, sorted_ids_offset(L)), &h->num_valid, counts,
-        at<uint64_t>(workspace, L.scan_status), &h->scan_counter,
-        at<uint32_t>(workspace, L.offsets), &h->total, &h->error);
+  }
+  return GS_OK;
+}
+
+// The row/column path (see the comment above kChunkBatches).
+static int32_t launch_bin_sort_rowcol(int64_t n, int64_t total, const int32_t* bounds,
+                                      const SortLayout& L, const void* count_workspace,
+                                      void* sort_workspace, int32_t* gaussian_ids,
+                                      int64_t* ranges, cudaStream_t stream) {
+  const CountLayout C(n);
+  const BinHeader* ch = at<BinHeader>(count_workspace, C.header);
+  const uint32_t* sorted_ids = at<uint32_t>(count_workspace, sorted_ids_offset(C));
+  const int4* b4 = reinterpret_cast<const int4*>(bounds);
+  const int rows = L.rows, cols = L.cols;
+  const int64_t pitch = static_cast<int64_t>(L.chunks_a);
+  const uint32_t capacity = static_cast<uint32_t>(total);  // segments and ids alike
+  uint32_t* seg_counts = at<uint32_t>(sort_workspace, L.seg_counts);
+  uint32_t* pair_counts = at<uint32_t>(sort_workspace, L.pair_counts);
+  uint32_t* row_segs = at<uint32_t>(sort_workspace, L.row_segs);
+  uint32_t* row_pairs = at<uint32_t>(sort_workspace, L.row_pairs);
+  uint32_t* row_seg_start = at<uint32_t>(sort_workspace, L.row_seg_start);
+  uint32_t* row_pair_start = at<uint32_t>(sort_workspace, L.row_pair_start);
+  uint32_t* row_chunk_start = at<uint32_t>(sort_workspace, L.row_chunk_start);
+  uint32_t* chunk_row = at<uint32_t>(sort_workspace, L.chunk_row);
+  uint32_t* col_counts = at<uint32_t>(sort_workspace, L.col_counts);
+  uint32_t* segs = at<uint32_t>(sort_workspace, L.segs);
+  if (n > 0) {
+    row_count_kernel<<<static_cast<unsigned>(L.chunks_a), kThreads, 0, stream>>>(
+        sorted_ids, &ch->num_valid, b4, rows, cols, pitch, seg_counts, pair_counts);
+    GS_TRY(check_launch());
+  }
+  row_scan_kernel<<<rows, kScanThreads, 0, stream>>>(&ch->num_valid, pitch, seg_counts,
+                                                     pair_counts, row_segs, row_pairs);
+  GS_TRY(check_launch());
+  row_layout_kernel<<<1, kScanThreads, 0, stream>>>(row_segs, row_pairs, rows, capacity,
+                                                    row_seg_start, row_pair_start,
+                                                    row_chunk_start, chunk_row);
+  GS_TRY(check_launch());
+  if (n > 0) {
+    row_scatter_kernel<<<static_cast<unsigned>(L.chunks_a), kThreads, 0, stream>>>(
+        sorted_ids, &ch->num_valid, b4, rows, cols, pitch, seg_counts, row_seg_start, capacity,
+        segs);
+    GS_TRY(check_launch());
+  }
+  const uint64_t grid_b = L.max_chunks_b < 8 * kSmCount ? L.max_chunks_b : 8 * kSmCount;
+  if (grid_b > 0) {
+    col_count_kernel<<<static_cast<unsigned>(grid_b), kThreads, 0, stream>>>(
+        segs, b4, rows, cols, row_seg_start, row_chunk_start, chunk_row, col_counts);
+    GS_TRY(check_launch());
+  }
+  col_scan_kernel<<<rows, kScanThreads, 0, stream>>>(cols, row_chunk_start, row_pair_start,
+                                                     total, col_counts, ranges);
+  GS_TRY(check_launch());
+  if (grid_b > 0 && total > 0) {
+    col_scatter_kernel<<<static_cast<unsigned>(grid_b), kThreads, 0, stream>>>(
+        segs, b4, rows, cols, row_seg_start, row_chunk_start, chunk_row, col_counts, total,
+        gaussian_ids);
     GS_TRY(check_launch());
   }
   return GS_OK;
 }
 
-// `total` is the capacity the buffers were sized for: the intersection total
-// itself, or more when the caller sized them before reading it. The kernels
-// read the true total from the count workspace and clamp it to the capacity
-// (an overflow leaves a wrong but in-bounds result, for the caller to redo).
-int32_t launch_bin_sort(int64_t n, int64_t total, const int32_t* bounds, const int32_t* counts,
-                        const gs_params& p, const void* count_workspace, void* sort_workspace,
-                        int32_t* gaussian_ids, int64_t* ranges, cudaStream_t stream) {
+// The fallback path for grids wider than the row/column tables: the count
+// scan's offsets, emission in depth order, a stable LSD radix sort of the
+// tile ids, then the ranges.
+static int32_t launch_bin_sort_radix(int64_t n, int64_t total, const int32_t* bounds,
+                                     const int32_t* counts, const gs_params& p,
+                                     const SortLayout& L, const void* count_workspace,
+                                     void* sort_workspace, int32_t* gaussian_ids,
+                                     int64_t* ranges, cudaStream_t stream) {
   const CountLayout C(n);
-  const int64_t tiles_w = p.width / p.tile_size;
-  const int64_t num_tiles = tiles_w * (p.height / p.tile_size);
-  const SortLayout L(total, num_tiles);
+  const int64_t tiles_w = L.cols;
+  const int64_t num_tiles = tiles_w * L.rows;
+  const RadixLayout& R = L.lsd;
   const BinHeader* ch = at<BinHeader>(count_workspace, C.header);
   BinHeader* h = at<BinHeader>(sort_workspace, L.header);
-  GS_CUDA_TRY(cudaMemsetAsync(sort_workspace, 0, L.zero_bytes, stream));
-  uint32_t* kA = at<uint32_t>(sort_workspace, L.keys_a);
-  uint32_t* kB = at<uint32_t>(sort_workspace, L.keys_b);
-  uint32_t* vA = at<uint32_t>(sort_workspace, L.values_a);
-  uint32_t* vB = at<uint32_t>(sort_workspace, L.values_b);
+  void* radix = at<char>(sort_workspace, L.radix);
+  BinHeader* rh = at<BinHeader>(radix, R.header);
+  GS_CUDA_TRY(cudaMemsetAsync(radix, 0, R.zero_bytes, stream));
+  uint32_t* kA = at<uint32_t>(radix, R.keys_a);
+  uint32_t* kB = at<uint32_t>(radix, R.keys_b);
+  uint32_t* vA = at<uint32_t>(radix, R.values_a);
+  uint32_t* vB = at<uint32_t>(radix, R.values_b);
   uint32_t* out_ids = reinterpret_cast<uint32_t*>(gaussian_ids);
+  uint32_t* offsets = at<uint32_t>(sort_workspace, L.offsets);
+  const uint32_t* sorted_ids = at<uint32_t>(count_workspace, sorted_ids_offset(C));
   const uint32_t* sorted_keys = kA;
   const Count live{total, nullptr, &ch->total};
+  if (n > 0) {
+    count_scan_kernel<<<(n + kTile - 1) / kTile, kThreads, 0, stream>>>(
+        sorted_ids, &ch->num_valid, counts, at<uint64_t>(sort_workspace, L.scan_status),
+        &h->scan_counter, offsets, &h->total, &h->error);
+    GS_TRY(check_launch());
+  }
   if (total > 0) {
-    const int passes = L.passes;
+    const int passes = R.passes;
     emit_kernel<<<ceil_div(n, kThreads), kThreads, 0, stream>>>(
-        at<uint32_t>(count_workspace, sorted_ids_offset(C)), &ch->num_valid,
-        at<uint32_t>(count_workspace, C.offsets), counts, reinterpret_cast<const int4*>(bounds),
+        sorted_ids, &ch->num_valid, offsets, counts, reinterpret_cast<const int4*>(bounds),
         static_cast<int>(tiles_w), total, kA, passes == 0 ? out_ids : vA);
     GS_TRY(check_launch());
     if (passes > 0) {
       upsweep_kernel<ArraySource, 16><<<upsweep_blocks(total), kThreads, 0, stream>>>(
-          ArraySource{kA, vA}, live, passes, 0, &h->hist[0][0], nullptr);
+          ArraySource{kA, vA}, live, passes, 0, &rh->hist[0][0], nullptr, nullptr);
       GS_TRY(check_launch());
       const int64_t blocks = (total + kTile - 1) / kTile;
       uint32_t* src_k = kA;
@@ -748,9 +1261,9 @@ int32_t launch_bin_sort(int64_t n, int64_t total, const int32_t* bounds, const i
         uint32_t* dst_k = (pass % 2 == 0) ? kB : kA;
         uint32_t* dst_v = (pass == passes - 1) ? out_ids : ((pass % 2 == 0) ? vB : vA);
         sort_pass_kernel<<<blocks, kThreads, 0, stream>>>(
-            ArraySource{src_k, src_v}, live, 8 * pass, &h->hist[pass][0],
-            at<uint32_t>(sort_workspace, L.status) + static_cast<int64_t>(pass) * blocks * kRadix,
-            &h->pass_counters[pass], dst_k, dst_v, &h->error);
+            ArraySource{src_k, src_v}, live, 8 * pass, &rh->hist[pass][0],
+            at<uint32_t>(radix, R.status) + static_cast<int64_t>(pass) * blocks * kRadix,
+            &rh->pass_counters[pass], dst_k, dst_v, &h->error);
         GS_TRY(check_launch());
         src_k = dst_k;
         src_v = dst_v;
@@ -766,16 +1279,33 @@ int32_t launch_bin_sort(int64_t n, int64_t total, const int32_t* bounds, const i
   return GS_OK;
 }
 
+// `total` is the capacity the buffers were sized for: the intersection total
+// itself, or more when the caller sized them before reading it. The kernels
+// read the true total from the count workspace and clamp to the capacity (an
+// overflow leaves a wrong but in-bounds result, for the caller to redo).
+int32_t launch_bin_sort(int64_t n, int64_t total, const int32_t* bounds, const int32_t* counts,
+                        const gs_params& p, const void* count_workspace, void* sort_workspace,
+                        int32_t* gaussian_ids, int64_t* ranges, cudaStream_t stream) {
+  const SortLayout L(n, total, p.width / p.tile_size, p.height / p.tile_size);
+  GS_CUDA_TRY(cudaMemsetAsync(sort_workspace, 0, L.zero_bytes, stream));
+  if (static_cast<int64_t>(L.rows) * L.cols == 0) return GS_OK;
+  if (L.rowcol)
+    return launch_bin_sort_rowcol(n, total, bounds, L, count_workspace, sort_workspace,
+                                  gaussian_ids, ranges, stream);
+  return launch_bin_sort_radix(n, total, bounds, counts, p, L, count_workspace, sort_workspace,
+                               gaussian_ids, ranges, stream);
+}
+
 // Stable sort of the positions 0..total-1 by keys[position] (< num_keys):
 // `order` receives the positions grouped by key, increasing within a key, and
 // segments [num_keys, 2] each key's [start, end) in `order`. The sort phase's
 // machinery on other keys: the deterministic backward groups the per-entry
 // gradient rows of each Gaussian this way. `workspace` holds
-// bin_sort_workspace_size(total, num_keys) bytes.
+// radix_sort_workspace_size(total, num_keys) bytes.
 int32_t launch_sort_positions(int64_t total, int64_t num_keys, const int32_t* keys,
                               void* workspace, uint32_t* order, int64_t* segments,
                               cudaStream_t stream) {
-  const SortLayout L(total, num_keys);
+  const RadixLayout L(total, num_keys);
   BinHeader* h = at<BinHeader>(workspace, L.header);
   GS_CUDA_TRY(cudaMemsetAsync(workspace, 0, L.zero_bytes, stream));
   uint32_t* kA = at<uint32_t>(workspace, L.keys_a);
@@ -789,7 +1319,7 @@ int32_t launch_sort_positions(int64_t total, int64_t num_keys, const int32_t* ke
   if (L.passes == 0 && num_keys > 1) return GS_ERR_INVALID_ARGUMENT;
   if (total > 0) {
     upsweep_kernel<PositionSource, 16><<<upsweep_blocks(total), kThreads, 0, stream>>>(
-        PositionSource{in_keys}, all, passes, 0, &h->hist[0][0], nullptr);
+        PositionSource{in_keys}, all, passes, 0, &h->hist[0][0], nullptr, nullptr);
     GS_TRY(check_launch());
     const int64_t blocks = (total + kTile - 1) / kTile;
     uint32_t* status = at<uint32_t>(workspace, L.status);

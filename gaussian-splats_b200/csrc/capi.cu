@@ -29,7 +29,7 @@ int32_t launch_project_bwd(int64_t, int32_t, const float*, const float*, const f
                            float*, float*, cudaStream_t);
 int32_t launch_det_math(int, int64_t, const float*, float*, cudaStream_t);
 uint64_t bin_count_workspace_size(int64_t);
-uint64_t bin_sort_workspace_size(int64_t, int64_t);
+uint64_t bin_sort_workspace_size(int64_t, int64_t, const gs_params&);
 uint64_t bin_error_word_offset();
 int32_t launch_bin_count(int64_t, const float*, const int32_t*, void*, int64_t*, uint32_t*,
                          cudaStream_t);
@@ -171,8 +171,9 @@ uint64_t gs_bin_count_workspace_size(int64_t n) {
   return gs::bin_count_workspace_size(n < 0 ? 0 : n);
 }
 
-uint64_t gs_bin_sort_workspace_size(int64_t total, int64_t num_tiles) {
-  return gs::bin_sort_workspace_size(total < 0 ? 0 : total, num_tiles < 0 ? 0 : num_tiles);
+uint64_t gs_bin_sort_workspace_size(int64_t n, int64_t total, const gs_params* params) {
+  if (gs::check_params(params) != GS_OK) return 0;
+  return gs::bin_sort_workspace_size(n < 0 ? 0 : n, total < 0 ? 0 : total, *params);
 }
 
 int32_t gs_bin_count(int64_t n, const float* projected_mean, const int32_t* counts,
@@ -197,10 +198,8 @@ int32_t gs_bin_sort(int64_t n, int64_t total, const int32_t* bounds, const int32
   GS_TRY(gs::check_params(params));
   if (n < 0 || n >= gs::kMaxGaussians || total < 0) return GS_ERR_INVALID_ARGUMENT;
   if (total >= gs::kMaxIntersections) return GS_ERR_CAPACITY;
-  const int64_t num_tiles = static_cast<int64_t>(params->width / params->tile_size) *
-                            (params->height / params->tile_size);
   if (count_workspace_bytes < gs::bin_count_workspace_size(n) ||
-      sort_workspace_bytes < gs::bin_sort_workspace_size(total, num_tiles))
+      sort_workspace_bytes < gs::bin_sort_workspace_size(n, total, *params))
     return GS_ERR_INVALID_ARGUMENT;
   if (!gs::aligned(count_workspace, 256) || !gs::aligned(sort_workspace, 256) ||
       !gs::aligned(bounds, 16))

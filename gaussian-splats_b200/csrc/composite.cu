@@ -51,7 +51,7 @@
 
 namespace gs {
 
-uint64_t bin_sort_workspace_size(int64_t, int64_t);
+uint64_t radix_sort_workspace_size(int64_t, int64_t);
 int32_t launch_sort_positions(int64_t, int64_t, const int32_t*, void*, uint32_t*, int64_t*,
                               cudaStream_t);
 
@@ -712,7 +712,7 @@ struct DeterministicLayout {
     rows = at; at = align(at + 36 * static_cast<uint64_t>(total));
     order = at; at = align(at + 4 * static_cast<uint64_t>(total));
     segments = at; at = align(at + 16 * static_cast<uint64_t>(n));
-    sort = at; at = align(at + bin_sort_workspace_size(total, n));
+    sort = at; at = align(at + radix_sort_workspace_size(total, n));
     bytes = at;
   }
 };
@@ -797,17 +797,30 @@ __device__ __forceinline__ uint32_t tile_work(const int64_t* __restrict__ ranges
 __global__ void __launch_bounds__(kOrderThreads) order_tiles_kernel(
     const int64_t* __restrict__ ranges, const uint32_t* __restrict__ work, int64_t num_tiles,
     int32_t* __restrict__ order) {
+  // A warp takes kOrderBatch tiles per lane at once, their loads in flight
+  // together: tiles t0 + i * kOrderThreads + lane.
+  constexpr int kOrderBatch = 8;
   __shared__ uint32_t s_next[kWorkClasses];
   const int lane = threadIdx.x & 31;
   const int64_t warp_first = threadIdx.x & ~31;
   const unsigned lower = (1u << lane) - 1u;
+  auto classes = [&](int64_t t0, int (&c)[kOrderBatch]) {
+#pragma unroll
+    for (int i = 0; i < kOrderBatch; ++i) {
+      const int64_t t = t0 + i * kOrderThreads + lane;
+      c[i] = t < num_tiles ? work_class(tile_work(ranges, work, t)) : kWorkClasses;
+    }
+  };
   if (threadIdx.x < kWorkClasses) s_next[threadIdx.x] = 0;
   __syncthreads();
-  for (int64_t t0 = warp_first; t0 < num_tiles; t0 += kOrderThreads) {  // warp-uniform
-    const int64_t t = t0 + lane;
-    const int c = t < num_tiles ? work_class(tile_work(ranges, work, t)) : kWorkClasses;
-    const unsigned peers = __match_any_sync(0xffffffffu, c);
-    if (c < kWorkClasses && (peers & lower) == 0) atomicAdd(&s_next[c], __popc(peers));
+  for (int64_t t0 = warp_first; t0 < num_tiles; t0 += kOrderThreads * kOrderBatch) {
+    int c[kOrderBatch];  // (t0 is warp-uniform)
+    classes(t0, c);
+#pragma unroll
+    for (int i = 0; i < kOrderBatch; ++i) {
+      const unsigned peers = __match_any_sync(0xffffffffu, c[i]);
+      if (c[i] < kWorkClasses && (peers & lower) == 0) atomicAdd(&s_next[c[i]], __popc(peers));
+    }
   }
   __syncthreads();
   if (threadIdx.x == 0) {  // exclusive offsets, heaviest class first
@@ -819,15 +832,19 @@ __global__ void __launch_bounds__(kOrderThreads) order_tiles_kernel(
     }
   }
   __syncthreads();
-  for (int64_t t0 = warp_first; t0 < num_tiles; t0 += kOrderThreads) {
-    const int64_t t = t0 + lane;
-    const int c = t < num_tiles ? work_class(tile_work(ranges, work, t)) : kWorkClasses;
-    const unsigned peers = __match_any_sync(0xffffffffu, c);
-    const int leader = __ffs(peers) - 1;
-    uint32_t base = 0;
-    if (c < kWorkClasses && lane == leader) base = atomicAdd(&s_next[c], __popc(peers));
-    base = __shfl_sync(0xffffffffu, base, leader);
-    if (c < kWorkClasses) order[base + __popc(peers & lower)] = static_cast<int32_t>(t);
+  for (int64_t t0 = warp_first; t0 < num_tiles; t0 += kOrderThreads * kOrderBatch) {
+    int c[kOrderBatch];
+    classes(t0, c);
+#pragma unroll
+    for (int i = 0; i < kOrderBatch; ++i) {
+      const unsigned peers = __match_any_sync(0xffffffffu, c[i]);
+      const int leader = __ffs(peers) - 1;
+      uint32_t base = 0;
+      if (c[i] < kWorkClasses && lane == leader) base = atomicAdd(&s_next[c[i]], __popc(peers));
+      base = __shfl_sync(0xffffffffu, base, leader);
+      if (c[i] < kWorkClasses)
+        order[base + __popc(peers & lower)] = static_cast<int32_t>(t0 + i * kOrderThreads + lane);
+    }
   }
 }
 
@@ -842,6 +859,7 @@ __global__ void __launch_bounds__(256) tile_max_contrib_kernel(
   const int x0 = static_cast<int>(t % tiles_w) * tile_size;
   const int y0 = static_cast<int>(t / tiles_w) * tile_size;
   int m = 0;
+#pragma unroll 4
   for (int k = lane; k < tile_size * tile_size; k += 32) {
     const int v = __ldg(n_contributors + static_cast<int64_t>(y0 + k / tile_size) * width + x0 +
                         k % tile_size);

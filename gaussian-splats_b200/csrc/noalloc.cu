@@ -30,7 +30,7 @@ int32_t launch_bin_count(int64_t, const float*, const int32_t*, void*, int64_t*,
 int32_t launch_bin_sort(int64_t, int64_t, const int32_t*, const int32_t*, const gs_params&,
                         const void*, void*, int32_t*, int64_t*, cudaStream_t);
 uint64_t bin_count_workspace_size(int64_t);
-uint64_t bin_sort_workspace_size(int64_t, int64_t);
+uint64_t bin_sort_workspace_size(int64_t, int64_t, const gs_params&);
 uint64_t bin_error_word_offset();
 
 namespace {
@@ -83,11 +83,8 @@ extern "C" int32_t gs_bin_noalloc(int64_t n, const float* projected_mean, const 
   GS_TRY(gs::launch_bin_count(n, projected_mean, counts, scratch, &total, &error, s));
   *total_host = total;
   if (error) return GS_ERR_TIMEOUT;
-  const int ts = params->tile_size;
-  const int64_t num_tiles =
-      static_cast<int64_t>(params->width / ts) * (params->height / ts);
   if (total > ids_capacity || total >= gs::kMaxIntersections ||
-      count_bytes + gs::bin_sort_workspace_size(total, num_tiles) > gs::kScratchBytes)
+      count_bytes + gs::bin_sort_workspace_size(n, total, *params) > gs::kScratchBytes)
     return GS_ERR_CAPACITY;  // *total_host says how many intersections there were
   char* sort_scratch = static_cast<char*>(scratch) + count_bytes;
   GS_TRY(gs::launch_bin_sort(n, total, bounds, counts, *params, scratch, sort_scratch,

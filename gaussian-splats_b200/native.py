@@ -221,7 +221,7 @@ def lib() -> ctypes.CDLL:
         "gs_bin_count_async": ([i64, vp, vp, vp, u64, vp, vp, vp], i32),
         "gs_bin_count_workspace_size": ([i64], u64),
         "gs_bin_sort": ([i64, i64, vp, vp, P, vp, u64, vp, u64, vp, vp, vp], i32),
-        "gs_bin_sort_workspace_size": ([i64, i64], u64),
+        "gs_bin_sort_workspace_size": ([i64, i64, P], u64),
         "gs_bin_check": ([vp, vp, vp], i32),
         "gs_bin_noalloc": ([i64, vp, vp, vp, P, vp, i64, vp, ctypes.POINTER(i64), vp], i32),
         "gs_tile_order": ([vp, vp, P, vp, vp, vp], i32),

@@ -280,7 +280,7 @@ def _rasterize(
 
         def sort_and_composite(capacity):
             gaussian_ids = torch.empty((capacity,), dtype=torch.int32, device=device)
-            sort_bytes = lib.gs_bin_sort_workspace_size(capacity, num_tiles)
+            sort_bytes = lib.gs_bin_sort_workspace_size(n, capacity, pref)
             sort_ws = torch.empty((sort_bytes,), dtype=torch.uint8, device=device)
             _mark("begin:bin_sort")
             native.check(lib.gs_bin_sort(
@@ -710,7 +710,7 @@ def rasterize_batch(
             pref = ctypes.byref(params[v])
             gaussian_ids = torch.empty((total,), dtype=torch.int32, device=device)
             ranges = torch.empty((num_tiles, 2), dtype=torch.int64, device=device)
-            sort_bytes = lib.gs_bin_sort_workspace_size(total, num_tiles)
+            sort_bytes = lib.gs_bin_sort_workspace_size(n, total, pref)
             sort_ws = torch.empty((sort_bytes,), dtype=torch.uint8, device=device)
             native.check(lib.gs_bin_sort(
                 n, total, _ptr(bounds[v]), _ptr(counts[v]), pref, _ptr(count_ws[v]),

@@ -137,7 +137,7 @@ int32_t gs_bin_count_async(int64_t n, const float *projected_mean, const int32_t
  * the reference's stable sort of (tile << 32 | depth bits) keys emitted in
  * Gaussian order; ranges [num_tiles, 2] receives each tile's [start, end).
  * count_workspace is the buffer gs_bin_count (or gs_bin_count_async) filled;
- * sort_workspace holds gs_bin_sort_workspace_size(total, num_tiles) bytes of
+ * sort_workspace holds gs_bin_sort_workspace_size(n, total, params) bytes of
  * scratch. `total` may be any capacity at least the intersection total: the
  * kernels read the true total from count_workspace, so the call can be
  * enqueued before the total reaches the host; gaussian_ids then holds its
@@ -149,7 +149,7 @@ int32_t gs_bin_sort(int64_t n, int64_t total, const int32_t *bounds, const int32
                     uint64_t count_workspace_bytes, void *sort_workspace,
                     uint64_t sort_workspace_bytes, int32_t *gaussian_ids, int64_t *ranges,
                     gs_stream_t stream);
-uint64_t gs_bin_sort_workspace_size(int64_t total, int64_t num_tiles);
+uint64_t gs_bin_sort_workspace_size(int64_t n, int64_t total, const gs_params *params);
 
 /* Binning without any device allocation, for callers that cannot allocate
  * (no counterpart in the reference). Some callers have no workspace to hand
@@ -160,10 +160,13 @@ uint64_t gs_bin_sort_workspace_size(int64_t total, int64_t num_tiles);
  * library (held on every GPU that loads the library until the process exits);
  * it never calls cudaMalloc or cudaFree.
  *  - Limit: the count-phase scratch for n Gaussians plus the sort-phase
- *    scratch for the intersection total must fit in 64 MiB (about 21 bytes
- *    per Gaussian plus 16.3 bytes per intersection; e.g. 1M Gaussians with
- *    up to 2.6M intersections). Larger inputs return GS_ERR_CAPACITY, as does
- *    a total above ids_capacity; *total_host still reports the total.
+ *    scratch for the intersection total must fit in 64 MiB (at 1920x1088
+ *    with 16x16 tiles about 18 bytes per Gaussian plus 4.5 bytes per
+ *    intersection: e.g. 1M Gaussians with up to 10M intersections; a grid of
+ *    more than 256 tile columns or 512 tile rows bins by radix sort, about
+ *    16.3 bytes per intersection). Larger inputs return
+ *    GS_ERR_CAPACITY, as does a total above ids_capacity; *total_host still
+ *    reports the total.
  *  - The first call on a device looks up the array's device address
  *    (cudaGetSymbolAddress), so make that first call before any stream
  *    capture.

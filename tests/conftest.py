@@ -164,7 +164,7 @@ def run_binning(bounds, depths, counts, tiles_w, tiles_h, tile_size=4):
     total = total.value
     ids = torch.empty(total, dtype=torch.int32, device="cuda")
     ranges = torch.empty((num_tiles, 2), dtype=torch.int64, device="cuda")
-    sbytes = lib.gs_bin_sort_workspace_size(total, num_tiles)
+    sbytes = lib.gs_bin_sort_workspace_size(n, total, ctypes.byref(params))
     sws = torch.empty(sbytes, dtype=torch.uint8, device="cuda")
     native.check(lib.gs_bin_sort(n, total, ptr(d_bounds), ptr(d_counts), ctypes.byref(params),
                                  ptr(cws), cbytes, ptr(sws), sbytes, ptr(ids), ptr(ranges),

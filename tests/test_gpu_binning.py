@@ -116,3 +116,26 @@ def test_negative_depths_sort_like_unsigned_bits(oracle):
     b, d, c = _random_case(rng, 3000, 8, 8, max_extent=3)
     d[::3] *= -1.0
     _check(oracle, b, d, c, 8, 8)
+
+
+@pytest.mark.parametrize("tiles_w,tiles_h", [
+    (240, 135),   # a 4K view at 16x16 tiles: row/column path
+    (256, 512),   # the largest grid the row/column path takes
+    (257, 6),     # one tile column too many for its tables: radix path
+    (32, 513),    # one tile row too many: radix path
+])
+def test_grid_shapes_and_both_paths(oracle, tiles_w, tiles_h):
+    """Both sort-phase paths (row/column scatter; emit + tile radix sort) and
+    the edges between them give the same bit-exact lists."""
+    rng = np.random.default_rng(tiles_w * 7 + tiles_h)
+    b, d, c = _random_case(rng, 40000, tiles_w, tiles_h, max_extent=12, culled=0.1)
+    ids, ranges = _check(oracle, b, d, c, tiles_w, tiles_h)
+    assert len(ids) > 0
+
+
+def test_one_row_many_segments(oracle):
+    """Every Gaussian in one tile row: one row's segments span many pass-B
+    chunks, whose look-back runs within the row."""
+    rng = np.random.default_rng(9)
+    b, d, c = _random_case(rng, 200_000, 120, 1, max_extent=5)
+    _check(oracle, b, d, c, 120, 1)

@@ -48,15 +48,27 @@ def test_version(lib):
 
 
 def test_workspace_sizes(lib):
+    from gaussian_splats_b200 import native
+
     # Grow with the problem, stay 256-byte granular, and are pure host queries.
     small = lib.gs_bin_count_workspace_size(1000)
     large = lib.gs_bin_count_workspace_size(1_000_000)
     assert 0 < small < large and small % 256 == 0 and large % 256 == 0
-    # Count phase holds 5 arrays of n 32-bit words plus per-tile status.
-    assert large >= 20 * 1_000_000
-    s0 = lib.gs_bin_sort_workspace_size(0, 8160)
-    s1 = lib.gs_bin_sort_workspace_size(5_000_000, 8160)
-    assert s0 < s1 and s1 >= 16 * 5_000_000
+    # Count phase holds 4 arrays of n 32-bit words plus per-tile status.
+    assert large >= 16 * 1_000_000
+    # Sort phase: a 1920x1088 view at 16x16 tiles (the row/column path holds
+    # a segment array of the capacity), and a grid too wide for its tables
+    # (the radix path: keys and values twice over).
+    wide = native.make_params(500.0, 500.0, 4160.0, 8.0, 8320, 16, 4, 0.999, 0.2, 100.0,
+                              "gaussian", 0.95)
+    view = native.make_params(1000.0, 1000.0, 960.0, 540.0, 1920, 1088, 16, 0.999, 0.2, 100.0,
+                              "gaussian", 0.95)
+    s0 = lib.gs_bin_sort_workspace_size(1_000_000, 0, ctypes.byref(view))
+    s1 = lib.gs_bin_sort_workspace_size(1_000_000, 5_000_000, ctypes.byref(view))
+    assert s0 < s1 and s1 >= 4 * 5_000_000
+    w1 = lib.gs_bin_sort_workspace_size(1_000_000, 5_000_000, ctypes.byref(wide))
+    assert w1 >= 16 * 5_000_000
+    assert lib.gs_bin_sort_workspace_size(1000, 1000, None) == 0  # invalid parameters
     assert lib.gs_bin_count_workspace_size(0) > 0
 
 

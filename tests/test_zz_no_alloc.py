@@ -64,7 +64,7 @@ def _regular(lib, native, params, pm, counts, bounds):
                                   ctypes.byref(total), stream), "gs_bin_count")
     ids = torch.empty(total.value, dtype=torch.int32, device="cuda")
     ranges = torch.empty((num_tiles, 2), dtype=torch.int64, device="cuda")
-    sbytes = lib.gs_bin_sort_workspace_size(total.value, num_tiles)
+    sbytes = lib.gs_bin_sort_workspace_size(n, total.value, ctypes.byref(params))
     sws = torch.empty(sbytes, dtype=torch.uint8, device="cuda")
     native.check(lib.gs_bin_sort(n, total.value, _ptr(bounds), _ptr(counts), ctypes.byref(params),
                                  _ptr(cws), cbytes, _ptr(sws), sbytes, _ptr(ids), _ptr(ranges),
@@ -127,16 +127,21 @@ SCRATCH_BYTES = 64 << 20  # the library's fixed scratch array
 def _synthetic_tiles(n, tiles_w, tiles_h, total, seed):
     """n Gaussians as the binning reads them -- depths, per-Gaussian tile
     counts and tile rectangles with count == area -- whose counts add up to
-    exactly `total` (rows of 1 x w rectangles take up the remainder)."""
+    exactly `total`: some rectangles cover the whole grid, the others are
+    random and rows of 1 x w rectangles take up the remainder."""
     rng = np.random.default_rng(seed)
-    widths = rng.integers(1, 17, n)
-    heights = rng.integers(1, 9, n)
+    grid = tiles_w * tiles_h
+    full = max(0, (total - 24 * n) // grid)  # whole-grid rectangles
+    m = n - full
+    widths = rng.integers(1, 17, m)
+    heights = rng.integers(1, 9, m)
     heights[::2] = 1  # half the rows stay one tile high, to take the remainder
     area = widths * heights
+    rest = total - full * grid
     # Scale the random rectangles down until they leave room for the rest.
-    keep = np.cumsum(area) <= total - (n - np.arange(1, n + 1))
+    keep = np.cumsum(area) <= rest - (m - np.arange(1, m + 1))
     widths[~keep], heights[~keep] = 1, 1
-    remainder = total - int((widths * heights).sum())
+    remainder = rest - int((widths * heights).sum())
     row = 0
     while remainder > 0:  # widen single-row rectangles, up to a full row each
         if heights[row] == 1:
@@ -144,6 +149,10 @@ def _synthetic_tiles(n, tiles_w, tiles_h, total, seed):
             widths[row] += add
             remainder -= add
         row += 1
+    widths = np.concatenate([widths, np.full(full, tiles_w)])
+    heights = np.concatenate([heights, np.full(full, tiles_h)])
+    order = rng.permutation(n)
+    widths, heights = widths[order], heights[order]
     assert int((widths * heights).sum()) == total
     x0 = rng.integers(0, tiles_w - widths + 1)
     y0 = rng.integers(0, tiles_h - heights + 1)
@@ -170,7 +179,8 @@ def test_noalloc_limit_is_the_documented_scratch_size():
     count_bytes = (lib.gs_bin_count_workspace_size(n) + 255) // 256 * 256
 
     def fits(t):
-        return count_bytes + lib.gs_bin_sort_workspace_size(t, num_tiles) <= SCRATCH_BYTES
+        return (count_bytes + lib.gs_bin_sort_workspace_size(n, t, ctypes.byref(params))
+                <= SCRATCH_BYTES)
 
     lo, hi = 0, SCRATCH_BYTES // 4
     while lo + 1 < hi:  # largest total that fits
@@ -178,7 +188,9 @@ def test_noalloc_limit_is_the_documented_scratch_size():
         lo, hi = (mid, hi) if fits(mid) else (lo, mid)
     limit = lo
     assert fits(limit) and not fits(limit + 1)
-    assert 3_000_000 < limit < 4_100_000  # ~16.3 B per intersection after ~2 MB for n
+    # ~18 B per Gaussian, then ~4.3 B per intersection at 64x64 tiles (the
+    # row/column path's segment array and pass-B status)
+    assert 14_000_000 < limit < 16_500_000
 
     pm, counts, bounds = _synthetic_tiles(n, tiles_w, tiles_h, limit, seed=5)
     ref_ids, ref_ranges = _regular(lib, native, params, pm, counts, bounds)
