@@ -298,13 +298,15 @@ def kernel_durations(outputs, params, camera, grad_image, settings, device, repe
     out_records = torch.empty_like(records)
     # the compositors' heavy-first tile orders, as the operator computes them per view
     fwd_order = torch.empty((ranges.shape[0],), dtype=torch.int32, device=device)
-    bwd_order = torch.empty_like(fwd_order)
-    tile_work = torch.empty_like(fwd_order)
-    native.check(lib.gs_tile_order(P(ranges), None, pref, P(fwd_order), None, stream),
+    order_work = torch.empty((ranges.shape[0] + 128,), dtype=torch.int32, device=device)
+    native.check(lib.gs_tile_order(P(ranges), None, pref, P(fwd_order), P(order_work), stream),
                  "gs_tile_order")
+    bwd_plan = torch.empty((lib.gs_composite_bwd_plan_size(pref),), dtype=torch.uint8,
+                           device=device)
     if grad_image is not None:
-        native.check(lib.gs_tile_order(P(ranges), P(n_contrib), pref, P(bwd_order),
-                                       P(tile_work), stream), "gs_tile_order")
+        native.check(lib.gs_composite_bwd_plan(P(ranges), P(n_contrib), pref, 0, P(bwd_plan),
+                                               bwd_plan.numel(), stream),
+                     "gs_composite_bwd_plan")
     launches = {
         "project_fwd": lambda: lib.gs_project_fwd(
             n, k, P(mean), P(rotation), P(scale), P(opacity), P(color), P(cam_r), P(cam_t), pref,
@@ -317,7 +319,7 @@ def kernel_durations(outputs, params, camera, grad_image, settings, device, repe
     if grad_image is not None:
         launches["composite_bwd"] = lambda: lib.gs_composite_bwd(
             n, P(records), P(ids), P(ranges), P(grad_image), P(final_t), P(n_contrib), pref,
-            P(grad_projected), P(bwd_order), stream)
+            P(grad_projected), P(bwd_plan), stream)
         launches["project_bwd"] = lambda: lib.gs_project_bwd(
             n, k, P(mean), P(rotation), P(scale), P(opacity), P(color), P(cam_r), P(cam_t),
             P(conic), P(grad_projected), P(counts), pref, *(P(g) for g in grads), stream)

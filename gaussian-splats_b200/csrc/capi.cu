@@ -38,8 +38,11 @@ int32_t launch_bin_sort(int64_t, int64_t, const int32_t*, const int32_t*, const 
 int32_t launch_composite_fwd(const float*, const int32_t*, const int64_t*, const gs_params&,
                              float*, float*, int32_t*, const int32_t*, cudaStream_t);
 int32_t launch_composite_bwd(int64_t, const float*, const int32_t*, const int64_t*, const float*,
-                             const float*, const int32_t*, const gs_params&, float*,
-                             const int32_t*, cudaStream_t);
+                             const float*, const int32_t*, const gs_params&, float*, void*,
+                             cudaStream_t);
+uint64_t composite_bwd_plan_size(const gs_params&);
+int32_t launch_composite_bwd_plan(const int64_t*, const int32_t*, const gs_params&, int, void*,
+                                  cudaStream_t);
 int32_t launch_tile_order(const int64_t*, const int32_t*, const gs_params&, int32_t*, uint32_t*,
                           cudaStream_t);
 uint64_t composite_bwd_deterministic_workspace_size(int64_t, int64_t);
@@ -226,8 +229,7 @@ int32_t gs_tile_order(const int64_t* ranges, const int32_t* n_contributors,
                       const gs_params* params, int32_t* tile_order, uint32_t* tile_work,
                       gs_stream_t stream) {
   GS_TRY(gs::check_params(params));
-  if (!tile_order || (n_contributors && !tile_work) || (!n_contributors && !ranges))
-    return GS_ERR_INVALID_ARGUMENT;
+  if (!tile_order || !tile_work || !ranges) return GS_ERR_INVALID_ARGUMENT;
   return gs::launch_tile_order(ranges, n_contributors, *params, tile_order, tile_work,
                                as_cuda(stream));
 }
@@ -246,14 +248,30 @@ int32_t gs_composite_fwd(const float* records, const int32_t* gaussian_ids,
 int32_t gs_composite_bwd(int64_t n, const float* records, const int32_t* gaussian_ids,
                          const int64_t* ranges, const float* grad_image,
                          const float* final_transmittance, const int32_t* n_contributors,
-                         const gs_params* params, float* grad_projected,
-                         const int32_t* tile_order, gs_stream_t stream) {
+                         const gs_params* params, float* grad_projected, const void* plan,
+                         gs_stream_t stream) {
   GS_TRY(gs::check_params(params));
   if (n < 0) return GS_ERR_INVALID_ARGUMENT;
-  if (!gs::aligned(records, 16)) return GS_ERR_MISALIGNED;
+  if (!gs::aligned(records, 16) || !gs::aligned(plan, 256)) return GS_ERR_MISALIGNED;
   return gs::launch_composite_bwd(n, records, gaussian_ids, ranges, grad_image,
                                   final_transmittance, n_contributors, *params, grad_projected,
-                                  tile_order, as_cuda(stream));
+                                  const_cast<void*>(plan), as_cuda(stream));
+}
+
+uint64_t gs_composite_bwd_plan_size(const gs_params* params) {
+  if (gs::check_params(params) != GS_OK) return 0;
+  return gs::composite_bwd_plan_size(*params);
+}
+
+int32_t gs_composite_bwd_plan(const int64_t* ranges, const int32_t* n_contributors,
+                              const gs_params* params, int32_t split_walk, void* plan,
+                              uint64_t plan_bytes, gs_stream_t stream) {
+  GS_TRY(gs::check_params(params));
+  if (!ranges || !n_contributors || !plan || split_walk < 0) return GS_ERR_INVALID_ARGUMENT;
+  if (plan_bytes < gs::composite_bwd_plan_size(*params)) return GS_ERR_INVALID_ARGUMENT;
+  if (!gs::aligned(plan, 256)) return GS_ERR_MISALIGNED;
+  return gs::launch_composite_bwd_plan(ranges, n_contributors, *params, split_walk, plan,
+                                       as_cuda(stream));
 }
 
 uint64_t gs_composite_bwd_deterministic_workspace_size(int64_t n, int64_t total) {

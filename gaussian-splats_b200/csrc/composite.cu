@@ -336,6 +336,15 @@ struct BackwardBatch {
       TileShape<TS, PPT>::kBatch < kMax ? TileShape<TS, PPT>::kBatch : kMax;
 };
 
+// Walk tags of the backward kernel (a walk accumulates only the suffix, or
+// the gradients too).
+struct SuffixPass {
+  static constexpr bool value = true;
+};
+struct GradientPass {
+  static constexpr bool value = false;
+};
+
 // kRows: the deterministic form. Instead of adding each warp's reduced
 // 9-vector into grad_projected[g] with atomics, every warp leaves it in shared
 // memory, and after each batch the CTA sums the warps' vectors in warp order
@@ -343,6 +352,17 @@ struct BackwardBatch {
 // reaches stay as the caller zeroed them). reduce_rows_kernel then adds each
 // Gaussian's rows in list-position order. No float addition depends on
 // scheduling, so the gradients are the same bits on every run.
+//
+// Split tiles. A tile whose walk is long is split into `parts` consecutive
+// sub-ranges of its list, each a CTA of its own, so that one dense tile no
+// longer sets the kernel's length. Part k needs the transmittance product and
+// composited colour of every entry behind it: its CTA first walks the parts
+// behind it accumulating only that suffix (the same per-pair decisions and
+// the same recurrence, so the same bits as an unsplit walk at that point, at
+// about a third of the per-entry cost: no gradients, reductions or atomics),
+// then walks its own part with gradients. `items`, when given, lists the work
+// of the launch: (tile, part, parts, -), tile -1 for none; else `tile_order`
+// (or row-major order) gives whole tiles.
 template <int TS, int PPT, bool kGaussian, bool kRows = false>
 __global__ void __launch_bounds__(TileShape<TS, PPT>::kThreads,
                                   min_blocks_for_32_warps(TileShape<TS, PPT>::kThreads))
@@ -352,7 +372,7 @@ __global__ void __launch_bounds__(TileShape<TS, PPT>::kThreads,
                          const float* __restrict__ final_transmittance,
                          const int32_t* __restrict__ n_contributors, const gs_params p,
                          float* __restrict__ grad_projected,
-                         const int32_t* __restrict__ tile_order) {
+                         const int32_t* __restrict__ tile_order, const int4* __restrict__ items) {
   using S = TileShape<TS, PPT>;
   // (the deterministic form's per-warp vectors of 32 x 32 tiles take smaller batches
   // to stay within 48 KB of shared memory)
@@ -369,8 +389,14 @@ __global__ void __launch_bounds__(TileShape<TS, PPT>::kThreads,
   __shared__ StageBuffer<NB> s_buf[kBuffers];
   __shared__ uint16_t s_list[S::kWarps][NB];
   __shared__ int s_max_contrib;
-  const int tile = visit_tile(tile_order, p);
+  int4 item = make_int4(0, 0, 1, 0);  // (tile, part, parts, -)
+  if (items != nullptr)
+    item = items[blockIdx.x];
+  else
+    item.x = visit_tile(tile_order, p);
+  const int tile = item.x;
   if (tile < 0) return;
+  const int part = item.y, parts = item.z;
   const int tid = threadIdx.x;
   const int lane = tid % S::kWarpLanes, warp = tid / S::kWarpLanes;
   const PixelMap<TS, PPT> pm(tile, p.width / TS, tid);
@@ -398,26 +424,15 @@ __global__ void __launch_bounds__(TileShape<TS, PPT>::kThreads,
   const int64_t start = ranges[2 * tile];
   int64_t end = ranges[2 * tile + 1];
   if (end > start + s_max_contrib) end = start + s_max_contrib;  // composite_bwd.py:81-83
-
-  // Batches walk back to front: [max(start, batch_end - NB), batch_end). Slot
-  // tid + s * kThreads of each batch is this thread's to stage; the ids of its
-  // next batch's slots are loaded one batch ahead.
-  int32_t next_id[kStage];
-  {
-    const int64_t first = end - NB > start ? end - NB : start;
-#pragma unroll
-    for (int s = 0; s < kStage; ++s) {
-      const int slot = tid + s * S::kThreads;
-      if (slot < NB && first + slot < end)
-        stage_async(records, __ldg(gaussian_ids + first + slot), s_buf[0], slot);
-      const int64_t first2 = first - NB > start ? first - NB : start;
-      next_id[s] = slot < NB && first2 + slot < first ? __ldg(gaussian_ids + first2 + slot) : 0;
-    }
+  // This CTA's part of the walk: [part_lo, part_hi) back to front (the
+  // whole walk unless the tile is split; positions stay relative to the
+  // tile's start), after the suffix of [part_hi, end).
+  int64_t part_lo = start, part_hi = end;
+  if (parts > 1) {
+    const int64_t chunk = (end - start + parts - 1) / parts;
+    part_lo = start + part * chunk < end ? start + part * chunk : end;
+    part_hi = part_lo + chunk < end ? part_lo + chunk : end;
   }
-  cp_async_commit();
-  cp_async_wait_all();
-  __syncthreads();
-
   uint16_t* list = s_list[warp];
   float st[Q], sr[Q], sg[Q], sb[Q];  // suffix behind the current entry
 #pragma unroll
@@ -425,14 +440,39 @@ __global__ void __launch_bounds__(TileShape<TS, PPT>::kThreads,
     st[q] = 1.0f;
     sr[q] = sg[q] = sb[q] = 0.0f;
   }
+  // One walk over [lo, hi) back to front; with a SuffixPass tag the suffix
+  // recurrence only.
+  auto walk = [&](auto pass, const int64_t lo, const int64_t hi) {
+  constexpr bool kSuffix = decltype(pass)::value;
+  const int64_t end = hi;
+
+  // Batches walk back to front: [max(start, batch_end - NB), batch_end). Slot
+  // tid + s * kThreads of each batch is this thread's to stage; the ids of its
+  // next batch's slots are loaded one batch ahead.
+  int32_t next_id[kStage];
+  {
+    const int64_t first = end - NB > lo ? end - NB : lo;
+#pragma unroll
+    for (int s = 0; s < kStage; ++s) {
+      const int slot = tid + s * S::kThreads;
+      if (slot < NB && first + slot < end)
+        stage_async(records, __ldg(gaussian_ids + first + slot), s_buf[0], slot);
+      const int64_t first2 = first - NB > lo ? first - NB : lo;
+      next_id[s] = slot < NB && first2 + slot < first ? __ldg(gaussian_ids + first2 + slot) : 0;
+    }
+  }
+  cp_async_commit();
+  cp_async_wait_all();
+  __syncthreads();
+
   int buf = 0;
-  for (int64_t batch_end = end; batch_end > start;
+  for (int64_t batch_end = end; batch_end > lo;
        batch_end -= NB, buf = kBackwardDoubleBuffer ? buf ^ 1 : 0) {
-    const int64_t batch_start = batch_end - NB > start ? batch_end - NB : start;
+    const int64_t batch_start = batch_end - NB > lo ? batch_end - NB : lo;
     // the next (earlier) batch's records fill the other buffer meanwhile
-    if (kBackwardDoubleBuffer && batch_start > start) {
-      const int64_t next_start = batch_start - NB > start ? batch_start - NB : start;
-      const int64_t after_start = next_start - NB > start ? next_start - NB : start;
+    if (kBackwardDoubleBuffer && batch_start > lo) {
+      const int64_t next_start = batch_start - NB > lo ? batch_start - NB : lo;
+      const int64_t after_start = next_start - NB > lo ? next_start - NB : lo;
 #pragma unroll
       for (int s = 0; s < kStage; ++s) {
         const int slot = tid + s * S::kThreads;
@@ -459,6 +499,7 @@ __global__ void __launch_bounds__(TileShape<TS, PPT>::kThreads,
       const float4 b = cur.b[j];
       const float dx = fpx - a.x;
       const float xx = a.z, xy = b.w, yy = b.x, o = b.y;
+      (void)xy;  // (not read by the ellipsoid suffix pass)
       const float adx = xx * dx, bdx = a.w * dx;
 #pragma unroll
       for (int q = 0; q < Q; ++q) {
@@ -477,6 +518,14 @@ __global__ void __launch_bounds__(TileShape<TS, PPT>::kThreads,
         if (!(alpha >= kAlphaMin)) continue;
         active = true;
         const float4 c = cur.c[j];
+        if constexpr (kSuffix) {  // the recurrence only (same expressions as below)
+          const float local_t = 1.0f - alpha;
+          sr[q] = fmaf(local_t, sr[q], alpha * c.x);
+          sg[q] = fmaf(local_t, sg[q], alpha * c.y);
+          sb[q] = fmaf(local_t, sb[q], alpha * c.z);
+          st[q] = st[q] * local_t;
+          continue;
+        }
         const float denominator = fmaxf(st[q] * (1.0f - alpha), 1e-4f);
         // T in front of the entry. The quotient only feeds gradients and the
         // termination re-test of the gradient path (tolerance-checked), so it
@@ -512,7 +561,7 @@ __global__ void __launch_bounds__(TileShape<TS, PPT>::kThreads,
         sb[q] = fmaf(local_t, sb[q], alpha * c.z);
         st[q] = st[q] * local_t;
       }
-      if (__any_sync(kMask, active)) {
+      if (!kSuffix && __any_sync(kMask, active)) {
         const int g = __float_as_int(cur.c[j].w);
         float* dst = kRows ? s_part[kRows ? warp : 0][kRows ? j : 0]
                            : grad_projected + 9 * static_cast<int64_t>(g);
@@ -566,9 +615,9 @@ __global__ void __launch_bounds__(TileShape<TS, PPT>::kThreads,
     } else {
       // one buffer: refill it once every warp is done with it
       __syncthreads();
-      if (batch_start > start) {
-        const int64_t next_start = batch_start - NB > start ? batch_start - NB : start;
-        const int64_t after_start = next_start - NB > start ? next_start - NB : start;
+      if (batch_start > lo) {
+        const int64_t next_start = batch_start - NB > lo ? batch_start - NB : lo;
+        const int64_t after_start = next_start - NB > lo ? next_start - NB : lo;
 #pragma unroll
         for (int s = 0; s < kStage; ++s) {
           const int slot = tid + s * S::kThreads;
@@ -584,6 +633,9 @@ __global__ void __launch_bounds__(TileShape<TS, PPT>::kThreads,
       __syncthreads();
     }
   }
+  };  // walk
+  if (part_hi < end) walk(SuffixPass{}, part_hi, end);
+  walk(GradientPass{}, part_lo, part_hi);
 }
 
 // Pixels per thread of the backward: two, so one warp reduction and one set
@@ -656,6 +708,293 @@ __global__ void __launch_bounds__(256) reduce_rows_kernel(
   for (int c = 0; c < 9; ++c) grad_projected[9 * g + c] = acc[c];
 }
 
+// ------------------------------------------------------ heavy-first tile order
+//
+// The compositors take a tile per CTA in CTA order. Tile costs are very
+// uneven (config 5's densest tile walks 850k pixel-Gaussian pairs, the mean
+// 47k; alone it takes half the backward's time), and in row-major order the
+// heavy central tiles start mid-launch on SMs already full of other tiles, so
+// they finish last. Visiting tiles by decreasing work starts them first.
+// Work classes are a quarter octave wide; order within a class is arbitrary
+// (no result depends on which CTA composites a tile).
+
+constexpr int kWorkClasses = 64;
+
+// Lanes of the warp holding the same class as this lane (classes 0..64, 64
+// marking no tile): one ballot per bit, cheaper than a match instruction.
+__device__ __forceinline__ unsigned same_class_lanes(int c) {
+  unsigned peers = 0xffffffffu;
+#pragma unroll
+  for (int bit = 0; bit < 7; ++bit) {
+    const bool set = (c >> bit) & 1;
+    const unsigned vote = __ballot_sync(0xffffffffu, set);
+    peers &= set ? vote : ~vote;
+  }
+  return peers;
+}
+
+// 0 for no work, else 1 + 4 floor(log2 w) + the two bits of w below its
+// leading one, capped at 63.
+__device__ __forceinline__ int work_class(uint32_t w) {
+  if (w == 0) return 0;
+  const int b = 31 - __clz(w);
+  const int frac = b >= 2 ? static_cast<int>((w >> (b - 2)) & 3u) : static_cast<int>((w << (2 - b)) & 3u);
+  const int c = 1 + 4 * b + frac;
+  return c < kWorkClasses - 1 ? c : kWorkClasses - 1;
+}
+
+__device__ __forceinline__ uint32_t tile_work(const int64_t* __restrict__ ranges,
+                                              const uint32_t* __restrict__ work, int64_t t) {
+  if (work) return __ldg(work + t);
+  const int64_t len = ranges[2 * t + 1] - ranges[2 * t];
+  return len <= 0 ? 0u : (len >= 0xffffffffLL ? 0xffffffffu : static_cast<uint32_t>(len));
+}
+
+// Class counts: one thread per tile; the lanes of a warp holding the same
+// class are found by ballots and their leader adds them with one atomic.
+__global__ void __launch_bounds__(256) order_count_kernel(const int64_t* __restrict__ ranges,
+                                                          const uint32_t* __restrict__ work,
+                                                          int64_t num_tiles,
+                                                          uint32_t* __restrict__ hist) {
+  const int lane = threadIdx.x & 31;
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int c = t < num_tiles ? work_class(tile_work(ranges, work, t)) : kWorkClasses;
+  const unsigned peers = same_class_lanes(c);
+  if (c < kWorkClasses && (peers & ((1u << lane) - 1u)) == 0) atomicAdd(hist + c, __popc(peers));
+}
+
+// The first place of each class, heaviest class first, from the counts (one
+// warp: two classes per lane); *total gets the number of places.
+__device__ __forceinline__ void class_starts(const uint32_t* __restrict__ hist, uint32_t* s_start,
+                                             uint32_t* total) {
+  const int lane = threadIdx.x & 31;
+  const uint32_t a = hist[kWorkClasses - 1 - 2 * lane], b = hist[kWorkClasses - 2 - 2 * lane];
+  uint32_t incl = a + b;
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  const uint32_t excl = incl - a - b;
+  s_start[kWorkClasses - 1 - 2 * lane] = excl;
+  s_start[kWorkClasses - 2 - 2 * lane] = excl + a;
+  if (total) *total = __shfl_sync(0xffffffffu, incl, 31);
+}
+
+// Each tile's place in the order: its class's start plus a per-class cursor
+// (one atomic per class and warp).
+__global__ void __launch_bounds__(256) order_scatter_kernel(
+    const int64_t* __restrict__ ranges, const uint32_t* __restrict__ work, int64_t num_tiles,
+    const uint32_t* __restrict__ hist, uint32_t* __restrict__ cursor,
+    int32_t* __restrict__ order) {
+  __shared__ uint32_t s_start[kWorkClasses];
+  if (threadIdx.x < 32) class_starts(hist, s_start, nullptr);
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int c = t < num_tiles ? work_class(tile_work(ranges, work, t)) : kWorkClasses;
+  const unsigned peers = same_class_lanes(c);
+  const int leader = __ffs(peers) - 1;
+  uint32_t base = 0;
+  if (c < kWorkClasses && lane == leader) base = atomicAdd(cursor + c, __popc(peers));
+  base = __shfl_sync(0xffffffffu, base, leader);
+  if (c < kWorkClasses)
+    order[s_start[c] + base + __popc(peers & ((1u << lane) - 1u))] = static_cast<int32_t>(t);
+}
+
+// The backward's work per tile: its largest contributor count (the backward
+// walks each tile's list that far). One warp per tile.
+__global__ void __launch_bounds__(256) tile_max_contrib_kernel(
+    const int32_t* __restrict__ n_contributors, int width, int tile_size, int tiles_w,
+    int64_t num_tiles, uint32_t* __restrict__ work) {
+  const int64_t t = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (t >= num_tiles) return;
+  const int x0 = static_cast<int>(t % tiles_w) * tile_size;
+  const int y0 = static_cast<int>(t / tiles_w) * tile_size;
+  int m = 0;
+#pragma unroll 4
+  for (int k = lane; k < tile_size * tile_size; k += 32) {
+    const int v = __ldg(n_contributors + static_cast<int64_t>(y0 + k / tile_size) * width + x0 +
+                        k % tile_size);
+    m = v > m ? v : m;
+  }
+  m = __reduce_max_sync(0xffffffffu, m);
+  if (lane == 0) work[t] = static_cast<uint32_t>(m);
+}
+
+// ------------------------------------------------ split backward: the plan
+//
+// The backward's plan of one view: its work items heavy first -- every tile,
+// and the tiles whose walk (list length up to the largest contributor count)
+// exceeds split_walk entries cut into parts of at most that many (part k's
+// CTA also walks the parts behind it for its suffix, at about a third of the
+// per-entry cost, which sets its place in the order). Layout (256-byte
+// aligned parts): header (items, extra parts; class counts, class cursors and
+// the extra-part counter at words 16, 80 and 144) | items int4 [tiles +
+// kExtraParts] | tile parts int2 [tiles] | work uint32 [tiles]. Tiles left
+// once kExtraParts parts beyond the tiles' first ones are handed out stay
+// whole.
+
+constexpr int kExtraParts = 1024;
+constexpr int kMaxSplitParts = 64;
+constexpr int kDefaultSplitWalk = 1024;
+
+struct BwdPlanLayout {
+  uint64_t header, items, tile_parts, work, bytes;
+  explicit BwdPlanLayout(int64_t num_tiles) {
+    auto align = [](uint64_t x) { return (x + 255) / 256 * 256; };
+    const uint64_t t = static_cast<uint64_t>(num_tiles);
+    uint64_t at = 0;
+    header = at; at = align(at + 1024);
+    items = at; at = align(at + 16 * (t + kExtraParts));
+    tile_parts = at; at = align(at + 8 * t);
+    work = at; at = align(at + 4 * t);
+    bytes = at;
+  }
+};
+
+// A tile's walk: its list up to its largest contributor count.
+__device__ __forceinline__ uint32_t tile_walk(const int64_t* __restrict__ ranges,
+                                              const uint32_t* __restrict__ max_contrib,
+                                              int64_t t) {
+  const int64_t len = ranges[2 * t + 1] - ranges[2 * t];
+  const int64_t m = static_cast<int64_t>(__ldg(max_contrib + t));
+  const int64_t w = len < m ? len : m;
+  return w <= 0 ? 0u : static_cast<uint32_t>(w);
+}
+
+// Work of part k of a tile cut into `parts` parts of `chunk` entries: its own
+// walk plus a third of each entry behind it.
+__device__ __forceinline__ uint32_t part_work(uint32_t chunk, int part, int parts) {
+  return chunk + static_cast<uint32_t>(parts - 1 - part) * chunk / 3;
+}
+
+// The plan's class counts: one thread per tile decides its parts (an extra
+// part is one more CTA; kExtraParts of them per view) and counts its items --
+// whole tiles by their leader's one atomic per warp and class, the parts of a
+// split tile each by its own.
+__global__ void __launch_bounds__(256) plan_count_kernel(
+    const int64_t* __restrict__ ranges, const uint32_t* __restrict__ max_contrib,
+    int64_t num_tiles, int split_walk, uint32_t* __restrict__ hist,
+    uint32_t* __restrict__ extra, int2* __restrict__ tile_parts) {
+  const int lane = threadIdx.x & 31;
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const uint32_t walk = t < num_tiles ? tile_walk(ranges, max_contrib, t) : 0u;
+  int parts = 1;
+  if (t < num_tiles && walk > static_cast<uint32_t>(split_walk)) {
+    const uint32_t want = (walk + split_walk - 1) / split_walk;
+    parts = want < kMaxSplitParts ? static_cast<int>(want) : kMaxSplitParts;
+    const uint32_t first = atomicAdd(extra, static_cast<uint32_t>(parts - 1));
+    if (first + parts - 1 > kExtraParts) parts = 1;  // out of parts: stays whole
+  }
+  if (t < num_tiles) tile_parts[t] = make_int2(parts, 0);
+  const bool whole = t < num_tiles && parts == 1;
+  const int c = whole ? work_class(walk) : kWorkClasses + 1 + lane % 31;
+  const unsigned peers = same_class_lanes(c);
+  if (whole && (peers & ((1u << lane) - 1u)) == 0) atomicAdd(hist + c, __popc(peers));
+  if (t < num_tiles && parts > 1) {
+    const uint32_t chunk = (walk + parts - 1) / parts;
+    for (int k = 0; k < parts; ++k) atomicAdd(hist + work_class(part_work(chunk, k, parts)), 1u);
+  }
+}
+
+// The plan's items: each tile's (or part's) place is its class's start plus
+// a per-class cursor; the places past the last item are marked empty.
+__global__ void __launch_bounds__(256) plan_scatter_kernel(
+    const int64_t* __restrict__ ranges, const uint32_t* __restrict__ max_contrib,
+    int64_t num_tiles, const uint32_t* __restrict__ hist, uint32_t* __restrict__ cursor,
+    const uint32_t* __restrict__ extra, const int2* __restrict__ tile_parts,
+    int4* __restrict__ items, uint32_t* __restrict__ header) {
+  __shared__ uint32_t s_start[kWorkClasses];
+  __shared__ uint32_t s_total;
+  if (threadIdx.x < 32) class_starts(hist, s_start, &s_total);
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const uint32_t walk = t < num_tiles ? tile_walk(ranges, max_contrib, t) : 0u;
+  const int parts = t < num_tiles ? tile_parts[t].x : 1;
+  const bool whole = t < num_tiles && parts == 1;
+  const int c = whole ? work_class(walk) : kWorkClasses + 1 + lane % 31;
+  const unsigned peers = same_class_lanes(c);
+  const int leader = __ffs(peers) - 1;
+  uint32_t base = 0;
+  if (whole && lane == leader) base = atomicAdd(cursor + c, __popc(peers));
+  base = __shfl_sync(0xffffffffu, base, leader);
+  if (whole)
+    items[s_start[c] + base + __popc(peers & ((1u << lane) - 1u))] =
+        make_int4(static_cast<int>(t), 0, 1, 0);
+  if (t < num_tiles && parts > 1) {
+    const uint32_t chunk = (walk + parts - 1) / parts;
+    for (int k = 0; k < parts; ++k) {
+      const int ck = work_class(part_work(chunk, k, parts));
+      items[s_start[ck] + atomicAdd(cursor + ck, 1u)] = make_int4(static_cast<int>(t), k, parts, 0);
+    }
+  }
+  const uint32_t total = s_total;
+  for (int64_t i = total + static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+       i < num_tiles + kExtraParts; i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    items[i] = make_int4(-1, 0, 1, 0);
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    header[0] = total;
+    header[1] = *extra < kExtraParts ? *extra : kExtraParts;
+  }
+}
+
+uint64_t composite_bwd_plan_size(const gs_params& p) {
+  const int64_t num_tiles =
+      static_cast<int64_t>(p.width / p.tile_size) * (p.height / p.tile_size);
+  return BwdPlanLayout(num_tiles).bytes;
+}
+
+int32_t launch_composite_bwd_plan(const int64_t* ranges, const int32_t* n_contributors,
+                                  const gs_params& p, int split_walk, void* plan,
+                                  cudaStream_t stream) {
+  const int tiles_w = p.width / p.tile_size;
+  const int64_t num_tiles = static_cast<int64_t>(tiles_w) * (p.height / p.tile_size);
+  const BwdPlanLayout L(num_tiles);
+  char* base = static_cast<char*>(plan);
+  if (num_tiles == 0) return GS_OK;
+  uint32_t* work = reinterpret_cast<uint32_t*>(base + L.work);
+  uint32_t* header = reinterpret_cast<uint32_t*>(base + L.header);
+  GS_CUDA_TRY(cudaMemsetAsync(header, 0, 1024, stream));
+  tile_max_contrib_kernel<<<ceil_div(num_tiles * 32, 256), 256, 0, stream>>>(
+      n_contributors, p.width, p.tile_size, tiles_w, num_tiles, work);
+  GS_TRY(check_launch());
+  int2* tile_parts = reinterpret_cast<int2*>(base + L.tile_parts);
+  const int walk = split_walk > 0 ? split_walk : kDefaultSplitWalk;
+  plan_count_kernel<<<ceil_div(num_tiles, 256), 256, 0, stream>>>(
+      ranges, work, num_tiles, walk, header + 16, header + 144, tile_parts);
+  GS_TRY(check_launch());
+  plan_scatter_kernel<<<ceil_div(num_tiles, 256), 256, 0, stream>>>(
+      ranges, work, num_tiles, header + 16, header + 80, header + 144, tile_parts,
+      reinterpret_cast<int4*>(base + L.items), header);
+  return check_launch();
+}
+
+// tile_work: [num_tiles] per-tile work (the backward's form), then class
+// counts and cursors [2 x kWorkClasses].
+int32_t launch_tile_order(const int64_t* ranges, const int32_t* n_contributors,
+                          const gs_params& p, int32_t* order, uint32_t* tile_work,
+                          cudaStream_t stream) {
+  const int tiles_w = p.width / p.tile_size;
+  const int64_t num_tiles = static_cast<int64_t>(tiles_w) * (p.height / p.tile_size);
+  if (num_tiles == 0) return GS_OK;
+  uint32_t* hist = tile_work + num_tiles;
+  GS_CUDA_TRY(cudaMemsetAsync(hist, 0, 2 * kWorkClasses * sizeof(uint32_t), stream));
+  const uint32_t* work = nullptr;
+  if (n_contributors != nullptr) {
+    tile_max_contrib_kernel<<<ceil_div(num_tiles * 32, 256), 256, 0, stream>>>(
+        n_contributors, p.width, p.tile_size, tiles_w, num_tiles, tile_work);
+    GS_TRY(check_launch());
+    work = tile_work;
+  }
+  order_count_kernel<<<ceil_div(num_tiles, 256), 256, 0, stream>>>(ranges, work, num_tiles, hist);
+  GS_TRY(check_launch());
+  order_scatter_kernel<<<ceil_div(num_tiles, 256), 256, 0, stream>>>(
+      ranges, work, num_tiles, hist, hist + kWorkClasses, order);
+  return check_launch();
+}
+
 int32_t launch_composite_fwd(const float* records, const int32_t* gaussian_ids,
                              const int64_t* ranges, const gs_params& p, float* image,
                              float* final_transmittance, int32_t* n_contributors,
@@ -679,26 +1018,30 @@ int32_t launch_composite_fwd(const float* records, const int32_t* gaussian_ids,
 int32_t launch_composite_bwd(int64_t n, const float* records, const int32_t* gaussian_ids,
                              const int64_t* ranges, const float* grad_image,
                              const float* final_transmittance, const int32_t* n_contributors,
-                             const gs_params& p, float* grad_projected,
-                             const int32_t* tile_order, cudaStream_t stream) {
+                             const gs_params& p, float* grad_projected, void* plan,
+                             cudaStream_t stream) {
   GS_CUDA_TRY(cudaMemsetAsync(grad_projected, 0, sizeof(float) * 9 * n, stream));
   const int64_t num_tiles =
       static_cast<int64_t>(p.width / p.tile_size) * (p.height / p.tile_size);
   if (num_tiles == 0 || n == 0) return GS_OK;
   const float4* rec = reinterpret_cast<const float4*>(records);
-#define GS_LAUNCH(TS)                                                                          \
-  if (p.gaussian_mode)                                                                         \
-    composite_bwd_kernel<TS, BwdPpt<TS>::value, true>                                          \
-        <<<static_cast<unsigned>(num_tiles), TileShape<TS, BwdPpt<TS>::value>::kThreads, 0,   \
-           stream>>>(rec, gaussian_ids, ranges, grad_image, final_transmittance,               \
-                     n_contributors, p, grad_projected, tile_order);                           \
-  else                                                                                         \
-    composite_bwd_kernel<TS, BwdPpt<TS>::value, false>                                         \
-        <<<static_cast<unsigned>(num_tiles), TileShape<TS, BwdPpt<TS>::value>::kThreads, 0,   \
-           stream>>>(rec, gaussian_ids, ranges, grad_image, final_transmittance,               \
-                     n_contributors, p, grad_projected, tile_order)
+  const BwdPlanLayout L(num_tiles);
+  const int4* items =
+      plan ? reinterpret_cast<const int4*>(static_cast<char*>(plan) + L.items) : nullptr;
+  const unsigned grid = static_cast<unsigned>(plan ? num_tiles + kExtraParts : num_tiles);
+#define GS_LAUNCH_MODE(TS, G)                                                                  \
+  composite_bwd_kernel<TS, BwdPpt<TS>::value, G>                                               \
+      <<<grid, TileShape<TS, BwdPpt<TS>::value>::kThreads, 0, stream>>>(                       \
+          rec, gaussian_ids, ranges, grad_image, final_transmittance, n_contributors, p,       \
+          grad_projected, nullptr, items)
+#define GS_LAUNCH(TS)                 \
+  if (p.gaussian_mode)                \
+    GS_LAUNCH_MODE(TS, true);         \
+  else                                \
+    GS_LAUNCH_MODE(TS, false)
   GS_TILE_DISPATCH(p.tile_size, GS_LAUNCH)
 #undef GS_LAUNCH
+#undef GS_LAUNCH_MODE
   return check_launch();
 }
 
@@ -743,12 +1086,12 @@ int32_t launch_composite_bwd_deterministic(int64_t n, int64_t total, const float
     composite_bwd_kernel<TS, BwdPpt<TS>::value, true, true>                                    \
         <<<static_cast<unsigned>(num_tiles), TileShape<TS, BwdPpt<TS>::value>::kThreads, 0,   \
            stream>>>(rec, gaussian_ids, ranges, grad_image, final_transmittance,               \
-                     n_contributors, p, rows, tile_order);                                     \
+                     n_contributors, p, rows, tile_order, nullptr);                            \
   else                                                                                         \
     composite_bwd_kernel<TS, BwdPpt<TS>::value, false, true>                                   \
         <<<static_cast<unsigned>(num_tiles), TileShape<TS, BwdPpt<TS>::value>::kThreads, 0,   \
            stream>>>(rec, gaussian_ids, ranges, grad_image, final_transmittance,               \
-                     n_contributors, p, rows, tile_order)
+                     n_contributors, p, rows, tile_order, nullptr)
     GS_TILE_DISPATCH(p.tile_size, GS_LAUNCH)
 #undef GS_LAUNCH
     GS_TRY(check_launch());
@@ -757,131 +1100,6 @@ int32_t launch_composite_bwd_deterministic(int64_t n, int64_t total, const float
   if (n == 0) return GS_OK;
   reduce_rows_kernel<<<ceil_div(n, 256), 256, 0, stream>>>(n, order, segments, rows,
                                                            grad_projected);
-  return check_launch();
-}
-
-// ------------------------------------------------------ heavy-first tile order
-//
-// The compositors take a tile per CTA in CTA order. Tile costs are very
-// uneven (config 5's densest tile walks 850k pixel-Gaussian pairs, the mean
-// 47k; alone it takes half the backward's time), and in row-major order the
-// heavy central tiles start mid-launch on SMs already full of other tiles, so
-// they finish last. Visiting tiles by decreasing work starts them first.
-// Work classes are a quarter octave wide; order within a class is arbitrary
-// (no result depends on which CTA composites a tile).
-
-constexpr int kOrderThreads = 1024;
-constexpr int kWorkClasses = 64;
-
-// 0 for no work, else 1 + 4 floor(log2 w) + the two bits of w below its
-// leading one, capped at 63.
-__device__ __forceinline__ int work_class(uint32_t w) {
-  if (w == 0) return 0;
-  const int b = 31 - __clz(w);
-  const int frac = b >= 2 ? static_cast<int>((w >> (b - 2)) & 3u) : static_cast<int>((w << (2 - b)) & 3u);
-  const int c = 1 + 4 * b + frac;
-  return c < kWorkClasses - 1 ? c : kWorkClasses - 1;
-}
-
-__device__ __forceinline__ uint32_t tile_work(const int64_t* __restrict__ ranges,
-                                              const uint32_t* __restrict__ work, int64_t t) {
-  if (work) return __ldg(work + t);
-  const int64_t len = ranges[2 * t + 1] - ranges[2 * t];
-  return len <= 0 ? 0u : (len >= 0xffffffffLL ? 0xffffffffu : static_cast<uint32_t>(len));
-}
-
-// One CTA: a counting sort of the tiles by decreasing work class. The lanes
-// of a warp holding the same class are found with one match, and their
-// leader adds them with one shared-memory atomic (all tiles fall into a few
-// classes, so per-tile atomics would serialise on a handful of counters).
-__global__ void __launch_bounds__(kOrderThreads) order_tiles_kernel(
-    const int64_t* __restrict__ ranges, const uint32_t* __restrict__ work, int64_t num_tiles,
-    int32_t* __restrict__ order) {
-  // A warp takes kOrderBatch tiles per lane at once, their loads in flight
-  // together: tiles t0 + i * kOrderThreads + lane.
-  constexpr int kOrderBatch = 8;
-  __shared__ uint32_t s_next[kWorkClasses];
-  const int lane = threadIdx.x & 31;
-  const int64_t warp_first = threadIdx.x & ~31;
-  const unsigned lower = (1u << lane) - 1u;
-  auto classes = [&](int64_t t0, int (&c)[kOrderBatch]) {
-#pragma unroll
-    for (int i = 0; i < kOrderBatch; ++i) {
-      const int64_t t = t0 + i * kOrderThreads + lane;
-      c[i] = t < num_tiles ? work_class(tile_work(ranges, work, t)) : kWorkClasses;
-    }
-  };
-  if (threadIdx.x < kWorkClasses) s_next[threadIdx.x] = 0;
-  __syncthreads();
-  for (int64_t t0 = warp_first; t0 < num_tiles; t0 += kOrderThreads * kOrderBatch) {
-    int c[kOrderBatch];  // (t0 is warp-uniform)
-    classes(t0, c);
-#pragma unroll
-    for (int i = 0; i < kOrderBatch; ++i) {
-      const unsigned peers = __match_any_sync(0xffffffffu, c[i]);
-      if (c[i] < kWorkClasses && (peers & lower) == 0) atomicAdd(&s_next[c[i]], __popc(peers));
-    }
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {  // exclusive offsets, heaviest class first
-    uint32_t run = 0;
-    for (int c = kWorkClasses - 1; c >= 0; --c) {
-      const uint32_t k = s_next[c];
-      s_next[c] = run;
-      run += k;
-    }
-  }
-  __syncthreads();
-  for (int64_t t0 = warp_first; t0 < num_tiles; t0 += kOrderThreads * kOrderBatch) {
-    int c[kOrderBatch];
-    classes(t0, c);
-#pragma unroll
-    for (int i = 0; i < kOrderBatch; ++i) {
-      const unsigned peers = __match_any_sync(0xffffffffu, c[i]);
-      const int leader = __ffs(peers) - 1;
-      uint32_t base = 0;
-      if (c[i] < kWorkClasses && lane == leader) base = atomicAdd(&s_next[c[i]], __popc(peers));
-      base = __shfl_sync(0xffffffffu, base, leader);
-      if (c[i] < kWorkClasses)
-        order[base + __popc(peers & lower)] = static_cast<int32_t>(t0 + i * kOrderThreads + lane);
-    }
-  }
-}
-
-// The backward's work per tile: its largest contributor count (the backward
-// walks each tile's list that far). One warp per tile.
-__global__ void __launch_bounds__(256) tile_max_contrib_kernel(
-    const int32_t* __restrict__ n_contributors, int width, int tile_size, int tiles_w,
-    int64_t num_tiles, uint32_t* __restrict__ work) {
-  const int64_t t = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (t >= num_tiles) return;
-  const int x0 = static_cast<int>(t % tiles_w) * tile_size;
-  const int y0 = static_cast<int>(t / tiles_w) * tile_size;
-  int m = 0;
-#pragma unroll 4
-  for (int k = lane; k < tile_size * tile_size; k += 32) {
-    const int v = __ldg(n_contributors + static_cast<int64_t>(y0 + k / tile_size) * width + x0 +
-                        k % tile_size);
-    m = v > m ? v : m;
-  }
-  m = __reduce_max_sync(0xffffffffu, m);
-  if (lane == 0) work[t] = static_cast<uint32_t>(m);
-}
-
-int32_t launch_tile_order(const int64_t* ranges, const int32_t* n_contributors,
-                          const gs_params& p, int32_t* order, uint32_t* work,
-                          cudaStream_t stream) {
-  const int tiles_w = p.width / p.tile_size;
-  const int64_t num_tiles = static_cast<int64_t>(tiles_w) * (p.height / p.tile_size);
-  if (num_tiles == 0) return GS_OK;
-  if (n_contributors != nullptr) {
-    tile_max_contrib_kernel<<<ceil_div(num_tiles * 32, 256), 256, 0, stream>>>(
-        n_contributors, p.width, p.tile_size, tiles_w, num_tiles, work);
-    GS_TRY(check_launch());
-  }
-  order_tiles_kernel<<<1, kOrderThreads, 0, stream>>>(
-      ranges, n_contributors != nullptr ? work : nullptr, num_tiles, order);
   return check_launch();
 }
 

@@ -41,6 +41,8 @@ EXPORTED_SYMBOLS = (
     "gs_tile_order",
     "gs_composite_fwd",
     "gs_composite_bwd",
+    "gs_composite_bwd_plan_size",
+    "gs_composite_bwd_plan",
     "gs_composite_bwd_deterministic",
     "gs_composite_bwd_deterministic_workspace_size",
     "gs_project_bwd",
@@ -227,6 +229,8 @@ def lib() -> ctypes.CDLL:
         "gs_tile_order": ([vp, vp, P, vp, vp, vp], i32),
         "gs_composite_fwd": ([vp] * 3 + [P] + [vp] * 4 + [vp], i32),
         "gs_composite_bwd": ([i64] + [vp] * 6 + [P, vp, vp, vp], i32),
+        "gs_composite_bwd_plan_size": ([P], u64),
+        "gs_composite_bwd_plan": ([vp, vp, P, i32, vp, u64, vp], i32),
         "gs_composite_bwd_deterministic": ([i64, i64] + [vp] * 6 + [P, vp, u64, vp, vp, vp],
                                            i32),
         "gs_composite_bwd_deterministic_workspace_size": ([i64, i64], u64),

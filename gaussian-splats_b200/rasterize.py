@@ -64,11 +64,23 @@ def _tile_order(ranges: torch.Tensor, n_contributors: torch.Tensor | None, pref,
     count (``n_contributors`` given) for the backward."""
     num_tiles = ranges.shape[0]
     order = torch.empty((num_tiles,), dtype=torch.int32, device=ranges.device)
-    work = (torch.empty((num_tiles,), dtype=torch.int32, device=ranges.device)
-            if n_contributors is not None else None)
+    work = torch.empty((num_tiles + 128,), dtype=torch.int32, device=ranges.device)
     native.check(native.lib().gs_tile_order(_ptr(ranges), _ptr(n_contributors), pref,
                                             _ptr(order), _ptr(work), stream), "gs_tile_order")
     return order
+
+
+def _backward_plan(ranges: torch.Tensor, n_contributors: torch.Tensor, pref,
+                   stream: ctypes.c_void_p) -> torch.Tensor:
+    """The compositing backward's plan of the render (gs_composite_bwd_plan):
+    tiles heaviest first, the longest walks split into parts."""
+    lib = native.lib()
+    plan = torch.empty((lib.gs_composite_bwd_plan_size(pref),), dtype=torch.uint8,
+                       device=ranges.device)
+    native.check(lib.gs_composite_bwd_plan(_ptr(ranges), _ptr(n_contributors), pref, 0,
+                                           _ptr(plan), plan.numel(), stream),
+                 "gs_composite_bwd_plan")
+    return plan
 
 
 def _check_inputs(mean: torch.Tensor, color: torch.Tensor, rendering_mode: str) -> None:
@@ -455,13 +467,13 @@ def _backward(ctx, *grad_outputs):
             native.check(lib.gs_pack_records(
                 n, _ptr(projected_mean), _ptr(inverse_covariance), _ptr(projected_color),
                 _ptr(projected_opacity), pref, _ptr(records), stream), "gs_pack_records")
-        order = _tile_order(ranges, n_contributors, pref, stream)
         if deterministic_backward():
             # order-fixed form: the same gradient bits on every run
             if torch.cuda.is_current_stream_capturing():
                 raise RuntimeError("the deterministic backward runs eagerly (a captured render's "
                                    "gaussian_ids is longer than its intersection total)")
             total = gaussian_ids.numel()
+            order = _tile_order(ranges, n_contributors, pref, stream)
             ws_bytes = lib.gs_composite_bwd_deterministic_workspace_size(n, total)
             workspace = torch.empty((ws_bytes,), dtype=torch.uint8, device=device)
             native.check(lib.gs_composite_bwd_deterministic(
@@ -470,10 +482,11 @@ def _backward(ctx, *grad_outputs):
                 ws_bytes, _ptr(grad_projected), _ptr(order), stream),
                 "gs_composite_bwd_deterministic")
         else:
+            plan = _backward_plan(ranges, n_contributors, pref, stream)
             native.check(lib.gs_composite_bwd(
                 n, _ptr(records), _ptr(gaussian_ids), _ptr(ranges), _ptr(grad_image),
                 _ptr(final_transmittance), _ptr(n_contributors), pref, _ptr(grad_projected),
-                _ptr(order), stream), "gs_composite_bwd")
+                _ptr(plan), stream), "gs_composite_bwd")
         _mark("composite_bwd")
         # The five gradients are carved out of one buffer (rotation and colour
         # first, keeping their 16-byte rows aligned), so a view-parallel step

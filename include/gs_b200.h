@@ -189,9 +189,10 @@ int32_t gs_bin_noalloc(int64_t n, const float *projected_mean, const int32_t *co
  * instead of whenever their row of tiles comes up. No counterpart in the
  * reference, whose Triton launches take tiles in grid order (composite.py:140,
  * composite_bwd.py:248). Work is each tile's list length (from ranges) for
- * the forward, or with n_contributors [H,W] its largest contributor count for
- * the backward (then tile_work, [num_tiles] uint32, is scratch). tile_order receives
- * [num_tiles] int32, a permutation of the tile indices. */
+ * the forward, or with n_contributors [H,W] its largest contributor count
+ * (for gs_composite_bwd_deterministic). tile_work is scratch of num_tiles +
+ * 128 uint32 words; tile_order receives [num_tiles] int32, a permutation of
+ * the tile indices. */
 int32_t gs_tile_order(const int64_t *ranges, const int32_t *n_contributors,
                       const gs_params *params, int32_t *tile_order, uint32_t *tile_work,
                       gs_stream_t stream);
@@ -210,13 +211,30 @@ int32_t gs_composite_fwd(const float *records, const int32_t *gaussian_ids, cons
  * index_add_ reduction (composite_bwd.py:47-277). Accumulates into
  * grad_projected [N,9] = (d mean_x, d mean_y, d conic_xx, d conic_xy,
  * d conic_yy, d r, d g, d b, d opacity), which this call zeroes first.
- * tile_order as for gs_composite_fwd (for the backward, gs_tile_order with
- * n_contributors). */
+ * plan: what gs_composite_bwd_plan built for this render (its tiles heaviest
+ * first, the longest ones split), or NULL for whole tiles in row-major order;
+ * the gradients agree either way within float rounding (the order of the
+ * float atomics differs). */
 int32_t gs_composite_bwd(int64_t n, const float *records, const int32_t *gaussian_ids,
                          const int64_t *ranges, const float *grad_image,
                          const float *final_transmittance, const int32_t *n_contributors,
-                         const gs_params *params, float *grad_projected,
-                         const int32_t *tile_order, gs_stream_t stream);
+                         const gs_params *params, float *grad_projected, const void *plan,
+                         gs_stream_t stream);
+
+/* The backward's work plan of one render (no counterpart in the reference,
+ * whose backward takes one tile per program, composite_bwd.py:248): every
+ * tile, heaviest first by its walk (list length up to its largest
+ * contributor count, composite_bwd.py:81-83), with the tiles whose walk is
+ * longer than split_walk entries (0: 1024) cut into parts of at most that
+ * many -- one CTA each, which first walks the parts behind its own for the
+ * suffix it starts from (the same recurrence, so the same bits) -- so one
+ * dense tile no longer sets the kernel's length. Up to 1024 parts beyond the
+ * tiles' first ones per view (tiles beyond stay whole). `plan` holds
+ * gs_composite_bwd_plan_size(params) bytes, 256-byte aligned. */
+uint64_t gs_composite_bwd_plan_size(const gs_params *params);
+int32_t gs_composite_bwd_plan(const int64_t *ranges, const int32_t *n_contributors,
+                              const gs_params *params, int32_t split_walk, void *plan,
+                              uint64_t plan_bytes, gs_stream_t stream);
 
 /* The same gradients, the same bits on every run: the reference's
  * per-intersection form (composite_bwd.py:237-277, its non-atomic default,

@@ -6,6 +6,7 @@ gradients within tolerance of the row-major order."""
 
 import ctypes
 
+import numpy as np
 import pytest
 import torch
 
@@ -44,9 +45,10 @@ def test_tile_order_is_heavy_first_and_changes_nothing(tile):
     stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
     num_tiles = ranges.shape[0]
     fwd_order = torch.empty((num_tiles,), dtype=torch.int32, device="cuda")
-    bwd_order = torch.empty_like(fwd_order)
-    scratch = torch.empty_like(fwd_order)
-    native.check(lib.gs_tile_order(P(ranges), None, pref, P(fwd_order), None, stream), "order")
+    bwd_order = torch.empty_like(fwd_order)  # (the deterministic backward's order)
+    scratch = torch.empty((num_tiles + 128,), dtype=torch.int32, device="cuda")
+    native.check(lib.gs_tile_order(P(ranges), None, pref, P(fwd_order), P(scratch), stream),
+                 "order")
     native.check(lib.gs_tile_order(P(ranges), P(n_contrib), pref, P(bwd_order), P(scratch),
                                    stream), "order")
     torch.cuda.synchronize()
@@ -77,14 +79,54 @@ def test_tile_order_is_heavy_first_and_changes_nothing(tile):
         assert torch.equal(img2, image) and torch.equal(t2, final_t)
         assert torch.equal(nc2, n_contrib)
 
-    # backward: row-major and heavy-first orders agree to the gradient tolerance
+    # backward: whole tiles in row-major order, the plan's heavy-first items,
+    # and plans that split every walk longer than 64 or 8 entries all agree
+    # to the gradient tolerance
     grad_image = torch.rand_like(image)
+    plan_bytes = lib.gs_composite_bwd_plan_size(pref)
     grads = []
-    for order in (None, P(bwd_order)):
+    for split_walk in (None, 0, 64, 8):
+        plan = None
+        if split_walk is not None:
+            plan = torch.empty((plan_bytes,), dtype=torch.uint8, device="cuda")
+            native.check(lib.gs_composite_bwd_plan(P(ranges), P(n_contrib), pref, split_walk,
+                                                   P(plan), plan_bytes, stream), "plan")
         gp = torch.empty((n, 9), device="cuda")
         native.check(lib.gs_composite_bwd(n, P(records), P(ids), P(ranges), P(grad_image),
-                                          P(final_t), P(n_contrib), pref, P(gp), order, stream),
+                                          P(final_t), P(n_contrib), pref, P(gp),
+                                          P(plan) if plan is not None else None, stream),
                      "bwd")
+        torch.cuda.synchronize()
         grads.append(gp)
-    torch.cuda.synchronize()
-    torch.testing.assert_close(grads[1], grads[0], rtol=1e-4, atol=1e-6)
+        if split_walk == 8:
+            _check_plan(plan, num_tiles, lengths, max_contrib, 8)
+    for g in grads[1:]:
+        torch.testing.assert_close(g, grads[0], rtol=1e-4, atol=1e-6)
+
+
+EXTRA_PARTS = 1024  # parts beyond the tiles' first ones that one plan can hold
+
+
+def _check_plan(plan, num_tiles, lengths, max_contrib, split_walk):
+    """Every tile's walk is covered once: one item per part, the parts of a
+    split tile numbered 0..parts-1, splits only where the walk is longer than
+    split_walk, no more extra parts than the plan holds."""
+    words = plan.cpu().numpy().view(np.int32)
+    num_items, extra = int(words[0]), int(words[1])
+    items = words[256:256 + 4 * (num_tiles + EXTRA_PARTS)].reshape(-1, 4)  # after 1 KB
+    live = items[:num_items]
+    assert np.all(items[num_items:, 0] == -1)
+    walks = np.minimum(np.asarray(lengths), np.asarray(max_contrib))
+    seen = {}
+    for tile, part, parts, _ in live:
+        seen.setdefault(int(tile), []).append((int(part), int(parts)))
+    assert sorted(seen) == list(range(num_tiles))
+    split_parts = 0
+    for tile, entries in seen.items():
+        parts = entries[0][1]
+        assert sorted(e[0] for e in entries) == list(range(parts))
+        assert all(e[1] == parts for e in entries)
+        if parts > 1:
+            assert walks[tile] > split_walk
+            split_parts += parts - 1
+    assert 0 < split_parts <= min(extra, EXTRA_PARTS)
