@@ -639,7 +639,22 @@ __device__ __forceinline__ void scatter_batch(int lo, int hi, int buckets, uint3
                                               uint32_t* s_base, uint32_t* s_run, int stride,
                                               Emit emit) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (int k = lo; k < hi; ++k) atomicOr(&s_cover[warp * stride + k], 1u << lane);
+  // Where the warp's intervals overlap heavily (a dense blob), per-lane
+  // atomics would serialise on a few words: there one ballot per bucket of
+  // the warp's span builds its masks; elsewhere each lane ORs in its own.
+  const int span_lo = __reduce_min_sync(0xffffffffu, lo < hi ? lo : 0x7fffffff);
+  const int span_hi = __reduce_max_sync(0xffffffffu, lo < hi ? hi : 0);
+  const int covered = __reduce_add_sync(0xffffffffu, hi - lo);
+  const int span = span_hi - span_lo;
+  const bool dense = span > 0 && span <= 64 && covered >= 2 * span;  // warp-uniform
+  if (dense) {
+    for (int k = span_lo; k < span_hi; ++k) {
+      const unsigned mask = __ballot_sync(0xffffffffu, lo <= k && k < hi);
+      if (lane == 0) s_cover[warp * stride + k] = mask;
+    }
+  } else {
+    for (int k = lo; k < hi; ++k) atomicOr(&s_cover[warp * stride + k], 1u << lane);
+  }
   __syncthreads();
   for (int k = threadIdx.x; k < buckets; k += kThreads) {
     uint32_t run = s_run[k];
@@ -652,8 +667,16 @@ __device__ __forceinline__ void scatter_batch(int lo, int hi, int buckets, uint3
   }
   __syncthreads();
   const unsigned lower = lanemask_lt();
-  for (int k = lo; k < hi; ++k)
-    emit(k, s_base[warp * stride + k] + __popc(s_cover[warp * stride + k] & lower));
+  if (dense) {
+    // bucket by bucket: the lanes covering bucket k write consecutive places
+    // of k's list together (one coalesced store)
+    for (int k = span_lo; k < span_hi; ++k)
+      if (lo <= k && k < hi)
+        emit(k, s_base[warp * stride + k] + __popc(s_cover[warp * stride + k] & lower));
+  } else {
+    for (int k = lo; k < hi; ++k)
+      emit(k, s_base[warp * stride + k] + __popc(s_cover[warp * stride + k] & lower));
+  }
   __syncthreads();
   for (int k = threadIdx.x; k < buckets; k += kThreads) {
 #pragma unroll
