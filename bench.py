@@ -70,6 +70,23 @@ def project_bwd_bytes(k):
     return 44 + 12 * k + 56 + 44 + 12 * k
 
 
+# Binning's bytes in this build, each array read or written once: the count
+# phase reads counts and depths (8 B per Gaussian) and moves 16 B per visible
+# Gaussian in each of its 4 depth passes; the row pass reads each visible
+# Gaussian's id and rectangle twice (40 B) and writes 4 B per row segment;
+# the column pass reads each segment and its column span twice (24 B) and
+# writes 4 B per intersection; the ranges are 16 B per tile.
+def binning_bytes(n, visible, segments, intersections, tiles):
+    return 8 * n + 104 * visible + 28 * segments + 4 * intersections + 16 * tiles
+
+
+# The reference's binning (intersections.py:10-88): per Gaussian its bounds,
+# depth and count (32 B); per intersection a 12-byte emit and a 64-bit key +
+# 32-bit id radix sort (6 passes x 24 B) plus the 8-byte range read.
+REF_BIN_BYTES_PER_GAUSSIAN = 32
+REF_BIN_BYTES_PER_INTERSECTION = 164
+
+
 # The projection also writes each visible Gaussian's 64-byte compositing
 # record (the compositors' staged form).
 RECORD_BYTES = 64
@@ -649,18 +666,25 @@ def sort_passes(num_tiles):
     return (bits + 7) // 8
 
 
-def launches_per_view(num_tiles, backward, peers=False, sharded=False):
+def launches_per_view(tiles_w, tiles_h, backward, peers=False, sharded=False):
     """This library's kernel launches for one view: projection; the count
-    phase (histogram, 4 depth passes, count scan); the sort phase (emit,
-    histogram when the tile sort has passes, the passes, ranges);
+    phase (histogram, 4 depth passes); the sort phase (the row/column path's
+    count, scan and scatter of rows and of columns, plus its row layout; or,
+    for grids over 256 tile columns or 512 rows, count scan, emit, histogram,
+    tile-sort passes and ranges); the forward's tile order (count, scatter);
     compositing; in a training step the L1 loss (partial sums, total,
-    gradient), compositing backward and projection backward; and with a peer
+    gradient), the backward's plan (per-tile contributor maximum, count,
+    scatter), compositing backward and projection backward; and with a peer
     exchange its handshake kernels (begin, publish, finish; the sharded form
     also its shard release)."""
-    passes = sort_passes(num_tiles)
-    forward = 1 + 6 + (2 + (1 + passes if passes else 0)) + 1
+    if tiles_w <= 256 and tiles_h <= 512:
+        sort_phase = 7
+    else:
+        passes = sort_passes(tiles_w * tiles_h)
+        sort_phase = 2 + (1 + passes if passes else 0) + 1
+    forward = 1 + 5 + sort_phase + 2 + 1
     handshakes = 4 if sharded else (3 if peers else 0)
-    return forward + (5 if backward else 0) + handshakes
+    return forward + (8 if backward else 0) + handshakes
 
 
 def main():
@@ -854,6 +878,12 @@ def main():
         lengths = out[8][:, 1] - out[8][:, 0]
         num_tiles = int(lengths.numel())
         pairs = int((torch.minimum(lengths, tile_max) * ts * ts).sum())
+        # Row segments (one per tile row a Gaussian's rectangle spans): the
+        # distinct (tile row, Gaussian) pairs of the lists.
+        tiles_w = out[2].shape[1] // ts
+        entry_row = torch.repeat_interleave(
+            torch.arange(num_tiles, device=lengths.device) // tiles_w, lengths)
+        segments = int(torch.unique((entry_row << 32) | out[7][:intersections].long()).numel())
         grad_image = None
         if backward:
             grad_image = torch.zeros_like(out[0])
@@ -991,6 +1021,24 @@ def main():
         "project_fwd": hbm("project_fwd", n * project_fwd_bytes(k) + visible * RECORD_BYTES),
         "composite_fwd": issue("composite_fwd", pairs * COMPOSITE_FWD_FLOPS),
     }
+    if "bin_count" in stage_ms and "bin_sort" in stage_ms:
+        # Binning, count and sort phases together (live stage times of the
+        # eager steps): this build's bytes against HBM, and the reference's
+        # emit + 64-bit key sort bytes as a rate of reference work.
+        bin_ms = stage_ms["bin_count"] + stage_ms["bin_sort"]
+        own = binning_bytes(n, visible, segments, intersections, num_tiles)
+        gbs = own / (bin_ms * 1e-3) / 1e9
+        ref = REF_BIN_BYTES_PER_GAUSSIAN * n + REF_BIN_BYTES_PER_INTERSECTION * intersections
+        rooflines["binning"] = {
+            "bound": "latency", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s",
+            "frac": gbs / hbm_peak, "ms": bin_ms, "algorithmic_bytes": own,
+            "segments": segments,
+            "reference_work": {"basis": "the reference's emit of 64-bit keys and their 6-pass "
+                                        "radix sort: 32 B per Gaussian + 164 B per intersection",
+                               "bytes": ref, "achieved": ref / (bin_ms * 1e-3) / 1e9,
+                               "unit": "GB/s"},
+            "note": "count + sort phases (5 + 7 launches, latency-bound: their bytes are few); "
+                    f"peak: {peak_kind} hbm_gbs (MEASURED_PEAKS.json)"}
     if backward:
         rooflines["project_bwd"] = hbm("project_bwd", n * project_bwd_bytes(k))
         rooflines["composite_bwd"] = issue("composite_bwd", pairs * COMPOSITE_BWD_FLOPS)
@@ -1044,14 +1092,14 @@ def main():
                 else "launched from Python"},
         "stage_ms": stage_ms, "kernel_ms": kernel_ms, "dominant_kernel": dominant,
         "view": {"visible": visible, "intersections": intersections, "tiles": num_tiles,
-                 "active_pairs": n_contrib, "reference_pairs": pairs},
+                 "segments": segments, "active_pairs": n_contrib, "reference_pairs": pairs},
         "roofline": main_roof, "rooflines": rooflines, "optimizer": optimizer,
         "e2e": {"value": views_per_step * 1000.0 / e2e_ms, "unit": UNIT, "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-        "gpu_launches": (launches_per_view(num_tiles, backward, peers,
+        "gpu_launches": (launches_per_view(tiles_w, num_tiles // tiles_w, backward, peers,
                                            peers and transport == "p2p-shard") * per_view
                          if not batched else
-                         (launches_per_view(num_tiles, False) - 1) * per_view
+                         (launches_per_view(tiles_w, num_tiles // tiles_w, False) - 1) * per_view
                          + -(-per_view // BATCH_VIEWS)) * args.steps,
         "clocks": clock,
         "rank_ms_per_step": headline_rank_ms,

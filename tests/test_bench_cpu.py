@@ -51,12 +51,16 @@ def test_launch_count_per_view():
     # 1080p at 16x16: 8160 tiles, 13 bits, two tile-sort passes.
     assert bench.sort_passes(8160) == 2 and bench.sort_passes(256) == 1
     assert bench.sort_passes(1) == 0
-    assert bench.launches_per_view(8160, backward=True) == 18
-    assert bench.launches_per_view(8160, backward=True, peers=True) == 21
-    assert bench.launches_per_view(8160, backward=True, peers=True, sharded=True) == 22
-    assert bench.launches_per_view(8160, backward=False) == 13
-    assert bench.launches_per_view(256, backward=True) == 17
-    assert bench.launches_per_view(1, backward=False) == 10
+    # 1080p at 16x16 tiles (row/column binning): 16 forward launches, 8 more
+    # for the training step's loss, plan and backward
+    assert bench.launches_per_view(120, 68, backward=True) == 24
+    assert bench.launches_per_view(120, 68, backward=True, peers=True) == 27
+    assert bench.launches_per_view(120, 68, backward=True, peers=True, sharded=True) == 28
+    # a grid too wide for the row/column tables: count scan, emit, histogram,
+    # two tile-sort passes and ranges
+    assert bench.launches_per_view(300, 6, backward=False) == 15
+    assert bench.launches_per_view(120, 68, backward=False) == 16
+    assert bench.launches_per_view(16, 16, backward=True) == 24
 
 
 def test_views_split_over_ranks():
