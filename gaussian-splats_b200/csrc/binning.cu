@@ -815,16 +815,29 @@ __global__ void __launch_bounds__(kThreads) row_scatter_kernel(
   for (int y = threadIdx.x; y < rows; y += kThreads)
     s_run[y] = row_seg_start[y] + seg_prefix[y * chunks_pitch + blockIdx.x];
   __syncthreads();
+  // All batches' ids, then all their rectangles, before the first barrier:
+  // the gathers' latencies overlap instead of one per batch.
+  uint32_t g[kChunkBatches];
+  int y0[kChunkBatches], y1[kChunkBatches];
+#pragma unroll
   for (int bt = 0; bt < kChunkBatches; ++bt) {
     const int64_t j = first + bt * kThreads + threadIdx.x;
-    uint32_t g = 0;
-    int4 b = make_int4(0, 0, 0, 0);
-    if (j < v) {
-      g = sorted_ids[j];
-      b = clamp_rect(__ldg(bounds + g), cols, rows);
+    g[bt] = j < v ? sorted_ids[j] : 0xffffffffu;
+  }
+#pragma unroll
+  for (int bt = 0; bt < kChunkBatches; ++bt) {
+    y0[bt] = y1[bt] = 0;
+    if (g[bt] != 0xffffffffu) {
+      const int4 b = clamp_rect(__ldg(bounds + g[bt]), cols, rows);
+      y0[bt] = b.z;
+      y1[bt] = b.w;
     }
-    scatter_batch(b.z, b.w, rows, s_cover, s_base, s_run, rows, [&](int, uint32_t pos) {
-      if (pos < seg_capacity) segs[pos] = g;
+  }
+#pragma unroll
+  for (int bt = 0; bt < kChunkBatches; ++bt) {
+    const uint32_t id = g[bt];
+    scatter_batch(y0[bt], y1[bt], rows, s_cover, s_base, s_run, rows, [&](int, uint32_t pos) {
+      if (pos < seg_capacity) segs[pos] = id;
     });
   }
 }
@@ -844,13 +857,19 @@ __global__ void __launch_bounds__(kThreads) col_count_kernel(
     const uint32_t y = chunk_row[c];
     const uint32_t s0 = row_seg_start[y] + (c - row_chunk_start[y]) * kChunkItems;
     const uint32_t end = row_seg_start[y + 1];
+    int2 span[kChunkBatches];
 #pragma unroll
     for (int bt = 0; bt < kChunkBatches; ++bt) {
       const uint32_t si = s0 + bt * kThreads + threadIdx.x;
-      if (si < end && si < s0 + kChunkItems) {
-        const int2 span = __ldg(reinterpret_cast<const int2*>(bounds + segs[si]));
-        const int x0 = min(max(span.x, 0), cols);  // as clamp_rect
-        const int x1 = min(max(span.y, x0), cols);
+      span[bt] = make_int2(0, 0);
+      if (si < end && si < s0 + kChunkItems)
+        span[bt] = __ldg(reinterpret_cast<const int2*>(bounds + segs[si]));
+    }
+#pragma unroll
+    for (int bt = 0; bt < kChunkBatches; ++bt) {
+      const int x0 = min(max(span[bt].x, 0), cols);  // as clamp_rect
+      const int x1 = min(max(span[bt].y, x0), cols);
+      if (x0 < x1) {
         atomicAdd(&s_diff[x0], 1);
         atomicAdd(&s_diff[x1], -1);
       }
