@@ -170,6 +170,7 @@ __global__ void __launch_bounds__(kThreads) upsweep_kernel(Source src, Count cou
                                                           int shift0, uint32_t* __restrict__ hist,
                                                           uint32_t* __restrict__ valid_total,
                                                           unsigned long long* __restrict__ weight_total) {
+  chain_wait();
   __shared__ uint32_t s_hist[4][kRadix];
   const int64_t n = count.get();
   for (int i = threadIdx.x; i < 4 * kRadix; i += kThreads) (&s_hist[0][0])[i] = 0;
@@ -300,6 +301,7 @@ __global__ void __launch_bounds__(kThreads, 4) sort_pass_kernel(
     uint32_t* __restrict__ status, uint32_t* __restrict__ tile_counter,
     uint32_t* __restrict__ keys_out, uint32_t* __restrict__ values_out,
     uint32_t* __restrict__ error) {
+  chain_wait();
   __shared__ uint32_t s_warp_hist[kWarps][kRadix];
   __shared__ uint32_t s_local_start[kRadix];
   __shared__ uint32_t s_global_base[kRadix];
@@ -398,6 +400,7 @@ __global__ void __launch_bounds__(kThreads) count_scan_kernel(
     const int32_t* __restrict__ counts, uint64_t* __restrict__ status,
     uint32_t* __restrict__ tile_counter, uint32_t* __restrict__ offsets,
     int64_t* __restrict__ total_out, uint32_t* __restrict__ error) {
+  chain_wait();
   __shared__ uint32_t s_tmp[kWarps];
   __shared__ uint32_t s_block;
   __shared__ uint64_t s_exclusive;
@@ -482,6 +485,7 @@ __global__ void __launch_bounds__(kThreads) emit_kernel(
     const uint32_t* __restrict__ offsets, const int32_t* __restrict__ counts,
     const int4* __restrict__ bounds, int tiles_w, int64_t capacity,
     uint32_t* __restrict__ tile_keys, uint32_t* __restrict__ values) {
+  chain_wait();
   const int lane = threadIdx.x & 31;
   const int64_t warp_first = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) - lane;
   const int64_t n = *num_valid;
@@ -534,6 +538,7 @@ __global__ void __launch_bounds__(kThreads) emit_kernel(
 constexpr int kRangeItems = 8;
 __global__ void ranges_kernel(const uint32_t* __restrict__ sorted_keys, Count count,
                               int64_t num_tiles, int64_t* __restrict__ ranges) {
+  chain_wait();
   const int64_t total = count.get();
   const int64_t i0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * kRangeItems;
   if (i0 > total) return;
@@ -692,6 +697,7 @@ __global__ void __launch_bounds__(kThreads) row_count_kernel(
     const uint32_t* __restrict__ sorted_ids, const uint32_t* __restrict__ num_valid,
     const int4* __restrict__ bounds, int rows, int cols, int64_t chunks_pitch,
     uint32_t* __restrict__ seg_counts, uint32_t* __restrict__ pair_counts) {
+  chain_wait();
   __shared__ int32_t s_seg[kMaxTileRows + 1];
   __shared__ int32_t s_pair[kMaxTileRows + 1];
   __shared__ uint32_t s_tmp[kWarps];
@@ -736,6 +742,7 @@ __global__ void __launch_bounds__(kScanThreads) row_scan_kernel(
     const uint32_t* __restrict__ num_valid, int64_t chunks_pitch,
     uint32_t* __restrict__ seg_counts, const uint32_t* __restrict__ pair_counts,
     uint32_t* __restrict__ row_segs, uint32_t* __restrict__ row_pairs) {
+  chain_wait();
   __shared__ uint32_t s_tmp[32];
   const int y = blockIdx.x;
   const int64_t chunks = (static_cast<int64_t>(*num_valid) + kChunkItems - 1) / kChunkItems;
@@ -772,6 +779,7 @@ __global__ void __launch_bounds__(kScanThreads) row_layout_kernel(
     uint32_t seg_capacity, uint32_t* __restrict__ row_seg_start,
     uint32_t* __restrict__ row_pair_start, uint32_t* __restrict__ row_chunk_start,
     uint32_t* __restrict__ chunk_row) {
+  chain_wait();
   __shared__ uint32_t s_tmp[32];
   const int y = threadIdx.x;  // rows <= kScanThreads
   const uint32_t segs = y < rows ? row_segs[y] : 0u;
@@ -805,6 +813,7 @@ __global__ void __launch_bounds__(kThreads) row_scatter_kernel(
     const int4* __restrict__ bounds, int rows, int cols, int64_t chunks_pitch,
     const uint32_t* __restrict__ seg_prefix, const uint32_t* __restrict__ row_seg_start,
     uint32_t seg_capacity, uint32_t* __restrict__ segs) {
+  chain_wait();
   __shared__ uint32_t s_cover[kWarps * kMaxTileRows];
   __shared__ uint32_t s_base[kWarps * kMaxTileRows];
   __shared__ uint32_t s_run[kMaxTileRows];
@@ -848,6 +857,7 @@ __global__ void __launch_bounds__(kThreads) col_count_kernel(
     const uint32_t* __restrict__ segs, const int4* __restrict__ bounds, int rows, int cols,
     const uint32_t* __restrict__ row_seg_start, const uint32_t* __restrict__ row_chunk_start,
     const uint32_t* __restrict__ chunk_row, uint32_t* __restrict__ col_counts) {
+  chain_wait();
   __shared__ int32_t s_diff[kMaxTileCols + 1];
   __shared__ uint32_t s_tmp[kWarps];
   const uint32_t num_chunks = row_chunk_start[rows];
@@ -893,6 +903,7 @@ __global__ void __launch_bounds__(kScanThreads) col_scan_kernel(
     int cols, const uint32_t* __restrict__ row_chunk_start,
     const uint32_t* __restrict__ row_pair_start, int64_t id_capacity,
     uint32_t* __restrict__ col_counts, int64_t* __restrict__ ranges) {
+  chain_wait();
   constexpr int kParts = kScanThreads / kMaxTileCols;  // 4
   __shared__ uint32_t s_part[kParts][kMaxTileCols];
   __shared__ uint32_t s_tmp[32];
@@ -953,6 +964,7 @@ __global__ void __launch_bounds__(kThreads) col_scatter_kernel(
     const uint32_t* __restrict__ row_seg_start, const uint32_t* __restrict__ row_chunk_start,
     const uint32_t* __restrict__ chunk_row, const uint32_t* __restrict__ col_first,
     int64_t id_capacity, int32_t* __restrict__ ids) {
+  chain_wait();
   __shared__ uint32_t s_cover[kWarps * kMaxTileCols];
   __shared__ uint32_t s_base[kWarps * kMaxTileCols];
   __shared__ uint32_t s_run[kMaxTileCols];
@@ -1166,7 +1178,7 @@ int32_t launch_bin_count_kernels(int64_t n, const float* projected_mean, const i
   if (n > 0) {
     const int64_t blocks = (n + kTile - 1) / kTile;
     static_assert(sizeof(h->total) == sizeof(unsigned long long), "64-bit total");
-    upsweep_kernel<DepthSource, 4><<<upsweep_blocks(n), kThreads, 0, stream>>>(
+    launch_chained(upsweep_kernel<DepthSource, 4>, upsweep_blocks(n), kThreads, stream,
         DepthSource{projected_mean, counts}, Count{n, nullptr}, 4, 0, &h->hist[0][0],
         &h->num_valid, reinterpret_cast<unsigned long long*>(&h->total));
     GS_TRY(check_launch());
@@ -1177,7 +1189,7 @@ int32_t launch_bin_count_kernels(int64_t n, const float* projected_mean, const i
     uint32_t* vB = at<uint32_t>(workspace, L.ids_b);
     // Pass 0 filters and reads the projection outputs directly; passes 1-3
     // ping-pong A -> B -> A so the ids finish in ids_a.
-    sort_pass_kernel<<<blocks, kThreads, 0, stream>>>(
+    launch_chained(sort_pass_kernel<DepthSource>, blocks, kThreads, stream,
         DepthSource{projected_mean, counts}, Count{n, nullptr}, 0, &h->hist[0][0], depth_status,
         &h->pass_counters[0], kB, vB, &h->error);
     GS_TRY(check_launch());
@@ -1186,7 +1198,7 @@ int32_t launch_bin_count_kernels(int64_t n, const float* projected_mean, const i
     uint32_t* outs_k[3] = {kA, kB, nullptr};
     uint32_t* outs_v[3] = {vA, vB, vA};
     for (int p = 1; p < 4; ++p) {
-      sort_pass_kernel<<<blocks, kThreads, 0, stream>>>(
+      launch_chained(sort_pass_kernel<ArraySource>, blocks, kThreads, stream,
           ArraySource{ins_k[p - 1], ins_v[p - 1]}, Count{0, &h->num_valid}, 8 * p,
           &h->hist[p][0], depth_status + static_cast<int64_t>(p) * blocks * kRadix,
           &h->pass_counters[p], outs_k[p - 1], outs_v[p - 1], &h->error);
@@ -1219,34 +1231,34 @@ static int32_t launch_bin_sort_rowcol(int64_t n, int64_t total, const int32_t* b
   uint32_t* col_counts = at<uint32_t>(sort_workspace, L.col_counts);
   uint32_t* segs = at<uint32_t>(sort_workspace, L.segs);
   if (n > 0) {
-    row_count_kernel<<<static_cast<unsigned>(L.chunks_a), kThreads, 0, stream>>>(
+    launch_chained(row_count_kernel, static_cast<unsigned>(L.chunks_a), kThreads, stream,
         sorted_ids, &ch->num_valid, b4, rows, cols, pitch, seg_counts, pair_counts);
     GS_TRY(check_launch());
   }
-  row_scan_kernel<<<rows, kScanThreads, 0, stream>>>(&ch->num_valid, pitch, seg_counts,
+  launch_chained(row_scan_kernel, rows, kScanThreads, stream, &ch->num_valid, pitch, seg_counts,
                                                      pair_counts, row_segs, row_pairs);
   GS_TRY(check_launch());
-  row_layout_kernel<<<1, kScanThreads, 0, stream>>>(row_segs, row_pairs, rows, capacity,
+  launch_chained(row_layout_kernel, 1, kScanThreads, stream, row_segs, row_pairs, rows, capacity,
                                                     row_seg_start, row_pair_start,
                                                     row_chunk_start, chunk_row);
   GS_TRY(check_launch());
   if (n > 0) {
-    row_scatter_kernel<<<static_cast<unsigned>(L.chunks_a), kThreads, 0, stream>>>(
+    launch_chained(row_scatter_kernel, static_cast<unsigned>(L.chunks_a), kThreads, stream,
         sorted_ids, &ch->num_valid, b4, rows, cols, pitch, seg_counts, row_seg_start, capacity,
         segs);
     GS_TRY(check_launch());
   }
   const uint64_t grid_b = L.max_chunks_b < 8 * kSmCount ? L.max_chunks_b : 8 * kSmCount;
   if (grid_b > 0) {
-    col_count_kernel<<<static_cast<unsigned>(grid_b), kThreads, 0, stream>>>(
+    launch_chained(col_count_kernel, static_cast<unsigned>(grid_b), kThreads, stream,
         segs, b4, rows, cols, row_seg_start, row_chunk_start, chunk_row, col_counts);
     GS_TRY(check_launch());
   }
-  col_scan_kernel<<<rows, kScanThreads, 0, stream>>>(cols, row_chunk_start, row_pair_start,
+  launch_chained(col_scan_kernel, rows, kScanThreads, stream, cols, row_chunk_start, row_pair_start,
                                                      total, col_counts, ranges);
   GS_TRY(check_launch());
   if (grid_b > 0 && total > 0) {
-    col_scatter_kernel<<<static_cast<unsigned>(grid_b), kThreads, 0, stream>>>(
+    launch_chained(col_scatter_kernel, static_cast<unsigned>(grid_b), kThreads, stream,
         segs, b4, rows, cols, row_seg_start, row_chunk_start, chunk_row, col_counts, total,
         gaussian_ids);
     GS_TRY(check_launch());
@@ -1281,19 +1293,19 @@ static int32_t launch_bin_sort_radix(int64_t n, int64_t total, const int32_t* bo
   const uint32_t* sorted_keys = kA;
   const Count live{total, nullptr, &ch->total};
   if (n > 0) {
-    count_scan_kernel<<<(n + kTile - 1) / kTile, kThreads, 0, stream>>>(
+    launch_chained(count_scan_kernel, (n + kTile - 1) / kTile, kThreads, stream,
         sorted_ids, &ch->num_valid, counts, at<uint64_t>(sort_workspace, L.scan_status),
         &h->scan_counter, offsets, &h->total, &h->error);
     GS_TRY(check_launch());
   }
   if (total > 0) {
     const int passes = R.passes;
-    emit_kernel<<<ceil_div(n, kThreads), kThreads, 0, stream>>>(
+    launch_chained(emit_kernel, ceil_div(n, kThreads), kThreads, stream,
         sorted_ids, &ch->num_valid, offsets, counts, reinterpret_cast<const int4*>(bounds),
         static_cast<int>(tiles_w), total, kA, passes == 0 ? out_ids : vA);
     GS_TRY(check_launch());
     if (passes > 0) {
-      upsweep_kernel<ArraySource, 16><<<upsweep_blocks(total), kThreads, 0, stream>>>(
+      launch_chained(upsweep_kernel<ArraySource, 16>, upsweep_blocks(total), kThreads, stream,
           ArraySource{kA, vA}, live, passes, 0, &rh->hist[0][0], nullptr, nullptr);
       GS_TRY(check_launch());
       const int64_t blocks = (total + kTile - 1) / kTile;
@@ -1302,7 +1314,7 @@ static int32_t launch_bin_sort_radix(int64_t n, int64_t total, const int32_t* bo
       for (int pass = 0; pass < passes; ++pass) {
         uint32_t* dst_k = (pass % 2 == 0) ? kB : kA;
         uint32_t* dst_v = (pass == passes - 1) ? out_ids : ((pass % 2 == 0) ? vB : vA);
-        sort_pass_kernel<<<blocks, kThreads, 0, stream>>>(
+        launch_chained(sort_pass_kernel<ArraySource>, blocks, kThreads, stream,
             ArraySource{src_k, src_v}, live, 8 * pass, &rh->hist[pass][0],
             at<uint32_t>(radix, R.status) + static_cast<int64_t>(pass) * blocks * kRadix,
             &rh->pass_counters[pass], dst_k, dst_v, &h->error);
@@ -1314,7 +1326,7 @@ static int32_t launch_bin_sort_radix(int64_t n, int64_t total, const int32_t* bo
     }
   }
   if (num_tiles > 0) {
-    ranges_kernel<<<ceil_div(ceil_div(total + 1, kRangeItems), 256), 256, 0, stream>>>(
+    launch_chained(ranges_kernel, ceil_div(ceil_div(total + 1, kRangeItems), 256), 256, stream,
         sorted_keys, live, num_tiles, ranges);
     GS_TRY(check_launch());
   }
@@ -1360,7 +1372,7 @@ int32_t launch_sort_positions(int64_t total, int64_t num_keys, const int32_t* ke
   const int passes = L.passes > 0 ? L.passes : 1;
   if (L.passes == 0 && num_keys > 1) return GS_ERR_INVALID_ARGUMENT;
   if (total > 0) {
-    upsweep_kernel<PositionSource, 16><<<upsweep_blocks(total), kThreads, 0, stream>>>(
+    launch_chained(upsweep_kernel<PositionSource, 16>, upsweep_blocks(total), kThreads, stream,
         PositionSource{in_keys}, all, passes, 0, &h->hist[0][0], nullptr, nullptr);
     GS_TRY(check_launch());
     const int64_t blocks = (total + kTile - 1) / kTile;
@@ -1370,11 +1382,11 @@ int32_t launch_sort_positions(int64_t total, int64_t num_keys, const int32_t* ke
       uint32_t* dst_v = (pass == passes - 1) ? order : ((pass % 2 == 0) ? vB : vA);
       uint32_t* pass_status = status + static_cast<int64_t>(pass) * blocks * kRadix;
       if (pass == 0)
-        sort_pass_kernel<<<blocks, kThreads, 0, stream>>>(
+        launch_chained(sort_pass_kernel<PositionSource>, blocks, kThreads, stream,
             PositionSource{in_keys}, all, 0, &h->hist[0][0], pass_status, &h->pass_counters[0],
             dst_k, dst_v, &h->error);
       else
-        sort_pass_kernel<<<blocks, kThreads, 0, stream>>>(
+        launch_chained(sort_pass_kernel<ArraySource>, blocks, kThreads, stream,
             ArraySource{pass % 2 ? kB : kA, pass % 2 ? vB : vA}, all, 8 * pass,
             &h->hist[pass][0], pass_status, &h->pass_counters[pass], dst_k, dst_v, &h->error);
       GS_TRY(check_launch());
@@ -1382,7 +1394,7 @@ int32_t launch_sort_positions(int64_t total, int64_t num_keys, const int32_t* ke
     }
   }
   if (num_keys > 0) {
-    ranges_kernel<<<ceil_div(ceil_div(total + 1, kRangeItems), 256), 256, 0, stream>>>(
+    launch_chained(ranges_kernel, ceil_div(ceil_div(total + 1, kRangeItems), 256), 256, stream,
         sorted_keys, all, num_keys, segments);
     GS_TRY(check_launch());
   }

@@ -44,6 +44,45 @@ inline int32_t check_launch() {
 
 inline cudaStream_t as_cuda(gs_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
 
+// Chained launches (programmatic dependent launch). A step is a chain of
+// short kernels on one stream. Launched normally, a kernel is set up only
+// once the one before has completed and its writes have been flushed;
+// launch_chained lets the GPU prepare the launch ahead, so the kernel's CTAs
+// start as soon as the previous kernel's last CTA exits, and the flush is
+// awaited inside the kernel: every CTA of a kernel in the pipeline first
+// executes chain_wait(), which blocks in hardware (no spinning) until the
+// previous kernel on the stream has completed and its writes are visible. No
+// kernel reads or writes memory before its predecessor is done, so stream
+// order holds as before; because every kernel waits before anything else
+// (also before an early return), completion stays ordered along the chain:
+// k+1 cannot finish before k. After an operation that is not one of these
+// kernels (a memset, a copy, another library's kernel) a chained launch is
+// ordered as a normal one; chain_wait is a no-op in a kernel launched
+// normally. The kernels do not signal their dependents early
+// (griddepcontrol.launch_dependents): CTAs of the next kernel parked on the
+// SMs while this one still runs cost more than the earlier start saved
+// (training step 1.40 -> 1.43 ms on a 1080p view of 1M Gaussians, against
+// 1.39 ms without the early signal).
+__device__ __forceinline__ void chain_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+template <class... Params, class... Args>
+inline cudaError_t launch_chained(void (*kernel)(Params...), dim3 grid, dim3 block,
+                                  cudaStream_t stream, Args&&... args) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t config = {};
+  config.gridDim = grid;
+  config.blockDim = block;
+  config.dynamicSmemBytes = 0;
+  config.stream = stream;
+  config.attrs = attr;
+  config.numAttrs = 1;
+  return cudaLaunchKernelEx(&config, kernel, static_cast<Args&&>(args)...);
+}
+
 inline unsigned ceil_div(int64_t a, int64_t b) { return static_cast<unsigned>((a + b - 1) / b); }
 
 // Gaussian index and intersection offsets are 32-bit in the binning kernels.

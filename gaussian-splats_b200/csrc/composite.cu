@@ -205,6 +205,7 @@ __global__ void __launch_bounds__(TileShape<TS, 1>::kThreads,
                          float* __restrict__ image, float* __restrict__ final_transmittance,
                          int32_t* __restrict__ n_contributors,
                          const int32_t* __restrict__ tile_order) {
+  chain_wait();
   using S = TileShape<TS, 1>;
   constexpr int NB = S::kBatch;
   constexpr int kWarps = S::kWarps;
@@ -373,6 +374,7 @@ __global__ void __launch_bounds__(TileShape<TS, PPT>::kThreads,
                          const int32_t* __restrict__ n_contributors, const gs_params p,
                          float* __restrict__ grad_projected,
                          const int32_t* __restrict__ tile_order, const int4* __restrict__ items) {
+  chain_wait();
   using S = TileShape<TS, PPT>;
   // (the deterministic form's per-warp vectors of 32 x 32 tiles take smaller batches
   // to stay within 48 KB of shared memory)
@@ -667,6 +669,7 @@ __global__ void __launch_bounds__(256) pack_records_kernel(
     int64_t n, const float* __restrict__ projected_mean,
     const float* __restrict__ inverse_covariance, const float* __restrict__ projected_color,
     const float* __restrict__ projected_opacity, const gs_params p, float4* __restrict__ records) {
+  chain_wait();
   const int64_t g = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (g >= n) return;
   const float4 conic = __ldg(reinterpret_cast<const float4*>(inverse_covariance) + g);
@@ -683,7 +686,7 @@ int32_t launch_pack_records(int64_t n, const float* projected_mean,
                             const float* projected_opacity, const gs_params& p, float* records,
                             cudaStream_t stream) {
   if (n == 0) return GS_OK;
-  pack_records_kernel<<<ceil_div(n, 256), 256, 0, stream>>>(
+  launch_chained(pack_records_kernel, ceil_div(n, 256), 256, stream,
       n, projected_mean, inverse_covariance, projected_color, projected_opacity, p,
       reinterpret_cast<float4*>(records));
   return check_launch();
@@ -695,6 +698,7 @@ int32_t launch_pack_records(int64_t n, const float* projected_mean,
 __global__ void __launch_bounds__(256) reduce_rows_kernel(
     int64_t n, const uint32_t* __restrict__ order, const int64_t* __restrict__ segments,
     const float* __restrict__ rows, float* __restrict__ grad_projected) {
+  chain_wait();
   const int64_t g = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (g >= n) return;
   float acc[9] = {};
@@ -756,6 +760,7 @@ __global__ void __launch_bounds__(256) order_count_kernel(const int64_t* __restr
                                                           const uint32_t* __restrict__ work,
                                                           int64_t num_tiles,
                                                           uint32_t* __restrict__ hist) {
+  chain_wait();
   const int lane = threadIdx.x & 31;
   const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int c = t < num_tiles ? work_class(tile_work(ranges, work, t)) : kWorkClasses;
@@ -786,6 +791,7 @@ __global__ void __launch_bounds__(256) order_scatter_kernel(
     const int64_t* __restrict__ ranges, const uint32_t* __restrict__ work, int64_t num_tiles,
     const uint32_t* __restrict__ hist, uint32_t* __restrict__ cursor,
     int32_t* __restrict__ order) {
+  chain_wait();
   __shared__ uint32_t s_start[kWorkClasses];
   if (threadIdx.x < 32) class_starts(hist, s_start, nullptr);
   __syncthreads();
@@ -806,6 +812,7 @@ __global__ void __launch_bounds__(256) order_scatter_kernel(
 __global__ void __launch_bounds__(256) tile_max_contrib_kernel(
     const int32_t* __restrict__ n_contributors, int width, int tile_size, int tiles_w,
     int64_t num_tiles, uint32_t* __restrict__ work) {
+  chain_wait();
   const int64_t t = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (t >= num_tiles) return;
@@ -877,6 +884,7 @@ __global__ void __launch_bounds__(256) plan_count_kernel(
     const int64_t* __restrict__ ranges, const uint32_t* __restrict__ max_contrib,
     int64_t num_tiles, int split_walk, uint32_t* __restrict__ hist,
     uint32_t* __restrict__ extra, int2* __restrict__ tile_parts) {
+  chain_wait();
   const int lane = threadIdx.x & 31;
   const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const uint32_t walk = t < num_tiles ? tile_walk(ranges, max_contrib, t) : 0u;
@@ -905,6 +913,7 @@ __global__ void __launch_bounds__(256) plan_scatter_kernel(
     int64_t num_tiles, const uint32_t* __restrict__ hist, uint32_t* __restrict__ cursor,
     const uint32_t* __restrict__ extra, const int2* __restrict__ tile_parts,
     int4* __restrict__ items, uint32_t* __restrict__ header) {
+  chain_wait();
   __shared__ uint32_t s_start[kWorkClasses];
   __shared__ uint32_t s_total;
   if (threadIdx.x < 32) class_starts(hist, s_start, &s_total);
@@ -957,15 +966,15 @@ int32_t launch_composite_bwd_plan(const int64_t* ranges, const int32_t* n_contri
   uint32_t* work = reinterpret_cast<uint32_t*>(base + L.work);
   uint32_t* header = reinterpret_cast<uint32_t*>(base + L.header);
   GS_CUDA_TRY(cudaMemsetAsync(header, 0, 1024, stream));
-  tile_max_contrib_kernel<<<ceil_div(num_tiles * 32, 256), 256, 0, stream>>>(
+  launch_chained(tile_max_contrib_kernel, ceil_div(num_tiles * 32, 256), 256, stream,
       n_contributors, p.width, p.tile_size, tiles_w, num_tiles, work);
   GS_TRY(check_launch());
   int2* tile_parts = reinterpret_cast<int2*>(base + L.tile_parts);
   const int walk = split_walk > 0 ? split_walk : kDefaultSplitWalk;
-  plan_count_kernel<<<ceil_div(num_tiles, 256), 256, 0, stream>>>(
+  launch_chained(plan_count_kernel, ceil_div(num_tiles, 256), 256, stream,
       ranges, work, num_tiles, walk, header + 16, header + 144, tile_parts);
   GS_TRY(check_launch());
-  plan_scatter_kernel<<<ceil_div(num_tiles, 256), 256, 0, stream>>>(
+  launch_chained(plan_scatter_kernel, ceil_div(num_tiles, 256), 256, stream,
       ranges, work, num_tiles, header + 16, header + 80, header + 144, tile_parts,
       reinterpret_cast<int4*>(base + L.items), header);
   return check_launch();
@@ -983,14 +992,15 @@ int32_t launch_tile_order(const int64_t* ranges, const int32_t* n_contributors,
   GS_CUDA_TRY(cudaMemsetAsync(hist, 0, 2 * kWorkClasses * sizeof(uint32_t), stream));
   const uint32_t* work = nullptr;
   if (n_contributors != nullptr) {
-    tile_max_contrib_kernel<<<ceil_div(num_tiles * 32, 256), 256, 0, stream>>>(
+    launch_chained(tile_max_contrib_kernel, ceil_div(num_tiles * 32, 256), 256, stream,
         n_contributors, p.width, p.tile_size, tiles_w, num_tiles, tile_work);
     GS_TRY(check_launch());
     work = tile_work;
   }
-  order_count_kernel<<<ceil_div(num_tiles, 256), 256, 0, stream>>>(ranges, work, num_tiles, hist);
+  launch_chained(order_count_kernel, ceil_div(num_tiles, 256), 256, stream, ranges, work,
+                 num_tiles, hist);
   GS_TRY(check_launch());
-  order_scatter_kernel<<<ceil_div(num_tiles, 256), 256, 0, stream>>>(
+  launch_chained(order_scatter_kernel, ceil_div(num_tiles, 256), 256, stream,
       ranges, work, num_tiles, hist, hist + kWorkClasses, order);
   return check_launch();
 }
@@ -1005,10 +1015,12 @@ int32_t launch_composite_fwd(const float* records, const int32_t* gaussian_ids,
   const float4* rec = reinterpret_cast<const float4*>(records);
 #define GS_LAUNCH(TS)                                                                          \
   if (p.gaussian_mode)                                                                         \
-    composite_fwd_kernel<TS, true><<<static_cast<unsigned>(num_tiles), TS * TS, 0, stream>>>(  \
-        rec, gaussian_ids, ranges, p, image, final_transmittance, n_contributors, tile_order); \
-  else                                                                                         \
-    composite_fwd_kernel<TS, false><<<static_cast<unsigned>(num_tiles), TS * TS, 0, stream>>>( \
+    launch_chained(composite_fwd_kernel<TS, true>, static_cast<unsigned>(num_tiles), TS * TS,   \
+                   stream, rec, gaussian_ids, ranges, p, image, final_transmittance,            \
+                   n_contributors, tile_order);                                                 \
+  else                                                                                          \
+    launch_chained(composite_fwd_kernel<TS, false>, static_cast<unsigned>(num_tiles), TS * TS,  \
+                   stream,                                                                      \
         rec, gaussian_ids, ranges, p, image, final_transmittance, n_contributors, tile_order)
   GS_TILE_DISPATCH(p.tile_size, GS_LAUNCH)
 #undef GS_LAUNCH
@@ -1030,8 +1042,8 @@ int32_t launch_composite_bwd(int64_t n, const float* records, const int32_t* gau
       plan ? reinterpret_cast<const int4*>(static_cast<char*>(plan) + L.items) : nullptr;
   const unsigned grid = static_cast<unsigned>(plan ? num_tiles + kExtraParts : num_tiles);
 #define GS_LAUNCH_MODE(TS, G)                                                                  \
-  composite_bwd_kernel<TS, BwdPpt<TS>::value, G>                                               \
-      <<<grid, TileShape<TS, BwdPpt<TS>::value>::kThreads, 0, stream>>>(                       \
+  launch_chained(composite_bwd_kernel<TS, BwdPpt<TS>::value, G>,                                \
+                 grid, TileShape<TS, BwdPpt<TS>::value>::kThreads, stream,                      \
           rec, gaussian_ids, ranges, grad_image, final_transmittance, n_contributors, p,       \
           grad_projected, nullptr, items)
 #define GS_LAUNCH(TS)                 \
@@ -1083,14 +1095,14 @@ int32_t launch_composite_bwd_deterministic(int64_t n, int64_t total, const float
   if (num_tiles > 0 && total > 0) {
 #define GS_LAUNCH(TS)                                                                          \
   if (p.gaussian_mode)                                                                         \
-    composite_bwd_kernel<TS, BwdPpt<TS>::value, true, true>                                    \
-        <<<static_cast<unsigned>(num_tiles), TileShape<TS, BwdPpt<TS>::value>::kThreads, 0,   \
-           stream>>>(rec, gaussian_ids, ranges, grad_image, final_transmittance,               \
+    launch_chained(composite_bwd_kernel<TS, BwdPpt<TS>::value, true, true>,                     \
+        static_cast<unsigned>(num_tiles), TileShape<TS, BwdPpt<TS>::value>::kThreads, stream,   \
+                     rec, gaussian_ids, ranges, grad_image, final_transmittance,                \
                      n_contributors, p, rows, tile_order, nullptr);                            \
   else                                                                                         \
-    composite_bwd_kernel<TS, BwdPpt<TS>::value, false, true>                                   \
-        <<<static_cast<unsigned>(num_tiles), TileShape<TS, BwdPpt<TS>::value>::kThreads, 0,   \
-           stream>>>(rec, gaussian_ids, ranges, grad_image, final_transmittance,               \
+    launch_chained(composite_bwd_kernel<TS, BwdPpt<TS>::value, false, true>,                    \
+        static_cast<unsigned>(num_tiles), TileShape<TS, BwdPpt<TS>::value>::kThreads, stream,   \
+                     rec, gaussian_ids, ranges, grad_image, final_transmittance,                \
                      n_contributors, p, rows, tile_order, nullptr)
     GS_TILE_DISPATCH(p.tile_size, GS_LAUNCH)
 #undef GS_LAUNCH
@@ -1098,7 +1110,7 @@ int32_t launch_composite_bwd_deterministic(int64_t n, int64_t total, const float
   }
   GS_TRY(launch_sort_positions(total, n, gaussian_ids, base + L.sort, order, segments, stream));
   if (n == 0) return GS_OK;
-  reduce_rows_kernel<<<ceil_div(n, 256), 256, 0, stream>>>(n, order, segments, rows,
+  launch_chained(reduce_rows_kernel, ceil_div(n, 256), 256, stream, n, order, segments, rows,
                                                            grad_projected);
   return check_launch();
 }

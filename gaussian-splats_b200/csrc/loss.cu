@@ -35,6 +35,7 @@ template <bool kVec>
 __global__ void __launch_bounds__(kThreads) l1_partial_kernel(
     const float* __restrict__ image, int64_t row_stride, const float* __restrict__ target,
     int64_t rows, int64_t row_length, float* __restrict__ partials) {
+  chain_wait();
   float sum = 0.0f;
   for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
     const float* image_row = image + r * row_stride;
@@ -68,6 +69,7 @@ __global__ void __launch_bounds__(kThreads) l1_partial_kernel(
 __global__ void __launch_bounds__(kThreads) l1_total_kernel(const float* __restrict__ partials,
                                                             int num_partials, int64_t count,
                                                             float* __restrict__ loss) {
+  chain_wait();
   double sum = 0.0;
   for (int k = threadIdx.x; k < num_partials; k += kThreads) sum += partials[k];
   __shared__ double s_warp[kThreads / 32];
@@ -94,6 +96,7 @@ __global__ void __launch_bounds__(kThreads) l1_grad_kernel(
     const float* __restrict__ image, int64_t height, int64_t row_stride,
     const float* __restrict__ target, int64_t rows, int64_t row_length,
     const float* __restrict__ grad_loss, float* __restrict__ grad_image) {
+  chain_wait();
   // g / count as torch's mean backward forms it: g times the float reciprocal
   const float scale = __ldg(grad_loss) * (1.0f / static_cast<float>(rows * row_length));
   for (int64_t r = blockIdx.x; r < height; r += gridDim.x) {
@@ -141,13 +144,13 @@ int32_t launch_l1_fwd(const float* image, int64_t height, int64_t width, int64_t
     return GS_ERR_INVALID_ARGUMENT;
   const int64_t row_stride = width * channels, row_length = target_width * channels;
   if (vectorisable(image, target, nullptr, row_stride, row_length))
-    l1_partial_kernel<true><<<kBlocks, kThreads, 0, stream>>>(image, row_stride, target,
+    launch_chained(l1_partial_kernel<true>, kBlocks, kThreads, stream, image, row_stride, target,
                                                               target_height, row_length, partials);
   else
-    l1_partial_kernel<false><<<kBlocks, kThreads, 0, stream>>>(image, row_stride, target,
+    launch_chained(l1_partial_kernel<false>, kBlocks, kThreads, stream, image, row_stride, target,
                                                                target_height, row_length, partials);
   GS_TRY(check_launch());
-  l1_total_kernel<<<1, kThreads, 0, stream>>>(partials, kBlocks,
+  launch_chained(l1_total_kernel, 1, kThreads, stream, partials, kBlocks,
                                               target_height * target_width * channels, loss);
   return check_launch();
 }
@@ -161,10 +164,10 @@ int32_t launch_l1_bwd(const float* image, int64_t height, int64_t width, int64_t
   if (height * width == 0) return GS_OK;
   const int64_t row_stride = width * channels, row_length = target_width * channels;
   if (vectorisable(image, target, grad_image, row_stride, row_length))
-    l1_grad_kernel<true><<<kBlocks, kThreads, 0, stream>>>(
+    launch_chained(l1_grad_kernel<true>, kBlocks, kThreads, stream,
         image, height, row_stride, target, target_height, row_length, grad_loss, grad_image);
   else
-    l1_grad_kernel<false><<<kBlocks, kThreads, 0, stream>>>(
+    launch_chained(l1_grad_kernel<false>, kBlocks, kThreads, stream,
         image, height, row_stride, target, target_height, row_length, grad_loss, grad_image);
   return check_launch();
 }

@@ -245,6 +245,7 @@ __global__ void __launch_bounds__(kProjectThreads) project_fwd_kernel(
     float* __restrict__ projected_mean, float* __restrict__ inverse_covariance,
     float* __restrict__ projected_color, float* __restrict__ projected_opacity,
     int4* __restrict__ bounds, int32_t* __restrict__ counts, float4* __restrict__ records) {
+  chain_wait();
   constexpr int kPitch = ShPitch<K>::value;
   __shared__ __align__(16) FwdRows<K> s;
   const int tid = threadIdx.x;
@@ -425,6 +426,7 @@ __global__ void __launch_bounds__(256) project_fwd_batch_kernel(
     float* __restrict__ projected_mean, float* __restrict__ inverse_covariance,
     float* __restrict__ projected_color, float* __restrict__ projected_opacity,
     int4* __restrict__ bounds, int32_t* __restrict__ counts, float4* __restrict__ records) {
+  chain_wait();
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= n) return;
   if (threadIdx.x == 0) {
@@ -859,6 +861,7 @@ __global__ void __launch_bounds__(128, K > 16 ? 3 : 4) project_bwd_views_kernel(
     const __grid_constant__ Source src, float* __restrict__ grad_mean,
     float* __restrict__ grad_rotation, float* __restrict__ grad_scale,
     float* __restrict__ grad_opacity, float* __restrict__ grad_color) {
+  chain_wait();
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= n) return;
   if (threadIdx.x == 0) {
@@ -990,6 +993,7 @@ __global__ void __launch_bounds__(project_bwd_threads(K)) project_bwd_kernel(
     const gs_params p, float* __restrict__ grad_mean, float* __restrict__ grad_rotation,
     float* __restrict__ grad_scale, float* __restrict__ grad_opacity,
     float* __restrict__ grad_color) {
+  chain_wait();
   constexpr int T = project_bwd_threads(K);
   constexpr int kPitch = ShPitch<K>::value;
   __shared__ __align__(16) BwdRows<K, T> s;
@@ -1044,7 +1048,7 @@ int32_t launch_project_fwd(int64_t n, int32_t num_sh, const float* mean, const f
   if (n == 0) return GS_OK;
   const unsigned blocks = ceil_div(n, kProjectThreads);
 #define GS_LAUNCH(K)                                                                          \
-  project_fwd_kernel<K><<<blocks, kProjectThreads, 0, stream>>>(                                          \
+  launch_chained(project_fwd_kernel<K>, blocks, kProjectThreads, stream,                       \
       n, mean, rotation, scale, opacity, color, camera_rotation, camera_translation, p,       \
       projected_mean, inverse_covariance, projected_color, projected_opacity,                 \
       reinterpret_cast<int4*>(bounds), counts, reinterpret_cast<float4*>(records))
@@ -1074,7 +1078,7 @@ int32_t launch_project_fwd_batch(int64_t n, int32_t num_sh, int32_t num_views, c
     }
     const int64_t o = static_cast<int64_t>(first) * n;
 #define GS_LAUNCH(K)                                                                          \
-  project_fwd_batch_kernel<K><<<blocks, 256, 0, stream>>>(                                    \
+  launch_chained(project_fwd_batch_kernel<K>, blocks, 256, stream,                             \
       n, mean, rotation, scale, opacity, color, batch, projected_mean + 3 * o,                 \
       inverse_covariance + 4 * o, projected_color + 3 * o, projected_opacity + o,              \
       reinterpret_cast<int4*>(bounds) + o, counts + o,                                        \
@@ -1096,7 +1100,7 @@ int32_t launch_project_bwd_views(int64_t n, int32_t num_sh, int32_t num_views,
   const unsigned blocks = ceil_div(n, 128);
   const ContiguousViews src{grad_projected, counts, n};
 #define GS_LAUNCH(K)                                                                          \
-  project_bwd_views_kernel<K, ContiguousViews><<<blocks, 128, 0, stream>>>(                   \
+  launch_chained(project_bwd_views_kernel<K, ContiguousViews>, blocks, 128, stream,            \
       n, num_views, mean, rotation, scale, opacity, color,                                    \
       static_cast<const ViewRecord*>(views), src, grad_mean, grad_rotation, grad_scale,       \
       grad_opacity, grad_color)
@@ -1138,8 +1142,8 @@ int32_t launch_project_bwd(int64_t n, int32_t num_sh, const float* mean, const f
                            float* grad_color, cudaStream_t stream) {
   if (n == 0) return GS_OK;
 #define GS_LAUNCH(K)                                                                          \
-  project_bwd_kernel<K><<<ceil_div(n, project_bwd_threads(K)), project_bwd_threads(K), 0,       \
-                          stream>>>(                                          \
+  launch_chained(project_bwd_kernel<K>, ceil_div(n, project_bwd_threads(K)),                   \
+                 project_bwd_threads(K), stream,                                               \
       n, mean, rotation, scale, opacity, color, camera_rotation, camera_translation,           \
       inverse_covariance, grad_projected, counts, p, grad_mean, grad_rotation, grad_scale,    \
       grad_opacity, grad_color)
@@ -1149,11 +1153,13 @@ int32_t launch_project_bwd(int64_t n, int32_t num_sh, const float* mean, const f
 }
 
 __global__ void det_exp_kernel(int64_t n, const float* __restrict__ x, float* __restrict__ y) {
+  chain_wait();
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i < n) y[i] = det_exp(x[i]);
 }
 
 __global__ void det_log_kernel(int64_t n, const float* __restrict__ x, float* __restrict__ y) {
+  chain_wait();
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i < n) y[i] = det_log(x[i]);
 }
@@ -1161,9 +1167,9 @@ __global__ void det_log_kernel(int64_t n, const float* __restrict__ x, float* __
 int32_t launch_det_math(int which, int64_t n, const float* x, float* y, cudaStream_t stream) {
   if (n == 0) return GS_OK;
   if (which == 0)
-    det_exp_kernel<<<ceil_div(n, 256), 256, 0, stream>>>(n, x, y);
+    launch_chained(det_exp_kernel, ceil_div(n, 256), 256, stream, n, x, y);
   else
-    det_log_kernel<<<ceil_div(n, 256), 256, 0, stream>>>(n, x, y);
+    launch_chained(det_log_kernel, ceil_div(n, 256), 256, stream, n, x, y);
   return check_launch();
 }
 
