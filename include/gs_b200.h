@@ -225,7 +225,7 @@ int32_t gs_composite_bwd(int64_t n, const float *records, const int32_t *gaussia
  * whose backward takes one tile per program, composite_bwd.py:248): every
  * tile, heaviest first by its walk (list length up to its largest
  * contributor count, composite_bwd.py:81-83), with the tiles whose walk is
- * longer than split_walk entries (0: 1024) cut into parts of at most that
+ * longer than split_walk entries (0: 2048) cut into parts of at most that
  * many -- one CTA each, which first walks the parts behind its own for the
  * suffix it starts from (the same recurrence, so the same bits) -- so one
  * dense tile no longer sets the kernel's length. Up to 1024 parts beyond the
