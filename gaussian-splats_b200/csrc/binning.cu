@@ -1236,11 +1236,10 @@ static int32_t launch_bin_sort_rowcol(int64_t n, int64_t total, const int32_t* b
     GS_TRY(check_launch());
   }
   launch_chained(row_scan_kernel, rows, kScanThreads, stream, &ch->num_valid, pitch, seg_counts,
-                                                     pair_counts, row_segs, row_pairs);
+                 pair_counts, row_segs, row_pairs);
   GS_TRY(check_launch());
   launch_chained(row_layout_kernel, 1, kScanThreads, stream, row_segs, row_pairs, rows, capacity,
-                                                    row_seg_start, row_pair_start,
-                                                    row_chunk_start, chunk_row);
+                 row_seg_start, row_pair_start, row_chunk_start, chunk_row);
   GS_TRY(check_launch());
   if (n > 0) {
     launch_chained(row_scatter_kernel, static_cast<unsigned>(L.chunks_a), kThreads, stream,
@@ -1254,8 +1253,8 @@ static int32_t launch_bin_sort_rowcol(int64_t n, int64_t total, const int32_t* b
         segs, b4, rows, cols, row_seg_start, row_chunk_start, chunk_row, col_counts);
     GS_TRY(check_launch());
   }
-  launch_chained(col_scan_kernel, rows, kScanThreads, stream, cols, row_chunk_start, row_pair_start,
-                                                     total, col_counts, ranges);
+  launch_chained(col_scan_kernel, rows, kScanThreads, stream, cols, row_chunk_start,
+                 row_pair_start, total, col_counts, ranges);
   GS_TRY(check_launch());
   if (grid_b > 0 && total > 0) {
     launch_chained(col_scatter_kernel, static_cast<unsigned>(grid_b), kThreads, stream,

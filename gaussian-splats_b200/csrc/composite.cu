@@ -1025,8 +1025,8 @@ int32_t launch_composite_fwd(const float* records, const int32_t* gaussian_ids,
                    n_contributors, tile_order);                                                 \
   else                                                                                          \
     launch_chained(composite_fwd_kernel<TS, false>, static_cast<unsigned>(num_tiles), TS * TS,  \
-                   stream,                                                                      \
-        rec, gaussian_ids, ranges, p, image, final_transmittance, n_contributors, tile_order)
+                   stream, rec, gaussian_ids, ranges, p, image, final_transmittance,            \
+                   n_contributors, tile_order)
   GS_TILE_DISPATCH(p.tile_size, GS_LAUNCH)
 #undef GS_LAUNCH
   return check_launch();
@@ -1049,8 +1049,8 @@ int32_t launch_composite_bwd(int64_t n, const float* records, const int32_t* gau
 #define GS_LAUNCH_MODE(TS, G)                                                                  \
   launch_chained(composite_bwd_kernel<TS, BwdPpt<TS>::value, G>,                                \
                  grid, TileShape<TS, BwdPpt<TS>::value>::kThreads, stream,                      \
-          rec, gaussian_ids, ranges, grad_image, final_transmittance, n_contributors, p,       \
-          grad_projected, nullptr, items)
+                 rec, gaussian_ids, ranges, grad_image, final_transmittance, n_contributors, p, \
+                 grad_projected, nullptr, items)
 #define GS_LAUNCH(TS)                 \
   if (p.gaussian_mode)                \
     GS_LAUNCH_MODE(TS, true);         \
@@ -1101,14 +1101,16 @@ int32_t launch_composite_bwd_deterministic(int64_t n, int64_t total, const float
 #define GS_LAUNCH(TS)                                                                          \
   if (p.gaussian_mode)                                                                         \
     launch_chained(composite_bwd_kernel<TS, BwdPpt<TS>::value, true, true>,                     \
-        static_cast<unsigned>(num_tiles), TileShape<TS, BwdPpt<TS>::value>::kThreads, stream,   \
-                     rec, gaussian_ids, ranges, grad_image, final_transmittance,                \
-                     n_contributors, p, rows, tile_order, nullptr);                            \
+                   static_cast<unsigned>(num_tiles),                                            \
+                   TileShape<TS, BwdPpt<TS>::value>::kThreads, stream, rec, gaussian_ids,       \
+                   ranges, grad_image, final_transmittance, n_contributors, p, rows,            \
+                   tile_order, nullptr);                                                        \
   else                                                                                         \
     launch_chained(composite_bwd_kernel<TS, BwdPpt<TS>::value, false, true>,                    \
-        static_cast<unsigned>(num_tiles), TileShape<TS, BwdPpt<TS>::value>::kThreads, stream,   \
-                     rec, gaussian_ids, ranges, grad_image, final_transmittance,                \
-                     n_contributors, p, rows, tile_order, nullptr)
+                   static_cast<unsigned>(num_tiles),                                            \
+                   TileShape<TS, BwdPpt<TS>::value>::kThreads, stream, rec, gaussian_ids,       \
+                   ranges, grad_image, final_transmittance, n_contributors, p, rows,            \
+                   tile_order, nullptr)
     GS_TILE_DISPATCH(p.tile_size, GS_LAUNCH)
 #undef GS_LAUNCH
     GS_TRY(check_launch());
@@ -1116,7 +1118,7 @@ int32_t launch_composite_bwd_deterministic(int64_t n, int64_t total, const float
   GS_TRY(launch_sort_positions(total, n, gaussian_ids, base + L.sort, order, segments, stream));
   if (n == 0) return GS_OK;
   launch_chained(reduce_rows_kernel, ceil_div(n, 256), 256, stream, n, order, segments, rows,
-                                                           grad_projected);
+                 grad_projected);
   return check_launch();
 }
 

@@ -145,13 +145,13 @@ int32_t launch_l1_fwd(const float* image, int64_t height, int64_t width, int64_t
   const int64_t row_stride = width * channels, row_length = target_width * channels;
   if (vectorisable(image, target, nullptr, row_stride, row_length))
     launch_chained(l1_partial_kernel<true>, kBlocks, kThreads, stream, image, row_stride, target,
-                                                              target_height, row_length, partials);
+                   target_height, row_length, partials);
   else
     launch_chained(l1_partial_kernel<false>, kBlocks, kThreads, stream, image, row_stride, target,
-                                                               target_height, row_length, partials);
+                   target_height, row_length, partials);
   GS_TRY(check_launch());
   launch_chained(l1_total_kernel, 1, kThreads, stream, partials, kBlocks,
-                                              target_height * target_width * channels, loss);
+                 target_height * target_width * channels, loss);
   return check_launch();
 }
 
