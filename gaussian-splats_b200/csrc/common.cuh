@@ -67,6 +67,9 @@ __device__ __forceinline__ void chain_wait() {
   asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
+// Launches `kernel` chained (see above). Like a <<<>>> launch, a failed launch
+// also leaves its error for cudaGetLastError, which is how the launchers read
+// it (check_launch() after each launch).
 template <class... Params, class... Args>
 inline cudaError_t launch_chained(void (*kernel)(Params...), dim3 grid, dim3 block,
                                   cudaStream_t stream, Args&&... args) {
